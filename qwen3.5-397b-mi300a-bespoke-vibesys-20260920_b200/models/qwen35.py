@@ -1,0 +1,377 @@
+"""Qwen3.5-MoE runtime: the ``Runner`` the scheduler drives.
+
+One instance per rank. It owns the static pools and runs every forward as one varlen batch of
+segments, so prefill, packed multi-request prefill, batched decode, mixed decode + prefill and
+MTP verify are the same call with different segment lengths:
+
+* paged KV pool per full-attention layer: ``[num_blocks * block_size, kv_heads_local, head_dim]``
+  (block 0 is the pad sentinel, reference ``block_pool.py:38``);
+* DeltaNet live state per lane: conv window ``[lanes, C_local, K-1]`` and fp32 recurrent state
+  ``[lanes, v_heads_local, dk, dv]`` per linear-attention layer;
+* snapshot pool (turn boundaries of the session cache): the same two states per slot, plus the
+  cached next-token logits and the MTP seed hidden of that boundary.
+
+Per-layer dataflow (``Model._forward``), with the TP collective fused into the next norm::
+
+    x = embed(tokens); h = rmsnorm(x, in_norm[0])
+    for each layer:
+        partial = deltanet(h) | gated_attention(h)        # row-parallel partial sums
+        x, h = allreduce_add_rmsnorm(partial, x, post_norm)
+        partial = moe(h)                                   # EP experts + TP shared expert
+        x, h = allreduce_add_rmsnorm(partial, x, next in_norm | final_norm)
+    logits = lm_head(h[logit rows])                        # vocab parallel, all-gathered
+
+Reference parity: ``model.py:1344-4355`` (``Model``; the ``Runner`` methods ``begin``,
+``prefill``, ``prefill_batch``, ``decode``, ``save_snapshot``/``load_snapshot``,
+``attach_blocks``/``extend_blocks``/``copy_block``, ``sample_batch``, ``cache_node_logits``,
+``score``) and ``scheduler.py:399-516`` (the ``Runner`` protocol).
+"""
+
+from __future__ import annotations
+
+import os
+from collections.abc import Sequence
+from dataclasses import dataclass
+
+import torch
+
+from ..ops import core as ops
+from ..parallel.comm import Comm
+from ..parallel.plan import Plan
+from .config import FULL, Qwen35Config
+
+RESERVED_BLOCK = 0
+
+
+@dataclass
+class StepInputs:
+    """Device-side description of one varlen forward (plus host copies for the CPU path)."""
+
+    tokens: torch.Tensor  # [T] int64
+    positions: torch.Tensor  # [T] int32
+    rows: torch.Tensor  # [T] int32 physical KV rows
+    seg_lane: torch.Tensor  # [S] int32
+    cu: torch.Tensor  # [S+1] int32
+    seg_start: torch.Tensor  # [S] int32
+    logit_rows: torch.Tensor  # [R] int64
+    seg_lane_h: list[int]
+    cu_h: list[int]
+    seg_start_h: list[int]
+
+
+class Model:
+    """Per-rank Qwen3.5-MoE model with its static pools; implements the scheduler's Runner."""
+
+    def __init__(
+        self,
+        cfg: Qwen35Config,
+        weights: dict,
+        plan: Plan,
+        comm: Comm | None = None,
+        device: torch.device | str = "cpu",
+        dtype: torch.dtype = torch.bfloat16,
+        max_batch: int = 8,
+        max_seq: int = 4096,
+        block_size: int = 16,
+        num_blocks: int | None = None,
+        num_snapshots: int = 16,
+    ) -> None:
+        self.cfg, self.w, self.plan = cfg, weights, plan
+        self.comm = comm or Comm()
+        self.device = torch.device(device)
+        self.dtype = dtype
+        self.max_batch = max_batch
+        self.max_seq = max_seq
+        self.block_size = block_size
+        self.max_blocks = (max_seq + block_size - 1) // block_size
+        if num_blocks is None:
+            num_blocks = max_batch * self.max_blocks + 1
+        self.num_blocks = num_blocks
+        self.num_snapshots = num_snapshots
+        self.mtp = None  # set by models.mtp.attach
+        self.full_slot = {i: j for j, i in enumerate(cfg.full_layers)}
+        self.lin_slot = {i: j for j, i in enumerate(cfg.linear_layers)}
+        p = plan
+        self.nq, self.nkv = p.q.count, p.kv.count
+        self.nk, self.nv = p.dn_k.count, p.dn_v.count
+        self.conv_ch = 2 * self.nk * cfg.dn_k_dim + self.nv * cfg.dn_v_dim
+        dev, dt = self.device, dtype
+        rows = num_blocks * block_size
+        self.k_cache = [torch.zeros(rows, self.nkv, cfg.head_dim, dtype=dt, device=dev) for _ in cfg.full_layers]
+        self.v_cache = [torch.zeros(rows, self.nkv, cfg.head_dim, dtype=dt, device=dev) for _ in cfg.full_layers]
+        nl, km1 = len(cfg.linear_layers), cfg.conv_kernel - 1
+        self.conv_state = torch.zeros(nl, max_batch, self.conv_ch, km1, dtype=dt, device=dev)
+        self.rec_state = torch.zeros(nl, max_batch, self.nv, cfg.dn_k_dim, cfg.dn_v_dim, dtype=torch.float32, device=dev)
+        self.snap_conv = torch.zeros(nl, num_snapshots, self.conv_ch, km1, dtype=dt, device=dev)
+        self.snap_rec = torch.zeros(nl, num_snapshots, self.nv, cfg.dn_k_dim, cfg.dn_v_dim, dtype=torch.float32, device=dev)
+        self.snap_logits: dict[int, torch.Tensor] = {}
+        self.tables: list[list[int]] = [[] for _ in range(max_batch)]
+        self.table_dev = torch.zeros(max_batch, self.max_blocks, dtype=torch.int32, device=dev)
+        self._dirty: set[int] = set(range(max_batch))
+        self.last_hidden: torch.Tensor | None = None  # pre-final-norm hidden of the logit rows (MTP seed)
+        self.fault: dict[str, object] = {}  # accuracy-gate calibration faults (serving.faults)
+
+    # ================================================================== Runner: lanes & blocks
+    def begin(self, lane: int) -> None:
+        for j in range(self.conv_state.shape[0]):
+            self.conv_state[j, lane].zero_()
+            self.rec_state[j, lane].zero_()
+        self.tables[lane] = []
+        self._dirty.add(lane)
+        if self.mtp is not None:
+            self.mtp.begin(lane)
+
+    def lane_blocks(self, lane: int) -> tuple[int, ...]:
+        return tuple(self.tables[lane])
+
+    def lane_block_count(self, lane: int) -> int:
+        return len(self.tables[lane])
+
+    def attach_blocks(self, lane: int, blocks: Sequence[int]) -> None:
+        if len(blocks) > self.max_blocks:
+            raise ValueError(f"lane {lane}: {len(blocks)} blocks > max {self.max_blocks}")
+        self.tables[lane] = list(blocks)
+        self._dirty.add(lane)
+
+    def extend_blocks(self, grants: Sequence[tuple[int, int]]) -> None:
+        for lane, blk in grants:
+            if len(self.tables[lane]) >= self.max_blocks:
+                raise ValueError(f"lane {lane}: block table full ({self.max_blocks})")
+            self.tables[lane].append(int(blk))
+            self._dirty.add(lane)
+
+    def copy_block(self, dst_block: int, src_block: int, filled: int) -> None:
+        bs = self.block_size
+        s, d = src_block * bs, dst_block * bs
+        for kc, vc in zip(self.k_cache, self.v_cache):
+            kc[d:d + filled].copy_(kc[s:s + filled])
+            vc[d:d + filled].copy_(vc[s:s + filled])
+        if self.mtp is not None:
+            self.mtp.copy_block(d, s, filled)
+
+    def _sync_tables(self) -> None:
+        if not self._dirty:
+            return
+        for lane in sorted(self._dirty):
+            t = self.tables[lane]
+            row = torch.zeros(self.max_blocks, dtype=torch.int32)
+            if t:
+                row[: len(t)] = torch.tensor(t, dtype=torch.int32)
+            self.table_dev[lane].copy_(row.to(self.device), non_blocking=True)
+        self._dirty.clear()
+
+    # ================================================================== Runner: snapshots
+    def save_snapshot(self, lane: int, snap: int) -> None:
+        self.snap_conv[:, snap].copy_(self.conv_state[:, lane])
+        self.snap_rec[:, snap].copy_(self.rec_state[:, lane])
+        if self.mtp is not None:
+            self.mtp.save_snapshot(lane, snap)
+
+    def load_snapshot(self, lane: int, snap: int) -> None:
+        self.conv_state[:, lane].copy_(self.snap_conv[:, snap])
+        self.rec_state[:, lane].copy_(self.snap_rec[:, snap])
+        if self.mtp is not None:
+            self.mtp.load_snapshot(lane, snap)
+
+    def cache_node_logits(self, snap: int, logits) -> None:
+        self.snap_logits[snap] = logits.detach().clone()
+
+    def cached_node_logits(self, snap: int):
+        return self.snap_logits[snap]
+
+    # ================================================================== inputs
+    def _row(self, lane: int, pos: int) -> int:
+        blk = pos // self.block_size
+        t = self.tables[lane]
+        if blk >= len(t):
+            raise IndexError(f"lane {lane}: position {pos} has no block (table has {len(t)})")
+        return t[blk] * self.block_size + pos % self.block_size
+
+    def make_inputs(self, segs: Sequence[tuple[int, Sequence[int], int]], logit_rows: Sequence[int] | None = None) -> StepInputs:
+        """``segs`` = ``(lane, ids, start)`` per segment; logits default to each segment's last row."""
+        toks, pos, rows, lanes, cu, starts, last = [], [], [], [], [0], [], []
+        for lane, ids, start in segs:
+            n = len(ids)
+            if n == 0:
+                raise ValueError("empty segment")
+            if start + n > self.max_seq:
+                raise ValueError(f"lane {lane}: {start + n} tokens > max_seq {self.max_seq}")
+            toks.extend(int(t) for t in ids)
+            pos.extend(range(start, start + n))
+            rows.extend(self._row(lane, p) for p in range(start, start + n))
+            lanes.append(lane)
+            starts.append(start)
+            cu.append(cu[-1] + n)
+            last.append(cu[-1] - 1)
+        if logit_rows is None:
+            logit_rows = last
+        dev = self.device
+        i32 = torch.int32
+        packed = torch.tensor(pos + rows + lanes + cu + starts, dtype=i32)
+        if dev.type == "cuda":
+            packed = packed.pin_memory().to(dev, non_blocking=True)
+            tok = torch.tensor(toks, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+            lr = torch.tensor(list(logit_rows), dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        else:
+            tok = torch.tensor(toks, dtype=torch.int64)
+            lr = torch.tensor(list(logit_rows), dtype=torch.int64)
+        t, s = len(toks), len(lanes)
+        o = 0
+        positions = packed[o:o + t]; o += t  # noqa: E702
+        prow = packed[o:o + t]; o += t  # noqa: E702
+        seg_lane = packed[o:o + s]; o += s  # noqa: E702
+        cu_d = packed[o:o + s + 1]; o += s + 1  # noqa: E702
+        seg_start = packed[o:o + s]
+        self._sync_tables()
+        return StepInputs(tok, positions, prow, seg_lane, cu_d, seg_start, lr, lanes, cu, starts)
+
+    # ================================================================== layers
+    def _deltanet(self, i: int, L: dict, h: torch.Tensor, b: StepInputs) -> torch.Tensor:
+        cfg = self.cfg
+        j = self.lin_slot[i]
+        nk, nv, dk, dv = self.nk, self.nv, cfg.dn_k_dim, cfg.dn_v_dim
+        c = self.conv_ch
+        proj = ops.linear(h, L["w_in"])  # [T, c + nv*dv + 2nv]
+        qkv = ops.causal_conv_varlen(proj[:, :c], self.conv_state[j], L["conv_w"], b.seg_lane, b.cu,
+                                     b.seg_lane_h, b.cu_h)
+        z = proj[:, c:c + nv * dv]
+        ab = proj[:, c + nv * dv:]
+        core = ops.gated_delta_varlen(qkv, ab, L["A_log"], L["dt_bias"], self.rec_state[j], b.seg_lane, b.cu,
+                                      nk, nv, dk, dv, b.seg_lane_h, b.cu_h)
+        if self.fault.get("skip_deltanet_gate"):
+            normed = ops.rmsnorm(core, torch.ones(dv, device=h.device), cfg.eps).reshape(-1, nv * dv)
+        else:
+            normed = ops.gated_rmsnorm(core, z.reshape(-1, nv, dv), L["norm_w"], cfg.eps).reshape(-1, nv * dv)
+        return ops.linear(normed, L["w_out"])
+
+    def _attention(self, i: int, L: dict, h: torch.Tensor, b: StepInputs) -> torch.Tensor:
+        cfg = self.cfg
+        j = self.full_slot[i]
+        hd, nq, nkv = cfg.head_dim, self.nq, self.nkv
+        qkv = ops.linear(h, L["w_qkv"])
+        t = qkv.shape[0]
+        qg = qkv[:, : nq * 2 * hd].reshape(t, nq, 2 * hd)
+        q, gate = qg[..., :hd], qg[..., hd:]
+        k = qkv[:, nq * 2 * hd: nq * 2 * hd + nkv * hd].reshape(t, nkv, hd)
+        v = qkv[:, nq * 2 * hd + nkv * hd:].reshape(t, nkv, hd)
+        theta = float(self.fault.get("rope_base", cfg.rope_theta))
+        q = ops.qk_norm_rope_kv_write(q, k, v, L["q_norm"], L["k_norm"], b.positions, b.rows,
+                                      self.k_cache[j], self.v_cache[j], cfg.rotary_dim, theta, cfg.eps)
+        o = ops.attention_varlen(q, self.k_cache[j], self.v_cache[j], self.table_dev, b.seg_lane, b.cu,
+                                 b.seg_start, self.block_size, b.seg_lane_h, b.cu_h, b.seg_start_h,
+                                 self.tables if h.device.type == "cpu" else None)
+        o = ops.sigmoid_gate_mul(o.reshape(t, nq * hd), gate.reshape(t, nq * hd))
+        return ops.linear(o, L["w_o"])
+
+    def _moe(self, L: dict, h: torch.Tensor) -> torch.Tensor:
+        cfg, p = self.cfg, self.plan
+        rl = ops.linear(h, L["w_router"])  # [T, E+1]: router logits | shared-expert gate logit
+        topw, topi = ops.router_topk(rl[:, : cfg.experts], cfg.top_k)
+        drop = self.fault.get("drop_expert")
+        if drop is not None:
+            topw = torch.where(topi == int(drop), torch.zeros_like(topw), topw)
+        routed = ops.moe_routed(h, topw, topi, L["experts"], p.experts.start, p.experts.count)
+        sh = ops.linear(ops.silu_mul(ops.linear(h, L["w_sh13"])), L["w_sh2"])
+        return ops.shared_gate_combine(routed, sh, rl[:, cfg.experts])
+
+    def _layers(self, x: torch.Tensor, b: StepInputs) -> tuple[torch.Tensor, torch.Tensor]:
+        cfg, comm, layers = self.cfg, self.comm, self.w["layers"]
+        h = ops.rmsnorm(x, layers[0]["in_norm"], cfg.eps)
+        for i, L in enumerate(layers):
+            mix = self._attention(i, L, h, b) if L["kind"] == FULL else self._deltanet(i, L, h, b)
+            x, h = comm.allreduce_add_rmsnorm(mix, x, L["post_norm"], cfg.eps)
+            m = self._moe(L, h)
+            nxt = layers[i + 1]["in_norm"] if i + 1 < len(layers) else self.w["final_norm"]
+            x, h = comm.allreduce_add_rmsnorm(m, x, nxt, cfg.eps)
+        return x, h
+
+    def _forward(self, b: StepInputs) -> torch.Tensor:
+        """Runs every layer over the batch; returns the final-normed hidden of the logit rows and
+        keeps the matching pre-norm residual in ``last_hidden`` (the MTP seed)."""
+        x = ops.embed(b.tokens, self.w["embed"])
+        x, h = self._layers(x, b)
+        self.last_hidden = x.index_select(0, b.logit_rows)
+        self.last_hidden_all = x
+        return h.index_select(0, b.logit_rows)
+
+    def logits(self, h: torch.Tensor) -> torch.Tensor:
+        """Full-vocab logits [R, V] (vocab-parallel GEMM, then all-gathered over ranks)."""
+        local = ops.linear(h, self.w["lm_head"])
+        return self.comm.all_gather_last(local)
+
+    # ================================================================== Runner: forwards
+    @torch.inference_mode()
+    def forward(self, segs, logit_rows=None) -> torch.Tensor:
+        b = self.make_inputs(segs, logit_rows)
+        return self.logits(self._forward(b))
+
+    def prefill(self, lane: int, ids: Sequence[int], start: int):
+        return self.forward([(lane, ids, start)])[0:1]
+
+    def prefill_batch(self, calls: Sequence[tuple[int, Sequence[int], int]]) -> list:
+        if not calls:
+            return []
+        lg = self.forward(list(calls))
+        return [lg[i:i + 1] for i in range(len(calls))]
+
+    def decode(self, lanes: Sequence[int], tokens: Sequence[int], positions: Sequence[int]):
+        return self.forward([(l, [t], p) for l, t, p in zip(lanes, tokens, positions)])
+
+    def decode_mixed(self, lanes, tokens, positions, prefill_calls):
+        segs = [(l, [t], p) for l, t, p in zip(lanes, tokens, positions)] + list(prefill_calls)
+        lg = self.forward(segs)
+        n = len(lanes)
+        return lg[:n], [lg[n + i:n + i + 1] for i in range(len(prefill_calls))]
+
+    def decode_row(self, logits, row: int):
+        return logits[row:row + 1]
+
+    def decode_tokens_per_step(self) -> int:
+        return 1 if self.mtp is None else self.mtp.k + 1
+
+    @torch.inference_mode()
+    def score(self, lane: int, ids: Sequence[int], continuation_start: int):
+        """Logits predicting ``ids[continuation_start:]`` (rows ``continuation_start-1 ..``)."""
+        rows = list(range(max(continuation_start - 1, 0), len(ids) - 1))
+        if not rows:
+            return torch.empty(0, self.cfg.vocab)
+        return self.forward([(lane, ids, 0)], logit_rows=rows)
+
+    def sample_batch(self, logits, temperatures: Sequence[float], generator=None) -> list[int]:
+        temps = list(temperatures)
+        out = ops.argmax_rows(logits)[1].tolist() if logits.shape[0] else []
+        for i, t in enumerate(temps):
+            if t and t > 0:
+                p = torch.softmax(logits[i].float() / t, dim=-1)
+                out[i] = int(torch.multinomial(p, 1, generator=generator).item())
+        return [int(x) for x in out]
+
+    def warmup(self) -> None:
+        pass
+
+    # ================================================================== convenience
+    @torch.inference_mode()
+    def generate(self, ids: Sequence[int], max_new: int, lane: int = 0, stop: Sequence[int] = ()) -> list[int]:
+        """Single-sequence greedy generation on ``lane`` with private block bookkeeping
+        (blocks ``1 + lane * max_blocks ..``); used by tests and examples, not by serving."""
+        self.begin(lane)
+        need = (len(ids) + max_new + self.block_size - 1) // self.block_size
+        base = 1 + lane * self.max_blocks
+        if base + need > self.num_blocks:
+            raise ValueError("pool too small for generate()")
+        self.attach_blocks(lane, list(range(base, base + need)))
+        lg = self.prefill(lane, ids, 0)
+        out: list[int] = []
+        pos = len(ids)
+        for _ in range(max_new):
+            tok = self.sample_batch(lg, [0.0])[0]
+            out.append(tok)
+            if tok in stop:
+                break
+            lg = self.decode([lane], [tok], [pos])
+            pos += 1
+        return out
+
+
+def env_flag(name: str, default: str = "0") -> bool:
+    return os.environ.get(name, default) not in ("0", "", "false", "False")

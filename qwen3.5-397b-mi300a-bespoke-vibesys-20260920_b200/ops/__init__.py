@@ -1,0 +1,1 @@
+"""See the package docstring of ``qwen35_b200``."""

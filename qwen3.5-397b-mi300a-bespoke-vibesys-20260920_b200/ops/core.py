@@ -1,0 +1,196 @@
+"""Entry points of every op the model runtime issues.
+
+CUDA tensors go to the compiled sm_100a extension (``ops._ext``; sources in ``csrc/``). If the
+extension is missing on a CUDA tensor the call raises: there is no silent eager fallback.
+CPU tensors use the PyTorch statements in ``ops.reference`` (hermetic tests, gloo ranks).
+
+Varlen conventions shared by the sequence ops: the batch is a concatenation of segments; a
+segment is ``cu[s]..cu[s+1]`` rows of lane ``seg_lane[s]`` whose first row is at absolute
+position ``seg_start[s]``. Lane state (conv window, recurrent state, block table) is indexed by
+lane. ``rows[t]`` is the physical paged-KV row of token ``t``.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.nn.functional as F
+
+from . import reference as ref
+from ._ext import ext
+
+
+def _cuda(x: torch.Tensor) -> bool:
+    return x.is_cuda
+
+
+# ----------------------------------------------------------------------------- norms
+def rmsnorm(x, w1p, eps):
+    if _cuda(x):
+        return ext().rmsnorm(x, w1p, eps)
+    return ref.rmsnorm(x, w1p, eps)
+
+
+def add_rmsnorm(x, residual, w1p, eps):
+    """Returns (residual + x, rmsnorm(residual + x)); on CUDA the residual is updated in place."""
+    if _cuda(x):
+        normed = torch.empty_like(residual)
+        ext().add_rmsnorm(x, residual, w1p, normed, eps)
+        return residual, normed
+    return ref.add_rmsnorm(x, residual, w1p, eps)
+
+
+def gated_rmsnorm(x, z, w, eps):
+    if _cuda(x):
+        return ext().gated_rmsnorm(x, z, w, eps)
+    return ref.gated_rmsnorm(x, z, w, eps)
+
+
+# ----------------------------------------------------------------------------- dense
+def linear(x, w, out=None):
+    """``x @ w.T`` (fp32 accumulate). CUDA: tcgen05 GEMM with the weight as the M operand."""
+    if _cuda(x):
+        return ext().linear(x, w, out)
+    y = ref.linear(x, w)
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def silu_mul(gu):
+    """``silu(gu[:, :n]) * gu[:, n:]`` rounded to the input dtype."""
+    if _cuda(gu):
+        return ext().silu_mul(gu)
+    n = gu.shape[-1] // 2
+    return (F.silu(gu[..., :n].float()) * gu[..., n:].float()).to(gu.dtype)
+
+
+def embed(tokens, table):
+    if _cuda(tokens):
+        return ext().embed(tokens, table)
+    return table[tokens]
+
+
+def argmax_rows(logits):
+    if _cuda(logits):
+        return ext().argmax_rows(logits)
+    v, i = logits.float().max(dim=-1)
+    return v, i
+
+
+# ----------------------------------------------------------------------------- deltanet
+def causal_conv_varlen(x, conv_state, w, seg_lane, cu, seg_lane_h=None, cu_h=None):
+    """Depthwise causal conv + SiLU over each segment, continuing from and updating
+    ``conv_state[lane]`` ([lanes, C, K-1]). ``x`` [T, C] (may be a column slice)."""
+    if _cuda(x):
+        return ext().causal_conv_varlen(x, conv_state, w, seg_lane, cu)
+    out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
+    lanes = seg_lane_h if seg_lane_h is not None else seg_lane.tolist()
+    cus = cu_h if cu_h is not None else cu.tolist()
+    for s, lane in enumerate(lanes):
+        a, b = cus[s], cus[s + 1]
+        o, st = ref.causal_conv(x[a:b], conv_state[lane], w)
+        out[a:b] = o
+        conv_state[lane].copy_(st)
+    return out
+
+
+def gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv,
+                       seg_lane_h=None, cu_h=None):
+    """Gated delta rule over each segment with the DeltaNet glue fused in.
+
+    ``qkv`` [T, 2*nk*dk + nv*dv] (conv output: q | k | v), ``ab`` [T, 2*nv] (``b`` then ``a``
+    projections). Per row: ``beta = sigmoid(b)``, ``g = -exp(A_log) * softplus(a + dt_bias)``,
+    q/k l2-normalised, ``q *= dk**-0.5``, key heads repeated to value heads. ``rec_state``
+    [lanes, nv, dk, dv] fp32 is continued and updated. Returns [T, nv, dv] in ``qkv.dtype``."""
+    if _cuda(qkv):
+        return ext().gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv)
+    t = qkv.shape[0]
+    q = qkv[:, : nk * dk].reshape(t, nk, dk).float()
+    k = qkv[:, nk * dk: 2 * nk * dk].reshape(t, nk, dk).float()
+    v = qkv[:, 2 * nk * dk:].reshape(t, nv, dv).float()
+    g, beta = ref.deltanet_gates(ab[:, nv:], ab[:, :nv], a_log, dt_bias)
+    rep = nv // nk
+    q = ref.l2norm(q).repeat_interleave(rep, dim=1) * dk ** -0.5
+    k = ref.l2norm(k).repeat_interleave(rep, dim=1)
+    out = torch.empty(t, nv, dv, dtype=torch.float32, device=qkv.device)
+    lanes = seg_lane_h if seg_lane_h is not None else seg_lane.tolist()
+    cus = cu_h if cu_h is not None else cu.tolist()
+    for s, lane in enumerate(lanes):
+        a, b = cus[s], cus[s + 1]
+        o, st = ref.gated_delta_rule(q[a:b], k[a:b], v[a:b], g[a:b], beta[a:b], rec_state[lane])
+        out[a:b] = o
+        rec_state[lane].copy_(st)
+    return out.to(qkv.dtype)
+
+
+# ----------------------------------------------------------------------------- attention
+def qk_norm_rope_kv_write(q, k, v, q_norm, k_norm, positions, rows, k_cache, v_cache, rot, theta, eps):
+    """Per-head RMSNorm of q and k, partial RoPE on the first ``rot`` dims, and the paged KV
+    write of (k, v) at physical ``rows``. Returns the normalised, rotated q [T, Hq, D]."""
+    if _cuda(q):
+        return ext().qk_norm_rope_kv_write(q, k, v, q_norm, k_norm, positions, rows, k_cache, v_cache,
+                                           rot, theta, eps)
+    qn = ref.rmsnorm(q, q_norm, eps)
+    kn = ref.rmsnorm(k, k_norm, eps)
+    cos, sin = ref.rope_cos_sin(positions, rot, theta, q.dtype)
+    qn = ref.apply_partial_rope(qn, cos, sin)
+    kn = ref.apply_partial_rope(kn, cos, sin)
+    k_cache[rows.long()] = kn.to(k_cache.dtype)
+    v_cache[rows.long()] = v.to(v_cache.dtype)
+    return qn
+
+
+def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, block_size,
+                     seg_lane_h=None, cu_h=None, seg_start_h=None, tables_h=None):
+    """Causal GQA attention of each segment's queries over its lane's paged context
+    ``[0, seg_start + len)``. ``q`` [T, Hq, D]; caches [rows, Hkv, D]. Returns [T, Hq, D]."""
+    if _cuda(q):
+        return ext().attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, block_size)
+    out = torch.empty_like(q)
+    lanes = seg_lane_h if seg_lane_h is not None else seg_lane.tolist()
+    cus = cu_h if cu_h is not None else cu.tolist()
+    starts = seg_start_h if seg_start_h is not None else seg_start.tolist()
+    for s, lane in enumerate(lanes):
+        a, b = cus[s], cus[s + 1]
+        n = starts[s] + (b - a)
+        if tables_h is not None:
+            blocks = tables_h[lane]
+        else:
+            blocks = block_table[lane].tolist()
+        nb = (n + block_size - 1) // block_size
+        rows = torch.tensor([blk * block_size + o for blk in blocks[:nb] for o in range(block_size)][:n],
+                            dtype=torch.long, device=q.device)
+        out[a:b] = ref.attention_prefix(q[a:b], k_cache[rows], v_cache[rows], starts[s])
+    return out
+
+
+def sigmoid_gate_mul(x, gate):
+    if _cuda(x):
+        return ext().sigmoid_gate_mul(x, gate)
+    return (x.float() * torch.sigmoid(gate.float())).to(x.dtype)
+
+
+# ----------------------------------------------------------------------------- moe
+def router_topk(logits, k):
+    """Softmax / top-k / renormalise over the first ``E`` columns; returns (w [T,k] fp32,
+    idx [T,k] int32)."""
+    if _cuda(logits):
+        return ext().router_topk(logits, k)
+    w, i = ref.router_topk(logits, k)
+    return w.float(), i.int()
+
+
+def moe_routed(h, topw, topi, experts, first, count):
+    """Sum of this rank's experts' weighted outputs for each row (zero for rows routed only to
+    other ranks' experts). fp32 accumulation, rounded once to ``h.dtype``."""
+    if _cuda(h):
+        return ext().moe_routed(h, topw, topi, experts, first, count)
+    return ref.routed_experts(h, topw, topi.long(), experts, first, count)
+
+
+def shared_gate_combine(routed, shared, gate_logit):
+    """``routed + sigmoid(gate_logit) * shared``."""
+    if _cuda(routed):
+        return ext().shared_gate_combine(routed, shared, gate_logit)
+    return (routed.float() + torch.sigmoid(gate_logit.float())[:, None] * shared.float()).to(routed.dtype)

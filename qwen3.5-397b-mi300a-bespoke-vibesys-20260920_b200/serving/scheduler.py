@@ -1,0 +1,431 @@
+"""Continuous-batching scheduler with the cross-turn prefix/session cache (host only).
+
+Iteration model: one ``step()`` is either one packed prefill call (several requests' prompt
+chunks concatenated, up to ``token_budget`` tokens) or one batched decode step over every lane
+past prefill; prefill wins ties for at most ``max_prefill_burst`` consecutive steps while
+lanes are decoding (reference ``scheduler.py:865-948``). With ``mixed=True`` a decode step
+also carries prefill chunks in the same forward (Sarathi-style), and with an MTP-capable runner
+decode steps are speculative rounds (draft, verify, accept).
+
+Admission (``_admit``): any free lane; the session cache resolves the deepest reusable
+boundary for the prompt, copy-on-write of its partial last block, adoption of its blocks and
+load of its DeltaNet snapshot; only the remaining prompt tail is prefilled. An exact repeat of
+a cached boundary is answered from the node's cached logits with no forward.
+
+Publishing: a turn-open node at ``len(prompt) - suffix_len`` (the chat template's generation
+suffix is excluded, so a follow-up turn whose history re-renders this turn without it still
+matches), and a turn-close node when a request finishes, at the last forwarded position (the
+final sampled token is never forwarded, so its logits are exactly the node's cached logits).
+
+The scheduler is the only block allocator while serving: every forward's KV rows are reserved
+here first (``_grow``), so under tensor parallelism every rank holds the same block ids.
+
+Reference behaviour: ``scheduler.py:612-2186`` (``Scheduler``, ``_admit``, ``_acquire``,
+``_grow_lanes``, ``_publish_boundary``, ``_publish_turn_close``, ``_select_prefill_batch``,
+``_finish_prefill_chunk``, ``_decode_step``, ``_speculative_decode_step``, ``_mixed_step``,
+``_emit``, ``_release``).
+"""
+
+from __future__ import annotations
+
+import queue
+import threading
+import time
+import traceback
+from collections import deque
+from collections.abc import Callable, Sequence
+from dataclasses import dataclass, field
+from typing import Any
+
+from ..utils.telemetry import StepTimer
+from .block_pool import blocks_for
+from .session_cache import Node, SessionCache, SessionCacheError
+
+Event = tuple[str, Any]
+
+PREFILL_CHUNK = 512
+PREFILL_TOKEN_BUDGET = 2048
+MAX_PREFILL_BURST = 4
+
+
+@dataclass
+class Request:
+    """One completion. ``emit`` receives ``("tok", id)`` per generated token, then
+    ``("end", (reason, generated, reused))`` or ``("error", message)``."""
+
+    prompt: list[int]
+    max_new: int
+    emit: Callable[[Event], None]
+    temperature: float = 0.0
+    stop: frozenset[int] = frozenset()
+    suffix_len: int = 0
+    has_history: bool = False
+    arrival: float = field(default_factory=time.perf_counter)
+    first_token_at: float | None = None
+
+
+@dataclass
+class _Flight:
+    req: Request
+    lane: int
+    pos: int
+    pending: list[int]
+    reused: int
+    parent: Node
+    resumed_from: Node
+    blocks: list[int]
+    boundary: int
+    next_token: int | None = None
+    generated: int = 0
+    out_ids: list[int] = field(default_factory=list)
+    last_logits: Any = None
+    done: bool = False
+
+
+@dataclass
+class ScoreJob:
+    ids: list[int]
+    continuation_start: int
+    finish: Callable[[Any], Any]
+    done: threading.Event = field(default_factory=threading.Event)
+    result: Any = None
+    error: str | None = None
+
+
+@dataclass
+class _Control:
+    fn: Callable[[], Any]
+    done: threading.Event = field(default_factory=threading.Event)
+    result: Any = None
+
+
+class Scheduler:
+    def __init__(self, runner, cache: SessionCache, prefill_chunk: int = PREFILL_CHUNK,
+                 token_budget: int = PREFILL_TOKEN_BUDGET, max_prefill_burst: int = MAX_PREFILL_BURST,
+                 mixed: bool = False, speculative: bool = False, timer: StepTimer | None = None) -> None:
+        self.runner = runner
+        self.cache = cache
+        self.block_size = cache.block_size
+        self.prefill_chunk = prefill_chunk
+        self.token_budget = token_budget
+        self.max_prefill_burst = max_prefill_burst
+        self.mixed = mixed
+        self.speculative = speculative
+        self.free_lanes: list[int] = list(range(runner.max_batch - 1, -1, -1))
+        self.incoming: queue.Queue = queue.Queue()
+        self.waiting: deque[Request] = deque()
+        self.prefilling: deque[_Flight] = deque()
+        self.decoding: list[_Flight] = []
+        self.burst = 0
+        self.timer = timer or StepTimer()
+        self.steps = 0
+        self._stop = threading.Event()
+        self.errors = 0
+
+    # ================================================================== public
+    def submit(self, req: Request) -> None:
+        self.incoming.put(req)
+
+    def reset_prefix_cache(self) -> int:
+        """Evict every cache entry not held by a live request (runs on the scheduler thread)."""
+        return self.control(lambda: self.cache.evict_all(self._live_parents()))
+
+    def score(self, job: ScoreJob) -> None:
+        self.incoming.put(job)
+
+    def control(self, fn: Callable[[], Any], timeout: float | None = 600.0):
+        c = _Control(fn)
+        self.incoming.put(c)
+        if not c.done.wait(timeout):
+            raise TimeoutError("scheduler did not run the control message")
+        return c.result
+
+    def idle(self) -> bool:
+        return not (self.waiting or self.prefilling or self.decoding) and self.incoming.empty()
+
+    def stop(self) -> None:
+        self._stop.set()
+        self.incoming.put(None)
+
+    def run(self) -> None:
+        while not self._stop.is_set():
+            if self.idle():
+                try:
+                    item = self.incoming.get(timeout=0.05)
+                except queue.Empty:
+                    continue
+                if item is not None:
+                    self._accept(item)
+            self.step()
+
+    def run_until_idle(self, max_steps: int = 10**9) -> None:
+        n = 0
+        while not self.idle() and n < max_steps:
+            self.step()
+            n += 1
+
+    # ================================================================== iteration
+    def _accept(self, item) -> None:
+        if isinstance(item, _Control):
+            try:
+                item.result = item.fn()
+            finally:
+                item.done.set()
+        elif isinstance(item, ScoreJob):
+            self._run_score(item)
+        elif isinstance(item, Request):
+            self.waiting.append(item)
+
+    def _drain(self) -> None:
+        while True:
+            try:
+                item = self.incoming.get_nowait()
+            except queue.Empty:
+                return
+            if item is not None:
+                self._accept(item)
+
+    def step(self) -> bool:
+        self._drain()
+        try:
+            while self.waiting and self.free_lanes:
+                if not self._admit(self.waiting[0]):
+                    break
+                self.waiting.popleft()
+            if self.prefilling and (not self.decoding or self.burst < self.max_prefill_burst):
+                if self.mixed and self.decoding:
+                    self._decode_step(with_prefill=True)
+                else:
+                    self._prefill_step()
+                    self.burst += 1
+                self.steps += 1
+                return True
+            if self.decoding:
+                self._decode_step()
+                self.burst = 0
+                self.steps += 1
+                return True
+            return False
+        except Exception as e:  # abort everything in flight, keep serving
+            self.errors += 1
+            msg = f"{type(e).__name__}: {e}"
+            traceback.print_exc()
+            self._abort_all(msg)
+            return True
+
+    # ================================================================== admission
+    def _live_parents(self) -> list[Node]:
+        return [f.parent for f in list(self.prefilling) + self.decoding]
+
+    def _admit(self, req: Request) -> bool:
+        if not req.prompt:
+            req.emit(("error", "empty prompt"))
+            return True
+        node = self.cache.lookup(req.prompt)
+        lane = self.free_lanes[-1]
+        protect = [node] + self._live_parents()
+        try:
+            if self.cache.needs_cow(node):
+                new = self.cache.reserve_blocks(1, protect)
+                self.runner.copy_block(new[0], node.blocks[-1], node.depth % self.block_size)
+                blocks = self.cache.adopt(node, new[0])
+            else:
+                blocks = self.cache.adopt(node)
+        except SessionCacheError:
+            if not (self.prefilling or self.decoding):
+                req.emit(("error", "KV block pool exhausted: no evictable cache entry left"))
+                return True
+            return False
+        self.free_lanes.pop()
+        self.runner.begin(lane)
+        self.runner.attach_blocks(lane, blocks)
+        if not node.is_root():
+            self.runner.load_snapshot(lane, node.snapshot)
+        boundary = len(req.prompt) - req.suffix_len
+        f = _Flight(req, lane, node.depth, list(req.prompt[node.depth:]), node.depth, node, node, blocks,
+                    boundary if boundary > node.depth else -1)
+        if not f.pending:  # exact repeat of a cached boundary: answer from its cached logits
+            logits = self.runner.cached_node_logits(node.snapshot)
+            self._first_token(f, logits)
+        else:
+            self.prefilling.append(f)
+        return True
+
+    def _grow(self, flights: Sequence[_Flight], upto: Sequence[int]) -> None:
+        grants = []
+        protect = self._live_parents()
+        for f, end in zip(flights, upto):
+            need = blocks_for(end, self.block_size) - len(f.blocks)
+            if need > 0:
+                ids = self.cache.reserve_blocks(need, protect)
+                f.blocks.extend(ids)
+                grants.extend((f.lane, b) for b in ids)
+        if grants:
+            self.runner.extend_blocks(grants)
+
+    # ================================================================== prefill
+    def _select_prefill(self) -> list[tuple[_Flight, list[int]]]:
+        batch, budget = [], self.token_budget
+        for f in self.prefilling:
+            n = min(len(f.pending), self.prefill_chunk, budget)
+            if f.boundary > f.pos:
+                n = min(n, f.boundary - f.pos)
+            if n <= 0:
+                break
+            batch.append((f, f.pending[:n]))
+            budget -= n
+            if budget <= 0:
+                break
+        return batch
+
+    def _prefill_step(self) -> None:
+        batch = self._select_prefill()
+        self._grow([f for f, _ in batch], [f.pos + len(ids) for f, ids in batch])
+        t0 = time.perf_counter()
+        logits = self.runner.prefill_batch([(f.lane, ids, f.pos) for f, ids in batch])
+        self._finish_prefill(batch, logits)
+        self.timer.record("prefill", sum(len(i) for _, i in batch), time.perf_counter() - t0)
+
+    def _finish_prefill(self, batch, logits) -> None:
+        for (f, ids), lg in zip(batch, logits):
+            f.pos += len(ids)
+            f.pending = f.pending[len(ids):]
+            if f.pos == f.boundary:
+                self._publish(f, f.req.prompt, f.pos, lg)
+            if not f.pending:
+                self.prefilling.remove(f)
+                self._first_token(f, lg)
+
+    def _first_token(self, f: _Flight, logits) -> None:
+        if f.req.max_new <= 0:
+            self._finish(f, "length")
+            return
+        tok = self.runner.sample_batch(logits, [f.req.temperature])[0]
+        f.last_logits = logits
+        self._emit(f, tok)
+        if not f.done:
+            self.decoding.append(f)
+
+    # ================================================================== decode
+    def _decode_step(self, with_prefill: bool = False) -> None:
+        flights = list(self.decoding)
+        if self.speculative and not with_prefill and self._spec_ok(flights):
+            return self._speculative_step(flights)
+        pre = self._select_prefill() if with_prefill else []
+        self._grow(flights + [f for f, _ in pre], [f.pos + 1 for f in flights] + [f.pos + len(i) for f, i in pre])
+        lanes = [f.lane for f in flights]
+        toks = [f.next_token for f in flights]
+        poss = [f.pos for f in flights]
+        t0 = time.perf_counter()
+        if pre:
+            logits, plog = self.runner.decode_mixed(lanes, toks, poss, [(f.lane, i, f.pos) for f, i in pre])
+        else:
+            logits, plog = self.runner.decode(lanes, toks, poss), []
+        sampled = self.runner.sample_batch(logits, [f.req.temperature for f in flights])
+        for i, (f, t) in enumerate(zip(flights, sampled)):
+            f.pos += 1
+            f.last_logits = self.runner.decode_row(logits, i)
+            self._emit(f, t)
+        if pre:
+            self._finish_prefill(pre, plog)
+        self.timer.record("mixed" if pre else "decode", len(flights), time.perf_counter() - t0)
+
+    def _spec_ok(self, flights: Sequence[_Flight]) -> bool:
+        k1 = self.runner.decode_tokens_per_step()
+        return k1 > 1 and all(f.pos + k1 <= self.runner.max_seq for f in flights)
+
+    def _speculative_step(self, flights: list[_Flight]) -> None:
+        k1 = self.runner.decode_tokens_per_step()
+        self._grow(flights, [f.pos + k1 for f in flights])
+        t0 = time.perf_counter()
+        budgets = [f.req.max_new - f.generated for f in flights]
+        stops = [sorted(f.req.stop) for f in flights]
+        committed = self.runner.speculative_decode([f.lane for f in flights], [f.next_token for f in flights],
+                                                   [f.pos for f in flights], budgets, stops)
+        n = 0
+        for f, toks in zip(flights, committed):
+            for t in toks:
+                f.pos += 1
+                n += 1
+                f.last_logits = None
+                self._emit(f, t)
+                if f.done:
+                    break
+        self.timer.record("spec", n, time.perf_counter() - t0)
+
+    # ================================================================== emit / finish
+    def _emit(self, f: _Flight, tok: int) -> None:
+        req = f.req
+        if req.first_token_at is None:
+            req.first_token_at = time.perf_counter()
+        if tok in req.stop:
+            self._finish(f, "stop")
+            return
+        f.generated += 1
+        f.out_ids.append(tok)
+        f.next_token = tok
+        req.emit(("tok", tok))
+        if f.generated >= req.max_new:
+            self._finish(f, "length")
+
+    def _publish(self, f: _Flight, tokens: Sequence[int], depth: int, logits) -> None:
+        if depth <= f.parent.depth or logits is None:
+            return
+        try:
+            snap = self.cache.reserve_snapshot([f.parent] + self._live_parents())
+        except SessionCacheError:
+            return
+        self.runner.save_snapshot(f.lane, snap)
+        self.runner.cache_node_logits(snap, logits)
+        node = self.cache.publish(tokens, depth, f.blocks, snap, resumed_from=f.resumed_from)
+        f.parent = node
+
+    def _finish(self, f: _Flight, reason: str) -> None:
+        if f.done:
+            return
+        f.done = True
+        full = list(f.req.prompt) + f.out_ids
+        if f.pos > len(f.req.prompt) and f.last_logits is not None:
+            self._publish(f, full, f.pos, f.last_logits)
+        self._release(f)
+        f.req.emit(("end", (reason, f.generated, f.reused)))
+
+    def _release(self, f: _Flight) -> None:
+        if f in self.decoding:
+            self.decoding.remove(f)
+        if f in self.prefilling:
+            self.prefilling.remove(f)
+        self.cache.release_lane_blocks(f.blocks)
+        f.blocks = []
+        self.free_lanes.append(f.lane)
+
+    def _abort_all(self, msg: str) -> None:
+        for f in list(self.prefilling) + list(self.decoding):
+            f.done = True
+            try:
+                self._release(f)
+            except Exception:  # pragma: no cover - best effort
+                pass
+            f.req.emit(("error", msg))
+        self.prefilling.clear()
+        self.decoding.clear()
+
+    # ================================================================== score
+    def _run_score(self, job: ScoreJob) -> None:
+        if not self.free_lanes:
+            self.incoming.put(job)
+            return
+        lane = self.free_lanes.pop()
+        blocks: list[int] = []
+        try:
+            blocks = self.cache.reserve_blocks(blocks_for(len(job.ids), self.block_size), self._live_parents())
+            self.runner.begin(lane)
+            self.runner.attach_blocks(lane, blocks)
+            job.result = job.finish(self.runner.score(lane, job.ids, job.continuation_start))
+        except Exception as e:
+            job.error = f"{type(e).__name__}: {e}"
+        finally:
+            if blocks:
+                self.cache.release_lane_blocks(blocks)
+            self.free_lanes.append(lane)
+            job.done.set()

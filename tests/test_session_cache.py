@@ -1,0 +1,67 @@
+from qwen35_b200.serving.block_pool import BlockAllocator
+from qwen35_b200.serving.session_cache import SessionCache
+
+
+def mk(blocks=64, bs=4, snaps=4):
+    return SessionCache(BlockAllocator(blocks, bs), bs, snaps)
+
+
+def test_lookup_publish_and_refs():
+    c = mk()
+    blocks = c.reserve_blocks(3)
+    toks = list(range(10))
+    s = c.reserve_snapshot()
+    n = c.publish(toks, 10, blocks, s)
+    assert c.lookup(toks + [99]) is n
+    assert c.lookup([5] + toks).is_root()
+    assert all(c.alloc.refcount(b) == 2 for b in blocks)  # lane + node
+    c.release_lane_blocks(blocks)
+    assert all(c.alloc.refcount(b) == 1 for b in blocks)
+
+
+def test_cow_needed_for_partial_last_block():
+    c = mk()
+    b = c.reserve_blocks(3)
+    n = c.publish(list(range(10)), 10, b, c.reserve_snapshot())
+    assert c.needs_cow(n)
+    new = c.reserve_blocks(1)
+    lane = c.adopt(n, new[0])
+    assert lane[:-1] == b[:-1] and lane[-1] == new[0]
+
+
+def test_lru_leaf_eviction_frees_blocks():
+    c = mk(blocks=9, bs=4, snaps=8)
+    b1 = c.reserve_blocks(4)
+    n1 = c.publish(list(range(16)), 16, b1, c.reserve_snapshot())
+    c.release_lane_blocks(b1)
+    b2 = c.reserve_blocks(4)
+    c.publish([7] * 16, 16, b2, c.reserve_snapshot())
+    c.release_lane_blocks(b2)
+    got = c.reserve_blocks(4)  # forces eviction of the LRU leaf (n1)
+    assert len(got) == 4 and c.lookup(list(range(16)) + [1]).is_root()
+    assert c.node_count() == 1 and n1.parent is not None
+
+
+def test_snapshot_reclaim_prefers_superseded_internal():
+    c = mk(blocks=64, bs=4, snaps=2)
+    t1 = list(range(8))
+    b = c.reserve_blocks(2)
+    n1 = c.publish(t1, 8, b, c.reserve_snapshot())
+    lane = c.adopt(n1)
+    b2 = lane + c.reserve_blocks(1)
+    n2 = c.publish(t1 + [50, 51, 52, 53], 12, b2, c.reserve_snapshot(), resumed_from=n1)
+    assert n1.superseded and n2.parent is n1
+    s = c.reserve_snapshot()  # pool full -> reclaims n1's snapshot, keeps n2
+    assert n1.snapshot == -1 and n2.snapshot >= 0 and s >= 0
+    assert c.lookup(t1 + [50, 51, 52, 53, 9]) is n2
+    assert c.lookup(t1 + [1]).is_root()
+
+
+def test_evict_all_respects_protect():
+    c = mk()
+    b = c.reserve_blocks(2)
+    n = c.publish(list(range(8)), 8, b, c.reserve_snapshot())
+    b2 = c.reserve_blocks(2)
+    c.publish([3] * 8, 8, b2, c.reserve_snapshot())
+    assert c.evict_all(protect=[n]) == 1
+    assert c.node_count() == 1
