@@ -1,0 +1,279 @@
+// PyTorch bindings of the sm_100a kernels. Each function checks shapes/dtypes/devices,
+// allocates outputs and scratch through the PyTorch caching allocator (so calls are
+// CUDA-graph capturable), and launches on the current stream. Launch failures raise.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <unordered_map>
+
+#include "kernels.h"
+
+namespace {
+
+using at::Tensor;
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+#define LAUNCH(expr)                                                         \
+  do {                                                                       \
+    int _rc = (expr);                                                        \
+    TORCH_CHECK(_rc == 0, "qwen35_b200 kernel launch failed: ", #expr, " rc=", _rc); \
+  } while (0)
+
+cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+// Device status word shared by every kernel with bounded waits (one per device).
+Tensor& status_tensor(const at::Device& dev) {
+  static std::mutex mu;
+  static std::unordered_map<int, Tensor> m;
+  std::lock_guard<std::mutex> g(mu);
+  auto it = m.find(dev.index());
+  if (it == m.end()) it = m.emplace(dev.index(), at::zeros({4}, at::TensorOptions().dtype(at::kInt).device(dev))).first;
+  return it->second;
+}
+int* err_ptr(const Tensor& like) { return status_tensor(like.device()).data_ptr<int>(); }
+
+long row_stride(const Tensor& t) { return t.dim() >= 2 ? t.stride(0) : t.size(-1); }
+
+// ------------------------------------------------------------------ dense
+Tensor linear(Tensor x, Tensor w, c10::optional<Tensor> out) {
+  CHECK_CUDA(x);
+  CHECK_CUDA(w);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "linear: shape mismatch");
+  TORCH_CHECK(x.scalar_type() == w.scalar_type(), "linear: dtype mismatch");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "linear: inner dim must be contiguous");
+  const bool bf = x.scalar_type() == at::kBFloat16;
+  TORCH_CHECK(bf || x.scalar_type() == at::kHalf, "linear: bf16/f16 only");
+  const int T = x.size(0), N = w.size(0), K = x.size(1);
+  Tensor y = out.has_value() ? *out : at::empty({T, N}, x.options());
+  TORCH_CHECK(y.stride(1) == 1, "linear: output inner dim must be contiguous");
+  TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "linear: row strides must be 16B multiples");
+  LAUNCH(qb::gemm_ws(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(), y.stride(0), T, N, K, bf, 0,
+                     err_ptr(x), stream(), 0));
+  return y;
+}
+
+// ------------------------------------------------------------------ norms / glue
+Tensor rmsnorm(Tensor x, Tensor w1p, double eps) {
+  CHECK_BF16(x);
+  const int H = x.size(-1);
+  auto x2 = x.reshape({-1, H});
+  TORCH_CHECK(x2.stride(1) == 1, "rmsnorm: inner dim must be contiguous");
+  Tensor out = at::empty({x2.size(0), H}, x.options());
+  LAUNCH(qb::rmsnorm(x2.data_ptr(), x2.stride(0), w1p.data_ptr<float>(), out.data_ptr(), H, x2.size(0), H, (float)eps,
+                     stream()));
+  return out.view(x.sizes());
+}
+
+void add_rmsnorm(Tensor x, Tensor res, Tensor w1p, Tensor out, double eps) {
+  CHECK_BF16(x);
+  CHECK_BF16(res);
+  const int H = x.size(-1);
+  TORCH_CHECK(res.is_contiguous() && out.is_contiguous(), "add_rmsnorm: residual/out must be contiguous");
+  TORCH_CHECK(x.stride(-1) == 1, "add_rmsnorm: x inner dim contiguous");
+  LAUNCH(qb::add_rmsnorm(x.data_ptr(), row_stride(x), res.data_ptr(), H, w1p.data_ptr<float>(), out.data_ptr(), H,
+                         res.numel() / H, H, (float)eps, stream()));
+}
+
+Tensor gated_rmsnorm(Tensor core, Tensor z, Tensor w, double eps) {
+  CHECK_BF16(core);
+  TORCH_CHECK(core.is_contiguous() && core.dim() == 3, "gated_rmsnorm: core [T, heads, dv] contiguous");
+  TORCH_CHECK(z.dim() == 3 && z.stride(2) == 1 && z.stride(1) == z.size(2), "gated_rmsnorm: z [T, heads, dv] view");
+  Tensor out = at::empty_like(core);
+  LAUNCH(qb::gated_rmsnorm(core.data_ptr(), z.data_ptr(), z.stride(0), w.data_ptr(), out.data_ptr(), core.size(0),
+                           core.size(1), core.size(2), (float)eps, stream()));
+  return out;
+}
+
+Tensor silu_mul(Tensor gu) {
+  CHECK_BF16(gu);
+  const int n = gu.size(-1) / 2;
+  Tensor out = at::empty({gu.size(0), n}, gu.options());
+  LAUNCH(qb::silu_mul(gu.data_ptr(), gu.stride(0), out.data_ptr(), n, gu.size(0), n, stream()));
+  return out;
+}
+
+Tensor embed(Tensor tok, Tensor table) {
+  TORCH_CHECK(tok.scalar_type() == at::kLong, "embed: int64 tokens");
+  Tensor out = at::empty({tok.size(0), table.size(1)}, table.options());
+  LAUNCH(qb::embed(tok.data_ptr<int64_t>(), table.data_ptr(), out.data_ptr(), tok.size(0), table.size(1), stream()));
+  return out;
+}
+
+std::tuple<Tensor, Tensor> argmax_rows(Tensor x) {
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "argmax_rows: [R, V] rows contiguous");
+  const int dt = x.scalar_type() == at::kBFloat16 ? qb::DT_BF16 : qb::DT_F32;
+  TORCH_CHECK(dt == qb::DT_F32 ? x.scalar_type() == at::kFloat : true, "argmax_rows: bf16 or fp32");
+  Tensor val = at::empty({x.size(0)}, x.options().dtype(at::kFloat));
+  Tensor idx = at::empty({x.size(0)}, x.options().dtype(at::kLong));
+  LAUNCH(qb::argmax_rows(x.data_ptr(), x.stride(0), dt, x.size(0), x.size(1), val.data_ptr<float>(),
+                         idx.data_ptr<int64_t>(), stream()));
+  return {val, idx};
+}
+
+Tensor sigmoid_gate_mul(Tensor x, Tensor g) {
+  CHECK_BF16(x);
+  Tensor out = at::empty({x.size(0), x.size(1)}, x.options());
+  LAUNCH(qb::sigmoid_gate_mul(x.data_ptr(), x.stride(0), g.data_ptr(), g.stride(0), out.data_ptr(), x.size(0),
+                              x.size(1), stream()));
+  return out;
+}
+
+Tensor shared_gate_combine(Tensor routed, Tensor shared, Tensor gl) {
+  CHECK_BF16(routed);
+  TORCH_CHECK(routed.is_contiguous() && shared.is_contiguous(), "shared_gate_combine: contiguous inputs");
+  Tensor out = at::empty_like(routed);
+  LAUNCH(qb::shared_gate_combine(routed.data_ptr(), shared.data_ptr(), gl.data_ptr(), gl.stride(0), out.data_ptr(),
+                                 routed.size(0), routed.size(1), stream()));
+  return out;
+}
+
+std::tuple<Tensor, Tensor> router_topk2(Tensor logits, int64_t k) {
+  CHECK_BF16(logits);
+  const int T = logits.size(0), E = logits.size(1);
+  Tensor w = at::empty({T, k}, logits.options().dtype(at::kFloat));
+  Tensor idx = at::empty({T, k}, logits.options().dtype(at::kInt));
+  LAUNCH(qb::router_topk(logits.data_ptr(), logits.stride(0), T, E, k, w.data_ptr<float>(), idx.data_ptr<int>(),
+                         stream()));
+  return {w, idx};
+}
+
+// ------------------------------------------------------------------ attention
+Tensor qk_norm_rope_kv_write(Tensor q, Tensor k, Tensor v, Tensor qn, Tensor kn, Tensor pos, Tensor rows, Tensor kc,
+                             Tensor vc, int64_t rot, double theta, double eps) {
+  CHECK_BF16(q);
+  const int T = q.size(0), nq = q.size(1), hd = q.size(2), nkv = k.size(1);
+  const auto* base = reinterpret_cast<const char*>(q.data_ptr());
+  TORCH_CHECK(q.stride(0) == k.stride(0) && k.stride(0) == v.stride(0), "qk_norm_rope: q/k/v must be views of one row");
+  TORCH_CHECK(reinterpret_cast<const char*>(k.data_ptr()) == base + (long)nq * 2 * hd * 2 &&
+                  reinterpret_cast<const char*>(v.data_ptr()) == base + ((long)nq * 2 * hd + (long)nkv * hd) * 2,
+              "qk_norm_rope: expected the fused [q|gate]*nq, k*nkv, v*nkv row layout");
+  TORCH_CHECK(kc.is_contiguous() && vc.is_contiguous(), "qk_norm_rope: caches contiguous");
+  Tensor qout = at::empty({T, nq, hd}, q.options());
+  LAUNCH(qb::qk_norm_rope_kv_write(q.data_ptr(), q.stride(0), nq, nkv, hd, qn.data_ptr<float>(), kn.data_ptr<float>(),
+                                   pos.data_ptr<int>(), rows.data_ptr<int>(), kc.data_ptr(), vc.data_ptr(),
+                                   qout.data_ptr(), T, rot, (float)theta, (float)eps, stream()));
+  return qout;
+}
+
+Tensor attention_varlen(Tensor q, Tensor kc, Tensor vc, Tensor table, Tensor seg_lane, Tensor cu, Tensor pos,
+                        int64_t block_size, int64_t max_ctx) {
+  CHECK_BF16(q);
+  TORCH_CHECK(q.is_contiguous(), "attention: q contiguous [T, nq, hd]");
+  const int T = q.size(0), nq = q.size(1), hd = q.size(2), nkv = kc.size(1);
+  const int S = seg_lane.size(0);
+  int dev_sms = 148;
+  // splits: enough CTAs to fill the GPU twice, at least 64 keys per split
+  long base_ctas = (long)T * nkv;
+  int splits = (int)((2L * dev_sms + base_ctas - 1) / base_ctas);
+  int max_splits = (int)((max_ctx + 63) / 64);
+  if (splits > max_splits) splits = max_splits;
+  if (splits < 1) splits = 1;
+  if (splits > 64) splits = 64;
+  Tensor out = at::empty_like(q);
+  Tensor ws;
+  if (splits > 1) ws = at::empty({(long)T * nq * splits * (hd + 2)}, q.options().dtype(at::kFloat));
+  LAUNCH(qb::attention_varlen(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), table.data_ptr<int>(), table.size(1),
+                              pos.data_ptr<int>(), seg_lane.data_ptr<int>(), cu.data_ptr<int>(), S, T, nq, nkv, hd,
+                              block_size, splits, splits > 1 ? ws.data_ptr<float>() : nullptr, out.data_ptr(),
+                              stream()));
+  return out;
+}
+
+// ------------------------------------------------------------------ deltanet
+Tensor causal_conv_varlen(Tensor x, Tensor state, Tensor w, Tensor seg_lane, Tensor cu) {
+  CHECK_BF16(x);
+  TORCH_CHECK(state.stride(2) == 1 && state.stride(1) == state.size(2), "conv: state [lanes, C, K-1] rows contiguous");
+  const int T = x.size(0), C = x.size(1), K = w.size(1);
+  Tensor out = at::empty({T, C}, x.options());
+  LAUNCH(qb::causal_conv_varlen(x.data_ptr(), x.stride(0), state.data_ptr(), state.stride(0), w.data_ptr(),
+                                seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), C, K, out.data_ptr(),
+                                stream()));
+  return out;
+}
+
+Tensor gated_delta_varlen(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, Tensor state, Tensor seg_lane,
+                          Tensor cu, int64_t nk, int64_t nv, int64_t dk, int64_t dv) {
+  CHECK_BF16(qkv);
+  TORCH_CHECK(state.scalar_type() == at::kFloat, "delta: fp32 state");
+  TORCH_CHECK(state.stride(3) == 1 && state.stride(2) == dv && state.stride(1) == dk * dv, "delta: state layout");
+  const int T = qkv.size(0);
+  Tensor out = at::empty({T, nv, dv}, qkv.options());
+  LAUNCH(qb::gated_delta_varlen(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0), a_log.data_ptr<float>(),
+                                dt_bias.data_ptr<float>(), state.data_ptr<float>(), state.stride(0),
+                                seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), nk, nv, dk, dv,
+                                out.data_ptr(), stream()));
+  return out;
+}
+
+// ------------------------------------------------------------------ moe
+Tensor moe_routed_impl(Tensor h, Tensor topw, Tensor topi, Tensor w13, c10::optional<Tensor> s13, Tensor w2,
+                       c10::optional<Tensor> s2, int64_t first, int64_t count) {
+  CHECK_BF16(h);
+  TORCH_CHECK(h.is_contiguous(), "moe: h contiguous");
+  const int T = h.size(0), H = h.size(1), k = topi.size(1);
+  const bool fp4 = s13.has_value();
+  const int n13 = w13.size(1);  // 2I
+  const int I = n13 / 2;
+  const int cap = T * k;
+  auto i32 = h.options().dtype(at::kInt);
+  Tensor meta = at::empty({2 * count + 2 * cap + cap + 1}, i32);
+  int* counts = meta.data_ptr<int>();
+  int* offsets = counts + count;
+  int* perm_tok = offsets + count;
+  int* perm_slot = perm_tok + cap;
+  int* inv = perm_slot + cap;
+  int* n_assign = inv + cap;
+  Tensor topi_c = topi.contiguous();
+  Tensor out = at::empty_like(h);
+  if (T == 0) return out;
+  LAUNCH(qb::moe_dispatch(topi_c.data_ptr<int>(), T, k, first, count, counts, offsets, perm_tok, perm_slot, inv,
+                          n_assign, stream()));
+  if (fp4) {
+    Tensor xh = at::empty({cap, H}, h.options().dtype(at::kHalf));
+    Tensor inter = at::empty({cap, I}, h.options().dtype(at::kHalf));
+    Tensor y2 = at::empty({cap, H}, h.options());
+    LAUNCH(qb::moe_gather_f16(h.data_ptr(), perm_tok, n_assign, cap, H, xh.data_ptr(), stream()));
+    LAUNCH(qb::moe_expert_gemm(xh.data_ptr(), H, w13.data_ptr<uint8_t>(), s13->data_ptr<uint8_t>(), n13, H, 0, 0,
+                               offsets, counts, count, cap, 1, inter.data_ptr(), I, err_ptr(h), stream(), 0));
+    LAUNCH(qb::moe_expert_gemm(inter.data_ptr(), I, w2.data_ptr<uint8_t>(), s2->data_ptr<uint8_t>(), H, I, 0, 0,
+                               offsets, counts, count, cap, 0, y2.data_ptr(), H, err_ptr(h), stream(), 0));
+    LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream()));
+  } else {
+    TORCH_CHECK(false, "moe: bf16 experts not supported on this path yet");
+  }
+  return out;
+}
+
+Tensor moe_routed_fp4(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13, Tensor w2, Tensor s2, int64_t first,
+                      int64_t count) {
+  return moe_routed_impl(h, topw, topi, w13, s13, w2, s2, first, count);
+}
+
+// ------------------------------------------------------------------ status
+Tensor status(Tensor like) { return status_tensor(like.device()).clone(); }
+void clear_status(Tensor like) { status_tensor(like.device()).zero_(); }
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("linear", &linear, "Y = X W^T on tcgen05", py::arg("x"), py::arg("w"), py::arg("out") = py::none());
+  m.def("rmsnorm", &rmsnorm);
+  m.def("add_rmsnorm", &add_rmsnorm);
+  m.def("gated_rmsnorm", &gated_rmsnorm);
+  m.def("silu_mul", &silu_mul);
+  m.def("embed", &embed);
+  m.def("argmax_rows", &argmax_rows);
+  m.def("sigmoid_gate_mul", &sigmoid_gate_mul);
+  m.def("shared_gate_combine", &shared_gate_combine);
+  m.def("router_topk", &router_topk2);
+  m.def("qk_norm_rope_kv_write", &qk_norm_rope_kv_write);
+  m.def("attention_varlen", &attention_varlen);
+  m.def("causal_conv_varlen", &causal_conv_varlen);
+  m.def("gated_delta_varlen", &gated_delta_varlen);
+  m.def("moe_routed_fp4", &moe_routed_fp4);
+  m.def("status", &status);
+  m.def("clear_status", &clear_status);
+}

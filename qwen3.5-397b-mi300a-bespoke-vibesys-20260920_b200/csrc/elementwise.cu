@@ -1,0 +1,402 @@
+// Norms, activations, embedding, greedy argmax, router top-k and the attention prologue
+// (q/k RMSNorm + partial RoPE + paged KV write). Activations are bf16; every kernel keeps the
+// rounding points of the HuggingFace modeling code (an op whose PyTorch statement produces a
+// bf16 tensor rounds to bf16 at the same place here), so greedy decoding agrees with it.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qb {
+
+using bf16 = __nv_bfloat16;
+
+__device__ __forceinline__ float rbf(float x) { return __bfloat162float(__float2bfloat16(x)); }
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  v = warp_sum(v);
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  if (threadIdx.x < 32) {
+    t = threadIdx.x < NT / 32 ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+  }
+  __syncthreads();
+  t = red[0];
+  __syncthreads();
+  return t;
+}
+
+// ------------------------------------------------------------------ rmsnorm / add_rmsnorm
+constexpr int NORM_T = 256;
+constexpr int NORM_MAXV = 4;  // up to 4 x 8 elements per thread (H <= 8192)
+
+template <bool ADD>
+__global__ void __launch_bounds__(NORM_T) norm_kernel(const bf16* x, long ldx, bf16* res, long ldr, const float* w1p,
+                                                      bf16* out, long ldo, int H, float eps) {
+  __shared__ float red[32];
+  const long r = blockIdx.x;
+  const bf16* xr = x + r * ldx;
+  bf16* rr = ADD ? res + r * ldr : nullptr;
+  float v[NORM_MAXV][8];
+  float ss = 0.f;
+  const int nvec = H / 8;
+#pragma unroll
+  for (int i = 0; i < NORM_MAXV; ++i) {
+    const int vi = threadIdx.x + i * NORM_T;
+    if (vi < nvec) {
+      uint4 raw = *reinterpret_cast<const uint4*>(xr + vi * 8);
+      const bf16* e = reinterpret_cast<const bf16*>(&raw);
+      if (ADD) {
+        uint4 rraw = *reinterpret_cast<const uint4*>(rr + vi * 8);
+        const bf16* re = reinterpret_cast<const bf16*>(&rraw);
+        uint4 o;
+        bf16* oe = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          oe[j] = __float2bfloat16(__bfloat162float(re[j]) + __bfloat162float(e[j]));
+          v[i][j] = __bfloat162float(oe[j]);
+        }
+        *reinterpret_cast<uint4*>(rr + vi * 8) = o;
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) v[i][j] = __bfloat162float(e[j]);
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) ss += v[i][j] * v[i][j];
+    }
+  }
+  const float tot = block_sum<NORM_T>(ss, red);
+  const float inv = rsqrtf(tot / H + eps);
+  bf16* orow = out + r * ldo;
+#pragma unroll
+  for (int i = 0; i < NORM_MAXV; ++i) {
+    const int vi = threadIdx.x + i * NORM_T;
+    if (vi < nvec) {
+      uint4 o;
+      bf16* oe = reinterpret_cast<bf16*>(&o);
+      const float4 w0 = *reinterpret_cast<const float4*>(w1p + vi * 8);
+      const float4 w1 = *reinterpret_cast<const float4*>(w1p + vi * 8 + 4);
+      const float wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oe[j] = __float2bfloat16(v[i][j] * inv * wv[j]);
+      *reinterpret_cast<uint4*>(orow + vi * 8) = o;
+    }
+  }
+}
+
+int rmsnorm(const void* x, long ldx, const float* w1p, void* out, long ldo, int rows, int H, float eps,
+            cudaStream_t s) {
+  if (H % 8 || H > NORM_T * NORM_MAXV * 8) return -1;
+  if (rows == 0) return 0;
+  norm_kernel<false><<<rows, NORM_T, 0, s>>>((const bf16*)x, ldx, nullptr, 0, w1p, (bf16*)out, ldo, H, eps);
+  return (int)cudaGetLastError();
+}
+
+int add_rmsnorm(const void* x, long ldx, void* res, long ldr, const float* w1p, void* out, long ldo, int rows, int H,
+                float eps, cudaStream_t s) {
+  if (H % 8 || H > NORM_T * NORM_MAXV * 8) return -1;
+  if (rows == 0) return 0;
+  norm_kernel<true><<<rows, NORM_T, 0, s>>>((const bf16*)x, ldx, (bf16*)res, ldr, w1p, (bf16*)out, ldo, H, eps);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ gated rmsnorm (DeltaNet)
+// One warp per (token, head): y = bf16(w * bf16(norm(x))) * silu(z), rounded to bf16.
+__global__ void gated_rmsnorm_kernel(const bf16* core, const bf16* z, long ldz, const bf16* w, bf16* out, int T,
+                                     int heads, int dv, float eps) {
+  const long gw = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (gw >= (long)T * heads) return;
+  const long t = gw / heads;
+  const int h = gw % heads;
+  const bf16* xr = core + gw * dv;
+  const bf16* zr = z + t * ldz + (long)h * dv;
+  float ss = 0.f;
+  for (int i = lane; i < dv; i += 32) {
+    float v = __bfloat162float(xr[i]);
+    ss += v * v;
+  }
+  ss = warp_sum(ss);
+  const float inv = rsqrtf(ss / dv + eps);
+  bf16* orow = out + gw * dv;
+  for (int i = lane; i < dv; i += 32) {
+    float y = rbf(__bfloat162float(xr[i]) * inv);
+    y = rbf(__bfloat162float(w[i]) * y);
+    float zz = __bfloat162float(zr[i]);
+    orow[i] = __float2bfloat16(y * (zz / (1.f + expf(-zz))));
+  }
+}
+
+int gated_rmsnorm(const void* core, const void* z, long ldz_row, const void* w, void* out, int T, int heads, int dv,
+                  float eps, cudaStream_t s) {
+  const long warps = (long)T * heads;
+  if (!warps) return 0;
+  gated_rmsnorm_kernel<<<(warps + 7) / 8, 256, 0, s>>>((const bf16*)core, (const bf16*)z, ldz_row, (const bf16*)w,
+                                                       (bf16*)out, T, heads, dv, eps);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ small elementwise ops
+__global__ void silu_mul_kernel(const bf16* gu, long ldg, bf16* out, long ldo, int T, int n) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)T * n) return;
+  const long t = i / n;
+  const int c = i % n;
+  const float g = __bfloat162float(gu[t * ldg + c]), u = __bfloat162float(gu[t * ldg + n + c]);
+  // HF: act_fn(gate) (bf16) * up (bf16)
+  out[t * ldo + c] = __float2bfloat16(rbf(g / (1.f + expf(-g))) * u);
+}
+
+int silu_mul(const void* gu, long ldg, void* out, long ldo, int T, int n, cudaStream_t s) {
+  const long tot = (long)T * n;
+  if (!tot) return 0;
+  silu_mul_kernel<<<(tot + 255) / 256, 256, 0, s>>>((const bf16*)gu, ldg, (bf16*)out, ldo, T, n);
+  return (int)cudaGetLastError();
+}
+
+__global__ void embed_kernel(const int64_t* tok, const bf16* table, bf16* out, int H) {
+  const long t = blockIdx.x;
+  const int64_t id = tok[t];
+  const uint4* src = reinterpret_cast<const uint4*>(table + id * H);
+  uint4* dst = reinterpret_cast<uint4*>(out + t * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+int embed(const int64_t* tok, const void* table, void* out, int T, int H, cudaStream_t s) {
+  if (!T) return 0;
+  if (H % 8) return -1;
+  embed_kernel<<<T, 128, 0, s>>>(tok, (const bf16*)table, (bf16*)out, H);
+  return (int)cudaGetLastError();
+}
+
+template <typename T>
+__global__ void argmax_kernel(const T* x, long ldx, int V, float* val, int64_t* idx) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+  const long r = blockIdx.x;
+  const T* row = x + r * ldx;
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    float v = to_f<T>(row[i]);
+    if (v > bv || (v == bv && i < bi)) {
+      bv = v;
+      bi = i;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffff, bv, o);
+    int oi = __shfl_xor_sync(0xffffffff, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) {
+      bv = ov;
+      bi = oi;
+    }
+  }
+  const int w = threadIdx.x / 32, l = threadIdx.x % 32;
+  if (l == 0) {
+    sv[w] = bv;
+    si[w] = bi;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int j = 1; j < blockDim.x / 32; ++j)
+      if (sv[j] > bv || (sv[j] == bv && si[j] < bi)) {
+        bv = sv[j];
+        bi = si[j];
+      }
+    val[r] = bv;
+    idx[r] = bi;
+  }
+}
+
+int argmax_rows(const void* x, long ldx, int dtype, int R, int V, float* val, int64_t* idx, cudaStream_t s) {
+  if (!R) return 0;
+  if (dtype == DT_BF16)
+    argmax_kernel<bf16><<<R, 1024, 0, s>>>((const bf16*)x, ldx, V, val, idx);
+  else
+    argmax_kernel<float><<<R, 1024, 0, s>>>((const float*)x, ldx, V, val, idx);
+  return (int)cudaGetLastError();
+}
+
+__global__ void sigmoid_gate_mul_kernel(const bf16* x, long ldx, const bf16* g, long ldg, bf16* out, int T, int D) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)T * D) return;
+  const long t = i / D;
+  const int c = i % D;
+  const float gv = __bfloat162float(g[t * ldg + c]);
+  const float sg = rbf(1.f / (1.f + expf(-gv)));
+  out[t * D + c] = __float2bfloat16(__bfloat162float(x[t * ldx + c]) * sg);
+}
+
+int sigmoid_gate_mul(const void* x, long ldx, const void* g, long ldg, void* out, int T, int D, cudaStream_t s) {
+  const long tot = (long)T * D;
+  if (!tot) return 0;
+  sigmoid_gate_mul_kernel<<<(tot + 255) / 256, 256, 0, s>>>((const bf16*)x, ldx, (const bf16*)g, ldg, (bf16*)out, T,
+                                                            D);
+  return (int)cudaGetLastError();
+}
+
+__global__ void shared_gate_combine_kernel(const bf16* routed, const bf16* shared, const bf16* gl, long ldgl,
+                                           bf16* out, int T, int H) {
+  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long)T * H) return;
+  const long t = i / H;
+  const float g = __bfloat162float(gl[t * ldgl]);
+  const float sg = rbf(1.f / (1.f + expf(-g)));
+  const float sh = rbf(sg * __bfloat162float(shared[i]));
+  out[i] = __float2bfloat16(__bfloat162float(routed[i]) + sh);
+}
+
+int shared_gate_combine(const void* routed, const void* shared, const void* gl, long ldgl, void* out, int T, int H,
+                        cudaStream_t s) {
+  const long tot = (long)T * H;
+  if (!tot) return 0;
+  shared_gate_combine_kernel<<<(tot + 255) / 256, 256, 0, s>>>((const bf16*)routed, (const bf16*)shared,
+                                                               (const bf16*)gl, ldgl, (bf16*)out, T, H);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ attention prologue
+// One CTA per token. Each warp normalises one head at a time (q heads then k heads):
+// RMSNorm(1+w) over head_dim -> bf16, then rotate-half RoPE on the first `rot` dims with the
+// HF rounding points (cos/sin rounded to bf16, each product and the sum rounded to bf16).
+// k heads and the v heads are written to the paged cache at physical row rows[t].
+__global__ void qk_norm_rope_kernel(const bf16* qkv, long ldqkv, int nq, int nkv, int hd, const float* qn,
+                                    const float* kn, const int* pos, const int* rows, bf16* kc, bf16* vc, bf16* qout,
+                                    int rot, float theta, float eps) {
+  extern __shared__ float sh[];  // [warps][hd] normalised head + [rot/2] cos + [rot/2] sin
+  const int t = blockIdx.x;
+  const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int half = rot / 2;
+  float* cs = sh + warps * hd;
+  float* sn = cs + half;
+  const float p = (float)pos[t];
+  for (int j = threadIdx.x; j < half; j += blockDim.x) {
+    const float inv = 1.0f / powf(theta, (float)(2 * j) / (float)rot);
+    const float f = p * inv;
+    cs[j] = rbf(cosf(f));
+    sn[j] = rbf(sinf(f));
+  }
+  __syncthreads();
+  const bf16* row = qkv + (long)t * ldqkv;
+  const long prow = rows[t];
+  float* buf = sh + w * hd;
+  for (int hh = w; hh < nq + nkv; hh += warps) {
+    const bool isq = hh < nq;
+    const bf16* src = isq ? row + (long)hh * 2 * hd : row + (long)nq * 2 * hd + (long)(hh - nq) * hd;
+    const float* wt = isq ? qn : kn;
+    float ss = 0.f;
+    for (int i = lane; i < hd; i += 32) {
+      float v = __bfloat162float(src[i]);
+      buf[i] = v;
+      ss += v * v;
+    }
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / hd + eps);
+    for (int i = lane; i < hd; i += 32) buf[i] = rbf(buf[i] * inv * wt[i]);
+    __syncwarp();
+    bf16* dst = isq ? qout + ((long)t * nq + hh) * hd : kc + (prow * nkv + (hh - nq)) * hd;
+    for (int i = lane; i < hd; i += 32) {
+      float o;
+      if (i < rot) {
+        const int j = i < half ? i : i - half;
+        const float rh = i < half ? -buf[i + half] : buf[i - half];
+        o = rbf(rbf(buf[i] * cs[j]) + rbf(rh * sn[j]));
+      } else {
+        o = buf[i];
+      }
+      dst[i] = __float2bfloat16(o);
+    }
+    __syncwarp();
+  }
+  // values: plain copy into the paged cache
+  const bf16* vsrc = row + (long)nq * 2 * hd + (long)nkv * hd;
+  bf16* vdst = vc + prow * nkv * hd;
+  for (int i = threadIdx.x; i < nkv * hd; i += blockDim.x) vdst[i] = vsrc[i];
+}
+
+int qk_norm_rope_kv_write(const void* qkv, long ldqkv, int nq, int nkv, int hd, const float* qn, const float* kn,
+                          const int* pos, const int* rows, void* kc, void* vc, void* qout, int T, int rot,
+                          float theta, float eps, cudaStream_t s) {
+  if (!T) return 0;
+  const int threads = 256, warps = threads / 32;
+  const size_t smem = (size_t)(warps * hd + rot) * sizeof(float);
+  qk_norm_rope_kernel<<<T, threads, smem, s>>>((const bf16*)qkv, ldqkv, nq, nkv, hd, qn, kn, pos, rows, (bf16*)kc,
+                                               (bf16*)vc, (bf16*)qout, rot, theta, eps);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ router softmax + top-k
+// One warp per token: fp32 softmax over E experts, k rounds of arg-max (ties -> lower
+// expert index), renormalised weights.
+__global__ void router_topk_kernel(const bf16* logits, long ld, int T, int E, int k, float* wout, int* iout) {
+  const long t = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int lane = threadIdx.x % 32;
+  if (t >= T) return;
+  constexpr int MAXPER = 32;  // E <= 1024
+  float p[MAXPER];
+  const int per = (E + 31) / 32;
+  const bf16* row = logits + t * ld;
+  float m = -INFINITY;
+  for (int i = 0; i < per; ++i) {
+    const int e = lane + 32 * i;
+    p[i] = e < E ? __bfloat162float(row[e]) : -INFINITY;
+    m = fmaxf(m, p[i]);
+  }
+  m = warp_max(m);
+  float s = 0.f;
+  for (int i = 0; i < per; ++i) {
+    p[i] = (lane + 32 * i) < E ? expf(p[i] - m) : 0.f;
+    s += p[i];
+  }
+  s = warp_sum(s);
+  const float invs = 1.f / s;
+  for (int i = 0; i < per; ++i) p[i] = (lane + 32 * i) < E ? p[i] * invs : -1.f;
+  float tw[16];
+  int ti[16];
+  float tot = 0.f;
+  for (int r = 0; r < k; ++r) {
+    float bv = -2.f;
+    int bi = 0x7fffffff;
+    for (int i = 0; i < per; ++i) {
+      const int e = lane + 32 * i;
+      if (p[i] > bv || (p[i] == bv && e < bi)) {
+        bv = p[i];
+        bi = e;
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffff, bv, o);
+      int oi = __shfl_xor_sync(0xffffffff, bi, o);
+      if (ov > bv || (ov == bv && oi < bi)) {
+        bv = ov;
+        bi = oi;
+      }
+    }
+    tw[r] = bv;
+    ti[r] = bi;
+    tot += bv;
+    if ((bi % 32) == lane) p[bi / 32] = -1.f;
+  }
+  if (lane == 0) {
+    for (int r = 0; r < k; ++r) {
+      // renormalised weight, rounded through the logits dtype like the reference (.to(bf16))
+      wout[t * k + r] = rbf(tw[r] / tot);
+      iout[t * k + r] = ti[r];
+    }
+  }
+}
+
+int router_topk(const void* logits, long ld, int T, int E, int k, float* w, int* idx, cudaStream_t s) {
+  if (!T) return 0;
+  if (E > 1024 || k > 16) return -1;
+  router_topk_kernel<<<(T + 7) / 8, 256, 0, s>>>((const bf16*)logits, ld, T, E, k, w, idx);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace qb

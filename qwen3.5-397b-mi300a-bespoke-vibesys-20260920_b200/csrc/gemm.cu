@@ -1,0 +1,297 @@
+// Dense GEMM on the 5th-generation tensor cores: Y[T, N] = X[T, K] @ W[N, K]^T.
+//
+// Weight-stationary orientation ("swap AB"): the weight tile is the 128-row MMA A operand and
+// the token tile is the N operand (16..256 wide). Decode batches (T <= 64) then use a narrow N
+// instead of padding tokens to 128, and every weight byte is streamed exactly once per tile.
+//
+// One persistent CTA per SM, 6 warps:
+//   warp 0      TMA producer: 128x64 weight tile + BNx64 token tile per stage (128B swizzle)
+//   warp 1      TMEM allocator and MMA issuer (one elected lane, tcgen05.mma kind::f16)
+//   warps 2..5  epilogue: tcgen05.ld of the fp32 accumulator, optional fused activation,
+//               transpose through shared memory, 16-byte coalesced stores of Y rows
+// The accumulator is double buffered in TMEM (2 x BN columns), so the epilogue of one tile
+// overlaps the MMAs of the next. All waits are bounded (see common.cuh).
+#include "common.cuh"
+#include "kernels.h"
+#include <cudaTypedefs.h>
+
+namespace qb {
+
+constexpr int GEMM_THREADS = 192;
+constexpr int BK = 64;  // K elements per stage (one 128-byte swizzle atom of 16-bit values)
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int A_BYTES = 128 * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE = A_BYTES + B_BYTES;
+  static constexpr int STAGING = 32 * 128 * 2;  // 32 token columns x 128 weight rows, 16-bit
+  static constexpr int STAGES = (200 * 1024 - STAGING) / STAGE > 8 ? 8 : (200 * 1024 - STAGING) / STAGE;
+  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + STAGING + 256;
+};
+
+struct GemmArgs {
+  void* y;
+  long ldy;
+  int T, N, K;
+  int act;  // 0: none, 1: silu(g)*u over row pairs (g rows [0,64), u rows [64,128) of each tile)
+  int* err;
+};
+
+template <int BN, typename OutT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_ws_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GemmArgs a,
+                   uint32_t idesc) {
+  using C = GemmCfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint16_t* staging = reinterpret_cast<uint16_t*>(smem + C::STAGES * C::STAGE);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + C::STAGES * C::STAGE + C::STAGING);
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued_p = const_cast<int*>(abort_flag) + 1;
+  int* consumed_p = issued_p + 1;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_tiles = (a.N + 127) / 128;
+  const int t_tiles = (a.T + BN - 1) / BN;
+  const int tiles = n_tiles * t_tiles;
+  const int kblocks = (a.K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *issued_p = 0;
+    *consumed_p = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (elect_one()) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+        const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) break;
+          uint8_t* st = stages + s * C::STAGE;
+          mbar_expect_tx(&full[s], C::STAGE);
+          tma_load_2d(st, &tmW, &full[s], kb * BK, n0);
+          tma_load_2d(st + C::A_BYTES, &tmX, &full[s], kb * BK, t0);
+          *issued_p = it + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      int it = 0, ti = 0;
+      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++ti) {
+        const int acc = ti & 1;
+        if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = smem_u32(stages + s * C::STAGE);
+          const uint64_t da = desc_sw128(sa), db = desc_sw128(sa + C::A_BYTES);
+#pragma unroll
+          for (int kk = 0; kk < BK / 16; ++kk) {
+            // +32 bytes per 16-element K step inside the swizzle atom (>>4 in the descriptor)
+            mma_f16_ss(d, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0);
+          }
+          mma_commit(&empty[s]);
+          *consumed_p = it + 1;
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+      }
+      // make sure no MMA is still writing TMEM when the CTA tears down
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err, ERR_DRAIN, nullptr);
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue (128 threads)
+    const int ew = warp & 3;             // TMEM lane quarter this warp may access
+    const int row = ew * 32 + lane;      // accumulator row = weight row within the tile
+    const int et = threadIdx.x - 64;     // 0..127
+    OutT* Y = reinterpret_cast<OutT*>(a.y);
+    int ti = 0;
+    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
+      const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
+      const int acc = ti & 1;
+      if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) break;
+      tc_fence_after();
+      constexpr int CH = BN < 32 ? BN : 32;
+      for (int c0 = 0; c0 < BN; c0 += CH) {
+        float v[32];
+        const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
+        if constexpr (CH == 32) tmem_ld32(taddr, v); else tmem_ld16(taddr, v);
+        // staging[j][row]: token column j, weight row `row`
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+          OutT o = from_f<OutT>(v[j]);
+          staging[j * 128 + row] = *reinterpret_cast<uint16_t*>(&o);
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (a.act == 1) {
+          // silu(gate) * up: rows [0,64) are gate rows, [64,128) the matching up rows;
+          // output columns are n0/2 .. n0/2 + 64
+          for (int idx = et; idx < CH * 64; idx += 128) {
+            const int j = idx / 64, r = idx % 64;
+            const int t = t0 + c0 + j, n = n0 / 2 + r;
+            if (t < a.T && n < a.N / 2) {
+              uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
+              float g = to_f<OutT>(*reinterpret_cast<OutT*>(&gb)), u = to_f<OutT>(*reinterpret_cast<OutT*>(&ub));
+              Y[(long)t * a.ldy + n] = from_f<OutT>(silu(g) * u);
+            }
+          }
+        } else {
+          // 16-byte vectors: each token row of the chunk is 128 outputs = 16 vectors
+          for (int idx = et; idx < CH * 16; idx += 128) {
+            const int j = idx / 16, q = idx % 16;
+            const int t = t0 + c0 + j, n = n0 + q * 8;
+            if (t < a.T) {
+              const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
+              OutT* dst = Y + (long)t * a.ldy + n;
+              if (n + 8 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+                *reinterpret_cast<uint4*>(dst) = val;
+              } else {
+                const uint16_t* e = reinterpret_cast<const uint16_t*>(&val);
+                for (int u = 0; u < 8 && n + u < a.N; ++u) reinterpret_cast<uint16_t*>(dst)[u] = e[u];
+              }
+            }
+          }
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    // drain TMA loads issued but never consumed before the shared memory goes away
+    for (int it = *consumed_p; it < *issued_p; ++it)
+      mbar_wait(&full[it % C::STAGES], (it / C::STAGES) & 1, a.err, ERR_DRAIN, nullptr);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D row-major [rows, cols] tensor of 16-bit (or 8-bit) elements, box [box_rows, box_cols].
+int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, long rows, long cols, long ld_elems,
+                 int box_rows, int box_cols, bool swizzle128) {
+  auto fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)(ld_elems * elem_bytes)};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUtensorMapDataType dt = elem_bytes == 2 ? CU_TENSOR_MAP_DATA_TYPE_UINT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8;
+  CUresult r = fn(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+static int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, typename OutT>
+static int launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, bool bf16, int max_ctas,
+                     cudaStream_t st) {
+  using C = GemmCfg<BN>;
+  auto k = gemm_ws_kernel<BN, OutT>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr = true;
+  }
+  const int tiles = ((a.N + 127) / 128) * ((a.T + BN - 1) / BN);
+  int grid = tiles < max_ctas ? tiles : max_ctas;
+  if (grid < 1) grid = 1;
+  k<<<grid, GEMM_THREADS, C::SMEM, st>>>(tw, tx, a, idesc_f16(128, BN, bf16));
+  return (int)cudaGetLastError();
+}
+
+int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
+            int act, int* err, cudaStream_t stream, int max_ctas) {
+  if (T <= 0 || N <= 0) return 0;
+  int BN = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  CUtensorMap tw, tx;
+  int r = make_tmap_2d(&tw, w, 2, N, K, ldw, 128, BK, true);
+  if (r) return 1000 + r;
+  r = make_tmap_2d(&tx, x, 2, T, K, ldx, BN, BK, true);
+  if (r) return 2000 + r;
+  GemmArgs a{y, ldy, T, N, K, act, err};
+  if (max_ctas <= 0) max_ctas = num_sms();
+  switch (BN) {
+    case 16: return bf16 ? launch_bn<16, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)
+                         : launch_bn<16, __half>(tw, tx, a, bf16, max_ctas, stream);
+    case 32: return bf16 ? launch_bn<32, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)
+                         : launch_bn<32, __half>(tw, tx, a, bf16, max_ctas, stream);
+    case 64: return bf16 ? launch_bn<64, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)
+                         : launch_bn<64, __half>(tw, tx, a, bf16, max_ctas, stream);
+    case 128: return bf16 ? launch_bn<128, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)
+                          : launch_bn<128, __half>(tw, tx, a, bf16, max_ctas, stream);
+    default: return bf16 ? launch_bn<256, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)
+                         : launch_bn<256, __half>(tw, tx, a, bf16, max_ctas, stream);
+  }
+}
+
+}  // namespace qb

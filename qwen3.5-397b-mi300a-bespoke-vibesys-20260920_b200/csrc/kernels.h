@@ -1,0 +1,59 @@
+// Host-side launchers of every kernel in csrc/ (raw pointers, element strides, a stream).
+// The torch bindings (bindings.cpp) validate tensors and call these. Each launcher returns
+// 0 on success or a CUDA / driver error code.
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace qb {
+
+// dtype codes used across launchers
+enum DType : int { DT_BF16 = 0, DT_F16 = 1, DT_F32 = 2 };
+
+int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, long rows, long cols, long ld_elems,
+                 int box_rows, int box_cols, bool swizzle128);
+
+// Y[T,N] = X[T,K] @ W[N,K]^T ; act 1 = silu(gate)*up over 64-row halves of each 128-row tile
+int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
+            int act, int* err, cudaStream_t stream, int max_ctas);
+
+int rmsnorm(const void* x, long ldx, const float* w1p, void* out, long ldo, int rows, int H, float eps,
+            cudaStream_t s);
+int add_rmsnorm(const void* x, long ldx, void* res, long ldr, const float* w1p, void* out, long ldo, int rows, int H,
+                float eps, cudaStream_t s);
+int gated_rmsnorm(const void* core, const void* z, long ldz_row, const void* w, void* out, int T, int heads, int dv,
+                  float eps, cudaStream_t s);
+int silu_mul(const void* gu, long ldg, void* out, long ldo, int T, int n, cudaStream_t s);
+int embed(const int64_t* tok, const void* table, void* out, int T, int H, cudaStream_t s);
+int argmax_rows(const void* x, long ldx, int dtype, int R, int V, float* val, int64_t* idx, cudaStream_t s);
+int sigmoid_gate_mul(const void* x, long ldx, const void* g, long ldg, void* out, int T, int D, cudaStream_t s);
+int shared_gate_combine(const void* routed, const void* shared, const void* gl, long ldgl, void* out, int T, int H,
+                        cudaStream_t s);
+int qk_norm_rope_kv_write(const void* qkv, long ldqkv, int nq, int nkv, int hd, const float* qn, const float* kn,
+                          const int* pos, const int* rows, void* kc, void* vc, void* qout, int T, int rot,
+                          float theta, float eps, cudaStream_t s);
+int causal_conv_varlen(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
+                       const int* cu, int S, int C, int K, void* out, cudaStream_t s);
+int gated_delta_varlen(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
+                       const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
+                       int S, int nk, int nv, int dk, int dv, void* out, cudaStream_t s);
+int attention_varlen(const void* q, const void* kc, const void* vc, const int* table, int max_blocks,
+                     const int* pos, const int* seg_lane, const int* cu, int S, int T, int nq, int nkv, int hd,
+                     int block_size, int splits, float* ws, void* out, cudaStream_t s);
+int router_topk(const void* logits, long ld, int T, int E, int k, float* w, int* idx, cudaStream_t s);
+
+// MoE: dispatch metadata + grouped MXFP4 expert GEMMs + combine
+int moe_dispatch(const int* topi, int T, int k, int first, int count, int* counts, int* offsets, int* perm_tok,
+                 int* perm_slot, int* inv, int* n_assign, cudaStream_t s);
+int moe_gather_f16(const void* h, const int* perm_tok, const int* n_assign, int cap, int H, void* xh,
+                   cudaStream_t s);
+int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8_t* ws, int n_rows, int k_cols,
+                    long w_expert_stride, long s_expert_stride, const int* offsets, const int* counts,
+                    int count, int cap, int act, void* out, int out_cols, int* err, cudaStream_t s, int max_ctas);
+int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s);
+int moe_expert_gemm_bf16(const void* xin, int in_cols, const void* w, int n_rows, int k_cols, long w_expert_stride,
+                         const int* offsets, const int* counts, int count, int cap, int act, void* out, int out_cols,
+                         cudaStream_t s);
+
+}  // namespace qb

@@ -1,0 +1,528 @@
+// Routed experts: dispatch metadata, token gather, grouped expert GEMMs on tcgen05 with the
+// MXFP4 weights decoded inside shared memory, and the weighted combine.
+//
+// MXFP4 -> tensor core: the packed e2m1 codes (two per byte, low nibble = even K) are brought
+// into shared memory by TMA exactly as stored (no dequantised weight ever touches HBM). Four
+// converter warps turn each 64-wide K slice of the 128-row weight tile into f16 with the
+// sm_100a hardware conversion `cvt.rn.f16x2.e2m1x2`, multiply by the block's e8m0 scale
+// (a power of two, exact in f16), and store it in the 128-byte-swizzled K-major layout the MMA
+// reads. Activations are gathered once per layer into an f16 copy (bf16 -> f16 is exact for
+// the normalised activations), so every product equals the bf16 reference product
+// `x_bf16 * dequant(w)`: `kind::f16` needs both operands in the same type.
+//
+// Warp roles (320 threads, one persistent CTA per SM):
+//   warp 0      TMA producer (raw fp4 tile, f16 token tile; e8m0 scales by bulk copy per unit)
+//   warp 1      TMEM allocator + MMA issuer
+//   warps 2..5  epilogue (silu(gate)*up for the gate_up GEMM, plain for down)
+//   warps 6..9  fp4 -> f16 converters (thread = weight row)
+// Work unit = (local expert, 128-row weight tile); each unit loops over its expert's token
+// tiles. For the gate_up GEMM a weight tile is 64 gate rows + the matching 64 up rows, so the
+// epilogue sees both halves of silu(g)*u in one accumulator.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qb {
+
+using bf16 = __nv_bfloat16;
+
+// ------------------------------------------------------------------ dispatch metadata
+// Counting sort of the (token, slot) assignments that hit local experts [first, first+count).
+__global__ void moe_dispatch_kernel(const int* topi, int T, int k, int first, int count, int* counts, int* offsets,
+                                    int* perm_tok, int* perm_slot, int* inv, int* n_assign) {
+  extern __shared__ int sh[];  // count counters + count cursors
+  int* cnt = sh;
+  int* cur = sh + count;
+  for (int e = threadIdx.x; e < count; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const int n = T * k;
+  for (int a = threadIdx.x; a < n; a += blockDim.x) {
+    const int e = topi[a] - first;
+    if (e >= 0 && e < count) atomicAdd(&cnt[e], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int run = 0;
+    for (int e = 0; e < count; ++e) {
+      cur[e] = run;
+      offsets[e] = run;
+      counts[e] = cnt[e];
+      run += cnt[e];
+    }
+    *n_assign = run;
+  }
+  __syncthreads();
+  for (int a = threadIdx.x; a < n; a += blockDim.x) {
+    const int e = topi[a] - first;
+    if (e >= 0 && e < count) {
+      const int p = atomicAdd(&cur[e], 1);
+      perm_tok[p] = a / k;
+      perm_slot[p] = a % k;
+      inv[a] = p;
+    } else {
+      inv[a] = -1;
+    }
+  }
+}
+
+int moe_dispatch(const int* topi, int T, int k, int first, int count, int* counts, int* offsets, int* perm_tok,
+                 int* perm_slot, int* inv, int* n_assign, cudaStream_t s) {
+  moe_dispatch_kernel<<<1, 1024, 2 * count * sizeof(int), s>>>(topi, T, k, first, count, counts, offsets, perm_tok,
+                                                                perm_slot, inv, n_assign);
+  return (int)cudaGetLastError();
+}
+
+// xh[a, :] = h[perm_tok[a], :] (bf16 -> f16, or bf16 copy when OUT_BF16)
+template <bool OUT_BF16>
+__global__ void moe_gather_kernel(const bf16* h, const int* perm_tok, const int* n_assign, int H, void* xh) {
+  const int a = blockIdx.x;
+  if (a >= *n_assign) return;
+  const bf16* src = h + (long)perm_tok[a] * H;
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(src + i);
+    if (OUT_BF16) {
+      *reinterpret_cast<uint4*>(reinterpret_cast<bf16*>(xh) + (long)a * H + i) = raw;
+    } else {
+      const bf16* e = reinterpret_cast<const bf16*>(&raw);
+      uint4 o;
+      __half* oe = reinterpret_cast<__half*>(&o);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) oe[j] = __float2half_rn(__bfloat162float(e[j]));
+      *reinterpret_cast<uint4*>(reinterpret_cast<__half*>(xh) + (long)a * H + i) = o;
+    }
+  }
+}
+
+int moe_gather_f16(const void* h, const int* perm_tok, const int* n_assign, int cap, int H, void* xh,
+                   cudaStream_t s) {
+  if (!cap) return 0;
+  moe_gather_kernel<false><<<cap, 128, 0, s>>>((const bf16*)h, perm_tok, n_assign, H, xh);
+  return (int)cudaGetLastError();
+}
+
+// out[t, :] = sum_j topw[t, j] * y2[inv[t, j], :] over local assignments (fp32, rounded once)
+__global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* topw, int k, int H, bf16* out) {
+  const long t = blockIdx.x;
+  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+    float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int j = 0; j < k; ++j) {
+      const int a = inv[t * k + j];
+      if (a < 0) continue;
+      const float w = topw[t * k + j];
+      const uint4 raw = *reinterpret_cast<const uint4*>(y2 + (long)a * H + i);
+      const bf16* e = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) acc[u] += w * __bfloat162float(e[u]);
+    }
+    uint4 o;
+    bf16* oe = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+    for (int u = 0; u < 8; ++u) oe[u] = __float2bfloat16(acc[u]);
+    *reinterpret_cast<uint4*>(out + t * H + i) = o;
+  }
+}
+
+int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s) {
+  if (!T) return 0;
+  moe_combine_kernel<<<T, 128, 0, s>>>((const bf16*)y2, inv, topw, k, H, (bf16*)out);
+  return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ grouped expert GEMM
+constexpr int MOE_THREADS = 320;
+constexpr int MBK = 64;
+
+template <int BN, bool FP4>
+struct MoeCfg {
+  static constexpr int RAW = FP4 ? 128 * MBK / 2 : 0;   // packed fp4 codes of the A tile
+  static constexpr int A = 128 * MBK * 2;                // f16/bf16 A tile (converted or TMA)
+  static constexpr int B = BN * MBK * 2;
+  static constexpr int STAGE = A + B + RAW;              // A first: keeps 1024-byte alignment
+  static constexpr int SCALE_MAX = 128 * 128;            // 128 rows x (K/32 <= 128) bytes
+  static constexpr int STAGING = 32 * 128 * 2;
+  static constexpr int BUDGET = 210 * 1024 - STAGING - (FP4 ? 2 * SCALE_MAX : 0);
+  static constexpr int STAGES = BUDGET / STAGE > 10 ? 10 : BUDGET / STAGE;
+  static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + STAGING + (FP4 ? 2 * SCALE_MAX : 0) + 512;
+};
+
+struct MoeArgs {
+  const uint8_t* scales;  // [E_local * n_rows, K/32] (FP4 only)
+  const int* offsets;
+  const int* counts;
+  void* out;
+  int out_cols;
+  int n_rows;  // weight rows per expert (2I for gate_up, H for down)
+  int K;
+  int count;   // local experts
+  int act;
+  int* err;
+};
+
+// Two e2m1 codes (one byte) -> f16x2; the low nibble becomes the low half.
+__device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
+  uint32_t r;
+  asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}" : "=r"(r) : "r"(byte));
+  return r;
+}
+
+template <int BN, bool FP4>
+__global__ void __launch_bounds__(MOE_THREADS, 1)
+    moe_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, MoeArgs a,
+                    uint32_t idesc) {
+  using C = MoeCfg<BN, FP4>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint16_t* staging = reinterpret_cast<uint16_t*>(smem + C::STAGES * C::STAGE);
+  uint8_t* sbuf = smem + C::STAGES * C::STAGE + C::STAGING;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbuf + (FP4 ? 2 * C::SCALE_MAX : 0));
+  uint64_t* full = bars;
+  uint64_t* conv = full + C::STAGES;
+  uint64_t* empty = conv + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* sc_full = acc_empty + 2;
+  uint64_t* sc_empty = sc_full + 2;
+  uint64_t* drain = sc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued_p = const_cast<int*>(abort_flag) + 1;
+  int* consumed_p = issued_p + 1;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_tiles = a.n_rows / 128;
+  const int units = a.count * n_tiles;
+  const int kblocks = a.K / MBK;
+  const int srow = a.K / 32;  // scale bytes per weight row
+  const bool gu = a.act == 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&conv[s], 128);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+      mbar_init(&sc_full[i], 1);
+      mbar_init(&sc_empty[i], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *issued_p = 0;
+    *consumed_p = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  // weight row (within the expert) of A-tile row r for tile nt
+  auto wrow = [&](int nt, int r) -> int {
+    return gu ? (r < 64 ? nt * 64 + r : a.n_rows / 2 + nt * 64 + (r - 64)) : nt * 128 + r;
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (elect_one()) {
+      int it = 0, ui = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        const int e = u / n_tiles, nt = u % n_tiles;
+        const int cnt = a.counts[e];
+        if (cnt == 0) continue;
+        const int off = a.offsets[e];
+        const long erow = (long)e * a.n_rows;
+        if (FP4) {
+          const int sb = ui & 1;
+          if (!mbar_wait(&sc_empty[sb], ((ui >> 1) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) break;
+          uint8_t* dst = sbuf + sb * C::SCALE_MAX;
+          const uint32_t half = 64 * srow;
+          mbar_expect_tx(&sc_full[sb], 2 * half);
+          const uint8_t* s0 = a.scales + (erow + wrow(nt, 0)) * srow;
+          const uint8_t* s1 = a.scales + (erow + wrow(nt, 64)) * srow;
+          asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                           smem_u32(dst)),
+                       "l"(s0), "r"(half), "r"(smem_u32(&sc_full[sb]))
+                       : "memory");
+          asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                           smem_u32(dst + half)),
+                       "l"(s1), "r"(half), "r"(smem_u32(&sc_full[sb]))
+                       : "memory");
+        }
+        ++ui;
+        for (int m0 = 0; m0 < cnt; m0 += BN) {
+          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            const int s = it % C::STAGES;
+            if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) goto prod_done;
+            uint8_t* st = stages + s * C::STAGE;
+            if (FP4) {
+              mbar_expect_tx(&full[s], C::RAW + C::B);
+              tma_load_2d(st + C::A + C::B, &tmW, &full[s], kb * MBK / 2, (int)(erow + wrow(nt, 0)));
+              tma_load_2d(st + C::A + C::B + C::RAW / 2, &tmW, &full[s], kb * MBK / 2, (int)(erow + wrow(nt, 64)));
+            } else {
+              mbar_expect_tx(&full[s], C::A + C::B);
+              tma_load_2d(st, &tmW, &full[s], kb * MBK, (int)(erow + wrow(nt, 0)));
+              tma_load_2d(st + C::A / 2, &tmW, &full[s], kb * MBK, (int)(erow + wrow(nt, 64)));
+            }
+            tma_load_2d(st + C::A, &tmX, &full[s], kb * MBK, off + m0);
+            *issued_p = it + 1;
+          }
+        }
+      }
+    prod_done:;
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      int it = 0, ti = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok && !*abort_flag; u += gridDim.x) {
+        const int e = u / n_tiles;
+        const int cnt = a.counts[e];
+        for (int m0 = 0; m0 < cnt && ok; m0 += BN, ++ti) {
+          const int acc = ti & 1;
+          if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + acc * BN;
+          for (int kb = 0; kb < kblocks; ++kb, ++it) {
+            const int s = it % C::STAGES;
+            uint64_t* ready = FP4 ? &conv[s] : &full[s];
+            if (!mbar_wait(ready, (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t sa = smem_u32(stages + s * C::STAGE);
+            const uint64_t da = desc_sw128(sa), db = desc_sw128(sa + C::A);
+#pragma unroll
+            for (int kk = 0; kk < MBK / 16; ++kk) mma_f16_ss(d, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0);
+            mma_commit(&empty[s]);
+            *consumed_p = it + 1;
+          }
+          if (!ok) break;
+          mma_commit(&acc_full[acc]);
+        }
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err, ERR_DRAIN, nullptr);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- epilogue
+    const int ew = warp & 3;
+    const int row = ew * 32 + lane;
+    const int et = threadIdx.x - 64;
+    int ti = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int e = u / n_tiles, nt = u % n_tiles;
+      const int cnt = a.counts[e];
+      const int off = a.offsets[e];
+      bool stop = false;
+      for (int m0 = 0; m0 < cnt; m0 += BN, ++ti) {
+        const int acc = ti & 1;
+        if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        constexpr int CH = BN < 32 ? BN : 32;
+        for (int c0 = 0; c0 < BN; c0 += CH) {
+          float v[32];
+          const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
+          if constexpr (CH == 32) tmem_ld32(taddr, v); else tmem_ld16(taddr, v);
+          // staging holds the fp32 accumulator rounded to bf16 (the reference rounding point)
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            bf16 o = __float2bfloat16(v[j]);
+            staging[j * 128 + row] = *reinterpret_cast<uint16_t*>(&o);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const int nvalid = min(CH, cnt - m0 - c0);
+          if (gu) {
+            __half* Y = reinterpret_cast<__half*>(a.out);
+            for (int idx = et; idx < CH * 64; idx += 128) {
+              const int j = idx / 64, r = idx % 64;
+              if (j < nvalid) {
+                uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
+                const float g = __bfloat162float(*reinterpret_cast<bf16*>(&gb));
+                const float uu = __bfloat162float(*reinterpret_cast<bf16*>(&ub));
+                const float sg = __bfloat162float(__float2bfloat16(g / (1.f + expf(-g))));
+                const float y = __bfloat162float(__float2bfloat16(sg * uu));
+                Y[(long)(off + m0 + c0 + j) * a.out_cols + nt * 64 + r] = __float2half_rn(y);
+              }
+            }
+          } else {
+            bf16* Y = reinterpret_cast<bf16*>(a.out);
+            for (int idx = et; idx < CH * 16; idx += 128) {
+              const int j = idx / 16, q = idx % 16;
+              if (j < nvalid) {
+                const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
+                *reinterpret_cast<uint4*>(Y + (long)(off + m0 + c0 + j) * a.out_cols + nt * 128 + q * 8) = val;
+              }
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+      }
+      if (stop) break;
+    }
+  } else if (FP4) {
+    // ---------------------------------------------------------------- fp4 -> f16 converters
+    const int r = threadIdx.x - 192;  // weight-tile row 0..127
+    int it = 0, ui = 0;
+    bool stop = false;
+    for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
+      const int e = u / n_tiles;
+      const int cnt = a.counts[e];
+      if (cnt == 0) continue;
+      const int sb = ui & 1;
+      if (!mbar_wait(&sc_full[sb], (ui >> 1) & 1, a.err, ERR_MMA_WAIT, abort_flag)) break;
+      const uint8_t* srw = sbuf + sb * C::SCALE_MAX + r * srow;
+      for (int m0 = 0; m0 < cnt && !stop; m0 += BN) {
+        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+            stop = true;
+            break;
+          }
+          uint8_t* st = stages + s * C::STAGE;
+          const uint4* raw = reinterpret_cast<const uint4*>(st + C::A + C::B + r * (MBK / 2));
+          const uint4 c0 = raw[0], c1 = raw[1];  // 64 codes = 2 scale blocks of 32
+          const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          uint8_t* arow = st + r * 128;  // SW128 row r: 16-byte chunk j stored at j ^ (r & 7)
+          // 64 codes = 8 chunks of 8 f16; chunk c comes from word c, scale block c / 4
+#pragma unroll
+          for (int chunk = 0; chunk < 8; ++chunk) {
+            const int blk = chunk / 4;
+            const int sexp = (int)srw[kb * 2 + blk] - 127;
+            const bool in_range = sexp >= -24 && sexp <= 15;
+            const __half2 sc2 = __half2half2(__float2half_rn(exp2f((float)sexp)));
+            const uint32_t w32 = words[chunk];  // 4 bytes = 8 codes = 8 f16 (16 bytes)
+            uint32_t outw[4];
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+              uint32_t h2 = e2m1x2_to_f16x2((w32 >> (8 * q)) & 0xff);
+              __half2 v = *reinterpret_cast<__half2*>(&h2);
+              if (in_range) {
+                v = __hmul2(v, sc2);
+              } else {
+                const float2 f = __half22float2(v);
+                const float sc = exp2f((float)sexp);
+                v = __floats2half2_rn(f.x * sc, f.y * sc);
+              }
+              outw[q] = *reinterpret_cast<uint32_t*>(&v);
+            }
+            *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) * 16)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
+          }
+          // make the generic-proxy shared-memory writes visible to the tensor core (async proxy)
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+          mbar_arrive(&conv[s]);
+        }
+      }
+      mbar_arrive(&sc_empty[sb]);
+      ++ui;
+    }
+  }
+
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    for (int it = *consumed_p; it < *issued_p; ++it)
+      mbar_wait(&full[it % C::STAGES], (it / C::STAGES) & 1, a.err, ERR_DRAIN, nullptr);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+static int moe_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN, bool FP4>
+static int moe_launch(const CUtensorMap& tw, const CUtensorMap& tx, const MoeArgs& a, int max_ctas,
+                      cudaStream_t st) {
+  using C = MoeCfg<BN, FP4>;
+  auto k = moe_gemm_kernel<BN, FP4>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr = true;
+  }
+  const int units = a.count * (a.n_rows / 128);
+  int grid = units < max_ctas ? units : max_ctas;
+  if (grid < 1) grid = 1;
+  k<<<grid, MOE_THREADS, C::SMEM, st>>>(tw, tx, a, idesc_f16(128, BN, !FP4));
+  return (int)cudaGetLastError();
+}
+
+static int pick_bn(int cap, int count) {
+  const int avg = (cap + count - 1) / (count > 0 ? count : 1);
+  return avg <= 16 ? 16 : avg <= 32 ? 32 : avg <= 64 ? 64 : 128;
+}
+
+int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8_t* ws, int n_rows, int k_cols,
+                    long w_expert_stride, long s_expert_stride, const int* offsets, const int* counts, int count,
+                    int cap, int act, void* out, int out_cols, int* err, cudaStream_t s, int max_ctas) {
+  if (!cap || !count) return 0;
+  if (n_rows % 128 || k_cols % MBK || k_cols / 32 > 128) return -1;
+  (void)w_expert_stride;
+  (void)s_expert_stride;
+  const int BN = pick_bn(cap, count);
+  CUtensorMap tw, tx;
+  int r = make_tmap_2d(&tw, wq, 1, (long)count * n_rows, k_cols / 2, k_cols / 2, 64, MBK / 2, false);
+  if (r) return 1000 + r;
+  r = make_tmap_2d(&tx, xin, 2, cap, k_cols, in_cols, BN, MBK, true);
+  if (r) return 2000 + r;
+  MoeArgs a{ws, offsets, counts, out, out_cols, n_rows, k_cols, count, act, err};
+  if (max_ctas <= 0) max_ctas = moe_sms();
+  switch (BN) {
+    case 16: return moe_launch<16, true>(tw, tx, a, max_ctas, s);
+    case 32: return moe_launch<32, true>(tw, tx, a, max_ctas, s);
+    case 64: return moe_launch<64, true>(tw, tx, a, max_ctas, s);
+    default: return moe_launch<128, true>(tw, tx, a, max_ctas, s);
+  }
+}
+
+int moe_expert_gemm_bf16(const void* xin, int in_cols, const void* w, int n_rows, int k_cols, long w_expert_stride,
+                         const int* offsets, const int* counts, int count, int cap, int act, void* out, int out_cols,
+                         cudaStream_t s) {
+  if (!cap || !count) return 0;
+  if (n_rows % 128 || k_cols % MBK) return -1;
+  (void)w_expert_stride;
+  const int BN = pick_bn(cap, count);
+  CUtensorMap tw, tx;
+  int r = make_tmap_2d(&tw, w, 2, (long)count * n_rows, k_cols, k_cols, 64, MBK, true);
+  if (r) return 1000 + r;
+  r = make_tmap_2d(&tx, xin, 2, cap, k_cols, in_cols, BN, MBK, true);
+  if (r) return 2000 + r;
+  MoeArgs a{nullptr, offsets, counts, out, out_cols, n_rows, k_cols, count, act, nullptr};
+  const int mc = moe_sms();
+  switch (BN) {
+    case 16: return moe_launch<16, false>(tw, tx, a, mc, s);
+    case 32: return moe_launch<32, false>(tw, tx, a, mc, s);
+    case 64: return moe_launch<64, false>(tw, tx, a, mc, s);
+    default: return moe_launch<128, false>(tw, tx, a, mc, s);
+  }
+}
+
+}  // namespace qb

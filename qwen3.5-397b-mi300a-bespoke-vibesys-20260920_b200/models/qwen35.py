@@ -57,6 +57,7 @@ class StepInputs:
     seg_lane_h: list[int]
     cu_h: list[int]
     seg_start_h: list[int]
+    max_ctx: int = 0
 
 
 class Model:
@@ -223,7 +224,8 @@ class Model:
         cu_d = packed[o:o + s + 1]; o += s + 1  # noqa: E702
         seg_start = packed[o:o + s]
         self._sync_tables()
-        return StepInputs(tok, positions, prow, seg_lane, cu_d, seg_start, lr, lanes, cu, starts)
+        max_ctx = max(st + (cu[i + 1] - cu[i]) for i, st in enumerate(starts))
+        return StepInputs(tok, positions, prow, seg_lane, cu_d, seg_start, lr, lanes, cu, starts, max_ctx)
 
     # ================================================================== layers
     def _deltanet(self, i: int, L: dict, h: torch.Tensor, b: StepInputs) -> torch.Tensor:
@@ -259,7 +261,7 @@ class Model:
                                       self.k_cache[j], self.v_cache[j], cfg.rotary_dim, theta, cfg.eps)
         o = ops.attention_varlen(q, self.k_cache[j], self.v_cache[j], self.table_dev, b.seg_lane, b.cu,
                                  b.seg_start, self.block_size, b.seg_lane_h, b.cu_h, b.seg_start_h,
-                                 self.tables if h.device.type == "cpu" else None)
+                                 self.tables if h.device.type == "cpu" else None, b.positions, b.max_ctx)
         o = ops.sigmoid_gate_mul(o.reshape(t, nq * hd), gate.reshape(t, nq * hd))
         return ops.linear(o, L["w_o"])
 

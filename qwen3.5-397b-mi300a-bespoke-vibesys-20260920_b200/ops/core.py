@@ -106,13 +106,14 @@ def gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv,
     if _cuda(qkv):
         return ext().gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv)
     t = qkv.shape[0]
-    q = qkv[:, : nk * dk].reshape(t, nk, dk).float()
-    k = qkv[:, nk * dk: 2 * nk * dk].reshape(t, nk, dk).float()
+    q = qkv[:, : nk * dk].reshape(t, nk, dk)
+    k = qkv[:, nk * dk: 2 * nk * dk].reshape(t, nk, dk)
     v = qkv[:, 2 * nk * dk:].reshape(t, nv, dv).float()
     g, beta = ref.deltanet_gates(ab[:, nv:], ab[:, :nv], a_log, dt_bias)
     rep = nv // nk
-    q = ref.l2norm(q).repeat_interleave(rep, dim=1) * dk ** -0.5
-    k = ref.l2norm(k).repeat_interleave(rep, dim=1)
+    # l2norm runs in the activation dtype, as in the HF modeling code
+    q = ref.l2norm(q).float().repeat_interleave(rep, dim=1) * dk ** -0.5
+    k = ref.l2norm(k).float().repeat_interleave(rep, dim=1)
     out = torch.empty(t, nv, dv, dtype=torch.float32, device=qkv.device)
     lanes = seg_lane_h if seg_lane_h is not None else seg_lane.tolist()
     cus = cu_h if cu_h is not None else cu.tolist()
@@ -142,11 +143,13 @@ def qk_norm_rope_kv_write(q, k, v, q_norm, k_norm, positions, rows, k_cache, v_c
 
 
 def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, block_size,
-                     seg_lane_h=None, cu_h=None, seg_start_h=None, tables_h=None):
+                     seg_lane_h=None, cu_h=None, seg_start_h=None, tables_h=None, positions=None, max_ctx=None):
     """Causal GQA attention of each segment's queries over its lane's paged context
-    ``[0, seg_start + len)``. ``q`` [T, Hq, D]; caches [rows, Hkv, D]. Returns [T, Hq, D]."""
+    ``[0, seg_start + len)``. ``q`` [T, Hq, D]; caches [rows, Hkv, D]. Returns [T, Hq, D].
+    On CUDA ``positions`` ([T] absolute positions) and ``max_ctx`` (longest context) are used."""
     if _cuda(q):
-        return ext().attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, block_size)
+        return ext().attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, positions, block_size,
+                                      int(max_ctx))
     out = torch.empty_like(q)
     lanes = seg_lane_h if seg_lane_h is not None else seg_lane.tolist()
     cus = cu_h if cu_h is not None else cu.tolist()
@@ -185,7 +188,10 @@ def moe_routed(h, topw, topi, experts, first, count):
     """Sum of this rank's experts' weighted outputs for each row (zero for rows routed only to
     other ranks' experts). fp32 accumulation, rounded once to ``h.dtype``."""
     if _cuda(h):
-        return ext().moe_routed(h, topw, topi, experts, first, count)
+        if "s13" in experts:
+            return ext().moe_routed_fp4(h, topw, topi, experts["w13"], experts["s13"], experts["w2"], experts["s2"],
+                                        first, count)
+        raise NotImplementedError("bf16 routed experts on CUDA")
     return ref.routed_experts(h, topw, topi.long(), experts, first, count)
 
 

@@ -126,7 +126,9 @@ def gated_delta_rule(q, k, v, g, beta, state):
 
 
 def deltanet_gates(a: torch.Tensor, b: torch.Tensor, a_log: torch.Tensor, dt_bias: torch.Tensor):
-    beta = torch.sigmoid(b.float())
+    """``beta = sigmoid(b)`` (in the activation dtype, as HF computes it), ``g = -exp(A_log) *
+    softplus(a + dt_bias)`` in fp32."""
+    beta = torch.sigmoid(b).float()
     g = -torch.exp(a_log.float()) * F.softplus(a.float() + dt_bias.float())
     return g, beta
 

@@ -1,0 +1,241 @@
+"""Every sm_100a kernel against the plain PyTorch fp32 statement of the same op (``ops.reference``)."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from qwen35_b200.ops import core as ops  # noqa: E402
+from qwen35_b200.ops import reference as ref  # noqa: E402
+from qwen35_b200.ops._ext import ext  # noqa: E402
+from qwen35_b200.utils import mxfp4  # noqa: E402
+
+DEV = "cuda"
+BF = torch.bfloat16
+
+
+def rnd(*shape, scale=1.0, dtype=BF, seed=None):
+    g = torch.Generator(device=DEV)
+    g.manual_seed(seed if seed is not None else hash(shape) % 10007)
+    return (torch.randn(*shape, generator=g, device=DEV) * scale).to(dtype)
+
+
+def close(a, b, rtol=2e-2, atol=2e-2):
+    a, b = a.float(), b.float()
+    err = (a - b).abs().max().item()
+    tol = atol + rtol * b.abs().max().item()
+    assert err <= tol, f"max err {err} > {tol}"
+
+
+def status_ok():
+    st = ext().status(torch.empty(1, device=DEV))
+    assert int(st.abs().sum()) == 0, st.tolist()
+
+
+@pytest.mark.parametrize("T,N,K", [(1, 128, 64), (7, 200, 256), (16, 384, 4096), (33, 256, 512), (100, 1024, 1024),
+                                   (300, 640, 4096), (1000, 256, 128), (64, 4096, 4096)])
+def test_linear(T, N, K):
+    x = rnd(T, K, scale=1.0, seed=T)
+    w = rnd(N, K, scale=0.05, seed=N + K)
+    y = ops.linear(x, w)
+    torch.cuda.synchronize()
+    close(y, x.float() @ w.float().t(), rtol=1e-2, atol=1e-2)
+    status_ok()
+
+
+def test_linear_strided_input_and_output():
+    base = rnd(40, 512, seed=3)
+    x = base[:, 128:384]  # row stride 512, 256 columns
+    w = rnd(192, 256, scale=0.05, seed=4)
+    out = torch.zeros(40, 320, dtype=BF, device=DEV)
+    ops.linear(x, w, out=out[:, 64:256])
+    torch.cuda.synchronize()
+    close(out[:, 64:256], x.float() @ w.float().t(), rtol=1e-2, atol=1e-2)
+    assert out[:, :64].abs().sum() == 0 and out[:, 256:].abs().sum() == 0
+
+
+def test_norms_and_glue():
+    x = rnd(37, 4096, seed=1)
+    res = rnd(37, 4096, seed=2)
+    w = (1 + 0.1 * torch.randn(4096, device=DEV)).float()
+    close(ops.rmsnorm(x, w, 1e-6), ref.rmsnorm(x, w, 1e-6))
+    r0 = res.clone()
+    r1, n1 = ops.add_rmsnorm(x, r0, w, 1e-6)
+    rr, nn = ref.add_rmsnorm(x, res, w, 1e-6)
+    close(r1, rr, atol=1e-2)
+    close(n1, nn)
+    core = rnd(37, 8, 128, seed=5)
+    zz = rnd(37, 8 * 128 + 64, seed=6)[:, :8 * 128].reshape(37, 8, 128)
+    gw = rnd(128, seed=7)
+    close(ops.gated_rmsnorm(core, zz, gw, 1e-6), ref.gated_rmsnorm(core, zz, gw, 1e-6))
+    gu = rnd(9, 2 * 1024, seed=8)
+    close(ops.silu_mul(gu), torch.nn.functional.silu(gu[:, :1024].float()) * gu[:, 1024:].float())
+    g = rnd(9, 2048, seed=9)
+    y = rnd(9, 1024, seed=10)
+    close(ops.sigmoid_gate_mul(y, g[:, :1024]), y.float() * torch.sigmoid(g[:, :1024].float()))
+    rl = rnd(9, 4096, seed=11)
+    sh = rnd(9, 4096, seed=12)
+    gl = rnd(9, 513, seed=13)
+    close(ops.shared_gate_combine(rl, sh, gl[:, 512]), rl.float() + torch.sigmoid(gl[:, 512:513].float()) * sh.float())
+    status_ok()
+
+
+def test_embed_argmax():
+    table = rnd(1000, 256, seed=14)
+    tok = torch.randint(0, 1000, (33,), device=DEV)
+    assert torch.equal(ops.embed(tok, table), table[tok])
+    lg = rnd(5, 248320, seed=15)
+    v, i = ops.argmax_rows(lg)
+    assert torch.equal(i, lg.float().argmax(-1))
+    lg2 = lg.float()
+    lg2[:, 7] = 1e9
+    lg2[:, 9] = 1e9
+    assert ops.argmax_rows(lg2)[1].tolist() == [7] * 5  # ties -> lowest index
+
+
+@pytest.mark.parametrize("E,k", [(512, 10), (32, 4)])
+def test_router_topk(E, k):
+    lg = rnd(50, E + 1, seed=E)
+    w, i = ops.router_topk(lg[:, :E], k)
+    rw, ri = ref.router_topk(lg[:, :E], k)
+    assert torch.equal(i.long().sort(-1).values, ri.sort(-1).values)
+    close(w.sort(-1).values, rw.float().sort(-1).values, atol=1e-2)
+
+
+@pytest.mark.parametrize("nq,nkv,hd,rot", [(8, 1, 256, 64), (32, 2, 256, 64), (2, 1, 64, 16)])
+def test_qk_norm_rope_kv_write(nq, nkv, hd, rot):
+    T = 11
+    qkv = rnd(T, nq * 2 * hd + 2 * nkv * hd, seed=hd)
+    qg = qkv[:, : nq * 2 * hd].reshape(T, nq, 2 * hd)
+    q = qg[..., :hd]
+    k = qkv[:, nq * 2 * hd: nq * 2 * hd + nkv * hd].reshape(T, nkv, hd)
+    v = qkv[:, nq * 2 * hd + nkv * hd:].reshape(T, nkv, hd)
+    qn = (1 + 0.1 * torch.randn(hd, device=DEV)).float()
+    kn = (1 + 0.1 * torch.randn(hd, device=DEV)).float()
+    pos = torch.tensor([0, 1, 5, 17, 100, 1000, 4095, 8000, 12, 13, 65535], dtype=torch.int32, device=DEV)
+    rows = torch.randperm(64, device=DEV)[:T].int()
+    kc = torch.zeros(64, nkv, hd, dtype=BF, device=DEV)
+    vc = torch.zeros_like(kc)
+    kc2, vc2 = kc.clone(), vc.clone()
+    qo = ops.qk_norm_rope_kv_write(q, k, v, qn, kn, pos, rows, kc, vc, rot, 1e7, 1e-6)
+    # oracle on CPU (same math)
+    qr = ops.qk_norm_rope_kv_write(q.cpu(), k.cpu(), v.cpu(), qn.cpu(), kn.cpu(), pos.cpu(), rows.cpu(),
+                                   kc2.cpu(), vc2.cpu(), rot, 1e7, 1e-6)
+    kref = kc2.cpu()
+    kref[rows.long().cpu()] = ref.apply_partial_rope(ref.rmsnorm(k.cpu(), kn.cpu(), 1e-6),
+                                                     *ref.rope_cos_sin(pos.cpu(), rot, 1e7, BF))
+    close(qo.cpu(), qr, atol=2e-2)
+    close(kc.cpu(), kref, atol=2e-2)
+    assert torch.equal(vc[rows.long()].cpu(), v.cpu())
+
+
+def _paged(ctx_lens, nkv, hd, bs=16, seed=0):
+    lanes = len(ctx_lens)
+    max_blocks = max((c + bs - 1) // bs for c in ctx_lens) + 1
+    nblocks = 1 + lanes * max_blocks
+    kc = rnd(nblocks * bs, nkv, hd, seed=seed)
+    vc = rnd(nblocks * bs, nkv, hd, seed=seed + 1)
+    perm = torch.randperm(nblocks - 1) + 1
+    table = torch.zeros(lanes, max_blocks, dtype=torch.int32)
+    for l in range(lanes):
+        table[l] = perm[l * max_blocks:(l + 1) * max_blocks].int()
+    return kc, vc, table.to(DEV), max_blocks
+
+
+@pytest.mark.parametrize("nq,nkv,hd", [(16, 1, 256), (4, 1, 256), (4, 2, 64)])
+def test_attention_decode_and_prefill(nq, nkv, hd):
+    bs = 16
+    ctx = [1, 37, 300, 2049]
+    kc, vc, table, mb = _paged(ctx, nkv, hd, bs, seed=nq)
+    # segments: lanes 0,1 decode one token; lane 2 prefill 5 tokens; lane 3 decode
+    segs = [(0, ctx[0] - 1, 1), (1, ctx[1] - 1, 1), (2, ctx[2] - 5, 5), (3, ctx[3] - 1, 1)]
+    T = sum(s[2] for s in segs)
+    q = rnd(T, nq, hd, seed=99)
+    pos, lanes, cu, starts = [], [], [0], []
+    for lane, st, n in segs:
+        pos += list(range(st, st + n))
+        lanes.append(lane)
+        starts.append(st)
+        cu.append(cu[-1] + n)
+    i32 = dict(dtype=torch.int32, device=DEV)
+    out = ops.attention_varlen(q, kc, vc, table, torch.tensor(lanes, **i32), torch.tensor(cu, **i32),
+                               torch.tensor(starts, **i32), bs, positions=torch.tensor(pos, **i32),
+                               max_ctx=max(ctx))
+    exp = ops.attention_varlen(q.cpu(), kc.cpu(), vc.cpu(), table.cpu(), torch.tensor(lanes), torch.tensor(cu),
+                               torch.tensor(starts), bs, lanes, cu, starts, table.cpu().tolist())
+    close(out.cpu(), exp, atol=2e-2)
+
+
+def test_causal_conv_and_delta_rule():
+    nk, nv, dk, dv, K = 2, 8, 128, 128, 4
+    C = 2 * nk * dk + nv * dv
+    lanes = 3
+    segs = [(0, 1), (2, 17), (1, 5)]
+    T = sum(n for _, n in segs)
+    x = rnd(T, C + 64, seed=21)[:, :C]
+    w = rnd(C, K, scale=0.3, seed=22)
+    st = rnd(lanes, C, K - 1, seed=23)
+    st2 = st.clone().cpu()
+    cu = [0]
+    for _, n in segs:
+        cu.append(cu[-1] + n)
+    ln = [l for l, _ in segs]
+    i32 = dict(dtype=torch.int32, device=DEV)
+    out = ops.causal_conv_varlen(x, st, w, torch.tensor(ln, **i32), torch.tensor(cu, **i32))
+    exp = ops.causal_conv_varlen(x.cpu(), st2, w.cpu(), torch.tensor(ln), torch.tensor(cu), ln, cu)
+    close(out.cpu(), exp, atol=2e-2)
+    close(st.cpu(), st2, atol=0)
+    # delta rule on the conv output
+    ab = rnd(T, 2 * nv, seed=24)
+    a_log = torch.log(torch.rand(nv, device=DEV) * 15 + 1)
+    dtb = torch.rand(nv, device=DEV)
+    rs = torch.randn(lanes, nv, dk, dv, device=DEV) * 0.1
+    rs2 = rs.clone().cpu()
+    o = ops.gated_delta_varlen(out, ab, a_log, dtb, rs, torch.tensor(ln, **i32), torch.tensor(cu, **i32), nk, nv, dk, dv)
+    oe = ops.gated_delta_varlen(out.cpu(), ab.cpu(), a_log.cpu(), dtb.cpu(), rs2, torch.tensor(ln), torch.tensor(cu),
+                                nk, nv, dk, dv, ln, cu)
+    close(o.cpu(), oe, atol=2e-2)
+    close(rs.cpu(), rs2, rtol=1e-3, atol=1e-3)
+
+
+@pytest.mark.parametrize("T,E,k,H,I", [(3, 32, 4, 256, 128), (40, 64, 8, 512, 256), (5, 512, 10, 4096, 1024),
+                                       (300, 64, 4, 1024, 256)])
+def test_moe_routed_mxfp4(T, E, k, H, I):
+    torch.manual_seed(T + E)
+    h = rnd(T, H, seed=T)
+    w13f = torch.randn(E, 2 * I, H, device=DEV) * 0.02
+    w2f = torch.randn(E, H, I, device=DEV) * 0.02
+    w13, s13 = mxfp4.quantize(w13f)
+    w2, s2 = mxfp4.quantize(w2f)
+    lg = rnd(T, E, seed=T + 1)
+    topw, topi = ops.router_topk(lg, k)
+    experts = {"w13": w13, "s13": s13, "w2": w2, "s2": s2}
+    first, count = (E // 4, E // 2) if E >= 64 else (0, E)
+    out = ops.moe_routed(h, topw, topi, experts, first, count)
+    torch.cuda.synchronize()
+    exp = ref.routed_experts(h, topw, topi.long(), experts, first, count)
+    close(out, exp, rtol=3e-2, atol=3e-3)
+    status_ok()
+
+
+def test_tiny_model_gpu_matches_cpu_reference(tiny_dir):
+    from qwen35_b200.models.config import load_config
+    from qwen35_b200.models.qwen35 import Model
+    from qwen35_b200.models.weights import load_weights
+    from qwen35_b200.parallel.plan import plan
+
+    cfg = load_config(tiny_dir)
+    p = plan(cfg, 0, 1)
+    mg = Model(cfg, load_weights(tiny_dir, cfg, p, DEV, BF), p, device=DEV, dtype=BF, max_batch=2, max_seq=512)
+    mc = Model(cfg, load_weights(tiny_dir, cfg, p, "cpu", torch.float32), p, device="cpu", dtype=torch.float32,
+               max_batch=2, max_seq=512)
+    ids = list(range(5, 105))
+    mg.begin(0); mc.begin(0)
+    mg.attach_blocks(0, list(range(1, 9))); mc.attach_blocks(0, list(range(1, 9)))
+    a = mg.prefill(0, ids, 0).float().cpu()
+    b = mc.prefill(0, ids, 0)
+    cos = torch.nn.functional.cosine_similarity(a, b).item()
+    assert cos > 0.99, cos
+    status_ok()
