@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include <atomic>
 #include <mutex>
 #include <unordered_map>
 
@@ -16,8 +17,11 @@ using at::Tensor;
 
 #define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
 #define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+std::atomic<long> g_launches{0};  // kernels launched through these bindings (bench evidence)
+
 #define LAUNCH(expr)                                                         \
   do {                                                                       \
+    g_launches.fetch_add(1, std::memory_order_relaxed);                      \
     int _rc = (expr);                                                        \
     TORCH_CHECK(_rc == 0, "qwen35_b200 kernel launch failed: ", #expr, " rc=", _rc); \
   } while (0)
@@ -146,7 +150,8 @@ Tensor qk_norm_rope_kv_write(Tensor q, Tensor k, Tensor v, Tensor qn, Tensor kn,
   CHECK_BF16(q);
   const int T = q.size(0), nq = q.size(1), hd = q.size(2), nkv = k.size(1);
   const auto* base = reinterpret_cast<const char*>(q.data_ptr());
-  TORCH_CHECK(q.stride(0) == k.stride(0) && k.stride(0) == v.stride(0), "qk_norm_rope: q/k/v must be views of one row");
+  TORCH_CHECK(T <= 1 || (q.stride(0) == k.stride(0) && k.stride(0) == v.stride(0)),
+              "qk_norm_rope: q/k/v must be views of one row");
   TORCH_CHECK(reinterpret_cast<const char*>(k.data_ptr()) == base + (long)nq * 2 * hd * 2 &&
                   reinterpret_cast<const char*>(v.data_ptr()) == base + ((long)nq * 2 * hd + (long)nkv * hd) * 2,
               "qk_norm_rope: expected the fused [q|gate]*nq, k*nkv, v*nkv row layout");
@@ -179,6 +184,7 @@ Tensor attention_varlen(Tensor q, Tensor kc, Tensor vc, Tensor table, Tensor seg
                               pos.data_ptr<int>(), seg_lane.data_ptr<int>(), cu.data_ptr<int>(), S, T, nq, nkv, hd,
                               block_size, splits, splits > 1 ? ws.data_ptr<float>() : nullptr, out.data_ptr(),
                               stream()));
+  if (splits > 1) g_launches.fetch_add(1, std::memory_order_relaxed);  // the split-combine kernel
   return out;
 }
 
@@ -253,6 +259,7 @@ Tensor moe_routed_fp4(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13
 }
 
 // ------------------------------------------------------------------ status
+int64_t launches() { return g_launches.load(); }
 Tensor status(Tensor like) { return status_tensor(like.device()).clone(); }
 void clear_status(Tensor like) { status_tensor(like.device()).zero_(); }
 
@@ -275,5 +282,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_delta_varlen", &gated_delta_varlen);
   m.def("moe_routed_fp4", &moe_routed_fp4);
   m.def("status", &status);
+  m.def("launches", &launches, "number of kernels launched through the bindings so far");
   m.def("clear_status", &clear_status);
 }

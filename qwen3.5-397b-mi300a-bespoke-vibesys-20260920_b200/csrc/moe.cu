@@ -14,7 +14,7 @@
 //   warp 0      TMA producer (raw fp4 tile, f16 token tile; e8m0 scales by bulk copy per unit)
 //   warp 1      TMEM allocator + MMA issuer
 //   warps 2..5  epilogue (silu(gate)*up for the gate_up GEMM, plain for down)
-//   warps 6..9  fp4 -> f16 converters (thread = weight row)
+//   warps 6..13 fp4 -> f16 converters (two threads per weight row, one 32-element block each)
 // Work unit = (local expert, 128-row weight tile); each unit loops over its expert's token
 // tiles. For the gate_up GEMM a weight tile is 64 gate rows + the matching 64 up rows, so the
 // epilogue sees both halves of silu(g)*u in one accumulator.
@@ -128,7 +128,7 @@ int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k,
 }
 
 // ------------------------------------------------------------------ grouped expert GEMM
-constexpr int MOE_THREADS = 320;
+constexpr int MOE_THREADS = 448;
 constexpr int MBK = 64;
 
 template <int BN, bool FP4>
@@ -199,14 +199,14 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&conv[s], 128);
+      mbar_init(&conv[s], 256);
       mbar_init(&empty[s], 1);
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 128);
       mbar_init(&sc_full[i], 1);
-      mbar_init(&sc_empty[i], 128);
+      mbar_init(&sc_empty[i], 256);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -380,7 +380,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
     }
   } else if (FP4) {
     // ---------------------------------------------------------------- fp4 -> f16 converters
-    const int r = threadIdx.x - 192;  // weight-tile row 0..127
+    const int ct = threadIdx.x - 192;  // 0..255
+    const int r = ct & 127;            // weight-tile row
+    const int blk = ct >> 7;           // which 32-element scale block of the 64-wide K slice
     int it = 0, ui = 0;
     bool stop = false;
     for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
@@ -398,32 +400,36 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
             break;
           }
           uint8_t* st = stages + s * C::STAGE;
-          const uint4* raw = reinterpret_cast<const uint4*>(st + C::A + C::B + r * (MBK / 2));
-          const uint4 c0 = raw[0], c1 = raw[1];  // 64 codes = 2 scale blocks of 32
-          const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          // 32 codes of this thread's block: 16 bytes
+          const uint4 c = *reinterpret_cast<const uint4*>(st + C::A + C::B + r * (MBK / 2) + blk * 16);
+          const uint32_t words[4] = {c.x, c.y, c.z, c.w};
+          const int sexp = (int)srw[kb * 2 + blk] - 127;
+          // f16 bit pattern of 2**sexp (normal range [-14, 15], subnormal down to -24)
+          const bool in_range = sexp >= -24 && sexp <= 15;
+          const uint16_t sbits = sexp >= -14 ? (uint16_t)((sexp + 15) << 10) : (uint16_t)(1u << (sexp + 24));
+          __half2 sc2;
+          {
+            const uint32_t sw = (uint32_t)sbits | ((uint32_t)sbits << 16);
+            sc2 = *reinterpret_cast<const __half2*>(&sw);
+          }
+          const float scf = exp2f((float)sexp);
           uint8_t* arow = st + r * 128;  // SW128 row r: 16-byte chunk j stored at j ^ (r & 7)
-          // 64 codes = 8 chunks of 8 f16; chunk c comes from word c, scale block c / 4
 #pragma unroll
-          for (int chunk = 0; chunk < 8; ++chunk) {
-            const int blk = chunk / 4;
-            const int sexp = (int)srw[kb * 2 + blk] - 127;
-            const bool in_range = sexp >= -24 && sexp <= 15;
-            const __half2 sc2 = __half2half2(__float2half_rn(exp2f((float)sexp)));
-            const uint32_t w32 = words[chunk];  // 4 bytes = 8 codes = 8 f16 (16 bytes)
+          for (int q = 0; q < 4; ++q) {  // chunk = 8 codes = 8 f16
             uint32_t outw[4];
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              uint32_t h2 = e2m1x2_to_f16x2((w32 >> (8 * q)) & 0xff);
+            for (int b2 = 0; b2 < 4; ++b2) {
+              uint32_t h2 = e2m1x2_to_f16x2((words[q] >> (8 * b2)) & 0xff);
               __half2 v = *reinterpret_cast<__half2*>(&h2);
               if (in_range) {
                 v = __hmul2(v, sc2);
               } else {
                 const float2 f = __half22float2(v);
-                const float sc = exp2f((float)sexp);
-                v = __floats2half2_rn(f.x * sc, f.y * sc);
+                v = __floats2half2_rn(f.x * scf, f.y * scf);
               }
-              outw[q] = *reinterpret_cast<uint32_t*>(&v);
+              outw[b2] = *reinterpret_cast<uint32_t*>(&v);
             }
+            const int chunk = blk * 4 + q;
             *reinterpret_cast<uint4*>(arow + ((chunk ^ (r & 7)) * 16)) = make_uint4(outw[0], outw[1], outw[2], outw[3]);
           }
           // make the generic-proxy shared-memory writes visible to the tensor core (async proxy)

@@ -111,6 +111,11 @@ class Model:
         self._dirty: set[int] = set(range(max_batch))
         self.last_hidden: torch.Tensor | None = None  # pre-final-norm hidden of the logit rows (MTP seed)
         self.fault: dict[str, object] = {}  # accuracy-gate calibration faults (serving.faults)
+        self._h2d = 0  # bytes copied host -> device for step inputs (bench accounting)
+        self._d2h = 0  # bytes read back device -> host (sampled ids)
+
+    def io_bytes(self) -> tuple[int, int]:
+        return self._h2d, self._d2h
 
     # ================================================================== Runner: lanes & blocks
     def begin(self, lane: int) -> None:
@@ -159,6 +164,7 @@ class Model:
             if t:
                 row[: len(t)] = torch.tensor(t, dtype=torch.int32)
             self.table_dev[lane].copy_(row.to(self.device), non_blocking=True)
+            self._h2d += row.numel() * 4
         self._dirty.clear()
 
     # ================================================================== Runner: snapshots
@@ -213,6 +219,7 @@ class Model:
             packed = packed.pin_memory().to(dev, non_blocking=True)
             tok = torch.tensor(toks, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
             lr = torch.tensor(list(logit_rows), dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+            self._h2d += packed.numel() * 4 + tok.numel() * 8 + lr.numel() * 8
         else:
             tok = torch.tensor(toks, dtype=torch.int64)
             lr = torch.tensor(list(logit_rows), dtype=torch.int64)
@@ -342,6 +349,7 @@ class Model:
     def sample_batch(self, logits, temperatures: Sequence[float], generator=None) -> list[int]:
         temps = list(temperatures)
         out = ops.argmax_rows(logits)[1].tolist() if logits.shape[0] else []
+        self._d2h += 8 * len(out)
         for i, t in enumerate(temps):
             if t and t > 0:
                 p = torch.softmax(logits[i].float() / t, dim=-1)

@@ -221,6 +221,10 @@ class Scheduler:
         if not req.prompt:
             req.emit(("error", "empty prompt"))
             return True
+        if len(req.prompt) + max(req.max_new, 0) > self.runner.max_seq:
+            req.emit(("error", f"prompt ({len(req.prompt)}) + max_tokens ({req.max_new}) exceeds the "
+                               f"context limit {self.runner.max_seq}"))
+            return True
         node = self.cache.lookup(req.prompt)
         lane = self.free_lanes[-1]
         protect = [node] + self._live_parents()

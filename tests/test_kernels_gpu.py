@@ -197,7 +197,7 @@ def test_causal_conv_and_delta_rule():
     oe = ops.gated_delta_varlen(out.cpu(), ab.cpu(), a_log.cpu(), dtb.cpu(), rs2, torch.tensor(ln), torch.tensor(cu),
                                 nk, nv, dk, dv, ln, cu)
     close(o.cpu(), oe, atol=2e-2)
-    close(rs.cpu(), rs2, rtol=1e-3, atol=1e-3)
+    close(rs.cpu(), rs2, rtol=1e-2, atol=1e-3)  # bf16 l2norm rounding emulation
 
 
 @pytest.mark.parametrize("T,E,k,H,I", [(3, 32, 4, 256, 128), (40, 64, 8, 512, 256), (5, 512, 10, 4096, 1024),
@@ -205,10 +205,15 @@ def test_causal_conv_and_delta_rule():
 def test_moe_routed_mxfp4(T, E, k, H, I):
     torch.manual_seed(T + E)
     h = rnd(T, H, seed=T)
-    w13f = torch.randn(E, 2 * I, H, device=DEV) * 0.02
-    w2f = torch.randn(E, H, I, device=DEV) * 0.02
-    w13, s13 = mxfp4.quantize(w13f)
-    w2, s2 = mxfp4.quantize(w2f)
+    if E * I * H <= 2 ** 24:
+        w13, s13 = mxfp4.quantize(torch.randn(E, 2 * I, H, device=DEV) * 0.02)
+        w2, s2 = mxfp4.quantize(torch.randn(E, H, I, device=DEV) * 0.02)
+    else:  # random codes and scales (quantising 4 GB of fp32 weights would not fit)
+        u8 = dict(dtype=torch.uint8, device=DEV)
+        w13 = torch.randint(0, 256, (E, 2 * I, H // 2), **u8)
+        s13 = torch.randint(116, 124, (E, 2 * I, H // 32), **u8)
+        w2 = torch.randint(0, 256, (E, H, I // 2), **u8)
+        s2 = torch.randint(116, 124, (E, H, I // 32), **u8)
     lg = rnd(T, E, seed=T + 1)
     topw, topi = ops.router_topk(lg, k)
     experts = {"w13": w13, "s13": s13, "w2": w2, "s2": s2}
