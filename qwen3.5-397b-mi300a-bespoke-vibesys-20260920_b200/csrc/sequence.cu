@@ -318,3 +318,58 @@ int attention_varlen(const void* q, const void* kc, const void* vc, const int* t
 }
 
 }  // namespace qb
+
+// ------------------------------------------------------------------ allocation-free entry point
+// See noalloc.h: the split-K scratch of the attention kernels above lives in this file-scope
+// device array, so callers that cannot allocate device memory can still run the kernel.
+#include <mutex>
+
+#include "noalloc.h"
+
+static __device__ __align__(256) float g_attn_noalloc_scratch[QB_ATTN_NOALLOC_SCRATCH_BYTES / sizeof(float)];
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[kMaxDevices] = {nullptr};
+
+// Device address of the scratch array for the current device (looked up once per device).
+int noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  if (dev < 0 || dev >= kMaxDevices) return QB_NOALLOC_ERR_ARGS;
+  std::lock_guard<std::mutex> g(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess || p == nullptr) return QB_NOALLOC_ERR_SYMBOL;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return QB_NOALLOC_OK;
+}
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) size_t qb_attention_noalloc_scratch_bytes(void) {
+  return QB_ATTN_NOALLOC_SCRATCH_BYTES;
+}
+
+extern "C" __attribute__((visibility("default"))) int qb_attention_varlen_noalloc(
+    const void* q, const void* k_cache, const void* v_cache, const int* block_table, int max_blocks,
+    const int* positions, const int* seg_lane, const int* cu, int num_segments, int num_rows, int nq, int nkv,
+    int head_dim, int block_size, int splits, void* out, cudaStream_t stream) {
+  if (num_rows < 0 || num_segments <= 0 || nq <= 0 || nkv <= 0 || splits < 1 || splits > 64 || block_size <= 0 ||
+      nq % nkv != 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256))
+    return QB_NOALLOC_ERR_ARGS;
+  if (num_rows == 0) return QB_NOALLOC_OK;
+  const size_t need = (size_t)num_rows * nq * splits * (head_dim + 2) * sizeof(float);
+  if (splits > 1 && need > QB_ATTN_NOALLOC_SCRATCH_BYTES) return QB_NOALLOC_ERR_TOO_LARGE;
+  float* ws = nullptr;
+  const int rc = noalloc_scratch(&ws);
+  if (rc != QB_NOALLOC_OK) return rc;
+  // the split kernel writes every (row, head, split) slot it owns before the combine reads it,
+  // so the scratch needs no clearing between calls
+  return qb::attention_varlen(q, k_cache, v_cache, block_table, max_blocks, positions, seg_lane, cu, num_segments,
+                              num_rows, nq, nkv, head_dim, block_size, splits, ws, out, stream);
+}
