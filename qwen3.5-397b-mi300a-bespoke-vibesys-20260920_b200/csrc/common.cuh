@@ -75,21 +75,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t phase) {
   return ok != 0;
 }
 
+// try_wait with a suspend-time hint: the waiting thread is descheduled until the phase
+// completes or `ns` nanoseconds pass, so idle roles do not steal issue slots from busy ones.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t phase, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(phase), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Waits for the phase with parity `phase` to complete. Returns false (and records `code` in
 // *err) if it does not complete within QB_WAIT_NS, or if another thread already aborted.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int* err, int code,
                                           volatile int* abort_flag) {
   if (mbar_try_wait(bar, phase)) return true;
-  uint64_t t0 = globaltimer();
-  for (uint32_t i = 1;; ++i) {
-    if (mbar_try_wait(bar, phase)) return true;
-    if ((i & 255) == 0) {
-      if (abort_flag && *abort_flag) return false;
-      if (globaltimer() - t0 > QB_WAIT_NS) {
-        if (err) atomicCAS(err, 0, code);
-        if (abort_flag) *abort_flag = 1;
-        return false;
-      }
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_sleep(bar, phase, 200000)) return true;  // sleep up to 0.2 ms per try
+    if (abort_flag && *abort_flag) return false;
+    if (globaltimer() - t0 > QB_WAIT_NS) {
+      if (err) atomicCAS(err, 0, code);
+      if (abort_flag) *abort_flag = 1;
+      return false;
     }
   }
 }
@@ -143,6 +153,31 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
       : "memory");
 }
+
+// D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16: the A operand is read from tensor memory
+// (row m in lane m, two 16-bit K elements per 32-bit column, low half = even K).
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  const uint32_t z = 0;
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(z), "r"(z), "r"(z), "r"(z)
+      : "memory");
+}
+
+// 32 consecutive 32-bit columns of this warp's 32 TMEM lanes from registers (one lane per thread).
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t* r) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]),
+      "r"(r[9]), "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15]), "r"(r[16]), "r"(r[17]),
+      "r"(r[18]), "r"(r[19]), "r"(r[20]), "r"(r[21]), "r"(r[22]), "r"(r[23]), "r"(r[24]), "r"(r[25]), "r"(r[26]),
+      "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
+      : "memory");
+}
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Arrives on `bar` once every previously issued tcgen05.mma of this thread has completed.
 __device__ __forceinline__ void mma_commit(uint64_t* bar) {

@@ -21,6 +21,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <cstdlib>
+
 namespace qb {
 
 using bf16 = __nv_bfloat16;
@@ -454,6 +456,353 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
   }
 }
 
+
+// ------------------------------------------------------------------ grouped MXFP4 GEMM, A in TMEM
+// Same work decomposition as moe_gemm_kernel, but the converted f16 weight tile is written to
+// tensor memory (tcgen05.st) and the MMA reads its A operand from there. Shared memory only
+// carries the packed fp4 codes and the token tiles. One pipeline stage covers 256 K elements:
+// the fp4 tile arrives as 128 rows x 128 bytes (full cache lines per row) and the token tile as
+// four 64-wide swizzle atoms; each of the 4 converter groups decodes one 64-wide sub-block.
+//   warp 0       TMA producer          warp 1      TMEM allocator + MMA issuer
+//   warps 2..5   epilogue              warps 6..21 converters: group g = sub-block g of every
+//                                      stage; warp w covers the TMEM lane quarter w % 4
+constexpr int MT_THREADS = 704;
+constexpr int MT_NA = 8;          // A ring depth in TMEM (32 columns = 64 K elements each)
+constexpr int MT_ABASE = 256;     // first TMEM column of the A ring
+constexpr int MT_SK = 256;        // K elements per stage
+
+template <int BN>
+struct MoeTmCfg {
+  static constexpr int B_ATOM = BN * 64 * 2;   // one 64-wide swizzled token tile
+  static constexpr int B = 4 * B_ATOM;
+  static constexpr int RAW = 128 * MT_SK / 2;   // 16 KB of packed codes
+  static constexpr int STAGE = B + RAW;         // multiple of 1024
+  static constexpr int SCALE_MAX = 128 * 128;
+  static constexpr int STAGING = 32 * 128 * 2;
+  static constexpr int BUDGET = 212 * 1024 - STAGING - 2 * SCALE_MAX;
+  static constexpr int STAGES = BUDGET / STAGE > 12 ? 12 : BUDGET / STAGE;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + STAGING + 2 * SCALE_MAX + 1024;
+};
+
+template <int BN>
+__global__ void __launch_bounds__(MT_THREADS, 1)
+    moe_fp4_tmem_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, MoeArgs a,
+                        uint32_t idesc) {
+  using C = MoeTmCfg<BN>;
+  static_assert(C::STAGE % 1024 == 0, "stage must keep the token tiles 1024-byte aligned");
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint16_t* staging = reinterpret_cast<uint16_t*>(smem + C::STAGES * C::STAGE);
+  uint8_t* sbuf = smem + C::STAGES * C::STAGE + C::STAGING;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sbuf + 2 * C::SCALE_MAX);
+  uint64_t* full = bars;
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* a_full = empty + C::STAGES;
+  uint64_t* a_empty = a_full + MT_NA;
+  uint64_t* acc_full = a_empty + MT_NA;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* sc_full = acc_empty + 2;
+  uint64_t* sc_empty = sc_full + 2;
+  uint64_t* drain = sc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued_p = const_cast<int*>(abort_flag) + 1;
+  int* consumed_p = issued_p + 1;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_tiles = a.n_rows / 128;
+  const int units = a.count * n_tiles;
+  const int ksub = a.K / MBK;                        // 64-wide sub-blocks in K
+  const int kstages = (a.K + MT_SK - 1) / MT_SK;     // stages per tile
+  const int srow = a.K / 32;
+  const bool gu = a.act == 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < MT_NA; ++i) {
+      mbar_init(&a_full[i], 128);
+      mbar_init(&a_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+      mbar_init(&sc_full[i], 1);
+      mbar_init(&sc_empty[i], 512);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *issued_p = 0;
+    *consumed_p = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  auto wrow = [&](int nt, int r) -> int {
+    return gu ? (r < 64 ? nt * 64 + r : a.n_rows / 2 + nt * 64 + (r - 64)) : nt * 128 + r;
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (elect_one()) {
+      int it = 0, ui = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        const int e = u / n_tiles, nt = u % n_tiles;
+        const int cnt = a.counts[e];
+        if (cnt == 0) continue;
+        const int off = a.offsets[e];
+        const long erow = (long)e * a.n_rows;
+        const int sb = ui & 1;
+        if (!mbar_wait(&sc_empty[sb], ((ui >> 1) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) break;
+        uint8_t* dst = sbuf + sb * C::SCALE_MAX;
+        const uint32_t half = 64 * srow;
+        mbar_expect_tx(&sc_full[sb], 2 * half);
+        const uint8_t* s0 = a.scales + (erow + wrow(nt, 0)) * srow;
+        const uint8_t* s1 = a.scales + (erow + wrow(nt, 64)) * srow;
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         smem_u32(dst)),
+                     "l"(s0), "r"(half), "r"(smem_u32(&sc_full[sb]))
+                     : "memory");
+        asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                         smem_u32(dst + half)),
+                     "l"(s1), "r"(half), "r"(smem_u32(&sc_full[sb]))
+                     : "memory");
+        ++ui;
+        for (int m0 = 0; m0 < cnt; m0 += BN) {
+          for (int ks = 0; ks < kstages; ++ks, ++it) {
+            const int s = it % C::STAGES;
+            if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) goto prod_done;
+            uint8_t* st = stages + s * C::STAGE;
+            mbar_expect_tx(&full[s], C::STAGE);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) tma_load_2d(st + j * C::B_ATOM, &tmX, &full[s], ks * MT_SK + j * 64, off + m0);
+            tma_load_2d(st + C::B, &tmW, &full[s], ks * MT_SK / 2, (int)(erow + wrow(nt, 0)));
+            tma_load_2d(st + C::B + C::RAW / 2, &tmW, &full[s], ks * MT_SK / 2, (int)(erow + wrow(nt, 64)));
+            *issued_p = it + 1;
+          }
+        }
+      }
+    prod_done:;
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      int it = 0, ti = 0, sit = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok && !*abort_flag; u += gridDim.x) {
+        const int e = u / n_tiles;
+        const int cnt = a.counts[e];
+        for (int m0 = 0; m0 < cnt && ok; m0 += BN, ++ti) {
+          const int acc = ti & 1;
+          if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t d = tmem + acc * BN;
+          for (int ks = 0; ks < kstages && ok; ++ks, ++it) {
+            const int s = it % C::STAGES;
+            if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+              ok = false;
+              break;
+            }
+            const int nsub = min(4, ksub - ks * 4);
+            const uint32_t sbase = smem_u32(stages + s * C::STAGE);
+            for (int j = 0; j < nsub; ++j, ++sit) {
+              const int ai = sit % MT_NA;
+              if (!mbar_wait(&a_full[ai], (sit / MT_NA) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              const uint64_t db = desc_sw128(sbase + j * C::B_ATOM);
+              const uint32_t at = tmem + MT_ABASE + ai * 32;
+#pragma unroll
+              for (int kk = 0; kk < MBK / 16; ++kk)
+                mma_f16_ts(d, at + kk * 8, db + 2 * kk, idesc, (ks | j | kk) != 0);
+              mma_commit(&a_empty[ai]);
+            }
+            if (!ok) break;
+            mma_commit(&empty[s]);
+            *consumed_p = it + 1;
+          }
+          if (!ok) break;
+          mma_commit(&acc_full[acc]);
+        }
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err, ERR_DRAIN, nullptr);
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- epilogue
+    const int ew = warp & 3;
+    const int row = ew * 32 + lane;
+    const int et = threadIdx.x - 64;
+    int ti = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x) {
+      const int e = u / n_tiles, nt = u % n_tiles;
+      const int cnt = a.counts[e];
+      const int off = a.offsets[e];
+      bool stop = false;
+      for (int m0 = 0; m0 < cnt; m0 += BN, ++ti) {
+        const int acc = ti & 1;
+        if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) {
+          stop = true;
+          break;
+        }
+        tc_fence_after();
+        constexpr int CH = BN < 32 ? BN : 32;
+        for (int c0 = 0; c0 < BN; c0 += CH) {
+          float v[32];
+          const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
+          if constexpr (CH == 32) tmem_ld32(taddr, v); else tmem_ld16(taddr, v);
+#pragma unroll
+          for (int j = 0; j < CH; ++j) {
+            bf16 o = __float2bfloat16(v[j]);
+            staging[j * 128 + row] = *reinterpret_cast<uint16_t*>(&o);
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+          const int nvalid = min(CH, cnt - m0 - c0);
+          if (gu) {
+            __half* Y = reinterpret_cast<__half*>(a.out);
+            for (int idx = et; idx < CH * 64; idx += 128) {
+              const int j = idx / 64, r = idx % 64;
+              if (j < nvalid) {
+                uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
+                const float g = __bfloat162float(*reinterpret_cast<bf16*>(&gb));
+                const float uu = __bfloat162float(*reinterpret_cast<bf16*>(&ub));
+                const float sg = __bfloat162float(__float2bfloat16(g / (1.f + expf(-g))));
+                const float y = __bfloat162float(__float2bfloat16(sg * uu));
+                Y[(long)(off + m0 + c0 + j) * a.out_cols + nt * 64 + r] = __float2half_rn(y);
+              }
+            }
+          } else {
+            bf16* Y = reinterpret_cast<bf16*>(a.out);
+            for (int idx = et; idx < CH * 16; idx += 128) {
+              const int j = idx / 16, q = idx % 16;
+              if (j < nvalid) {
+                const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
+                *reinterpret_cast<uint4*>(Y + (long)(off + m0 + c0 + j) * a.out_cols + nt * 128 + q * 8) = val;
+              }
+            }
+          }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+      }
+      if (stop) break;
+    }
+  } else {
+    // ---------------------------------------------------------------- fp4 -> f16 converters
+    const int cw = warp - 6;   // 0..15
+    const int grp = cw >> 2;   // sub-block of every stage this group decodes
+    const int q = warp & 3;    // TMEM lane quarter
+    const int r = q * 32 + lane;
+    int it = 0, ui = 0, sit0 = 0;
+    bool stop = false;
+    for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
+      const int e = u / n_tiles;
+      const int cnt = a.counts[e];
+      if (cnt == 0) continue;
+      const int sb = ui & 1;
+      if (!mbar_wait(&sc_full[sb], (ui >> 1) & 1, a.err, ERR_MMA_WAIT, abort_flag)) break;
+      const uint8_t* srw = sbuf + sb * C::SCALE_MAX + r * srow;
+      for (int m0 = 0; m0 < cnt && !stop; m0 += BN) {
+        for (int ks = 0; ks < kstages; ++ks, ++it) {
+          const int nsub = min(4, ksub - ks * 4);
+          const int sit = sit0 + grp;
+          sit0 += nsub;
+          if (grp >= nsub) continue;
+          const int s = it % C::STAGES, ai = sit % MT_NA;
+          if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag) ||
+              !mbar_wait(&a_empty[ai], ((sit / MT_NA) & 1) ^ 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+            stop = true;
+            break;
+          }
+          const int kb = ks * 4 + grp;  // 64-wide K sub-block index
+          const uint8_t* raw = stages + s * C::STAGE + C::B + r * (MT_SK / 2) + grp * 32;
+          const uint4 c0 = *reinterpret_cast<const uint4*>(raw);
+          const uint4 c1 = *reinterpret_cast<const uint4*>(raw + 16);
+          const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+          uint32_t outw[32];
+#pragma unroll
+          for (int blk = 0; blk < 2; ++blk) {
+            const int sexp = (int)srw[kb * 2 + blk] - 127;
+            const bool in_range = sexp >= -24 && sexp <= 15;
+            const uint32_t sbits = sexp >= -14 ? (uint32_t)((sexp + 15) << 10) : (1u << (sexp + 24));
+            const uint32_t sw = (sbits & 0xffff) | ((sbits & 0xffff) << 16);
+            const __half2 sc2 = *reinterpret_cast<const __half2*>(&sw);
+            const float scf = exp2f((float)sexp);
+#pragma unroll
+            for (int w4 = 0; w4 < 4; ++w4) {
+              const uint32_t wd = words[blk * 4 + w4];
+#pragma unroll
+              for (int b2 = 0; b2 < 4; ++b2) {
+                uint32_t h2 = e2m1x2_to_f16x2((wd >> (8 * b2)) & 0xff);
+                __half2 v = *reinterpret_cast<__half2*>(&h2);
+                if (in_range) {
+                  v = __hmul2(v, sc2);
+                } else {
+                  const float2 f = __half22float2(v);
+                  v = __floats2half2_rn(f.x * scf, f.y * scf);
+                }
+                outw[blk * 16 + w4 * 4 + b2] = *reinterpret_cast<uint32_t*>(&v);
+              }
+            }
+          }
+          tmem_st32(tmem + MT_ABASE + ai * 32 + ((uint32_t)(q * 32) << 16), outw);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(&a_full[ai]);
+        }
+      }
+      mbar_arrive(&sc_empty[sb]);
+      ++ui;
+    }
+  }
+
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    for (int it = *consumed_p; it < *issued_p; ++it)
+      mbar_wait(&full[it % C::STAGES], (it / C::STAGES) & 1, a.err, ERR_DRAIN, nullptr);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+template <int BN>
+static int moe_tm_launch(const CUtensorMap& tw, const CUtensorMap& tx, const MoeArgs& a, int max_ctas,
+                         cudaStream_t st) {
+  using C = MoeTmCfg<BN>;
+  auto k = moe_fp4_tmem_kernel<BN>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr = true;
+  }
+  const int units = a.count * (a.n_rows / 128);
+  int grid = units < max_ctas ? units : max_ctas;
+  if (grid < 1) grid = 1;
+  k<<<grid, MT_THREADS, C::SMEM, st>>>(tw, tx, a, idesc_f16(128, BN, false));
+  return (int)cudaGetLastError();
+}
+
 static int moe_sms() {
   static int n = 0;
   if (!n) {
@@ -495,17 +844,33 @@ int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8
   (void)s_expert_stride;
   const int BN = pick_bn(cap, count);
   CUtensorMap tw, tx;
-  int r = make_tmap_2d(&tw, wq, 1, (long)count * n_rows, k_cols / 2, k_cols / 2, 64, MBK / 2, false);
+  MoeArgs a{ws, offsets, counts, out, out_cols, n_rows, k_cols, count, act, err};
+  if (max_ctas <= 0) max_ctas = moe_sms();
+  static const bool smem_a = getenv("QB_MOE_SMEM_A") && getenv("QB_MOE_SMEM_A")[0] == '1';
+  int r;
+  if (!smem_a) {
+    const int bn = BN > 64 ? 64 : BN;
+    r = make_tmap_2d(&tw, wq, 1, (long)count * n_rows, k_cols / 2, k_cols / 2, 64, MT_SK / 2, false);
+    if (r) return 1000 + r;
+    r = make_tmap_2d(&tx, xin, 2, cap, k_cols, in_cols, bn, MBK, true);
+    if (r) return 2000 + r;
+    switch (bn) {
+      case 16: return moe_tm_launch<16>(tw, tx, a, max_ctas, s);
+      case 32: return moe_tm_launch<32>(tw, tx, a, max_ctas, s);
+      default: return moe_tm_launch<64>(tw, tx, a, max_ctas, s);
+    }
+  }
+  r = make_tmap_2d(&tw, wq, 1, (long)count * n_rows, k_cols / 2, k_cols / 2, 64, MBK / 2, false);
   if (r) return 1000 + r;
   r = make_tmap_2d(&tx, xin, 2, cap, k_cols, in_cols, BN, MBK, true);
   if (r) return 2000 + r;
-  MoeArgs a{ws, offsets, counts, out, out_cols, n_rows, k_cols, count, act, err};
-  if (max_ctas <= 0) max_ctas = moe_sms();
-  switch (BN) {
-    case 16: return moe_launch<16, true>(tw, tx, a, max_ctas, s);
-    case 32: return moe_launch<32, true>(tw, tx, a, max_ctas, s);
-    case 64: return moe_launch<64, true>(tw, tx, a, max_ctas, s);
-    default: return moe_launch<128, true>(tw, tx, a, max_ctas, s);
+  {  // converted tile in shared memory (A/B comparison path)
+    switch (BN) {
+      case 16: return moe_launch<16, true>(tw, tx, a, max_ctas, s);
+      case 32: return moe_launch<32, true>(tw, tx, a, max_ctas, s);
+      case 64: return moe_launch<64, true>(tw, tx, a, max_ctas, s);
+      default: return moe_launch<128, true>(tw, tx, a, max_ctas, s);
+    }
   }
 }
 
