@@ -123,6 +123,13 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
+def _elapsed_ms(a, b) -> float:
+    """Milliseconds between two marks: CUDA events on GPU, host perf_counter values on CPU."""
+    if isinstance(a, float):
+        return (b - a) * 1e3
+    return a.elapsed_time(b)
+
+
 def build_model(args, rank, world, device):
     import torch
 
@@ -203,9 +210,10 @@ def main():
             torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
-        ev = torch.cuda.Event(enable_timing=True) if device.type == "cuda" else None
-        if ev is not None:
-            ev.record()
+        if device.type != "cuda":
+            return time.perf_counter()
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record()
         return ev
 
     model.bench_marks = []
@@ -213,7 +221,7 @@ def main():
 
     if rank != 0:
         serve_worker(model, Channel(group))
-        t = model.bench_marks[0].elapsed_time(model.bench_marks[1]) if len(model.bench_marks) >= 2 else 0.0
+        t = _elapsed_ms(model.bench_marks[0], model.bench_marks[1]) if len(model.bench_marks) >= 2 else 0.0
         gathered = [None] * world
         dist.all_gather_object(gathered, t)
         dist.destroy_process_group()
@@ -280,7 +288,7 @@ def main():
     launches = (_ext.ext().launches() - launches0) if device.type == "cuda" else 0
     h2d1, d2h1 = model.io_bytes()
     step1 = step_no[0]
-    window_ms = ev_start.elapsed_time(ev_end) if ev_start is not None else (t_host1 - t_host0) * 1e3
+    window_ms = _elapsed_ms(ev_start, ev_end)
     if world > 1:
         runner.shutdown()
         gathered = [None] * world

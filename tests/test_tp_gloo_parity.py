@@ -1,0 +1,67 @@
+"""the tiny model at TP=4 over gloo (4 CPU processes, the real scheduler,
+session cache and SPMD driver) reproduces the HuggingFace oracle's greedy tokens, turn by turn,
+for 2 chat sessions x 3 turns with 32 new tokens each."""
+
+import json
+import os
+import random
+import subprocess
+import sys
+
+import pytest
+
+from hf_oracle import build_hf, hf_greedy
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+@pytest.mark.slow
+def test_tp4_gloo_multiturn_matches_hf(tiny_dir, tmp_path):
+    out = str(tmp_path / "tp4.json")
+    port = 29700 + random.randrange(200)
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "tp_gloo_rank.py"), str(r), "4", tiny_dir, out,
+                               str(port)]) for r in range(4)]
+    codes = [p.wait(timeout=900) for p in procs]
+    assert codes == [0, 0, 0, 0], codes
+    res = json.load(open(out))
+    assert res["hits"] > 0  # later turns resumed from cached boundaries
+    model, _ = build_hf(tiny_dir)
+    exact = 0
+    for t in res["turns"]:
+        exact += t["out"] == hf_greedy(model, t["prompt"], 32)
+        check_teacher_forced(model, t["prompt"], t["out"])
+    assert exact >= len(res["turns"]) // 2, exact
+
+
+def check_teacher_forced(model, prompt, ours, tol=2e-2):
+    """Every generated token is the HF model's top-1 for our own prefix, up to ``tol``.
+
+    On a random-weight model the router's top-k has near-ties, and a tie flipped by summation
+    order changes later logits by ~1e-2; HF's own cached ``generate`` and its uncached forward
+    disagree at such points. Teacher-forcing checks each step on its own prefix instead."""
+    import torch
+
+    seq = list(prompt) + list(ours)
+    with torch.inference_mode():
+        lg = model(torch.tensor([seq])).logits[0, len(prompt) - 1:-1].float()
+    top = lg.max(dim=-1).values
+    got = lg[torch.arange(len(ours)), torch.tensor(ours)]
+    bad = (got < top - tol).nonzero().flatten().tolist()
+    assert not bad, [(i, ours[i], got[i].item(), top[i].item()) for i in bad]
+
+
+def test_single_process_matches_hf(tiny_dir):
+    import torch
+
+    from qwen35_b200.models.config import load_config
+    from qwen35_b200.models.qwen35 import Model
+    from qwen35_b200.models.weights import load_weights
+    from qwen35_b200.parallel.plan import plan
+
+    cfg = load_config(tiny_dir)
+    p = plan(cfg, 0, 1)
+    m = Model(cfg, load_weights(tiny_dir, cfg, p, "cpu", torch.float32), p, device="cpu", dtype=torch.float32,
+              max_batch=2, max_seq=512)
+    model, _ = build_hf(tiny_dir)
+    ids = list(range(10, 140))
+    assert m.generate(ids, 16) == hf_greedy(model, ids, 16)
