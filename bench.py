@@ -269,7 +269,9 @@ def main():
     # ---- timed window
     launches0 = _ext.ext().launches() if device.type == "cuda" else 0
     h2d0, d2h0 = model.io_bytes()
-    clocks = ClockSampler([local + i for i in range(world)] if world > 1 else [local])
+    cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+    phys = [int(x) for x in cvd.split(",") if x.strip().isdigit()] if cvd else list(range(8))
+    clocks = ClockSampler(phys[:world] if phys else list(range(world)))
     clocks.start()
     if world > 1:
         runner.channel.send(Op.CALL, ("bench_mark", ("start",), {}))

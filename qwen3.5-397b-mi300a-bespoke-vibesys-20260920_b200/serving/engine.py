@@ -1,0 +1,67 @@
+"""Model construction for serving and benchmarking (one place for pool sizing).
+
+``build_model`` creates this rank's ``Model`` either from a checkpoint directory (the published
+safetensors layout) or with random-init weights of a named geometry (``full`` / ``tiny``), and
+sizes the paged KV pool, lane count and snapshot pool from the arguments. On a single GPU the
+full geometry does not fit (205 GB of MXFP4 experts); ``distinct_expert_layers`` then lets
+later layers reuse earlier layers' expert storage, sized from free memory.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+
+import torch
+
+from ..models.config import Qwen35Config, full_config, load_config, tiny_config
+from ..models.qwen35 import Model
+from ..models.weights import expert_bytes_per_layer, load_weights, random_weights
+from ..parallel.comm import Comm
+from ..parallel.plan import plan
+
+
+@dataclass
+class PoolSpec:
+    lanes: int = 32
+    max_seq: int = 16384
+    block_size: int = 16
+    kv_tokens: int | None = None  # paged KV capacity (tokens); default lanes * max_seq
+    snapshots: int | None = None  # default 2 * lanes + 16
+
+
+def pool_bytes(cfg: Qwen35Config, p, spec: PoolSpec) -> tuple[int, int, int]:
+    kv_tokens = spec.kv_tokens or spec.lanes * spec.max_seq
+    num_blocks = kv_tokens // spec.block_size + 1
+    snaps = spec.snapshots or 2 * spec.lanes + 16
+    kv = num_blocks * spec.block_size * len(cfg.full_layers) * 2 * p.kv.count * cfg.head_dim * 2
+    nv, nk = p.dn_v.count, p.dn_k.count
+    conv_ch = 2 * nk * cfg.dn_k_dim + nv * cfg.dn_v_dim
+    per_state = len(cfg.linear_layers) * (nv * cfg.dn_k_dim * cfg.dn_v_dim * 4 + conv_ch * (cfg.conv_kernel - 1) * 2)
+    return kv, (spec.lanes + snaps) * per_state, num_blocks
+
+
+def build_model(model: str, rank: int, world: int, device: torch.device, spec: PoolSpec,
+                dtype=torch.bfloat16, seed: int = 0, with_mtp: bool = False, comm: Comm | None = None,
+                reserve_bytes: float = 14e9) -> tuple[Model, int | None]:
+    """``model`` is a checkpoint directory, ``"full"`` or ``"tiny"`` (random init)."""
+    if model in ("full", "tiny"):
+        cfg = full_config() if model == "full" else tiny_config()
+    else:
+        cfg = load_config(model)
+    p = plan(cfg, rank, world)
+    kv, state, num_blocks = pool_bytes(cfg, p, spec)
+    distinct = None
+    if model == "full" and device.type == "cuda":
+        total = torch.cuda.get_device_properties(device).total_memory
+        dense = 20e9 / world + 4e9
+        budget = total - dense - kv - state - reserve_bytes
+        n = max(1, min(cfg.layers, int(budget // expert_bytes_per_layer(cfg, p))))
+        distinct = None if n >= cfg.layers else n
+    if model in ("full", "tiny"):
+        w = random_weights(cfg, p, device, dtype, seed=seed, with_mtp=with_mtp, distinct_expert_layers=distinct)
+    else:
+        w = load_weights(model, cfg, p, device, dtype, with_mtp=with_mtp)
+    m = Model(cfg, w, p, comm or Comm(rank, world, None, device), device=device, dtype=dtype,
+              max_batch=spec.lanes, max_seq=spec.max_seq, block_size=spec.block_size, num_blocks=num_blocks,
+              num_snapshots=spec.snapshots or 2 * spec.lanes + 16)
+    return m, distinct

@@ -1,0 +1,14 @@
+"""Accuracy-gate calibration faults (reference ``model.py:149-173``, ``server.py:780-840``).
+
+Each fault deliberately breaks one piece of the model so an accuracy checker can be shown to
+catch it; all are off unless set, and are switched at runtime through ``POST /debug/fault``
+(enabled with ``QB_FAULT_ENDPOINT=1``) or by setting ``Model.fault[name]`` directly. They act
+on the host side of the model (which arguments the kernels receive); none of them makes a GPU
+kernel fault or hang.
+
+* ``rope_base``          - RoPE theta used by the attention layers (a wrong base)
+* ``drop_expert``        - zero the routing weight of one expert id
+* ``skip_deltanet_gate`` - replace the DeltaNet gated output norm by a plain RMSNorm
+"""
+
+FAULTS = {"rope_base", "drop_expert", "skip_deltanet_gate"}

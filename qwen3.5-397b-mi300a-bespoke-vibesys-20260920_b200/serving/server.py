@@ -1,0 +1,371 @@
+"""OpenAI-compatible HTTP server and process launcher.
+
+    python -m qwen35_b200.serving.server --model-path DIR|full|tiny --tp N --port 8000
+
+Rank 0 serves HTTP, runs the scheduler thread and drives the other ranks through the SPMD
+command protocol (``parallel.driver``); it re-executes this module once per extra rank with
+``--rank r`` (one process per GPU). Endpoints (reference ``server.py:1162-1183``):
+
+* ``GET /health`` - 200 once the model is loaded and every worker process is alive, else 503;
+* ``GET /v1/models``;
+* ``POST /v1/chat/completions`` - streaming SSE (``data: [DONE]`` terminated) and non-streaming;
+  honours ``max_tokens``, ``temperature``, ``ignore_eos``, ``chat_template_kwargs.enable_thinking``
+  and ``stream_options.include_usage``; ``usage.prompt_tokens_details.cached_tokens`` reports
+  prompt tokens served from the session cache;
+* ``POST /v1/completions`` - ``prompt`` as text or as a list of token ids; the response carries
+  the generated ``token_ids`` too (the id-level benchmark workloads use it);
+* ``POST /reset_prefix_cache``; ``POST /v1/score`` (teacher-forced log-probabilities);
+* ``POST /debug/fault`` (only with ``QB_FAULT_ENDPOINT=1``) - accuracy-gate calibration faults.
+"""
+
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+import uuid
+
+import torch
+
+
+def parse(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model-path", default=os.environ.get("MODEL_PATH", "tiny"))
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    ap.add_argument("--tp", type=int, default=1)
+    ap.add_argument("--rank", type=int, default=0)
+    ap.add_argument("--master-port", type=int, default=29555)
+    ap.add_argument("--max-seq-len", type=int, default=16384)
+    ap.add_argument("--max-batch", type=int, default=32)
+    ap.add_argument("--kv-tokens", type=int, default=None)
+    ap.add_argument("--snapshots", type=int, default=None)
+    ap.add_argument("--prefill-chunk", type=int, default=2048)
+    ap.add_argument("--token-budget", type=int, default=2048)
+    ap.add_argument("--device", default="auto", choices=["auto", "cuda", "cpu"])
+    ap.add_argument("--dtype", default="auto", choices=["auto", "bf16", "fp32"])
+    ap.add_argument("--seed", type=int, default=0)
+    return ap.parse_args(argv)
+
+
+def _device(args):
+    use_cuda = args.device == "cuda" or (args.device == "auto" and torch.cuda.is_available())
+    return torch.device("cuda", args.rank % max(1, torch.cuda.device_count())) if use_cuda else torch.device("cpu")
+
+
+def _dtype(args, device):
+    if args.dtype == "fp32" or (args.dtype == "auto" and device.type == "cpu"):
+        return torch.float32
+    return torch.bfloat16
+
+
+def _init_dist(args):
+    from ..parallel import comm as commmod
+
+    os.environ.update(RANK=str(args.rank), WORLD_SIZE=str(args.tp), LOCAL_RANK=str(args.rank),
+                      MASTER_ADDR=os.environ.get("MASTER_ADDR", "127.0.0.1"), MASTER_PORT=str(args.master_port))
+    device = _device(args)
+    if device.type == "cuda":
+        torch.cuda.set_device(device)
+    if args.tp > 1:
+        commmod.init("nccl" if device.type == "cuda" else "gloo", timeout_s=3600)
+    return device
+
+
+def _build(args, device):
+    from ..parallel.driver import command_group, pool_handshake
+    from .engine import PoolSpec, build_model
+
+    spec = PoolSpec(lanes=args.max_batch, max_seq=args.max_seq_len, kv_tokens=args.kv_tokens,
+                    snapshots=args.snapshots)
+    model, _ = build_model(args.model_path, args.rank, args.tp, device, spec, dtype=_dtype(args, device),
+                           seed=args.seed)
+    group = command_group(args.tp)
+    pool_handshake(model)
+    return model, group
+
+
+def run_worker(args) -> None:
+    from ..parallel.driver import Channel, serve_worker
+
+    device = _init_dist(args)
+    model, group = _build(args, device)
+    serve_worker(model, Channel(group))
+
+
+# ============================================================================ engine
+class Engine:
+    """Rank 0: model + scheduler thread + tokenizer; owns the worker processes."""
+
+    def __init__(self, args, workers: list[subprocess.Popen]):
+        self.args = args
+        self.workers = workers
+        self.ready = False
+        self.error: str | None = None
+        self.sched = None
+        self.runner = None
+        self.tok = None
+        self.model_name = os.path.basename(str(args.model_path).rstrip("/")) or "qwen3.5"
+        self.thread = threading.Thread(target=self._boot, daemon=True)
+        self.thread.start()
+
+    def _boot(self):
+        try:
+            from ..parallel.driver import Broadcaster, Channel
+            from .block_pool import BlockAllocator
+            from .scheduler import Scheduler
+            from .session_cache import SessionCache
+            from .tokenizer import load_tokenizer
+
+            device = _init_dist(self.args)
+            model, group = _build(self.args, device)
+            self.model = model
+            self.runner = Broadcaster(model, Channel(group) if self.args.tp > 1 else None)
+            cache = SessionCache(BlockAllocator(model.num_blocks, model.block_size), model.block_size,
+                                 model.num_snapshots)
+            self.sched = Scheduler(self.runner, cache, prefill_chunk=self.args.prefill_chunk,
+                                   token_budget=self.args.token_budget)
+            path = self.args.model_path if os.path.isdir(str(self.args.model_path)) else None
+            self.tok = load_tokenizer(path, model.cfg.vocab, model.cfg.eos_token_id)
+            self.ready = True
+            self.sched.run()
+        except Exception as e:  # surfaced through /health
+            import traceback
+
+            traceback.print_exc()
+            self.error = f"{type(e).__name__}: {e}"
+
+    def healthy(self) -> bool:
+        return self.ready and self.error is None and all(w.poll() is None for w in self.workers)
+
+    def shutdown(self):
+        if self.sched is not None:
+            self.sched.stop()
+        if self.runner is not None and self.args.tp > 1:
+            try:
+                self.runner.shutdown()
+            except Exception:
+                pass
+        for w in self.workers:
+            if w.poll() is None:
+                w.terminate()
+
+
+# ============================================================================ HTTP
+def make_app(engine: Engine):
+    from aiohttp import web
+
+    from .scheduler import Request, ScoreJob
+    from .tokenizer import Detokenizer
+
+    routes = web.RouteTableDef()
+
+    def submit(prompt_ids, max_new, temperature, stop, suffix_len, has_history):
+        loop = asyncio.get_running_loop()
+        q: asyncio.Queue = asyncio.Queue()
+
+        def emit(ev):
+            loop.call_soon_threadsafe(q.put_nowait, ev)
+
+        engine.sched.submit(Request(list(prompt_ids), int(max_new), emit, float(temperature), frozenset(stop),
+                                    suffix_len, has_history))
+        return q
+
+    def stops(body):
+        eos = engine.tok.eos_token_id
+        return set() if body.get("ignore_eos", False) or eos is None else {int(eos)}
+
+    async def stream_tokens(q, on_token):
+        while True:
+            kind, val = await q.get()
+            if kind == "tok":
+                await on_token(val)
+            elif kind == "end":
+                return val, None
+            else:
+                return None, str(val)
+
+    @routes.get("/health")
+    async def health(_):
+        if engine.healthy():
+            return web.json_response({"status": "ok"})
+        return web.json_response({"status": "unavailable", "error": engine.error}, status=503)
+
+    @routes.get("/v1/models")
+    async def models(_):
+        return web.json_response({"object": "list", "data": [{"id": engine.model_name, "object": "model"}]})
+
+    async def generate(request, prompt_ids, suffix_len, has_history, body, chat: bool):
+        max_new = int(body.get("max_tokens") or body.get("max_completion_tokens") or 256)
+        temp = float(body.get("temperature", 0.0) or 0.0)
+        stream = bool(body.get("stream", False))
+        usage_opt = bool((body.get("stream_options") or {}).get("include_usage", False))
+        rid = ("chatcmpl-" if chat else "cmpl-") + uuid.uuid4().hex[:24]
+        created = int(time.time())
+        q = submit(prompt_ids, max_new, temp, stops(body), suffix_len, has_history)
+        detok = Detokenizer(engine.tok)
+        out_ids: list[int] = []
+        obj = "chat.completion.chunk" if chat else "text_completion"
+
+        def chunk(text=None, finish=None, role=False, ids=None):
+            if chat:
+                delta = {"role": "assistant"} if role else ({"content": text} if text is not None else {})
+                ch = {"index": 0, "delta": delta, "finish_reason": finish}
+            else:
+                ch = {"index": 0, "text": text or "", "finish_reason": finish}
+                if ids is not None:
+                    ch["token_ids"] = ids
+            return {"id": rid, "object": obj, "created": created, "model": engine.model_name, "choices": [ch]}
+
+        if stream:
+            resp = web.StreamResponse(headers={"Content-Type": "text/event-stream", "Cache-Control": "no-cache"})
+            await resp.prepare(request)
+
+            async def send(o):
+                await resp.write(b"data: " + json.dumps(o).encode() + b"\n\n")
+
+            if chat:
+                await send(chunk(role=True))
+
+            async def on_tok(t):
+                out_ids.append(t)
+                text = detok.push(t)
+                if text or not chat:
+                    await send(chunk(text, ids=[t] if not chat else None))
+
+            end, err = await stream_tokens(q, on_tok)
+            if err is not None:
+                await send({"error": {"message": err, "type": "server_error"}})
+            else:
+                tail = detok.flush()
+                if tail:
+                    await send(chunk(tail))
+                reason = "stop" if end[0] == "stop" else "length"
+                await send(chunk(None, reason))
+                if usage_opt:
+                    await send({"id": rid, "object": obj, "created": created, "model": engine.model_name,
+                                "choices": [], "usage": usage(prompt_ids, end)})
+            await resp.write(b"data: [DONE]\n\n")
+            await resp.write_eof()
+            return resp
+
+        async def on_tok(t):
+            out_ids.append(t)
+
+        end, err = await stream_tokens(q, on_tok)
+        if err is not None:
+            return web.json_response({"error": {"message": err, "type": "server_error"}}, status=500)
+        text = engine.tok.decode(out_ids)
+        reason = "stop" if end[0] == "stop" else "length"
+        if chat:
+            choice = {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
+            o = "chat.completion"
+        else:
+            choice = {"index": 0, "text": text, "token_ids": out_ids, "finish_reason": reason}
+            o = "text_completion"
+        return web.json_response({"id": rid, "object": o, "created": created, "model": engine.model_name,
+                                  "choices": [choice], "usage": usage(prompt_ids, end)})
+
+    def usage(prompt_ids, end):
+        return {"prompt_tokens": len(prompt_ids), "completion_tokens": int(end[1]),
+                "total_tokens": len(prompt_ids) + int(end[1]),
+                "prompt_tokens_details": {"cached_tokens": int(end[2])}}
+
+    @routes.post("/v1/chat/completions")
+    async def chat(request):
+        if not engine.healthy():
+            return web.json_response({"error": {"message": "not ready"}}, status=503)
+        body = await request.json()
+        msgs = body.get("messages") or []
+        kw = body.get("chat_template_kwargs") or {}
+        ids, suffix = engine.tok.render_chat(msgs, enable_thinking=bool(kw.get("enable_thinking", False)))
+        has_history = any(m.get("role") == "assistant" for m in msgs)
+        return await generate(request, ids, suffix, has_history, body, chat=True)
+
+    @routes.post("/v1/completions")
+    async def completions(request):
+        if not engine.healthy():
+            return web.json_response({"error": {"message": "not ready"}}, status=503)
+        body = await request.json()
+        prompt = body.get("prompt")
+        if isinstance(prompt, list) and prompt and isinstance(prompt[0], list):
+            prompt = prompt[0]
+        ids = [int(x) for x in prompt] if isinstance(prompt, list) else engine.tok.encode(str(prompt))
+        return await generate(request, ids, 0, False, body, chat=False)
+
+    @routes.post("/reset_prefix_cache")
+    async def reset(_):
+        n = await asyncio.get_running_loop().run_in_executor(None, engine.sched.reset_prefix_cache)
+        return web.json_response({"evicted": n})
+
+    @routes.post("/v1/score")
+    async def score(request):
+        body = await request.json()
+        p = body.get("prompt", [])
+        c = body.get("continuation", [])
+        pids = [int(x) for x in p] if isinstance(p, list) else engine.tok.encode(p)
+        cids = [int(x) for x in c] if isinstance(c, list) else engine.tok.encode(c)
+        ids = pids + cids
+
+        def finish(logits):
+            lp = torch.log_softmax(logits.float(), dim=-1)
+            tgt = torch.tensor(cids, device=lp.device)
+            return lp[torch.arange(len(cids), device=lp.device), tgt].tolist()
+
+        job = ScoreJob(ids, len(pids), finish)
+        engine.sched.score(job)
+        await asyncio.get_running_loop().run_in_executor(None, job.done.wait, 600)
+        if job.error:
+            return web.json_response({"error": {"message": job.error}}, status=500)
+        return web.json_response({"logprobs": job.result, "tokens": cids})
+
+    @routes.post("/debug/fault")
+    async def fault(request):
+        if os.environ.get("QB_FAULT_ENDPOINT", "0") != "1":
+            return web.json_response({"error": {"message": "fault endpoint disabled"}}, status=404)
+        body = await request.json()
+        from .faults import FAULTS
+
+        name = body.get("name")
+        if name not in FAULTS:
+            return web.json_response({"error": {"message": f"unknown fault {name}"}}, status=400)
+        value = body.get("value")
+        engine.sched.control(lambda: engine.runner.set_fault(name, value))
+        return web.json_response({"fault": name, "value": value})
+
+    app = web.Application(client_max_size=64 * 1024 * 1024)
+    app.add_routes(routes)
+    return app
+
+
+def start_workers(args) -> list[subprocess.Popen]:
+    procs = []
+    for r in range(1, args.tp):
+        cmd = [sys.executable, "-m", "qwen35_b200.serving.server", "--rank", str(r)] + [
+            a for a in sys.argv[1:] if not a.startswith("--rank")]
+        procs.append(subprocess.Popen(cmd, env=dict(os.environ)))
+    return procs
+
+
+def main(argv=None):
+    args = parse(argv)
+    if args.rank > 0:
+        run_worker(args)
+        return
+    from aiohttp import web
+
+    workers = start_workers(args)
+    engine = Engine(args, workers)
+    try:
+        web.run_app(make_app(engine), host=args.host, port=args.port, print=None)
+    finally:
+        engine.shutdown()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,137 @@
+"""Tokenizer adapters and incremental detokenization.
+
+``load_tokenizer(model_dir)`` returns the checkpoint's HuggingFace tokenizer when the directory
+has one, and otherwise ``ByteTokenizer``: UTF-8 bytes map to ids 0..255 and the chat-template
+specials sit at the top of the vocabulary (``chat.TokenTemplate.for_vocab``), which is what the
+random-init models use. ``Detokenizer`` turns a growing id list into text deltas whose
+concatenation equals decoding the whole list at once (it holds back text that ends in an
+incomplete UTF-8 sequence); reference behaviour ``server.py:325-349``. ``PromptCache`` reuses the
+ids of the longest previously tokenized prefix that ends at a special token (reference
+``prompt_cache.py:21-80``).
+"""
+
+from __future__ import annotations
+
+import os
+from collections import OrderedDict
+
+from .chat import TokenTemplate
+
+
+class ByteTokenizer:
+    """Bytes as token ids plus the template specials; ``eos`` is the model's eos id."""
+
+    def __init__(self, vocab: int, eos: int):
+        self.vocab = vocab
+        self.eos_token_id = eos
+        self.template = TokenTemplate.for_vocab(vocab)
+        self._special = self.template.reserved | {eos}
+
+    def encode(self, text: str) -> list[int]:
+        return list(text.encode("utf-8"))
+
+    def decode(self, ids) -> str:
+        return bytes(i for i in ids if 0 <= i < 256).decode("utf-8", errors="replace")
+
+    def render_chat(self, messages: list[dict], enable_thinking: bool = False) -> tuple[list[int], int]:
+        msgs = [(m["role"], self.encode(str(m.get("content") or ""))) for m in messages]
+        return self.template.render(msgs, True, enable_thinking)
+
+
+class HFTokenizer:
+    """A HuggingFace tokenizer with Qwen's chat template."""
+
+    def __init__(self, path: str):
+        from transformers import AutoTokenizer
+
+        self.tok = AutoTokenizer.from_pretrained(path)
+        self.eos_token_id = self.tok.eos_token_id
+
+    def encode(self, text: str) -> list[int]:
+        return self.tok.encode(text, add_special_tokens=False)
+
+    def decode(self, ids) -> str:
+        return self.tok.decode(ids, skip_special_tokens=True)
+
+    def render_chat(self, messages: list[dict], enable_thinking: bool = False) -> tuple[list[int], int]:
+        text = self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=True,
+                                            enable_thinking=enable_thinking)
+        ids = self.encode(text)
+        suffix = 0
+        if not enable_thinking:
+            bare = self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=True,
+                                                enable_thinking=True)
+            common = os.path.commonprefix([text, bare])
+            suffix = max(0, len(ids) - len(self.encode(common)))
+        return ids, suffix
+
+
+def load_tokenizer(model_dir: str | None, vocab: int, eos: int):
+    if model_dir and any(os.path.exists(os.path.join(model_dir, f)) for f in ("tokenizer.json", "tokenizer_config.json")):
+        try:
+            return HFTokenizer(model_dir)
+        except Exception:
+            pass
+    return ByteTokenizer(vocab, eos)
+
+
+class Detokenizer:
+    """Incremental decode: ``push(id)`` returns the new text a full decode would add."""
+
+    def __init__(self, tokenizer, window: int = 8):
+        self.tok = tokenizer
+        self.ids: list[int] = []
+        self.prefix = 0  # start of the decode window
+        self.read = 0  # ids already reflected in emitted text
+        self.window = window
+
+    def push(self, tid: int) -> str:
+        self.ids.append(tid)
+        prev = self.tok.decode(self.ids[self.prefix:self.read])
+        cur = self.tok.decode(self.ids[self.prefix:])
+        if cur.endswith("�"):
+            return ""  # incomplete multi-byte character: wait for more ids
+        delta = cur[len(prev):]
+        self.read = len(self.ids)
+        if self.read - self.prefix > self.window:
+            self.prefix = self.read - self.window
+        return delta
+
+    def flush(self) -> str:
+        prev = self.tok.decode(self.ids[self.prefix:self.read])
+        cur = self.tok.decode(self.ids[self.prefix:])
+        self.read = len(self.ids)
+        return cur[len(prev):]
+
+
+class PromptCache:
+    """Incremental tokenization of chat prompts that share a prefix with an earlier prompt."""
+
+    def __init__(self, tokenizer, capacity: int = 256, boundary: str = "<|im_end|>"):
+        self.tok = tokenizer
+        self.capacity = capacity
+        self.boundary = boundary
+        self.entries: OrderedDict[str, list[int]] = OrderedDict()
+
+    def encode(self, text: str) -> list[int]:
+        best = ""
+        for k in self.entries:
+            if len(k) > len(best) and text.startswith(k):
+                best = k
+        if best:
+            ids = list(self.entries[best]) + self.tok.encode(text[len(best):])
+            self.entries.move_to_end(best)
+        else:
+            ids = self.tok.encode(text)
+        cut = text.rfind(self.boundary)
+        if cut > 0:
+            key = text[: cut + len(self.boundary)]
+            if key not in self.entries:
+                self.entries[key] = self.tok.encode(key)
+                if len(self.entries) > self.capacity:
+                    self.entries.popitem(last=False)
+        return ids
+
+    def selfcheck(self, samples: list[str]) -> bool:
+        """Incremental ids equal full tokenization for every sample (run at boot)."""
+        return all(self.encode(s) == self.tok.encode(s) for s in samples)

@@ -1,0 +1,138 @@
+"""The HTTP server end to end on the tiny random-init model (CPU): SSE contract, token-id
+completions, exact max_tokens, cache reuse across turns, reset, score, health, faults, TP=2."""
+
+import json
+import os
+import random
+import socket
+import subprocess
+import sys
+import time
+
+import pytest
+import requests
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def start(tp=1, env_extra=None, model="tiny"):
+    port = free_port()
+    env = dict(os.environ, PYTHONPATH=ROOT, OMP_NUM_THREADS="2", **(env_extra or {}))
+    cmd = [sys.executable, "-m", "qwen35_b200.serving.server", "--model-path", model, "--port", str(port),
+           "--tp", str(tp), "--device", "cpu", "--max-batch", "4", "--max-seq-len", "2048", "--kv-tokens", "16384",
+           "--master-port", str(free_port())]
+    proc = subprocess.Popen(cmd, cwd=ROOT, env=env, stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL,
+                            start_new_session=True)
+    url = f"http://127.0.0.1:{port}"
+    for _ in range(300):
+        try:
+            if requests.get(url + "/health", timeout=2).status_code == 200:
+                return proc, url
+        except Exception:
+            pass
+        if proc.poll() is not None:
+            raise RuntimeError("server exited")
+        time.sleep(0.5)
+    proc.kill()
+    raise RuntimeError("server did not become healthy")
+
+
+def stop(proc):
+    try:
+        os.killpg(proc.pid, 15)
+    except Exception:
+        pass
+    proc.wait(timeout=30)
+
+
+@pytest.fixture(scope="module")
+def server():
+    proc, url = start()
+    yield url
+    stop(proc)
+
+
+def sse(resp):
+    out = []
+    for line in resp.iter_lines():
+        if not line:
+            continue
+        assert line.startswith(b"data: "), line
+        payload = line[6:]
+        if payload == b"[DONE]":
+            out.append("[DONE]")
+            break
+        out.append(json.loads(payload))
+    return out
+
+
+def test_completions_token_ids_exact_length(server):
+    ids = [random.Random(1).randrange(3000) for _ in range(50)]
+    r = requests.post(server + "/v1/completions", json={"prompt": ids, "max_tokens": 12, "ignore_eos": True}).json()
+    ch = r["choices"][0]
+    assert len(ch["token_ids"]) == 12 and r["usage"]["completion_tokens"] == 12
+    assert r["usage"]["prompt_tokens"] == 50
+    r2 = requests.post(server + "/v1/completions", json={"prompt": ids, "max_tokens": 12, "ignore_eos": True}).json()
+    assert r2["choices"][0]["token_ids"] == ch["token_ids"]  # greedy + exact-duplicate cache
+
+
+def test_chat_stream_contract_and_usage(server):
+    body = {"messages": [{"role": "user", "content": "hello there, how are you?"}], "max_tokens": 10,
+            "stream": True, "ignore_eos": True, "stream_options": {"include_usage": True},
+            "chat_template_kwargs": {"enable_thinking": False}}
+    with requests.post(server + "/v1/chat/completions", json=body, stream=True) as resp:
+        chunks = sse(resp)
+    assert chunks[-1] == "[DONE]"
+    assert chunks[0]["choices"][0]["delta"] == {"role": "assistant"}
+    finals = [c for c in chunks[:-1] if c["choices"] and c["choices"][0]["finish_reason"]]
+    assert finals and finals[-1]["choices"][0]["finish_reason"] == "length"
+    usage = [c for c in chunks[:-1] if c.get("usage")]
+    assert usage and usage[-1]["usage"]["completion_tokens"] == 10
+
+
+def test_second_turn_reuses_cache(server):
+    msgs = [{"role": "user", "content": "tell me about the sea " * 5}]
+    r1 = requests.post(server + "/v1/chat/completions", json={"messages": msgs, "max_tokens": 8, "ignore_eos": True}).json()
+    msgs += [{"role": "assistant", "content": r1["choices"][0]["message"]["content"]},
+             {"role": "user", "content": "and the mountains?"}]
+    r2 = requests.post(server + "/v1/chat/completions", json={"messages": msgs, "max_tokens": 8, "ignore_eos": True}).json()
+    assert r2["usage"]["prompt_tokens_details"]["cached_tokens"] > 0
+
+
+def test_reset_score_health(server):
+    assert requests.get(server + "/health").status_code == 200
+    assert requests.get(server + "/v1/models").json()["data"]
+    ev = requests.post(server + "/reset_prefix_cache").json()
+    assert "evicted" in ev
+    s = requests.post(server + "/v1/score", json={"prompt": [5, 6, 7, 8], "continuation": [9, 10, 11]}).json()
+    assert len(s["logprobs"]) == 3 and all(x <= 0 for x in s["logprobs"])
+    assert requests.post(server + "/debug/fault", json={"name": "rope_base", "value": 10}).status_code == 404
+
+
+@pytest.mark.slow
+def test_fault_endpoint_changes_output_and_tp2_matches_tp1(tiny_dir):
+    ids = list(range(100, 180))
+    p1, u1 = start(env_extra={"QB_FAULT_ENDPOINT": "1"}, model=tiny_dir)
+    try:
+        base = requests.post(u1 + "/v1/completions", json={"prompt": ids, "max_tokens": 10, "ignore_eos": True}).json()
+        assert requests.post(u1 + "/debug/fault", json={"name": "drop_expert", "value": 3}).status_code == 200
+        requests.post(u1 + "/reset_prefix_cache")
+        assert requests.post(u1 + "/debug/fault", json={"name": "rope_base", "value": 10.0}).status_code == 200
+        hurt = requests.post(u1 + "/v1/completions", json={"prompt": ids, "max_tokens": 10, "ignore_eos": True}).json()
+        assert hurt["choices"][0]["token_ids"] != base["choices"][0]["token_ids"]
+    finally:
+        stop(p1)
+    p2, u2 = start(tp=2, model=tiny_dir)
+    try:
+        tp2 = requests.post(u2 + "/v1/completions", json={"prompt": ids, "max_tokens": 10, "ignore_eos": True}).json()
+        assert tp2["choices"][0]["token_ids"] == base["choices"][0]["token_ids"]
+    finally:
+        stop(p2)
