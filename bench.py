@@ -131,44 +131,14 @@ def _elapsed_ms(a, b) -> float:
 
 
 def build_model(args, rank, world, device):
-    import torch
+    """This rank's model (random init, full or tiny geometry) wrapped in its CUDA-graph runner."""
+    from qwen35_b200.serving.engine import PoolSpec, build_model as build
 
-    from qwen35_b200.models.config import full_config, tiny_config
-    from qwen35_b200.models.qwen35 import Model
-    from qwen35_b200.models.weights import expert_bytes_per_layer, random_weights
-    from qwen35_b200.parallel.comm import Comm
-    from qwen35_b200.parallel.plan import plan
-
-    cfg = full_config() if args.model == "full" else tiny_config()
-    p = plan(cfg, rank, world)
-    bs = 16
-    lanes = args.concurrency
-    # paged KV sized for every in-flight context plus cached history (need-based, with a cap)
-    kv_tokens = int(1.5 * lanes * args.max_seq) if args.model == "tiny" else min(lanes * args.max_seq,
-                                                                                 (480_000 * world) // 1)
-    num_blocks = kv_tokens // bs + 1
-    num_snaps = 2 * lanes + 16
-    # memory plan: pools first, then as many distinct expert layers as fit
-    kv_bytes = num_blocks * bs * len(cfg.full_layers) * 2 * p.kv.count * cfg.head_dim * 2
-    nv, nk = p.dn_v.count, p.dn_k.count
-    conv_ch = 2 * nk * cfg.dn_k_dim + nv * cfg.dn_v_dim
-    per_state = len(cfg.linear_layers) * (nv * cfg.dn_k_dim * cfg.dn_v_dim * 4 + conv_ch * 3 * 2)
-    state_bytes = (lanes + num_snaps) * per_state
-    distinct = None
-    if device.type == "cuda" and args.model == "full":
-        total = torch.cuda.get_device_properties(device).total_memory
-        dense = 20e9 / world + 4e9  # attention/DeltaNet/shared/router shards + embedding + lm_head
-        budget = total - dense - kv_bytes - state_bytes - 14e9
-        per_layer = expert_bytes_per_layer(cfg, p)
-        distinct = max(1, min(cfg.layers, int(budget // per_layer)))
-        if distinct >= cfg.layers:
-            distinct = None
-    w = random_weights(cfg, p, device, torch.bfloat16, seed=args.seed, with_mtp=False,
-                       distinct_expert_layers=distinct)
-    comm = Comm(rank, world, None, device)
-    m = Model(cfg, w, p, comm, device=device, dtype=torch.bfloat16, max_batch=lanes, max_seq=args.max_seq,
-              block_size=bs, num_blocks=num_blocks, num_snapshots=num_snaps)
-    return cfg, m, distinct
+    kv_tokens = int(1.5 * args.concurrency * args.max_seq) if args.model == "tiny" else \
+        min(args.concurrency * args.max_seq, 480_000 * world)
+    spec = PoolSpec(lanes=args.concurrency, max_seq=args.max_seq, kv_tokens=kv_tokens)
+    runner, distinct = build(args.model, rank, world, device, spec, seed=args.seed)
+    return runner.cfg, runner, distinct
 
 
 def main():
@@ -224,11 +194,13 @@ def main():
         t = _elapsed_ms(model.bench_marks[0], model.bench_marks[1]) if len(model.bench_marks) >= 2 else 0.0
         gathered = [None] * world
         dist.all_gather_object(gathered, t)
+        if hasattr(model, "release"):
+            model.release()
         dist.destroy_process_group()
         return
 
     runner = Broadcaster(model, Channel(group) if world > 1 else None)
-    alloc = BlockAllocator(model.num_blocks, model.block_size)
+    alloc = BlockAllocator(model.num_blocks, model.block_size)  # the runner's max_batch excludes the pad lane
     cache = SessionCache(alloc, model.block_size, model.num_snapshots)
     sched = Scheduler(runner, cache, prefill_chunk=args.prefill_chunk, token_budget=args.token_budget)
     spec = ChatSpec(sessions=args.sessions, concurrency=args.concurrency, turns=args.turns, seed=args.seed,
@@ -356,6 +328,8 @@ def main():
         with open(args.out, "w") as f:
             f.write(line + "\n")
     if world > 1:
+        if hasattr(model, "release"):
+            model.release()
         dist.destroy_process_group()
 
 

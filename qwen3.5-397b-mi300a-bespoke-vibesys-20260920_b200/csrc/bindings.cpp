@@ -194,9 +194,10 @@ Tensor causal_conv_varlen(Tensor x, Tensor state, Tensor w, Tensor seg_lane, Ten
   TORCH_CHECK(state.stride(2) == 1 && state.stride(1) == state.size(2), "conv: state [lanes, C, K-1] rows contiguous");
   const int T = x.size(0), C = x.size(1), K = w.size(1);
   Tensor out = at::empty({T, C}, x.options());
-  LAUNCH(qb::causal_conv_varlen(x.data_ptr(), x.stride(0), state.data_ptr(), state.stride(0), w.data_ptr(),
-                                seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), C, K, out.data_ptr(),
-                                stream()));
+  LAUNCH(qb::causal_conv_varlen_t(x.data_ptr(), x.stride(0), state.data_ptr(), state.stride(0), w.data_ptr(),
+                                  seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), T, C, K,
+                                  out.data_ptr(), stream()));
+  g_launches.fetch_add(1, std::memory_order_relaxed);  // output + state kernels
   return out;
 }
 
@@ -207,10 +208,12 @@ Tensor gated_delta_varlen(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, T
   TORCH_CHECK(state.stride(3) == 1 && state.stride(2) == dv && state.stride(1) == dk * dv, "delta: state layout");
   const int T = qkv.size(0);
   Tensor out = at::empty({T, nv, dv}, qkv.options());
-  LAUNCH(qb::gated_delta_varlen(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0), a_log.data_ptr<float>(),
-                                dt_bias.data_ptr<float>(), state.data_ptr<float>(), state.stride(0),
-                                seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), nk, nv, dk, dv,
-                                out.data_ptr(), stream()));
+  Tensor scratch = at::empty({(long)T * (2 * nk * dk + 2 * nv)}, qkv.options().dtype(at::kFloat));
+  LAUNCH(qb::gated_delta_varlen_t(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0),
+                                  a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), state.data_ptr<float>(),
+                                  state.stride(0), seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), T,
+                                  nk, nv, dk, dv, scratch.data_ptr<float>(), out.data_ptr(), stream()));
+  g_launches.fetch_add(1, std::memory_order_relaxed);  // prep + recurrence kernels
   return out;
 }
 
@@ -260,6 +263,8 @@ Tensor moe_routed_fp4(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13
 
 // ------------------------------------------------------------------ status
 int64_t launches() { return g_launches.load(); }
+// graph replays launch the captured kernels without passing through these bindings
+void add_launches(int64_t n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
 Tensor status(Tensor like) { return status_tensor(like.device()).clone(); }
 void clear_status(Tensor like) { status_tensor(like.device()).zero_(); }
 
@@ -283,5 +288,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_routed_fp4", &moe_routed_fp4);
   m.def("status", &status);
   m.def("launches", &launches, "number of kernels launched through the bindings so far");
+  m.def("add_launches", &add_launches, "account kernels launched by a CUDA-graph replay");
   m.def("clear_status", &clear_status);
 }

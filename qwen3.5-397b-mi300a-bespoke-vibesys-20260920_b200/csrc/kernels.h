@@ -33,11 +33,11 @@ int shared_gate_combine(const void* routed, const void* shared, const void* gl, 
 int qk_norm_rope_kv_write(const void* qkv, long ldqkv, int nq, int nkv, int hd, const float* qn, const float* kn,
                           const int* pos, const int* rows, void* kc, void* vc, void* qout, int T, int rot,
                           float theta, float eps, cudaStream_t s);
-int causal_conv_varlen(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
-                       const int* cu, int S, int C, int K, void* out, cudaStream_t s);
-int gated_delta_varlen(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
-                       const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
-                       int S, int nk, int nv, int dk, int dv, void* out, cudaStream_t s);
+int causal_conv_varlen_t(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
+                         const int* cu, int S, int T, int C, int K, void* out, cudaStream_t s);
+int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
+                         const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
+                         int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out, cudaStream_t s);
 int attention_varlen(const void* q, const void* kc, const void* vc, const int* table, int max_blocks,
                      const int* pos, const int* seg_lane, const int* cu, int S, int T, int nq, int nkv, int hd,
                      int block_size, int splits, float* ws, void* out, cudaStream_t s);

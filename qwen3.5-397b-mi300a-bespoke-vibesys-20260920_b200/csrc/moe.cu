@@ -830,9 +830,12 @@ static int moe_launch(const CUtensorMap& tw, const CUtensorMap& tx, const MoeArg
   return (int)cudaGetLastError();
 }
 
+// Token-tile width: an expert with more tokens than one tile converts its weight tile once per
+// tile, so size the tile for about twice the mean load (routing is uneven) rather than the mean.
 static int pick_bn(int cap, int count) {
   const int avg = (cap + count - 1) / (count > 0 ? count : 1);
-  return avg <= 16 ? 16 : avg <= 32 ? 32 : avg <= 64 ? 64 : 128;
+  const int want = 2 * avg + 2;
+  return want <= 16 ? 16 : want <= 32 ? 32 : want <= 64 ? 64 : 128;
 }
 
 int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8_t* ws, int n_rows, int k_cols,

@@ -22,143 +22,187 @@ __device__ __forceinline__ int seg_of(const int* cu, int S, int t) {
 }
 
 // ------------------------------------------------------------------ causal conv
+// Output kernel: one thread per (token, channel); the K-1 inputs before a segment's first
+// token come from the lane's saved window. State kernel (launched after): the window becomes
+// the last K-1 inputs of the segment (old window entries when the segment is shorter).
 template <int K>
-__global__ void conv_kernel(const bf16* x, long ldx, bf16* state, long lane_stride, const bf16* w,
-                            const int* seg_lane, const int* cu, int C, bf16* out) {
+__global__ void conv_out_kernel(const bf16* x, long ldx, const bf16* state, long lane_stride, const bf16* w,
+                                const int* seg_lane, const int* cu, int S, int C, bf16* out) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
+  const int t = blockIdx.y;
+  if (c >= C) return;
+  const int s = seg_of(cu, S, t);
+  const int t0 = cu[s];
+  const bf16* st = state + (long)seg_lane[s] * lane_stride + (long)c * (K - 1);
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < K; ++j) {
+    const int src = t - (K - 1) + j;  // absolute row of input j
+    const float xv = src >= t0 ? __bfloat162float(x[(long)src * ldx + c]) : __bfloat162float(st[src - t0 + K - 1]);
+    acc += __bfloat162float(w[(long)c * K + j]) * xv;
+  }
+  const float a = rbf2(acc);
+  out[(long)t * C + c] = __float2bfloat16(a / (1.f + expf(-a)));
+}
+
+template <int K>
+__global__ void conv_state_kernel(const bf16* x, long ldx, bf16* state, long lane_stride, const int* seg_lane,
+                                  const int* cu, int C) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int s = blockIdx.y;
   if (c >= C) return;
-  const int lane = seg_lane[s];
-  bf16* st = state + (long)lane * lane_stride + (long)c * (K - 1);
-  float win[K - 1], wt[K];
+  const int t0 = cu[s], len = cu[s + 1] - cu[s];
+  bf16* st = state + (long)seg_lane[s] * lane_stride + (long)c * (K - 1);
 #pragma unroll
-  for (int j = 0; j < K - 1; ++j) win[j] = __bfloat162float(st[j]);
-#pragma unroll
-  for (int j = 0; j < K; ++j) wt[j] = __bfloat162float(w[(long)c * K + j]);
-  for (int t = cu[s]; t < cu[s + 1]; ++t) {
-    const float xt = __bfloat162float(x[(long)t * ldx + c]);
-    float acc = wt[K - 1] * xt;
-#pragma unroll
-    for (int j = 0; j < K - 1; ++j) acc += wt[j] * win[j];
-    const float a = rbf2(acc);
-    out[(long)t * C + c] = __float2bfloat16(a / (1.f + expf(-a)));
-#pragma unroll
-    for (int j = 0; j < K - 2; ++j) win[j] = win[j + 1];
-    win[K - 2] = xt;
+  for (int i = 0; i < K - 1; ++i) {  // ascending: reads index len + i > i before it is overwritten
+    const int src = len + i;       // position in [window(K-1) | segment(len)]
+    st[i] = src < K - 1 ? st[src] : x[(long)(t0 + src - (K - 1)) * ldx + c];
   }
-#pragma unroll
-  for (int j = 0; j < K - 1; ++j) st[j] = __float2bfloat16(win[j]);
 }
 
-int causal_conv_varlen(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
-                       const int* cu, int S, int C, int K, void* out, cudaStream_t s) {
-  if (!S) return 0;
+int causal_conv_varlen_t(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
+                         const int* cu, int S, int T, int C, int K, void* out, cudaStream_t s) {
+  if (!S || !T) return 0;
   if (K != 4) return -1;
-  dim3 grid((C + 127) / 128, S);
-  conv_kernel<4><<<grid, 128, 0, s>>>((const bf16*)x, ldx, (bf16*)state, lane_stride, (const bf16*)w, seg_lane, cu,
-                                      C, (bf16*)out);
+  conv_out_kernel<4><<<dim3((C + 127) / 128, T), 128, 0, s>>>((const bf16*)x, ldx, (const bf16*)state, lane_stride,
+                                                               (const bf16*)w, seg_lane, cu, S, C, (bf16*)out);
+  conv_state_kernel<4><<<dim3((C + 127) / 128, S), 128, 0, s>>>((const bf16*)x, ldx, (bf16*)state, lane_stride,
+                                                                 seg_lane, cu, C);
   return (int)cudaGetLastError();
 }
 
 // ------------------------------------------------------------------ gated delta rule
-// One CTA per (value head, segment), DV threads; thread j owns state column j (DK fp32 values
-// in registers) so the recurrence needs no cross-thread reduction:
-//   S *= exp(g);  delta_j = (v_j - sum_i S_ij k_i) * beta;  S_ij += k_i delta_j;  o_j = sum_i S_ij q_i
-template <int DK>
-__global__ void __launch_bounds__(128) delta_kernel(const bf16* qkv, long ldqkv, const bf16* ab, long ldab,
-                                                    const float* a_log, const float* dt_bias, float* state,
-                                                    long lane_stride, const int* seg_lane, const int* cu, int nk,
-                                                    int nv, int dv, bf16* out) {
-  __shared__ float qs[DK], ks[DK], red[8], gb[2];
-  const int h = blockIdx.x, s = blockIdx.y, j = threadIdx.x;
-  const int lane = seg_lane[s];
-  const int hk = h / (nv / nk);
-  float* st = state + (long)lane * lane_stride + (long)h * DK * dv;
-  float S[DK];
-  if (j < dv) {
-#pragma unroll
-    for (int i = 0; i < DK; ++i) S[i] = st[(long)i * dv + j];
+// Prep kernel (parallel over tokens): per key head the l2-normalised q (times dk**-0.5) and k in
+// fp32, computed with the bf16 rounding points of the HF code; per value head the decay
+// exp(g) and beta. Recurrence kernel: grid (value head, segment, column block of 32); four
+// threads share one state column (32 rows each), so per token a thread does ~32-wide dot
+// products and two 2-step shuffle reductions. Tokens are staged in shared memory in chunks.
+__global__ void delta_prep_kernel(const bf16* qkv, long ldqkv, const bf16* ab, long ldab, const float* a_log,
+                                  const float* dt_bias, int nk, int nv, int dk, float* qn, float* kn, float* gb) {
+  const int t = blockIdx.x;
+  const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const bf16* row = qkv + (long)t * ldqkv;
+  const float scale = rsqrtf((float)dk);
+  for (int hh = w; hh < 2 * nk; hh += warps) {  // q heads then k heads
+    const bool isq = hh < nk;
+    const int h = isq ? hh : hh - nk;
+    const bf16* src = row + (isq ? 0 : (long)nk * dk) + (long)h * dk;
+    float ss = 0.f;
+    for (int i = lane; i < dk; i += 32) {
+      const float v = __bfloat162float(src[i]);
+      ss += rbf2(v * v);
+    }
+    ss = warp_sum(ss);
+    const float inv = rbf2(rsqrtf(rbf2(rbf2(ss) + 1e-6f)));
+    float* dst = (isq ? qn : kn) + ((long)t * nk + h) * dk;
+    for (int i = lane; i < dk; i += 32) {
+      const float v = rbf2(__bfloat162float(src[i]) * inv);
+      dst[i] = isq ? v * scale : v;
+    }
   }
-  const float A = -expf(a_log[h]);
-  const float dtb = dt_bias[h];
-  const float scale = rsqrtf((float)DK);
-  const int nw = (blockDim.x + 31) / 32;
-  for (int t = cu[s]; t < cu[s + 1]; ++t) {
-    const bf16* row = qkv + (long)t * ldqkv;
-    // l2norm of q and k in bf16 arithmetic (HF applies it to the bf16 tensors)
-    float qv = 0.f, kv = 0.f, qq = 0.f, kk = 0.f;
-    if (j < DK) {
-      qv = __bfloat162float(row[(long)hk * DK + j]);
-      kv = __bfloat162float(row[(long)nk * DK + (long)hk * DK + j]);
-      qq = rbf2(qv * qv);
-      kk = rbf2(kv * kv);
-    }
-    qq = warp_sum(qq);
-    kk = warp_sum(kk);
-    if ((j & 31) == 0) {
-      red[j / 32] = qq;
-      red[4 + j / 32] = kk;
-    }
-    if (j == 0) {
-      const float b = __bfloat162float(ab[(long)t * ldab + h]);
-      const float a = __bfloat162float(ab[(long)t * ldab + nv + h]);
-      gb[0] = A * softplus(a + dtb);   // log decay (fp32)
-      gb[1] = rbf2(1.f / (1.f + expf(-b)));  // beta, rounded like the bf16 sigmoid
-    }
-    __syncthreads();
-    if (j < DK) {
-      float sq = 0.f, sk = 0.f;
-      for (int w = 0; w < nw && w < 4; ++w) {
-        sq += red[w];
-        sk += red[4 + w];
-      }
-      const float iq = rbf2(rsqrtf(rbf2(rbf2(sq) + 1e-6f)));
-      const float ik = rbf2(rsqrtf(rbf2(rbf2(sk) + 1e-6f)));
-      qs[j] = rbf2(qv * iq) * scale;
-      ks[j] = rbf2(kv * ik);
-    }
-    __syncthreads();
-    if (j < dv) {
-      const float decay = expf(gb[0]), beta = gb[1];
-      const float v = __bfloat162float(row[2L * nk * DK + (long)h * dv + j]);
-      float kvm = 0.f;
-#pragma unroll
-      for (int i = 0; i < DK; ++i) {
-        S[i] *= decay;
-        kvm += S[i] * ks[i];
-      }
-      const float delta = (v - kvm) * beta;
-      float o = 0.f;
-#pragma unroll
-      for (int i = 0; i < DK; ++i) {
-        S[i] += ks[i] * delta;
-        o += S[i] * qs[i];
-      }
-      out[((long)t * nv + h) * dv + j] = __float2bfloat16(o);
-    }
-    __syncthreads();
-  }
-  if (j < dv) {
-#pragma unroll
-    for (int i = 0; i < DK; ++i) st[(long)i * dv + j] = S[i];
+  for (int h = threadIdx.x; h < nv; h += blockDim.x) {
+    const float b = __bfloat162float(ab[(long)t * ldab + h]);
+    const float a = __bfloat162float(ab[(long)t * ldab + nv + h]);
+    gb[((long)t * nv + h) * 2 + 0] = expf(-expf(a_log[h]) * softplus(a + dt_bias[h]));
+    gb[((long)t * nv + h) * 2 + 1] = rbf2(1.f / (1.f + expf(-b)));
   }
 }
 
-int gated_delta_varlen(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
-                       const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
-                       int S, int nk, int nv, int dk, int dv, void* out, cudaStream_t s) {
-  if (!S) return 0;
-  if (dv > 128 || dk > 128) return -1;
-  const int threads = ((dv > dk ? dv : dk) + 31) / 32 * 32;
-  dim3 grid(nv, S);
-#define QB_DELTA(DKV)                                                                                        \
-  delta_kernel<DKV><<<grid, threads, 0, s>>>((const bf16*)qkv, ldqkv, (const bf16*)ab, ldab, a_log, dt_bias, \
-                                             state, lane_stride, seg_lane, cu, nk, nv, dv, (bf16*)out)
-  if (dk == 128) QB_DELTA(128);
-  else if (dk == 64) QB_DELTA(64);
-  else if (dk == 32) QB_DELTA(32);
+constexpr int DR_CT = 16;  // tokens staged per chunk
+
+template <int DK>
+__global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const float* kn, const float* gb,
+                                                        const bf16* qkv, long ldqkv, float* state, long lane_stride,
+                                                        const int* seg_lane, const int* cu, int nk, int nv, int dv,
+                                                        bf16* out) {
+  constexpr int PART = DK / 4;        // rows per thread
+  constexpr int PST = PART + 4;       // padded part stride (floats)
+  __shared__ __align__(16) float qs[DR_CT][4 * PST];
+  __shared__ __align__(16) float ks[DR_CT][4 * PST];
+  __shared__ float vs[DR_CT][32];
+  __shared__ float gs[DR_CT][2];
+  const int h = blockIdx.x, s = blockIdx.y, cb = blockIdx.z;
+  const int tid = threadIdx.x;
+  const int col = tid >> 2, part = tid & 3;
+  const int j = cb * 32 + col;          // state column (value dim)
+  const int lane = seg_lane[s];
+  const int hk = h / (nv / nk);
+  float* st = state + (long)lane * lane_stride + (long)h * DK * dv;
+  const bool active = j < dv;
+  float S[PART];
+#pragma unroll
+  for (int i = 0; i < PART; ++i) S[i] = active ? st[(long)(part * PART + i) * dv + j] : 0.f;
+  const int t0 = cu[s], t1 = cu[s + 1];
+  for (int c0 = t0; c0 < t1; c0 += DR_CT) {
+    const int n = min(DR_CT, t1 - c0);
+    __syncthreads();
+    for (int idx = tid; idx < n * DK; idx += blockDim.x) {
+      const int tt = idx / DK, i = idx % DK;
+      const long base = ((long)(c0 + tt) * nk + hk) * DK + i;
+      qs[tt][(i / PART) * PST + i % PART] = qn[base];
+      ks[tt][(i / PART) * PST + i % PART] = kn[base];
+    }
+    for (int idx = tid; idx < n * 32; idx += blockDim.x) {
+      const int tt = idx / 32, cc = idx % 32;
+      const int jj = cb * 32 + cc;
+      vs[tt][cc] = jj < dv ? __bfloat162float(qkv[(long)(c0 + tt) * ldqkv + 2L * nk * DK + (long)h * dv + jj]) : 0.f;
+    }
+    for (int idx = tid; idx < n * 2; idx += blockDim.x) gs[idx / 2][idx % 2] = gb[((long)(c0 + idx / 2) * nv + h) * 2 + idx % 2];
+    __syncthreads();
+    for (int tt = 0; tt < n; ++tt) {
+      const float* kp = &ks[tt][part * PST];
+      const float* qp = &qs[tt][part * PST];
+      const float decay = gs[tt][0], beta = gs[tt][1];
+      float kv = 0.f;
+#pragma unroll
+      for (int i = 0; i < PART; i += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kp + i);
+        kv += S[i] * k4.x + S[i + 1] * k4.y + S[i + 2] * k4.z + S[i + 3] * k4.w;
+      }
+      kv += __shfl_xor_sync(0xffffffff, kv, 1);
+      kv += __shfl_xor_sync(0xffffffff, kv, 2);
+      const float delta = (vs[tt][col] - decay * kv) * beta;
+      float o = 0.f;
+#pragma unroll
+      for (int i = 0; i < PART; i += 4) {
+        const float4 k4 = *reinterpret_cast<const float4*>(kp + i);
+        const float4 q4 = *reinterpret_cast<const float4*>(qp + i);
+        S[i] = S[i] * decay + k4.x * delta;
+        S[i + 1] = S[i + 1] * decay + k4.y * delta;
+        S[i + 2] = S[i + 2] * decay + k4.z * delta;
+        S[i + 3] = S[i + 3] * decay + k4.w * delta;
+        o += S[i] * q4.x + S[i + 1] * q4.y + S[i + 2] * q4.z + S[i + 3] * q4.w;
+      }
+      o += __shfl_xor_sync(0xffffffff, o, 1);
+      o += __shfl_xor_sync(0xffffffff, o, 2);
+      if (part == 0 && active) out[((long)(c0 + tt) * nv + h) * dv + j] = __float2bfloat16(o);
+    }
+  }
+  if (active) {
+#pragma unroll
+    for (int i = 0; i < PART; ++i) st[(long)(part * PART + i) * dv + j] = S[i];
+  }
+}
+
+int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
+                         const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
+                         int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out, cudaStream_t s) {
+  if (!S || !T) return 0;
+  if (dk % 16 || dk > 128) return -1;
+  float* qn = scratch;
+  float* kn = qn + (long)T * nk * dk;
+  float* gb = kn + (long)T * nk * dk;
+  delta_prep_kernel<<<T, 256, 0, s>>>((const bf16*)qkv, ldqkv, (const bf16*)ab, ldab, a_log, dt_bias, nk, nv, dk,
+                                      qn, kn, gb);
+  dim3 grid(nv, S, (dv + 31) / 32);
+#define QB_DREC(DKV)                                                                                          \
+  delta_rec_kernel<DKV><<<grid, 128, 0, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, state, lane_stride, seg_lane, \
+                                             cu, nk, nv, dv, (bf16*)out)
+  if (dk == 128) QB_DREC(128);
+  else if (dk == 64) QB_DREC(64);
+  else if (dk == 32) QB_DREC(32);
   else return -1;
-#undef QB_DELTA
+#undef QB_DREC
   return (int)cudaGetLastError();
 }
 

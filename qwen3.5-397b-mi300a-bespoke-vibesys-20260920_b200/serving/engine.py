@@ -42,8 +42,12 @@ def pool_bytes(cfg: Qwen35Config, p, spec: PoolSpec) -> tuple[int, int, int]:
 
 def build_model(model: str, rank: int, world: int, device: torch.device, spec: PoolSpec,
                 dtype=torch.bfloat16, seed: int = 0, with_mtp: bool = False, comm: Comm | None = None,
-                reserve_bytes: float = 14e9) -> tuple[Model, int | None]:
-    """``model`` is a checkpoint directory, ``"full"`` or ``"tiny"`` (random init)."""
+                reserve_bytes: float = 14e9, graphs: bool | None = None):
+    """``model`` is a checkpoint directory, ``"full"`` or ``"tiny"`` (random init). On CUDA the
+    result is wrapped in a ``GraphRunner`` (captured decode buckets) unless ``graphs=False``;
+    every rank must call this in the same order, since capture runs the collectives."""
+    if graphs is None:
+        graphs = device.type == "cuda" and __import__("os").environ.get("QB_GRAPHS", "1") != "0"
     if model in ("full", "tiny"):
         cfg = full_config() if model == "full" else tiny_config()
     else:
@@ -62,6 +66,12 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
     else:
         w = load_weights(model, cfg, p, device, dtype, with_mtp=with_mtp)
     m = Model(cfg, w, p, comm or Comm(rank, world, None, device), device=device, dtype=dtype,
-              max_batch=spec.lanes, max_seq=spec.max_seq, block_size=spec.block_size, num_blocks=num_blocks,
-              num_snapshots=spec.snapshots or 2 * spec.lanes + 16)
+              max_batch=spec.lanes + (1 if graphs else 0), max_seq=spec.max_seq, block_size=spec.block_size,
+              num_blocks=num_blocks, num_snapshots=spec.snapshots or 2 * spec.lanes + 16)
+    if graphs:
+        from .graphs import GraphRunner
+
+        g = GraphRunner(m)
+        g.prepare()
+        return g, distinct
     return m, distinct
