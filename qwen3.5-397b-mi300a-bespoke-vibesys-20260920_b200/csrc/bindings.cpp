@@ -6,6 +6,9 @@
 #include <torch/extension.h>
 
 #include <atomic>
+#include <cstring>
+#include <string>
+#include <vector>
 #include <mutex>
 #include <unordered_map>
 
@@ -261,6 +264,47 @@ Tensor moe_routed_fp4(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13
   return moe_routed_impl(h, topw, topi, w13, s13, w2, s2, first, count);
 }
 
+// ------------------------------------------------------------------ symmetric memory (IPC)
+// One cudaMalloc'd region per rank, exported with cudaIpcGetMemHandle and mapped by every peer.
+py::tuple symm_alloc(int64_t bytes) {
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, bytes) == cudaSuccess, "symm_alloc: cudaMalloc failed");
+  TORCH_CHECK(cudaMemset(p, 0, bytes) == cudaSuccess, "symm_alloc: cudaMemset failed");
+  cudaIpcMemHandle_t h;
+  TORCH_CHECK(cudaIpcGetMemHandle(&h, p) == cudaSuccess, "symm_alloc: cudaIpcGetMemHandle failed");
+  return py::make_tuple((int64_t)reinterpret_cast<uintptr_t>(p), py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)));
+}
+
+int64_t symm_open(py::bytes handle) {
+  std::string s = handle;
+  TORCH_CHECK(s.size() == sizeof(cudaIpcMemHandle_t), "symm_open: bad handle size");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, s.data(), sizeof(h));
+  void* p = nullptr;
+  TORCH_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess) == cudaSuccess,
+              "symm_open: cudaIpcOpenMemHandle failed");
+  return (int64_t)reinterpret_cast<uintptr_t>(p);
+}
+
+void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+void symm_free(int64_t ptr) { cudaFree(reinterpret_cast<void*>(ptr)); }
+
+void symm_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor partial, Tensor res, Tensor w1p, Tensor out,
+                         double eps, int64_t slot_elems, int64_t max_blocks, Tensor epoch, double timeout_s) {
+  CHECK_BF16(partial);
+  CHECK_BF16(res);
+  TORCH_CHECK(res.is_contiguous() && out.is_contiguous() && partial.stride(-1) == 1, "symm_ar: layouts");
+  std::vector<void*> b(bases.size());
+  for (size_t i = 0; i < bases.size(); ++i) b[i] = reinterpret_cast<void*>(bases[i]);
+  const int H = res.size(-1);
+  const int rows = res.numel() / H;
+  int* ep = epoch.data_ptr<int>();
+  LAUNCH(qb::symm_ar_add_rmsnorm(b.data(), (int)b.size(), (int)rank, partial.data_ptr(), partial.stride(0),
+                                 res.data_ptr(), w1p.data_ptr<float>(), out.data_ptr(), rows, H, (float)eps,
+                                 slot_elems, (int)max_blocks, ep, ep + 1, err_ptr(res),
+                                 (unsigned long long)(timeout_s * 1e9), stream()));
+}
+
 // ------------------------------------------------------------------ status
 int64_t launches() { return g_launches.load(); }
 // graph replays launch the captured kernels without passing through these bindings
@@ -287,6 +331,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gated_delta_varlen", &gated_delta_varlen);
   m.def("moe_routed_fp4", &moe_routed_fp4);
   m.def("status", &status);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_free", &symm_free);
+  m.def("symm_ar_add_rmsnorm", &symm_ar_add_rmsnorm);
   m.def("launches", &launches, "number of kernels launched through the bindings so far");
   m.def("add_launches", &add_launches, "account kernels launched by a CUDA-graph replay");
   m.def("clear_status", &clear_status);

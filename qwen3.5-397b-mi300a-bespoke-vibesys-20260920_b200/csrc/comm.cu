@@ -1,0 +1,171 @@
+// Fused all-reduce + residual add + RMSNorm over NVLink peer memory (one-shot), and the
+// symmetric-buffer plumbing it needs (IPC export/import of one cudaMalloc'd region per rank).
+//
+// Every rank owns a symmetric region: two data slots of [max_rows, H] bf16 (double buffering
+// across consecutive calls) and two flag arrays of [max_blocks] int. A call with epoch e uses
+// slot s = e & 1. Block b of every rank
+//   1. copies its row chunk of the local partial sum into its own slot s,
+//   2. publishes flag[s][b] = e with a system-scope release,
+//   3. waits (bounded) until every peer's flag[s][b] == e (system-scope acquire, peer loads),
+//   4. sums the W partial rows in rank order (fp32, so every rank gets identical bits), rounds
+//      to bf16, adds the residual, writes the new residual and its RMSNorm.
+// A rank reaching call e+2 overwrites slot s only after it saw every peer's flag for e+1, and a
+// peer's kernel for e+1 starts only after its kernel for e finished: no peer still reads slot s.
+// The epoch lives in device memory (read by every block at entry, advanced by the last block to
+// finish), so the kernel can be captured in a CUDA graph and replayed.
+// Waits are bounded by `timeout_ns` (%globaltimer); on expiry the kernel records ERR_PEER_WAIT in
+// the status word, skips the reduction and returns. Reference counterpart: the one-shot IPC
+// all-reduce family of allreduce_custom.py (its watchdog traps; this one never does).
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qb {
+
+using bf16 = __nv_bfloat16;
+
+struct SymmPtrs {
+  void* data[8];   // per-rank region bases (peer-mapped; own entry is local)
+  int world;
+  int rank;
+};
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+constexpr int AR_THREADS = 256;
+
+__global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
+    SymmPtrs ptrs, const bf16* partial, long ldp, bf16* res, const float* w1p, bf16* out, int rows, int H,
+    float eps, long slot_elems, int max_blocks, int* epoch, int* done, int* err, unsigned long long timeout_ns) {
+  __shared__ float red[32];
+  __shared__ int s_epoch;
+  __shared__ int s_ok;
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile int*>(epoch) + 1;
+  __syncthreads();
+  const int e = s_epoch;
+  const int slot = e & 1;
+  const int W = ptrs.world, me = ptrs.rank;
+  auto flags_of = [&](int r) -> int* {
+    return reinterpret_cast<int*>(reinterpret_cast<bf16*>(ptrs.data[r]) + 2 * slot_elems) + slot * max_blocks;
+  };
+  bf16* mine = reinterpret_cast<bf16*>(ptrs.data[me]) + slot * slot_elems;
+  const int b = blockIdx.x;
+  // 1. stage this block's rows of the local partial
+  for (int r = b; r < rows; r += gridDim.x)
+    for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8)
+      *reinterpret_cast<uint4*>(mine + (long)r * H + i) = *reinterpret_cast<const uint4*>(partial + (long)r * ldp + i);
+  __syncthreads();
+  // 2. publish
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    st_release_sys(flags_of(me) + b, e);
+  }
+  // 3. wait for every peer's chunk (bounded)
+  if (threadIdx.x == 0) {
+    int ok = 1;
+    const uint64_t t0 = globaltimer();
+    for (int p = 0; p < W && ok; ++p) {
+      if (p == me) continue;
+      const int* f = flags_of(p) + b;
+      while (ld_acquire_sys(f) < e) {
+        if (globaltimer() - t0 > timeout_ns) {
+          atomicCAS(err, 0, ERR_PEER_WAIT);
+          ok = 0;
+          break;
+        }
+      }
+    }
+    s_ok = ok;
+  }
+  __syncthreads();
+  if (s_ok) {
+    // 4. reduce in rank order, add residual, RMSNorm
+    for (int r = b; r < rows; r += gridDim.x) {
+      float acc[16];
+      float ss = 0.f;
+      const int nper = (H + AR_THREADS * 8 - 1) / (AR_THREADS * 8);  // chunks of 8 per thread (<= 2)
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int i = (threadIdx.x + c * AR_THREADS) * 8;
+        if (c < nper && i < H) {
+          float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          for (int p = 0; p < W; ++p) {
+            const bf16* src = reinterpret_cast<const bf16*>(ptrs.data[p]) + slot * slot_elems + (long)r * H + i;
+            const uint4 raw = __ldcv(reinterpret_cast<const uint4*>(src));  // bypass L1: slots are reused
+            const bf16* ev = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) sum[u] += __bfloat162float(ev[u]);
+          }
+          const uint4 rr = *reinterpret_cast<const uint4*>(res + (long)r * H + i);
+          const bf16* rv = reinterpret_cast<const bf16*>(&rr);
+          uint4 nr;
+          bf16* nv = reinterpret_cast<bf16*>(&nr);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float sb = __bfloat162float(__float2bfloat16(sum[u]));
+            nv[u] = __float2bfloat16(__bfloat162float(rv[u]) + sb);
+            acc[c * 8 + u] = __bfloat162float(nv[u]);
+            ss += acc[c * 8 + u] * acc[c * 8 + u];
+          }
+          *reinterpret_cast<uint4*>(res + (long)r * H + i) = nr;
+        }
+      }
+      ss = warp_sum(ss);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        float t = threadIdx.x < AR_THREADS / 32 ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+      }
+      __syncthreads();
+      const float inv = rsqrtf(red[0] / H + eps);
+      __syncthreads();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int i = (threadIdx.x + c * AR_THREADS) * 8;
+        if (c < nper && i < H) {
+          uint4 o;
+          bf16* ov = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) ov[u] = __float2bfloat16(acc[c * 8 + u] * inv * w1p[i + u]);
+          *reinterpret_cast<uint4*>(out + (long)r * H + i) = o;
+        }
+      }
+    }
+  }
+  // the last block to finish advances the epoch (every block already read it at entry)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int d = atomicAdd(done, 1);
+    if (d == (int)gridDim.x - 1) {
+      *done = 0;
+      __threadfence();
+      atomicExch(epoch, e);
+    }
+  }
+}
+
+int symm_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
+                        const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
+                        int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s) {
+  if (world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || (long)rows * H > slot_elems) return -1;
+  SymmPtrs p{};
+  for (int r = 0; r < world; ++r) p.data[r] = bases[r];
+  p.world = world;
+  p.rank = rank;
+  int grid = rows < max_blocks ? rows : max_blocks;
+  if (grid < 1) grid = 1;
+  ar_add_rmsnorm_kernel<<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res, w1p, (bf16*)out, rows,
+                                                    H, eps, slot_elems, max_blocks, epoch, done, err, timeout_ns);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace qb

@@ -99,7 +99,9 @@ class Comm:
                               eps: float) -> tuple[torch.Tensor, torch.Tensor]:
         """``residual + sum_ranks(partial)`` and its RMSNorm; returns (residual, normed)."""
         if self.world > 1 and partial.is_cuda and self.symm is not None and self.mode == "fused":
-            return self.symm.allreduce_add_rmsnorm(partial, residual, w1p, eps)
+            got = self.symm.allreduce_add_rmsnorm(partial, residual, w1p, eps)
+            if got is not None:
+                return got
         summed = self.all_reduce(partial)
         return ops.add_rmsnorm(summed, residual, w1p, eps)
 

@@ -65,7 +65,14 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
         w = random_weights(cfg, p, device, dtype, seed=seed, with_mtp=with_mtp, distinct_expert_layers=distinct)
     else:
         w = load_weights(model, cfg, p, device, dtype, with_mtp=with_mtp)
-    m = Model(cfg, w, p, comm or Comm(rank, world, None, device), device=device, dtype=dtype,
+    if comm is None:
+        comm = Comm(rank, world, None, device)
+        if world > 1 and device.type == "cuda" and comm.mode == "fused":
+            from ..parallel.symm import SymmComm
+
+            rows = int(__import__("os").environ.get("QB_SYMM_MAX_ROWS", "512"))
+            comm.symm = SymmComm(rank, world, device, max_rows=rows, hidden=cfg.hidden)
+    m = Model(cfg, w, p, comm, device=device, dtype=dtype,
               max_batch=spec.lanes + (1 if graphs else 0), max_seq=spec.max_seq, block_size=spec.block_size,
               num_blocks=num_blocks, num_snapshots=spec.snapshots or 2 * spec.lanes + 16)
     if graphs:

@@ -1,0 +1,69 @@
+"""One rank of the two-GPU fused all-reduce check (see test_symm_gpu.py)."""
+
+import os
+import sys
+
+sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def main(rank, world, port):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE=str(world),
+                      LOCAL_RANK=str(rank))
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from qwen35_b200.ops import core as ops
+    from qwen35_b200.ops._ext import ext
+    from qwen35_b200.parallel.symm import SymmComm
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                            device_id=dev)
+    H = 4096
+    s = SymmComm(rank, world, dev, max_rows=512, hidden=H, timeout_s=10.0)
+    g = torch.Generator(device=dev).manual_seed(100 + rank)
+    w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).float()
+    dist.broadcast(w, 0)
+    for it, rows in enumerate([1, 7, 32, 32, 300, 512, 3, 3, 3]):
+        x = torch.randn(rows, H, device=dev, generator=g).bfloat16()
+        base = torch.randn(rows, H, device=dev, generator=torch.Generator(device=dev).manual_seed(it)).bfloat16()
+        r1 = base.clone()
+        r1, n1 = s.allreduce_add_rmsnorm(x, r1, w, 1e-6)
+        y = x.float()
+        dist.all_reduce(y)
+        r2, n2 = ops.add_rmsnorm(y.bfloat16(), base.clone(), w, 1e-6)
+        torch.cuda.synchronize()
+        assert torch.equal(r1, r2), (it, (r1.float() - r2.float()).abs().max().item())
+        assert (n1.float() - n2.float()).abs().max().item() < 1e-2 * n2.float().abs().max().item() + 1e-3
+    # graph capture + replay
+    x = torch.randn(16, H, device=dev, generator=g).bfloat16()
+    res = torch.zeros(16, H, device=dev).bfloat16()
+    st = torch.cuda.Stream()
+    with torch.cuda.stream(st):
+        s.allreduce_add_rmsnorm(x, res, w, 1e-6)
+    torch.cuda.synchronize()
+    gr = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gr):
+        out = s.allreduce_add_rmsnorm(x, res, w, 1e-6)
+    res.zero_()
+    for _ in range(5):
+        gr.replay()
+    torch.cuda.synchronize()
+    y = x.float()
+    dist.all_reduce(y)
+    exp = torch.zeros(16, H, device=dev)
+    for _ in range(5):
+        exp = (exp + y.bfloat16().float()).bfloat16().float()
+    assert (res.float() - exp).abs().max().item() < 1e-2 * exp.abs().max().item() + 1e-2
+    st_word = ext().status(torch.empty(1, device=dev)).tolist()
+    assert st_word[0] == 0, st_word
+    del gr
+    s.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main(int(sys.argv[1]), int(sys.argv[2]), int(sys.argv[3]))
