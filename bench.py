@@ -151,7 +151,7 @@ def main():
 
     from qwen35_b200.ops import _ext
     from qwen35_b200.parallel import comm as commmod
-    from qwen35_b200.parallel.driver import Broadcaster, Channel, Op, command_group, pool_handshake, serve_worker
+    from qwen35_b200.parallel.driver import Broadcaster, Op, command_group, open_channel, pool_handshake, serve_worker
     from qwen35_b200.serving.block_pool import BlockAllocator
     from qwen35_b200.serving.scheduler import Scheduler
     from qwen35_b200.serving.session_cache import SessionCache
@@ -172,6 +172,7 @@ def main():
         model.comm.group = None
     group = command_group(world)
     pool_handshake(model)
+    channel = open_channel(world, rank, group, device.type)
     boot_s = time.perf_counter() - t_boot
 
     def mark(tag: str):
@@ -190,7 +191,7 @@ def main():
     model.bench_mark = lambda tag: model.bench_marks.append(mark(tag))
 
     if rank != 0:
-        serve_worker(model, Channel(group))
+        serve_worker(model, channel)
         t = _elapsed_ms(model.bench_marks[0], model.bench_marks[1]) if len(model.bench_marks) >= 2 else 0.0
         gathered = [None] * world
         dist.all_gather_object(gathered, t)
@@ -199,7 +200,7 @@ def main():
         dist.destroy_process_group()
         return
 
-    runner = Broadcaster(model, Channel(group) if world > 1 else None)
+    runner = Broadcaster(model, channel)
     alloc = BlockAllocator(model.num_blocks, model.block_size)  # the runner's max_batch excludes the pad lane
     cache = SessionCache(alloc, model.block_size, model.num_snapshots)
     sched = Scheduler(runner, cache, prefill_chunk=args.prefill_chunk, token_budget=args.token_budget)
@@ -246,7 +247,7 @@ def main():
     clocks = ClockSampler(phys[:world] if phys else list(range(world)))
     clocks.start()
     if world > 1:
-        runner.channel.send(Op.CALL, ("bench_mark", ("start",), {}))
+        channel.send(Op.CALL, ("bench_mark", ("start",), {}))
     ev_start = mark("start")
     step0 = step_no[0]
     t_host0 = time.perf_counter()
@@ -255,7 +256,7 @@ def main():
     for _ in range(args.steps):
         one_step(events if device.type == "cuda" else None)
     if world > 1:
-        runner.channel.send(Op.CALL, ("bench_mark", ("end",), {}))
+        channel.send(Op.CALL, ("bench_mark", ("end",), {}))
     ev_end = mark("end")
     t_host1 = time.perf_counter()
     clk = clocks.stop()

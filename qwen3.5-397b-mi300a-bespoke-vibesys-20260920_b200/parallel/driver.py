@@ -68,6 +68,23 @@ class Channel:
         return Op(op), args
 
 
+def open_channel(world: int, rank: int, group, device_type: str = "cuda"):
+    """The command channel for this node: the shared-memory ring (``QB_CMD_CHANNEL=shm``, the
+    default) or the gloo broadcast channel (``gloo``). Every rank must call this."""
+    import os
+
+    if world <= 1:
+        return None
+    if os.environ.get("QB_CMD_CHANNEL", "shm") == "shm":
+        from .shm_channel import make_channel
+
+        ch = make_channel(world, rank, group)
+        if device_type != "cuda":
+            ch.poll_s = 5e-5  # CPU ranks share cores with the compute: do not spin hard
+        return ch
+    return Channel(group)
+
+
 def command_group(world: int):
     """A gloo group over all ranks for the command channel (every rank must call this)."""
     if world <= 1:

@@ -91,11 +91,11 @@ def _build(args, device):
 
 
 def run_worker(args) -> None:
-    from ..parallel.driver import Channel, serve_worker
+    from ..parallel.driver import open_channel, serve_worker
 
     device = _init_dist(args)
     model, group = _build(args, device)
-    serve_worker(model, Channel(group))
+    serve_worker(model, open_channel(args.tp, args.rank, group, device.type))
 
 
 # ============================================================================ engine
@@ -116,7 +116,7 @@ class Engine:
 
     def _boot(self):
         try:
-            from ..parallel.driver import Broadcaster, Channel
+            from ..parallel.driver import Broadcaster, open_channel
             from .block_pool import BlockAllocator
             from .scheduler import Scheduler
             from .session_cache import SessionCache
@@ -125,7 +125,7 @@ class Engine:
             device = _init_dist(self.args)
             model, group = _build(self.args, device)
             self.model = model
-            self.runner = Broadcaster(model, Channel(group) if self.args.tp > 1 else None)
+            self.runner = Broadcaster(model, open_channel(self.args.tp, 0, group, device.type))
             cache = SessionCache(BlockAllocator(model.num_blocks, model.block_size), model.block_size,
                                  model.num_snapshots)
             self.sched = Scheduler(self.runner, cache, prefill_chunk=self.args.prefill_chunk,

@@ -26,7 +26,7 @@ def main(rank: int, world: int, model_dir: str, out_path: str, port: int) -> Non
     from qwen35_b200.models.qwen35 import Model
     from qwen35_b200.models.weights import load_weights
     from qwen35_b200.parallel.comm import Comm
-    from qwen35_b200.parallel.driver import Broadcaster, Channel, command_group, pool_handshake, serve_worker
+    from qwen35_b200.parallel.driver import Broadcaster, command_group, open_channel, pool_handshake, serve_worker
     from qwen35_b200.parallel.plan import plan
     from qwen35_b200.serving.block_pool import BlockAllocator
     from qwen35_b200.serving.chat import TokenTemplate
@@ -41,11 +41,12 @@ def main(rank: int, world: int, model_dir: str, out_path: str, port: int) -> Non
               num_blocks=200, num_snapshots=8)
     group = command_group(world)
     pool_handshake(m)
+    channel = open_channel(world, rank, group, "cpu")
     if rank != 0:
-        serve_worker(m, Channel(group))
+        serve_worker(m, channel)
         dist.destroy_process_group()
         return
-    runner = Broadcaster(m, Channel(group))
+    runner = Broadcaster(m, channel)
     cache = SessionCache(BlockAllocator(m.num_blocks, m.block_size), m.block_size, m.num_snapshots)
     sched = Scheduler(runner, cache, prefill_chunk=128, token_budget=256)
     tpl = TokenTemplate.for_vocab(cfg.vocab)
