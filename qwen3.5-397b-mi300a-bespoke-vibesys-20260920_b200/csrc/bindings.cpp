@@ -192,20 +192,20 @@ Tensor attention_varlen(Tensor q, Tensor kc, Tensor vc, Tensor table, Tensor seg
 }
 
 // ------------------------------------------------------------------ deltanet
-Tensor causal_conv_varlen(Tensor x, Tensor state, Tensor w, Tensor seg_lane, Tensor cu) {
+Tensor causal_conv_varlen(Tensor x, Tensor state, Tensor w, Tensor seg_lane, Tensor cu, bool commit) {
   CHECK_BF16(x);
   TORCH_CHECK(state.stride(2) == 1 && state.stride(1) == state.size(2), "conv: state [lanes, C, K-1] rows contiguous");
   const int T = x.size(0), C = x.size(1), K = w.size(1);
   Tensor out = at::empty({T, C}, x.options());
   LAUNCH(qb::causal_conv_varlen_t(x.data_ptr(), x.stride(0), state.data_ptr(), state.stride(0), w.data_ptr(),
                                   seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), T, C, K,
-                                  out.data_ptr(), stream()));
+                                  out.data_ptr(), commit, stream()));
   g_launches.fetch_add(1, std::memory_order_relaxed);  // output + state kernels
   return out;
 }
 
 Tensor gated_delta_varlen(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, Tensor state, Tensor seg_lane,
-                          Tensor cu, int64_t nk, int64_t nv, int64_t dk, int64_t dv) {
+                          Tensor cu, int64_t nk, int64_t nv, int64_t dk, int64_t dv, bool commit) {
   CHECK_BF16(qkv);
   TORCH_CHECK(state.scalar_type() == at::kFloat, "delta: fp32 state");
   TORCH_CHECK(state.stride(3) == 1 && state.stride(2) == dv && state.stride(1) == dk * dv, "delta: state layout");
@@ -215,7 +215,7 @@ Tensor gated_delta_varlen(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, T
   LAUNCH(qb::gated_delta_varlen_t(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0),
                                   a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), state.data_ptr<float>(),
                                   state.stride(0), seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), T,
-                                  nk, nv, dk, dv, scratch.data_ptr<float>(), out.data_ptr(), stream()));
+                                  nk, nv, dk, dv, scratch.data_ptr<float>(), out.data_ptr(), commit, stream()));
   g_launches.fetch_add(1, std::memory_order_relaxed);  // prep + recurrence kernels
   return out;
 }
@@ -254,9 +254,22 @@ Tensor moe_routed_impl(Tensor h, Tensor topw, Tensor topi, Tensor w13, c10::opti
                                offsets, counts, count, cap, 0, y2.data_ptr(), H, err_ptr(h), stream(), 0));
     LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream()));
   } else {
-    TORCH_CHECK(false, "moe: bf16 experts not supported on this path yet");
+    // bf16 experts (the MTP layer of the published checkpoint): TMA-fed bf16 weight tiles
+    Tensor xh = at::empty({cap, H}, h.options());
+    Tensor inter = at::empty({cap, I}, h.options());
+    Tensor y2 = at::empty({cap, H}, h.options());
+    LAUNCH(qb::moe_gather_bf16(h.data_ptr(), perm_tok, n_assign, cap, H, xh.data_ptr(), stream()));
+    LAUNCH(qb::moe_expert_gemm_bf16(xh.data_ptr(), H, w13.data_ptr(), n13, H, 0, offsets, counts, count, cap, 1,
+                                    inter.data_ptr(), I, stream()));
+    LAUNCH(qb::moe_expert_gemm_bf16(inter.data_ptr(), I, w2.data_ptr(), H, I, 0, offsets, counts, count, cap, 0,
+                                    y2.data_ptr(), H, stream()));
+    LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream()));
   }
   return out;
+}
+
+Tensor moe_routed_bf16(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor w2, int64_t first, int64_t count) {
+  return moe_routed_impl(h, topw, topi, w13, c10::nullopt, w2, c10::nullopt, first, count);
 }
 
 Tensor moe_routed_fp4(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13, Tensor w2, Tensor s2, int64_t first,
@@ -330,6 +343,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("causal_conv_varlen", &causal_conv_varlen);
   m.def("gated_delta_varlen", &gated_delta_varlen);
   m.def("moe_routed_fp4", &moe_routed_fp4);
+  m.def("moe_routed_bf16", &moe_routed_bf16);
   m.def("status", &status);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);

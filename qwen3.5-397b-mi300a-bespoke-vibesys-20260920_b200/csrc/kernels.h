@@ -34,10 +34,11 @@ int qk_norm_rope_kv_write(const void* qkv, long ldqkv, int nq, int nkv, int hd, 
                           const int* pos, const int* rows, void* kc, void* vc, void* qout, int T, int rot,
                           float theta, float eps, cudaStream_t s);
 int causal_conv_varlen_t(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
-                         const int* cu, int S, int T, int C, int K, void* out, cudaStream_t s);
+                         const int* cu, int S, int T, int C, int K, void* out, bool commit, cudaStream_t s);
 int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
                          const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
-                         int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out, cudaStream_t s);
+                         int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out, bool commit,
+                         cudaStream_t s);
 int attention_varlen(const void* q, const void* kc, const void* vc, const int* table, int max_blocks,
                      const int* pos, const int* seg_lane, const int* cu, int S, int T, int nq, int nkv, int hd,
                      int block_size, int splits, float* ws, void* out, cudaStream_t s);
@@ -51,6 +52,8 @@ int moe_gather_f16(const void* h, const int* perm_tok, const int* n_assign, int 
 int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8_t* ws, int n_rows, int k_cols,
                     long w_expert_stride, long s_expert_stride, const int* offsets, const int* counts,
                     int count, int cap, int act, void* out, int out_cols, int* err, cudaStream_t s, int max_ctas);
+int moe_gather_bf16(const void* h, const int* perm_tok, const int* n_assign, int cap, int H, void* xh,
+                    cudaStream_t s);
 int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s);
 int moe_expert_gemm_bf16(const void* xin, int in_cols, const void* w, int n_rows, int k_cols, long w_expert_stride,
                          const int* offsets, const int* counts, int count, int cap, int act, void* out, int out_cols,

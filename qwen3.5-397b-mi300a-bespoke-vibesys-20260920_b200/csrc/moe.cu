@@ -101,6 +101,13 @@ int moe_gather_f16(const void* h, const int* perm_tok, const int* n_assign, int 
   return (int)cudaGetLastError();
 }
 
+int moe_gather_bf16(const void* h, const int* perm_tok, const int* n_assign, int cap, int H, void* xh,
+                    cudaStream_t s) {
+  if (!cap) return 0;
+  moe_gather_kernel<true><<<cap, 128, 0, s>>>((const bf16*)h, perm_tok, n_assign, H, xh);
+  return (int)cudaGetLastError();
+}
+
 // out[t, :] = sum_j topw[t, j] * y2[inv[t, j], :] over local assignments (fp32, rounded once)
 __global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* topw, int k, int H, bf16* out) {
   const long t = blockIdx.x;

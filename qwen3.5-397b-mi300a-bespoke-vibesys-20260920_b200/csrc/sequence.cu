@@ -61,13 +61,14 @@ __global__ void conv_state_kernel(const bf16* x, long ldx, bf16* state, long lan
 }
 
 int causal_conv_varlen_t(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
-                         const int* cu, int S, int T, int C, int K, void* out, cudaStream_t s) {
+                         const int* cu, int S, int T, int C, int K, void* out, bool commit, cudaStream_t s) {
   if (!S || !T) return 0;
   if (K != 4) return -1;
   conv_out_kernel<4><<<dim3((C + 127) / 128, T), 128, 0, s>>>((const bf16*)x, ldx, (const bf16*)state, lane_stride,
                                                                (const bf16*)w, seg_lane, cu, S, C, (bf16*)out);
-  conv_state_kernel<4><<<dim3((C + 127) / 128, S), 128, 0, s>>>((const bf16*)x, ldx, (bf16*)state, lane_stride,
-                                                                 seg_lane, cu, C);
+  if (commit)
+    conv_state_kernel<4><<<dim3((C + 127) / 128, S), 128, 0, s>>>((const bf16*)x, ldx, (bf16*)state, lane_stride,
+                                                                   seg_lane, cu, C);
   return (int)cudaGetLastError();
 }
 
@@ -114,7 +115,7 @@ template <int DK>
 __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const float* kn, const float* gb,
                                                         const bf16* qkv, long ldqkv, float* state, long lane_stride,
                                                         const int* seg_lane, const int* cu, int nk, int nv, int dv,
-                                                        bf16* out) {
+                                                        bf16* out, int commit) {
   constexpr int PART = DK / 4;        // rows per thread
   constexpr int PST = PART + 4;       // padded part stride (floats)
   __shared__ __align__(16) float qs[DR_CT][4 * PST];
@@ -178,7 +179,7 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
       if (part == 0 && active) out[((long)(c0 + tt) * nv + h) * dv + j] = __float2bfloat16(o);
     }
   }
-  if (active) {
+  if (active && commit) {
 #pragma unroll
     for (int i = 0; i < PART; ++i) st[(long)(part * PART + i) * dv + j] = S[i];
   }
@@ -186,7 +187,8 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
 
 int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
                          const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
-                         int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out, cudaStream_t s) {
+                         int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out, bool commit,
+                         cudaStream_t s) {
   if (!S || !T) return 0;
   if (dk % 16 || dk > 128) return -1;
   float* qn = scratch;
@@ -197,7 +199,7 @@ int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab,
   dim3 grid(nv, S, (dv + 31) / 32);
 #define QB_DREC(DKV)                                                                                          \
   delta_rec_kernel<DKV><<<grid, 128, 0, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, state, lane_stride, seg_lane, \
-                                             cu, nk, nv, dv, (bf16*)out)
+                                             cu, nk, nv, dv, (bf16*)out, commit ? 1 : 0)
   if (dk == 128) QB_DREC(128);
   else if (dk == 64) QB_DREC(64);
   else if (dk == 32) QB_DREC(32);

@@ -58,6 +58,7 @@ class StepInputs:
     cu_h: list[int]
     seg_start_h: list[int]
     max_ctx: int = 0
+    verify: bool = False  # MTP verify: DeltaNet layers keep their inputs and do not write state
 
 
 class Model:
@@ -111,6 +112,7 @@ class Model:
         self._dirty: set[int] = set(range(max_batch))
         self.last_hidden: torch.Tensor | None = None  # pre-final-norm hidden of the logit rows (MTP seed)
         self.fault: dict[str, object] = {}  # accuracy-gate calibration faults (serving.faults)
+        self._vsave: dict = {}  # MTP verify: per DeltaNet layer (conv inputs, ab rows)
         self._h2d = 0  # bytes copied host -> device for step inputs (bench accounting)
         self._d2h = 0  # bytes read back device -> host (sampled ids)
 
@@ -241,12 +243,15 @@ class Model:
         nk, nv, dk, dv = self.nk, self.nv, cfg.dn_k_dim, cfg.dn_v_dim
         c = self.conv_ch
         proj = ops.linear(h, L["w_in"])  # [T, c + nv*dv + 2nv]
+        commit = not b.verify
+        if b.verify:  # keep the per-row inputs: the accepted prefix is committed later
+            self._vsave[j] = (proj[:, :c].clone(), proj[:, c + nv * dv:].clone())
         qkv = ops.causal_conv_varlen(proj[:, :c], self.conv_state[j], L["conv_w"], b.seg_lane, b.cu,
-                                     b.seg_lane_h, b.cu_h)
+                                     b.seg_lane_h, b.cu_h, commit=commit)
         z = proj[:, c:c + nv * dv]
         ab = proj[:, c + nv * dv:]
         core = ops.gated_delta_varlen(qkv, ab, L["A_log"], L["dt_bias"], self.rec_state[j], b.seg_lane, b.cu,
-                                      nk, nv, dk, dv, b.seg_lane_h, b.cu_h)
+                                      nk, nv, dk, dv, b.seg_lane_h, b.cu_h, commit=commit)
         if self.fault.get("skip_deltanet_gate"):
             normed = ops.rmsnorm(core, torch.ones(dv, device=h.device), cfg.eps).reshape(-1, nv * dv)
         else:
@@ -254,8 +259,11 @@ class Model:
         return ops.linear(normed, L["w_out"])
 
     def _attention(self, i: int, L: dict, h: torch.Tensor, b: StepInputs) -> torch.Tensor:
-        cfg = self.cfg
         j = self.full_slot[i]
+        return self._attention_core(L, h, b, self.k_cache[j], self.v_cache[j])
+
+    def _attention_core(self, L: dict, h: torch.Tensor, b: StepInputs, k_cache, v_cache) -> torch.Tensor:
+        cfg = self.cfg
         hd, nq, nkv = cfg.head_dim, self.nq, self.nkv
         qkv = ops.linear(h, L["w_qkv"])
         t = qkv.shape[0]
@@ -265,8 +273,8 @@ class Model:
         v = qkv[:, nq * 2 * hd + nkv * hd:].reshape(t, nkv, hd)
         theta = float(self.fault.get("rope_base", cfg.rope_theta))
         q = ops.qk_norm_rope_kv_write(q, k, v, L["q_norm"], L["k_norm"], b.positions, b.rows,
-                                      self.k_cache[j], self.v_cache[j], cfg.rotary_dim, theta, cfg.eps)
-        o = ops.attention_varlen(q, self.k_cache[j], self.v_cache[j], self.table_dev, b.seg_lane, b.cu,
+                                      k_cache, v_cache, cfg.rotary_dim, theta, cfg.eps)
+        o = ops.attention_varlen(q, k_cache, v_cache, self.table_dev, b.seg_lane, b.cu,
                                  b.seg_start, self.block_size, b.seg_lane_h, b.cu_h, b.seg_start_h,
                                  self.tables if h.device.type == "cpu" else None, b.positions, b.max_ctx)
         o = ops.sigmoid_gate_mul(o.reshape(t, nq * hd), gate.reshape(t, nq * hd))
@@ -300,7 +308,7 @@ class Model:
         x = ops.embed(b.tokens, self.w["embed"])
         x, h = self._layers(x, b)
         self.last_hidden = x.index_select(0, b.logit_rows)
-        self.last_hidden_all = x
+        self.last_h_all = h
         return h.index_select(0, b.logit_rows)
 
     def logits(self, h: torch.Tensor) -> torch.Tensor:
@@ -312,7 +320,74 @@ class Model:
     @torch.inference_mode()
     def forward(self, segs, logit_rows=None) -> torch.Tensor:
         b = self.make_inputs(segs, logit_rows)
-        return self.logits(self._forward(b))
+        lg = self.logits(self._forward(b))
+        if self.mtp is not None:
+            self.mtp.catch_up(b, self.last_h_all)
+        return lg
+
+    # ================================================================== MTP speculative decode
+    @torch.inference_mode()
+    def speculative_decode(self, lanes, tokens, positions, budgets, stops) -> list[list[int]]:
+        """One MTP round per lane (see ``models.mtp``): draft k, verify k+1 rows in one forward,
+        accept, commit DeltaNet state over the accepted rows, re-run the MTP layer on them."""
+        mtp = self.mtp
+        k = mtp.k
+        B = len(lanes)
+        drafts = mtp.draft(lanes, tokens, positions)  # [B, k]
+        segs = [(l, [0] * (k + 1), p) for l, p in zip(lanes, positions)]
+        b = self.make_inputs(segs, logit_rows=list(range(B * (k + 1))))
+        tok0 = torch.tensor([int(t) for t in tokens], dtype=torch.int64, device=self.device)
+        b.tokens = torch.cat([tok0[:, None], drafts], dim=1).reshape(-1)
+        b.verify = True
+        self._vsave = {}
+        h = self._forward(b)
+        logits = self.logits(h)
+        am = ops.argmax_rows(logits)[1].view(B, k + 1)
+        am_h, dr_h = am.tolist(), drafts.tolist()  # the round's one host sync
+        self._d2h += 8 * B * (2 * k + 1)
+        ns = [mtp.accept(dr_h[i], am_h[i]) for i in range(B)]
+        mtp.rounds += B
+        mtp.accepted += sum(ns)
+        self._commit_verify(b, lanes, positions, ns, k)
+        out = []
+        for i in range(B):
+            toks = dr_h[i][:ns[i]] + [am_h[i][ns[i]]]
+            st = set(stops[i])
+            cut = next((j for j, t in enumerate(toks) if t in st), None)
+            if cut is not None:
+                toks = toks[:cut + 1]
+            out.append(toks[:max(1, budgets[i])])
+        return out
+
+    def _commit_verify(self, b: StepInputs, lanes, positions, ns, k) -> None:
+        """Advance DeltaNet state over each lane's accepted rows (the committed token plus the
+        accepted drafts) from the verify forward's saved inputs, then run the MTP catch-up."""
+        dev = self.device
+        idx, cu, seg_l = [], [0], []
+        for i, (l, n) in enumerate(zip(lanes, ns)):
+            idx.extend(range(i * (k + 1), i * (k + 1) + n + 1))
+            cu.append(cu[-1] + n + 1)
+            seg_l.append(l)
+        it = torch.tensor(idx, dtype=torch.long, device=dev)
+        seg_lane_d = torch.tensor(seg_l, dtype=torch.int32, device=dev)
+        cu_d = torch.tensor(cu, dtype=torch.int32, device=dev)
+        cfg = self.cfg
+        for i, L in enumerate(self.w["layers"]):
+            if L["kind"] == FULL:
+                continue
+            j = self.lin_slot[i]
+            conv_in, ab = self._vsave[j]
+            qkv = ops.causal_conv_varlen(conv_in.index_select(0, it), self.conv_state[j], L["conv_w"], seg_lane_d,
+                                         cu_d, seg_l, cu, commit=True)
+            ops.gated_delta_varlen(qkv, ab.index_select(0, it), L["A_log"], L["dt_bias"], self.rec_state[j],
+                                   seg_lane_d, cu_d, self.nk, self.nv, cfg.dn_k_dim, cfg.dn_v_dim, seg_l, cu,
+                                   commit=True)
+        self._vsave = {}
+        if self.mtp is not None:
+            acc_segs = [(l, [0] * (n + 1), p) for l, n, p in zip(lanes, ns, positions)]
+            ab_in = self.make_inputs(acc_segs)
+            ab_in.tokens = b.tokens.index_select(0, it)
+            self.mtp.catch_up(ab_in, self.last_h_all.index_select(0, it))
 
     def prefill(self, lane: int, ids: Sequence[int], start: int):
         return self.forward([(lane, ids, start)])[0:1]

@@ -79,11 +79,11 @@ def argmax_rows(logits):
 
 
 # ----------------------------------------------------------------------------- deltanet
-def causal_conv_varlen(x, conv_state, w, seg_lane, cu, seg_lane_h=None, cu_h=None):
-    """Depthwise causal conv + SiLU over each segment, continuing from and updating
-    ``conv_state[lane]`` ([lanes, C, K-1]). ``x`` [T, C] (may be a column slice)."""
+def causal_conv_varlen(x, conv_state, w, seg_lane, cu, seg_lane_h=None, cu_h=None, commit=True):
+    """Depthwise causal conv + SiLU over each segment, continuing from ``conv_state[lane]``
+    ([lanes, C, K-1]) and, when ``commit``, updating it. ``x`` [T, C] (may be a column slice)."""
     if _cuda(x):
-        return ext().causal_conv_varlen(x, conv_state, w, seg_lane, cu)
+        return ext().causal_conv_varlen(x, conv_state, w, seg_lane, cu, commit)
     out = torch.empty(x.shape, dtype=x.dtype, device=x.device)
     lanes = seg_lane_h if seg_lane_h is not None else seg_lane.tolist()
     cus = cu_h if cu_h is not None else cu.tolist()
@@ -91,12 +91,13 @@ def causal_conv_varlen(x, conv_state, w, seg_lane, cu, seg_lane_h=None, cu_h=Non
         a, b = cus[s], cus[s + 1]
         o, st = ref.causal_conv(x[a:b], conv_state[lane], w)
         out[a:b] = o
-        conv_state[lane].copy_(st)
+        if commit:
+            conv_state[lane].copy_(st)
     return out
 
 
 def gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv,
-                       seg_lane_h=None, cu_h=None):
+                       seg_lane_h=None, cu_h=None, commit=True):
     """Gated delta rule over each segment with the DeltaNet glue fused in.
 
     ``qkv`` [T, 2*nk*dk + nv*dv] (conv output: q | k | v), ``ab`` [T, 2*nv] (``b`` then ``a``
@@ -121,7 +122,8 @@ def gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv,
         a, b = cus[s], cus[s + 1]
         o, st = ref.gated_delta_rule(q[a:b], k[a:b], v[a:b], g[a:b], beta[a:b], rec_state[lane])
         out[a:b] = o
-        rec_state[lane].copy_(st)
+        if commit:
+            rec_state[lane].copy_(st)
     return out.to(qkv.dtype)
 
 
@@ -191,7 +193,7 @@ def moe_routed(h, topw, topi, experts, first, count):
         if "s13" in experts:
             return ext().moe_routed_fp4(h, topw, topi, experts["w13"], experts["s13"], experts["w2"], experts["s2"],
                                         first, count)
-        raise NotImplementedError("bf16 routed experts on CUDA")
+        return ext().moe_routed_bf16(h, topw, topi, experts["w13"], experts["w2"], first, count)
     return ref.routed_experts(h, topw, topi.long(), experts, first, count)
 
 

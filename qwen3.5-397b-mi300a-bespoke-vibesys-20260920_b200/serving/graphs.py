@@ -131,7 +131,7 @@ class GraphRunner:
     def decode(self, lanes, tokens, positions):
         n = len(lanes)
         B = next((b for b in self.buckets if b >= n), None)
-        if not self._b or B is None or B not in self._b:
+        if not self._b or B is None or B not in self._b or self.model.mtp is not None:
             return self.model.decode(lanes, tokens, positions)
         bk = self._b[B]
         with torch.inference_mode():

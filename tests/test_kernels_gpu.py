@@ -244,3 +244,47 @@ def test_tiny_model_gpu_matches_cpu_reference(tiny_dir):
     cos = torch.nn.functional.cosine_similarity(a, b).item()
     assert cos > 0.99, cos
     status_ok()
+
+
+@pytest.mark.parametrize("T,E,k,H,I", [(3, 32, 4, 256, 128), (40, 64, 8, 512, 256), (9, 128, 10, 4096, 1024)])
+def test_moe_routed_bf16_experts(T, E, k, H, I):
+    h = rnd(T, H, seed=T + 7)
+    experts = {"w13": rnd(E, 2 * I, H, scale=0.02, seed=E), "w2": rnd(E, H, I, scale=0.02, seed=E + 1)}
+    topw, topi = ops.router_topk(rnd(T, E, seed=T + 8), k)
+    out = ops.moe_routed(h, topw, topi, experts, 0, E)
+    torch.cuda.synchronize()
+    exp = ref.routed_experts(h, topw, topi.long(), experts, 0, E)
+    close(out, exp, rtol=3e-2, atol=3e-3)
+    status_ok()
+
+
+def test_mtp_round_on_gpu_equals_plain_decode():
+    from qwen35_b200.models import mtp as mtpmod
+    from qwen35_b200.models.config import tiny_config
+    from qwen35_b200.models.qwen35 import Model
+    from qwen35_b200.models.weights import random_weights
+    from qwen35_b200.parallel.plan import plan
+
+    cfg = tiny_config()
+    p = plan(cfg, 0, 1)
+    w = random_weights(cfg, p, torch.device(DEV), BF, seed=3, with_mtp=True)
+    outs = []
+    for spec in (False, True):
+        m = Model(cfg, w, p, device=DEV, dtype=BF, max_batch=2, max_seq=512)
+        if spec:
+            mtpmod.attach(m, k=3)
+        m.begin(0)
+        m.attach_blocks(0, list(range(1, 20)))
+        ids = list(range(11, 91))
+        lg = m.prefill(0, ids, 0)
+        tok, pos, got = int(lg.float().argmax()), len(ids), []
+        while len(got) < 12:
+            if spec:
+                new = m.speculative_decode([0], [tok], [pos], [12 - len(got)], [[]])[0]
+            else:
+                new = [int(m.decode([0], [tok], [pos]).float().argmax())]
+            got += [tok] + new[:-1]
+            pos += len(new)
+            tok = new[-1]
+        outs.append(got[:12])
+    assert outs[0] == outs[1]
