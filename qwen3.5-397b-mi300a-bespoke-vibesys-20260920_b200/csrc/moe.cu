@@ -22,6 +22,7 @@
 #include "kernels.h"
 
 #include <cstdlib>
+#include <type_traits>
 
 namespace qb {
 
@@ -358,7 +359,9 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
           asm volatile("bar.sync 1, 128;" ::: "memory");
           const int nvalid = min(CH, cnt - m0 - c0);
           if (gu) {
-            __half* Y = reinterpret_cast<__half*>(a.out);
+            // the intermediate feeds the down GEMM: f16 for the fp4 path, bf16 for bf16 experts
+            using IT = typename std::conditional<FP4, __half, bf16>::type;
+            IT* Y = reinterpret_cast<IT*>(a.out);
             for (int idx = et; idx < CH * 64; idx += 128) {
               const int j = idx / 64, r = idx % 64;
               if (j < nvalid) {
@@ -367,7 +370,7 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
                 const float uu = __bfloat162float(*reinterpret_cast<bf16*>(&ub));
                 const float sg = __bfloat162float(__float2bfloat16(g / (1.f + expf(-g))));
                 const float y = __bfloat162float(__float2bfloat16(sg * uu));
-                Y[(long)(off + m0 + c0 + j) * a.out_cols + nt * 64 + r] = __float2half_rn(y);
+                Y[(long)(off + m0 + c0 + j) * a.out_cols + nt * 64 + r] = from_f<IT>(y);
               }
             }
           } else {
