@@ -12,6 +12,8 @@ lane. ``rows[t]`` is the physical paged-KV row of token ``t``.
 
 from __future__ import annotations
 
+import os
+
 import torch
 import torch.nn.functional as F
 
@@ -105,7 +107,7 @@ def gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv,
     q/k l2-normalised, ``q *= dk**-0.5``, key heads repeated to value heads. ``rec_state``
     [lanes, nv, dk, dv] fp32 is continued and updated. Returns [T, nv, dv] in ``qkv.dtype``."""
     if _cuda(qkv):
-        return ext().gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv)
+        return ext().gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv, commit)
     t = qkv.shape[0]
     q = qkv[:, : nk * dk].reshape(t, nk, dk)
     k = qkv[:, nk * dk: 2 * nk * dk].reshape(t, nk, dk)
@@ -150,6 +152,10 @@ def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, 
     ``[0, seg_start + len)``. ``q`` [T, Hq, D]; caches [rows, Hkv, D]. Returns [T, Hq, D].
     On CUDA ``positions`` ([T] absolute positions) and ``max_ctx`` (longest context) are used."""
     if _cuda(q):
+        if prefill_shaped(q, k_cache, cu_h, block_size):
+            tiles = fa_tiles(cu_h, q.shape[1] // k_cache.shape[1])
+            t = torch.tensor(tiles, dtype=torch.int32).pin_memory().to(q.device, non_blocking=True)
+            return ext().attention_prefill(q, k_cache, v_cache, block_table, seg_lane, positions, t, block_size)
         return ext().attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, positions, block_size,
                                       int(max_ctx))
     out = torch.empty_like(q)
@@ -167,6 +173,29 @@ def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, 
         rows = torch.tensor([blk * block_size + o for blk in blocks[:nb] for o in range(block_size)][:n],
                             dtype=torch.long, device=q.device)
         out[a:b] = ref.attention_prefix(q[a:b], k_cache[rows], v_cache[rows], starts[s])
+    return out
+
+
+def prefill_shaped(q, k_cache, cu_h, block_size) -> bool:
+    """Prefill-shaped batches (>= 4 rows per segment on average) use the tcgen05 flash-attention
+    kernel; decode-shaped ones the split-K kernel."""
+    if cu_h is None or block_size != 16 or os.environ.get("QB_FA_PREFILL", "1") == "0":
+        return False
+    g = q.shape[1] // k_cache.shape[1]
+    if 128 % g or q.shape[2] not in (64, 128, 256):
+        return False
+    segs = len(cu_h) - 1
+    return segs > 0 and q.shape[0] >= 4 * segs
+
+
+def fa_tiles(cu_h, g: int) -> list[list[int]]:
+    """[segment, first row, rows] per 128/g-token query tile of every segment."""
+    qt = 128 // g
+    out = []
+    for s in range(len(cu_h) - 1):
+        a, b = cu_h[s], cu_h[s + 1]
+        for r in range(a, b, qt):
+            out.append([s, r, min(qt, b - r)])
     return out
 
 

@@ -259,6 +259,11 @@ def test_moe_routed_bf16_experts(T, E, k, H, I):
 
 
 def test_mtp_round_on_gpu_equals_plain_decode():
+    """Speculative rounds (draft, wide verify, DeltaNet commit of the accepted rows) emit the
+    plain model's greedy tokens. The verify forward runs other kernels than one-row decode
+    (flash attention, wider GEMM and MoE tiles), so bf16 summation order differs; on random
+    weights a near-tie can flip. Each emitted token is therefore checked teacher-forced: it is
+    the plain model's top-1 on its own prefix, up to a bf16 margin."""
     from qwen35_b200.models import mtp as mtpmod
     from qwen35_b200.models.config import tiny_config
     from qwen35_b200.models.qwen35 import Model
@@ -268,23 +273,75 @@ def test_mtp_round_on_gpu_equals_plain_decode():
     cfg = tiny_config()
     p = plan(cfg, 0, 1)
     w = random_weights(cfg, p, torch.device(DEV), BF, seed=3, with_mtp=True)
-    outs = []
-    for spec in (False, True):
+    ids = list(range(11, 91))
+
+    def fresh(spec):
         m = Model(cfg, w, p, device=DEV, dtype=BF, max_batch=2, max_seq=512)
         if spec:
             mtpmod.attach(m, k=3)
         m.begin(0)
         m.attach_blocks(0, list(range(1, 20)))
-        ids = list(range(11, 91))
-        lg = m.prefill(0, ids, 0)
-        tok, pos, got = int(lg.float().argmax()), len(ids), []
-        while len(got) < 12:
-            if spec:
-                new = m.speculative_decode([0], [tok], [pos], [12 - len(got)], [[]])[0]
-            else:
-                new = [int(m.decode([0], [tok], [pos]).float().argmax())]
-            got += [tok] + new[:-1]
-            pos += len(new)
-            tok = new[-1]
-        outs.append(got[:12])
-    assert outs[0] == outs[1]
+        return m, m.prefill(0, ids, 0)
+
+    plain, lg = fresh(False)
+    ref, t = [], int(lg.float().argmax())
+    for j in range(40):  # the plain model's greedy continuation, used as oracle drafts
+        ref.append(t)
+        t = int(plain.decode([0], [t], [len(ids) + j]).float().argmax())
+
+    m, lg = fresh(True)
+    head = m.mtp
+    calls = [0]
+
+    def oracle_draft(lanes, tokens, positions):
+        j = positions[0] - len(ids)
+        d = [ref[min(j + 1 + i, len(ref) - 1)] for i in range(head.k)]
+        calls[0] += 1
+        if calls[0] % 2 == 0:  # every other round: last draft wrong -> partial acceptance
+            d[-1] = (d[-1] + 1) % cfg.vocab
+        head.drafted += head.k
+        return torch.tensor([d], device=DEV)
+
+    head.draft = oracle_draft
+    tok, pos, got = int(lg.float().argmax()), len(ids), []
+    while len(got) < 16:
+        new = m.speculative_decode([0], [tok], [pos], [16 - len(got)], [[]])[0]
+        got += [tok] + new[:-1]
+        pos += len(new)
+        tok = new[-1]
+    got = got[:16]
+    assert head.accepted > 0
+    plain, lg = fresh(False)
+    for j, t in enumerate(got):
+        lg = lg.float().flatten()
+        top = lg.max().item()
+        assert lg[t].item() >= top - 3e-2 * max(1.0, abs(top)), (j, t, lg[t].item(), top)
+        lg = plain.decode([0], [t], [len(ids) + j])
+    status_ok()
+
+
+@pytest.mark.parametrize("nq,nkv,hd", [(32, 2, 256), (4, 1, 256), (8, 2, 64), (16, 1, 128)])
+def test_flash_attention_prefill(nq, nkv, hd):
+    """tcgen05 prefill attention: prompt chunks continuing a cached prefix, several segments."""
+    bs = 16
+    ctx = [300, 77, 1000, 130]
+    kc, vc, table, mb = _paged([c + 8 for c in ctx], nkv, hd, bs, seed=hd + nq)
+    segs = [(0, 0, 300), (1, 40, 37), (2, 700, 300), (3, 129, 1)]  # (lane, start, rows)
+    T = sum(s[2] for s in segs)
+    q = rnd(T, nq, hd, seed=5 + hd)
+    pos, lanes, cu, starts = [], [], [0], []
+    for lane, st, n in segs:
+        pos += list(range(st, st + n))
+        lanes.append(lane)
+        starts.append(st)
+        cu.append(cu[-1] + n)
+    i32 = dict(dtype=torch.int32, device=DEV)
+    assert ops.prefill_shaped(q, kc, cu, bs)
+    out = ops.attention_varlen(q, kc, vc, table, torch.tensor(lanes, **i32), torch.tensor(cu, **i32),
+                               torch.tensor(starts, **i32), bs, lanes, cu, starts, None,
+                               positions=torch.tensor(pos, **i32), max_ctx=max(ctx))
+    torch.cuda.synchronize()
+    exp = ops.attention_varlen(q.cpu(), kc.cpu(), vc.cpu(), table.cpu(), torch.tensor(lanes), torch.tensor(cu),
+                               torch.tensor(starts), bs, lanes, cu, starts, table.cpu().tolist())
+    close(out.cpu(), exp, atol=2e-2)
+    status_ok()
