@@ -175,6 +175,24 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   return r;
 }
 
+// Eight e2m1 codes (one 32-bit word, code j in bits 4j..4j+3) -> four f16x2 words, on the
+// integer ALU. A code [s e1 e0 m] placed at f16 bits 15 / 11 / 10 / 9 is exactly its value times
+// 2^-14 (e = 0 lands in the f16 subnormal range, e > 0 in the normal range, both scaled by the
+// same 2^-14), so a byte permute plus a mask builds the f16 bits and one multiply by the
+// power of two `sc` = 2^(14 + block exponent) applies the e8m0 scale exactly.
+__device__ __forceinline__ void e2m1x8_placed(uint32_t w, uint32_t* o) {
+  // even codes: e/m bits to byte bits 1..3, sign to bit 7; odd codes likewise from the high nibble
+  const uint32_t ev = ((w << 1) & 0x0E0E0E0Eu) | ((w << 4) & 0x80808080u);
+  const uint32_t od = ((w >> 3) & 0x0E0E0E0Eu) | (w & 0x80808080u);
+  // interleave (even, odd) byte pairs, then spread each pair into the high bytes of two halves
+  // (selector 4 = a byte of the zero operand)
+  const uint32_t p01 = __byte_perm(ev, od, 0x5140), p23 = __byte_perm(ev, od, 0x7362);
+  o[0] = __byte_perm(p01, 0, 0x1404);
+  o[1] = __byte_perm(p01, 0, 0x3424);
+  o[2] = __byte_perm(p23, 0, 0x1404);
+  o[3] = __byte_perm(p23, 0, 0x3424);
+}
+
 template <int BN, bool FP4>
 __global__ void __launch_bounds__(MOE_THREADS, 1)
     moe_gemm_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, MoeArgs a,
@@ -471,27 +489,44 @@ __global__ void __launch_bounds__(MOE_THREADS, 1)
 // Same work decomposition as moe_gemm_kernel, but the converted f16 weight tile is written to
 // tensor memory (tcgen05.st) and the MMA reads its A operand from there. Shared memory only
 // carries the packed fp4 codes and the token tiles. One pipeline stage covers 256 K elements:
-// the fp4 tile arrives as 128 rows x 128 bytes (full cache lines per row) and the token tile as
-// four 64-wide swizzle atoms; each of the 4 converter groups decodes one 64-wide sub-block.
-//   warp 0       TMA producer          warp 1      TMEM allocator + MMA issuer
-//   warps 2..5   epilogue              warps 6..21 converters: group g = sub-block g of every
-//                                      stage; warp w covers the TMEM lane quarter w % 4
+// the fp4 tile arrives as 128 rows x 128 bytes (128-byte swizzled, so the per-row reads of the
+// converters are bank-conflict free) and the token tile as four 64-wide swizzle atoms.
+//   warp 0       TMA producer (codes, token tile; e8m0 scales by bulk copy per tile)
+//   warp 1       TMEM allocator
+//   warps 2..5   epilogue
+//   warps 6..21  four converter groups of four warps (warp w covers TMEM lane quarter w % 4).
+//                Group g decodes sub-block g of every stage and one of its threads issues that
+//                sub-block's MMAs into the group's own accumulator, so MMA issue is spread over
+//                four threads that already run at the converters' pace (a single issuer thread
+//                sharing its scheduler with four ALU-bound converter warps fell behind), and the
+//                four accumulators form independent chains. The epilogue adds them.
 constexpr int MT_THREADS = 704;
 constexpr int MT_NA = 8;          // A ring depth in TMEM (32 columns = 64 K elements each)
-constexpr int MT_ABASE = 256;     // first TMEM column of the A ring
+constexpr int MT_ABASE = 256;     // first TMEM column of the A ring; accumulators below it
 constexpr int MT_SK = 256;        // K elements per stage
+constexpr int MT_MAX_EXPERTS = 1024;  // local experts per launch (tile prefix lives in shared memory)
+
+// Columns (tokens) of one tile: the rest of the expert's tokens, rounded up to 16, at most BN.
+template <int BN>
+__device__ __forceinline__ int tile_cols(int rest) {
+  const int n = (rest + 15) & ~15;
+  return n < BN ? n : BN;
+}
 
 template <int BN>
 struct MoeTmCfg {
+  static constexpr int ACC_COLS = 4 * BN;                        // one tile: 4 group accumulators
+  static constexpr int NBUF = MT_ABASE / ACC_COLS >= 2 ? 2 : 1;  // tile buffers below the A ring
   static constexpr int B_ATOM = BN * 64 * 2;   // one 64-wide swizzled token tile
   static constexpr int B = 4 * B_ATOM;
   static constexpr int RAW = 128 * MT_SK / 2;   // 16 KB of packed codes
   static constexpr int STAGE = B + RAW;         // multiple of 1024
   static constexpr int SCALE_MAX = 128 * 128;
-  static constexpr int STAGING = 32 * 128 * 2;
-  static constexpr int BUDGET = 212 * 1024 - STAGING - 2 * SCALE_MAX;
+  static constexpr int STAGING = BN * 128 * 2;  // one whole output tile (bf16)
+  static constexpr int PREFIX = 4 * (MT_MAX_EXPERTS + 1);
+  static constexpr int BUDGET = 212 * 1024 - STAGING - 2 * SCALE_MAX - PREFIX;
   static constexpr int STAGES = BUDGET / STAGE > 12 ? 12 : BUDGET / STAGE;
-  static constexpr int SMEM = 1024 + STAGES * STAGE + STAGING + 2 * SCALE_MAX + 1024;
+  static constexpr int SMEM = 1024 + STAGES * STAGE + STAGING + 2 * SCALE_MAX + 1024 + PREFIX;
 };
 
 template <int BN>
@@ -500,6 +535,7 @@ __global__ void __launch_bounds__(MT_THREADS, 1)
                         uint32_t idesc) {
   using C = MoeTmCfg<BN>;
   static_assert(C::STAGE % 1024 == 0, "stage must keep the token tiles 1024-byte aligned");
+  static_assert(C::NBUF * C::ACC_COLS <= MT_ABASE, "accumulators overlap the A ring");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -514,15 +550,14 @@ __global__ void __launch_bounds__(MT_THREADS, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* sc_full = acc_empty + 2;
   uint64_t* sc_empty = sc_full + 2;
-  uint64_t* drain = sc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  uint64_t* drain = sc_empty + 2;  // [4], one per issuing group
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_p = const_cast<int*>(abort_flag) + 1;
-  int* consumed_p = issued_p + 1;
+  int* tstart = reinterpret_cast<int*>(sbuf + 2 * C::SCALE_MAX + 1024);  // [count + 1]
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_tiles = a.n_rows / 128;
-  const int units = a.count * n_tiles;
   const int ksub = a.K / MBK;                        // 64-wide sub-blocks in K
   const int kstages = (a.K + MT_SK - 1) / MT_SK;     // stages per tile
   const int srow = a.K / 32;
@@ -531,22 +566,21 @@ __global__ void __launch_bounds__(MT_THREADS, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], 4);  // one commit (or plain arrive) per converter group
     }
     for (int i = 0; i < MT_NA; ++i) {
       mbar_init(&a_full[i], 128);
       mbar_init(&a_empty[i], 1);
     }
     for (int i = 0; i < 2; ++i) {
-      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_full[i], 4);
       mbar_init(&acc_empty[i], 128);
       mbar_init(&sc_full[i], 1);
       mbar_init(&sc_empty[i], 512);
     }
-    mbar_init(drain, 1);
+    for (int i = 0; i < 4; ++i) mbar_init(&drain[i], 1);
     *abort_flag = 0;
     *issued_p = 0;
-    *consumed_p = 0;
     fence_barrier_init();
     prefetch_tmap(&tmW);
     prefetch_tmap(&tmX);
@@ -555,11 +589,42 @@ __global__ void __launch_bounds__(MT_THREADS, 1)
     tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
+  if (warp == 2) {
+    // exclusive prefix of token tiles per expert: tstart[e] = sum over e' < e of ceil(counts[e'] / BN)
+    int run = 0;
+    for (int base = 0; base < a.count; base += 32) {
+      const int e = base + lane;
+      const int t = e < a.count ? (a.counts[e] + BN - 1) / BN : 0;
+      int incl = t;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffff, incl, o);
+        if (lane >= o) incl += v;
+      }
+      if (e < a.count) tstart[e] = run + incl - t;
+      run += __shfl_sync(0xffffffff, incl, 31);
+    }
+    if (lane == 0) tstart[a.count] = run;
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-
+  // Work unit = (token tile, 128-row weight tile), weight tile fastest: one hot expert's token
+  // tiles spread over many CTAs, and CTAs working on one token tile run side by side (the tile
+  // stays in L2).
+  const int units = tstart[a.count] * n_tiles;
+  auto unit = [&](int u, int& e, int& nt, int& m0) {
+    const int tt = u / n_tiles;
+    nt = u % n_tiles;
+    int lo = 0, hi = a.count - 1;  // last expert whose first tile is <= tt (empty experts share starts)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tstart[mid] <= tt) lo = mid; else hi = mid - 1;
+    }
+    e = lo;
+    m0 = (tt - tstart[e]) * BN;
+  };
   auto wrow = [&](int nt, int r) -> int {
     return gu ? (r < 64 ? nt * 64 + r : a.n_rows / 2 + nt * 64 + (r - 64)) : nt * 128 + r;
   };
@@ -569,9 +634,9 @@ __global__ void __launch_bounds__(MT_THREADS, 1)
     if (elect_one()) {
       int it = 0, ui = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-        const int e = u / n_tiles, nt = u % n_tiles;
+        int e, nt, m0;
+        unit(u, e, nt, m0);
         const int cnt = a.counts[e];
-        if (cnt == 0) continue;
         const int off = a.offsets[e];
         const long erow = (long)e * a.n_rows;
         const int sb = ui & 1;
@@ -590,204 +655,207 @@ __global__ void __launch_bounds__(MT_THREADS, 1)
                      "l"(s1), "r"(half), "r"(smem_u32(&sc_full[sb]))
                      : "memory");
         ++ui;
-        for (int m0 = 0; m0 < cnt; m0 += BN) {
-          for (int ks = 0; ks < kstages; ++ks, ++it) {
-            const int s = it % C::STAGES;
-            if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) goto prod_done;
-            uint8_t* st = stages + s * C::STAGE;
-            mbar_expect_tx(&full[s], C::STAGE);
+        const int ne = tile_cols<BN>(cnt - m0);
+        for (int ks = 0; ks < kstages; ++ks, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) goto prod_done;
+          uint8_t* st = stages + s * C::STAGE;
+          mbar_expect_tx(&full[s], 4 * ne * 128 + C::RAW);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_2d(st + j * C::B_ATOM, &tmX, &full[s], ks * MT_SK + j * 64, off + m0);
-            tma_load_2d(st + C::B, &tmW, &full[s], ks * MT_SK / 2, (int)(erow + wrow(nt, 0)));
-            tma_load_2d(st + C::B + C::RAW / 2, &tmW, &full[s], ks * MT_SK / 2, (int)(erow + wrow(nt, 64)));
-            *issued_p = it + 1;
-          }
+          for (int j = 0; j < 4; ++j)
+            for (int t = 0; t < ne; t += 16)
+              tma_load_2d(st + j * C::B_ATOM + t * 128, &tmX, &full[s], ks * MT_SK + j * 64, off + m0 + t);
+          tma_load_2d(st + C::B, &tmW, &full[s], ks * MT_SK / 2, (int)(erow + wrow(nt, 0)));
+          tma_load_2d(st + C::B + C::RAW / 2, &tmW, &full[s], ks * MT_SK / 2, (int)(erow + wrow(nt, 64)));
+          *issued_p = it + 1;
         }
       }
     prod_done:;
     }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    if (elect_one()) {
-      int it = 0, ti = 0, sit = 0;
-      bool ok = true;
-      for (int u = blockIdx.x; u < units && ok && !*abort_flag; u += gridDim.x) {
-        const int e = u / n_tiles;
-        const int cnt = a.counts[e];
-        for (int m0 = 0; m0 < cnt && ok; m0 += BN, ++ti) {
-          const int acc = ti & 1;
-          if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc_fence_after();
-          const uint32_t d = tmem + acc * BN;
-          for (int ks = 0; ks < kstages && ok; ++ks, ++it) {
-            const int s = it % C::STAGES;
-            if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
-              ok = false;
-              break;
-            }
-            const int nsub = min(4, ksub - ks * 4);
-            const uint32_t sbase = smem_u32(stages + s * C::STAGE);
-            for (int j = 0; j < nsub; ++j, ++sit) {
-              const int ai = sit % MT_NA;
-              if (!mbar_wait(&a_full[ai], (sit / MT_NA) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
-                ok = false;
-                break;
-              }
-              tc_fence_after();
-              const uint64_t db = desc_sw128(sbase + j * C::B_ATOM);
-              const uint32_t at = tmem + MT_ABASE + ai * 32;
-#pragma unroll
-              for (int kk = 0; kk < MBK / 16; ++kk)
-                mma_f16_ts(d, at + kk * 8, db + 2 * kk, idesc, (ks | j | kk) != 0);
-              mma_commit(&a_empty[ai]);
-            }
-            if (!ok) break;
-            mma_commit(&empty[s]);
-            *consumed_p = it + 1;
-          }
-          if (!ok) break;
-          mma_commit(&acc_full[acc]);
-        }
-      }
-      mma_commit(drain);
-      mbar_wait(drain, 0, a.err, ERR_DRAIN, nullptr);
-    }
-  } else if (warp < 6) {
+  } else if (warp >= 2 && warp < 6) {
     // ---------------------------------------------------------------- epilogue
     const int ew = warp & 3;
     const int row = ew * 32 + lane;
     const int et = threadIdx.x - 64;
+    const int nacc = ksub < 4 ? ksub : 4;  // group accumulators written (group g owns sub-blocks g mod 4)
     int ti = 0;
-    for (int u = blockIdx.x; u < units; u += gridDim.x) {
-      const int e = u / n_tiles, nt = u % n_tiles;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++ti) {
+      int e, nt, m0;
+      unit(u, e, nt, m0);
       const int cnt = a.counts[e];
       const int off = a.offsets[e];
-      bool stop = false;
-      for (int m0 = 0; m0 < cnt; m0 += BN, ++ti) {
-        const int acc = ti & 1;
-        if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) {
-          stop = true;
-          break;
-        }
-        tc_fence_after();
-        constexpr int CH = BN < 32 ? BN : 32;
-        for (int c0 = 0; c0 < BN; c0 += CH) {
-          float v[32];
-          const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
-          if constexpr (CH == 32) tmem_ld32(taddr, v); else tmem_ld16(taddr, v);
+      const int ab = ti % C::NBUF;
+      if (!mbar_wait(&acc_full[ab], (ti / C::NBUF) & 1, a.err, ERR_EPI_WAIT, abort_flag)) break;
+      tc_fence_after();
+      const int ne = tile_cols<BN>(cnt - m0);
+      // TMEM -> registers (sum of the group accumulators) -> bf16 staging; then free the buffer
+      for (int c0 = 0; c0 < ne; c0 += 16) {
+        float v[16];
+        const uint32_t taddr = tmem + ab * C::ACC_COLS + c0 + ((uint32_t)(ew * 32) << 16);
+        tmem_ld16(taddr, v);
+        for (int g = 1; g < nacc; ++g) {
+          float w[16];
+          tmem_ld16(taddr + g * BN, w);
 #pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            bf16 o = __float2bfloat16(v[j]);
-            staging[j * 128 + row] = *reinterpret_cast<uint16_t*>(&o);
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
-          const int nvalid = min(CH, cnt - m0 - c0);
-          if (gu) {
-            __half* Y = reinterpret_cast<__half*>(a.out);
-            for (int idx = et; idx < CH * 64; idx += 128) {
-              const int j = idx / 64, r = idx % 64;
-              if (j < nvalid) {
-                uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
-                const float g = __bfloat162float(*reinterpret_cast<bf16*>(&gb));
-                const float uu = __bfloat162float(*reinterpret_cast<bf16*>(&ub));
-                const float sg = __bfloat162float(__float2bfloat16(g / (1.f + expf(-g))));
-                const float y = __bfloat162float(__float2bfloat16(sg * uu));
-                Y[(long)(off + m0 + c0 + j) * a.out_cols + nt * 64 + r] = __float2half_rn(y);
-              }
-            }
-          } else {
-            bf16* Y = reinterpret_cast<bf16*>(a.out);
-            for (int idx = et; idx < CH * 16; idx += 128) {
-              const int j = idx / 16, q = idx % 16;
-              if (j < nvalid) {
-                const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
-                *reinterpret_cast<uint4*>(Y + (long)(off + m0 + c0 + j) * a.out_cols + nt * 128 + q * 8) = val;
-              }
-            }
-          }
-          asm volatile("bar.sync 1, 128;" ::: "memory");
+          for (int j = 0; j < 16; ++j) v[j] += w[j];
         }
-        tc_fence_before();
-        mbar_arrive(&acc_empty[acc]);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          bf16 o = __float2bfloat16(v[j]);
+          staging[(c0 + j) * 128 + row] = *reinterpret_cast<uint16_t*>(&o);
+        }
       }
-      if (stop) break;
+      tc_fence_before();
+      mbar_arrive(&acc_empty[ab]);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const int nvalid = min(ne, cnt - m0);
+      if (gu) {
+        __half* Y = reinterpret_cast<__half*>(a.out);
+        for (int idx = et; idx < nvalid * 64; idx += 128) {
+          const int j = idx / 64, r = idx % 64;
+          uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
+          const float g = __bfloat162float(*reinterpret_cast<bf16*>(&gb));
+          const float uu = __bfloat162float(*reinterpret_cast<bf16*>(&ub));
+          const float sg = __bfloat162float(__float2bfloat16(g / (1.f + expf(-g))));
+          const float y = __bfloat162float(__float2bfloat16(sg * uu));
+          Y[(long)(off + m0 + j) * a.out_cols + nt * 64 + r] = __float2half_rn(y);
+        }
+      } else {
+        bf16* Y = reinterpret_cast<bf16*>(a.out);
+        for (int idx = et; idx < nvalid * 16; idx += 128) {
+          const int j = idx / 16, q = idx % 16;
+          const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
+          *reinterpret_cast<uint4*>(Y + (long)(off + m0 + j) * a.out_cols + nt * 128 + q * 8) = val;
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
     }
-  } else {
-    // ---------------------------------------------------------------- fp4 -> f16 converters
+  } else if (warp >= 6) {
+    // ---------------------------------------------------------------- converters + MMA issue
     const int cw = warp - 6;   // 0..15
     const int grp = cw >> 2;   // sub-block of every stage this group decodes
     const int q = warp & 3;    // TMEM lane quarter
     const int r = q * 32 + lane;
-    int it = 0, ui = 0, sit0 = 0;
+    // the issuing warp of the group (one per SMSP); it waits as a whole warp so that it stays
+    // converged for the warp-collective tcgen05.st, and its lane 0 issues the MMAs and commits
+    const bool iwarp = q == grp;
+    int it = 0, ui = 0, sit0 = 0, ti = 0;
     bool stop = false;
-    for (int u = blockIdx.x; u < units && !stop; u += gridDim.x) {
-      const int e = u / n_tiles;
-      const int cnt = a.counts[e];
-      if (cnt == 0) continue;
+    for (int u = blockIdx.x; u < units && !stop; u += gridDim.x, ++ti) {
+      int e, nt, m0;
+      unit(u, e, nt, m0);
+      const int ab = ti % C::NBUF;
+      const uint32_t dacc = tmem + ab * C::ACC_COLS + grp * BN;
+      const uint32_t id_t = (idesc & ~(0x3Fu << 17)) | ((uint32_t)(tile_cols<BN>(a.counts[e] - m0) >> 3) << 17);
       const int sb = ui & 1;
       if (!mbar_wait(&sc_full[sb], (ui >> 1) & 1, a.err, ERR_MMA_WAIT, abort_flag)) break;
       const uint8_t* srw = sbuf + sb * C::SCALE_MAX + r * srow;
-      for (int m0 = 0; m0 < cnt && !stop; m0 += BN) {
-        for (int ks = 0; ks < kstages; ++ks, ++it) {
-          const int nsub = min(4, ksub - ks * 4);
-          const int sit = sit0 + grp;
-          sit0 += nsub;
-          if (grp >= nsub) continue;
-          const int s = it % C::STAGES, ai = sit % MT_NA;
-          if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag) ||
-              !mbar_wait(&a_empty[ai], ((sit / MT_NA) & 1) ^ 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+      // the group's last stage with a sub-block in this tile (its acc_full commit follows it)
+      const int last_ks = grp < ksub ? (ksub - 1 - grp) / 4 : -1;
+      if (iwarp) {
+        // the tile buffer must be free of the epilogue before the group's first MMA into it
+        if (!mbar_wait(&acc_empty[ab], ((ti / C::NBUF) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) stop = true;
+        tc_fence_after();
+        if (last_ks < 0 && !stop && lane == 0) mbar_arrive(&acc_full[ab]);  // nothing to add for this group
+        __syncwarp();
+      }
+      uint4 scw = make_uint4(0, 0, 0, 0);  // this row's scale bytes of two stages (16-byte rows only)
+      for (int ks = 0; ks < kstages && !stop; ++ks, ++it) {
+        const int nsub = min(4, ksub - ks * 4);
+        const int sit = sit0 + grp;
+        sit0 += nsub;
+        const int s = it % C::STAGES;
+        if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+          stop = true;
+          break;
+        }
+        if (grp >= nsub) {  // no sub-block for this group in this stage
+          if (iwarp && lane == 0) mbar_arrive(&empty[s]);
+          continue;
+        }
+        const int ai = sit % MT_NA;
+        if (!mbar_wait(&a_empty[ai], ((sit / MT_NA) & 1) ^ 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+          stop = true;
+          break;
+        }
+        const int kb = ks * 4 + grp;  // 64-wide K sub-block index
+        // the fp4 tile is 128-byte swizzled: 16-byte chunk c of row r sits at chunk c ^ (r & 7)
+        const uint8_t* rrow = stages + s * C::STAGE + C::B + r * (MT_SK / 2);
+        const uint4 c0 = *reinterpret_cast<const uint4*>(rrow + (((2 * grp) ^ (r & 7)) << 4));
+        const uint4 c1 = *reinterpret_cast<const uint4*>(rrow + (((2 * grp + 1) ^ (r & 7)) << 4));
+        const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+        uint32_t sc16;  // the two block exponents of this sub-block, low byte first
+        if (srow % 16 == 0) {
+          if ((ks & 1) == 0) scw = *reinterpret_cast<const uint4*>(srw + ks * 8);
+          const uint32_t wsel = (ks & 1) ? ((grp & 2) ? scw.w : scw.z) : ((grp & 2) ? scw.y : scw.x);
+          sc16 = (wsel >> ((grp & 1) * 16)) & 0xffff;
+        } else {
+          sc16 = srw[kb * 2] | ((uint32_t)srw[kb * 2 + 1] << 8);
+        }
+        uint32_t outw[32];
+#pragma unroll
+        for (int blk = 0; blk < 2; ++blk) {
+          const int sexp = (int)((sc16 >> (8 * blk)) & 0xff) - 127;
+#pragma unroll
+          for (int w4 = 0; w4 < 4; ++w4) e2m1x8_placed(words[blk * 4 + w4], outw + blk * 16 + w4 * 4);
+          if (sexp >= -23 && sexp <= 1) {  // 2^(14 + sexp) is a normal f16 and every product is exact
+            const uint32_t sb16 = (uint32_t)(sexp + 29) << 10;
+            const uint32_t sw = sb16 | (sb16 << 16);
+            const __half2 sc2 = *reinterpret_cast<const __half2*>(&sw);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              __half2 v = __hmul2(*reinterpret_cast<const __half2*>(&outw[blk * 16 + j]), sc2);
+              outw[blk * 16 + j] = *reinterpret_cast<uint32_t*>(&v);
+            }
+          } else {  // large or tiny scales: scale in fp32, round once to f16
+            const float scf = exp2f((float)(sexp + 14));
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&outw[blk * 16 + j]));
+              __half2 v = __floats2half2_rn(f.x * scf, f.y * scf);
+              outw[blk * 16 + j] = *reinterpret_cast<uint32_t*>(&v);
+            }
+          }
+        }
+        tmem_st32(tmem + MT_ABASE + ai * 32 + ((uint32_t)(q * 32) << 16), outw);
+        tmem_wait_st();
+        tc_fence_before();
+        mbar_arrive(&a_full[ai]);
+        if (iwarp) {
+          // all four warps of the group have stored their lane quarters of this sub-block
+          if (!mbar_wait(&a_full[ai], (sit / MT_NA) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
             stop = true;
             break;
           }
-          const int kb = ks * 4 + grp;  // 64-wide K sub-block index
-          const uint8_t* raw = stages + s * C::STAGE + C::B + r * (MT_SK / 2) + grp * 32;
-          const uint4 c0 = *reinterpret_cast<const uint4*>(raw);
-          const uint4 c1 = *reinterpret_cast<const uint4*>(raw + 16);
-          const uint32_t words[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-          uint32_t outw[32];
+          tc_fence_after();
+          if (lane == 0) {
+            const uint64_t db = desc_sw128(smem_u32(stages + s * C::STAGE + grp * C::B_ATOM));
+            const uint32_t at = tmem + MT_ABASE + ai * 32;
 #pragma unroll
-          for (int blk = 0; blk < 2; ++blk) {
-            const int sexp = (int)srw[kb * 2 + blk] - 127;
-            const bool in_range = sexp >= -24 && sexp <= 15;
-            const uint32_t sbits = sexp >= -14 ? (uint32_t)((sexp + 15) << 10) : (1u << (sexp + 24));
-            const uint32_t sw = (sbits & 0xffff) | ((sbits & 0xffff) << 16);
-            const __half2 sc2 = *reinterpret_cast<const __half2*>(&sw);
-            const float scf = exp2f((float)sexp);
-#pragma unroll
-            for (int w4 = 0; w4 < 4; ++w4) {
-              const uint32_t wd = words[blk * 4 + w4];
-#pragma unroll
-              for (int b2 = 0; b2 < 4; ++b2) {
-                uint32_t h2 = e2m1x2_to_f16x2((wd >> (8 * b2)) & 0xff);
-                __half2 v = *reinterpret_cast<__half2*>(&h2);
-                if (in_range) {
-                  v = __hmul2(v, sc2);
-                } else {
-                  const float2 f = __half22float2(v);
-                  v = __floats2half2_rn(f.x * scf, f.y * scf);
-                }
-                outw[blk * 16 + w4 * 4 + b2] = *reinterpret_cast<uint32_t*>(&v);
-              }
-            }
+            for (int kk = 0; kk < MBK / 16; ++kk)
+              mma_f16_ts(dacc, at + kk * 8, db + 2 * kk, id_t, (ks | kk) != 0);
+            mma_commit(&a_empty[ai]);
+            mma_commit(&empty[s]);
+            if (ks == last_ks) mma_commit(&acc_full[ab]);
           }
-          tmem_st32(tmem + MT_ABASE + ai * 32 + ((uint32_t)(q * 32) << 16), outw);
-          tmem_wait_st();
-          tc_fence_before();
-          mbar_arrive(&a_full[ai]);
+          __syncwarp();
         }
       }
       mbar_arrive(&sc_empty[sb]);
       ++ui;
     }
+    if (iwarp && lane == 0) {  // every MMA of this thread completes before TMEM is released
+      mma_commit(&drain[grp]);
+      mbar_wait(&drain[grp], 0, a.err, ERR_DRAIN, nullptr);
+    }
   }
 
   __syncthreads();
   if (*abort_flag && threadIdx.x == 0) {
-    for (int it = *consumed_p; it < *issued_p; ++it)
-      mbar_wait(&full[it % C::STAGES], (it / C::STAGES) & 1, a.err, ERR_DRAIN, nullptr);
+    // TMA copies may still be in flight for the last issued stages: wait for each of them
+    const int n = *issued_p;
+    for (int i = n - C::STAGES < 0 ? 0 : n - C::STAGES; i < n; ++i)
+      mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, a.err, ERR_DRAIN, nullptr);
   }
   __syncthreads();
   if (warp == 1) {
@@ -862,10 +930,12 @@ int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8
   static const bool smem_a = getenv("QB_MOE_SMEM_A") && getenv("QB_MOE_SMEM_A")[0] == '1';
   int r;
   if (!smem_a) {
-    const int bn = BN > 64 ? 64 : BN;
-    r = make_tmap_2d(&tw, wq, 1, (long)count * n_rows, k_cols / 2, k_cols / 2, 64, MT_SK / 2, false);
+    if (count > MT_MAX_EXPERTS) return -2;
+    static const int bn_max = getenv("QB_MOE_BN_MAX") ? atoi(getenv("QB_MOE_BN_MAX")) : 64;
+    const int bn = BN > bn_max ? bn_max : BN;
+    r = make_tmap_2d(&tw, wq, 1, (long)count * n_rows, k_cols / 2, k_cols / 2, 64, MT_SK / 2, true);
     if (r) return 1000 + r;
-    r = make_tmap_2d(&tx, xin, 2, cap, k_cols, in_cols, bn, MBK, true);
+    r = make_tmap_2d(&tx, xin, 2, cap, k_cols, in_cols, 16, MBK, true);  // 16-token boxes
     if (r) return 2000 + r;
     switch (bn) {
       case 16: return moe_tm_launch<16>(tw, tx, a, max_ctas, s);
