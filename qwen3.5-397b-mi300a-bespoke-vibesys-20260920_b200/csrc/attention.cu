@@ -24,6 +24,7 @@ constexpr int FA_KT = 64;        // keys per tile
 constexpr int FA_THREADS = 192;
 constexpr int FA_S_COL = 0;      // S buffers: cols [0, 64) and [64, 128)
 constexpr int FA_O_COL = 256;    // O accumulator
+constexpr int FA_WS_HEAD = 4;    // partial record: max, sum, 2 pad words, then O (16-byte aligned)
 
 // K-major SW128 descriptor is desc_sw128; MN-major SW128 needs explicit LBO (MN-atom stride) and
 // SBO (8-row K-group stride).
@@ -67,6 +68,8 @@ struct FaArgs {
   bf16* out;         // [T, nq, HD]
   float scale_log2;  // head_dim**-0.5 * log2(e)
   int* err;
+  int splits;        // key-range splits per tile (grid z); > 1 writes partial results to ws
+  float* ws;         // [T * nq][splits][4 + HD]: running max (log2 units), sum, 2 pad, unnormalised O
 };
 
 template <int HD>
@@ -96,7 +99,24 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   const int seg = a.tiles[tile * 3], row0 = a.tiles[tile * 3 + 1], nrows = a.tiles[tile * 3 + 2];
   const int lane_id = a.seg_lane[seg];
   const int last_pos = a.pos[row0 + nrows - 1];
-  const int n_kt = (last_pos + FA_KT) / FA_KT;
+  // key tiles [kt0, kt1) of this split (all tiles up to the tile's last position when unsplit)
+  const int n_all = (last_pos + FA_KT) / FA_KT;
+  int kt0 = 0, kt1 = n_all;
+  if (a.splits > 1) {
+    const int per = (n_all + a.splits - 1) / a.splits;
+    kt0 = blockIdx.z * per;
+    kt1 = min(n_all, kt0 + per);
+    if (kt0 >= kt1) {  // nothing to read: an empty partial (the combine skips it)
+      if (threadIdx.x < 128 && threadIdx.x / a.G < nrows) {
+        const int r = threadIdx.x;
+        float* w = a.ws + (((long)(row0 + r / a.G) * a.nq + (long)g * a.G + r % a.G) * a.splits + blockIdx.z) * (HD + FA_WS_HEAD);
+        w[0] = -INFINITY;
+        w[1] = 0.f;
+      }
+      return;
+    }
+  }
+  const int n_kt = kt1 - kt0;
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -136,7 +156,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
         mbar_expect_tx(&kv_full[st], C::STAGE);
 #pragma unroll
         for (int p = 0; p < FA_KT / 16; ++p) {
-          const int blk = (i * FA_KT) / 16 + p;
+          const int blk = ((kt0 + i) * FA_KT) / 16 + p;
           const int page = blk < a.max_blocks ? tab[blk] : 0;
 #pragma unroll
           for (int j = 0; j < C::ATOMS; ++j) {
@@ -215,7 +235,7 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       tmem_ld32(tmem + lane_off + FA_S_COL + st * FA_KT + 32, sv + 32);
       tc_fence_before();
       mbar_arrive(&s_free[st]);
-      const int k0 = i * FA_KT;
+      const int k0 = (kt0 + i) * FA_KT;
       float mx = -INFINITY;
 #pragma unroll
       for (int jj = 0; jj < 64; ++jj) {
@@ -267,12 +287,22 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
     if (ok && mbar_wait(o_done, (n_kt - 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      bf16* dst = a.out + ((long)(valid ? row0 + tok : 0) * a.nq + (long)g * a.G + (r % a.G)) * HD;
+      const long orow = (long)(valid ? row0 + tok : 0) * a.nq + (long)g * a.G + (r % a.G);
+      bf16* dst = a.out + orow * HD;
+      float* wsr = a.splits > 1 ? a.ws + (orow * a.splits + blockIdx.z) * (HD + FA_WS_HEAD) : nullptr;
+      if (wsr && valid) {
+        wsr[0] = m;
+        wsr[1] = l;
+      }
 #pragma unroll 1
       for (int c0 = 0; c0 < HD; c0 += 32) {
         float ov[32];
         tmem_ld32(tmem + lane_off + FA_O_COL + c0, ov);  // every lane: the load is warp-collective
-        if (valid) {
+        if (wsr && valid) {
+#pragma unroll
+          for (int u = 0; u < 32; u += 4)
+            *reinterpret_cast<float4*>(wsr + FA_WS_HEAD + c0 + u) = make_float4(ov[u], ov[u + 1], ov[u + 2], ov[u + 3]);
+        } else if (valid) {
           uint32_t w[16];
 #pragma unroll
           for (int u = 0; u < 16; ++u) {
@@ -296,6 +326,29 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 512);
+  }
+}
+
+// Merge the key-range partials of every (row, head): O = sum_s 2^(m_s - M) O_s / sum_s 2^(m_s - M) l_s.
+template <int HD>
+__global__ void fa_combine_kernel(const float* ws, int splits, bf16* out) {
+  const long th = blockIdx.x;  // row * nq + head
+  const float* base = ws + th * splits * (HD + FA_WS_HEAD);
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, base[s * (HD + FA_WS_HEAD)]);
+  float L = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float mm = base[s * (HD + FA_WS_HEAD)];
+    if (mm > -INFINITY) L += exp2f(mm - M) * base[s * (HD + FA_WS_HEAD) + 1];
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  for (int d = threadIdx.x; d < HD; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float mm = base[s * (HD + FA_WS_HEAD)];
+      if (mm > -INFINITY) acc += exp2f(mm - M) * base[s * (HD + FA_WS_HEAD) + FA_WS_HEAD + d];
+    }
+    out[th * HD + d] = __float2bfloat16(acc * inv);
   }
 }
 
@@ -324,8 +377,9 @@ static int tmap3(CUtensorMap* m, const void* base, long d0, long d1, long d2, in
 
 int fa_prefill(const void* q, const void* kc, const void* vc, long cache_rows, const int* table, int max_blocks,
                const int* pos, const int* seg_lane, const int* tiles, int n_tiles, int T, int nq, int nkv, int hd,
-               int block_size, void* out, int* err, cudaStream_t s) {
+               int block_size, int splits, float* ws, void* out, int* err, cudaStream_t s) {
   const int G = nq / nkv;
+  if (splits < 1 || (splits > 1 && !ws)) return -1;
   if (block_size != 16 || nq % nkv || 128 % G || (hd != 64 && hd != 128 && hd != 256)) return -1;
   if (!n_tiles) return 0;
   CUtensorMap tq, tk, tv;
@@ -336,8 +390,8 @@ int fa_prefill(const void* q, const void* kc, const void* vc, long cache_rows, c
   r = tmap3(&tv, vc, hd, nkv, cache_rows, 1, 16);
   if (r) return 3000 + r;
   FaArgs a{tiles, pos, seg_lane, table, max_blocks, G, 128 / G, nq, (bf16*)out,
-           (float)(1.4426950408889634 / sqrt((double)hd)), err};
-  dim3 grid(n_tiles, nkv);
+           (float)(1.4426950408889634 / sqrt((double)hd)), err, splits, ws};
+  dim3 grid(n_tiles, nkv, splits);
 #define QB_FA(H)                                                                                          \
   {                                                                                                       \
     static bool attr = false;                                                                             \
@@ -346,6 +400,7 @@ int fa_prefill(const void* q, const void* kc, const void* vc, long cache_rows, c
       attr = true;                                                                                        \
     }                                                                                                     \
     fa_prefill_kernel<H><<<grid, FA_THREADS, FaCfg<H>::SMEM, s>>>(tq, tk, tv, a);                          \
+    if (splits > 1) fa_combine_kernel<H><<<(long)T * nq, 64, 0, s>>>(ws, splits, (bf16*)out);             \
   }
   if (hd == 256) QB_FA(256) else if (hd == 128) QB_FA(128) else QB_FA(64)
 #undef QB_FA

@@ -191,15 +191,20 @@ Tensor attention_varlen(Tensor q, Tensor kc, Tensor vc, Tensor table, Tensor seg
   return out;
 }
 
-Tensor attention_prefill(Tensor q, Tensor kc, Tensor vc, Tensor table, Tensor seg_lane, Tensor pos, Tensor tiles,
-                         int64_t block_size) {
+Tensor attention_fa(Tensor q, Tensor kc, Tensor vc, Tensor table, Tensor seg_lane, Tensor pos, Tensor tiles,
+                    int64_t block_size, int64_t splits) {
   CHECK_BF16(q);
-  TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "attention_prefill: contiguous");
+  TORCH_CHECK(q.is_contiguous() && kc.is_contiguous() && vc.is_contiguous(), "attention_fa: contiguous");
+  TORCH_CHECK(tiles.dim() == 2 && tiles.size(1) == 3 && tiles.scalar_type() == at::kInt, "attention_fa: tiles [n, 3]");
   const int T = q.size(0), nq = q.size(1), hd = q.size(2), nkv = kc.size(1);
   Tensor out = at::empty_like(q);
+  Tensor ws;
+  if (splits > 1) ws = at::empty({(long)T * nq * splits * (hd + 4)}, q.options().dtype(at::kFloat));
   LAUNCH(qb::fa_prefill(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), kc.size(0), table.data_ptr<int>(), table.size(1),
                         pos.data_ptr<int>(), seg_lane.data_ptr<int>(), tiles.data_ptr<int>(), tiles.size(0), T, nq,
-                        nkv, hd, block_size, out.data_ptr(), err_ptr(q), stream()));
+                        nkv, hd, block_size, (int)splits, splits > 1 ? ws.data_ptr<float>() : nullptr,
+                        out.data_ptr(), err_ptr(q), stream()));
+  if (splits > 1) g_launches.fetch_add(1, std::memory_order_relaxed);  // the combine kernel
   return out;
 }
 
@@ -352,7 +357,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("router_topk", &router_topk2);
   m.def("qk_norm_rope_kv_write", &qk_norm_rope_kv_write);
   m.def("attention_varlen", &attention_varlen);
-  m.def("attention_prefill", &attention_prefill);
+  m.def("attention_fa", &attention_fa);
   m.def("causal_conv_varlen", &causal_conv_varlen);
   m.def("gated_delta_varlen", &gated_delta_varlen);
   m.def("moe_routed_fp4", &moe_routed_fp4);

@@ -42,10 +42,11 @@ int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab,
 int attention_varlen(const void* q, const void* kc, const void* vc, const int* table, int max_blocks,
                      const int* pos, const int* seg_lane, const int* cu, int S, int T, int nq, int nkv, int hd,
                      int block_size, int splits, float* ws, void* out, cudaStream_t s);
-// tcgen05 flash attention for prefill rows (attention.cu); tiles = [n_tiles][segment, row0, rows]
+// tcgen05 flash attention (attention.cu); tiles = [n_tiles][segment, row0, rows]; splits > 1 splits
+// every tile's key range (partials in ws, merged by a second kernel)
 int fa_prefill(const void* q, const void* kc, const void* vc, long cache_rows, const int* table, int max_blocks,
                const int* pos, const int* seg_lane, const int* tiles, int n_tiles, int T, int nq, int nkv, int hd,
-               int block_size, void* out, int* err, cudaStream_t s);
+               int block_size, int splits, float* ws, void* out, int* err, cudaStream_t s);
 int router_topk(const void* logits, long ld, int T, int E, int k, float* w, int* idx, cudaStream_t s);
 
 // MoE: dispatch metadata + grouped MXFP4 expert GEMMs + combine

@@ -152,10 +152,10 @@ def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, 
     ``[0, seg_start + len)``. ``q`` [T, Hq, D]; caches [rows, Hkv, D]. Returns [T, Hq, D].
     On CUDA ``positions`` ([T] absolute positions) and ``max_ctx`` (longest context) are used."""
     if _cuda(q):
-        if prefill_shaped(q, k_cache, cu_h, block_size):
-            tiles = fa_tiles(cu_h, q.shape[1] // k_cache.shape[1])
-            t = torch.tensor(tiles, dtype=torch.int32).pin_memory().to(q.device, non_blocking=True)
-            return ext().attention_prefill(q, k_cache, v_cache, block_table, seg_lane, positions, t, block_size)
+        plan = fa_plan(q, k_cache, cu_h, block_size, max_ctx)
+        if plan is not None:
+            tiles, splits = plan
+            return ext().attention_fa(q, k_cache, v_cache, block_table, seg_lane, positions, tiles, block_size, splits)
         return ext().attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, positions, block_size,
                                       int(max_ctx))
     out = torch.empty_like(q)
@@ -176,16 +176,37 @@ def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, 
     return out
 
 
-def prefill_shaped(q, k_cache, cu_h, block_size) -> bool:
-    """Prefill-shaped batches (>= 4 rows per segment on average) use the tcgen05 flash-attention
-    kernel; decode-shaped ones the split-K kernel."""
-    if cu_h is None or block_size != 16 or os.environ.get("QB_FA_PREFILL", "1") == "0":
-        return False
+_FA_SMS = 148
+_fa_tiles_cache: dict = {}
+
+
+def fa_plan(q, k_cache, cu_h, block_size, max_ctx):
+    """(device tile list, key splits) for the tcgen05 flash-attention kernel, or None when the
+    shape is outside what it supports (then the CUDA-core split-K kernel runs).
+
+    Every tile is (segment, first row, rows) with rows <= 128 / G, so a tile's G query heads x
+    rows fill the 128 MMA rows. When there are fewer (tile, kv head) CTAs than SMs (decode), each
+    tile's key range is split so that one wave covers the GPU; the partials are merged by a
+    second kernel. The tile tensor is cached per (segments, G): a CUDA-graph capture then reads a
+    persistent device tensor instead of recording a copy from a temporary host buffer."""
+    if cu_h is None or block_size != 16 or os.environ.get("QB_FA", "1") == "0":
+        return None
     g = q.shape[1] // k_cache.shape[1]
-    if 128 % g or q.shape[2] not in (64, 128, 256):
-        return False
-    segs = len(cu_h) - 1
-    return segs > 0 and q.shape[0] >= 4 * segs
+    if 128 % g or q.shape[2] not in (64, 128, 256) or len(cu_h) < 2:
+        return None
+    key = (tuple(cu_h), g, q.device)
+    tiles = _fa_tiles_cache.get(key)
+    if tiles is None:
+        host = torch.tensor(fa_tiles(cu_h, g), dtype=torch.int32)
+        tiles = host.to(q.device)
+        if len(_fa_tiles_cache) >= 256:
+            _fa_tiles_cache.pop(next(iter(_fa_tiles_cache)))
+        _fa_tiles_cache[key] = tiles
+    base = tiles.shape[0] * k_cache.shape[1]
+    splits = 1
+    if base < _FA_SMS:
+        splits = max(1, min(_FA_SMS // base, (int(max_ctx) + 63) // 64, 128))
+    return tiles, splits
 
 
 def fa_tiles(cu_h, g: int) -> list[list[int]]:

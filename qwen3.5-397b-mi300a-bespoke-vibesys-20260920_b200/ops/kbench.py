@@ -1,0 +1,206 @@
+"""Kernel micro-benchmarks at the full model's shapes, with roofline fractions.
+
+    python -m qwen35_b200.ops.kbench [--case moe|gemm|attn_prefill|attn_decode|deltanet|all]
+                                     [--tokens N] [--ctx N] [--iters N]
+
+Each case builds random inputs of one hot op at the Qwen3.5-397B-A17B geometry (one GPU, TP=1
+shard sizes unless noted), warms up, then times ``--iters`` launches with CUDA events on the
+launching stream, synchronising before and after. Inputs are far larger than the 126 MB L2
+where the case is bandwidth-bound (weights, KV cache), so nothing is served from a warm L2.
+Reported per case: mean time per call, achieved bytes/s and FLOP/s from the algorithmic
+counts, and the fraction of the measured peaks (``MEASURED_PEAKS.json`` at the repository root
+when present: STREAM-style copy bandwidth and cuBLAS bf16 GEMM throughput).
+
+The same command with one case and a small ``--iters`` is the capture target for ncu; the
+summaries under ``profiles/`` name the exact command lines.
+
+Reference counterparts (behaviour, not code): ``mxfp4_gemv.py`` / ``moe_hip.py`` /
+``prefill_moe.py`` (routed experts), ``skinny_gemm.py`` (dense GEMMs), ``varlen_prefill_attn.py``
+and ``decode_attn_v2.py`` (attention), ``deltanet_fused.py`` (gated delta rule).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from . import core as ops
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_DEFAULT_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
+
+
+def peaks() -> dict:
+    """Measured roofline denominators; the documented fallback when the file is absent."""
+    for p in (os.path.join(HERE, "..", "..", "MEASURED_PEAKS.json"), "MEASURED_PEAKS.json"):
+        if os.path.exists(p):
+            with open(p) as f:
+                d = json.load(f)
+            return {"hbm_gbs": float(d["hbm_gbs"]), "bf16_tflops": float(d["bf16_tflops"]), "source": "measured"}
+    return dict(_DEFAULT_PEAKS, source="fallback")
+
+
+def _time(fn, iters: int) -> float:
+    """Mean milliseconds per call (CUDA events, synchronised on both sides)."""
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(iters):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e) / iters
+
+
+def _report(name: str, ms: float, bytes_: float, flops: float, pk: dict, **extra) -> dict:
+    gbs = bytes_ / ms / 1e6
+    tfs = flops / ms / 1e9
+    row = {"case": name, "ms": round(ms, 4), "GB_s": round(gbs, 1), "TFLOP_s": round(tfs, 2),
+           "hbm_frac": round(gbs / pk["hbm_gbs"], 3), "tensor_frac": round(tfs / pk["bf16_tflops"], 3),
+           "peaks": pk["source"], **extra}
+    print(json.dumps(row), flush=True)
+    return row
+
+
+def _g(seed: int) -> torch.Generator:
+    return torch.Generator(device="cuda").manual_seed(seed)
+
+
+def case_moe(tokens: int, iters: int, pk: dict, experts: int = 512, top_k: int = 10, hidden: int = 4096,
+             inter: int = 1024) -> dict:
+    """Routed MXFP4 experts (gate_up + SiLU*mul + down + weighted combine) for ``tokens`` rows
+    with uniform random routing; bytes = packed weights + scales of every expert hit."""
+    dev = "cuda"
+    g = _g(0)
+    ex = {"w13": torch.randint(0, 256, (experts, 2 * inter, hidden // 2), device=dev, dtype=torch.uint8, generator=g),
+          "s13": torch.full((experts, 2 * inter, hidden // 32), 120, device=dev, dtype=torch.uint8),
+          "w2": torch.randint(0, 256, (experts, hidden, inter // 2), device=dev, dtype=torch.uint8, generator=g),
+          "s2": torch.full((experts, hidden, inter // 32), 120, device=dev, dtype=torch.uint8)}
+    h = torch.randn(tokens, hidden, device=dev, generator=g).to(torch.bfloat16)
+    lg = torch.randn(tokens, experts, device=dev, generator=g).to(torch.bfloat16)
+    tw, ti = ops.router_topk(lg, top_k)
+    active = int((torch.bincount(ti.flatten().long(), minlength=experts) > 0).sum())
+    per_expert = (2 * inter * hidden + hidden * inter) // 2 * (1 + 1 / 16)
+    ms = _time(lambda: ops.moe_routed(h, tw, ti, ex, 0, experts), iters)
+    flops = 2 * tokens * top_k * 3 * hidden * inter
+    return _report(f"moe_T{tokens}", ms, active * per_expert, flops, pk, active_experts=active)
+
+
+def case_gemm(tokens: int, iters: int, pk: dict, n: int = 12288, k: int = 4096) -> dict:
+    """Dense bf16 GEMM y = x W^T (the fused q/k/v/gate projection width at TP=1 by default)."""
+    g = _g(1)
+    # several weight copies cycled so that consecutive calls never hit a warm L2
+    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for _ in range(4)]
+    x = torch.randn(tokens, k, device="cuda", generator=g).to(torch.bfloat16)
+    out = torch.empty(tokens, n, device="cuda", dtype=torch.bfloat16)
+    i = [0]
+
+    def fn():
+        ops.linear(x, ws[i[0] % 4], out)
+        i[0] += 1
+
+    ms = _time(fn, iters)
+    return _report(f"gemm_T{tokens}_N{n}_K{k}", ms, 2 * (n * k + tokens * (k + n)), 2 * tokens * n * k, pk)
+
+
+def _paged_kv(lanes: int, ctx: int, nkv: int, hd: int, bs: int = 16, seed: int = 2):
+    g = _g(seed)
+    per = (ctx + 64 + bs - 1) // bs
+    nblocks = 1 + lanes * per
+    kc = torch.randn(nblocks * bs, nkv, hd, device="cuda", generator=g).to(torch.bfloat16)
+    vc = torch.randn(nblocks * bs, nkv, hd, device="cuda", generator=g).to(torch.bfloat16)
+    table = (torch.arange(lanes * per, dtype=torch.int32).view(lanes, per) + 1).cuda()
+    return kc, vc, table
+
+
+def case_attn_prefill(tokens: int, ctx: int, iters: int, pk: dict, nq: int = 32, nkv: int = 2, hd: int = 256) -> dict:
+    """One prompt chunk of ``tokens`` rows continuing ``ctx`` cached tokens (tcgen05 flash
+    attention). FLOPs count the causal QK^T and PV products actually needed."""
+    bs = 16
+    kc, vc, table = _paged_kv(1, ctx + tokens, nkv, hd)
+    q = torch.randn(tokens, nq, hd, device="cuda", generator=_g(3)).to(torch.bfloat16)
+    i32 = dict(dtype=torch.int32, device="cuda")
+    pos = torch.arange(ctx, ctx + tokens, **i32)
+    lanes, cu, starts = [0], [0, tokens], [ctx]
+    args = (torch.tensor(lanes, **i32), torch.tensor(cu, **i32), torch.tensor(starts, **i32), bs, lanes, cu, starts,
+            None)
+    ms = _time(lambda: ops.attention_varlen(q, kc, vc, table, *args, positions=pos, max_ctx=ctx + tokens), iters)
+    keys = tokens * ctx + tokens * (tokens + 1) / 2
+    flops = 4 * nq * hd * keys
+    kv_bytes = 2 * (ctx + tokens) * nkv * hd * 2
+    return _report(f"attn_prefill_T{tokens}_ctx{ctx}", ms, kv_bytes + 2 * q.numel() * 2, flops, pk)
+
+
+def case_attn_decode(lanes: int, ctx: int, iters: int, pk: dict, nq: int = 32, nkv: int = 2, hd: int = 256) -> dict:
+    """``lanes`` decode rows at context ``ctx`` each (split-K paged attention); bytes = the KV
+    cache read."""
+    bs = 16
+    kc, vc, table = _paged_kv(lanes, ctx, nkv, hd)
+    q = torch.randn(lanes, nq, hd, device="cuda", generator=_g(4)).to(torch.bfloat16)
+    i32 = dict(dtype=torch.int32, device="cuda")
+    pos = torch.full((lanes,), ctx - 1, **i32)
+    ln, cu, st = list(range(lanes)), list(range(lanes + 1)), [ctx - 1] * lanes
+    args = (torch.tensor(ln, **i32), torch.tensor(cu, **i32), torch.tensor(st, **i32), bs, ln, cu, st, None)
+    ms = _time(lambda: ops.attention_varlen(q, kc, vc, table, *args, positions=pos, max_ctx=ctx), iters)
+    kv_bytes = 2 * lanes * ctx * nkv * hd * 2
+    return _report(f"attn_decode_B{lanes}_ctx{ctx}", ms, kv_bytes, 4 * lanes * nq * hd * ctx, pk)
+
+
+def case_deltanet(tokens: int, lanes: int, iters: int, pk: dict, nk: int = 16, nv: int = 64, dk: int = 128,
+                  dv: int = 128) -> dict:
+    """Gated delta rule over ``lanes`` segments of ``tokens`` rows each (fp32 state
+    [nv, dk, dv] per lane read and written once); FLOPs ~ 4 * dk * dv per head per row."""
+    C = 2 * nk * dk + nv * dv
+    g = _g(5)
+    qkv = torch.randn(lanes * tokens, C, device="cuda", generator=g).to(torch.bfloat16)
+    ab = torch.randn(lanes * tokens, 2 * nv, device="cuda", generator=g).to(torch.bfloat16)
+    a_log = torch.log(torch.rand(nv, device="cuda", generator=g) * 15 + 1)
+    dtb = torch.rand(nv, device="cuda", generator=g)
+    rs = torch.randn(lanes, nv, dk, dv, device="cuda", generator=g) * 0.1
+    i32 = dict(dtype=torch.int32, device="cuda")
+    seg = torch.arange(lanes, **i32)
+    cu = torch.arange(0, lanes * tokens + 1, tokens, **i32)
+    ms = _time(lambda: ops.gated_delta_varlen(qkv, ab, a_log, dtb, rs, seg, cu, nk, nv, dk, dv), iters)
+    bytes_ = 2 * rs.numel() * 4 + qkv.numel() * 2 + lanes * tokens * nv * dv * 2
+    flops = 4 * lanes * tokens * nv * dk * dv
+    return _report(f"deltanet_T{tokens}_B{lanes}", ms, bytes_, flops, pk)
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="all",
+                    choices=["moe", "gemm", "attn_prefill", "attn_decode", "deltanet", "all"])
+    ap.add_argument("--tokens", type=int, default=None)
+    ap.add_argument("--ctx", type=int, default=None)
+    ap.add_argument("--lanes", type=int, default=None)
+    ap.add_argument("--iters", type=int, default=20)
+    a = ap.parse_args(argv)
+    if not torch.cuda.is_available():
+        raise SystemExit("kbench needs a CUDA device")
+    pk = peaks()
+    run = []
+    if a.case in ("moe", "all"):
+        for t in ([a.tokens] if a.tokens else [32, 800, 2048]):
+            run.append(case_moe(t, a.iters, pk))
+    if a.case in ("gemm", "all"):
+        for t in ([a.tokens] if a.tokens else [32, 2048]):
+            run.append(case_gemm(t, a.iters, pk))
+    if a.case in ("attn_prefill", "all"):
+        run.append(case_attn_prefill(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.iters, pk))
+    if a.case in ("attn_decode", "all"):
+        run.append(case_attn_decode(a.lanes or 32, a.ctx or 6000, a.iters, pk))
+    if a.case in ("deltanet", "all"):
+        run.append(case_deltanet(a.tokens or 1, a.lanes or 32, a.iters, pk))
+        if a.case == "all":
+            run.append(case_deltanet(800, 1, a.iters, pk))
+    return run
+
+
+if __name__ == "__main__":
+    main()

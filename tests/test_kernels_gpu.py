@@ -336,7 +336,36 @@ def test_flash_attention_prefill(nq, nkv, hd):
         starts.append(st)
         cu.append(cu[-1] + n)
     i32 = dict(dtype=torch.int32, device=DEV)
-    assert ops.prefill_shaped(q, kc, cu, bs)
+    assert ops.fa_plan(q, kc, cu, bs, max(ctx)) is not None
+    out = ops.attention_varlen(q, kc, vc, table, torch.tensor(lanes, **i32), torch.tensor(cu, **i32),
+                               torch.tensor(starts, **i32), bs, lanes, cu, starts, None,
+                               positions=torch.tensor(pos, **i32), max_ctx=max(ctx))
+    torch.cuda.synchronize()
+    exp = ops.attention_varlen(q.cpu(), kc.cpu(), vc.cpu(), table.cpu(), torch.tensor(lanes), torch.tensor(cu),
+                               torch.tensor(starts), bs, lanes, cu, starts, table.cpu().tolist())
+    close(out.cpu(), exp, atol=2e-2)
+    status_ok()
+
+
+@pytest.mark.parametrize("nq,nkv,hd", [(32, 2, 256), (8, 2, 64), (16, 1, 128)])
+def test_flash_attention_decode_splits(nq, nkv, hd):
+    """Decode-shaped batches through the tcgen05 kernel with key-range splits: one-row lanes with
+    short and long contexts (some splits get no keys) and a 4-row verify-style segment."""
+    bs = 16
+    ctx = [1, 20, 700, 3000, 64]
+    kc, vc, table, mb = _paged([c + 4 for c in ctx], nkv, hd, bs, seed=hd + 7)
+    segs = [(0, 0, 1), (1, 19, 1), (2, 699, 1), (3, 2996, 4), (4, 63, 1)]  # (lane, start, rows)
+    T = sum(s[2] for s in segs)
+    q = rnd(T, nq, hd, seed=11 + hd)
+    pos, lanes, cu, starts = [], [], [0], []
+    for lane, st, n in segs:
+        pos += list(range(st, st + n))
+        lanes.append(lane)
+        starts.append(st)
+        cu.append(cu[-1] + n)
+    i32 = dict(dtype=torch.int32, device=DEV)
+    plan = ops.fa_plan(q, kc, cu, bs, max(ctx))
+    assert plan is not None and plan[1] > 1
     out = ops.attention_varlen(q, kc, vc, table, torch.tensor(lanes, **i32), torch.tensor(cu, **i32),
                                torch.tensor(starts, **i32), bs, lanes, cu, starts, None,
                                positions=torch.tensor(pos, **i32), max_ctx=max(ctx))
