@@ -289,6 +289,51 @@ Tensor moe_routed_bf16(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor w2
   return moe_routed_impl(h, topw, topi, w13, c10::nullopt, w2, c10::nullopt, first, count);
 }
 
+// Block-scaled path: weights' e8m0 scales pre-arranged in 512-byte chunks (s13c / s2c).
+Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
+                     int64_t first, int64_t count) {
+  CHECK_BF16(h);
+  TORCH_CHECK(h.is_contiguous(), "moe: h contiguous");
+  const int T = h.size(0), H = h.size(1), k = topi.size(1);
+  const int n13 = w13.size(1), I = n13 / 2;
+  const int cap = T * k;
+  auto i32 = h.options().dtype(at::kInt);
+  Tensor out = at::empty_like(h);
+  if (T == 0) return out;
+  Tensor meta = at::empty({2 * count + 3 * cap + 1 + count + 1}, i32);
+  int* counts = meta.data_ptr<int>();
+  int* offsets = counts + count;
+  int* perm_tok = offsets + count;
+  int* perm_slot = perm_tok + cap;
+  int* inv = perm_slot + cap;
+  int* n_assign = inv + cap;
+  int* tstart = n_assign + 1;
+  Tensor topi_c = topi.contiguous();
+  LAUNCH(qb::moe_dispatch(topi_c.data_ptr<int>(), T, k, first, count, counts, offsets, perm_tok, perm_slot, inv,
+                          n_assign, stream()));
+  const int BN = qb::mx_token_tile(cap, count);
+  LAUNCH(qb::mx_tile_prefix(counts, count, BN, tstart, stream()));
+  const long tiles = count + (cap + BN - 1) / BN;
+  const int KM = H > I ? H : I;
+  auto u8 = h.options().dtype(at::kByte);
+  Tensor hi = at::empty({(long)cap * KM}, u8), lo = at::empty({(long)cap * KM}, u8);
+  Tensor sfh = at::empty({tiles * (KM / 128) * 512}, u8), sfl = at::empty({tiles * (KM / 128) * 512}, u8);
+  Tensor inter = at::empty({cap, I}, h.options());
+  Tensor y2 = at::empty({cap, H}, h.options());
+  uint8_t *hp = hi.data_ptr<uint8_t>(), *lp = lo.data_ptr<uint8_t>();
+  uint8_t *shp = sfh.data_ptr<uint8_t>(), *slp = sfl.data_ptr<uint8_t>();
+  LAUNCH(qb::mx_quant(h.data_ptr(), perm_tok, n_assign, cap, H, offsets, counts, tstart, count, BN, hp, lp, shp, slp,
+                      stream()));
+  LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w13.data_ptr<uint8_t>(), s13c.data_ptr<uint8_t>(), n13, H, offsets,
+                         counts, tstart, count, BN, 1, inter.data_ptr(), I, err_ptr(h), stream()));
+  LAUNCH(qb::mx_quant(inter.data_ptr(), nullptr, n_assign, cap, I, offsets, counts, tstart, count, BN, hp, lp, shp,
+                      slp, stream()));
+  LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w2.data_ptr<uint8_t>(), s2c.data_ptr<uint8_t>(), H, I, offsets,
+                         counts, tstart, count, BN, 0, y2.data_ptr(), H, err_ptr(h), stream()));
+  LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream()));
+  return out;
+}
+
 Tensor moe_routed_fp4(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13, Tensor w2, Tensor s2, int64_t first,
                       int64_t count) {
   return moe_routed_impl(h, topw, topi, w13, s13, w2, s2, first, count);
@@ -358,6 +403,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_kv_write", &qk_norm_rope_kv_write);
   m.def("attention_varlen", &attention_varlen);
   m.def("attention_fa", &attention_fa);
+  m.def("moe_routed_mx", &moe_routed_mx);
   m.def("causal_conv_varlen", &causal_conv_varlen);
   m.def("gated_delta_varlen", &gated_delta_varlen);
   m.def("moe_routed_fp4", &moe_routed_fp4);

@@ -42,6 +42,15 @@ int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab,
 int attention_varlen(const void* q, const void* kc, const void* vc, const int* table, int max_blocks,
                      const int* pos, const int* seg_lane, const int* cu, int S, int T, int nq, int nkv, int hd,
                      int block_size, int splits, float* ws, void* out, cudaStream_t s);
+// block-scaled MoE (moe_mx.cu): token tile width, tile prefix, activation split, expert GEMM
+int mx_token_tile(int cap, int count);
+int mx_tile_prefix(const int* counts, int count, int BN, int* tstart, cudaStream_t s);
+int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, const int* offsets, const int* counts,
+             const int* tstart, int count, int BN, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi, uint8_t* sf_lo,
+             cudaStream_t s);
+int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, const uint8_t* sf_lo, int cap,
+                const uint8_t* wq, const uint8_t* sfa, int n_rows, int K, const int* offsets, const int* counts,
+                const int* tstart, int count, int BN, int act, void* out, int out_cols, int* err, cudaStream_t s);
 // tcgen05 flash attention (attention.cu); tiles = [n_tiles][segment, row0, rows]; splits > 1 splits
 // every tile's key range (partials in ws, merged by a second kernel)
 int fa_prefill(const void* q, const void* kc, const void* vc, long cache_rows, const int* table, int max_blocks,

@@ -1,0 +1,517 @@
+// Routed MXFP4 experts on the block-scaled tensor-core MMA (tcgen05.mma kind::mxf8f6f4).
+//
+// Weights: the packed e2m1 codes go from HBM to shared memory by TMA with the 16U4_ALIGN16B data
+// type, which places every 16 codes in a 16-byte slot (the operand layout the MMA reads for 4-bit
+// types), under the 128-byte swizzle. Their e8m0 block scales (one per 32 K) are applied by the
+// MMA itself from tensor memory. No weight is decoded by any thread and none reaches HBM in a
+// wider type.
+//
+// Activations: every bf16 activation x is written as two e4m3 terms with per-32 e8m0 scales,
+//   x = 2^E * hi + 2^(E-4) * lo,   E = floor(log2(block max)) - 7,
+// hi = x / 2^E truncated to e4m3, lo = the remainder * 16 truncated to e4m3. A bf16 value has 8
+// significant bits; hi takes the top 4 and lo the next 4, so the split is exact for every element
+// within 2^14 of its block maximum (smaller ones keep an error below 2^-20 of the block maximum).
+// e2m1 x e4m3 products are exact, so the two MMAs per K-block (hi then lo, same fp32 accumulator)
+// reproduce the bf16 reference's products, as the f16 path does.
+//
+// Scale factors in tensor memory: for 128 rows and 4 consecutive K-blocks, one 512-byte chunk
+// (32 lines of 16 bytes; line r holds the 4 scales of rows r, r+32, r+64, r+96) is copied by
+// tcgen05.cp .32x128b.warpx4 into 4 columns of all four lane quarters; the MMA of K-block j of
+// the chunk selects byte j (bits 30-31 of the scale address and the sf-id fields of the
+// instruction descriptor). Weight chunks are arranged once at load time; activation chunks are
+// written by the quantisation kernel per token tile.
+//
+// Kernel roles (256 threads, one CTA per SM, persistent over work units = (token tile, 128-row
+// weight tile), weight tile fastest):
+//   warp 0      TMA producer: fp4 tile (128 rows x 128 K), hi/lo token tiles, three scale chunks
+//   warp 1      TMEM allocator + MMA issuer (tcgen05.cp of the chunks, then 8 MMAs per stage)
+//   warps 4..7  epilogue (TMEM lane quarters 0..3): SiLU(gate) * up or plain, bf16 out
+//
+// Reference behaviour: `prefill_moe.py` (grouped expert GEMM over expert-sorted rows),
+// `mxfp4_gemv.py` (MXFP4 layout: low nibble = even K, e8m0 per 32), `moe_hip.hip`.
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qb {
+
+using bf16 = __nv_bfloat16;
+
+constexpr int MX_THREADS = 256;
+constexpr int MX_SK = 128;            // K per stage: one 128-byte swizzle atom of each operand
+constexpr int MX_CHUNK = 512;         // bytes of one scale chunk (128 rows x 4 K-blocks)
+constexpr int MX_MAX_EXPERTS = 1024;
+
+template <int BN>
+struct MxCfg {
+  static constexpr int A = 128 * MX_SK;          // fp4 tile, one byte per code in shared memory
+  static constexpr int B = BN * MX_SK;           // one e4m3 token tile (hi or lo)
+  static constexpr int STAGE = A + 2 * B;        // multiple of 1024
+  static constexpr int SF = 3 * MX_CHUNK;        // weight, hi and lo scale chunks per stage
+  static constexpr int STAGING = BN * 128 * 2;   // one output tile (bf16)
+  static constexpr int PREFIX = (4 * (MX_MAX_EXPERTS + 1) + 15) / 16 * 16;  // keeps the mbarriers after it 8-byte aligned
+  static constexpr int BUDGET = 210 * 1024 - STAGING - PREFIX;
+  static constexpr int STAGES = BUDGET / (STAGE + SF) > 12 ? 12 : BUDGET / (STAGE + SF);
+  static constexpr int SMEM = 1024 + STAGES * STAGE + STAGES * SF + STAGING + PREFIX + 1024;
+  static constexpr int SF_COL = 2 * BN;          // TMEM: accumulators [0, 2 BN), then 12 columns per stage
+  static constexpr int TMEM_COLS = 512;
+  static_assert(SF_COL + 12 * STAGES <= TMEM_COLS, "tensor memory overflow");
+  static_assert((STAGES * (STAGE + SF) + STAGING + PREFIX) % 16 == 0, "mbarriers must stay aligned");
+};
+
+struct MxArgs {
+  const uint8_t* sfa;      // weight scale chunks [E][n_tiles][K/128][512]
+  const uint8_t* sfb_hi;   // activation scale chunks [tiles][K/128][512]
+  const uint8_t* sfb_lo;
+  const int* offsets;
+  const int* counts;
+  const int* tstart;       // [count + 1] first token tile of every expert
+  void* out;
+  int out_cols;
+  int n_rows;
+  int K;
+  int count;
+  int act;
+  int* err;
+};
+
+// e8m0 x e2m1 (A) x e4m3 (B), fp32 accumulate, M = 128, N = n, K-major operands.
+__host__ __device__ constexpr uint32_t idesc_mxf8f6f4(int n) {
+  return (5u << 7) | (0u << 10) | ((uint32_t)(n >> 3) << 17) | (1u << 23) | ((uint32_t)(128 >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_mx(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa,
+                                       uint32_t sfb, bool acc) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+      " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}\n" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"((uint32_t)acc), "r"(sfa), "r"(sfb));
+}
+
+// 512 contiguous bytes (32 rows of 16 bytes) -> 4 columns x 32 lanes, repeated in all 4 lane quarters.
+__device__ __forceinline__ void tmem_cp_chunk(uint32_t taddr, uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)(128 >> 4) << 16;  // leading byte offset (one 16-byte column: unused)
+  d |= (uint64_t)(128 >> 4) << 32;  // stride byte offset: 8 rows x 16 bytes
+  d |= (uint64_t)1 << 46;           // descriptor version
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(d) : "memory");
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+template <int BN>
+__device__ __forceinline__ int mx_cols(int rest) {
+  const int n = (rest + 15) & ~15;
+  return n < BN ? n : BN;
+}
+
+template <int BN>
+__global__ void __launch_bounds__(MX_THREADS, 1)
+    moe_mx_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmH,
+                  const __grid_constant__ CUtensorMap tmL, MxArgs a) {
+  using C = MxCfg<BN>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* stages = smem;
+  uint8_t* sfs = smem + C::STAGES * C::STAGE;                    // [STAGES][3][512]
+  uint16_t* staging = reinterpret_cast<uint16_t*>(sfs + C::STAGES * C::SF);
+  int* tstart = reinterpret_cast<int*>(reinterpret_cast<uint8_t*>(staging) + C::STAGING);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(tstart) + C::PREFIX);
+  uint64_t* full = bars;
+  uint64_t* empty = full + C::STAGES;
+  uint64_t* acc_full = empty + C::STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* drain = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drain + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* issued_p = const_cast<int*>(abort_flag) + 1;
+
+  const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
+  const int n_tiles = a.n_rows / 128;
+  const int kstages = a.K / MX_SK;
+  const bool gu = a.act == 1;
+
+  for (int i = threadIdx.x; i <= a.count; i += blockDim.x) tstart[i] = a.tstart[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    *issued_p = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tmW);
+    prefetch_tmap(&tmH);
+    prefetch_tmap(&tmL);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const int units = tstart[a.count] * n_tiles;
+  auto unit = [&](int u, int& e, int& nt, int& tt) {
+    tt = u / n_tiles;
+    nt = u % n_tiles;
+    int lo = 0, hi = a.count - 1;  // last expert whose first tile is <= tt
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tstart[mid] <= tt) lo = mid; else hi = mid - 1;
+    }
+    e = lo;
+  };
+  auto wrow = [&](int nt, int r) -> int {
+    return gu ? (r < 64 ? nt * 64 + r : a.n_rows / 2 + nt * 64 + (r - 64)) : nt * 128 + r;
+  };
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    if (elect_one()) {
+      int it = 0;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        int e, nt, tt;
+        unit(u, e, nt, tt);
+        const int m0 = (tt - tstart[e]) * BN;
+        const int ne = mx_cols<BN>(a.counts[e] - m0);
+        const int row_b = a.offsets[e] + m0;
+        const long erow = (long)e * a.n_rows;
+        const uint8_t* sfa_u = a.sfa + ((long)e * n_tiles + nt) * kstages * MX_CHUNK;
+        const uint8_t* sfh_u = a.sfb_hi + (long)tt * kstages * MX_CHUNK;
+        const uint8_t* sfl_u = a.sfb_lo + (long)tt * kstages * MX_CHUNK;
+        for (int ks = 0; ks < kstages; ++ks, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) goto prod_done;
+          uint8_t* st = stages + s * C::STAGE;
+          uint8_t* sf = sfs + s * C::SF;
+          // the fp4 tile counts its global (packed) bytes: half of its shared-memory footprint
+          mbar_expect_tx(&full[s], C::A / 2 + 2 * ne * MX_SK + 3 * MX_CHUNK);
+          tma_load_2d(st, &tmW, &full[s], ks * MX_SK, (int)(erow + wrow(nt, 0)));
+          tma_load_2d(st + 64 * MX_SK, &tmW, &full[s], ks * MX_SK, (int)(erow + wrow(nt, 64)));
+          for (int t = 0; t < ne; t += 16) {
+            tma_load_2d(st + C::A + t * MX_SK, &tmH, &full[s], ks * MX_SK, row_b + t);
+            tma_load_2d(st + C::A + C::B + t * MX_SK, &tmL, &full[s], ks * MX_SK, row_b + t);
+          }
+          bulk_g2s(sf, sfa_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
+          bulk_g2s(sf + MX_CHUNK, sfh_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
+          bulk_g2s(sf + 2 * MX_CHUNK, sfl_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
+          *issued_p = it + 1;
+        }
+      }
+    prod_done:;
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (elect_one()) {
+      int it = 0, ti = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < units && ok && !*abort_flag; u += gridDim.x, ++ti) {
+        int e, nt, tt;
+        unit(u, e, nt, tt);
+        const int m0 = (tt - tstart[e]) * BN;
+        const uint32_t idesc = idesc_mxf8f6f4(mx_cols<BN>(a.counts[e] - m0));
+        const int acc = ti & 1;
+        if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * BN;
+        for (int ks = 0; ks < kstages; ++ks, ++it) {
+          const int s = it % C::STAGES;
+          if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sf_t = tmem + C::SF_COL + s * 12;
+          const uint32_t sf_s = smem_u32(sfs + s * C::SF);
+          tmem_cp_chunk(sf_t, sf_s);
+          tmem_cp_chunk(sf_t + 4, sf_s + MX_CHUNK);
+          tmem_cp_chunk(sf_t + 8, sf_s + 2 * MX_CHUNK);
+          const uint32_t sbase = smem_u32(stages + s * C::STAGE);
+          const uint64_t da = desc_sw128(sbase), dh = desc_sw128(sbase + C::A), dl = desc_sw128(sbase + C::A + C::B);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // K-block j of the stage: 32 codes = 32 shared-memory bytes
+            const uint32_t id_j = idesc | ((uint32_t)j << 29) | ((uint32_t)j << 4);
+            const uint32_t bsel = (uint32_t)j << 30;
+            mma_mx(d, da + 2 * j, dh + 2 * j, id_j, (sf_t) | bsel, (sf_t + 4) | bsel, (ks | j) != 0);
+            mma_mx(d, da + 2 * j, dl + 2 * j, id_j, (sf_t) | bsel, (sf_t + 8) | bsel, true);
+          }
+          mma_commit(&empty[s]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[acc]);
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err, ERR_DRAIN, nullptr);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- epilogue
+    const int ew = warp & 3;
+    const int row = ew * 32 + lane;
+    const int et = threadIdx.x - 128;
+    int ti = 0;
+    for (int u = blockIdx.x; u < units; u += gridDim.x, ++ti) {
+      int e, nt, tt;
+      unit(u, e, nt, tt);
+      const int m0 = (tt - tstart[e]) * BN;
+      const int cnt = a.counts[e];
+      const int row_b = a.offsets[e] + m0;
+      const int acc = ti & 1;
+      if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) break;
+      tc_fence_after();
+      const int ne = mx_cols<BN>(cnt - m0);
+      for (int c0 = 0; c0 < ne; c0 += 16) {
+        float v[16];
+        tmem_ld16(tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16), v);
+#pragma unroll
+        for (int j = 0; j < 16; ++j) {
+          bf16 o = __float2bfloat16(v[j]);
+          staging[(c0 + j) * 128 + row] = *reinterpret_cast<uint16_t*>(&o);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&acc_empty[acc]);
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      const int nvalid = min(ne, cnt - m0);
+      bf16* Y = reinterpret_cast<bf16*>(a.out);
+      if (gu) {
+        for (int idx = et; idx < nvalid * 64; idx += 128) {
+          const int j = idx / 64, r = idx % 64;
+          uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
+          const float g = __bfloat162float(*reinterpret_cast<bf16*>(&gb));
+          const float uu = __bfloat162float(*reinterpret_cast<bf16*>(&ub));
+          const float sg = __bfloat162float(__float2bfloat16(g / (1.f + expf(-g))));
+          Y[(long)(row_b + j) * a.out_cols + nt * 64 + r] = __float2bfloat16(sg * uu);
+        }
+      } else {
+        for (int idx = et; idx < nvalid * 16; idx += 128) {
+          const int j = idx / 16, q = idx % 16;
+          const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
+          *reinterpret_cast<uint4*>(Y + (long)(row_b + j) * a.out_cols + nt * 128 + q * 8) = val;
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    }
+  }
+
+  __syncthreads();
+  if (*abort_flag && threadIdx.x == 0) {
+    const int n = *issued_p;
+    for (int i = n - C::STAGES < 0 ? 0 : n - C::STAGES; i < n; ++i)
+      mbar_wait(&full[i % C::STAGES], (i / C::STAGES) & 1, a.err, ERR_DRAIN, nullptr);
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// ------------------------------------------------------------------ activation split
+// |v| (< 256) -> (e4m3 code, its value) truncated toward zero.
+__device__ __forceinline__ uint32_t e4m3_trunc(float av, float& val) {
+  const uint32_t b = __float_as_uint(av);
+  if (b >= 0x3C800000u) {  // >= 2^-6: normal e4m3, keep 3 mantissa bits
+    val = __uint_as_float(b & 0xFFF00000u);
+    return ((((b >> 23) & 0xFF) - 127 + 7) << 3) | ((b >> 20) & 7);
+  }
+  const uint32_t m = (uint32_t)(av * 512.f);  // subnormal: m x 2^-9, m < 8
+  val = (float)m * (1.f / 512.f);
+  return m;
+}
+
+// One warp per row: rows `a < *n_rows` of x (row a read from x[perm[a]] when perm is given) ->
+// hi / lo e4m3 bytes [cap, K] and their scales, written straight into the per-tile chunks (the
+// token tile of row a is the tile of its expert's run; tiles of BN rows). Each lane holds 8
+// consecutive elements, so 4 lanes form one 32-element block.
+__global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_rows, int K, const int* offsets,
+                                const int* tstart, int count, int BN, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi,
+                                uint8_t* sf_lo) {
+  const int lane = threadIdx.x % 32;
+  const int a = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (a >= *n_rows) return;
+  // expert of assignment row a: the last expert whose first row is <= a (an empty expert shares
+  // its offset with the next one, so the last such expert is never empty); then its token tile
+  int lo_e = 0, hi_e = count - 1;
+  while (lo_e < hi_e) {
+    const int mid = (lo_e + hi_e + 1) >> 1;
+    if (offsets[mid] <= a) lo_e = mid; else hi_e = mid - 1;
+  }
+  const int r_e = a - offsets[lo_e];
+  const int tt = tstart[lo_e] + r_e / BN, rr = r_e % BN;
+  const bf16* src = x + (long)(perm ? perm[a] : a) * K;
+  uint8_t* hrow = hi + (long)a * K;
+  uint8_t* lrow = lo + (long)a * K;
+  const long sf_row = (long)tt * (K / MX_SK) * MX_CHUNK + (rr % 32) * 16 + (rr / 32) * 4;
+  for (int kbase = 0; kbase < K; kbase += 256) {  // warp-uniform trip count (shuffles below)
+    const int k0 = kbase + lane * 8;
+    const bool valid = k0 < K;                       // K is a multiple of 128, not always of 256
+    const uint4 raw = valid ? *reinterpret_cast<const uint4*>(src + k0) : make_uint4(0, 0, 0, 0);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(p2[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+    uint32_t mb = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(fabsf(v[i])));
+    mb = max(mb, __shfl_xor_sync(0xffffffff, mb, 1));
+    mb = max(mb, __shfl_xor_sync(0xffffffff, mb, 2));  // max over the 4 lanes of the block
+    int E = mb ? (int)(mb >> 23) - 127 - 7 : -127;      // block max / 2^E in [128, 256)
+    if (E < -123) E = -123;                             // lo scale E - 4 stays a valid e8m0
+    const float inv = __uint_as_float((uint32_t)(127 - E) << 23);  // 2^-E, exact
+    uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float xs = fabsf(v[i]) * inv;
+      float hv, lv;
+      const uint32_t ch = e4m3_trunc(xs, hv);
+      const uint32_t cl = e4m3_trunc((xs - hv) * 16.f, lv);
+      const uint32_t sg = v[i] < 0.f ? 0x80u : 0u;
+      hw[i / 4] |= (ch | (ch ? sg : 0u)) << (8 * (i % 4));
+      lw[i / 4] |= (cl | (cl ? sg : 0u)) << (8 * (i % 4));
+    }
+    if (!valid) continue;
+    *reinterpret_cast<uint2*>(hrow + k0) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(lrow + k0) = make_uint2(lw[0], lw[1]);
+    if ((lane & 3) == 0) {
+      const int kb = k0 / 32;
+      const long off = sf_row + (long)(kb / 4) * MX_CHUNK + (kb % 4);
+      sf_hi[off] = (uint8_t)(E + 127);
+      sf_lo[off] = (uint8_t)(E - 4 + 127);
+    }
+  }
+}
+
+// tstart[e] = sum over e' < e of ceil(counts[e'] / BN), tstart[count] = total token tiles.
+__global__ void mx_tile_prefix_kernel(const int* counts, int count, int BN, int* tstart) {
+  const int lane = threadIdx.x;
+  int run = 0;
+  for (int base = 0; base < count; base += 32) {
+    const int e = base + lane;
+    const int t = e < count ? (counts[e] + BN - 1) / BN : 0;
+    int incl = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int v = __shfl_up_sync(0xffffffff, incl, o);
+      if (lane >= o) incl += v;
+    }
+    if (e < count) tstart[e] = run + incl - t;
+    run += __shfl_sync(0xffffffff, incl, 31);
+  }
+  if (lane == 0) tstart[count] = run;
+}
+
+// ------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 mx_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D map [rows][cols] with a (128 elements x box_rows) box and the 128-byte swizzle; fp4 = packed
+// e2m1 codes unpacked to one code per shared-memory byte (16U4_ALIGN16B), else one byte per element.
+static int mx_tmap(CUtensorMap* m, const void* base, long rows, long cols, long row_bytes, int box_rows, bool fp4) {
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)row_bytes};
+  cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = mx_encode()(m, fp4 ? CU_TENSOR_MAP_DATA_TYPE_16U4_ALIGN16B : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                           const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+static int mx_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  }
+  return n;
+}
+
+template <int BN>
+static int mx_launch(const CUtensorMap& tw, const CUtensorMap& th, const CUtensorMap& tl, const MxArgs& a,
+                     cudaStream_t st) {
+  using C = MxCfg<BN>;
+  auto k = moe_mx_kernel<BN>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr = true;
+  }
+  k<<<mx_sms(), MX_THREADS, C::SMEM, st>>>(tw, th, tl, a);
+  return (int)cudaGetLastError();
+}
+
+int mx_token_tile(int cap, int count) {
+  const int avg = (cap + count - 1) / (count > 0 ? count : 1);
+  const int want = 2 * avg + 2;
+  return want <= 16 ? 16 : want <= 32 ? 32 : want <= 64 ? 64 : 128;
+}
+
+int mx_tile_prefix(const int* counts, int count, int BN, int* tstart, cudaStream_t s) {
+  mx_tile_prefix_kernel<<<1, 32, 0, s>>>(counts, count, BN, tstart);
+  return (int)cudaGetLastError();
+}
+
+int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, const int* offsets, const int* counts,
+             const int* tstart, int count, int BN, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi, uint8_t* sf_lo,
+             cudaStream_t s) {
+  if (!cap) return 0;
+  if (K % MX_SK) return -1;
+  (void)counts;
+  mx_quant_kernel<<<(unsigned)((cap + 7) / 8), 256, 0, s>>>((const bf16*)x, perm, n_rows, K, offsets, tstart, count,
+                                                             BN, hi, lo, sf_hi, sf_lo);
+  return (int)cudaGetLastError();
+}
+
+int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, const uint8_t* sf_lo, int cap,
+                const uint8_t* wq, const uint8_t* sfa, int n_rows, int K, const int* offsets, const int* counts,
+                const int* tstart, int count, int BN, int act, void* out, int out_cols, int* err, cudaStream_t s) {
+  if (!cap || !count) return 0;
+  if (n_rows % 128 || K % MX_SK || count > MX_MAX_EXPERTS) return -1;
+  if ((reinterpret_cast<uintptr_t>(wq) & 31) || (reinterpret_cast<uintptr_t>(hi) & 15) ||
+      (reinterpret_cast<uintptr_t>(lo) & 15))
+    return -2;
+  CUtensorMap tw, th, tl;
+  int r = mx_tmap(&tw, wq, (long)count * n_rows, K, K / 2, 64, true);
+  if (r) return 1000 + r;
+  r = mx_tmap(&th, hi, cap, K, K, 16, false);
+  if (r) return 2000 + r;
+  r = mx_tmap(&tl, lo, cap, K, K, 16, false);
+  if (r) return 3000 + r;
+  MxArgs a{sfa, sf_hi, sf_lo, offsets, counts, tstart, out, out_cols, n_rows, K, count, act, err};
+  switch (BN) {
+    case 16: return mx_launch<16>(tw, th, tl, a, s);
+    case 32: return mx_launch<32>(tw, th, tl, a, s);
+    case 64: return mx_launch<64>(tw, th, tl, a, s);
+    default: return mx_launch<128>(tw, th, tl, a, s);
+  }
+}
+
+}  // namespace qb

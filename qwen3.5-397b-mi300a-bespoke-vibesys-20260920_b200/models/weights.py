@@ -123,6 +123,17 @@ def load_moe_dense(r: _Rd, cfg: Qwen35Config, p: Plan) -> dict:
     }
 
 
+def _device_experts(ex: dict) -> dict:
+    """On a CUDA device with the block-scaled MoE path, re-lay the e8m0 scales once into the
+    chunk layout its MMA reads (same bytes, permuted); the row-major copy is dropped."""
+    from ..ops import core as ops
+
+    if ex["w13"].is_cuda and ops.moe_impl() == "mx" and ex["w13"].shape[2] * 2 % 128 == 0 \
+            and ex["w2"].shape[2] * 2 % 128 == 0:
+        ops.prepare_experts(ex)
+    return ex
+
+
 def load_experts(r: _Rd, p: Plan, threads: int = 16) -> dict:
     """Stack this rank's experts. MXFP4 experts stay packed (codes + scales, uint8); bf16
     experts (the MTP layer of the published checkpoint) are stacked as bf16."""
@@ -143,12 +154,12 @@ def load_experts(r: _Rd, p: Plan, threads: int = 16) -> dict:
     with ThreadPoolExecutor(threads) as ex:
         parts = list(ex.map(one, range(first, first + n)))
     if quant:
-        return {
+        return _device_experts({
             "w13": torch.stack([x[0] for x in parts]).to(r.device),
             "s13": torch.stack([x[1] for x in parts]).to(r.device),
             "w2": torch.stack([x[2] for x in parts]).to(r.device),
             "s2": torch.stack([x[3] for x in parts]).to(r.device),
-        }
+        })
     return {
         "w13": torch.stack([x[0] for x in parts]).to(r.device, r.dtype),
         "w2": torch.stack([x[1] for x in parts]).to(r.device, r.dtype),
@@ -245,12 +256,12 @@ def random_layer(kind: str, cfg: Qwen35Config, p: Plan, gen, device, dtype, expe
         }
         return d
     u8 = dict(dtype=torch.uint8, device=device)
-    d["experts"] = {
+    d["experts"] = _device_experts({
         "w13": torch.randint(0, 256, (ne, 2 * inter, h // 2), generator=gen, **u8),
         "s13": torch.full((ne, 2 * inter, h // 32), 120, **u8),
         "w2": torch.randint(0, 256, (ne, h, inter // 2), generator=gen, **u8),
         "s2": torch.full((ne, h, inter // 32), 120, **u8),
-    }
+    })
     return d
 
 

@@ -236,10 +236,50 @@ def router_topk(logits, k):
     return w.float(), i.int()
 
 
+def mx_scale_chunks(s: torch.Tensor, gate_up: bool) -> torch.Tensor:
+    """Weight e8m0 scales [E, rows, K/32] -> the tensor-memory chunk layout of the block-scaled
+    MMA: [E, rows/128, K/128, 512] bytes, one 512-byte chunk per (128-row weight tile, 4 K-blocks),
+    line r (16 bytes) = the 4 scales of tile rows r, r+32, r+64, r+96. For gate_up a tile's rows
+    are 64 gate rows followed by the matching 64 up rows (the epilogue pairs them)."""
+    E, rows, kb = s.shape
+    nt = rows // 128
+    if gate_up:
+        half = rows // 2
+        t = torch.arange(nt, device=s.device)[:, None]
+        r = torch.arange(128, device=s.device)[None, :]
+        order = torch.where(r < 64, t * 64 + r, half + t * 64 + (r - 64)).reshape(-1)
+        s = s[:, order, :]
+    x = s.reshape(E, nt, 4, 32, kb // 4, 4)         # [E, tile, c, r0, k-chunk, j]
+    return x.permute(0, 1, 4, 3, 2, 5).contiguous().reshape(E, nt, kb // 4, 512)
+
+
+def prepare_experts(experts: dict, keep_rows: bool = False) -> dict:
+    """Add the chunked scale layout the block-scaled CUDA path reads (``s13c``/``s2c``); drop the
+    row-major scales unless ``keep_rows`` (the CPU reference and the f16-decode path read them)."""
+    if "s13" in experts and "s13c" not in experts and experts["s13"].is_cuda:
+        experts["s13c"] = mx_scale_chunks(experts["s13"], True)
+        experts["s2c"] = mx_scale_chunks(experts["s2"], False)
+        if not keep_rows:
+            del experts["s13"], experts["s2"]
+    return experts
+
+
+def moe_impl() -> str:
+    """``mx`` (block-scaled MMA, default) or ``f16`` (codes decoded to f16 by the converter warps)."""
+    return os.environ.get("QB_MOE_IMPL", "mx")
+
+
 def moe_routed(h, topw, topi, experts, first, count):
     """Sum of this rank's experts' weighted outputs for each row (zero for rows routed only to
     other ranks' experts). fp32 accumulation, rounded once to ``h.dtype``."""
     if _cuda(h):
+        if "s13c" in experts and (moe_impl() == "mx" or "s13" not in experts):
+            return ext().moe_routed_mx(h, topw, topi, experts["w13"], experts["s13c"], experts["w2"],
+                                       experts["s2c"], first, count)
+        if "s13" in experts and moe_impl() == "mx" and h.shape[1] % 128 == 0 \
+                and experts["w2"].shape[2] * 2 % 128 == 0:
+            prepare_experts(experts, keep_rows=True)
+            return moe_routed(h, topw, topi, experts, first, count)
         if "s13" in experts:
             return ext().moe_routed_fp4(h, topw, topi, experts["w13"], experts["s13"], experts["w2"], experts["s2"],
                                         first, count)

@@ -202,7 +202,11 @@ def test_causal_conv_and_delta_rule():
 
 @pytest.mark.parametrize("T,E,k,H,I", [(3, 32, 4, 256, 128), (40, 64, 8, 512, 256), (5, 512, 10, 4096, 1024),
                                        (300, 64, 4, 1024, 256)])
-def test_moe_routed_mxfp4(T, E, k, H, I):
+@pytest.mark.parametrize("impl", ["mx", "f16"])
+def test_moe_routed_mxfp4(T, E, k, H, I, impl, monkeypatch):
+    """Both CUDA paths (block-scaled MMA with hi/lo e4m3 activations, and f16 decode) against
+    the fp32 dequantised reference."""
+    monkeypatch.setenv("QB_MOE_IMPL", impl)
     torch.manual_seed(T + E)
     h = rnd(T, H, seed=T)
     if E * I * H <= 2 ** 24:
