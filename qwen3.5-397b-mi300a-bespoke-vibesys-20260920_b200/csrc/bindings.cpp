@@ -309,10 +309,9 @@ Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c
   int* n_assign = inv + cap;
   int* tstart = n_assign + 1;
   Tensor topi_c = topi.contiguous();
-  LAUNCH(qb::moe_dispatch(topi_c.data_ptr<int>(), T, k, first, count, counts, offsets, perm_tok, perm_slot, inv,
-                          n_assign, stream()));
   const int BN = qb::mx_token_tile(cap, count);
-  LAUNCH(qb::mx_tile_prefix(counts, count, BN, tstart, stream()));
+  LAUNCH(qb::moe_dispatch(topi_c.data_ptr<int>(), T, k, first, count, counts, offsets, perm_tok, perm_slot, inv,
+                          n_assign, stream(), BN, tstart));
   const long tiles = count + (cap + BN - 1) / BN;
   const int KM = H > I ? H : I;
   auto u8 = h.options().dtype(at::kByte);

@@ -60,7 +60,7 @@ int router_topk(const void* logits, long ld, int T, int E, int k, float* w, int*
 
 // MoE: dispatch metadata + grouped MXFP4 expert GEMMs + combine
 int moe_dispatch(const int* topi, int T, int k, int first, int count, int* counts, int* offsets, int* perm_tok,
-                 int* perm_slot, int* inv, int* n_assign, cudaStream_t s);
+                 int* perm_slot, int* inv, int* n_assign, cudaStream_t s, int tile = 0, int* tstart = nullptr);
 int moe_gather_f16(const void* h, const int* perm_tok, const int* n_assign, int cap, int H, void* xh,
                    cudaStream_t s);
 int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8_t* ws, int n_rows, int k_cols,

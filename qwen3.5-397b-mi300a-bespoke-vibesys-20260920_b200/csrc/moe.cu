@@ -31,7 +31,7 @@ using bf16 = __nv_bfloat16;
 // ------------------------------------------------------------------ dispatch metadata
 // Counting sort of the (token, slot) assignments that hit local experts [first, first+count).
 __global__ void moe_dispatch_kernel(const int* topi, int T, int k, int first, int count, int* counts, int* offsets,
-                                    int* perm_tok, int* perm_slot, int* inv, int* n_assign) {
+                                    int* perm_tok, int* perm_slot, int* inv, int* n_assign, int tile, int* tstart) {
   extern __shared__ int sh[];  // count counters + count cursors
   int* cnt = sh;
   int* cur = sh + count;
@@ -44,14 +44,19 @@ __global__ void moe_dispatch_kernel(const int* topi, int T, int k, int first, in
   }
   __syncthreads();
   if (threadIdx.x == 0) {
-    int run = 0;
+    int run = 0, tiles = 0;
     for (int e = 0; e < count; ++e) {
       cur[e] = run;
       offsets[e] = run;
       counts[e] = cnt[e];
       run += cnt[e];
+      if (tstart) {  // first token tile of every expert (tiles of `tile` rows), for the block-scaled GEMM
+        tstart[e] = tiles;
+        tiles += (cnt[e] + tile - 1) / tile;
+      }
     }
     *n_assign = run;
+    if (tstart) tstart[count] = tiles;
   }
   __syncthreads();
   for (int a = threadIdx.x; a < n; a += blockDim.x) {
@@ -68,9 +73,9 @@ __global__ void moe_dispatch_kernel(const int* topi, int T, int k, int first, in
 }
 
 int moe_dispatch(const int* topi, int T, int k, int first, int count, int* counts, int* offsets, int* perm_tok,
-                 int* perm_slot, int* inv, int* n_assign, cudaStream_t s) {
+                 int* perm_slot, int* inv, int* n_assign, cudaStream_t s, int tile, int* tstart) {
   moe_dispatch_kernel<<<1, 1024, 2 * count * sizeof(int), s>>>(topi, T, k, first, count, counts, offsets, perm_tok,
-                                                                perm_slot, inv, n_assign);
+                                                                perm_slot, inv, n_assign, tile, tstart);
   return (int)cudaGetLastError();
 }
 
@@ -112,7 +117,10 @@ int moe_gather_bf16(const void* h, const int* perm_tok, const int* n_assign, int
 // out[t, :] = sum_j topw[t, j] * y2[inv[t, j], :] over local assignments (fp32, rounded once)
 __global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* topw, int k, int H, bf16* out) {
   const long t = blockIdx.x;
-  for (int i = threadIdx.x * 8; i < H; i += blockDim.x * 8) {
+  // blockIdx.y splits the row so that small batches still spread over the SMs
+  const int per = (H + gridDim.y - 1) / gridDim.y;
+  const int i0 = blockIdx.y * per, i1 = min(H, i0 + per);
+  for (int i = i0 + threadIdx.x * 8; i < i1; i += blockDim.x * 8) {
     float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     for (int j = 0; j < k; ++j) {
       const int a = inv[t * k + j];
@@ -133,7 +141,9 @@ __global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* 
 
 int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s) {
   if (!T) return 0;
-  moe_combine_kernel<<<T, 128, 0, s>>>((const bf16*)y2, inv, topw, k, H, (bf16*)out);
+  int split = 1;  // row chunks of at least 1024 columns (multiples of 8) until ~2 blocks per SM
+  while (T * split < 296 && H / (split * 2) >= 1024 && (H / (split * 2)) % 8 == 0) split *= 2;
+  moe_combine_kernel<<<dim3(T, split), 128, 0, s>>>((const bf16*)y2, inv, topw, k, H, (bf16*)out);
   return (int)cudaGetLastError();
 }
 

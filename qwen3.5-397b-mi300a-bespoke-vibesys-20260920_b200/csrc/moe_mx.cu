@@ -34,6 +34,8 @@
 #include "common.cuh"
 #include "kernels.h"
 
+#include <cstdlib>
+
 namespace qb {
 
 using bf16 = __nv_bfloat16;
@@ -468,10 +470,16 @@ static int mx_launch(const CUtensorMap& tw, const CUtensorMap& th, const CUtenso
   return (int)cudaGetLastError();
 }
 
+// Token-tile width: about 1.5x the mean tokens per expert (routing is uneven), at most 64 so that
+// the pipeline keeps at least 5 stages (QB_MX_BN_MAX overrides the cap). Wider tiles only save
+// re-reads of an expert's weights, which the unit order serves from L2 (an expert's token tiles
+// are scheduled side by side); narrower tiles buy pipeline depth, which HBM streaming needs more.
 int mx_token_tile(int cap, int count) {
+  static const int bn_max = getenv("QB_MX_BN_MAX") ? atoi(getenv("QB_MX_BN_MAX")) : 64;
   const int avg = (cap + count - 1) / (count > 0 ? count : 1);
-  const int want = 2 * avg + 2;
-  return want <= 16 ? 16 : want <= 32 ? 32 : want <= 64 ? 64 : 128;
+  const int want = avg + avg / 2 + 2;
+  const int bn = want <= 16 ? 16 : want <= 32 ? 32 : want <= 64 ? 64 : 128;
+  return bn > bn_max ? (bn_max >= 64 ? 64 : bn_max >= 32 ? 32 : 16) : bn;
 }
 
 int mx_tile_prefix(const int* counts, int count, int BN, int* tstart, cudaStream_t s) {
