@@ -13,11 +13,12 @@ closed-loop client; the other ranks mirror every model call (``parallel.driver``
 3. ``K`` timed scheduler steps, bracketed by a barrier and ``torch.cuda.synchronize()`` on every
    rank; every step is also bracketed by CUDA events on rank 0.
 
-``value`` = p95 TTFT of turns >= 2 whose first token landed in the timed window, device-timed
-(from the start event of the step that admitted the request to the end event of the step that
-produced its first token). ``e2e`` = the same metric on the host clock through the public
-``Scheduler.submit`` API (every step copies its inputs host->device from pinned memory and reads
-the sampled ids back). The weights stream from HBM every step (far larger than L2), so no
+``value`` = p95 TTFT of turns >= 2 whose first token landed in the timed window, device-timed:
+the sum, over the steps from the one that admitted the request to the one that produced its
+first token, of each step's device interval (CUDA event at the step's first input upload to the
+event just before its last result read). ``e2e`` = the same metric on the host clock through the
+public ``Scheduler.submit`` API: it also counts the host's scheduling work between steps (every
+step copies its inputs host->device from pinned memory and reads the sampled ids back). The weights stream from HBM every step (far larger than L2), so no
 extra L2 flush is needed between steps.
 """
 
@@ -210,15 +211,25 @@ def main():
     step_no = [0]
     loop = ClosedLoop(sched, spec, step_index=lambda: step_no[0])
 
+    inner = getattr(model, "model", model)  # the Model under a GraphRunner
+
     def one_step(events=None):
+        """One scheduler step. With ``events``, append the step's device interval: from the
+        event at its first input upload to the event before its last result read (or, for a
+        step that reads nothing back, an event after its last launch); host gaps between steps
+        are outside every interval."""
         if events is not None:
-            s = torch.cuda.Event(enable_timing=True)
-            e = torch.cuda.Event(enable_timing=True)
-            s.record()
+            inner.gpu_marks = []
         sched.step()
         if events is not None:
-            e.record()
-            events.append((s, e))
+            marks = inner.gpu_marks
+            inner.gpu_marks = None
+            end = torch.cuda.Event(enable_timing=True)
+            end.record()
+            first_in = next((ev for tag, ev in marks if tag == "in"), None)
+            last_in = max((i for i, (tag, _) in enumerate(marks) if tag == "in"), default=-1)
+            outs = [ev for i, (tag, ev) in enumerate(marks) if tag == "out" and i > last_in]
+            events.append((first_in, outs[-1] if outs else end) if first_in is not None else None)
         step_no[0] += 1
         loop.pump()
 
@@ -274,8 +285,8 @@ def main():
     for r in loop.records:
         if r.turn >= 1 and r.submit_step >= step0 and 0 <= r.first_step < step1:
             i0, i1 = r.submit_step - step0, r.first_step - step0
-            if device.type == "cuda":
-                ttft_dev.append(events[i0][0].elapsed_time(events[i1][1]))
+            if device.type == "cuda":  # device time of the steps from admission to first token
+                ttft_dev.append(sum(ev[0].elapsed_time(ev[1]) for ev in events[i0:i1 + 1] if ev is not None))
             ttft_host.append((r.t_first - r.t_submit) * 1e3)
     # tokens generated inside the window: every emitted token of every turn, counted by step
     done_now = sum(r.generated for r in loop.records if r.end_step >= 0)

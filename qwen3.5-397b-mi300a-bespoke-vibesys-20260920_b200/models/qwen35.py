@@ -115,6 +115,15 @@ class Model:
         self._vsave: dict = {}  # MTP verify: per DeltaNet layer (conv inputs, ab rows)
         self._h2d = 0  # bytes copied host -> device for step inputs (bench accounting)
         self._d2h = 0  # bytes read back device -> host (sampled ids)
+        self.gpu_marks = None  # list -> CUDA events at each input upload ("in") and result read ("out")
+
+    def _gpu_mark(self, tag: str) -> None:
+        """Stream-ordered event where a step's device work starts (input upload) or ends (the
+        result read): a benchmark sums these intervals as the device time of its steps."""
+        if self.gpu_marks is not None and self.device.type == "cuda":
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.gpu_marks.append((tag, ev))
 
     def io_bytes(self) -> tuple[int, int]:
         return self._h2d, self._d2h
@@ -214,6 +223,7 @@ class Model:
             last.append(cu[-1] - 1)
         if logit_rows is None:
             logit_rows = last
+        self._gpu_mark("in")
         dev = self.device
         i32 = torch.int32
         packed = torch.tensor(pos + rows + lanes + cu + starts, dtype=i32)
@@ -343,6 +353,7 @@ class Model:
         h = self._forward(b)
         logits = self.logits(h)
         am = ops.argmax_rows(logits)[1].view(B, k + 1)
+        self._gpu_mark("out")
         am_h, dr_h = am.tolist(), drafts.tolist()  # the round's one host sync
         self._d2h += 8 * B * (2 * k + 1)
         ns = [mtp.accept(dr_h[i], am_h[i]) for i in range(B)]
@@ -423,7 +434,9 @@ class Model:
 
     def sample_batch(self, logits, temperatures: Sequence[float], generator=None) -> list[int]:
         temps = list(temperatures)
-        out = ops.argmax_rows(logits)[1].tolist() if logits.shape[0] else []
+        am = ops.argmax_rows(logits)[1] if logits.shape[0] else None
+        self._gpu_mark("out")
+        out = am.tolist() if am is not None else []
         self._d2h += 8 * len(out)
         for i, t in enumerate(temps):
             if t and t > 0:

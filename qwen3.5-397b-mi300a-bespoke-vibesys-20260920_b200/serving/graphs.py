@@ -69,6 +69,7 @@ class GraphRunner:
     # ------------------------------------------------------------------ capture
     def _fill(self, bk: _Bucket, lanes, tokens, positions):
         m = self.model
+        m._gpu_mark("in")
         B, n = bk.B, len(lanes)
         pos = list(positions) + [0] * (B - n)
         ln = list(lanes) + [self.pad_lane] * (B - n)
