@@ -193,6 +193,8 @@ def main():
 
     if rank != 0:
         serve_worker(model, channel)
+        if hasattr(channel, "close"):
+            channel.close()
         t = _elapsed_ms(model.bench_marks[0], model.bench_marks[1]) if len(model.bench_marks) >= 2 else 0.0
         gathered = [None] * world
         dist.all_gather_object(gathered, t)
@@ -277,6 +279,8 @@ def main():
     window_ms = _elapsed_ms(ev_start, ev_end)
     if world > 1:
         runner.shutdown()
+        if hasattr(channel, "close"):
+            channel.close()
         gathered = [None] * world
         dist.all_gather_object(gathered, window_ms)
         window_ms = max(gathered)

@@ -14,6 +14,8 @@ Layout: [write_seq u64][read_seq u64 x world][pad to 4 KiB][ring bytes]. ``write
 
 from __future__ import annotations
 
+import atexit
+
 import pickle
 import struct
 import time
@@ -37,6 +39,8 @@ class ShmChannel:
             self.shm = shared_memory.SharedMemory(name=name)
         self.ctr = np.ndarray((1 + world,), dtype=np.uint64, buffer=self.shm.buf[:8 * (1 + world)])
         self.ring = self.shm.buf[HEADER:HEADER + size]
+        self._closed = False
+        atexit.register(self.close)
         self.poll_s = poll_s
         self.timeout_s = timeout_s
         self.owner = create
@@ -97,6 +101,11 @@ class ShmChannel:
                 time.sleep(self.poll_s)
 
     def close(self) -> None:
+        """Release the views, unmap (and unlink, for the creator). Idempotent; also registered
+        with ``atexit``, since unmapping at interpreter teardown with live views fails."""
+        if getattr(self, "_closed", True):
+            return
+        self._closed = True
         del self.ctr
         self.ring.release()
         self.shm.close()
