@@ -43,20 +43,64 @@ __global__ void moe_dispatch_kernel(const int* topi, int T, int k, int first, in
     if (e >= 0 && e < count) atomicAdd(&cnt[e], 1);
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0, tiles = 0;
-    for (int e = 0; e < count; ++e) {
-      cur[e] = run;
-      offsets[e] = run;
-      counts[e] = cnt[e];
-      run += cnt[e];
-      if (tstart) {  // first token tile of every expert (tiles of `tile` rows), for the block-scaled GEMM
-        tstart[e] = tiles;
-        tiles += (cnt[e] + tile - 1) / tile;
+  // exclusive prefix over experts (token rows, and token tiles of `tile` rows): block-wide scan,
+  // one expert per thread per round of blockDim.x experts
+  __shared__ int warp_tot[2][32];
+  __shared__ int carry[2];
+  if (threadIdx.x == 0) carry[0] = carry[1] = 0;
+  const int lane = threadIdx.x % 32, wid = threadIdx.x / 32, nw = blockDim.x / 32;
+  for (int base = 0; base < count; base += blockDim.x) {
+    __syncthreads();
+    const int e = base + threadIdx.x;
+    const int c = e < count ? cnt[e] : 0;
+    const int t = (e < count && tstart) ? (c + tile - 1) / tile : 0;
+    int ic = c, itl = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int vc = __shfl_up_sync(0xffffffff, ic, o), vt = __shfl_up_sync(0xffffffff, itl, o);
+      if (lane >= o) {
+        ic += vc;
+        itl += vt;
       }
     }
-    *n_assign = run;
-    if (tstart) tstart[count] = tiles;
+    if (lane == 31) {
+      warp_tot[0][wid] = ic;
+      warp_tot[1][wid] = itl;
+    }
+    __syncthreads();
+    if (wid == 0) {
+      int wc = lane < nw ? warp_tot[0][lane] : 0, wt = lane < nw ? warp_tot[1][lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int vc = __shfl_up_sync(0xffffffff, wc, o), vt = __shfl_up_sync(0xffffffff, wt, o);
+        if (lane >= o) {
+          wc += vc;
+          wt += vt;
+        }
+      }
+      if (lane < nw) {  // exclusive warp offsets
+        warp_tot[0][lane] = wc - warp_tot[0][lane];
+        warp_tot[1][lane] = wt - warp_tot[1][lane];
+      }
+    }
+    __syncthreads();
+    const int ex_c = carry[0] + warp_tot[0][wid] + ic - c, ex_t = carry[1] + warp_tot[1][wid] + itl - t;
+    if (e < count) {
+      cur[e] = ex_c;
+      offsets[e] = ex_c;
+      counts[e] = c;
+      if (tstart) tstart[e] = ex_t;
+    }
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) {  // running totals for the next round of experts
+      carry[0] = ex_c + c;
+      carry[1] = ex_t + t;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *n_assign = carry[0];
+    if (tstart) tstart[count] = carry[1];
   }
   __syncthreads();
   for (int a = threadIdx.x; a < n; a += blockDim.x) {

@@ -339,12 +339,14 @@ __device__ __forceinline__ uint32_t e4m3_trunc(float av, float& val) {
 // hi / lo e4m3 bytes [cap, K] and their scales, written straight into the per-tile chunks (the
 // token tile of row a is the tile of its expert's run; tiles of BN rows). Each lane holds 8
 // consecutive elements, so 4 lanes form one 32-element block.
-__global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_rows, int K, const int* offsets,
+__global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_rows, int K, int wpr, const int* offsets,
                                 const int* tstart, int count, int BN, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi,
                                 uint8_t* sf_lo) {
   const int lane = threadIdx.x % 32;
-  const int a = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int a = w / wpr, part = w % wpr;  // `wpr` warps share a row when there are few rows
   if (a >= *n_rows) return;
+  const int kseg = K / wpr, kbeg = part * kseg, kend = kbeg + kseg;
   // expert of assignment row a: the last expert whose first row is <= a (an empty expert shares
   // its offset with the next one, so the last such expert is never empty); then its token tile
   int lo_e = 0, hi_e = count - 1;
@@ -358,9 +360,9 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
   uint8_t* hrow = hi + (long)a * K;
   uint8_t* lrow = lo + (long)a * K;
   const long sf_row = (long)tt * (K / MX_SK) * MX_CHUNK + (rr % 32) * 16 + (rr / 32) * 4;
-  for (int kbase = 0; kbase < K; kbase += 256) {  // warp-uniform trip count (shuffles below)
+  for (int kbase = kbeg; kbase < kend; kbase += 256) {  // warp-uniform trip count (shuffles below)
     const int k0 = kbase + lane * 8;
-    const bool valid = k0 < K;                       // K is a multiple of 128, not always of 256
+    const bool valid = k0 < kend;                       // segments are multiples of 128, not always of 256
     const uint4 raw = valid ? *reinterpret_cast<const uint4*>(src + k0) : make_uint4(0, 0, 0, 0);
     const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
     float v[8];
@@ -493,8 +495,12 @@ int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, 
   if (!cap) return 0;
   if (K % MX_SK) return -1;
   (void)counts;
-  mx_quant_kernel<<<(unsigned)((cap + 7) / 8), 256, 0, s>>>((const bf16*)x, perm, n_rows, K, offsets, tstart, count,
-                                                             BN, hi, lo, sf_hi, sf_lo);
+  // warps per row: enough warps in flight for small batches (at least 256 elements per warp)
+  int wpr = 1;
+  while ((long)cap * wpr < 2048 && (K / (wpr * 2)) % 256 == 0) wpr *= 2;
+  const long warps = (long)cap * wpr;
+  mx_quant_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const bf16*)x, perm, n_rows, K, wpr, offsets, tstart,
+                                                               count, BN, hi, lo, sf_hi, sf_lo);
   return (int)cudaGetLastError();
 }
 
