@@ -57,8 +57,16 @@ Tensor linear(Tensor x, Tensor w, c10::optional<Tensor> out) {
   Tensor y = out.has_value() ? *out : at::empty({T, N}, x.options());
   TORCH_CHECK(y.stride(1) == 1, "linear: output inner dim must be contiguous");
   TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "linear: row strides must be 16B multiples");
+  // split-K workspace when the output has too few tiles to occupy the SMs (decode projections)
+  const long wsf = qb::gemm_split_ws_floats(T, N, K);
+  Tensor ws, cnt;
+  if (wsf) {
+    ws = at::empty({wsf}, x.options().dtype(at::kFloat));
+    cnt = at::zeros({(long)((N + 127) / 128) * ((T + 15) / 16)}, x.options().dtype(at::kInt));
+  }
   LAUNCH(qb::gemm_ws(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(), y.stride(0), T, N, K, bf, 0,
-                     err_ptr(x), stream(), 0));
+                     err_ptr(x), stream(), 0, wsf ? ws.data_ptr<float>() : nullptr,
+                     wsf ? cnt.data_ptr<int>() : nullptr));
   return y;
 }
 
@@ -228,12 +236,31 @@ Tensor gated_delta_varlen(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, T
   TORCH_CHECK(state.stride(3) == 1 && state.stride(2) == dv && state.stride(1) == dk * dv, "delta: state layout");
   const int T = qkv.size(0);
   Tensor out = at::empty({T, nv, dv}, qkv.options());
-  Tensor scratch = at::empty({(long)T * (2 * nk * dk + 2 * nv)}, qkv.options().dtype(at::kFloat));
+  Tensor scratch = at::empty({(long)T * (2 * nk * dk + 4 * nv)}, qkv.options().dtype(at::kFloat));
   LAUNCH(qb::gated_delta_varlen_t(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0),
                                   a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), state.data_ptr<float>(),
                                   state.stride(0), seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), T,
                                   nk, nv, dk, dv, scratch.data_ptr<float>(), out.data_ptr(), commit, stream()));
   g_launches.fetch_add(1, std::memory_order_relaxed);  // prep + recurrence kernels
+  return out;
+}
+
+Tensor gated_delta_chunked(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, Tensor state, Tensor seg_lane,
+                           Tensor chunks, Tensor seg_chunk0, int64_t nk, int64_t nv, int64_t dk, int64_t dv,
+                           bool commit) {
+  CHECK_BF16(qkv);
+  TORCH_CHECK(state.scalar_type() == at::kFloat, "delta: fp32 state");
+  TORCH_CHECK(state.stride(3) == 1 && state.stride(2) == dv && state.stride(1) == dk * dv, "delta: state layout");
+  TORCH_CHECK(chunks.dim() == 2 && chunks.size(1) == 3, "delta: chunks [n, 3]");
+  const int T = qkv.size(0), n_chunks = chunks.size(0);
+  Tensor out = at::empty({T, nv, dv}, qkv.options());
+  Tensor scratch = at::empty({qb::gated_delta_chunked_scratch(T, n_chunks, nk, nv, dk)}, qkv.options().dtype(at::kFloat));
+  LAUNCH(qb::gated_delta_chunked(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0), a_log.data_ptr<float>(),
+                                 dt_bias.data_ptr<float>(), state.data_ptr<float>(), state.stride(0),
+                                 seg_lane.data_ptr<int>(), chunks.data_ptr<int>(), n_chunks,
+                                 seg_chunk0.data_ptr<int>(), seg_lane.size(0), T, nk, nv, dk, dv,
+                                 scratch.data_ptr<float>(), out.data_ptr(), commit, stream()));
+  g_launches.fetch_add(2, std::memory_order_relaxed);  // prep + chunk prep + chunk state kernels
   return out;
 }
 
@@ -403,6 +430,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_varlen", &attention_varlen);
   m.def("attention_fa", &attention_fa);
   m.def("moe_routed_mx", &moe_routed_mx);
+  m.def("gated_delta_chunked", &gated_delta_chunked);
   m.def("causal_conv_varlen", &causal_conv_varlen);
   m.def("gated_delta_varlen", &gated_delta_varlen);
   m.def("moe_routed_fp4", &moe_routed_fp4);

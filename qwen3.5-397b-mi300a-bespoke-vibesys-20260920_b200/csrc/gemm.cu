@@ -11,6 +11,12 @@
 //               transpose through shared memory, 16-byte coalesced stores of Y rows
 // The accumulator is double buffered in TMEM (2 x BN columns), so the epilogue of one tile
 // overlaps the MMAs of the next. All waits are bounded (see common.cuh).
+//
+// Split-K: when the output has too few 128-row tiles to occupy the SMs (decode projections with
+// N = 4096 are 32 tiles), each tile's K range is split over `splits` work units. A unit writes
+// its fp32 partial tile to a workspace and bumps the tile's counter; the unit that arrives last
+// adds the partials and runs the normal epilogue (activation included), then re-arms the
+// counter for the next call.
 #include "common.cuh"
 #include "kernels.h"
 #include <cudaTypedefs.h>
@@ -37,6 +43,9 @@ struct GemmArgs {
   int T, N, K;
   int act;  // 0: none, 1: silu(g)*u over row pairs (g rows [0,64), u rows [64,128) of each tile)
   int* err;
+  int splits;  // K splits per tile (1: none)
+  float* ws;   // [tiles * splits][128][BN] fp32 partials
+  int* cnt;    // [tiles] arrival counters, zero between calls
 };
 
 template <int BN, typename OutT>
@@ -57,12 +66,19 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* issued_p = const_cast<int*>(abort_flag) + 1;
   int* consumed_p = issued_p + 1;
+  volatile int* last_p = consumed_p + 1;
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_tiles = (a.N + 127) / 128;
   const int t_tiles = (a.T + BN - 1) / BN;
-  const int tiles = n_tiles * t_tiles;
+  const int splits = a.splits;
+  const int tiles = n_tiles * t_tiles * splits;  // work units: (tile, K split), splits fastest
   const int kblocks = (a.K + BK - 1) / BK;
+  auto krange = [&](int u, int& k0, int& k1) {
+    const int sp = u % splits;
+    k0 = (int)((long)kblocks * sp / splits);
+    k1 = (int)((long)kblocks * (sp + 1) / splits);
+  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -94,9 +110,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---------------------------------------------------------------- producer
     if (elect_one()) {
       int it = 0;
-      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x) {
+      for (int u = blockIdx.x; u < tiles && !*abort_flag; u += gridDim.x) {
+        const int tile = u / splits;
         const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        int k0, k1;
+        krange(u, k0, k1);
+        for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) break;
           uint8_t* st = stages + s * C::STAGE;
@@ -111,13 +130,15 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---------------------------------------------------------------- MMA issuer
     if (elect_one()) {
       int it = 0, ti = 0;
-      for (int tile = blockIdx.x; tile < tiles && !*abort_flag; tile += gridDim.x, ++ti) {
+      for (int u = blockIdx.x; u < tiles && !*abort_flag; u += gridDim.x, ++ti) {
         const int acc = ti & 1;
         if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
         bool ok = true;
-        for (int kb = 0; kb < kblocks; ++kb, ++it) {
+        int k0, k1;
+        krange(u, k0, k1);
+        for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
             ok = false;
@@ -129,7 +150,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             // +32 bytes per 16-element K step inside the swizzle atom (>>4 in the descriptor)
-            mma_f16_ss(d, da + 2 * kk, db + 2 * kk, idesc, (kb | kk) != 0);
+            mma_f16_ss(d, da + 2 * kk, db + 2 * kk, idesc, (kb != k0) || kk != 0);
           }
           mma_commit(&empty[s]);
           *consumed_p = it + 1;
@@ -147,57 +168,101 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int row = ew * 32 + lane;      // accumulator row = weight row within the tile
     const int et = threadIdx.x - 64;     // 0..127
     OutT* Y = reinterpret_cast<OutT*>(a.y);
+    constexpr int CH = BN < 32 ? BN : 32;
+    // stage one chunk of CH token columns (fp32 values of this thread's weight row) and store it
+    auto emit = [&](int n0, int t0, int c0, const float* v) {
+#pragma unroll
+      for (int j = 0; j < CH; ++j) {  // staging[j][row]: token column j, weight row `row`
+        OutT o = from_f<OutT>(v[j]);
+        staging[j * 128 + row] = *reinterpret_cast<uint16_t*>(&o);
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (a.act == 1) {
+        // silu(gate) * up: rows [0,64) are gate rows, [64,128) the matching up rows;
+        // output columns are n0/2 .. n0/2 + 64
+        for (int idx = et; idx < CH * 64; idx += 128) {
+          const int j = idx / 64, r = idx % 64;
+          const int t = t0 + c0 + j, n = n0 / 2 + r;
+          if (t < a.T && n < a.N / 2) {
+            uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
+            float g = to_f<OutT>(*reinterpret_cast<OutT*>(&gb)), u = to_f<OutT>(*reinterpret_cast<OutT*>(&ub));
+            Y[(long)t * a.ldy + n] = from_f<OutT>(silu(g) * u);
+          }
+        }
+      } else {
+        // 16-byte vectors: each token row of the chunk is 128 outputs = 16 vectors
+        for (int idx = et; idx < CH * 16; idx += 128) {
+          const int j = idx / 16, q = idx % 16;
+          const int t = t0 + c0 + j, n = n0 + q * 8;
+          if (t < a.T) {
+            const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
+            OutT* dst = Y + (long)t * a.ldy + n;
+            if (n + 8 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
+              *reinterpret_cast<uint4*>(dst) = val;
+            } else {
+              const uint16_t* e = reinterpret_cast<const uint16_t*>(&val);
+              for (int u = 0; u < 8 && n + u < a.N; ++u) reinterpret_cast<uint16_t*>(dst)[u] = e[u];
+            }
+          }
+        }
+      }
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+    };
     int ti = 0;
-    for (int tile = blockIdx.x; tile < tiles; tile += gridDim.x, ++ti) {
+    for (int u = blockIdx.x; u < tiles; u += gridDim.x, ++ti) {
+      const int tile = u / splits;
       const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
       const int acc = ti & 1;
       if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) break;
       tc_fence_after();
-      constexpr int CH = BN < 32 ? BN : 32;
+      if (splits == 1) {
+        for (int c0 = 0; c0 < BN; c0 += CH) {
+          float v[32];
+          const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
+          if constexpr (CH == 32) tmem_ld32(taddr, v); else tmem_ld16(taddr, v);
+          emit(n0, t0, c0, v);
+        }
+        tc_fence_before();
+        mbar_arrive(&acc_empty[acc]);
+        continue;
+      }
+      // split-K: this unit's fp32 partial -> workspace; the last unit of the tile adds them up
+      float* part = a.ws + ((long)u * 128 + row) * BN;
       for (int c0 = 0; c0 < BN; c0 += CH) {
         float v[32];
         const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
         if constexpr (CH == 32) tmem_ld32(taddr, v); else tmem_ld16(taddr, v);
-        // staging[j][row]: token column j, weight row `row`
 #pragma unroll
-        for (int j = 0; j < CH; ++j) {
-          OutT o = from_f<OutT>(v[j]);
-          staging[j * 128 + row] = *reinterpret_cast<uint16_t*>(&o);
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (a.act == 1) {
-          // silu(gate) * up: rows [0,64) are gate rows, [64,128) the matching up rows;
-          // output columns are n0/2 .. n0/2 + 64
-          for (int idx = et; idx < CH * 64; idx += 128) {
-            const int j = idx / 64, r = idx % 64;
-            const int t = t0 + c0 + j, n = n0 / 2 + r;
-            if (t < a.T && n < a.N / 2) {
-              uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
-              float g = to_f<OutT>(*reinterpret_cast<OutT*>(&gb)), u = to_f<OutT>(*reinterpret_cast<OutT*>(&ub));
-              Y[(long)t * a.ldy + n] = from_f<OutT>(silu(g) * u);
-            }
-          }
-        } else {
-          // 16-byte vectors: each token row of the chunk is 128 outputs = 16 vectors
-          for (int idx = et; idx < CH * 16; idx += 128) {
-            const int j = idx / 16, q = idx % 16;
-            const int t = t0 + c0 + j, n = n0 + q * 8;
-            if (t < a.T) {
-              const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
-              OutT* dst = Y + (long)t * a.ldy + n;
-              if (n + 8 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
-                *reinterpret_cast<uint4*>(dst) = val;
-              } else {
-                const uint16_t* e = reinterpret_cast<const uint16_t*>(&val);
-                for (int u = 0; u < 8 && n + u < a.N; ++u) reinterpret_cast<uint16_t*>(dst)[u] = e[u];
-              }
-            }
-          }
-        }
-        asm volatile("bar.sync 1, 128;" ::: "memory");
+        for (int j = 0; j < CH; j += 4)
+          *reinterpret_cast<float4*>(part + c0 + j) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
+      __threadfence();
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (et == 0) *last_p = atomicAdd(&a.cnt[tile], 1) == splits - 1;
+      asm volatile("bar.sync 1, 128;" ::: "memory");
+      if (!*last_p) continue;
+      __threadfence();
+      const float* base = a.ws + ((long)tile * splits * 128 + row) * BN;
+      for (int c0 = 0; c0 < BN; c0 += CH) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < CH; ++j) v[j] = 0.f;
+        for (int sp = 0; sp < splits; ++sp) {
+          const float* pp = base + (long)sp * 128 * BN + c0;
+#pragma unroll
+          for (int j = 0; j < CH; j += 4) {
+            const float4 f = __ldcg(reinterpret_cast<const float4*>(pp + j));
+            v[j] += f.x;
+            v[j + 1] += f.y;
+            v[j + 2] += f.z;
+            v[j + 3] += f.w;
+          }
+        }
+        emit(n0, t0, c0, v);
+      }
+      if (et == 0) a.cnt[tile] = 0;  // re-armed for the next call on this stream
     }
   }
 
@@ -262,23 +327,46 @@ static int launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArg
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr = true;
   }
-  const int tiles = ((a.N + 127) / 128) * ((a.T + BN - 1) / BN);
+  const int tiles = ((a.N + 127) / 128) * ((a.T + BN - 1) / BN) * a.splits;
   int grid = tiles < max_ctas ? tiles : max_ctas;
   if (grid < 1) grid = 1;
   k<<<grid, GEMM_THREADS, C::SMEM, st>>>(tw, tx, a, idesc_f16(128, BN, bf16));
   return (int)cudaGetLastError();
 }
 
+static int gemm_bn(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256; }
+
+// K splits for an output of too few tiles to cover the SMs (each split keeps >= 8 K-blocks).
+int gemm_splits(int T, int N, int K) {
+  const int BN = gemm_bn(T);
+  const int tiles = ((N + 127) / 128) * ((T + BN - 1) / BN);
+  const int kblocks = (K + BK - 1) / BK;
+  const int sms = num_sms();
+  if (tiles * 2 > sms || kblocks < 16) return 1;
+  int s = sms / tiles;
+  if (s > kblocks / 8) s = kblocks / 8;
+  if (s > 16) s = 16;
+  return s < 1 ? 1 : s;
+}
+
+long gemm_split_ws_floats(int T, int N, int K) {
+  const int s = gemm_splits(T, N, K);
+  if (s == 1) return 0;
+  const int BN = gemm_bn(T);
+  return (long)((N + 127) / 128) * ((T + BN - 1) / BN) * s * 128 * BN;
+}
+
 int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
-            int act, int* err, cudaStream_t stream, int max_ctas) {
+            int act, int* err, cudaStream_t stream, int max_ctas, float* ws, int* cnt) {
   if (T <= 0 || N <= 0) return 0;
-  int BN = T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256;
+  int BN = gemm_bn(T);
   CUtensorMap tw, tx;
   int r = make_tmap_2d(&tw, w, 2, N, K, ldw, 128, BK, true);
   if (r) return 1000 + r;
   r = make_tmap_2d(&tx, x, 2, T, K, ldx, BN, BK, true);
   if (r) return 2000 + r;
-  GemmArgs a{y, ldy, T, N, K, act, err};
+  const int splits = (ws && cnt) ? gemm_splits(T, N, K) : 1;
+  GemmArgs a{y, ldy, T, N, K, act, err, splits, ws, cnt};
   if (max_ctas <= 0) max_ctas = num_sms();
   switch (BN) {
     case 16: return bf16 ? launch_bn<16, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)

@@ -16,7 +16,10 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, long rows, 
 
 // Y[T,N] = X[T,K] @ W[N,K]^T ; act 1 = silu(gate)*up over 64-row halves of each 128-row tile
 int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
-            int act, int* err, cudaStream_t stream, int max_ctas);
+            int act, int* err, cudaStream_t stream, int max_ctas = 0, float* ws = nullptr, int* cnt = nullptr);
+// split-K workspace (fp32 floats; 0 = no split) and counters (one per 128-row x BN tile)
+long gemm_split_ws_floats(int T, int N, int K);
+int gemm_splits(int T, int N, int K);
 
 int rmsnorm(const void* x, long ldx, const float* w1p, void* out, long ldo, int rows, int H, float eps,
             cudaStream_t s);
@@ -42,6 +45,14 @@ int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab,
 int attention_varlen(const void* q, const void* kc, const void* vc, const int* table, int max_blocks,
                      const int* pos, const int* seg_lane, const int* cu, int S, int T, int nq, int nkv, int hd,
                      int block_size, int splits, float* ws, void* out, cudaStream_t s);
+// chunked gated delta rule (deltanet.cu) and the shared DeltaNet prep kernel (sequence.cu)
+int delta_prep(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log, const float* dt_bias,
+               int T, int nk, int nv, int dk, float* qn, float* kn, float* gb, cudaStream_t s);
+int gated_delta_chunked(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
+                        const float* dt_bias, float* state, long lane_stride, const int* seg_lane,
+                        const int* chunks, int n_chunks, const int* seg_chunk0, int S, int T, int nk, int nv, int dk,
+                        int dv, float* scratch, void* out, bool commit, cudaStream_t s);
+long gated_delta_chunked_scratch(int T, int n_chunks, int nk, int nv, int dk);
 // block-scaled MoE (moe_mx.cu): token tile width, tile prefix, activation split, expert GEMM
 int mx_token_tile(int cap, int count);
 int mx_tile_prefix(const int* counts, int count, int BN, int* tstart, cudaStream_t s);

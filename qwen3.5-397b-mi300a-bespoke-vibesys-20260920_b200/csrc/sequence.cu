@@ -78,7 +78,7 @@ int causal_conv_varlen_t(const void* x, long ldx, void* state, long lane_stride,
 // exp(g) and beta. Recurrence kernel: grid (value head, segment, column block of 32); four
 // threads share one state column (32 rows each), so per token a thread does ~32-wide dot
 // products and two 2-step shuffle reductions. Tokens are staged in shared memory in chunks.
-__global__ void delta_prep_kernel(const bf16* qkv, long ldqkv, const bf16* ab, long ldab, const float* a_log,
+__global__ void __launch_bounds__(256) delta_prep_kernel(const bf16* qkv, long ldqkv, const bf16* ab, long ldab, const float* a_log,
                                   const float* dt_bias, int nk, int nv, int dk, float* qn, float* kn, float* gb) {
   const int t = blockIdx.x;
   const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -101,31 +101,33 @@ __global__ void delta_prep_kernel(const bf16* qkv, long ldqkv, const bf16* ab, l
       dst[i] = isq ? v * scale : v;
     }
   }
-  for (int h = threadIdx.x; h < nv; h += blockDim.x) {
+  for (int h = threadIdx.x; h < nv; h += blockDim.x) {  // per value head: (decay, beta, log decay, 0)
     const float b = __bfloat162float(ab[(long)t * ldab + h]);
     const float a = __bfloat162float(ab[(long)t * ldab + nv + h]);
-    gb[((long)t * nv + h) * 2 + 0] = expf(-expf(a_log[h]) * softplus(a + dt_bias[h]));
-    gb[((long)t * nv + h) * 2 + 1] = rbf2(1.f / (1.f + expf(-b)));
+    const float g = -expf(a_log[h]) * softplus(a + dt_bias[h]);
+    *reinterpret_cast<float4*>(gb + ((long)t * nv + h) * 4) = make_float4(expf(g), rbf2(1.f / (1.f + expf(-b))), g, 0.f);
   }
 }
 
 constexpr int DR_CT = 16;  // tokens staged per chunk
+constexpr int DR_TPC = 4;  // threads per state column
 
 template <int DK>
 __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const float* kn, const float* gb,
                                                         const bf16* qkv, long ldqkv, float* state, long lane_stride,
                                                         const int* seg_lane, const int* cu, int nk, int nv, int dv,
                                                         bf16* out, int commit) {
-  constexpr int PART = DK / 4;        // rows per thread
-  constexpr int PST = PART + 4;       // padded part stride (floats)
-  __shared__ __align__(16) float qs[DR_CT][4 * PST];
-  __shared__ __align__(16) float ks[DR_CT][4 * PST];
-  __shared__ float vs[DR_CT][32];
+  constexpr int COLS = 128 / DR_TPC;  // state columns per CTA
+  constexpr int PART = DK / DR_TPC;   // rows per thread
+  constexpr int PST = PART + 4;       // padded part stride (floats): the 8 parts sit in different banks
+  __shared__ __align__(16) float qs[DR_CT][DR_TPC * PST];
+  __shared__ __align__(16) float ks[DR_CT][DR_TPC * PST];
+  __shared__ float vs[DR_CT][COLS];
   __shared__ float gs[DR_CT][2];
   const int h = blockIdx.x, s = blockIdx.y, cb = blockIdx.z;
   const int tid = threadIdx.x;
-  const int col = tid >> 2, part = tid & 3;
-  const int j = cb * 32 + col;          // state column (value dim)
+  const int col = tid / DR_TPC, part = tid % DR_TPC;
+  const int j = cb * COLS + col;  // state column (value dim)
   const int lane = seg_lane[s];
   const int hk = h / (nv / nk);
   float* st = state + (long)lane * lane_stride + (long)h * DK * dv;
@@ -143,27 +145,31 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
       qs[tt][(i / PART) * PST + i % PART] = qn[base];
       ks[tt][(i / PART) * PST + i % PART] = kn[base];
     }
-    for (int idx = tid; idx < n * 32; idx += blockDim.x) {
-      const int tt = idx / 32, cc = idx % 32;
-      const int jj = cb * 32 + cc;
+    for (int idx = tid; idx < n * COLS; idx += blockDim.x) {
+      const int tt = idx / COLS, cc = idx % COLS;
+      const int jj = cb * COLS + cc;
       vs[tt][cc] = jj < dv ? __bfloat162float(qkv[(long)(c0 + tt) * ldqkv + 2L * nk * DK + (long)h * dv + jj]) : 0.f;
     }
-    for (int idx = tid; idx < n * 2; idx += blockDim.x) gs[idx / 2][idx % 2] = gb[((long)(c0 + idx / 2) * nv + h) * 2 + idx % 2];
+    for (int idx = tid; idx < n * 2; idx += blockDim.x) gs[idx / 2][idx % 2] = gb[((long)(c0 + idx / 2) * nv + h) * 4 + idx % 2];
     __syncthreads();
     for (int tt = 0; tt < n; ++tt) {
       const float* kp = &ks[tt][part * PST];
       const float* qp = &qs[tt][part * PST];
       const float decay = gs[tt][0], beta = gs[tt][1];
-      float kv = 0.f;
+      float kv4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums: short dependency chains
 #pragma unroll
       for (int i = 0; i < PART; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(kp + i);
-        kv += S[i] * k4.x + S[i + 1] * k4.y + S[i + 2] * k4.z + S[i + 3] * k4.w;
+        kv4[0] += S[i] * k4.x;
+        kv4[1] += S[i + 1] * k4.y;
+        kv4[2] += S[i + 2] * k4.z;
+        kv4[3] += S[i + 3] * k4.w;
       }
-      kv += __shfl_xor_sync(0xffffffff, kv, 1);
-      kv += __shfl_xor_sync(0xffffffff, kv, 2);
+      float kv = (kv4[0] + kv4[1]) + (kv4[2] + kv4[3]);
+#pragma unroll
+      for (int o = 1; o < DR_TPC; o <<= 1) kv += __shfl_xor_sync(0xffffffff, kv, o);
       const float delta = (vs[tt][col] - decay * kv) * beta;
-      float o = 0.f;
+      float o4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < PART; i += 4) {
         const float4 k4 = *reinterpret_cast<const float4*>(kp + i);
@@ -172,10 +178,14 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
         S[i + 1] = S[i + 1] * decay + k4.y * delta;
         S[i + 2] = S[i + 2] * decay + k4.z * delta;
         S[i + 3] = S[i + 3] * decay + k4.w * delta;
-        o += S[i] * q4.x + S[i + 1] * q4.y + S[i + 2] * q4.z + S[i + 3] * q4.w;
+        o4[0] += S[i] * q4.x;
+        o4[1] += S[i + 1] * q4.y;
+        o4[2] += S[i + 2] * q4.z;
+        o4[3] += S[i + 3] * q4.w;
       }
-      o += __shfl_xor_sync(0xffffffff, o, 1);
-      o += __shfl_xor_sync(0xffffffff, o, 2);
+      float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
+#pragma unroll
+      for (int of = 1; of < DR_TPC; of <<= 1) o += __shfl_xor_sync(0xffffffff, o, of);
       if (part == 0 && active) out[((long)(c0 + tt) * nv + h) * dv + j] = __float2bfloat16(o);
     }
   }
@@ -185,18 +195,25 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
   }
 }
 
+int delta_prep(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log, const float* dt_bias,
+               int T, int nk, int nv, int dk, float* qn, float* kn, float* gb, cudaStream_t s) {
+  delta_prep_kernel<<<T, 256, 0, s>>>((const bf16*)qkv, ldqkv, (const bf16*)ab, ldab, a_log, dt_bias, nk, nv, dk,
+                                      qn, kn, gb);
+  return (int)cudaGetLastError();
+}
+
 int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
                          const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
                          int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out, bool commit,
                          cudaStream_t s) {
   if (!S || !T) return 0;
-  if (dk % 16 || dk > 128) return -1;
+  if (dk % (4 * DR_TPC) || dk > 128) return -1;
   float* qn = scratch;
   float* kn = qn + (long)T * nk * dk;
   float* gb = kn + (long)T * nk * dk;
   delta_prep_kernel<<<T, 256, 0, s>>>((const bf16*)qkv, ldqkv, (const bf16*)ab, ldab, a_log, dt_bias, nk, nv, dk,
                                       qn, kn, gb);
-  dim3 grid(nv, S, (dv + 31) / 32);
+  dim3 grid(nv, S, (dv + 128 / DR_TPC - 1) / (128 / DR_TPC));
 #define QB_DREC(DKV)                                                                                          \
   delta_rec_kernel<DKV><<<grid, 128, 0, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, state, lane_stride, seg_lane, \
                                              cu, nk, nv, dv, (bf16*)out, commit ? 1 : 0)

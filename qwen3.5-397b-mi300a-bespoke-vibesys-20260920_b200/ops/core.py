@@ -107,6 +107,11 @@ def gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv,
     q/k l2-normalised, ``q *= dk**-0.5``, key heads repeated to value heads. ``rec_state``
     [lanes, nv, dk, dv] fp32 is continued and updated. Returns [T, nv, dv] in ``qkv.dtype``."""
     if _cuda(qkv):
+        plan = dn_chunk_plan(cu_h, dk, dv, qkv.device)
+        if plan is not None:
+            chunks, seg0 = plan
+            return ext().gated_delta_chunked(qkv, ab, a_log, dt_bias, rec_state, seg_lane, chunks, seg0, nk, nv, dk,
+                                             dv, commit)
         return ext().gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv, commit)
     t = qkv.shape[0]
     q = qkv[:, : nk * dk].reshape(t, nk, dk)
@@ -174,6 +179,39 @@ def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, 
                             dtype=torch.long, device=q.device)
         out[a:b] = ref.attention_prefix(q[a:b], k_cache[rows], v_cache[rows], starts[s])
     return out
+
+
+DN_CHUNK = 64
+DN_CHUNK_MIN = 64
+_dn_chunk_cache: dict = {}
+
+
+def dn_chunk_plan(cu_h, dk, dv, device):
+    """(device chunk table [n, 3] = (segment, first row, rows), device first-chunk index per
+    segment [S + 1]) for the chunked delta rule, or None (the token-serial kernel runs).
+
+    Opt-in (``QB_DN_CHUNKED=1``): on fp32 CUDA cores the chunked form does about as many FLOPs
+    as the token recurrence (it buys parallelism, not work), and measured slower than the
+    latency-tuned token kernel; it serves as the exact fp32 formulation for a tensor-core
+    version. Only batches whose longest segment reaches a chunk, and head size 128."""
+    if cu_h is None or dk != 128 or dv != 128 or os.environ.get("QB_DN_CHUNKED", "0") != "1":
+        return None
+    lens = [cu_h[i + 1] - cu_h[i] for i in range(len(cu_h) - 1)]
+    if not lens or max(lens) < DN_CHUNK_MIN:
+        return None
+    key = (tuple(cu_h), device)
+    hit = _dn_chunk_cache.get(key)
+    if hit is None:
+        rows, seg0 = [], [0]
+        for s, n in enumerate(lens):
+            for r in range(0, n, DN_CHUNK):
+                rows.append([s, cu_h[s] + r, min(DN_CHUNK, n - r)])
+            seg0.append(len(rows))
+        hit = (torch.tensor(rows, dtype=torch.int32).to(device), torch.tensor(seg0, dtype=torch.int32).to(device))
+        if len(_dn_chunk_cache) >= 256:
+            _dn_chunk_cache.pop(next(iter(_dn_chunk_cache)))
+        _dn_chunk_cache[key] = hit
+    return hit
 
 
 _FA_SMS = 148

@@ -1,7 +1,7 @@
 """Kernel micro-benchmarks at the full model's shapes, with roofline fractions.
 
-    python -m qwen35_b200.ops.kbench [--case moe|gemm|attn_prefill|attn_decode|deltanet|all]
-                                     [--tokens N] [--ctx N] [--iters N]
+    python -m qwen35_b200.ops.kbench [--case moe|gemm|attn_prefill|attn_decode|deltanet|model|all]
+                                     [--tokens N] [--ctx N] [--lanes N] [--iters N]
 
 Each case builds random inputs of one hot op at the Qwen3.5-397B-A17B geometry (one GPU, TP=1
 shard sizes unless noted), warms up, then times ``--iters`` launches with CUDA events on the
@@ -155,7 +155,9 @@ def case_attn_decode(lanes: int, ctx: int, iters: int, pk: dict, nq: int = 32, n
 def case_deltanet(tokens: int, lanes: int, iters: int, pk: dict, nk: int = 16, nv: int = 64, dk: int = 128,
                   dv: int = 128) -> dict:
     """Gated delta rule over ``lanes`` segments of ``tokens`` rows each (fp32 state
-    [nv, dk, dv] per lane read and written once); FLOPs ~ 4 * dk * dv per head per row."""
+    [nv, dk, dv] per lane read and written once); FLOPs ~ 4 * dk * dv per head per row (the
+    token recurrence's count; the chunked form used for long segments does more arithmetic in
+    parallel). The host segment table is passed, as the model does, so routing matches it."""
     C = 2 * nk * dk + nv * dv
     g = _g(5)
     qkv = torch.randn(lanes * tokens, C, device="cuda", generator=g).to(torch.bfloat16)
@@ -166,16 +168,62 @@ def case_deltanet(tokens: int, lanes: int, iters: int, pk: dict, nk: int = 16, n
     i32 = dict(dtype=torch.int32, device="cuda")
     seg = torch.arange(lanes, **i32)
     cu = torch.arange(0, lanes * tokens + 1, tokens, **i32)
-    ms = _time(lambda: ops.gated_delta_varlen(qkv, ab, a_log, dtb, rs, seg, cu, nk, nv, dk, dv), iters)
+    seg_h, cu_h = list(range(lanes)), list(range(0, lanes * tokens + 1, tokens))
+    ms = _time(lambda: ops.gated_delta_varlen(qkv, ab, a_log, dtb, rs, seg, cu, nk, nv, dk, dv, seg_h, cu_h), iters)
     bytes_ = 2 * rs.numel() * 4 + qkv.numel() * 2 + lanes * tokens * nv * dv * 2
     flops = 4 * lanes * tokens * nv * dk * dv
     return _report(f"deltanet_T{tokens}_B{lanes}", ms, bytes_, flops, pk)
 
 
+def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
+    """Whole-model steps at the full geometry on one GPU (random weights; experts of the first
+    layers reused by the rest, as the one-GPU benchmark does): one prefill of ``tokens`` new
+    tokens continuing ``ctx`` cached ones, and one ``lanes``-row decode step at context
+    ``max(ctx, 2048)``. Prints the step times (CUDA events) and the per-kernel share of device
+    time (torch profiler, a separate run)."""
+    import collections
+
+    from ..serving.engine import PoolSpec, build_model
+
+    dev = torch.device("cuda", 0)
+    spec = PoolSpec(lanes=lanes, max_seq=16384, kv_tokens=lanes * 9600, snapshots=8)
+    m, _ = build_model("full", 0, 1, dev, spec, graphs=False)
+    per = 600
+    for lane in range(lanes):
+        m.begin(lane)
+        m.attach_blocks(lane, list(range(1 + lane * per, 1 + (lane + 1) * per)))
+    ids = [(i * 7919) % 150000 for i in range(tokens)]
+    res = {}
+
+    def prefill():
+        m.forward([(0, ids, ctx)])
+
+    def decode():
+        m.decode(list(range(lanes)), [5] * lanes, [max(ctx, 2048) + lane for lane in range(lanes)])
+
+    for f in (prefill, decode):
+        ms = _time(f, 1)
+        with torch.profiler.profile(activities=[torch.profiler.ProfilerActivity.CUDA]) as prof:
+            f()
+            torch.cuda.synchronize()
+        agg = collections.defaultdict(lambda: [0, 0.0])
+        for ev in prof.events():
+            if ev.device_type == torch.autograd.DeviceType.CUDA:
+                agg[ev.name.split("(")[0][:60]][0] += 1
+                agg[ev.name.split("(")[0][:60]][1] += getattr(ev, "device_time_total", 0.0)
+        tot = sum(v[1] for v in agg.values()) or 1.0
+        top = sorted(agg.items(), key=lambda kv: -kv[1][1])[:12]
+        row = {"case": f"model_{f.__name__}", "tokens": tokens if f is prefill else lanes, "ctx": ctx,
+               "ms": round(ms, 2), "kernels": [(k, n, round(t / tot, 3)) for k, (n, t) in top]}
+        print(json.dumps(row), flush=True)
+        res[f.__name__] = row
+    return res
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="all",
-                    choices=["moe", "gemm", "attn_prefill", "attn_decode", "deltanet", "all"])
+                    choices=["moe", "gemm", "attn_prefill", "attn_decode", "deltanet", "model", "all"])
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--lanes", type=int, default=None)
@@ -195,6 +243,8 @@ def main(argv=None):
         run.append(case_attn_prefill(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.iters, pk))
     if a.case in ("attn_decode", "all"):
         run.append(case_attn_decode(a.lanes or 32, a.ctx or 6000, a.iters, pk))
+    if a.case == "model":
+        return case_model(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.lanes or 32)
     if a.case in ("deltanet", "all"):
         run.append(case_deltanet(a.tokens or 1, a.lanes or 32, a.iters, pk))
         if a.case == "all":

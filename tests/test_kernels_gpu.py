@@ -378,3 +378,40 @@ def test_flash_attention_decode_splits(nq, nkv, hd):
                                torch.tensor(starts), bs, lanes, cu, starts, table.cpu().tolist())
     close(out.cpu(), exp, atol=2e-2)
     status_ok()
+
+
+def test_chunked_delta_rule_matches_recurrence(monkeypatch):
+    """Chunked (WY) delta rule on prefill-sized segments vs the fp32 token recurrence: outputs
+    and the carried state, several segments (one shorter than a chunk, one of a single row)."""
+    monkeypatch.setenv("QB_DN_CHUNKED", "1")
+    nk, nv, dk, dv = 2, 8, 128, 128
+    C = 2 * nk * dk + nv * dv
+    lanes = 4
+    segs = [(0, 200), (2, 64), (1, 1), (3, 130)]
+    T = sum(n for _, n in segs)
+    cu = [0]
+    for _, n in segs:
+        cu.append(cu[-1] + n)
+    ln = [l for l, _ in segs]
+    qkv = rnd(T, C, seed=31)
+    ab = rnd(T, 2 * nv, seed=32)
+    a_log = torch.log(torch.rand(nv, device=DEV) * 15 + 1)
+    dtb = torch.rand(nv, device=DEV)
+    rs = torch.randn(lanes, nv, dk, dv, device=DEV) * 0.1
+    rs2 = rs.clone().cpu()
+    i32 = dict(dtype=torch.int32, device=DEV)
+    assert ops.dn_chunk_plan(cu, dk, dv, qkv.device) is not None
+    o = ops.gated_delta_varlen(qkv, ab, a_log, dtb, rs, torch.tensor(ln, **i32), torch.tensor(cu, **i32), nk, nv, dk,
+                               dv, ln, cu)
+    torch.cuda.synchronize()
+    oe = ops.gated_delta_varlen(qkv.cpu(), ab.cpu(), a_log.cpu(), dtb.cpu(), rs2, torch.tensor(ln), torch.tensor(cu),
+                                nk, nv, dk, dv, ln, cu)
+    close(o.cpu(), oe, atol=2e-2)
+    close(rs.cpu(), rs2, rtol=1e-2, atol=1e-3)
+    # commit=False leaves the state alone
+    before = rs.clone()
+    ops.gated_delta_varlen(qkv, ab, a_log, dtb, rs, torch.tensor(ln, **i32), torch.tensor(cu, **i32), nk, nv, dk,
+                           dv, ln, cu, commit=False)
+    torch.cuda.synchronize()
+    assert torch.equal(rs, before)
+    status_ok()
