@@ -6,7 +6,8 @@
 // slot s = e & 1. Block b of every rank
 //   1. copies its row chunk of the local partial sum into its own slot s,
 //   2. publishes flag[s][b] = e with a system-scope release,
-//   3. waits (bounded) until every peer's flag[s][b] == e (system-scope acquire, peer loads),
+//   3. waits (bounded) until every peer's flag[s][b] == e (system-scope acquire, peer loads; one
+//      thread per peer, so the remote round trips overlap),
 //   4. sums the W partial rows in rank order (fp32, so every rank gets identical bits), rounds
 //      to bf16, adds the residual, writes the new residual and its RMSNorm.
 // A rank reaching call e+2 overwrites slot s only after it saw every peer's flag for e+1, and a
@@ -45,7 +46,6 @@ __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
     float eps, long slot_elems, int max_blocks, int* epoch, int* done, int* err, unsigned long long timeout_ns) {
   __shared__ float red[32];
   __shared__ int s_epoch;
-  __shared__ int s_ok;
   if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile int*>(epoch) + 1;
   __syncthreads();
   const int e = s_epoch;
@@ -66,25 +66,21 @@ __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
     __threadfence_system();
     st_release_sys(flags_of(me) + b, e);
   }
-  // 3. wait for every peer's chunk (bounded)
-  if (threadIdx.x == 0) {
-    int ok = 1;
+  // 3. wait for every peer's chunk (bounded); thread p polls peer p, so the W - 1 remote
+  //    round trips overlap instead of following one another
+  int ok = 1;
+  if (threadIdx.x < W && threadIdx.x != me) {
+    const int* f = flags_of(threadIdx.x) + b;
     const uint64_t t0 = globaltimer();
-    for (int p = 0; p < W && ok; ++p) {
-      if (p == me) continue;
-      const int* f = flags_of(p) + b;
-      while (ld_acquire_sys(f) < e) {
-        if (globaltimer() - t0 > timeout_ns) {
-          atomicCAS(err, 0, ERR_PEER_WAIT);
-          ok = 0;
-          break;
-        }
+    while (ld_acquire_sys(f) < e) {
+      if (globaltimer() - t0 > timeout_ns) {
+        atomicCAS(err, 0, ERR_PEER_WAIT);
+        ok = 0;
+        break;
       }
     }
-    s_ok = ok;
   }
-  __syncthreads();
-  if (s_ok) {
+  if (__syncthreads_and(ok)) {
     // 4. reduce in rank order, add residual, RMSNorm
     for (int r = b; r < rows; r += gridDim.x) {
       float acc[16];
@@ -95,12 +91,21 @@ __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
         const int i = (threadIdx.x + c * AR_THREADS) * 8;
         if (c < nper && i < H) {
           float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-          for (int p = 0; p < W; ++p) {
-            const bf16* src = reinterpret_cast<const bf16*>(ptrs.data[p]) + slot * slot_elems + (long)r * H + i;
-            const uint4 raw = __ldcv(reinterpret_cast<const uint4*>(src));  // bypass L1: slots are reused
-            const bf16* ev = reinterpret_cast<const bf16*>(&raw);
+          uint4 raw[8];  // every rank's chunk in flight at once, then summed in rank order
 #pragma unroll
-            for (int u = 0; u < 8; ++u) sum[u] += __bfloat162float(ev[u]);
+          for (int p = 0; p < 8; ++p) {
+            if (p < W) {
+              const bf16* src = reinterpret_cast<const bf16*>(ptrs.data[p]) + slot * slot_elems + (long)r * H + i;
+              raw[p] = __ldcv(reinterpret_cast<const uint4*>(src));  // bypass L1: slots are reused
+            }
+          }
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            if (p < W) {
+              const bf16* ev = reinterpret_cast<const bf16*>(&raw[p]);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) sum[u] += __bfloat162float(ev[u]);
+            }
           }
           const uint4 rr = *reinterpret_cast<const uint4*>(res + (long)r * H + i);
           const bf16* rv = reinterpret_cast<const bf16*>(&rr);

@@ -20,6 +20,7 @@
 // epilogue sees both halves of silu(g)*u in one accumulator.
 #include "common.cuh"
 #include "kernels.h"
+#include "numerics.cuh"
 
 #include <cstdlib>
 #include <type_traits>
@@ -227,24 +228,6 @@ __device__ __forceinline__ uint32_t e2m1x2_to_f16x2(uint32_t byte) {
   uint32_t r;
   asm("{\n .reg .b8 b;\n cvt.u8.u32 b, %1;\n cvt.rn.f16x2.e2m1x2 %0, b;\n}" : "=r"(r) : "r"(byte));
   return r;
-}
-
-// Eight e2m1 codes (one 32-bit word, code j in bits 4j..4j+3) -> four f16x2 words, on the
-// integer ALU. A code [s e1 e0 m] placed at f16 bits 15 / 11 / 10 / 9 is exactly its value times
-// 2^-14 (e = 0 lands in the f16 subnormal range, e > 0 in the normal range, both scaled by the
-// same 2^-14), so a byte permute plus a mask builds the f16 bits and one multiply by the
-// power of two `sc` = 2^(14 + block exponent) applies the e8m0 scale exactly.
-__device__ __forceinline__ void e2m1x8_placed(uint32_t w, uint32_t* o) {
-  // even codes: e/m bits to byte bits 1..3, sign to bit 7; odd codes likewise from the high nibble
-  const uint32_t ev = ((w << 1) & 0x0E0E0E0Eu) | ((w << 4) & 0x80808080u);
-  const uint32_t od = ((w >> 3) & 0x0E0E0E0Eu) | (w & 0x80808080u);
-  // interleave (even, odd) byte pairs, then spread each pair into the high bytes of two halves
-  // (selector 4 = a byte of the zero operand)
-  const uint32_t p01 = __byte_perm(ev, od, 0x5140), p23 = __byte_perm(ev, od, 0x7362);
-  o[0] = __byte_perm(p01, 0, 0x1404);
-  o[1] = __byte_perm(p01, 0, 0x3424);
-  o[2] = __byte_perm(p23, 0, 0x1404);
-  o[3] = __byte_perm(p23, 0, 0x3424);
 }
 
 template <int BN, bool FP4>

@@ -9,8 +9,9 @@
 // Activations: every bf16 activation x is written as two e4m3 terms with per-32 e8m0 scales,
 //   x = 2^E * hi + 2^(E-4) * lo,   E = floor(log2(block max)) - 7,
 // hi = x / 2^E truncated to e4m3, lo = the remainder * 16 truncated to e4m3. A bf16 value has 8
-// significant bits; hi takes the top 4 and lo the next 4, so the split is exact for every element
-// within 2^14 of its block maximum (smaller ones keep an error below 2^-20 of the block maximum).
+// significant bits; hi takes the top 4 and lo the next 4, so the split is exact whenever hi is a
+// normal e4m3 (|x| >= 2^(E-6), which holds for every element within 2^13 of its block maximum);
+// smaller ones keep an error below 2^-20 of the block maximum.
 // e2m1 x e4m3 products are exact, so the two MMAs per K-block (hi then lo, same fp32 accumulator)
 // reproduce the bf16 reference's products, as the f16 path does.
 //
@@ -33,6 +34,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "numerics.cuh"
 
 #include <cstdlib>
 
@@ -323,18 +325,6 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 }
 
 // ------------------------------------------------------------------ activation split
-// |v| (< 256) -> (e4m3 code, its value) truncated toward zero.
-__device__ __forceinline__ uint32_t e4m3_trunc(float av, float& val) {
-  const uint32_t b = __float_as_uint(av);
-  if (b >= 0x3C800000u) {  // >= 2^-6: normal e4m3, keep 3 mantissa bits
-    val = __uint_as_float(b & 0xFFF00000u);
-    return ((((b >> 23) & 0xFF) - 127 + 7) << 3) | ((b >> 20) & 7);
-  }
-  const uint32_t m = (uint32_t)(av * 512.f);  // subnormal: m x 2^-9, m < 8
-  val = (float)m * (1.f / 512.f);
-  return m;
-}
-
 // One warp per row: rows `a < *n_rows` of x (row a read from x[perm[a]] when perm is given) ->
 // hi / lo e4m3 bytes [cap, K] and their scales, written straight into the per-tile chunks (the
 // token tile of row a is the tile of its expert's run; tiles of BN rows). Each lane holds 8
@@ -359,7 +349,7 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
   const bf16* src = x + (long)(perm ? perm[a] : a) * K;
   uint8_t* hrow = hi + (long)a * K;
   uint8_t* lrow = lo + (long)a * K;
-  const long sf_row = (long)tt * (K / MX_SK) * MX_CHUNK + (rr % 32) * 16 + (rr / 32) * 4;
+  const long sf_tile = (long)tt * (K / MX_SK) * MX_CHUNK;
   for (int kbase = kbeg; kbase < kend; kbase += 256) {  // warp-uniform trip count (shuffles below)
     const int k0 = kbase + lane * 8;
     const bool valid = k0 < kend;                       // segments are multiples of 128, not always of 256
@@ -377,26 +367,21 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
     for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(fabsf(v[i])));
     mb = max(mb, __shfl_xor_sync(0xffffffff, mb, 1));
     mb = max(mb, __shfl_xor_sync(0xffffffff, mb, 2));  // max over the 4 lanes of the block
-    int E = mb ? (int)(mb >> 23) - 127 - 7 : -127;      // block max / 2^E in [128, 256)
-    if (E < -123) E = -123;                             // lo scale E - 4 stays a valid e8m0
-    const float inv = __uint_as_float((uint32_t)(127 - E) << 23);  // 2^-E, exact
+    const int E = mx_block_exponent(mb);  // block max / 2^E in [128, 256)
     uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float xs = fabsf(v[i]) * inv;
-      float hv, lv;
-      const uint32_t ch = e4m3_trunc(xs, hv);
-      const uint32_t cl = e4m3_trunc((xs - hv) * 16.f, lv);
-      const uint32_t sg = v[i] < 0.f ? 0x80u : 0u;
-      hw[i / 4] |= (ch | (ch ? sg : 0u)) << (8 * (i % 4));
-      lw[i / 4] |= (cl | (cl ? sg : 0u)) << (8 * (i % 4));
+      uint8_t ch, cl;
+      mx_split(v[i], E, ch, cl);
+      hw[i / 4] |= (uint32_t)ch << (8 * (i % 4));
+      lw[i / 4] |= (uint32_t)cl << (8 * (i % 4));
     }
     if (!valid) continue;
     *reinterpret_cast<uint2*>(hrow + k0) = make_uint2(hw[0], hw[1]);
     *reinterpret_cast<uint2*>(lrow + k0) = make_uint2(lw[0], lw[1]);
     if ((lane & 3) == 0) {
       const int kb = k0 / 32;
-      const long off = sf_row + (long)(kb / 4) * MX_CHUNK + (kb % 4);
+      const long off = sf_tile + (long)(kb / 4) * MX_CHUNK + mx_chunk_offset(rr, kb % 4);
       sf_hi[off] = (uint8_t)(E + 127);
       sf_lo[off] = (uint8_t)(E - 4 + 127);
     }
