@@ -112,6 +112,15 @@ __global__ void __launch_bounds__(256) delta_prep_kernel(const bf16* qkv, long l
 constexpr int DR_CT = 16;  // tokens staged per chunk
 constexpr int DR_TPC = 4;  // threads per state column
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// Token recurrence. Tokens are staged in chunks of DR_CT through two shared-memory buffers filled
+// by 16-byte cp.async copies: chunk c+1 is in flight while chunk c is computed.
 template <int DK>
 __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const float* kn, const float* gb,
                                                         const bf16* qkv, long ldqkv, float* state, long lane_stride,
@@ -119,11 +128,12 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
                                                         bf16* out, int commit) {
   constexpr int COLS = 128 / DR_TPC;  // state columns per CTA
   constexpr int PART = DK / DR_TPC;   // rows per thread
-  constexpr int PST = PART + 4;       // padded part stride (floats): the 8 parts sit in different banks
-  __shared__ __align__(16) float qs[DR_CT][DR_TPC * PST];
-  __shared__ __align__(16) float ks[DR_CT][DR_TPC * PST];
-  __shared__ float vs[DR_CT][COLS];
-  __shared__ float gs[DR_CT][2];
+  constexpr int PST = PART + 4;       // padded part stride (floats; 16-byte multiple): parts in different banks
+  static_assert((PST * 4) % 16 == 0 && PART % 4 == 0, "16-byte staging");
+  __shared__ __align__(16) float qs[2][DR_CT][DR_TPC * PST];
+  __shared__ __align__(16) float ks[2][DR_CT][DR_TPC * PST];
+  __shared__ __align__(16) bf16 vs[2][DR_CT][COLS];
+  __shared__ __align__(16) float gs[2][DR_CT][4];
   const int h = blockIdx.x, s = blockIdx.y, cb = blockIdx.z;
   const int tid = threadIdx.x;
   const int col = tid / DR_TPC, part = tid % DR_TPC;
@@ -132,30 +142,54 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
   const int hk = h / (nv / nk);
   float* st = state + (long)lane * lane_stride + (long)h * DK * dv;
   const bool active = j < dv;
+  // v rows by 16-byte cp.async when the column block is whole and the rows are 16-byte aligned
+  const bool vfull = cb * COLS + COLS <= dv && (ldqkv % 8) == 0 && (reinterpret_cast<uintptr_t>(qkv) % 16) == 0;
   float S[PART];
 #pragma unroll
   for (int i = 0; i < PART; ++i) S[i] = active ? st[(long)(part * PART + i) * dv + j] : 0.f;
   const int t0 = cu[s], t1 = cu[s + 1];
-  for (int c0 = t0; c0 < t1; c0 += DR_CT) {
+  auto stage = [&](int buf, int c0) {  // issue the copies of tokens [c0, c0 + n) into buffer `buf`
     const int n = min(DR_CT, t1 - c0);
-    __syncthreads();
-    for (int idx = tid; idx < n * DK; idx += blockDim.x) {
-      const int tt = idx / DK, i = idx % DK;
-      const long base = ((long)(c0 + tt) * nk + hk) * DK + i;
-      qs[tt][(i / PART) * PST + i % PART] = qn[base];
-      ks[tt][(i / PART) * PST + i % PART] = kn[base];
+    constexpr int QV = DK / 4;  // 16-byte pieces per q (or k) row
+    for (int idx = tid; idx < n * QV; idx += blockDim.x) {
+      const int tt = idx / QV, i4 = (idx % QV) * 4;
+      const long base = ((long)(c0 + tt) * nk + hk) * DK + i4;
+      const int off = (i4 / PART) * PST + i4 % PART;
+      cp_async16(&qs[buf][tt][off], qn + base);
+      cp_async16(&ks[buf][tt][off], kn + base);
     }
-    for (int idx = tid; idx < n * COLS; idx += blockDim.x) {
-      const int tt = idx / COLS, cc = idx % COLS;
-      const int jj = cb * COLS + cc;
-      vs[tt][cc] = jj < dv ? __bfloat162float(qkv[(long)(c0 + tt) * ldqkv + 2L * nk * DK + (long)h * dv + jj]) : 0.f;
+    if (vfull) {
+      constexpr int VV = COLS / 8;  // 16-byte pieces of one token's v slice
+      for (int idx = tid; idx < n * VV; idx += blockDim.x) {
+        const int tt = idx / VV, c8 = (idx % VV) * 8;
+        cp_async16(&vs[buf][tt][c8], qkv + (long)(c0 + tt) * ldqkv + 2L * nk * DK + (long)h * dv + cb * COLS + c8);
+      }
+    } else {
+      for (int idx = tid; idx < n * COLS; idx += blockDim.x) {
+        const int tt = idx / COLS, cc = idx % COLS;
+        const int jj = cb * COLS + cc;
+        vs[buf][tt][cc] = jj < dv ? qkv[(long)(c0 + tt) * ldqkv + 2L * nk * DK + (long)h * dv + jj]
+                                  : __float2bfloat16(0.f);
+      }
     }
-    for (int idx = tid; idx < n * 2; idx += blockDim.x) gs[idx / 2][idx % 2] = gb[((long)(c0 + idx / 2) * nv + h) * 4 + idx % 2];
+    for (int tt = tid; tt < n; tt += blockDim.x) cp_async16(&gs[buf][tt][0], gb + ((long)(c0 + tt) * nv + h) * 4);
+    cp_async_commit();
+  };
+  if (t0 < t1) stage(0, t0);
+  int buf = 0;
+  for (int c0 = t0; c0 < t1; c0 += DR_CT, buf ^= 1) {
+    const int n = min(DR_CT, t1 - c0);
+    if (c0 + DR_CT < t1) {
+      stage(buf ^ 1, c0 + DR_CT);  // the next chunk lands while this one is computed
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
     __syncthreads();
     for (int tt = 0; tt < n; ++tt) {
-      const float* kp = &ks[tt][part * PST];
-      const float* qp = &qs[tt][part * PST];
-      const float decay = gs[tt][0], beta = gs[tt][1];
+      const float* kp = &ks[buf][tt][part * PST];
+      const float* qp = &qs[buf][tt][part * PST];
+      const float decay = gs[buf][tt][0], beta = gs[buf][tt][1];
       float kv4[4] = {0.f, 0.f, 0.f, 0.f};  // independent partial sums: short dependency chains
 #pragma unroll
       for (int i = 0; i < PART; i += 4) {
@@ -168,7 +202,7 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
       float kv = (kv4[0] + kv4[1]) + (kv4[2] + kv4[3]);
 #pragma unroll
       for (int o = 1; o < DR_TPC; o <<= 1) kv += __shfl_xor_sync(0xffffffff, kv, o);
-      const float delta = (vs[tt][col] - decay * kv) * beta;
+      const float delta = (__bfloat162float(vs[buf][tt][col]) - decay * kv) * beta;
       float o4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < PART; i += 4) {
@@ -188,6 +222,7 @@ __global__ void __launch_bounds__(128) delta_rec_kernel(const float* qn, const f
       for (int of = 1; of < DR_TPC; of <<= 1) o += __shfl_xor_sync(0xffffffff, o, of);
       if (part == 0 && active) out[((long)(c0 + tt) * nv + h) * dv + j] = __float2bfloat16(o);
     }
+    __syncthreads();  // buffer `buf` is refilled two chunks later
   }
   if (active && commit) {
 #pragma unroll
