@@ -406,6 +406,22 @@ void symm_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor partia
                                  (unsigned long long)(timeout_s * 1e9), stream()));
 }
 
+void symm_sp_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor partial, Tensor res, Tensor w1p, Tensor out,
+                         double eps, int64_t slot_elems, int64_t max_blocks, Tensor epoch, double timeout_s) {
+  CHECK_BF16(partial);
+  CHECK_BF16(res);
+  TORCH_CHECK(res.is_contiguous() && out.is_contiguous() && partial.stride(-1) == 1, "symm_sp_ar: layouts");
+  std::vector<void*> b(bases.size());
+  for (size_t i = 0; i < bases.size(); ++i) b[i] = reinterpret_cast<void*>(bases[i]);
+  const int H = res.size(-1);
+  const int rows = res.numel() / H;
+  int* ep = epoch.data_ptr<int>();
+  LAUNCH(qb::symm_sp_ar_add_rmsnorm(b.data(), (int)b.size(), (int)rank, partial.data_ptr(), partial.stride(0),
+                                 res.data_ptr(), w1p.data_ptr<float>(), out.data_ptr(), rows, H, (float)eps,
+                                 slot_elems, (int)max_blocks, ep, ep + 1, err_ptr(res),
+                                 (unsigned long long)(timeout_s * 1e9), stream()));
+}
+
 // ------------------------------------------------------------------ status
 int64_t launches() { return g_launches.load(); }
 // graph replays launch the captured kernels without passing through these bindings
@@ -441,6 +457,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
   m.def("symm_ar_add_rmsnorm", &symm_ar_add_rmsnorm);
+  m.def("symm_sp_ar_add_rmsnorm", &symm_sp_ar_add_rmsnorm);
   m.def("launches", &launches, "number of kernels launched through the bindings so far");
   m.def("add_launches", &add_launches, "account kernels launched by a CUDA-graph replay");
   m.def("clear_status", &clear_status);

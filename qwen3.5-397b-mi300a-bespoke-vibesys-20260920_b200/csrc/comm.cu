@@ -158,6 +158,186 @@ __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
   }
 }
 
+// ------------------------------------------------------------------ sequence-parallel variant
+// Reduce-scatter + residual add + RMSNorm + all-gather, for prefill-sized messages. Rank r owns
+// rows [r R / W, (r+1) R / W); inside every rank's range, block b handles rows b, b + G, ... (the
+// same (rank, block) units on every rank). Region per rank and slot: the staged partial
+// [R_max, H] and the results [R_max, 2H] (new residual row, normed row); then phase-A and
+// phase-B flags [2 slots][max_blocks] each.
+//   A. block b stages, for every owner rank, its unit's rows of the local partial; flag A[b] = e
+//   B. block b waits for flag A[b] of every peer (one thread per peer), then for its own unit:
+//      rank-order fp32 sum of the W partial rows, bf16 round, + residual, RMSNorm; writes the
+//      results to its slot and to the local tensors; flag B[b] = e
+//   C. block b waits for flag B[b] of every peer and copies their units' result rows.
+// Same bits as the one-shot kernel (and as NCCL all-reduce + add + RMSNorm); each rank moves
+// about 3 (W-1)/W of the bf16 payload over NVLink instead of (W-1) copies of it.
+__device__ __forceinline__ bool wait_peers(const SymmPtrs& ptrs, long flag_off, int b, int e, int* err,
+                                           unsigned long long timeout_ns) {
+  int ok = 1;
+  if (threadIdx.x < ptrs.world && threadIdx.x != ptrs.rank) {
+    const int* f = reinterpret_cast<const int*>(reinterpret_cast<const char*>(ptrs.data[threadIdx.x]) + flag_off) + b;
+    const uint64_t t0 = globaltimer();
+    while (ld_acquire_sys(f) < e) {
+      if (globaltimer() - t0 > timeout_ns) {
+        atomicCAS(err, 0, ERR_PEER_WAIT);
+        ok = 0;
+        break;
+      }
+    }
+  }
+  return __syncthreads_and(ok);
+}
+
+__global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
+    SymmPtrs ptrs, const bf16* partial, long ldp, bf16* res, const float* w1p, bf16* out, int rows, int H,
+    float eps, long slot_elems, int max_blocks, int* epoch, int* done, int* err, unsigned long long timeout_ns) {
+  __shared__ float red[32];
+  __shared__ int s_epoch;
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile int*>(epoch) + 1;
+  __syncthreads();
+  const int e = s_epoch, slot = e & 1;
+  const int W = ptrs.world, me = ptrs.rank, b = blockIdx.x, G = gridDim.x;
+  const long slot_stride = 3 * slot_elems;                          // elements per slot
+  const long flags_base = 2 * slot_stride * (long)sizeof(bf16);     // bytes
+  const long flagA = flags_base + (long)slot * max_blocks * 4;
+  const long flagB = flags_base + (2L + slot) * max_blocks * 4;
+  auto part_of = [&](int r) { return reinterpret_cast<bf16*>(ptrs.data[r]) + slot * slot_stride; };
+  auto result_of = [&](int r) { return reinterpret_cast<bf16*>(ptrs.data[r]) + slot * slot_stride + slot_elems; };
+  auto range = [&](int r, int& r0, int& r1) {
+    r0 = (int)((long)rows * r / W);
+    r1 = (int)((long)rows * (r + 1) / W);
+  };
+  auto publish = [&](long off) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence_system();
+      st_release_sys(reinterpret_cast<int*>(reinterpret_cast<char*>(ptrs.data[me]) + off) + b, e);
+    }
+  };
+  // A. stage this block's rows of every owner's range
+  bf16* mine = part_of(me);
+  for (int r = 0; r < W; ++r) {
+    int r0, r1;
+    range(r, r0, r1);
+    for (int row = r0 + b; row < r1; row += G)
+      for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8)
+        *reinterpret_cast<uint4*>(mine + (long)row * H + i) =
+            *reinterpret_cast<const uint4*>(partial + (long)row * ldp + i);
+  }
+  publish(flagA);
+  // B. reduce + add + norm for this block's unit of my range
+  if (wait_peers(ptrs, flagA, b, e, err, timeout_ns)) {
+    int r0, r1;
+    range(me, r0, r1);
+    bf16* myres = result_of(me);
+    const int nper = (H + AR_THREADS * 8 - 1) / (AR_THREADS * 8);  // chunks of 8 per thread (<= 2)
+    for (int row = r0 + b; row < r1; row += G) {
+      float acc[16];
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int i = (threadIdx.x + c * AR_THREADS) * 8;
+        if (c < nper && i < H) {
+          float sum[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+          uint4 raw[8];
+#pragma unroll
+          for (int p = 0; p < 8; ++p)
+            if (p < W) raw[p] = __ldcv(reinterpret_cast<const uint4*>(part_of(p) + (long)row * H + i));
+#pragma unroll
+          for (int p = 0; p < 8; ++p) {
+            if (p < W) {
+              const bf16* ev = reinterpret_cast<const bf16*>(&raw[p]);
+#pragma unroll
+              for (int u = 0; u < 8; ++u) sum[u] += __bfloat162float(ev[u]);
+            }
+          }
+          const uint4 rr = *reinterpret_cast<const uint4*>(res + (long)row * H + i);
+          const bf16* rv = reinterpret_cast<const bf16*>(&rr);
+          uint4 nr;
+          bf16* nv = reinterpret_cast<bf16*>(&nr);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const float sb = __bfloat162float(__float2bfloat16(sum[u]));
+            nv[u] = __float2bfloat16(__bfloat162float(rv[u]) + sb);
+            acc[c * 8 + u] = __bfloat162float(nv[u]);
+            ss += acc[c * 8 + u] * acc[c * 8 + u];
+          }
+          *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr;
+          *reinterpret_cast<uint4*>(myres + (long)row * 2 * H + i) = nr;
+        }
+      }
+      ss = warp_sum(ss);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        float t = threadIdx.x < AR_THREADS / 32 ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+      }
+      __syncthreads();
+      const float inv = rsqrtf(red[0] / H + eps);
+      __syncthreads();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int i = (threadIdx.x + c * AR_THREADS) * 8;
+        if (c < nper && i < H) {
+          uint4 o;
+          bf16* ov = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) ov[u] = __float2bfloat16(acc[c * 8 + u] * inv * w1p[i + u]);
+          *reinterpret_cast<uint4*>(out + (long)row * H + i) = o;
+          *reinterpret_cast<uint4*>(myres + (long)row * 2 * H + H + i) = o;
+        }
+      }
+    }
+    publish(flagB);
+    // C. gather the peers' result rows of this block's units
+    if (wait_peers(ptrs, flagB, b, e, err, timeout_ns)) {
+      for (int p = 0; p < W; ++p) {
+        if (p == me) continue;
+        int q0, q1;
+        range(p, q0, q1);
+        const bf16* pr = result_of(p);
+        for (int row = q0 + b; row < q1; row += G)
+          for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8) {
+            const uint4 nr = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + i));
+            const uint4 o = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + H + i));
+            *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr;
+            *reinterpret_cast<uint4*>(out + (long)row * H + i) = o;
+          }
+      }
+    }
+  }
+  // the last block to finish advances the epoch (every block already read it at entry)
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int d = atomicAdd(done, 1);
+    if (d == (int)gridDim.x - 1) {
+      *done = 0;
+      __threadfence();
+      atomicExch(epoch, e);
+    }
+  }
+}
+
+int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
+                           const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
+                           int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s) {
+  if (world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || (long)rows * H > slot_elems) return -1;
+  SymmPtrs p{};
+  for (int r = 0; r < world; ++r) p.data[r] = bases[r];
+  p.world = world;
+  p.rank = rank;
+  int per = (rows + world - 1) / world;  // rows of one rank's range: one block per row, up to max_blocks
+  int grid = per < max_blocks ? per : max_blocks;
+  if (grid < 1) grid = 1;
+  sp_ar_add_rmsnorm_kernel<<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res, w1p, (bf16*)out,
+                                                       rows, H, eps, slot_elems, max_blocks, epoch, done, err,
+                                                       timeout_ns);
+  return (int)cudaGetLastError();
+}
+
 int symm_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                         const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
                         int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s) {

@@ -336,17 +336,30 @@ static int launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArg
 
 static int gemm_bn(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256; }
 
-// K splits for an output of too few tiles to cover the SMs (each split keeps >= 8 K-blocks).
+// K splits per output tile: the S (each split keeping >= 8 K-blocks, at most 16) that minimises
+// the number of persistent-CTA waves per split, ceil(tiles * S / SMs) / S, plus 2 % per split for
+// the fp32 partials each extra split writes and reads. Few tiles (N = 4096 decode projections)
+// split until they fill the SMs; a count just above the SM count (161 tiles) splits so the ragged
+// second wave shrinks; large outputs (LM head) stay unsplit.
 int gemm_splits(int T, int N, int K) {
   const int BN = gemm_bn(T);
   const int tiles = ((N + 127) / 128) * ((T + BN - 1) / BN);
   const int kblocks = (K + BK - 1) / BK;
   const int sms = num_sms();
-  if (tiles * 2 > sms || kblocks < 16) return 1;
-  int s = sms / tiles;
-  if (s > kblocks / 8) s = kblocks / 8;
-  if (s > 16) s = 16;
-  return s < 1 ? 1 : s;
+  // decode shapes only (token tile <= 64): there the GEMM streams weights and the partials are
+  // small; a prefill GEMM is compute bound and its 128 x BN fp32 partials would rival its weights
+  if (BN > 64 || kblocks < 16 || tiles >= 4 * sms) return 1;
+  int best = 1;
+  double best_cost = 1e30;
+  for (int s = 1; s <= 16 && s <= kblocks / 8; ++s) {
+    const double waves = (double)((tiles * s + sms - 1) / sms) / s;
+    const double cost = waves * (1.0 + 0.02 * (s - 1));
+    if (cost < best_cost - 1e-9) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
 }
 
 long gemm_split_ws_floats(int T, int N, int K) {

@@ -88,5 +88,8 @@ int moe_expert_gemm_bf16(const void* xin, int in_cols, const void* w, int n_rows
 int symm_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                         const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
                         int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s);
+int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
+                        const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
+                        int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s);
 
 }  // namespace qb

@@ -22,8 +22,15 @@ MAX_BLOCKS = 296  # two CTAs per SM on a 148-SM B200
 
 
 class SymmComm:
+    """One-shot region (``max_rows`` rows) for decode-sized messages and, when ``sp_rows`` > 0, a
+    sequence-parallel region for prefill-sized ones (reduce-scatter + add + RMSNorm +
+    all-gather, ``csrc/comm.cu``). Each family has its own slots, flags and device epoch."""
+
+    ONESHOT_MAX_ROWS = 64  # above this many rows the sequence-parallel kernel moves fewer bytes
+
     def __init__(self, rank: int, world: int, device, max_rows: int, hidden: int, group=None,
-                 timeout_s: float = 10.0, bases: list[int] | None = None):
+                 timeout_s: float = 10.0, bases: list[int] | None = None, sp_rows: int = 0,
+                 sp_bases: list[int] | None = None):
         if world > 8:
             raise ValueError("one-shot symmetric all-reduce supports up to 8 ranks")
         self.rank, self.world, self.device = rank, world, torch.device(device)
@@ -31,40 +38,69 @@ class SymmComm:
         self.slot_elems = max_rows * hidden
         self.max_blocks = MAX_BLOCKS
         self.timeout_s = timeout_s
-        nbytes = 2 * self.slot_elems * 2 + 2 * self.max_blocks * 4
-        self.own = None
+        self.own: list[int] = []
         self.opened: list[int] = []
-        if bases is None:
-            with torch.cuda.device(self.device):
-                ptr, handle = ext().symm_alloc(nbytes)
-            self.own = ptr
-            handles = [None] * world
-            dist.all_gather_object(handles, handle, group=group)
-            bases = []
-            for r in range(world):
-                if r == rank:
-                    bases.append(ptr)
-                else:
-                    with torch.cuda.device(self.device):
-                        p = ext().symm_open(handles[r])
-                    self.opened.append(p)
-                    bases.append(p)
-        self.bases = list(bases)
+        self.bases = self._region(2 * self.slot_elems * 2 + 2 * self.max_blocks * 4, group, bases)
         self.epoch = torch.zeros(2, dtype=torch.int32, device=self.device)  # [epoch, finished blocks]
+        self.sp_rows = sp_rows
+        self.sp_slot_elems = sp_rows * hidden
+        self.sp_bases = None
+        if sp_rows > 0:
+            self.sp_bases = self._region(self.sp_region_bytes(sp_rows, hidden), group, sp_bases)
+            self.sp_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
+
+    @staticmethod
+    def sp_region_bytes(sp_rows: int, hidden: int) -> int:
+        # two slots of [partial | result residual + normed] = 3 x rows x hidden bf16, then A and B flags
+        return 2 * 3 * sp_rows * hidden * 2 + 4 * MAX_BLOCKS * 4
+
+    def _region(self, nbytes: int, group, bases):
+        """Allocate and export this rank's region, map every peer's (or use given bases)."""
+        if bases is not None:
+            return list(bases)
+        with torch.cuda.device(self.device):
+            ptr, handle = ext().symm_alloc(nbytes)
+        self.own.append(ptr)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, handle, group=group)
+        out = []
+        for r in range(self.world):
+            if r == self.rank:
+                out.append(ptr)
+            else:
+                with torch.cuda.device(self.device):
+                    p = ext().symm_open(handles[r])
+                self.opened.append(p)
+                out.append(p)
+        return out
 
     @staticmethod
     def region_bytes(max_rows: int, hidden: int) -> int:
         return 2 * max_rows * hidden * 2 + 2 * MAX_BLOCKS * 4
 
     def fits(self, rows: int) -> bool:
-        return rows <= self.max_rows
+        return rows <= self.max_rows or rows <= self.sp_rows
 
-    def allreduce_add_rmsnorm(self, partial, residual, w1p, eps):
-        """``residual += sum_ranks(partial)`` (in place) and returns (residual, rmsnorm(residual))."""
+    def allreduce_add_rmsnorm(self, partial, residual, w1p, eps, kind: str = "auto"):
+        """``residual += sum_ranks(partial)`` (in place) and returns (residual, rmsnorm(residual)).
+        One-shot kernel for up to ``ONESHOT_MAX_ROWS`` rows (one peer round trip), the
+        sequence-parallel kernel above that (``kind`` = "oneshot" / "sp" forces one); None when
+        the message fits neither region."""
         rows = residual.numel() // residual.shape[-1]
-        if not self.fits(rows):
-            return None
         normed = torch.empty_like(residual)
+        fits_sp = self.sp_bases is not None and rows <= self.sp_rows
+        if kind == "sp":
+            use_sp = fits_sp
+        elif kind == "oneshot":
+            use_sp = False
+        else:
+            use_sp = fits_sp and (rows > self.ONESHOT_MAX_ROWS or rows > self.max_rows)
+        if use_sp:
+            ext().symm_sp_ar_add_rmsnorm(self.sp_bases, self.rank, partial, residual, w1p, normed, float(eps),
+                                         self.sp_slot_elems, self.max_blocks, self.sp_epoch, self.timeout_s)
+            return residual, normed
+        if rows > self.max_rows:
+            return None
         ext().symm_ar_add_rmsnorm(self.bases, self.rank, partial, residual, w1p, normed, float(eps), self.slot_elems,
                                   self.max_blocks, self.epoch, self.timeout_s)
         return residual, normed
@@ -73,6 +109,6 @@ class SymmComm:
         for p in self.opened:
             ext().symm_close(p)
         self.opened.clear()
-        if self.own is not None:
-            ext().symm_free(self.own)
-            self.own = None
+        for p in self.own:
+            ext().symm_free(p)
+        self.own.clear()

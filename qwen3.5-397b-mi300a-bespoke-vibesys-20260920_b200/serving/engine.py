@@ -70,8 +70,10 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
         if world > 1 and device.type == "cuda" and comm.mode == "fused":
             from ..parallel.symm import SymmComm
 
-            rows = int(__import__("os").environ.get("QB_SYMM_MAX_ROWS", "512"))
-            comm.symm = SymmComm(rank, world, device, max_rows=rows, hidden=cfg.hidden)
+            env = __import__("os").environ
+            rows = int(env.get("QB_SYMM_MAX_ROWS", "512"))
+            sp_rows = int(env.get("QB_SP_MAX_ROWS", "4096"))  # prefill-sized messages: sequence-parallel kernel
+            comm.symm = SymmComm(rank, world, device, max_rows=rows, hidden=cfg.hidden, sp_rows=sp_rows)
     m = Model(cfg, w, p, comm, device=device, dtype=dtype,
               max_batch=spec.lanes + (1 if graphs else 0), max_seq=spec.max_seq, block_size=spec.block_size,
               num_blocks=num_blocks, num_snapshots=spec.snapshots or 2 * spec.lanes + 16)

@@ -23,11 +23,12 @@ def main(rank, world, port):
     dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
                             device_id=dev)
     H = 4096
-    s = SymmComm(rank, world, dev, max_rows=512, hidden=H, timeout_s=10.0)
+    s = SymmComm(rank, world, dev, max_rows=512, hidden=H, timeout_s=10.0, sp_rows=2048)
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).float()
     dist.broadcast(w, 0)
-    for it, rows in enumerate([1, 7, 32, 32, 300, 512, 3, 3, 3]):
+    # rows <= 64: one-shot kernel; more: sequence-parallel kernel (odd counts split unevenly over ranks)
+    for it, rows in enumerate([1, 7, 32, 32, 300, 512, 3, 3, 3, 1000, 2048, 65, 2047]):
         x = torch.randn(rows, H, device=dev, generator=g).bfloat16()
         base = torch.randn(rows, H, device=dev, generator=torch.Generator(device=dev).manual_seed(it)).bfloat16()
         r1 = base.clone()
