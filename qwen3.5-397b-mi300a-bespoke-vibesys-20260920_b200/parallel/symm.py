@@ -18,7 +18,8 @@ import torch.distributed as dist
 
 from ..ops._ext import ext
 
-MAX_BLOCKS = 296  # two CTAs per SM on a 148-SM B200
+MAX_BLOCKS = 296  # one-shot kernel: two CTAs per SM on a 148-SM B200
+SP_MAX_BLOCKS = 296  # sequence-parallel kernel: one row per CTA; more CTAs measured slower
 
 
 class SymmComm:
@@ -26,7 +27,9 @@ class SymmComm:
     sequence-parallel region for prefill-sized ones (reduce-scatter + add + RMSNorm +
     all-gather, ``csrc/comm.cu``). Each family has its own slots, flags and device epoch."""
 
-    ONESHOT_MAX_ROWS = 64  # above this many rows the sequence-parallel kernel moves fewer bytes
+    # The one-shot kernel pulls (W - 1) x the message into every GPU in one phase; the sequence-
+    # parallel kernel moves ~3 (W - 1) / W x in three. One-shot while (W - 1) x rows stays small.
+    ONESHOT_ROW_BUDGET = 1024
 
     def __init__(self, rank: int, world: int, device, max_rows: int, hidden: int, group=None,
                  timeout_s: float = 10.0, bases: list[int] | None = None, sp_rows: int = 0,
@@ -52,7 +55,7 @@ class SymmComm:
     @staticmethod
     def sp_region_bytes(sp_rows: int, hidden: int) -> int:
         # two slots of [partial | result residual + normed] = 3 x rows x hidden bf16, then A and B flags
-        return 2 * 3 * sp_rows * hidden * 2 + 4 * MAX_BLOCKS * 4
+        return 2 * 3 * sp_rows * hidden * 2 + 4 * SP_MAX_BLOCKS * 4
 
     def _region(self, nbytes: int, group, bases):
         """Allocate and export this rank's region, map every peer's (or use given bases)."""
@@ -83,9 +86,9 @@ class SymmComm:
 
     def allreduce_add_rmsnorm(self, partial, residual, w1p, eps, kind: str = "auto"):
         """``residual += sum_ranks(partial)`` (in place) and returns (residual, rmsnorm(residual)).
-        One-shot kernel for up to ``ONESHOT_MAX_ROWS`` rows (one peer round trip), the
-        sequence-parallel kernel above that (``kind`` = "oneshot" / "sp" forces one); None when
-        the message fits neither region."""
+        One-shot kernel while ``rows * (world - 1)`` is within ``ONESHOT_ROW_BUDGET`` (one peer
+        round trip), the sequence-parallel kernel above that (``kind`` = "oneshot" / "sp" forces
+        one); None when the message fits neither region."""
         rows = residual.numel() // residual.shape[-1]
         normed = torch.empty_like(residual)
         fits_sp = self.sp_bases is not None and rows <= self.sp_rows
@@ -94,10 +97,10 @@ class SymmComm:
         elif kind == "oneshot":
             use_sp = False
         else:
-            use_sp = fits_sp and (rows > self.ONESHOT_MAX_ROWS or rows > self.max_rows)
+            use_sp = fits_sp and (rows > self.max_rows or rows * (self.world - 1) > self.ONESHOT_ROW_BUDGET)
         if use_sp:
             ext().symm_sp_ar_add_rmsnorm(self.sp_bases, self.rank, partial, residual, w1p, normed, float(eps),
-                                         self.sp_slot_elems, self.max_blocks, self.sp_epoch, self.timeout_s)
+                                         self.sp_slot_elems, SP_MAX_BLOCKS, self.sp_epoch, self.timeout_s)
             return residual, normed
         if rows > self.max_rows:
             return None

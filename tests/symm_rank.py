@@ -27,12 +27,14 @@ def main(rank, world, port):
     g = torch.Generator(device=dev).manual_seed(100 + rank)
     w = (1 + 0.1 * torch.randn(H, device=dev, generator=g)).float()
     dist.broadcast(w, 0)
-    # rows <= 64: one-shot kernel; more: sequence-parallel kernel (odd counts split unevenly over ranks)
-    for it, rows in enumerate([1, 7, 32, 32, 300, 512, 3, 3, 3, 1000, 2048, 65, 2047]):
+    # both kernels on every size they take (odd counts split unevenly over ranks)
+    cases = [(1, "auto"), (7, "auto"), (32, "auto"), (32, "sp"), (300, "oneshot"), (512, "auto"), (3, "sp"),
+             (3, "auto"), (1000, "auto"), (2048, "auto"), (65, "sp"), (2047, "sp")]
+    for it, (rows, kind) in enumerate(cases):
         x = torch.randn(rows, H, device=dev, generator=g).bfloat16()
         base = torch.randn(rows, H, device=dev, generator=torch.Generator(device=dev).manual_seed(it)).bfloat16()
         r1 = base.clone()
-        r1, n1 = s.allreduce_add_rmsnorm(x, r1, w, 1e-6)
+        r1, n1 = s.allreduce_add_rmsnorm(x, r1, w, 1e-6, kind=kind)
         y = x.float()
         dist.all_reduce(y)
         r2, n2 = ops.add_rmsnorm(y.bfloat16(), base.clone(), w, 1e-6)
