@@ -365,6 +365,12 @@ Tensor moe_routed_fp4(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13
   return moe_routed_impl(h, topw, topi, w13, s13, w2, s2, first, count);
 }
 
+void stamp(Tensor buf, int64_t slot) {
+  TORCH_CHECK(buf.is_cuda() && buf.scalar_type() == at::kLong, "stamp: int64 CUDA buffer");
+  TORCH_CHECK(slot >= 0 && slot < buf.numel(), "stamp: slot out of range");
+  LAUNCH(qb::stamp(reinterpret_cast<unsigned long long*>(buf.data_ptr<int64_t>()), (int)slot, stream()));
+}
+
 // ------------------------------------------------------------------ symmetric memory (IPC)
 // One cudaMalloc'd region per rank, exported with cudaIpcGetMemHandle and mapped by every peer.
 py::tuple symm_alloc(int64_t bytes) {
@@ -446,6 +452,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_varlen", &attention_varlen);
   m.def("attention_fa", &attention_fa);
   m.def("moe_routed_mx", &moe_routed_mx);
+  m.def("stamp", &stamp);
   m.def("gated_delta_chunked", &gated_delta_chunked);
   m.def("causal_conv_varlen", &causal_conv_varlen);
   m.def("gated_delta_varlen", &gated_delta_varlen);

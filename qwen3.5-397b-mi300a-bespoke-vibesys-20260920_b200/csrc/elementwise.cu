@@ -399,4 +399,14 @@ int router_topk(const void* logits, long ld, int T, int E, int k, float* w, int*
   return (int)cudaGetLastError();
 }
 
+// ------------------------------------------------------------------ clock stamp
+// One thread writes %globaltimer (ns) into buf[slot]: a stream-ordered timestamp that also works
+// inside a captured CUDA graph, where timing events cannot be recorded (in-graph attribution).
+__global__ void stamp_kernel(unsigned long long* buf, int slot) { buf[slot] = globaltimer(); }
+
+int stamp(unsigned long long* buf, int slot, cudaStream_t s) {
+  stamp_kernel<<<1, 1, 0, s>>>(buf, slot);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace qb

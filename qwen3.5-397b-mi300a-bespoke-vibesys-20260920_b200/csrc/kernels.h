@@ -53,6 +53,8 @@ int gated_delta_chunked(const void* qkv, long ldqkv, const void* ab, long ldab, 
                         const int* chunks, int n_chunks, const int* seg_chunk0, int S, int T, int nk, int nv, int dk,
                         int dv, float* scratch, void* out, bool commit, cudaStream_t s);
 long gated_delta_chunked_scratch(int T, int n_chunks, int nk, int nv, int dk);
+// in-graph clock stamp (elementwise.cu): buf[slot] = %globaltimer
+int stamp(unsigned long long* buf, int slot, cudaStream_t s);
 // block-scaled MoE (moe_mx.cu): token tile width, tile prefix, activation split, expert GEMM
 int mx_token_tile(int cap, int count);
 int mx_tile_prefix(const int* counts, int count, int BN, int* tstart, cudaStream_t s);

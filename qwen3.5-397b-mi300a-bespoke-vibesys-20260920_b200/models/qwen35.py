@@ -116,6 +116,7 @@ class Model:
         self._h2d = 0  # bytes copied host -> device for step inputs (bench accounting)
         self._d2h = 0  # bytes read back device -> host (sampled ids)
         self.gpu_marks = None  # list -> CUDA events at each input upload ("in") and result read ("out")
+        self.stamps = None  # utils.telemetry.Stamps -> in-graph clock stamps at layer boundaries
 
     def _gpu_mark(self, tag: str) -> None:
         """Stream-ordered event where a step's device work starts (input upload) or ends (the
@@ -124,6 +125,10 @@ class Model:
             ev = torch.cuda.Event(enable_timing=True)
             ev.record()
             self.gpu_marks.append((tag, ev))
+
+    def _stamp(self, tag: str) -> None:
+        if self.stamps is not None:
+            self.stamps.mark(tag)
 
     def io_bytes(self) -> tuple[int, int]:
         return self._h2d, self._d2h
@@ -304,17 +309,24 @@ class Model:
     def _layers(self, x: torch.Tensor, b: StepInputs) -> tuple[torch.Tensor, torch.Tensor]:
         cfg, comm, layers = self.cfg, self.comm, self.w["layers"]
         h = ops.rmsnorm(x, layers[0]["in_norm"], cfg.eps)
+        self._stamp("embed")
         for i, L in enumerate(layers):
-            mix = self._attention(i, L, h, b) if L["kind"] == FULL else self._deltanet(i, L, h, b)
+            full = L["kind"] == FULL
+            mix = self._attention(i, L, h, b) if full else self._deltanet(i, L, h, b)
+            self._stamp("attention" if full else "deltanet")
             x, h = comm.allreduce_add_rmsnorm(mix, x, L["post_norm"], cfg.eps)
+            self._stamp("allreduce")
             m = self._moe(L, h)
+            self._stamp("moe")
             nxt = layers[i + 1]["in_norm"] if i + 1 < len(layers) else self.w["final_norm"]
             x, h = comm.allreduce_add_rmsnorm(m, x, nxt, cfg.eps)
+            self._stamp("allreduce")
         return x, h
 
     def _forward(self, b: StepInputs) -> torch.Tensor:
         """Runs every layer over the batch; returns the final-normed hidden of the logit rows and
         keeps the matching pre-norm residual in ``last_hidden`` (the MTP seed)."""
+        self._stamp("start")
         x = ops.embed(b.tokens, self.w["embed"])
         x, h = self._layers(x, b)
         self.last_hidden = x.index_select(0, b.logit_rows)
@@ -324,7 +336,9 @@ class Model:
     def logits(self, h: torch.Tensor) -> torch.Tensor:
         """Full-vocab logits [R, V] (vocab-parallel GEMM, then all-gathered over ranks)."""
         local = ops.linear(h, self.w["lm_head"])
-        return self.comm.all_gather_last(local)
+        out = self.comm.all_gather_last(local)
+        self._stamp("lm_head")
+        return out
 
     # ================================================================== Runner: forwards
     @torch.inference_mode()

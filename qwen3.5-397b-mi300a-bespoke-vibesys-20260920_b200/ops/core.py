@@ -12,13 +12,14 @@ lane. ``rows[t]`` is the physical paged-KV row of token ``t``.
 
 from __future__ import annotations
 
-import os
+import time
 
 import torch
 import torch.nn.functional as F
 
 from . import reference as ref
 from ._ext import ext
+from ..utils import flags
 
 
 def _cuda(x: torch.Tensor) -> bool:
@@ -78,6 +79,15 @@ def argmax_rows(logits):
         return ext().argmax_rows(logits)
     v, i = logits.float().max(dim=-1)
     return v, i
+
+
+def stamp(buf: torch.Tensor, slot: int) -> None:
+    """``buf[slot]`` = the device clock (ns, ``%globaltimer``) when the stream reaches this point;
+    a one-thread kernel, so it can sit inside a captured CUDA graph. On CPU: the host clock."""
+    if _cuda(buf):
+        ext().stamp(buf, slot)
+    else:
+        buf[slot] = time.perf_counter_ns()
 
 
 # ----------------------------------------------------------------------------- deltanet
@@ -194,7 +204,7 @@ def dn_chunk_plan(cu_h, dk, dv, device):
     as the token recurrence (it buys parallelism, not work), and measured slower than the
     latency-tuned token kernel; it serves as the exact fp32 formulation for a tensor-core
     version. Only batches whose longest segment reaches a chunk, and head size 128."""
-    if cu_h is None or dk != 128 or dv != 128 or os.environ.get("QB_DN_CHUNKED", "0") != "1":
+    if cu_h is None or dk != 128 or dv != 128 or not flags.get("QB_DN_CHUNKED"):
         return None
     lens = [cu_h[i + 1] - cu_h[i] for i in range(len(cu_h) - 1)]
     if not lens or max(lens) < DN_CHUNK_MIN:
@@ -227,7 +237,7 @@ def fa_plan(q, k_cache, cu_h, block_size, max_ctx):
     tile's key range is split so that one wave covers the GPU; the partials are merged by a
     second kernel. The tile tensor is cached per (segments, G): a CUDA-graph capture then reads a
     persistent device tensor instead of recording a copy from a temporary host buffer."""
-    if cu_h is None or block_size != 16 or os.environ.get("QB_FA", "1") == "0":
+    if cu_h is None or block_size != 16 or not flags.get("QB_FA"):
         return None
     g = q.shape[1] // k_cache.shape[1]
     if 128 % g or q.shape[2] not in (64, 128, 256) or len(cu_h) < 2:
@@ -304,7 +314,7 @@ def prepare_experts(experts: dict, keep_rows: bool = False) -> dict:
 
 def moe_impl() -> str:
     """``mx`` (block-scaled MMA, default) or ``f16`` (codes decoded to f16 by the converter warps)."""
-    return os.environ.get("QB_MOE_IMPL", "mx")
+    return flags.get("QB_MOE_IMPL")
 
 
 def moe_routed(h, topw, topi, experts, first, count):

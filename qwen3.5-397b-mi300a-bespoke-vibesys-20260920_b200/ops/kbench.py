@@ -186,7 +186,7 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
     from ..serving.engine import PoolSpec, build_model
 
     dev = torch.device("cuda", 0)
-    spec = PoolSpec(lanes=lanes, max_seq=16384, kv_tokens=lanes * 9600, snapshots=8)
+    spec = PoolSpec(lanes=lanes + 1, max_seq=16384, kv_tokens=(lanes + 1) * 9600, snapshots=8)  # + pad lane
     m, _ = build_model("full", 0, 1, dev, spec, graphs=False)
     per = 600
     for lane in range(lanes):
@@ -217,6 +217,22 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
                "ms": round(ms, 2), "kernels": [(k, n, round(t / tot, 3)) for k, (n, t) in top]}
         print(json.dumps(row), flush=True)
         res[f.__name__] = row
+    # the same decode step replayed from a CUDA graph, and its per-part device time from clock
+    # stamps inside a separate diagnostic capture
+    from ..serving.graphs import GraphRunner
+
+    g = GraphRunner(m, buckets=(lanes,))
+    g.prepare()
+    pos = [max(ctx, 2048) + lane for lane in range(lanes)]
+    ms = _time(lambda: g.decode(list(range(lanes)), [5] * lanes, pos), 5)
+    att = g.attribution(lanes, replays=5)
+    tot = att.get("total", 0.0) or 1.0
+    row = {"case": "model_decode_graph", "lanes": lanes, "ctx": max(ctx, 2048), "ms": round(ms, 2),
+           "parts_ms": {k: round(v, 3) for k, v in sorted(att.items())},
+           "parts_share": {k: round(v / tot, 3) for k, v in sorted(att.items()) if k != "total"}}
+    print(json.dumps(row), flush=True)
+    res["decode_graph"] = row
+    g.release()
     return res
 
 

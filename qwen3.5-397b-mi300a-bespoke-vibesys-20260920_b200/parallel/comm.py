@@ -23,6 +23,7 @@ import torch
 import torch.distributed as dist
 
 from ..ops import core as ops
+from ..utils import flags
 
 
 def env_rank_world() -> tuple[int, int, int]:
@@ -44,6 +45,11 @@ def init(backend: str | None = None, rank: int | None = None, world: int | None 
         backend = "nccl" if torch.cuda.is_available() else "gloo"
     if backend == "nccl":
         torch.cuda.set_device(local)
+        from ..utils.hostinfo import apply_for_device
+
+        note = apply_for_device(local)  # host threads and pages next to this rank's GPU
+        if note:
+            print(f"[host-numa] rank {rank}: {note}", flush=True)
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     os.environ.setdefault("MASTER_PORT", "29500")
     kw = {}
@@ -61,7 +67,7 @@ class Comm:
         self.rank, self.world, self.group = rank, world, group
         self.device = device
         self.symm = symm  # parallel.symm.SymmComm for the fused CUDA kernels, or None
-        self.mode = os.environ.get("QB_COMM", "fused")
+        self.mode = flags.get("QB_COMM")
 
     # ------------------------------------------------------------------ primitives
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:

@@ -71,11 +71,11 @@ class Channel:
 def open_channel(world: int, rank: int, group, device_type: str = "cuda"):
     """The command channel for this node: the shared-memory ring (``QB_CMD_CHANNEL=shm``, the
     default) or the gloo broadcast channel (``gloo``). Every rank must call this."""
-    import os
+    from ..utils import flags
 
     if world <= 1:
         return None
-    if os.environ.get("QB_CMD_CHANNEL", "shm") == "shm":
+    if flags.get("QB_CMD_CHANNEL") == "shm":
         from .shm_channel import make_channel
 
         ch = make_channel(world, rank, group)
@@ -246,8 +246,10 @@ class Broadcaster:
 
 def pool_signature(model) -> str:
     """Hash of everything that must agree across ranks for the protocol to stay in lockstep."""
+    from ..utils import flags
+
     d = (model.cfg.to_json(), model.max_batch, model.max_seq, model.block_size, model.num_blocks,
-         model.num_snapshots, model.plan.world)
+         model.num_snapshots, model.plan.world, flags.signature())
     return hashlib.sha1(repr(d).encode()).hexdigest()
 
 

@@ -18,6 +18,7 @@ from ..models.qwen35 import Model
 from ..models.weights import expert_bytes_per_layer, load_weights, random_weights
 from ..parallel.comm import Comm
 from ..parallel.plan import plan
+from ..utils import flags, memtimeline
 
 
 @dataclass
@@ -47,7 +48,11 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
     result is wrapped in a ``GraphRunner`` (captured decode buckets) unless ``graphs=False``;
     every rank must call this in the same order, since capture runs the collectives."""
     if graphs is None:
-        graphs = device.type == "cuda" and __import__("os").environ.get("QB_GRAPHS", "1") != "0"
+        graphs = device.type == "cuda" and flags.get("QB_GRAPHS")
+    if device.type == "cuda":
+        memtimeline.set_rank(rank)
+        memtimeline.preflight()
+        memtimeline.mark("start", device)
     if model in ("full", "tiny"):
         cfg = full_config() if model == "full" else tiny_config()
     else:
@@ -65,22 +70,29 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
         w = random_weights(cfg, p, device, dtype, seed=seed, with_mtp=with_mtp, distinct_expert_layers=distinct)
     else:
         w = load_weights(model, cfg, p, device, dtype, with_mtp=with_mtp)
+    memtimeline.mark("weights", device)
     if comm is None:
         comm = Comm(rank, world, None, device)
         if world > 1 and device.type == "cuda" and comm.mode == "fused":
             from ..parallel.symm import SymmComm
 
-            env = __import__("os").environ
-            rows = int(env.get("QB_SYMM_MAX_ROWS", "512"))
-            sp_rows = int(env.get("QB_SP_MAX_ROWS", "4096"))  # prefill-sized messages: sequence-parallel kernel
+            rows = flags.get("QB_SYMM_MAX_ROWS")
+            sp_rows = flags.get("QB_SP_MAX_ROWS")  # prefill-sized messages: sequence-parallel kernel
             comm.symm = SymmComm(rank, world, device, max_rows=rows, hidden=cfg.hidden, sp_rows=sp_rows)
     m = Model(cfg, w, p, comm, device=device, dtype=dtype,
               max_batch=spec.lanes + (1 if graphs else 0), max_seq=spec.max_seq, block_size=spec.block_size,
               num_blocks=num_blocks, num_snapshots=spec.snapshots or 2 * spec.lanes + 16)
+    memtimeline.mark("pools", device)
+    if device.type == "cuda" and flags.get("QB_RANK_BW_PROBE"):
+        from ..utils.hostinfo import probe
+
+        probe(rank, device)
     if graphs:
         from .graphs import GraphRunner
 
         g = GraphRunner(m)
         g.prepare()
+        memtimeline.report(g, device)
         return g, distinct
+    memtimeline.report(m, device)
     return m, distinct

@@ -15,11 +15,11 @@ Reference behaviour: ``graph_decode.py:250-1725`` (``DEFAULT_BUCKET_SIZES``, ``G
 
 from __future__ import annotations
 
-import os
 
 import torch
 
 from ..models.qwen35 import StepInputs
+from ..utils import flags
 
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
 
@@ -62,7 +62,7 @@ class GraphRunner:
             self.buckets.append(lim)
         self.pool = torch.cuda.graph_pool_handle()
         self._b = {}
-        self.enabled = os.environ.get("QB_GRAPHS", "1") != "0"
+        self.enabled = flags.get("QB_GRAPHS")
         self.replays = 0
         self.launch_per_replay: dict[int, int] = {}
 
@@ -120,6 +120,41 @@ class GraphRunner:
             bk.graph = g
             self._b[B] = bk
         torch.cuda.synchronize()
+
+    def attribution(self, B: int, replays: int = 10) -> dict[str, float]:
+        """Device time per layer part (ms) of one captured ``B``-row decode step.
+
+        Captures a separate diagnostic graph of the bucket with clock stamps between the layer
+        parts (``utils.telemetry.Stamps``), replays it ``replays`` times and reads the stamps of
+        the last replay; the serving graphs never contain a stamp. Every rank must call this
+        (the capture runs the collectives). Reference behaviour: ``decode_stamps.py`` with its
+        separate diagnostic capture."""
+        from ..utils.telemetry import Stamps
+
+        m = self.model
+        bk = _Bucket(m, B, None)
+        self._fill(bk, [], [], [])
+        st = Stamps(m.device)
+        m.stamps = st
+        try:
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.inference_mode(), torch.cuda.stream(s):
+                self._run(bk)
+            torch.cuda.current_stream().wait_stream(s)
+            torch.cuda.synchronize()
+            st.reset()
+            g = torch.cuda.CUDAGraph()
+            with torch.inference_mode(), torch.cuda.graph(g):
+                self._run(bk)
+        finally:
+            m.stamps = None
+        for _ in range(replays):
+            g.replay()
+        torch.cuda.synchronize()
+        out = st.by_tag_ms()
+        del g
+        return out
 
     def release(self) -> None:
         """Drop the graphs (before destroy_process_group: they hold NCCL work)."""

@@ -32,6 +32,8 @@ import uuid
 
 import torch
 
+from ..utils import flags
+
 
 def parse(argv=None):
     ap = argparse.ArgumentParser()
@@ -326,7 +328,7 @@ def make_app(engine: Engine):
 
     @routes.post("/debug/fault")
     async def fault(request):
-        if os.environ.get("QB_FAULT_ENDPOINT", "0") != "1":
+        if not flags.get("QB_FAULT_ENDPOINT"):
             return web.json_response({"error": {"message": "fault endpoint disabled"}}, status=404)
         body = await request.json()
         from .faults import FAULTS

@@ -1,0 +1,120 @@
+"""Typed registry of every ``QB_*`` environment flag the framework reads.
+
+Each flag is declared once with its type, default and meaning; code reads it through ``get``
+(Python) or ``getenv`` (the CUDA launchers, marked ``native``). ``snapshot()`` returns the values
+of the flags that must agree across ranks (they change a kernel's numerics, which collective runs
+at a given size, or which steps are captured), and ``signature()`` hashes them: the multi-rank
+driver folds that hash into its pool signature, so ranks started with different flags refuse to
+run together instead of computing different numbers or waiting in different collectives.
+
+Reference behaviour: the reference reads ``SEED_*`` variables ad hoc across its modules
+(``mem_timeline.py:22``, ``host_numa.py:13``, ``step_timing.py``); here they are declared in one
+place so a test can check that no module reads an undeclared name.
+"""
+
+from __future__ import annotations
+
+import hashlib
+import json
+import os
+from dataclasses import dataclass
+
+
+@dataclass(frozen=True)
+class Flag:
+    name: str
+    kind: type  # bool, int, float or str
+    default: object
+    doc: str
+    lockstep: bool = False  # must agree across ranks: part of the pool signature
+    native: bool = False  # read by the C++/CUDA side with getenv
+
+
+_FLAGS: dict[str, Flag] = {}
+
+
+def _def(name, kind, default, doc, lockstep=False, native=False) -> None:
+    _FLAGS[name] = Flag(name, kind, default, doc, lockstep, native)
+
+
+# ---- kernels and numerics
+_def("QB_MOE_IMPL", str, "mx", "routed-expert kernel: mx (block-scaled fp8 tcgen05), f16 (fp4 decoded to "
+     "f16 in TMEM), bf16 (dequantised weights)", lockstep=True)
+_def("QB_MX_BN_MAX", int, 64, "largest token tile of the block-scaled MoE kernel", native=True)
+_def("QB_MOE_BN_MAX", int, 64, "largest token tile of the f16-decode MoE kernel", native=True)
+_def("QB_MOE_SMEM_A", bool, False, "f16-decode MoE: stage decoded weights in shared memory", native=True)
+_def("QB_FA", bool, True, "tcgen05 flash attention for full-attention layers (else the CUDA-core kernel)",
+     lockstep=True)
+_def("QB_DN_CHUNKED", bool, False, "chunked (WY) DeltaNet prefill instead of the token recurrence",
+     lockstep=True)
+_def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
+# ---- collectives and multi-rank plumbing
+_def("QB_COMM", str, "fused", "tensor-parallel all-reduce: fused (peer-memory kernels) or nccl", lockstep=True)
+_def("QB_SYMM_MAX_ROWS", int, 512, "rows of the one-shot fused all-reduce buffers", lockstep=True)
+_def("QB_SP_MAX_ROWS", int, 4096, "rows of the sequence-parallel fused all-reduce buffers (0: off)",
+     lockstep=True)
+_def("QB_CMD_CHANNEL", str, "shm", "leader -> worker command channel: shm (shared-memory ring) or gloo (broadcast)",
+     lockstep=True)
+# ---- diagnostics (off by default; none of them changes a number)
+_def("QB_STEP_TIMING", int, 0, "log a [step-timing] line every n scheduler steps (0: off)")
+_def("QB_SERVICE_TRACE", str, "", "append one JSON record per scheduler step to this path")
+_def("QB_STAMPS", bool, False, "in-graph %globaltimer stamps at layer boundaries")
+_def("QB_MEM_TIMELINE", bool, False, "print a [mem] line at each boot phase and a [mem-cls] report")
+_def("QB_MEM_TIMELINE_DIR", str, "", "also write every allocator segment of the timeline as JSON here")
+_def("QB_BOOT_MEM_PREFLIGHT_GIB", float, 0.0, "before boot, wait until the device has this much free memory")
+_def("QB_BOOT_MEM_PREFLIGHT_WAIT_S", float, 300.0, "how long the preflight waits before it fails")
+_def("QB_RANK_BW_PROBE", bool, False, "print a [rank-bw] line (HBM read and pinned copy bandwidth) at boot",
+     lockstep=True)
+_def("QB_HOST_CPU_NODES", str, "", "run this process's threads on these NUMA nodes' CPUs (auto: the GPU's node)")
+_def("QB_HOST_MEM_NODES", str, "", "interleave this process's host pages over these NUMA nodes (auto: the GPU's)")
+_def("QB_FAULT_ENDPOINT", bool, False, "expose POST /debug/fault (accuracy-gate calibration faults)")
+
+
+def registry() -> dict[str, Flag]:
+    return dict(_FLAGS)
+
+
+def _parse(f: Flag, raw: str):
+    if f.kind is bool:
+        return raw.strip().lower() in ("1", "true", "yes", "on")
+    if f.kind is int:
+        return int(raw)
+    if f.kind is float:
+        return float(raw)
+    return raw
+
+
+def get(name: str, env: dict | None = None):
+    """The flag's value from ``env`` (default ``os.environ``), parsed to its type; its default
+    when unset or empty. Reading an undeclared name is an error."""
+    f = _FLAGS.get(name)
+    if f is None:
+        raise KeyError(f"undeclared flag {name}")
+    raw = (os.environ if env is None else env).get(name)
+    if raw is None or raw == "":
+        return f.default
+    try:
+        return _parse(f, raw)
+    except ValueError as e:
+        raise ValueError(f"{name}={raw!r}: expected {f.kind.__name__}") from e
+
+
+def snapshot(env: dict | None = None, numerics_only: bool = True) -> dict:
+    return {n: get(n, env) for n, f in sorted(_FLAGS.items()) if f.lockstep or not numerics_only}
+
+
+def signature(env: dict | None = None) -> str:
+    return hashlib.sha256(json.dumps(snapshot(env), sort_keys=True).encode()).hexdigest()[:16]
+
+
+def describe() -> str:
+    """One line per flag: name, type, default, meaning (``python -m ... utils.flags``)."""
+    rows = []
+    for f in sorted(_FLAGS.values(), key=lambda f: f.name):
+        tag = " [native]" if f.native else ""
+        rows.append(f"{f.name:30s} {f.kind.__name__:5s} default={f.default!r:8s} {f.doc}{tag}")
+    return "\n".join(rows)
+
+
+if __name__ == "__main__":
+    print(describe())

@@ -15,18 +15,19 @@ import threading
 import time
 from collections import defaultdict
 
+from . import flags
+
 
 class StepTimer:
     """Per-kind rolling windows of host wall time per scheduler step."""
 
     def __init__(self, every: int | None = None, sink=print) -> None:
-        env = os.environ.get("QB_STEP_TIMING", "0")
-        self.every = every if every is not None else (int(env) if env.isdigit() else 0)
+        self.every = every if every is not None else flags.get("QB_STEP_TIMING")
         self.sink = sink
         self.win: dict[str, list[tuple[int, float]]] = defaultdict(list)
         self.total: dict[str, list[float]] = defaultdict(lambda: [0, 0.0, 0])
         self.n = 0
-        trace = os.environ.get("QB_SERVICE_TRACE")
+        trace = flags.get("QB_SERVICE_TRACE")
         self.trace = ServiceTrace(trace) if trace else None
 
     def record(self, kind: str, tokens: int, seconds: float) -> None:
@@ -95,3 +96,47 @@ class GapMeter:
         for (a0, a1), (b0, _) in zip(self.events, self.events[1:]):
             out.append(a1.elapsed_time(b0))
         return out
+
+
+class Stamps:
+    """In-graph clock stamps: ``mark(tag)`` ends the current segment of the stream as ``tag``.
+
+    Each mark launches a one-thread kernel that writes ``%globaltimer`` (ns) into its slot of a
+    device buffer. Timing events cannot be recorded inside a captured CUDA graph; a stamp can,
+    and on one stream it runs after the previous kernel has finished, so the difference between
+    consecutive stamps is the stream time of the segment that ended at the later one. Slots are
+    assigned at record time, so a captured graph rewrites the same slots on every replay and
+    ``segments_ms`` reads the latest replay. Reference behaviour: ``decode_stamps.py:43-76``
+    (``Recorder``, ``mark``, ``segments_ms``), there with the 100 MHz ``s_memrealtime`` counter.
+    """
+
+    def __init__(self, device, capacity: int = 4096) -> None:
+        import torch
+
+        self.buf = torch.zeros(capacity, dtype=torch.int64, device=device)
+        self.tags: list[str] = []
+
+    def mark(self, tag: str) -> None:
+        from ..ops import core as ops
+
+        k = len(self.tags)
+        if k >= self.buf.numel():
+            raise RuntimeError("Stamps: capacity exceeded")
+        self.tags.append(tag)
+        ops.stamp(self.buf, k)
+
+    def reset(self) -> None:
+        self.tags = []
+
+    def segments_ms(self) -> list[tuple[str, float]]:
+        """``(tag, ms)`` per segment: the time from the previous stamp to this one."""
+        t = self.buf[: len(self.tags)].tolist()
+        return [(self.tags[k], (t[k] - t[k - 1]) * 1e-6) for k in range(1, len(self.tags))]
+
+    def by_tag_ms(self) -> dict[str, float]:
+        """Segment times summed per tag, plus ``total`` (first stamp to last)."""
+        out: dict[str, float] = defaultdict(float)
+        for tag, ms in self.segments_ms():
+            out[tag] += ms
+        out["total"] = sum(ms for _, ms in self.segments_ms())
+        return dict(out)

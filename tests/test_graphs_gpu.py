@@ -36,3 +36,61 @@ def test_graph_decode_matches_eager():
         toks = a.argmax(-1).tolist()
         pos = [x + 1 for x in pos]
     assert g.replays == 3
+
+
+def test_stamps_inside_captured_graph():
+    """%globaltimer stamps recorded inside a CUDA graph: segments are positive and their sum is
+    the replay's device time (CUDA events around the replay)."""
+    from qwen35_b200.utils.telemetry import Stamps
+
+    dev = torch.device("cuda")
+    a = torch.randn(2048, 2048, device=dev, dtype=torch.bfloat16)
+    st = Stamps(dev, capacity=16)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        (a @ a).sum()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        st.mark("start")
+        b = a @ a
+        st.mark("gemm")
+        for _ in range(8):
+            b = b * 1.0001
+        st.mark("elementwise")
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for _ in range(3):
+        g.replay()
+    e0.record()
+    g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    seg = dict(st.segments_ms())
+    assert seg["gemm"] > 0 and seg["elementwise"] > 0
+    total = st.by_tag_ms()["total"]
+    assert total <= e0.elapsed_time(e1) * 1.05 + 0.01
+
+
+def test_graph_attribution_tiny():
+    from qwen35_b200.models.config import tiny_config
+    from qwen35_b200.models.qwen35 import Model
+    from qwen35_b200.models.weights import random_weights
+    from qwen35_b200.parallel.plan import plan
+    from qwen35_b200.serving.graphs import GraphRunner
+
+    dev = torch.device("cuda")
+    cfg = tiny_config()
+    p = plan(cfg, 0, 1)
+    m = Model(cfg, random_weights(cfg, p, dev, torch.bfloat16, seed=1, with_mtp=False), p, device=dev,
+              max_batch=5, max_seq=512)
+    g = GraphRunner(m, buckets=(1, 4))
+    g.prepare()
+    att = g.attribution(4, replays=3)
+    assert m.stamps is None
+    for k in ("moe", "allreduce", "lm_head", "total"):
+        assert k in att and att[k] >= 0
+    assert att["total"] > 0
+    parts = sum(v for k, v in att.items() if k != "total")
+    assert abs(parts - att["total"]) < 1e-6 + 1e-6 * att["total"]

@@ -1,0 +1,151 @@
+"""Flag registry, host NUMA placement, memory preflight and clock stamps (CPU parts)."""
+
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from qwen35_b200.utils import flags, hostinfo, memtimeline
+from qwen35_b200.utils.telemetry import Stamps
+
+PKG = Path(__file__).resolve().parent.parent / "qwen3.5-397b-mi300a-bespoke-vibesys-20260920_b200"
+
+
+def _sources(*suffixes):
+    return [p for p in PKG.rglob("*") if p.suffix in suffixes and "_build" not in p.parts]
+
+
+def test_every_python_flag_read_is_declared():
+    reg = flags.registry()
+    for p in _sources(".py"):
+        text = p.read_text()
+        for name in re.findall(r'flags\.get\("(QB_[A-Z0-9_]+)"', text):
+            assert name in reg, (p.name, name)
+        if p.name != "flags.py":
+            # QB_* variables are read through the registry only
+            assert not re.search(r'environ(?:\.get)?[\[(]\s*"QB_', text), p.name
+            assert not re.search(r'getenv\(\s*"QB_', text), p.name
+
+
+def test_every_native_flag_read_is_declared():
+    reg = flags.registry()
+    seen = set()
+    for p in _sources(".cu", ".cpp", ".h", ".cuh"):
+        for name in re.findall(r'getenv\("(QB_[A-Z0-9_]+)"\)', p.read_text()):
+            seen.add(name)
+            assert name in reg and reg[name].native, (p.name, name)
+    assert seen == {n for n, f in reg.items() if f.native}
+
+
+def test_flag_parsing_and_signature():
+    assert flags.get("QB_GRAPHS", {}) is True
+    assert flags.get("QB_GRAPHS", {"QB_GRAPHS": "0"}) is False
+    assert flags.get("QB_SP_MAX_ROWS", {"QB_SP_MAX_ROWS": "128"}) == 128
+    assert flags.get("QB_SP_MAX_ROWS", {"QB_SP_MAX_ROWS": ""}) == 4096
+    with pytest.raises(ValueError):
+        flags.get("QB_SP_MAX_ROWS", {"QB_SP_MAX_ROWS": "many"})
+    with pytest.raises(KeyError):
+        flags.get("QB_NOT_A_FLAG", {})
+    base = flags.signature({})
+    assert flags.signature({"QB_STEP_TIMING": "5"}) == base  # diagnostics do not enter it
+    assert flags.signature({"QB_COMM": "nccl"}) != base
+    assert flags.signature({"QB_MOE_IMPL": "f16"}) != base
+    assert "QB_MOE_IMPL" in flags.describe()
+
+
+def test_parse_nodes_and_node_cpus(tmp_path):
+    assert hostinfo.parse_nodes("") == []
+    assert hostinfo.parse_nodes("1,2,3") == [1, 2, 3]
+    assert hostinfo.parse_nodes("3,1-2, 2") == [1, 2, 3]
+    (tmp_path / "node1").mkdir()
+    (tmp_path / "node1" / "cpulist").write_text("24-26,120\n")
+    assert hostinfo.node_cpus(1, root=tmp_path) == {24, 25, 26, 120}
+
+
+def test_gpu_numa_node_from_sysfs(tmp_path):
+    d = tmp_path / "0000:1b:00.0"
+    d.mkdir()
+    (d / "numa_node").write_text("1\n")
+    assert hostinfo.gpu_numa_node("0000:1B:00.0", root=tmp_path) == 1
+    assert hostinfo.gpu_numa_node("0000:99:00.0", root=tmp_path) == -1
+
+
+def test_apply_placement_with_fakes(tmp_path):
+    for n, cpus in ((0, "0-3"), (1, "4-7")):
+        (tmp_path / f"node{n}").mkdir()
+        (tmp_path / f"node{n}" / "cpulist").write_text(cpus)
+    calls = {}
+
+    def aff(pid, cpus):
+        calls["cpus"] = cpus
+
+    def pol(nodes):
+        calls["mem"] = nodes
+
+    assert hostinfo.apply({}, 1, tmp_path, aff, pol) == ""
+    assert not calls
+    note = hostinfo.apply({"QB_HOST_CPU_NODES": "auto", "QB_HOST_MEM_NODES": "auto"}, 1, tmp_path, aff, pol)
+    assert calls == {"cpus": {4, 5, 6, 7}, "mem": [1]} and "mem_bind=[1]" in note
+    calls.clear()
+    note = hostinfo.apply({"QB_HOST_MEM_NODES": "0-1"}, -1, tmp_path, aff, pol)
+    assert calls == {"mem": [0, 1]} and "mem_interleave" in note
+    calls.clear()
+    # auto with an unknown GPU node does nothing
+    assert hostinfo.apply({"QB_HOST_CPU_NODES": "auto"}, -1, tmp_path, aff, pol) == "" and not calls
+
+
+def test_node_meminfo(tmp_path):
+    (tmp_path / "node0").mkdir()
+    (tmp_path / "node0" / "meminfo").write_text(
+        "Node 0 MemTotal:       1048576 kB\nNode 0 MemFree:         524288 kB\nNode 0 MemUsed:  524288 kB\n")
+    assert hostinfo.node_meminfo_gib(tmp_path) == {"node0": {"MemFree": 0.5, "MemUsed": 0.5}}
+
+
+def test_preflight_waits_then_fails_or_passes():
+    t = [0.0]
+    free = iter([10.0, 20.0, 60.0])
+    logs = []
+    memtimeline.preflight(50.0, 30.0, read=lambda: next(free), sleep=lambda s: t.__setitem__(0, t[0] + s),
+                          clock=lambda: t[0], sink=logs.append)
+    assert logs and "ok" in logs[0]
+    with pytest.raises(RuntimeError, match="another process"):
+        memtimeline.preflight(50.0, 5.0, read=lambda: 1.0, sleep=lambda s: t.__setitem__(0, t[0] + s),
+                              clock=lambda: t[0], sink=logs.append)
+    memtimeline.preflight(0.0, 5.0, read=lambda: 0.0)  # off: returns at once
+
+
+def test_mem_timeline_is_off_by_default():
+    assert memtimeline.mark("x", torch.device("cpu")) is None
+
+
+def test_stamps_on_cpu():
+    st = Stamps(torch.device("cpu"), capacity=8)
+    for tag in ("start", "a", "b", "a"):
+        st.mark(tag)
+    seg = st.segments_ms()
+    assert [t for t, _ in seg] == ["a", "b", "a"] and all(ms >= 0 for _, ms in seg)
+    agg = st.by_tag_ms()
+    assert set(agg) == {"a", "b", "total"}
+    assert abs(agg["total"] - sum(ms for _, ms in seg)) < 1e-9
+    for _ in range(4):
+        st.mark("x")
+    with pytest.raises(RuntimeError):
+        st.mark("overflow")
+
+
+def test_model_stamps_on_cpu():
+    """A tiny CPU model step with stamps installed tags every layer part once per layer."""
+    from qwen35_b200.serving.engine import PoolSpec, build_model
+
+    m, _ = build_model("tiny", 0, 1, torch.device("cpu"), PoolSpec(lanes=2, max_seq=64, kv_tokens=128),
+                       dtype=torch.float32, graphs=False)
+    m.begin(0)
+    m.attach_blocks(0, [1, 2])
+    m.stamps = Stamps(torch.device("cpu"))
+    m.forward([(0, [1, 2, 3], 0)])
+    tags = m.stamps.tags
+    n = m.cfg.layers
+    assert tags[0] == "start" and tags[-1] == "lm_head"
+    assert tags.count("moe") == n and tags.count("allreduce") == 2 * n
+    assert tags.count("attention") + tags.count("deltanet") == n
