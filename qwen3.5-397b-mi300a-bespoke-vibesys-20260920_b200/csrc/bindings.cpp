@@ -2,6 +2,7 @@
 // allocates outputs and scratch through the PyTorch caching allocator (so calls are
 // CUDA-graph capturable), and launches on the current stream. Launch failures raise.
 #include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGraphsC10Utils.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
@@ -45,6 +46,25 @@ int* err_ptr(const Tensor& like) { return status_tensor(like.device()).data_ptr<
 long row_stride(const Tensor& t) { return t.dim() >= 2 ? t.stride(0) : t.size(-1); }
 
 // ------------------------------------------------------------------ dense
+// Stream-K arrival counters: one zeroed array per device, re-armed to zero by the kernel itself,
+// so a GEMM (eager or replayed from a graph) needs no memset. GEMMs of one device run on one
+// stream in this engine; the array is made on the first call outside a graph capture (the graph
+// runner's warm-up), and a call that meets a capture first gets a zeroed array of its own.
+Tensor gemm_counters(const Tensor& like, long n) {
+  static std::mutex mu;
+  static std::unordered_map<int, Tensor> per_dev;
+  constexpr long kCounters = 1 << 15;
+  const int dev = like.get_device();
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = per_dev.find(dev);
+  if (it != per_dev.end() && n <= kCounters) return it->second;
+  const bool capturing = c10::cuda::currentStreamCaptureStatusMayInitCtx() != c10::cuda::CaptureStatus::None;
+  if (capturing || n > kCounters) return at::zeros({n}, like.options().dtype(at::kInt));
+  Tensor t = at::zeros({kCounters}, like.options().dtype(at::kInt));
+  per_dev[dev] = t;
+  return t;
+}
+
 Tensor linear(Tensor x, Tensor w, c10::optional<Tensor> out) {
   CHECK_CUDA(x);
   CHECK_CUDA(w);
@@ -57,12 +77,12 @@ Tensor linear(Tensor x, Tensor w, c10::optional<Tensor> out) {
   Tensor y = out.has_value() ? *out : at::empty({T, N}, x.options());
   TORCH_CHECK(y.stride(1) == 1, "linear: output inner dim must be contiguous");
   TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "linear: row strides must be 16B multiples");
-  // split-K workspace when the output has too few tiles to occupy the SMs (decode projections)
+  // stream-K workspace when the tiles do not divide evenly over the SMs (decode projections)
   const long wsf = qb::gemm_split_ws_floats(T, N, K);
   Tensor ws, cnt;
   if (wsf) {
     ws = at::empty({wsf}, x.options().dtype(at::kFloat));
-    cnt = at::zeros({(long)((N + 127) / 128) * ((T + 15) / 16)}, x.options().dtype(at::kInt));
+    cnt = gemm_counters(x, (long)((N + 127) / 128) * ((T + 15) / 16));
   }
   LAUNCH(qb::gemm_ws(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(), y.stride(0), T, N, K, bf, 0,
                      err_ptr(x), stream(), 0, wsf ? ws.data_ptr<float>() : nullptr,

@@ -12,14 +12,19 @@
 // The accumulator is double buffered in TMEM (2 x BN columns), so the epilogue of one tile
 // overlaps the MMAs of the next. All waits are bounded (see common.cuh).
 //
-// Split-K: when the output has too few 128-row tiles to occupy the SMs (decode projections with
-// N = 4096 are 32 tiles), each tile's K range is split over `splits` work units. A unit writes
-// its fp32 partial tile to a workspace and bumps the tile's counter; the unit that arrives last
-// adds the partials and runs the normal epilogue (activation included), then re-arms the
-// counter for the next call.
+// Stream-K for decode shapes (token tile <= 64): when the output's 128-row tiles do not divide
+// evenly over the CTAs (N = 4096 projections are 32 tiles, N = 20608 is 161), every CTA takes an
+// equal contiguous share of the (tile, K-block) space instead of whole tiles. A CTA's first and
+// last segment may cover part of a tile's K range: it writes that fp32 partial to its own
+// workspace slot and bumps the tile's counter (one releasing thread after a barrier); the CTA
+// that arrives last adds the tile's partials (a handful, loaded two at a time) and runs the
+// normal epilogue, then re-arms the counter. Segments in between cover whole tiles and take the
+// normal epilogue directly.
 #include "common.cuh"
 #include "kernels.h"
 #include <cudaTypedefs.h>
+
+#include <algorithm>
 
 namespace qb {
 
@@ -43,10 +48,46 @@ struct GemmArgs {
   int T, N, K;
   int act;  // 0: none, 1: silu(g)*u over row pairs (g rows [0,64), u rows [64,128) of each tile)
   int* err;
-  int splits;  // K splits per tile (1: none)
-  float* ws;   // [tiles * splits][128][BN] fp32 partials
-  int* cnt;    // [tiles] arrival counters, zero between calls
+  int ctas;    // stream-K: CTAs sharing the (tile, K-block) space (0: whole tiles per CTA)
+  float* ws;   // stream-K: [ctas][2][128][BN] fp32 partials (a CTA's first and last segment)
+  int* cnt;    // stream-K: [tiles] arrival counters, zero between calls
 };
+
+// The sequence of (tile, K-block range) segments one CTA works through, identical for its
+// producer, MMA and epilogue roles.
+struct SegIter {
+  long pos, end;  // stream-K: position in the (tile, K-block) space
+  int u, step;    // whole tiles: next tile, stride
+  int tiles, kblocks;
+  bool sk;
+  __device__ SegIter(int cta, int ctas, int grid, int tiles_, int kblocks_)
+      : tiles(tiles_), kblocks(kblocks_), sk(ctas > 0) {
+    const long W = (long)tiles_ * kblocks_;
+    pos = sk ? (long)cta * W / ctas : 0;
+    end = sk ? (long)(cta + 1) * W / ctas : 0;
+    u = cta;
+    step = grid;
+  }
+  __device__ bool next(int& tile, int& k0, int& k1) {
+    if (sk) {
+      if (pos >= end) return false;
+      tile = (int)(pos / kblocks);
+      k0 = (int)(pos % kblocks);
+      k1 = (int)min((long)kblocks, k0 + (end - pos));
+      pos += k1 - k0;
+      return true;
+    }
+    if (u >= tiles) return false;
+    tile = u;
+    k0 = 0;
+    k1 = kblocks;
+    u += step;
+    return true;
+  }
+};
+
+// Stream-K: the CTA whose share contains position p of the (tile, K-block) space of size W.
+__device__ __forceinline__ int sk_owner(long p, long W, int ctas) { return (int)(((p + 1) * ctas - 1) / W); }
 
 template <int BN, typename OutT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
@@ -71,14 +112,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_tiles = (a.N + 127) / 128;
   const int t_tiles = (a.T + BN - 1) / BN;
-  const int splits = a.splits;
-  const int tiles = n_tiles * t_tiles * splits;  // work units: (tile, K split), splits fastest
+  const int tiles = n_tiles * t_tiles;
   const int kblocks = (a.K + BK - 1) / BK;
-  auto krange = [&](int u, int& k0, int& k1) {
-    const int sp = u % splits;
-    k0 = (int)((long)kblocks * sp / splits);
-    k1 = (int)((long)kblocks * (sp + 1) / splits);
-  };
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
@@ -110,11 +145,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---------------------------------------------------------------- producer
     if (elect_one()) {
       int it = 0;
-      for (int u = blockIdx.x; u < tiles && !*abort_flag; u += gridDim.x) {
-        const int tile = u / splits;
+      SegIter sg(blockIdx.x, a.ctas, gridDim.x, tiles, kblocks);
+      int tile, k0, k1;
+      while (!*abort_flag && sg.next(tile, k0, k1)) {
         const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
-        int k0, k1;
-        krange(u, k0, k1);
         for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) break;
@@ -130,14 +164,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     // ---------------------------------------------------------------- MMA issuer
     if (elect_one()) {
       int it = 0, ti = 0;
-      for (int u = blockIdx.x; u < tiles && !*abort_flag; u += gridDim.x, ++ti) {
+      SegIter sg(blockIdx.x, a.ctas, gridDim.x, tiles, kblocks);
+      int tile, k0, k1;
+      for (; !*abort_flag && sg.next(tile, k0, k1); ++ti) {
         const int acc = ti & 1;
         if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
         bool ok = true;
-        int k0, k1;
-        krange(u, k0, k1);
         for (int kb = k0; kb < k1; ++kb, ++it) {
           const int s = it % C::STAGES;
           if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
@@ -209,13 +243,16 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       asm volatile("bar.sync 1, 128;" ::: "memory");
     };
     int ti = 0;
-    for (int u = blockIdx.x; u < tiles; u += gridDim.x, ++ti) {
-      const int tile = u / splits;
+    SegIter sg(blockIdx.x, a.ctas, gridDim.x, tiles, kblocks);
+    const long W = (long)tiles * kblocks;
+    const int first_tile = a.ctas ? (int)(sg.pos / kblocks) : -1;  // tile of this CTA's first segment
+    int tile, k0, k1;
+    for (; sg.next(tile, k0, k1); ++ti) {
       const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
       const int acc = ti & 1;
       if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) break;
       tc_fence_after();
-      if (splits == 1) {
+      if (k0 == 0 && k1 == kblocks) {  // a whole tile
         for (int c0 = 0; c0 < BN; c0 += CH) {
           float v[32];
           const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
@@ -226,8 +263,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         mbar_arrive(&acc_empty[acc]);
         continue;
       }
-      // split-K: this unit's fp32 partial -> workspace; the last unit of the tile adds them up
-      float* part = a.ws + ((long)u * 128 + row) * BN;
+      // part of a tile's K range: fp32 partial -> this CTA's slot; the last arriver adds them up
+      const int slot = tile == first_tile ? 0 : 1;
+      float* part = a.ws + (((long)blockIdx.x * 2 + slot) * 128 + row) * BN;
       for (int c0 = 0; c0 < BN; c0 += CH) {
         float v[32];
         const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
@@ -238,26 +276,40 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       }
       tc_fence_before();
       mbar_arrive(&acc_empty[acc]);
-      __threadfence();
+      const long p0 = (long)tile * kblocks;
+      const int cf = sk_owner(p0, W, a.ctas), cl = sk_owner(p0 + kblocks - 1, W, a.ctas);
       asm volatile("bar.sync 1, 128;" ::: "memory");
-      if (et == 0) *last_p = atomicAdd(&a.cnt[tile], 1) == splits - 1;
+      if (et == 0) {
+        // release this CTA's partial (ordered before by the barrier), count it, acquire the others
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        const bool last = atomicAdd(&a.cnt[tile], 1) == cl - cf;
+        if (last) asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        *last_p = last;
+      }
       asm volatile("bar.sync 1, 128;" ::: "memory");
       if (!*last_p) continue;
-      __threadfence();
-      const float* base = a.ws + ((long)tile * splits * 128 + row) * BN;
       for (int c0 = 0; c0 < BN; c0 += CH) {
         float v[32];
 #pragma unroll
         for (int j = 0; j < CH; ++j) v[j] = 0.f;
-        for (int sp = 0; sp < splits; ++sp) {
-          const float* pp = base + (long)sp * 128 * BN + c0;
+        for (int c = cf; c <= cl; c += 2) {  // two partials' loads in flight together
+          const int s0 = (int)(((long)c * W / a.ctas) / kblocks) == tile ? 0 : 1;
+          const float* p0p = a.ws + (((long)c * 2 + s0) * 128 + row) * BN + c0;
+          const bool two = c + 1 <= cl;
+          const int s1 = two && (int)(((long)(c + 1) * W / a.ctas) / kblocks) == tile ? 0 : 1;
+          const float* p1p = a.ws + (((long)(two ? c + 1 : c) * 2 + s1) * 128 + row) * BN + c0;
+          float4 f0[CH / 4], f1[CH / 4];
 #pragma unroll
-          for (int j = 0; j < CH; j += 4) {
-            const float4 f = __ldcg(reinterpret_cast<const float4*>(pp + j));
-            v[j] += f.x;
-            v[j + 1] += f.y;
-            v[j + 2] += f.z;
-            v[j + 3] += f.w;
+          for (int j = 0; j < CH / 4; ++j) {
+            f0[j] = __ldcg(reinterpret_cast<const float4*>(p0p) + j);
+            f1[j] = two ? __ldcg(reinterpret_cast<const float4*>(p1p) + j) : make_float4(0.f, 0.f, 0.f, 0.f);
+          }
+#pragma unroll
+          for (int j = 0; j < CH / 4; ++j) {
+            v[4 * j] += f0[j].x + f1[j].x;
+            v[4 * j + 1] += f0[j].y + f1[j].y;
+            v[4 * j + 2] += f0[j].z + f1[j].z;
+            v[4 * j + 3] += f0[j].w + f1[j].w;
           }
         }
         emit(n0, t0, c0, v);
@@ -327,8 +379,8 @@ static int launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArg
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr = true;
   }
-  const int tiles = ((a.N + 127) / 128) * ((a.T + BN - 1) / BN) * a.splits;
-  int grid = tiles < max_ctas ? tiles : max_ctas;
+  const int tiles = ((a.N + 127) / 128) * ((a.T + BN - 1) / BN);
+  int grid = a.ctas ? a.ctas : tiles < max_ctas ? tiles : max_ctas;
   if (grid < 1) grid = 1;
   k<<<grid, GEMM_THREADS, C::SMEM, st>>>(tw, tx, a, idesc_f16(128, BN, bf16));
   return (int)cudaGetLastError();
@@ -336,37 +388,27 @@ static int launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArg
 
 static int gemm_bn(int T) { return T <= 16 ? 16 : T <= 32 ? 32 : T <= 64 ? 64 : T <= 128 ? 128 : 256; }
 
-// K splits per output tile: the S (each split keeping >= 8 K-blocks, at most 16) that minimises
-// the number of persistent-CTA waves per split, ceil(tiles * S / SMs) / S, plus 2 % per split for
-// the fp32 partials each extra split writes and reads. Few tiles (N = 4096 decode projections)
-// split until they fill the SMs; a count just above the SM count (161 tiles) splits so the ragged
-// second wave shrinks; large outputs (LM head) stay unsplit.
-int gemm_splits(int T, int N, int K) {
+// Stream-K CTAs for a GEMM (0: whole tiles per CTA). Decode shapes only (token tile <= 64): they
+// stream weights and their 128 x BN fp32 partials are small next to the weights, while a prefill
+// GEMM is compute bound with wide partials. Each CTA keeps at least 8 K-blocks so that its
+// pipeline fills. Chosen when the longest CTA's K-blocks, plus the partial write and fixup
+// (measured at about 15 % plus 8 K-blocks), beat whole tiles: N = 4096 (32 tiles) and N = 20608
+// (161 tiles, a ragged second wave) split; 136 tiles on 148 SMs stay whole.
+int gemm_streamk_ctas(int T, int N, int K) {
   const int BN = gemm_bn(T);
-  const int tiles = ((N + 127) / 128) * ((T + BN - 1) / BN);
-  const int kblocks = (K + BK - 1) / BK;
+  const long tiles = (long)((N + 127) / 128) * ((T + BN - 1) / BN);
+  const long kblocks = (K + BK - 1) / BK;
   const int sms = num_sms();
-  // decode shapes only (token tile <= 64): there the GEMM streams weights and the partials are
-  // small; a prefill GEMM is compute bound and its 128 x BN fp32 partials would rival its weights
-  if (BN > 64 || kblocks < 16 || tiles >= 4 * sms) return 1;
-  int best = 1;
-  double best_cost = 1e30;
-  for (int s = 1; s <= 16 && s <= kblocks / 8; ++s) {
-    const double waves = (double)((tiles * s + sms - 1) / sms) / s;
-    const double cost = waves * (1.0 + 0.02 * (s - 1));
-    if (cost < best_cost - 1e-9) {
-      best_cost = cost;
-      best = s;
-    }
-  }
-  return best;
+  if (BN > 64 || kblocks < 16 || tiles % sms == 0) return 0;
+  const long ctas = std::min<long>(sms, tiles * kblocks / 8);
+  const double whole = (double)((tiles + sms - 1) / sms) * kblocks;
+  const double split = (double)tiles * kblocks / ctas * 1.15 + 8.0;
+  return split < whole ? (int)ctas : 0;
 }
 
 long gemm_split_ws_floats(int T, int N, int K) {
-  const int s = gemm_splits(T, N, K);
-  if (s == 1) return 0;
-  const int BN = gemm_bn(T);
-  return (long)((N + 127) / 128) * ((T + BN - 1) / BN) * s * 128 * BN;
+  const int c = gemm_streamk_ctas(T, N, K);
+  return c ? (long)c * 2 * 128 * gemm_bn(T) : 0;
 }
 
 int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
@@ -378,8 +420,8 @@ int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy,
   if (r) return 1000 + r;
   r = make_tmap_2d(&tx, x, 2, T, K, ldx, BN, BK, true);
   if (r) return 2000 + r;
-  const int splits = (ws && cnt) ? gemm_splits(T, N, K) : 1;
-  GemmArgs a{y, ldy, T, N, K, act, err, splits, ws, cnt};
+  const int ctas = (ws && cnt) ? gemm_streamk_ctas(T, N, K) : 0;
+  GemmArgs a{y, ldy, T, N, K, act, err, ctas, ws, cnt};
   if (max_ctas <= 0) max_ctas = num_sms();
   switch (BN) {
     case 16: return bf16 ? launch_bn<16, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)

@@ -17,9 +17,9 @@ int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, long rows, 
 // Y[T,N] = X[T,K] @ W[N,K]^T ; act 1 = silu(gate)*up over 64-row halves of each 128-row tile
 int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
             int act, int* err, cudaStream_t stream, int max_ctas = 0, float* ws = nullptr, int* cnt = nullptr);
-// split-K workspace (fp32 floats; 0 = no split) and counters (one per 128-row x BN tile)
+// stream-K workspace (fp32 floats; 0 = whole tiles per CTA) and CTA count; counters: one per tile
 long gemm_split_ws_floats(int T, int N, int K);
-int gemm_splits(int T, int N, int K);
+int gemm_streamk_ctas(int T, int N, int K);
 
 int rmsnorm(const void* x, long ldx, const float* w1p, void* out, long ldo, int rows, int H, float eps,
             cudaStream_t s);

@@ -130,6 +130,11 @@ class Model:
         if self.stamps is not None:
             self.stamps.mark(tag)
 
+    def _dstamp(self, tag: str) -> None:
+        """A stamp inside a layer part (only when the installed ``Stamps`` asks for detail)."""
+        if self.stamps is not None and self.stamps.detail:
+            self.stamps.mark(tag)
+
     def io_bytes(self) -> tuple[int, int]:
         return self._h2d, self._d2h
 
@@ -258,19 +263,23 @@ class Model:
         nk, nv, dk, dv = self.nk, self.nv, cfg.dn_k_dim, cfg.dn_v_dim
         c = self.conv_ch
         proj = ops.linear(h, L["w_in"])  # [T, c + nv*dv + 2nv]
+        self._dstamp("dn.in_proj")
         commit = not b.verify
         if b.verify:  # keep the per-row inputs: the accepted prefix is committed later
             self._vsave[j] = (proj[:, :c].clone(), proj[:, c + nv * dv:].clone())
         qkv = ops.causal_conv_varlen(proj[:, :c], self.conv_state[j], L["conv_w"], b.seg_lane, b.cu,
                                      b.seg_lane_h, b.cu_h, commit=commit)
+        self._dstamp("dn.conv")
         z = proj[:, c:c + nv * dv]
         ab = proj[:, c + nv * dv:]
         core = ops.gated_delta_varlen(qkv, ab, L["A_log"], L["dt_bias"], self.rec_state[j], b.seg_lane, b.cu,
                                       nk, nv, dk, dv, b.seg_lane_h, b.cu_h, commit=commit)
+        self._dstamp("dn.recurrence")
         if self.fault.get("skip_deltanet_gate"):
             normed = ops.rmsnorm(core, torch.ones(dv, device=h.device), cfg.eps).reshape(-1, nv * dv)
         else:
             normed = ops.gated_rmsnorm(core, z.reshape(-1, nv, dv), L["norm_w"], cfg.eps).reshape(-1, nv * dv)
+        self._dstamp("dn.gated_norm")
         return ops.linear(normed, L["w_out"])
 
     def _attention(self, i: int, L: dict, h: torch.Tensor, b: StepInputs) -> torch.Tensor:
@@ -281,6 +290,7 @@ class Model:
         cfg = self.cfg
         hd, nq, nkv = cfg.head_dim, self.nq, self.nkv
         qkv = ops.linear(h, L["w_qkv"])
+        self._dstamp("attn.qkv_proj")
         t = qkv.shape[0]
         qg = qkv[:, : nq * 2 * hd].reshape(t, nq, 2 * hd)
         q, gate = qg[..., :hd], qg[..., hd:]
@@ -289,21 +299,34 @@ class Model:
         theta = float(self.fault.get("rope_base", cfg.rope_theta))
         q = ops.qk_norm_rope_kv_write(q, k, v, L["q_norm"], L["k_norm"], b.positions, b.rows,
                                       k_cache, v_cache, cfg.rotary_dim, theta, cfg.eps)
+        self._dstamp("attn.norm_rope_kv")
         o = ops.attention_varlen(q, k_cache, v_cache, self.table_dev, b.seg_lane, b.cu,
                                  b.seg_start, self.block_size, b.seg_lane_h, b.cu_h, b.seg_start_h,
                                  self.tables if h.device.type == "cpu" else None, b.positions, b.max_ctx)
+        self._dstamp("attn.core")
         o = ops.sigmoid_gate_mul(o.reshape(t, nq * hd), gate.reshape(t, nq * hd))
+        self._dstamp("attn.gate")
         return ops.linear(o, L["w_o"])
 
     def _moe(self, L: dict, h: torch.Tensor) -> torch.Tensor:
         cfg, p = self.cfg, self.plan
-        rl = ops.linear(h, L["w_router"])  # [T, E+1]: router logits | shared-expert gate logit
+        if "w_rsh" in L:  # router and shared gate|up in one GEMM
+            rs = ops.linear(h, L["w_rsh"])
+            rl, g13 = rs[:, : cfg.experts + 1], rs[:, L["rsh_off"]:]
+        else:
+            rl, g13 = ops.linear(h, L["w_router"]), None  # [T, E+1]: router logits | shared-expert gate logit
+        self._dstamp("moe.router_proj")
         topw, topi = ops.router_topk(rl[:, : cfg.experts], cfg.top_k)
+        self._dstamp("moe.topk")
         drop = self.fault.get("drop_expert")
         if drop is not None:
             topw = torch.where(topi == int(drop), torch.zeros_like(topw), topw)
         routed = ops.moe_routed(h, topw, topi, L["experts"], p.experts.start, p.experts.count)
-        sh = ops.linear(ops.silu_mul(ops.linear(h, L["w_sh13"])), L["w_sh2"])
+        self._dstamp("moe.routed")
+        if g13 is None:
+            g13 = ops.linear(h, L["w_sh13"])
+        sh = ops.linear(ops.silu_mul(g13), L["w_sh2"])
+        self._dstamp("moe.shared")
         return ops.shared_gate_combine(routed, sh, rl[:, cfg.experts])
 
     def _layers(self, x: torch.Tensor, b: StepInputs) -> tuple[torch.Tensor, torch.Tensor]:

@@ -112,15 +112,29 @@ def load_attention(r: _Rd, cfg: Qwen35Config, p: Plan) -> dict:
     }
 
 
+def fuse_router_shared(d: dict) -> dict:
+    """One weight for the two projections of the MoE input: router rows (plus the shared-expert
+    gate row), zero rows up to a multiple of 8, then the shared expert's gate|up rows. One GEMM
+    then reads ``h`` once and launches once; ``w_router`` and ``w_sh13`` become row views of it
+    (no second copy), and the shared-expert columns of its output start 16-byte aligned."""
+    wr, ws = d["w_router"], d["w_sh13"]
+    off = (wr.shape[0] + 7) // 8 * 8
+    w = torch.zeros(off + ws.shape[0], wr.shape[1], dtype=wr.dtype, device=wr.device)
+    w[: wr.shape[0]] = wr
+    w[off:] = ws
+    d.update(w_rsh=w, rsh_off=off, w_router=w[: wr.shape[0]], w_sh13=w[off:])
+    return d
+
+
 def load_moe_dense(r: _Rd, cfg: Qwen35Config, p: Plan) -> dict:
     sh = (p.shared.start, p.shared.stop)
-    return {
+    return fuse_router_shared({
         "w_router": torch.cat([r.w("mlp.gate.weight"), r.w("mlp.shared_expert_gate.weight")]).contiguous(),
         "w_sh13": torch.cat(
             [r.w("mlp.shared_expert.gate_proj.weight", sh), r.w("mlp.shared_expert.up_proj.weight", sh)]
         ).contiguous(),
         "w_sh2": r.cols("mlp.shared_expert.down_proj.weight", sh[0], sh[1]),
-    }
+    })
 
 
 def _device_experts(ex: dict) -> dict:
@@ -245,6 +259,7 @@ def random_layer(kind: str, cfg: Qwen35Config, p: Plan, gen, device, dtype, expe
         w_sh13=_randn((2 * p.shared.count, h), gen, device, dtype),
         w_sh2=_randn((h, p.shared.count), gen, device, dtype),
     )
+    fuse_router_shared(d)
     if experts_from is not None:
         d["experts"] = experts_from
         return d

@@ -92,21 +92,31 @@ def case_moe(tokens: int, iters: int, pk: dict, experts: int = 512, top_k: int =
     return _report(f"moe_T{tokens}", ms, active * per_expert, flops, pk, active_experts=active)
 
 
-def case_gemm(tokens: int, iters: int, pk: dict, n: int = 12288, k: int = 4096) -> dict:
+def case_gemm(tokens: int, iters: int, pk: dict, n: int = 12288, k: int = 4096, name: str = "") -> dict:
     """Dense bf16 GEMM y = x W^T (the fused q/k/v/gate projection width at TP=1 by default)."""
     g = _g(1)
-    # several weight copies cycled so that consecutive calls never hit a warm L2
-    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for _ in range(4)]
+    # enough weight copies cycled (>= 4, >= 384 MB) that consecutive calls never hit a warm L2
+    copies = max(4, -(-(384 << 20) // (2 * n * k)))
+    ws = [(torch.randn(n, k, device="cuda", generator=g) * 0.02).to(torch.bfloat16) for _ in range(copies)]
     x = torch.randn(tokens, k, device="cuda", generator=g).to(torch.bfloat16)
     out = torch.empty(tokens, n, device="cuda", dtype=torch.bfloat16)
     i = [0]
 
     def fn():
-        ops.linear(x, ws[i[0] % 4], out)
+        ops.linear(x, ws[i[0] % copies], out)
         i[0] += 1
 
-    ms = _time(fn, iters)
-    return _report(f"gemm_T{tokens}_N{n}_K{k}", ms, 2 * (n * k + tokens * (k + n)), 2 * tokens * n * k, pk)
+    ms = _time(fn, max(iters, copies))
+    return _report(f"gemm{name}_T{tokens}_N{n}_K{k}", ms, 2 * (n * k + tokens * (k + n)), 2 * tokens * n * k, pk)
+
+
+# every dense projection of the full model at TP=1: (name, N, K)
+MODEL_GEMMS = (("_dn_in", 20608, 4096), ("_dn_out", 4096, 8192), ("_attn_qkv", 17408, 4096),
+               ("_attn_o", 4096, 8192), ("_router", 513, 4096), ("_sh13", 2048, 4096), ("_sh2", 4096, 1024))
+
+
+def case_gemm_shapes(tokens: int, iters: int, pk: dict) -> list:
+    return [case_gemm(tokens, iters, pk, n, k, name) for name, n, k in MODEL_GEMMS]
 
 
 def _paged_kv(lanes: int, ctx: int, nkv: int, hd: int, bs: int = 16, seed: int = 2):
@@ -232,6 +242,10 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
            "parts_share": {k: round(v / tot, 3) for k, v in sorted(att.items()) if k != "total"}}
     print(json.dumps(row), flush=True)
     res["decode_graph"] = row
+    att = g.attribution(lanes, replays=5, detail=True)
+    row = {"case": "model_decode_graph_detail", "lanes": lanes,
+           "parts_ms": {k: round(v, 3) for k, v in sorted(att.items(), key=lambda kv: -kv[1])}}
+    print(json.dumps(row), flush=True)
     g.release()
     return res
 
@@ -239,7 +253,7 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="all",
-                    choices=["moe", "gemm", "attn_prefill", "attn_decode", "deltanet", "model", "all"])
+                    choices=["moe", "gemm", "gemm_shapes", "attn_prefill", "attn_decode", "deltanet", "model", "all"])
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--lanes", type=int, default=None)
@@ -255,6 +269,9 @@ def main(argv=None):
     if a.case in ("gemm", "all"):
         for t in ([a.tokens] if a.tokens else [32, 2048]):
             run.append(case_gemm(t, a.iters, pk))
+    if a.case == "gemm_shapes":
+        for t in ([a.tokens] if a.tokens else [1, 32, 800]):
+            run.extend(case_gemm_shapes(t, a.iters, pk))
     if a.case in ("attn_prefill", "all"):
         run.append(case_attn_prefill(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.iters, pk))
     if a.case in ("attn_decode", "all"):

@@ -121,12 +121,13 @@ class GraphRunner:
             self._b[B] = bk
         torch.cuda.synchronize()
 
-    def attribution(self, B: int, replays: int = 10) -> dict[str, float]:
+    def attribution(self, B: int, replays: int = 10, detail: bool = False) -> dict[str, float]:
         """Device time per layer part (ms) of one captured ``B``-row decode step.
 
         Captures a separate diagnostic graph of the bucket with clock stamps between the layer
         parts (``utils.telemetry.Stamps``), replays it ``replays`` times and reads the stamps of
-        the last replay; the serving graphs never contain a stamp. Every rank must call this
+        the last replay (``detail``: also between the kernels of each part, tagged
+        ``dn.*``/``attn.*``/``moe.*``); the serving graphs never contain a stamp. Every rank must call this
         (the capture runs the collectives). Reference behaviour: ``decode_stamps.py`` with its
         separate diagnostic capture."""
         from ..utils.telemetry import Stamps
@@ -134,7 +135,7 @@ class GraphRunner:
         m = self.model
         bk = _Bucket(m, B, None)
         self._fill(bk, [], [], [])
-        st = Stamps(m.device)
+        st = Stamps(m.device, detail=detail)
         m.stamps = st
         try:
             s = torch.cuda.Stream()

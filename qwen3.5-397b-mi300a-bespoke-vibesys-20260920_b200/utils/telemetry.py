@@ -110,11 +110,12 @@ class Stamps:
     (``Recorder``, ``mark``, ``segments_ms``), there with the 100 MHz ``s_memrealtime`` counter.
     """
 
-    def __init__(self, device, capacity: int = 4096) -> None:
+    def __init__(self, device, capacity: int = 4096, detail: bool = False) -> None:
         import torch
 
         self.buf = torch.zeros(capacity, dtype=torch.int64, device=device)
         self.tags: list[str] = []
+        self.detail = detail  # also stamp between the kernels inside a layer part
 
     def mark(self, tag: str) -> None:
         from ..ops import core as ops

@@ -45,6 +45,35 @@ def test_linear(T, N, K):
     status_ok()
 
 
+@pytest.mark.parametrize("T,N,K", [(32, 20608, 4096), (32, 4096, 8192), (32, 513, 4096), (1, 2048, 4096),
+                                   (17, 4096, 1024), (64, 1000, 2048)])
+def test_linear_streamk(T, N, K):
+    """Decode shapes whose tiles do not divide over the SMs: stream-K partials and their fixup,
+    three calls in a row (the arrival counters re-arm themselves) and a graph replay."""
+    x = rnd(T, K, scale=1.0, seed=T + 1)
+    w = rnd(N, K, scale=0.05, seed=N)
+    ref = x.float() @ w.float().t()
+    for _ in range(3):
+        y = ops.linear(x, w)
+        torch.cuda.synchronize()
+        close(y, ref, rtol=1e-2, atol=1e-2)
+    out = torch.empty(T, N, dtype=BF, device=DEV)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        ops.linear(x, w, out=out)
+    torch.cuda.current_stream().wait_stream(s)
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        ops.linear(x, w, out=out)
+    out.zero_()
+    for _ in range(2):
+        g.replay()
+    torch.cuda.synchronize()
+    close(out, ref, rtol=1e-2, atol=1e-2)
+    status_ok()
+
+
 def test_linear_strided_input_and_output():
     base = rnd(40, 512, seed=3)
     x = base[:, 128:384]  # row stride 512, 256 columns
