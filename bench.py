@@ -222,6 +222,7 @@ def main():
         are outside every interval."""
         if events is not None:
             inner.gpu_marks = []
+            sched.timer.last_kind = None
         sched.step()
         if events is not None:
             marks = inner.gpu_marks
@@ -232,6 +233,7 @@ def main():
             last_in = max((i for i, (tag, _) in enumerate(marks) if tag == "in"), default=-1)
             outs = [ev for i, (tag, ev) in enumerate(marks) if tag == "out" and i > last_in]
             events.append((first_in, outs[-1] if outs else end) if first_in is not None else None)
+            kinds.append(sched.timer.last_kind)
         step_no[0] += 1
         loop.pump()
 
@@ -264,7 +266,7 @@ def main():
     ev_start = mark("start")
     step0 = step_no[0]
     t_host0 = time.perf_counter()
-    events = []
+    events, kinds = [], []
     gen0 = sum(r.generated for r in loop.records if r.end_step >= 0)
     for _ in range(args.steps):
         one_step(events if device.type == "cuda" else None)
@@ -297,6 +299,11 @@ def main():
     inflight = sum(len(getattr(f, "out_ids", [])) for f in sched.decoding)
     tokens_in_window = max(0, done_now + inflight - gen0)
     p95_dev = percentile(ttft_dev, 95) if ttft_dev else percentile(ttft_host, 95)
+    by_kind: dict = {}
+    for ev, kind in zip(events, kinds):  # device time of one step, by the step's kind
+        if ev is not None and kind is not None:
+            by_kind.setdefault(kind, []).append(ev[0].elapsed_time(ev[1]))
+    device_ms_by_kind = {k: round(sum(v) / len(v), 3) for k, v in by_kind.items()}
     n_steps = step1 - step0
     res = {
         "metric": METRIC,
@@ -337,6 +344,7 @@ def main():
         "setup_s": round(setup_s, 1),
         "boot_s": round(boot_s, 1),
         "step_kinds": sched.timer.summary(),
+        "device_ms_per_step": device_ms_by_kind,
     }
     line = json.dumps(res)
     print(line, flush=True)

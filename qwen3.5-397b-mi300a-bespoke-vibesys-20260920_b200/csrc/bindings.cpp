@@ -265,6 +265,25 @@ Tensor gated_delta_varlen(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, T
   return out;
 }
 
+Tensor deltanet_decode(Tensor proj, Tensor conv_state, Tensor conv_w, Tensor a_log, Tensor dt_bias, Tensor state,
+                       Tensor norm_w, Tensor seg_lane, int64_t nk, int64_t nv, int64_t dk, int64_t dv, double eps) {
+  CHECK_BF16(proj);
+  TORCH_CHECK(proj.stride(1) == 1, "deltanet_decode: proj rows contiguous");
+  TORCH_CHECK(state.scalar_type() == at::kFloat && state.stride(3) == 1 && state.stride(2) == dv &&
+                  state.stride(1) == dk * dv, "deltanet_decode: fp32 state [lanes, nv, dk, dv]");
+  TORCH_CHECK(conv_state.scalar_type() == at::kBFloat16 && conv_state.stride(2) == 1 &&
+                  conv_state.stride(1) == conv_state.size(2), "deltanet_decode: conv state [lanes, C, K-1]");
+  TORCH_CHECK(conv_w.is_contiguous() && norm_w.is_contiguous() && seg_lane.is_contiguous(), "deltanet_decode: contiguous");
+  const int T = proj.size(0);
+  TORCH_CHECK(seg_lane.size(0) == T, "deltanet_decode: one token per lane");
+  Tensor out = at::empty({T, nv * dv}, proj.options());
+  LAUNCH(qb::deltanet_decode(proj.data_ptr(), proj.stride(0), conv_state.data_ptr(), conv_state.stride(0),
+                             conv_w.data_ptr(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
+                             state.data_ptr<float>(), state.stride(0), norm_w.data_ptr(), seg_lane.data_ptr<int>(), T,
+                             nk, nv, dk, dv, conv_w.size(1), (float)eps, out.data_ptr(), stream()));
+  return out;
+}
+
 Tensor gated_delta_chunked(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, Tensor state, Tensor seg_lane,
                            Tensor chunks, Tensor seg_chunk0, int64_t nk, int64_t nv, int64_t dk, int64_t dv,
                            bool commit) {
@@ -473,6 +492,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fa", &attention_fa);
   m.def("moe_routed_mx", &moe_routed_mx);
   m.def("stamp", &stamp);
+  m.def("deltanet_decode", &deltanet_decode);
   m.def("gated_delta_chunked", &gated_delta_chunked);
   m.def("causal_conv_varlen", &causal_conv_varlen);
   m.def("gated_delta_varlen", &gated_delta_varlen);

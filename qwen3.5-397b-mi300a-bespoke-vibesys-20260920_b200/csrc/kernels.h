@@ -53,6 +53,10 @@ int gated_delta_chunked(const void* qkv, long ldqkv, const void* ab, long ldab, 
                         const int* chunks, int n_chunks, const int* seg_chunk0, int S, int T, int nk, int nv, int dk,
                         int dv, float* scratch, void* out, bool commit, cudaStream_t s);
 long gated_delta_chunked_scratch(int T, int n_chunks, int nk, int nv, int dk);
+// DeltaNet token mixer for one token per lane (conv, l2norm, gated delta step, gated RMSNorm)
+int deltanet_decode(const void* proj, long ldp, void* conv_state, long cls, const void* conv_w, const float* a_log,
+                    const float* dt_bias, float* state, long sls, const void* norm_w, const int* seg_lane, int T,
+                    int nk, int nv, int dk, int dv, int K, float eps, void* out, cudaStream_t s);
 // in-graph clock stamp (elementwise.cu): buf[slot] = %globaltimer
 int stamp(unsigned long long* buf, int slot, cudaStream_t s);
 // block-scaled MoE (moe_mx.cu): token tile width, tile prefix, activation split, expert GEMM

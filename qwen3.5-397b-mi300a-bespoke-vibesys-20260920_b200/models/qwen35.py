@@ -264,6 +264,14 @@ class Model:
         c = self.conv_ch
         proj = ops.linear(h, L["w_in"])  # [T, c + nv*dv + 2nv]
         self._dstamp("dn.in_proj")
+        if (h.is_cuda and not b.verify and b.cu_h is not None and len(b.cu_h) - 1 == h.shape[0]
+                and not self.fault.get("skip_deltanet_gate")):
+            # decode (one token per lane): conv, delta step and gated norm in one kernel
+            normed = ops.deltanet_decode(proj, self.conv_state[j], L["conv_w"], L["A_log"], L["dt_bias"],
+                                         self.rec_state[j], L["norm_w"], b.seg_lane, nk, nv, dk, dv, cfg.eps,
+                                         b.seg_lane_h)
+            self._dstamp("dn.decode_mixer")
+            return ops.linear(normed, L["w_out"])
         commit = not b.verify
         if b.verify:  # keep the per-row inputs: the accepted prefix is committed later
             self._vsave[j] = (proj[:, :c].clone(), proj[:, c + nv * dv:].clone())

@@ -81,6 +81,28 @@ def argmax_rows(logits):
     return v, i
 
 
+def deltanet_decode(proj, conv_state, conv_w, a_log, dt_bias, rec_state, norm_w, seg_lane, nk, nv, dk, dv, eps,
+                    seg_lane_h=None):
+    """DeltaNet token mixer for a batch of one token per lane, from the input projection ``proj``
+    ([T, conv channels | z | b | a]) to the gated-normed heads [T, nv*dv]: causal conv + SiLU,
+    q/k l2norm, gated delta step and gated RMSNorm, the lane's conv window and fp32 state
+    continued and updated. One fused kernel on CUDA (dk = dv = 128, conv kernel 4); elsewhere the
+    separate ops. Reference behaviour: ``deltanet_fused.py`` decode step, ``model.py:3596``."""
+    if _cuda(proj) and dk == 128 and dv == 128 and conv_w.shape[1] == 4:
+        return ext().deltanet_decode(proj, conv_state, conv_w, a_log, dt_bias, rec_state, norm_w, seg_lane,
+                                     nk, nv, dk, dv, eps)
+    t = proj.shape[0]
+    c = 2 * nk * dk + nv * dv
+    cu_h = list(range(t + 1))
+    lanes_h = seg_lane.tolist() if seg_lane_h is None else list(seg_lane_h)
+    cu = torch.arange(t + 1, dtype=torch.int32, device=proj.device)
+    qkv = causal_conv_varlen(proj[:, :c], conv_state, conv_w, seg_lane, cu, lanes_h, cu_h)
+    core = gated_delta_varlen(qkv, proj[:, c + nv * dv:], a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv,
+                              lanes_h, cu_h)
+    z = proj[:, c:c + nv * dv].reshape(t, nv, dv)
+    return gated_rmsnorm(core, z, norm_w, eps).reshape(t, nv * dv)
+
+
 def stamp(buf: torch.Tensor, slot: int) -> None:
     """``buf[slot]`` = the device clock (ns, ``%globaltimer``) when the stream reaches this point;
     a one-thread kernel, so it can sit inside a captured CUDA graph. On CPU: the host clock."""

@@ -235,9 +235,11 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
     g.prepare()
     pos = [max(ctx, 2048) + lane for lane in range(lanes)]
     ms = _time(lambda: g.decode(list(range(lanes)), [5] * lanes, pos), 5)
+    replay_ms = _time(lambda: g._b[lanes].graph.replay(), 5)
     att = g.attribution(lanes, replays=5)
     tot = att.get("total", 0.0) or 1.0
     row = {"case": "model_decode_graph", "lanes": lanes, "ctx": max(ctx, 2048), "ms": round(ms, 2),
+           "replay_ms": round(replay_ms, 2),
            "parts_ms": {k: round(v, 3) for k, v in sorted(att.items())},
            "parts_share": {k: round(v / tot, 3) for k, v in sorted(att.items()) if k != "total"}}
     print(json.dumps(row), flush=True)

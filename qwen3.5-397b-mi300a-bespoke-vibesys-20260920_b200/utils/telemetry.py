@@ -27,10 +27,12 @@ class StepTimer:
         self.win: dict[str, list[tuple[int, float]]] = defaultdict(list)
         self.total: dict[str, list[float]] = defaultdict(lambda: [0, 0.0, 0])
         self.n = 0
+        self.last_kind = None  # kind of the most recent step
         trace = flags.get("QB_SERVICE_TRACE")
         self.trace = ServiceTrace(trace) if trace else None
 
     def record(self, kind: str, tokens: int, seconds: float) -> None:
+        self.last_kind = kind
         t = self.total[kind]
         t[0] += 1
         t[1] += seconds

@@ -444,3 +444,36 @@ def test_chunked_delta_rule_matches_recurrence(monkeypatch):
     torch.cuda.synchronize()
     assert torch.equal(rs, before)
     status_ok()
+
+
+@pytest.mark.parametrize("nk,nv,lanes", [(16, 64, 32), (4, 8, 3), (2, 8, 5)])
+def test_deltanet_decode_fused(nk, nv, lanes):
+    """The fused one-token-per-lane DeltaNet mixer equals the separate conv, delta-rule and
+    gated-norm kernels: output, fp32 state and conv window (lanes in shuffled order)."""
+    dk = dv = 128
+    C = 2 * nk * dk + nv * dv
+    g = torch.Generator(device=DEV).manual_seed(nv + lanes)
+    proj = (torch.randn(lanes, C + nv * dv + 2 * nv, device=DEV, generator=g)).to(BF)
+    conv_w = (0.3 * torch.randn(C, 4, device=DEV, generator=g)).to(BF)
+    a_log = torch.log(torch.rand(nv, device=DEV, generator=g) * 15 + 1)
+    dt_bias = torch.randn(nv, device=DEV, generator=g)
+    norm_w = (1 + 0.1 * torch.randn(dv, device=DEV, generator=g)).to(BF)
+    n_lanes = lanes + 2
+    cs0 = torch.randn(n_lanes, C, 3, device=DEV, generator=g).to(BF)
+    st0 = 0.1 * torch.randn(n_lanes, nv, dk, dv, device=DEV, generator=g)
+    seg_lane = torch.randperm(n_lanes, generator=torch.Generator().manual_seed(1))[:lanes].int().to(DEV)
+    cs1, st1 = cs0.clone(), st0.clone()
+    out = ops.deltanet_decode(proj, cs1, conv_w, a_log, dt_bias, st1, norm_w, seg_lane, nk, nv, dk, dv, 1e-6)
+    # the separate kernels on copies
+    cs2, st2 = cs0.clone(), st0.clone()
+    cu = torch.arange(lanes + 1, dtype=torch.int32, device=DEV)
+    lanes_h, cu_h = seg_lane.tolist(), list(range(lanes + 1))
+    qkv = ops.causal_conv_varlen(proj[:, :C], cs2, conv_w, seg_lane, cu, lanes_h, cu_h)
+    core = ops.gated_delta_varlen(qkv, proj[:, C + nv * dv:], a_log, dt_bias, st2, seg_lane, cu, nk, nv, dk, dv,
+                                  lanes_h, cu_h)
+    exp = ops.gated_rmsnorm(core, proj[:, C:C + nv * dv].reshape(lanes, nv, dv), norm_w, 1e-6).reshape(lanes, -1)
+    torch.cuda.synchronize()
+    assert torch.equal(cs1, cs2)
+    assert (st1 - st2).abs().max().item() < 1e-4 * st2.abs().max().item() + 1e-6
+    close(out, exp, rtol=2e-2, atol=2e-2)
+    status_ok()
