@@ -357,7 +357,7 @@ Tensor moe_routed_bf16(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor w2
 
 // Block-scaled path: weights' e8m0 scales pre-arranged in 512-byte chunks (s13c / s2c).
 Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
-                     int64_t first, int64_t count) {
+                     int64_t first, int64_t count, bool tiled) {
   CHECK_BF16(h);
   TORCH_CHECK(h.is_contiguous(), "moe: h contiguous");
   const int T = h.size(0), H = h.size(1), k = topi.size(1);
@@ -381,20 +381,22 @@ Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c
   const long tiles = count + (cap + BN - 1) / BN;
   const int KM = H > I ? H : I;
   auto u8 = h.options().dtype(at::kByte);
-  Tensor hi = at::empty({(long)cap * KM}, u8), lo = at::empty({(long)cap * KM}, u8);
-  Tensor sfh = at::empty({tiles * (KM / 128) * 512}, u8), sfl = at::empty({tiles * (KM / 128) * 512}, u8);
+  // hi plane then lo plane; scale chunks either hi then lo regions, or (merged) per chunk hi|lo
+  const bool merged = qb::mx_merged(tiled, BN);
+  const long plane = ((long)cap * KM + 127) / 128 * 128, sf_plane = tiles * (KM / 128) * 512;
+  Tensor hl = at::empty({2 * plane}, u8), sf = at::empty({2 * sf_plane}, u8);
   Tensor inter = at::empty({cap, I}, h.options());
   Tensor y2 = at::empty({cap, H}, h.options());
-  uint8_t *hp = hi.data_ptr<uint8_t>(), *lp = lo.data_ptr<uint8_t>();
-  uint8_t *shp = sfh.data_ptr<uint8_t>(), *slp = sfl.data_ptr<uint8_t>();
+  uint8_t *hp = hl.data_ptr<uint8_t>(), *lp = hp + plane;
+  uint8_t *shp = sf.data_ptr<uint8_t>(), *slp = merged ? shp : shp + sf_plane;
   LAUNCH(qb::mx_quant(h.data_ptr(), perm_tok, n_assign, cap, H, offsets, counts, tstart, count, BN, hp, lp, shp, slp,
-                      stream()));
+                      stream(), merged));
   LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w13.data_ptr<uint8_t>(), s13c.data_ptr<uint8_t>(), n13, H, offsets,
-                         counts, tstart, count, BN, 1, inter.data_ptr(), I, err_ptr(h), stream()));
+                         counts, tstart, count, BN, 1, inter.data_ptr(), I, err_ptr(h), stream(), tiled));
   LAUNCH(qb::mx_quant(inter.data_ptr(), nullptr, n_assign, cap, I, offsets, counts, tstart, count, BN, hp, lp, shp,
-                      slp, stream()));
+                      slp, stream(), merged));
   LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w2.data_ptr<uint8_t>(), s2c.data_ptr<uint8_t>(), H, I, offsets,
-                         counts, tstart, count, BN, 0, y2.data_ptr(), H, err_ptr(h), stream()));
+                         counts, tstart, count, BN, 0, y2.data_ptr(), H, err_ptr(h), stream(), tiled));
   LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream()));
   return out;
 }
@@ -492,6 +494,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_fa", &attention_fa);
   m.def("moe_routed_mx", &moe_routed_mx);
   m.def("stamp", &stamp);
+  m.def("mx_probe", []() {
+    Tensor t = at::zeros({8}, at::kLong);
+    TORCH_CHECK(qb::mx_probe_read(reinterpret_cast<unsigned long long*>(t.data_ptr<int64_t>())) == 0, "mx_probe");
+    return t;
+  });
   m.def("deltanet_decode", &deltanet_decode);
   m.def("gated_delta_chunked", &gated_delta_chunked);
   m.def("causal_conv_varlen", &causal_conv_varlen);

@@ -64,10 +64,15 @@ int mx_token_tile(int cap, int count);
 int mx_tile_prefix(const int* counts, int count, int BN, int* tstart, cudaStream_t s);
 int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, const int* offsets, const int* counts,
              const int* tstart, int count, int BN, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi, uint8_t* sf_lo,
-             cudaStream_t s);
+             cudaStream_t s, bool merged = false);
+// diagnostic wait-cycle counters of the block-scaled MoE kernel (QB_MX_PROBE=1), read and cleared
+int mx_probe_read(unsigned long long* out);
+// merged activation buffers are used (tiled codes with one TMA box per operand)
+bool mx_merged(bool tiled, int BN);
 int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, const uint8_t* sf_lo, int cap,
                 const uint8_t* wq, const uint8_t* sfa, int n_rows, int K, const int* offsets, const int* counts,
-                const int* tstart, int count, int BN, int act, void* out, int out_cols, int* err, cudaStream_t s);
+                const int* tstart, int count, int BN, int act, void* out, int out_cols, int* err, cudaStream_t s,
+                bool tiled = false);
 // tcgen05 flash attention (attention.cu); tiles = [n_tiles][segment, row0, rows]; splits > 1 splits
 // every tile's key range (partials in ws, merged by a second kernel)
 int fa_prefill(const void* q, const void* kc, const void* vc, long cache_rows, const int* table, int max_blocks,

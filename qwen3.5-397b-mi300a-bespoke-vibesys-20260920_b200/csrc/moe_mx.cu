@@ -45,7 +45,7 @@ using bf16 = __nv_bfloat16;
 constexpr int MX_THREADS = 256;
 constexpr int MX_SK = 128;            // K per stage: one 128-byte swizzle atom of each operand
 constexpr int MX_CHUNK = 512;         // bytes of one scale chunk (128 rows x 4 K-blocks)
-constexpr int MX_MAX_EXPERTS = 1024;
+constexpr int MX_MAX_EXPERTS = 512;  // experts per rank (the model has 512)
 
 template <int BN>
 struct MxCfg {
@@ -54,11 +54,16 @@ struct MxCfg {
   static constexpr int STAGE = A + 2 * B;        // multiple of 1024
   static constexpr int SF = 3 * MX_CHUNK;        // weight, hi and lo scale chunks per stage
   static constexpr int STAGING = BN * 128 * 2;   // one output tile (bf16)
-  static constexpr int PREFIX = (4 * (MX_MAX_EXPERTS + 1) + 15) / 16 * 16;  // keeps the mbarriers after it 8-byte aligned
+  // token-tile prefix, counts and offsets of the experts in shared memory (16-byte multiple: the
+  // mbarriers after it stay aligned)
+  static constexpr int PREFIX = (4 * (3 * MX_MAX_EXPERTS + 1) + 15) / 16 * 16;
   static constexpr int BUDGET = 210 * 1024 - STAGING - PREFIX;
   static constexpr int STAGES = BUDGET / (STAGE + SF) > 12 ? 12 : BUDGET / (STAGE + SF);
   static constexpr int SMEM = 1024 + STAGES * STAGE + STAGES * SF + STAGING + PREFIX + 1024;
-  static constexpr int SF_COL = 2 * BN;          // TMEM: accumulators [0, 2 BN), then 12 columns per stage
+  // TMEM: two accumulators of ACC columns (2 BN: the hi and lo products side by side when BN <= 64),
+  // then 12 scale columns per stage
+  static constexpr int ACC = BN <= 64 ? 2 * BN : BN;
+  static constexpr int SF_COL = 2 * ACC;
   static constexpr int TMEM_COLS = 512;
   static_assert(SF_COL + 12 * STAGES <= TMEM_COLS, "tensor memory overflow");
   static_assert((STAGES * (STAGE + SF) + STAGING + PREFIX) % 16 == 0, "mbarriers must stay aligned");
@@ -78,7 +83,17 @@ struct MxArgs {
   int count;
   int act;
   int* err;
+  int tiled;               // weights re-laid so that every (128-row tile, K stage) block is contiguous
+  int wide;                // tiled only: one 128-row weight box and one BN-row box per token tile
+  int probe;               // diagnostics: accumulate the roles' wait cycles into g_mx_probe
 };
+
+// Diagnostic cycle counters (QB_MX_PROBE=1): [0] producer waiting for a free stage, [1] producer
+// total, [2] MMA issuer waiting for a full stage, [3] MMA issuer total, [4] MMA waiting for the
+// epilogue to free an accumulator, [5] producer cycles issuing a stage's copies, [6] MMA issuer
+// cycles issuing a stage's scale copies and MMAs, [7] stages. Summed over CTAs; read (and
+// cleared) by mx_probe_read.
+__device__ unsigned long long g_mx_probe[8];
 
 // e8m0 x e2m1 (A) x e4m3 (B), fp32 accumulate, M = 128, N = n, K-major operands.
 __host__ __device__ constexpr uint32_t idesc_mxf8f6f4(int n) {
@@ -142,7 +157,13 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
   const int kstages = a.K / MX_SK;
   const bool gu = a.act == 1;
 
+  int* cnts = tstart + MX_MAX_EXPERTS + 1;
+  int* offs = cnts + MX_MAX_EXPERTS;
   for (int i = threadIdx.x; i <= a.count; i += blockDim.x) tstart[i] = a.tstart[i];
+  for (int i = threadIdx.x; i < a.count; i += blockDim.x) {
+    cnts[i] = a.counts[i];
+    offs[i] = a.offsets[i];
+  }
   if (threadIdx.x == 0) {
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -169,15 +190,13 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
   const int units = tstart[a.count] * n_tiles;
+  // unit u -> (expert e, weight tile nt, token tile tt). Each role walks its units in increasing
+  // order, so e (the last expert whose first token tile is <= tt) only moves forward from the
+  // caller's previous value.
   auto unit = [&](int u, int& e, int& nt, int& tt) {
     tt = u / n_tiles;
     nt = u % n_tiles;
-    int lo = 0, hi = a.count - 1;  // last expert whose first tile is <= tt
-    while (lo < hi) {
-      const int mid = (lo + hi + 1) >> 1;
-      if (tstart[mid] <= tt) lo = mid; else hi = mid - 1;
-    }
-    e = lo;
+    while (e + 1 < a.count && tstart[e + 1] <= tt) ++e;
   };
   auto wrow = [&](int nt, int r) -> int {
     return gu ? (r < 64 ? nt * 64 + r : a.n_rows / 2 + nt * 64 + (r - 64)) : nt * 128 + r;
@@ -187,76 +206,141 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     // ---------------------------------------------------------------- producer
     if (elect_one()) {
       int it = 0;
+      long long pw = 0, pi = 0, w1 = 0;
+      const long long p0 = clock64();
+      int e = 0;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
-        int e, nt, tt;
+        int nt, tt;
         unit(u, e, nt, tt);
         const int m0 = (tt - tstart[e]) * BN;
-        const int ne = mx_cols<BN>(a.counts[e] - m0);
-        const int row_b = a.offsets[e] + m0;
+        const int ne = mx_cols<BN>(cnts[e] - m0);
+        const int row_b = offs[e] + m0;
         const long erow = (long)e * a.n_rows;
         const uint8_t* sfa_u = a.sfa + ((long)e * n_tiles + nt) * kstages * MX_CHUNK;
         const uint8_t* sfh_u = a.sfb_hi + (long)tt * kstages * MX_CHUNK;
         const uint8_t* sfl_u = a.sfb_lo + (long)tt * kstages * MX_CHUNK;
         for (int ks = 0; ks < kstages; ++ks, ++it) {
           const int s = it % C::STAGES;
+          const long long w0 = a.probe ? clock64() : 0;
           if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) goto prod_done;
+          if (a.probe) {
+            w1 = clock64();
+            pw += w1 - w0;
+          }
           uint8_t* st = stages + s * C::STAGE;
           uint8_t* sf = sfs + s * C::SF;
           // the fp4 tile counts its global (packed) bytes: half of its shared-memory footprint
-          mbar_expect_tx(&full[s], C::A / 2 + 2 * ne * MX_SK + 3 * MX_CHUNK);
-          tma_load_2d(st, &tmW, &full[s], ks * MX_SK, (int)(erow + wrow(nt, 0)));
-          tma_load_2d(st + 64 * MX_SK, &tmW, &full[s], ks * MX_SK, (int)(erow + wrow(nt, 64)));
-          for (int t = 0; t < ne; t += 16) {
+          if (a.wide) {  // one box per operand: the 8 KB weight block, BN token rows of hi and lo
+            mbar_expect_tx(&full[s], C::A / 2 + 2 * BN * MX_SK + 2 * MX_CHUNK);
+            const int trow = (int)((((long)e * n_tiles + nt) * kstages + ks) * 128);
+            tma_load_2d(st, &tmW, &full[s], 0, trow);
+            tma_load_3d(st + C::A, &tmH, &full[s], ks * MX_SK, row_b, 0);  // hi then lo plane
+            bulk_g2s(sf, sfa_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
+            bulk_g2s(sf + MX_CHUNK, a.sfb_hi + ((long)tt * kstages + ks) * MX_CHUNK, MX_CHUNK, &full[s]);
+          } else {
+            mbar_expect_tx(&full[s], C::A / 2 + 2 * ne * MX_SK + 3 * MX_CHUNK);
+          }
+          if (a.wide) {
+          } else if (a.tiled) {  // one contiguous 8 KB block: rows (tile, stage, 0..127) of 64 bytes
+            const int trow = (int)((((long)e * n_tiles + nt) * kstages + ks) * 128);
+            tma_load_2d(st, &tmW, &full[s], 0, trow);
+            tma_load_2d(st + 64 * MX_SK, &tmW, &full[s], 0, trow + 64);
+          } else {
+            tma_load_2d(st, &tmW, &full[s], ks * MX_SK, (int)(erow + wrow(nt, 0)));
+            tma_load_2d(st + 64 * MX_SK, &tmW, &full[s], ks * MX_SK, (int)(erow + wrow(nt, 64)));
+          }
+          for (int t = 0; !a.wide && t < ne; t += 16) {
             tma_load_2d(st + C::A + t * MX_SK, &tmH, &full[s], ks * MX_SK, row_b + t);
             tma_load_2d(st + C::A + C::B + t * MX_SK, &tmL, &full[s], ks * MX_SK, row_b + t);
           }
-          bulk_g2s(sf, sfa_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
-          bulk_g2s(sf + MX_CHUNK, sfh_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
-          bulk_g2s(sf + 2 * MX_CHUNK, sfl_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
+          if (!a.wide) {
+            bulk_g2s(sf, sfa_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
+            bulk_g2s(sf + MX_CHUNK, sfh_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
+            bulk_g2s(sf + 2 * MX_CHUNK, sfl_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
+          }
           *issued_p = it + 1;
+          if (a.probe) pi += clock64() - w1;
         }
       }
-    prod_done:;
+    prod_done:
+      if (a.probe) {
+        atomicAdd(&g_mx_probe[0], (unsigned long long)pw);
+        atomicAdd(&g_mx_probe[1], (unsigned long long)(clock64() - p0));
+        atomicAdd(&g_mx_probe[5], (unsigned long long)pi);
+        atomicAdd(&g_mx_probe[7], (unsigned long long)it);
+      }
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     if (elect_one()) {
       int it = 0, ti = 0;
       bool ok = true;
+      long long mw = 0, aw = 0, mi = 0, m1 = 0;
+      const long long m0c = clock64();
+      int e = 0;
       for (int u = blockIdx.x; u < units && ok && !*abort_flag; u += gridDim.x, ++ti) {
-        int e, nt, tt;
-        unit(u, e, nt, tt);
-        const int m0 = (tt - tstart[e]) * BN;
-        const uint32_t idesc = idesc_mxf8f6f4(mx_cols<BN>(a.counts[e] - m0));
+        // wide: hi and lo token rows form one N = 2 BN operand (all BN rows of each: the lo rows start
+        // at BN); else one MMA per term with N = the tile's valid rows
+        uint32_t idesc = idesc_mxf8f6f4(2 * BN);
+        if (!a.wide) {
+          int nt, tt;
+          unit(u, e, nt, tt);
+          idesc = idesc_mxf8f6f4(mx_cols<BN>(cnts[e] - (tt - tstart[e]) * BN));
+        }
         const int acc = ti & 1;
+        const long long a0 = a.probe ? clock64() : 0;
         if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
+        if (a.probe) aw += clock64() - a0;
         tc_fence_after();
-        const uint32_t d = tmem + acc * BN;
+        const uint32_t d = tmem + acc * C::ACC;
         for (int ks = 0; ks < kstages; ++ks, ++it) {
           const int s = it % C::STAGES;
+          const long long w0 = a.probe ? clock64() : 0;
           if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
             ok = false;
             break;
           }
+          if (a.probe) {
+            m1 = clock64();
+            mw += m1 - w0;
+          }
           tc_fence_after();
           const uint32_t sf_t = tmem + C::SF_COL + s * 12;
           const uint32_t sf_s = smem_u32(sfs + s * C::SF);
-          tmem_cp_chunk(sf_t, sf_s);
-          tmem_cp_chunk(sf_t + 4, sf_s + MX_CHUNK);
-          tmem_cp_chunk(sf_t + 8, sf_s + 2 * MX_CHUNK);
           const uint32_t sbase = smem_u32(stages + s * C::STAGE);
           const uint64_t da = desc_sw128(sbase), dh = desc_sw128(sbase + C::A), dl = desc_sw128(sbase + C::A + C::B);
+          if (a.wide) {
+            tmem_cp_chunk(sf_t, sf_s);
+            tmem_cp_chunk(sf_t + 4, sf_s + MX_CHUNK);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {  // K-block j of the stage: 32 codes = 32 shared-memory bytes
-            const uint32_t id_j = idesc | ((uint32_t)j << 29) | ((uint32_t)j << 4);
-            const uint32_t bsel = (uint32_t)j << 30;
-            mma_mx(d, da + 2 * j, dh + 2 * j, id_j, (sf_t) | bsel, (sf_t + 4) | bsel, (ks | j) != 0);
-            mma_mx(d, da + 2 * j, dl + 2 * j, id_j, (sf_t) | bsel, (sf_t + 8) | bsel, true);
+            for (int j = 0; j < 4; ++j) {  // K-block j: hi | lo products into accumulator columns [0, 2 BN)
+              const uint32_t id_j = idesc | ((uint32_t)j << 29) | ((uint32_t)j << 4);
+              const uint32_t bsel = (uint32_t)j << 30;
+              mma_mx(d, da + 2 * j, dh + 2 * j, id_j, (sf_t) | bsel, (sf_t + 4) | bsel, (ks | j) != 0);
+            }
+          } else {
+            tmem_cp_chunk(sf_t, sf_s);
+            tmem_cp_chunk(sf_t + 4, sf_s + MX_CHUNK);
+            tmem_cp_chunk(sf_t + 8, sf_s + 2 * MX_CHUNK);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // K-block j of the stage: 32 codes = 32 shared-memory bytes
+              const uint32_t id_j = idesc | ((uint32_t)j << 29) | ((uint32_t)j << 4);
+              const uint32_t bsel = (uint32_t)j << 30;
+              mma_mx(d, da + 2 * j, dh + 2 * j, id_j, (sf_t) | bsel, (sf_t + 4) | bsel, (ks | j) != 0);
+              mma_mx(d, da + 2 * j, dl + 2 * j, id_j, (sf_t) | bsel, (sf_t + 8) | bsel, true);
+            }
           }
           mma_commit(&empty[s]);
+          if (a.probe) mi += clock64() - m1;
         }
         if (!ok) break;
         mma_commit(&acc_full[acc]);
+      }
+      if (a.probe) {
+        atomicAdd(&g_mx_probe[2], (unsigned long long)mw);
+        atomicAdd(&g_mx_probe[3], (unsigned long long)(clock64() - m0c));
+        atomicAdd(&g_mx_probe[4], (unsigned long long)aw);
+        atomicAdd(&g_mx_probe[6], (unsigned long long)mi);
       }
       mma_commit(drain);
       mbar_wait(drain, 0, a.err, ERR_DRAIN, nullptr);
@@ -267,19 +351,27 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     const int row = ew * 32 + lane;
     const int et = threadIdx.x - 128;
     int ti = 0;
+    int e = 0;
     for (int u = blockIdx.x; u < units; u += gridDim.x, ++ti) {
-      int e, nt, tt;
+      int nt, tt;
       unit(u, e, nt, tt);
       const int m0 = (tt - tstart[e]) * BN;
-      const int cnt = a.counts[e];
-      const int row_b = a.offsets[e] + m0;
+      const int cnt = cnts[e];
+      const int row_b = offs[e] + m0;
       const int acc = ti & 1;
       if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) break;
       tc_fence_after();
       const int ne = mx_cols<BN>(cnt - m0);
       for (int c0 = 0; c0 < ne; c0 += 16) {
         float v[16];
-        tmem_ld16(tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16), v);
+        const uint32_t ta = tmem + acc * C::ACC + c0 + ((uint32_t)(ew * 32) << 16);
+        tmem_ld16(ta, v);
+        if (a.wide) {  // hi products in columns [0, BN), lo products in [BN, 2 BN)
+          float vl[16];
+          tmem_ld16(ta + BN, vl);
+#pragma unroll
+          for (int j = 0; j < 16; ++j) v[j] += vl[j];
+        }
 #pragma unroll
         for (int j = 0; j < 16; ++j) {
           bf16 o = __float2bfloat16(v[j]);
@@ -331,7 +423,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 // consecutive elements, so 4 lanes form one 32-element block.
 __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_rows, int K, int wpr, const int* offsets,
                                 const int* tstart, int count, int BN, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi,
-                                uint8_t* sf_lo) {
+                                uint8_t* sf_lo, int cstride, int lo_rows) {
   const int lane = threadIdx.x % 32;
   const int w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int a = w / wpr, part = w % wpr;  // `wpr` warps share a row when there are few rows
@@ -349,7 +441,7 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
   const bf16* src = x + (long)(perm ? perm[a] : a) * K;
   uint8_t* hrow = hi + (long)a * K;
   uint8_t* lrow = lo + (long)a * K;
-  const long sf_tile = (long)tt * (K / MX_SK) * MX_CHUNK;
+  const long sf_tile = (long)tt * (K / MX_SK) * cstride;  // cstride: bytes from one chunk to the next
   for (int kbase = kbeg; kbase < kend; kbase += 256) {  // warp-uniform trip count (shuffles below)
     const int k0 = kbase + lane * 8;
     const bool valid = k0 < kend;                       // segments are multiples of 128, not always of 256
@@ -381,9 +473,9 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
     *reinterpret_cast<uint2*>(lrow + k0) = make_uint2(lw[0], lw[1]);
     if ((lane & 3) == 0) {
       const int kb = k0 / 32;
-      const long off = sf_tile + (long)(kb / 4) * MX_CHUNK + mx_chunk_offset(rr, kb % 4);
-      sf_hi[off] = (uint8_t)(E + 127);
-      sf_lo[off] = (uint8_t)(E - 4 + 127);
+      const long cb = sf_tile + (long)(kb / 4) * cstride;
+      sf_hi[cb + mx_chunk_offset(rr, kb % 4)] = (uint8_t)(E + 127);
+      sf_lo[cb + mx_chunk_offset(rr + lo_rows, kb % 4)] = (uint8_t)(E - 4 + 127);
     }
   }
 }
@@ -433,6 +525,34 @@ static int mx_tmap(CUtensorMap* m, const void* base, long rows, long cols, long 
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 
+// 3-D map of the hi and lo activation planes [2][rows][cols] (bytes), box (128, box_rows, 2):
+// one load brings a token tile's hi rows followed by its lo rows.
+static int mx_tmap_planes(CUtensorMap* m, const void* base, long rows, long cols, long plane_bytes, int box_rows) {
+  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)cols, (cuuint64_t)plane_bytes};
+  cuuint32_t box[3] = {128, (cuuint32_t)box_rows, 2};
+  cuuint32_t es[3] = {1, 1, 1};
+  CUresult r = mx_encode()(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 3, const_cast<void*>(base), dims, strides, box, es,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+int mx_probe_read(unsigned long long* out) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_mx_probe, sizeof(g_mx_probe));
+  if (e != cudaSuccess) return (int)e;
+  static const unsigned long long zero[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  return (int)cudaMemcpyToSymbol(g_mx_probe, zero, sizeof(zero));
+}
+
+// Merged activation layout (wide boxes over tiled codes, token tiles of at most 64): the lo plane
+// right after the hi plane, and one scale chunk per (token tile, K stage) holding the hi scales in
+// rows [0, BN) and the lo scales in rows [BN, 2 BN), the rows of the one N = 2 BN MMA operand.
+bool mx_merged(bool tiled, int BN) {
+  static const bool wide_env = !getenv("QB_MX_WIDE") || atoi(getenv("QB_MX_WIDE")) != 0;
+  return tiled && wide_env && BN <= 64;
+}
+
 static int mx_sms() {
   static int n = 0;
   if (!n) {
@@ -476,7 +596,7 @@ int mx_tile_prefix(const int* counts, int count, int BN, int* tstart, cudaStream
 
 int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, const int* offsets, const int* counts,
              const int* tstart, int count, int BN, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi, uint8_t* sf_lo,
-             cudaStream_t s) {
+             cudaStream_t s, bool merged) {
   if (!cap) return 0;
   if (K % MX_SK) return -1;
   (void)counts;
@@ -485,26 +605,34 @@ int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, 
   while ((long)cap * wpr < 2048 && (K / (wpr * 2)) % 256 == 0) wpr *= 2;
   const long warps = (long)cap * wpr;
   mx_quant_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const bf16*)x, perm, n_rows, K, wpr, offsets, tstart,
-                                                               count, BN, hi, lo, sf_hi, sf_lo);
+                                                               count, BN, hi, lo, sf_hi, sf_lo, MX_CHUNK,
+                                                               merged ? BN : 0);
   return (int)cudaGetLastError();
 }
 
 int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, const uint8_t* sf_lo, int cap,
                 const uint8_t* wq, const uint8_t* sfa, int n_rows, int K, const int* offsets, const int* counts,
-                const int* tstart, int count, int BN, int act, void* out, int out_cols, int* err, cudaStream_t s) {
+                const int* tstart, int count, int BN, int act, void* out, int out_cols, int* err, cudaStream_t s,
+                bool tiled) {
   if (!cap || !count) return 0;
   if (n_rows % 128 || K % MX_SK || count > MX_MAX_EXPERTS) return -1;
   if ((reinterpret_cast<uintptr_t>(wq) & 31) || (reinterpret_cast<uintptr_t>(hi) & 15) ||
       (reinterpret_cast<uintptr_t>(lo) & 15))
     return -2;
   CUtensorMap tw, th, tl;
-  int r = mx_tmap(&tw, wq, (long)count * n_rows, K, K / 2, 64, true);
+  // row-major codes [count * n_rows][K/2 bytes], or tiled: [count * n_rows * K/128][64 bytes]
+  const bool wide = mx_merged(tiled, BN);
+  if (wide && (lo <= hi || ((lo - hi) & 15))) return -3;
+  int r = tiled ? mx_tmap(&tw, wq, (long)count * n_rows * (K / MX_SK), MX_SK, MX_SK / 2, wide ? 128 : 64, true)
+                : mx_tmap(&tw, wq, (long)count * n_rows, K, K / 2, 64, true);
   if (r) return 1000 + r;
-  r = mx_tmap(&th, hi, cap, K, K, 16, false);
+  r = wide ? mx_tmap_planes(&th, hi, cap, K, lo - hi, BN) : mx_tmap(&th, hi, cap, K, K, 16, false);
   if (r) return 2000 + r;
   r = mx_tmap(&tl, lo, cap, K, K, 16, false);
   if (r) return 3000 + r;
-  MxArgs a{sfa, sf_hi, sf_lo, offsets, counts, tstart, out, out_cols, n_rows, K, count, act, err};
+  static const int probe = getenv("QB_MX_PROBE") ? atoi(getenv("QB_MX_PROBE")) : 0;
+  MxArgs a{sfa, sf_hi, sf_lo, offsets, counts, tstart, out, out_cols, n_rows, K, count, act, err, tiled ? 1 : 0,
+           wide ? 1 : 0, probe};
   switch (BN) {
     case 16: return mx_launch<16>(tw, th, tl, a, s);
     case 32: return mx_launch<32>(tw, th, tl, a, s);

@@ -323,14 +323,39 @@ def mx_scale_chunks(s: torch.Tensor, gate_up: bool) -> torch.Tensor:
     return x.permute(0, 1, 4, 3, 2, 5).contiguous().reshape(E, nt, kb // 4, 512)
 
 
+def mx_tile_codes(w: torch.Tensor, gate_up: bool) -> torch.Tensor:
+    """Packed e2m1 codes [E, rows, K/2] -> the same bytes with every (128-row weight tile, 128-K
+    stage) block contiguous: [E, rows/128, K/128, 128 rows, 64 bytes], returned in the original
+    shape. One TMA box of the block-scaled kernel then reads 4 KB of consecutive memory instead
+    of 64 rows of 64 bytes each 2 KB apart. For gate_up a tile's rows are 64 gate rows followed
+    by the matching 64 up rows (as for the scale chunks)."""
+    E, rows, kb2 = w.shape
+    nt, ks = rows // 128, kb2 // 64
+    if gate_up:
+        t = w.view(E, 2, nt, 64, ks, 64).permute(0, 2, 4, 1, 3, 5)  # [E, tile, stage, gate|up, r, byte]
+    else:
+        t = w.view(E, nt, 128, ks, 64).permute(0, 1, 3, 2, 4)       # [E, tile, stage, r, byte]
+    return t.contiguous().view(E, rows, kb2)
+
+
 def prepare_experts(experts: dict, keep_rows: bool = False) -> dict:
-    """Add the chunked scale layout the block-scaled CUDA path reads (``s13c``/``s2c``); drop the
-    row-major scales unless ``keep_rows`` (the CPU reference and the f16-decode path read them)."""
+    """Add the layouts the block-scaled CUDA path reads: chunked scales (``s13c``/``s2c``) and
+    tile-contiguous codes. Without ``keep_rows`` the row-major scales are dropped and the codes
+    replaced in place (``tiled``); with it (the CPU reference and the f16-decode path read the
+    row-major forms) the tiled codes are kept beside them as ``w13t``/``w2t``."""
     if "s13" in experts and "s13c" not in experts and experts["s13"].is_cuda:
         experts["s13c"] = mx_scale_chunks(experts["s13"], True)
         experts["s2c"] = mx_scale_chunks(experts["s2"], False)
-        if not keep_rows:
+        if not flags.get("QB_MX_TILED"):
+            if not keep_rows:
+                del experts["s13"], experts["s2"]
+            return experts
+        w13t, w2t = mx_tile_codes(experts["w13"], True), mx_tile_codes(experts["w2"], False)
+        if keep_rows:
+            experts["w13t"], experts["w2t"] = w13t, w2t
+        else:
             del experts["s13"], experts["s2"]
+            experts["w13"], experts["w2"], experts["tiled"] = w13t, w2t, True
     return experts
 
 
@@ -344,8 +369,11 @@ def moe_routed(h, topw, topi, experts, first, count):
     other ranks' experts). fp32 accumulation, rounded once to ``h.dtype``."""
     if _cuda(h):
         if "s13c" in experts and (moe_impl() == "mx" or "s13" not in experts):
+            if "w13t" in experts:
+                return ext().moe_routed_mx(h, topw, topi, experts["w13t"], experts["s13c"], experts["w2t"],
+                                           experts["s2c"], first, count, True)
             return ext().moe_routed_mx(h, topw, topi, experts["w13"], experts["s13c"], experts["w2"],
-                                       experts["s2c"], first, count)
+                                       experts["s2c"], first, count, bool(experts.get("tiled", False)))
         if "s13" in experts and moe_impl() == "mx" and h.shape[1] % 128 == 0 \
                 and experts["w2"].shape[2] * 2 % 128 == 0:
             prepare_experts(experts, keep_rows=True)

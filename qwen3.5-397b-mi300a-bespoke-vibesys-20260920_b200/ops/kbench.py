@@ -29,6 +29,8 @@ import os
 import torch
 
 from . import core as ops
+from ._ext import ext
+from ..utils import flags
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 _DEFAULT_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}
@@ -87,9 +89,23 @@ def case_moe(tokens: int, iters: int, pk: dict, experts: int = 512, top_k: int =
     tw, ti = ops.router_topk(lg, top_k)
     active = int((torch.bincount(ti.flatten().long(), minlength=experts) > 0).sum())
     per_expert = (2 * inter * hidden + hidden * inter) // 2 * (1 + 1 / 16)
+    probe = flags.get("QB_MX_PROBE")
+    if probe:
+        ops.moe_routed(h, tw, ti, ex, 0, experts)  # the experts' layouts are prepared on first use
+        torch.cuda.synchronize()
+        ext().mx_probe()
     ms = _time(lambda: ops.moe_routed(h, tw, ti, ex, 0, experts), iters)
     flops = 2 * tokens * top_k * 3 * hidden * inter
-    return _report(f"moe_T{tokens}", ms, active * per_expert, flops, pk, active_experts=active)
+    extra = {}
+    if probe:  # share of each single-thread role's cycles spent waiting
+        p = ext().mx_probe().tolist()
+        extra = {"producer_wait_free_stage": round(p[0] / max(1, p[1]), 3),
+                 "mma_wait_full_stage": round(p[2] / max(1, p[3]), 3),
+                 "mma_wait_accumulator": round(p[4] / max(1, p[3]), 3),
+                 "producer_issue_cycles_per_stage": round(p[5] / max(1, p[7]), 1),
+                 "mma_issue_cycles_per_stage": round(p[6] / max(1, p[7]), 1),
+                 "producer_cycles_per_stage": round(p[1] / max(1, p[7]), 1)}
+    return _report(f"moe_T{tokens}", ms, active * per_expert, flops, pk, active_experts=active, **extra)
 
 
 def case_gemm(tokens: int, iters: int, pk: dict, n: int = 12288, k: int = 4096, name: str = "") -> dict:

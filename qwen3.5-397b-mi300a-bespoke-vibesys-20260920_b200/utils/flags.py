@@ -41,6 +41,10 @@ def _def(name, kind, default, doc, lockstep=False, native=False) -> None:
 _def("QB_MOE_IMPL", str, "mx", "routed-expert kernel: mx (block-scaled fp8 tcgen05), f16 (fp4 decoded to "
      "f16 in TMEM), bf16 (dequantised weights)", lockstep=True)
 _def("QB_MX_BN_MAX", int, 64, "largest token tile of the block-scaled MoE kernel", native=True)
+_def("QB_MX_TILED", bool, True, "block-scaled MoE: expert codes re-laid tile-contiguous at load")
+_def("QB_MX_WIDE", bool, True, "block-scaled MoE, tiled codes: one TMA box per operand and stage", native=True)
+_def("QB_MX_PROBE", bool, False, "block-scaled MoE: count the producer / MMA wait cycles (diagnostic)",
+     native=True)
 _def("QB_MOE_BN_MAX", int, 64, "largest token tile of the f16-decode MoE kernel", native=True)
 _def("QB_MOE_SMEM_A", bool, False, "f16-decode MoE: stage decoded weights in shared memory", native=True)
 _def("QB_FA", bool, True, "tcgen05 flash attention for full-attention layers (else the CUDA-core kernel)",

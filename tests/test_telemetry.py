@@ -149,3 +149,23 @@ def test_model_stamps_on_cpu():
     assert tags[0] == "start" and tags[-1] == "lm_head"
     assert tags.count("moe") == n and tags.count("allreduce") == 2 * n
     assert tags.count("attention") + tags.count("deltanet") == n
+
+
+def test_mx_tile_codes_layout():
+    """Tile-contiguous expert codes: block (expert, tile, stage) holds rows of that tile (gate rows
+    then the matching up rows for gate_up) and bytes of that K stage, in order."""
+    from qwen35_b200.ops.core import mx_tile_codes
+
+    E, rows, kb2 = 2, 256, 128  # 2 tiles, 2 stages
+    w = torch.randint(0, 256, (E, rows, kb2), dtype=torch.uint8)
+    for gate_up in (False, True):
+        t = mx_tile_codes(w, gate_up).view(E, rows // 128, kb2 // 64, 128, 64)
+        for e in range(E):
+            for nt in range(rows // 128):
+                for ks in range(kb2 // 64):
+                    for r in (0, 5, 63, 64, 100, 127):
+                        if gate_up:
+                            src = nt * 64 + r if r < 64 else rows // 2 + nt * 64 + (r - 64)
+                        else:
+                            src = nt * 128 + r
+                        assert torch.equal(t[e, nt, ks, r], w[e, src, ks * 64:(ks + 1) * 64])
