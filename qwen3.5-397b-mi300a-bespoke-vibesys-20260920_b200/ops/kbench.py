@@ -201,6 +201,34 @@ def case_deltanet(tokens: int, lanes: int, iters: int, pk: dict, nk: int = 16, n
     return _report(f"deltanet_T{tokens}_B{lanes}", ms, bytes_, flops, pk)
 
 
+def case_deltanet_decode(lanes: int, iters: int, pk: dict, nk: int = 16, nv: int = 64, dk: int = 128,
+                         dv: int = 128, layers: int = 8) -> dict:
+    """The fused one-token-per-lane DeltaNet mixer (conv, l2norm, gated delta step, gated
+    RMSNorm) from the input projection's output. ``layers`` distinct state pools are cycled so
+    that every call streams its lanes' fp32 states from HBM (as consecutive layers do); bytes =
+    state read + write, conv windows, projection row in, normed row out."""
+    C = 2 * nk * dk + nv * dv
+    g = _g(6)
+    proj = torch.randn(lanes, C + nv * dv + 2 * nv, device="cuda", generator=g).to(torch.bfloat16)
+    conv_w = (0.3 * torch.randn(C, 4, device="cuda", generator=g)).to(torch.bfloat16)
+    a_log = torch.log(torch.rand(nv, device="cuda", generator=g) * 15 + 1)
+    dtb = torch.rand(nv, device="cuda", generator=g)
+    norm_w = torch.ones(dv, device="cuda", dtype=torch.bfloat16)
+    pools = [(torch.randn(lanes, C, 3, device="cuda", generator=g).to(torch.bfloat16),
+              0.1 * torch.randn(lanes, nv, dk, dv, device="cuda", generator=g)) for _ in range(layers)]
+    seg = torch.arange(lanes, dtype=torch.int32, device="cuda")
+    i = [0]
+
+    def fn():
+        cs, rs = pools[i[0] % layers]
+        ops.deltanet_decode(proj, cs, conv_w, a_log, dtb, rs, norm_w, seg, nk, nv, dk, dv, 1e-6)
+        i[0] += 1
+
+    ms = _time(fn, max(iters, layers))
+    bytes_ = 2 * lanes * nv * dk * dv * 4 + 2 * lanes * C * 3 * 2 + proj.numel() * 2 + lanes * nv * dv * 2
+    return _report(f"deltanet_decode_B{lanes}", ms, bytes_, 4 * lanes * nv * dk * dv, pk)
+
+
 def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
     """Whole-model steps at the full geometry on one GPU (random weights; experts of the first
     layers reused by the rest, as the one-GPU benchmark does): one prefill of ``tokens`` new
@@ -271,7 +299,8 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="all",
-                    choices=["moe", "gemm", "gemm_shapes", "attn_prefill", "attn_decode", "deltanet", "model", "all"])
+                    choices=["moe", "gemm", "gemm_shapes", "attn_prefill", "attn_decode", "deltanet",
+                             "deltanet_decode", "model", "all"])
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--lanes", type=int, default=None)
@@ -296,6 +325,8 @@ def main(argv=None):
         run.append(case_attn_decode(a.lanes or 32, a.ctx or 6000, a.iters, pk))
     if a.case == "model":
         return case_model(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.lanes or 32)
+    if a.case in ("deltanet_decode", "all"):
+        run.append(case_deltanet_decode(a.lanes or 32, a.iters, pk))
     if a.case in ("deltanet", "all"):
         run.append(case_deltanet(a.tokens or 1, a.lanes or 32, a.iters, pk))
         if a.case == "all":
