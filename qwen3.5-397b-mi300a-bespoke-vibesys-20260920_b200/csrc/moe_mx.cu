@@ -118,6 +118,57 @@ __device__ __forceinline__ void tmem_cp_chunk(uint32_t taddr, uint32_t saddr) {
   asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(d) : "memory");
 }
 
+// Shared-memory-address (u32) forms of the per-stage operations, for the single-thread loops of
+// the wide path: they keep the stage ring in 32-bit shared addresses advanced by constants.
+__device__ __forceinline__ bool mbar_try_wait_s(uint32_t bar, uint32_t phase, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(phase), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait (as mbar_wait): false after QB_WAIT_NS or when another role aborted
+__device__ __forceinline__ bool mbar_wait_s(uint32_t bar, uint32_t phase, int* err, int code,
+                                            volatile int* abort_flag) {
+  if (mbar_try_wait_s(bar, phase, 0)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_s(bar, phase, 200000)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > QB_WAIT_NS) {
+      if (err) atomicCAS(err, 0, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void mbar_expect_tx_s(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_s(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_s(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                              int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void mma_commit_s(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
   asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
                    smem_u32(dst)),
@@ -204,7 +255,55 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
-    if (elect_one()) {
+    if (a.wide && elect_one()) {
+      // stage ring in 32-bit shared addresses; stage index and barrier parity advanced, not divided
+      const uint32_t st0 = smem_u32(stages), sf0 = smem_u32(sfs), full0 = smem_u32(full), empty0 = smem_u32(empty);
+      int it = 0, s = 0;
+      uint32_t ph = 1;  // parity of the empty barrier a first-round stage waits on (passes at once)
+      long long pw = 0, pi = 0, w1 = 0;
+      const long long p0 = clock64();
+      int e = 0;
+      constexpr uint32_t TX = C::A / 2 + 2 * BN * MX_SK + 2 * MX_CHUNK;
+      for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
+        int nt, tt;
+        unit(u, e, nt, tt);
+        const int row_b = offs[e] + (tt - tstart[e]) * BN;
+        const int wtile = e * n_tiles + nt;
+        int trow = wtile * kstages * 128;  // < 2^31: 512 experts x 32 tiles x 32 stages x 128
+        const uint8_t* sfw = a.sfa + (long)wtile * kstages * MX_CHUNK;
+        const uint8_t* sfb = a.sfb_hi + (long)tt * kstages * MX_CHUNK;
+        for (int kx = 0; kx < kstages * MX_SK; kx += MX_SK, ++it) {
+          const long long w0 = a.probe ? clock64() : 0;
+          if (!mbar_wait_s(empty0 + 8 * s, ph, a.err, ERR_TMA_WAIT, abort_flag)) goto prod_done_w;
+          if (a.probe) {
+            w1 = clock64();
+            pw += w1 - w0;
+          }
+          const uint32_t fb = full0 + 8 * s, st = st0 + s * C::STAGE, sf = sf0 + s * C::SF;
+          mbar_expect_tx_s(fb, TX);
+          tma_load_2d_s(st, &tmW, fb, 0, trow);
+          tma_load_3d_s(st + C::A, &tmH, fb, kx, row_b, 0);  // hi then lo plane
+          bulk_g2s_s(sf, sfw, MX_CHUNK, fb);
+          bulk_g2s_s(sf + MX_CHUNK, sfb, MX_CHUNK, fb);
+          trow += 128;
+          sfw += MX_CHUNK;
+          sfb += MX_CHUNK;
+          *issued_p = it + 1;
+          if (a.probe) pi += clock64() - w1;
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+      }
+    prod_done_w:
+      if (a.probe) {
+        atomicAdd(&g_mx_probe[0], (unsigned long long)pw);
+        atomicAdd(&g_mx_probe[1], (unsigned long long)(clock64() - p0));
+        atomicAdd(&g_mx_probe[5], (unsigned long long)pi);
+        atomicAdd(&g_mx_probe[7], (unsigned long long)it);
+      }
+    } else if (!a.wide && elect_one()) {
       int it = 0;
       long long pw = 0, pi = 0, w1 = 0;
       const long long p0 = clock64();
@@ -272,7 +371,65 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (elect_one()) {
+    if (a.wide && elect_one()) {
+      const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty), accf0 = smem_u32(acc_full),
+                     acce0 = smem_u32(acc_empty);
+      const uint64_t da0 = desc_sw128(smem_u32(stages)), db0 = desc_sw128(smem_u32(stages) + C::A);
+      const uint32_t sf_s0 = smem_u32(sfs);
+      const uint32_t idesc = idesc_mxf8f6f4(2 * BN);  // hi | lo rows: one N = 2 BN operand
+      int s = 0, ti = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      long long mw = 0, aw = 0, mi = 0, m1 = 0;
+      const long long m0c = clock64();
+      for (int u = blockIdx.x; u < units && ok && !*abort_flag; u += gridDim.x, ++ti) {
+        const int acc = ti & 1;
+        const long long a0 = a.probe ? clock64() : 0;
+        if (!mbar_wait_s(acce0 + 8 * acc, ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
+        if (a.probe) aw += clock64() - a0;
+        tc_fence_after();
+        const uint32_t d = tmem + acc * C::ACC;
+        for (int ks = 0; ks < kstages; ++ks) {
+          const long long w0 = a.probe ? clock64() : 0;
+          if (!mbar_wait_s(full0 + 8 * s, ph, a.err, ERR_MMA_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
+          if (a.probe) {
+            m1 = clock64();
+            mw += m1 - w0;
+          }
+          tc_fence_after();
+          const uint32_t sf_t = tmem + C::SF_COL + s * 12, sf_s = sf_s0 + s * C::SF;
+          const uint64_t so = (uint64_t)((s * C::STAGE) >> 4);  // descriptor address field: bytes / 16
+          const uint64_t da = da0 + so, dh = db0 + so;
+          tmem_cp_chunk(sf_t, sf_s);
+          tmem_cp_chunk(sf_t + 4, sf_s + MX_CHUNK);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {  // K-block j: hi | lo products into accumulator columns [0, 2 BN)
+            const uint32_t id_j = idesc | ((uint32_t)j << 29) | ((uint32_t)j << 4);
+            const uint32_t bsel = (uint32_t)j << 30;
+            mma_mx(d, da + 2 * j, dh + 2 * j, id_j, (sf_t) | bsel, (sf_t + 4) | bsel, (ks | j) != 0);
+          }
+          mma_commit_s(empty0 + 8 * s);
+          if (a.probe) mi += clock64() - m1;
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
+        }
+        if (!ok) break;
+        mma_commit_s(accf0 + 8 * acc);
+      }
+      if (a.probe) {
+        atomicAdd(&g_mx_probe[2], (unsigned long long)mw);
+        atomicAdd(&g_mx_probe[3], (unsigned long long)(clock64() - m0c));
+        atomicAdd(&g_mx_probe[4], (unsigned long long)aw);
+        atomicAdd(&g_mx_probe[6], (unsigned long long)mi);
+      }
+      mma_commit(drain);
+      mbar_wait(drain, 0, a.err, ERR_DRAIN, nullptr);
+    } else if (!a.wide && elect_one()) {
       int it = 0, ti = 0;
       bool ok = true;
       long long mw = 0, aw = 0, mi = 0, m1 = 0;
