@@ -47,17 +47,20 @@ constexpr int MX_SK = 128;            // K per stage: one 128-byte swizzle atom 
 constexpr int MX_CHUNK = 512;         // bytes of one scale chunk (128 rows x 4 K-blocks)
 constexpr int MX_MAX_EXPERTS = 512;  // experts per rank (the model has 512)
 
-template <int BN>
+// W: the wide path (tiled codes, one box per operand, one hi|lo MMA operand, two scale chunks
+// per stage: weight and activation); else three chunks (weight, hi, lo).
+template <int BN, bool W>
 struct MxCfg {
   static constexpr int A = 128 * MX_SK;          // fp4 tile, one byte per code in shared memory
   static constexpr int B = BN * MX_SK;           // one e4m3 token tile (hi or lo)
   static constexpr int STAGE = A + 2 * B;        // multiple of 1024
-  static constexpr int SF = 3 * MX_CHUNK;        // weight, hi and lo scale chunks per stage
+  static constexpr int SF = (W ? 2 : 3) * MX_CHUNK;  // scale chunks per stage
+  static constexpr int SF_COLS = W ? 8 : 12;     // their tensor-memory columns
   static constexpr int STAGING = BN * 128 * 2;   // one output tile (bf16)
   // token-tile prefix, counts and offsets of the experts in shared memory (16-byte multiple: the
   // mbarriers after it stay aligned)
   static constexpr int PREFIX = (4 * (3 * MX_MAX_EXPERTS + 1) + 15) / 16 * 16;
-  static constexpr int BUDGET = 210 * 1024 - STAGING - PREFIX;
+  static constexpr int BUDGET = (W ? 222 : 210) * 1024 - STAGING - PREFIX;
   static constexpr int STAGES = BUDGET / (STAGE + SF) > 12 ? 12 : BUDGET / (STAGE + SF);
   static constexpr int SMEM = 1024 + STAGES * STAGE + STAGES * SF + STAGING + PREFIX + 1024;
   // TMEM: two accumulators of ACC columns (2 BN: the hi and lo products side by side when BN <= 64),
@@ -65,7 +68,8 @@ struct MxCfg {
   static constexpr int ACC = BN <= 64 ? 2 * BN : BN;
   static constexpr int SF_COL = 2 * ACC;
   static constexpr int TMEM_COLS = 512;
-  static_assert(SF_COL + 12 * STAGES <= TMEM_COLS, "tensor memory overflow");
+  static_assert(SF_COL + SF_COLS * STAGES <= TMEM_COLS, "tensor memory overflow");
+  static_assert(SMEM <= 232448, "shared memory per block");
   static_assert((STAGES * (STAGE + SF) + STAGING + PREFIX) % 16 == 0, "mbarriers must stay aligned");
 };
 
@@ -182,11 +186,11 @@ __device__ __forceinline__ int mx_cols(int rest) {
   return n < BN ? n : BN;
 }
 
-template <int BN>
+template <int BN, bool W>
 __global__ void __launch_bounds__(MX_THREADS, 1)
     moe_mx_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmH,
                   const __grid_constant__ CUtensorMap tmL, MxArgs a) {
-  using C = MxCfg<BN>;
+  using C = MxCfg<BN, W>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -255,7 +259,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
-    if (a.wide && elect_one()) {
+    if (W && elect_one()) {
       // stage ring in 32-bit shared addresses; stage index and barrier parity advanced, not divided
       const uint32_t st0 = smem_u32(stages), sf0 = smem_u32(sfs), full0 = smem_u32(full), empty0 = smem_u32(empty);
       int it = 0, s = 0;
@@ -303,7 +307,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         atomicAdd(&g_mx_probe[5], (unsigned long long)pi);
         atomicAdd(&g_mx_probe[7], (unsigned long long)it);
       }
-    } else if (!a.wide && elect_one()) {
+    } else if (!W && elect_one()) {
       int it = 0;
       long long pw = 0, pi = 0, w1 = 0;
       const long long p0 = clock64();
@@ -329,7 +333,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
           uint8_t* st = stages + s * C::STAGE;
           uint8_t* sf = sfs + s * C::SF;
           // the fp4 tile counts its global (packed) bytes: half of its shared-memory footprint
-          if (a.wide) {  // one box per operand: the 8 KB weight block, BN token rows of hi and lo
+          if (W) {  // one box per operand: the 8 KB weight block, BN token rows of hi and lo
             mbar_expect_tx(&full[s], C::A / 2 + 2 * BN * MX_SK + 2 * MX_CHUNK);
             const int trow = (int)((((long)e * n_tiles + nt) * kstages + ks) * 128);
             tma_load_2d(st, &tmW, &full[s], 0, trow);
@@ -339,7 +343,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
           } else {
             mbar_expect_tx(&full[s], C::A / 2 + 2 * ne * MX_SK + 3 * MX_CHUNK);
           }
-          if (a.wide) {
+          if (W) {
           } else if (a.tiled) {  // one contiguous 8 KB block: rows (tile, stage, 0..127) of 64 bytes
             const int trow = (int)((((long)e * n_tiles + nt) * kstages + ks) * 128);
             tma_load_2d(st, &tmW, &full[s], 0, trow);
@@ -348,11 +352,11 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
             tma_load_2d(st, &tmW, &full[s], ks * MX_SK, (int)(erow + wrow(nt, 0)));
             tma_load_2d(st + 64 * MX_SK, &tmW, &full[s], ks * MX_SK, (int)(erow + wrow(nt, 64)));
           }
-          for (int t = 0; !a.wide && t < ne; t += 16) {
+          for (int t = 0; !W && t < ne; t += 16) {
             tma_load_2d(st + C::A + t * MX_SK, &tmH, &full[s], ks * MX_SK, row_b + t);
             tma_load_2d(st + C::A + C::B + t * MX_SK, &tmL, &full[s], ks * MX_SK, row_b + t);
           }
-          if (!a.wide) {
+          if (!W) {
             bulk_g2s(sf, sfa_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
             bulk_g2s(sf + MX_CHUNK, sfh_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
             bulk_g2s(sf + 2 * MX_CHUNK, sfl_u + ks * MX_CHUNK, MX_CHUNK, &full[s]);
@@ -371,7 +375,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
-    if (a.wide && elect_one()) {
+    if (W && elect_one()) {
       const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty), accf0 = smem_u32(acc_full),
                      acce0 = smem_u32(acc_empty);
       const uint64_t da0 = desc_sw128(smem_u32(stages)), db0 = desc_sw128(smem_u32(stages) + C::A);
@@ -400,7 +404,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
             mw += m1 - w0;
           }
           tc_fence_after();
-          const uint32_t sf_t = tmem + C::SF_COL + s * 12, sf_s = sf_s0 + s * C::SF;
+          const uint32_t sf_t = tmem + C::SF_COL + s * C::SF_COLS, sf_s = sf_s0 + s * C::SF;
           const uint64_t so = (uint64_t)((s * C::STAGE) >> 4);  // descriptor address field: bytes / 16
           const uint64_t da = da0 + so, dh = db0 + so;
           tmem_cp_chunk(sf_t, sf_s);
@@ -429,7 +433,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
       }
       mma_commit(drain);
       mbar_wait(drain, 0, a.err, ERR_DRAIN, nullptr);
-    } else if (!a.wide && elect_one()) {
+    } else if (!W && elect_one()) {
       int it = 0, ti = 0;
       bool ok = true;
       long long mw = 0, aw = 0, mi = 0, m1 = 0;
@@ -439,7 +443,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         // wide: hi and lo token rows form one N = 2 BN operand (all BN rows of each: the lo rows start
         // at BN); else one MMA per term with N = the tile's valid rows
         uint32_t idesc = idesc_mxf8f6f4(2 * BN);
-        if (!a.wide) {
+        if (!W) {
           int nt, tt;
           unit(u, e, nt, tt);
           idesc = idesc_mxf8f6f4(mx_cols<BN>(cnts[e] - (tt - tstart[e]) * BN));
@@ -462,11 +466,11 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
             mw += m1 - w0;
           }
           tc_fence_after();
-          const uint32_t sf_t = tmem + C::SF_COL + s * 12;
+          const uint32_t sf_t = tmem + C::SF_COL + s * C::SF_COLS;
           const uint32_t sf_s = smem_u32(sfs + s * C::SF);
           const uint32_t sbase = smem_u32(stages + s * C::STAGE);
           const uint64_t da = desc_sw128(sbase), dh = desc_sw128(sbase + C::A), dl = desc_sw128(sbase + C::A + C::B);
-          if (a.wide) {
+          if (W) {
             tmem_cp_chunk(sf_t, sf_s);
             tmem_cp_chunk(sf_t + 4, sf_s + MX_CHUNK);
 #pragma unroll
@@ -523,7 +527,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         float v[16];
         const uint32_t ta = tmem + acc * C::ACC + c0 + ((uint32_t)(ew * 32) << 16);
         tmem_ld16(ta, v);
-        if (a.wide) {  // hi products in columns [0, BN), lo products in [BN, 2 BN)
+        if (W) {  // hi products in columns [0, BN), lo products in [BN, 2 BN)
           float vl[16];
           tmem_ld16(ta + BN, vl);
 #pragma unroll
@@ -720,11 +724,11 @@ static int mx_sms() {
   return n;
 }
 
-template <int BN>
+template <int BN, bool W>
 static int mx_launch(const CUtensorMap& tw, const CUtensorMap& th, const CUtensorMap& tl, const MxArgs& a,
                      cudaStream_t st) {
-  using C = MxCfg<BN>;
-  auto k = moe_mx_kernel<BN>;
+  using C = MxCfg<BN, W>;
+  auto k = moe_mx_kernel<BN, W>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -791,10 +795,10 @@ int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, cons
   MxArgs a{sfa, sf_hi, sf_lo, offsets, counts, tstart, out, out_cols, n_rows, K, count, act, err, tiled ? 1 : 0,
            wide ? 1 : 0, probe};
   switch (BN) {
-    case 16: return mx_launch<16>(tw, th, tl, a, s);
-    case 32: return mx_launch<32>(tw, th, tl, a, s);
-    case 64: return mx_launch<64>(tw, th, tl, a, s);
-    default: return mx_launch<128>(tw, th, tl, a, s);
+    case 16: return wide ? mx_launch<16, true>(tw, th, tl, a, s) : mx_launch<16, false>(tw, th, tl, a, s);
+    case 32: return wide ? mx_launch<32, true>(tw, th, tl, a, s) : mx_launch<32, false>(tw, th, tl, a, s);
+    case 64: return wide ? mx_launch<64, true>(tw, th, tl, a, s) : mx_launch<64, false>(tw, th, tl, a, s);
+    default: return mx_launch<128, false>(tw, th, tl, a, s);
   }
 }
 
