@@ -104,6 +104,57 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t phase, int* er
   }
 }
 
+// Shared-memory-address (u32) forms of the per-stage operations, for the single-thread producer
+// and MMA loops: they keep a stage ring in 32-bit shared addresses advanced by constants.
+__device__ __forceinline__ bool mbar_try_wait_s(uint32_t bar, uint32_t phase, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(phase), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait (as mbar_wait): false after QB_WAIT_NS or when another role aborted
+__device__ __forceinline__ bool mbar_wait_s(uint32_t bar, uint32_t phase, int* err, int code,
+                                            volatile int* abort_flag) {
+  if (mbar_try_wait_s(bar, phase, 0)) return true;
+  const uint64_t t0 = globaltimer();
+  while (true) {
+    if (mbar_try_wait_s(bar, phase, 200000)) return true;
+    if (*abort_flag) return false;
+    if (globaltimer() - t0 > QB_WAIT_NS) {
+      if (err) atomicCAS(err, 0, code);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+}
+__device__ __forceinline__ void mbar_expect_tx_s(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_s(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_3d_s(uint32_t dst, const CUtensorMap* map, uint32_t bar, int c0, int c1,
+                                              int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4, %5}], [%2];"
+      ::"r"(dst), "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_g2s_s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ void mma_commit_s(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int c0, int c1) {
   asm volatile(

@@ -37,9 +37,11 @@ struct GemmCfg {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE = A_BYTES + B_BYTES;
   static constexpr int STAGING = 32 * 128 * 2;  // 32 token columns x 128 weight rows, 16-bit
+  // at most 8 stages in 200 KB (more stages measured no faster on the decode shapes)
   static constexpr int STAGES = (200 * 1024 - STAGING) / STAGE > 8 ? 8 : (200 * 1024 - STAGING) / STAGE;
   static constexpr int TMEM_COLS = (2 * BN) < 32 ? 32 : 2 * BN;
   static constexpr int SMEM = 1024 + STAGES * STAGE + STAGING + 256;
+  static_assert(SMEM <= 232448, "shared memory per block");
 };
 
 struct GemmArgs {
@@ -147,17 +149,29 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int it = 0;
       SegIter sg(blockIdx.x, a.ctas, gridDim.x, tiles, kblocks);
       int tile, k0, k1;
+      // stage ring in 32-bit shared addresses; stage index and parity advanced, not divided
+      const uint32_t st0 = smem_u32(stages), full0 = smem_u32(full), empty0 = smem_u32(empty);
+      int s = 0;
+      uint32_t ph = 1;  // a first-round stage waits on the parity that passes at once
       while (!*abort_flag && sg.next(tile, k0, k1)) {
         const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
-        for (int kb = k0; kb < k1; ++kb, ++it) {
-          const int s = it % C::STAGES;
-          if (!mbar_wait(&empty[s], ((it / C::STAGES) & 1) ^ 1, a.err, ERR_TMA_WAIT, abort_flag)) break;
-          uint8_t* st = stages + s * C::STAGE;
-          mbar_expect_tx(&full[s], C::STAGE);
-          tma_load_2d(st, &tmW, &full[s], kb * BK, n0);
-          tma_load_2d(st + C::A_BYTES, &tmX, &full[s], kb * BK, t0);
+        bool ok = true;
+        for (int kx = k0 * BK; kx < k1 * BK; kx += BK, ++it) {
+          if (!mbar_wait_s(empty0 + 8 * s, ph, a.err, ERR_TMA_WAIT, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t st = st0 + s * C::STAGE, fb = full0 + 8 * s;
+          mbar_expect_tx_s(fb, C::STAGE);
+          tma_load_2d_s(st, &tmW, fb, kx, n0);
+          tma_load_2d_s(st + C::A_BYTES, &tmX, fb, kx, t0);
           *issued_p = it + 1;
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
         }
+        if (!ok) break;
       }
     }
   } else if (warp == 1) {
@@ -166,31 +180,39 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int it = 0, ti = 0;
       SegIter sg(blockIdx.x, a.ctas, gridDim.x, tiles, kblocks);
       int tile, k0, k1;
+      const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty), accf0 = smem_u32(acc_full),
+                     acce0 = smem_u32(acc_empty);
+      const uint64_t da0 = desc_sw128(smem_u32(stages)), db0 = desc_sw128(smem_u32(stages) + C::A_BYTES);
+      int s = 0;
+      uint32_t ph = 0;
       for (; !*abort_flag && sg.next(tile, k0, k1); ++ti) {
         const int acc = ti & 1;
-        if (!mbar_wait(&acc_empty[acc], ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
+        if (!mbar_wait_s(acce0 + 8 * acc, ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
         tc_fence_after();
         const uint32_t d = tmem + acc * BN;
         bool ok = true;
         for (int kb = k0; kb < k1; ++kb, ++it) {
-          const int s = it % C::STAGES;
-          if (!mbar_wait(&full[s], (it / C::STAGES) & 1, a.err, ERR_MMA_WAIT, abort_flag)) {
+          if (!mbar_wait_s(full0 + 8 * s, ph, a.err, ERR_MMA_WAIT, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t sa = smem_u32(stages + s * C::STAGE);
-          const uint64_t da = desc_sw128(sa), db = desc_sw128(sa + C::A_BYTES);
+          const uint64_t so = (uint64_t)((s * C::STAGE) >> 4);  // descriptor address field: bytes / 16
+          const uint64_t da = da0 + so, db = db0 + so;
 #pragma unroll
           for (int kk = 0; kk < BK / 16; ++kk) {
             // +32 bytes per 16-element K step inside the swizzle atom (>>4 in the descriptor)
             mma_f16_ss(d, da + 2 * kk, db + 2 * kk, idesc, (kb != k0) || kk != 0);
           }
-          mma_commit(&empty[s]);
+          mma_commit_s(empty0 + 8 * s);
           *consumed_p = it + 1;
+          if (++s == C::STAGES) {
+            s = 0;
+            ph ^= 1;
+          }
         }
         if (!ok) break;
-        mma_commit(&acc_full[acc]);
+        mma_commit_s(accf0 + 8 * acc);
       }
       // make sure no MMA is still writing TMEM when the CTA tears down
       mma_commit(drain);
