@@ -222,7 +222,15 @@ def load_weights(model_dir: str, cfg: Qwen35Config, p: Plan, device, dtype, with
 
 # ============================================================================ random init
 def _randn(shape, gen, device, dtype, std=0.02):
-    return (torch.randn(shape, generator=gen, device=device, dtype=torch.float32) * std).to(dtype)
+    """N(0, std) in ``dtype``, drawn in fp32 pieces of at most 2^28 elements (a 1 GB temporary) so
+    that multi-GB weights do not need twice their size while they are made."""
+    out = torch.empty(shape, device=device, dtype=dtype)
+    flat = out.view(-1)
+    step = 1 << 28
+    for i in range(0, flat.numel(), step):
+        n = min(step, flat.numel() - i)
+        flat[i:i + n] = torch.randn(n, generator=gen, device=device, dtype=torch.float32) * std
+    return out
 
 
 def random_layer(kind: str, cfg: Qwen35Config, p: Plan, gen, device, dtype, experts_from: dict | None,

@@ -29,6 +29,7 @@ def main():
     ap.add_argument("--k", type=int, default=3)
     ap.add_argument("--accept", type=float, default=0.7)
     ap.add_argument("--rounds", type=int, default=20)
+    ap.add_argument("--graphs", type=int, default=1, help="replay captured rounds (CUDA; 0: eager)")
     args = ap.parse_args()
     from ..models import mtp as mtpmod
     from ..parallel import comm as commmod
@@ -41,14 +42,20 @@ def main():
     if cuda:
         torch.cuda.set_device(dev)
     lanes = max(args.batches)
-    spec = PoolSpec(lanes=lanes, max_seq=args.ctx + 64 * (args.k + 1) + 64,
-                    kv_tokens=lanes * (args.ctx + 64 * (args.k + 1) + 64), snapshots=2)
+    spec = PoolSpec(lanes=lanes + 1, max_seq=args.ctx + 64 * (args.k + 1) + 64,  # + the graphs' pad lane
+                    kv_tokens=(lanes + 1) * (args.ctx + 64 * (args.k + 1) + 64), snapshots=2)
     dtype = torch.bfloat16 if cuda else torch.float32
     model, _ = build_model(args.model, rank, world, dev, spec, dtype=dtype, with_mtp=True, graphs=False)
     command_group(world)
     pool_handshake(model)
     head = mtpmod.attach(model, k=args.k, forced_accept=args.accept)
     head.rng.seed(1234)  # identical acceptance draws on every rank
+    runner = model
+    if cuda and args.graphs:
+        from .graphs import GraphRunner
+
+        runner = GraphRunner(model, buckets=args.batches)
+        runner.prepare_speculative()
     rng = random.Random(0)
     per = (spec.max_seq + model.block_size - 1) // model.block_size
     results = []
@@ -63,7 +70,7 @@ def main():
         tok, pos = [5] * B, [args.ctx] * B
         acc0 = head.accepted
         for _ in range(2):  # warm-up rounds
-            got = model.speculative_decode(ls, tok, pos, [1 << 20] * B, [[] for _ in ls])
+            got = runner.speculative_decode(ls, tok, pos, [1 << 20] * B, [[] for _ in ls])
             pos = [p + len(g) for p, g in zip(pos, got)]
             tok = [g[-1] for g in got]
         if cuda:
@@ -80,7 +87,7 @@ def main():
             s.record()
         committed = 0
         for _ in range(args.rounds):
-            got = model.speculative_decode(ls, tok, pos, [1 << 20] * B, [[] for _ in ls])
+            got = runner.speculative_decode(ls, tok, pos, [1 << 20] * B, [[] for _ in ls])
             committed += sum(len(g) for g in got)
             pos = [p + len(g) for p, g in zip(pos, got)]
             tok = [g[-1] for g in got]
@@ -102,7 +109,10 @@ def main():
                         "draft_accept_rate": round((head.accepted - acc0) / (B * args.rounds * args.k), 3)})
     if rank == 0:
         for r in results:
-            print(json.dumps({"bench": "mtp_forced", "n_gpus": world, "k": args.k, "ctx": args.ctx, **r}))
+            print(json.dumps({"bench": "mtp_forced", "n_gpus": world, "k": args.k, "ctx": args.ctx,
+                              "graphs": bool(cuda and args.graphs), **r}))
+    if hasattr(runner, "release"):
+        runner.release()  # graphs hold NCCL work: drop them before the process group
     if world > 1:
         dist.destroy_process_group()
 

@@ -63,6 +63,9 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
     if model == "full" and device.type == "cuda":
         total = torch.cuda.get_device_properties(device).total_memory
         dense = 20e9 / world + 4e9
+        if with_mtp:  # the MTP layer: bf16 (or MXFP4) experts of this rank plus its dense part
+            per = 3 * cfg.hidden * cfg.moe_inter
+            dense += p.experts.count * (2 * per if cfg.mtp_experts_bf16 else per // 2 + per // 32) + 1e9
         budget = total - dense - kv - state - reserve_bytes
         n = max(1, min(cfg.layers, int(budget // expert_bytes_per_layer(cfg, p))))
         distinct = None if n >= cfg.layers else n

@@ -19,6 +19,7 @@ from __future__ import annotations
 import torch
 
 from ..models.qwen35 import StepInputs
+from ..ops import core as ops
 from ..utils import flags
 
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
@@ -47,6 +48,50 @@ class _Bucket:
                           list(range(B)), list(range(B + 1)), [0] * B, model.max_seq)
 
 
+class _SpecBucket:
+    """Static buffers of one captured speculative round for ``B`` lanes and draft depth ``k``:
+    the draft steps' positions and KV rows, the verify forward's ``B x (k+1)`` rows, and the
+    round's outputs (drafts, the verify argmax, the DeltaNet inputs it keeps for the commit)."""
+
+    def __init__(self, model, B: int, k: int):
+        dev = model.device
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.B, self.k = B, k
+        R = B * (k + 1)
+        self.n_host = B + 2 * k * B + 2 * R + B  # lanes | draft pos, rows | verify pos, rows | starts
+        self.packed_host = torch.zeros(self.n_host, dtype=torch.int32).pin_memory()
+        self.packed_dev = torch.zeros(self.n_host, **i32)
+        self.tok_host = torch.zeros(B, dtype=torch.int64).pin_memory()
+        self.tok0 = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.lanes = torch.zeros(B, **i32)
+        self.pos_d = [torch.zeros(B, **i32) for _ in range(k)]
+        self.rows_d = [torch.zeros(B, **i32) for _ in range(k)]
+        self.pos_v = torch.zeros(R, **i32)
+        self.rows_v = torch.zeros(R, **i32)
+        self.start_v = torch.zeros(B, **i32)
+        self.cu_d = torch.arange(B + 1, **i32)
+        self.cu_v = torch.arange(0, R + 1, k + 1, **i32)
+        self.logit_rows_d = torch.arange(B, dtype=torch.int64, device=dev)
+        self.logit_rows_v = torch.arange(R, dtype=torch.int64, device=dev)
+        self.graph = None
+        self.drafts = self.am = self.vb = self.vsave = self.h_all = None
+
+    def unpack(self) -> None:
+        B, k = self.B, self.k
+        R = B * (k + 1)
+        pd = self.packed_dev
+        self.lanes.copy_(pd[:B])
+        o = B
+        for i in range(k):
+            self.pos_d[i].copy_(pd[o:o + B])
+            self.rows_d[i].copy_(pd[o + k * B:o + k * B + B])
+            o += B
+        o = B + 2 * k * B
+        self.pos_v.copy_(pd[o:o + R])
+        self.rows_v.copy_(pd[o + R:o + 2 * R])
+        self.start_v.copy_(pd[o + 2 * R:o + 2 * R + B])
+
+
 class GraphRunner:
     """Runner that replays captured decode graphs; see the module docstring."""
 
@@ -62,6 +107,7 @@ class GraphRunner:
             self.buckets.append(lim)
         self.pool = torch.cuda.graph_pool_handle()
         self._b = {}
+        self._spec: dict[int, _SpecBucket] = {}
         self.enabled = flags.get("QB_GRAPHS")
         self.replays = 0
         self.launch_per_replay: dict[int, int] = {}
@@ -121,6 +167,116 @@ class GraphRunner:
             self._b[B] = bk
         torch.cuda.synchronize()
 
+    # ------------------------------------------------------------------ speculative rounds
+    def _spec_fill(self, bk: _SpecBucket, lanes, tokens, positions) -> None:
+        m = self.model
+        m._gpu_mark("in")
+        B, k, n = bk.B, bk.k, len(lanes)
+        ln = list(lanes) + [self.pad_lane] * (B - n)
+        pos = list(positions) + [0] * (B - n)
+        real = [True] * n + [False] * (B - n)
+        vals = list(ln)
+        for i in range(k):  # draft step i writes the MTP KV row of position p + i
+            vals.extend(p + i for p in pos)
+        for i in range(k):
+            vals.extend(m._row(l, p + i) if r else 0 for l, p, r in zip(ln, pos, real))
+        vals.extend(p + j for p in pos for j in range(k + 1))
+        vals.extend(m._row(l, p + j) if r else 0 for l, p, r in zip(ln, pos, real) for j in range(k + 1))
+        vals.extend(pos)
+        bk.packed_host.copy_(torch.tensor(vals, dtype=torch.int32))
+        bk.tok_host[:n] = torch.tensor([int(t) for t in tokens], dtype=torch.int64)
+        bk.tok_host[n:] = 0
+        bk.packed_dev.copy_(bk.packed_host, non_blocking=True)
+        bk.tok0.copy_(bk.tok_host, non_blocking=True)
+        bk.unpack()
+        m._h2d += bk.n_host * 4 + B * 8
+        m._sync_tables()
+
+    def _spec_run(self, bk: _SpecBucket) -> None:
+        """Draft ``k`` tokens per lane with the MTP layer, then the wide verify forward and its
+        argmax, all on the bucket's static buffers (the body of the captured graph)."""
+        m, mtp = self.model, self.model.mtp
+        B, k = bk.B, bk.k
+        hidden = mtp.seed_h.index_select(0, bk.lanes.long())
+        tok = bk.tok0
+        outs = []
+        for i in range(k):
+            b = StepInputs(tok, bk.pos_d[i], bk.rows_d[i], bk.lanes, bk.cu_d, bk.pos_d[i], bk.logit_rows_d,
+                           list(range(B)), list(range(B + 1)), [0] * B, m.max_seq)
+            h = mtp.layer(mtp.combine(tok, hidden), b)
+            tok = ops.argmax_rows(m.logits(h))[1]
+            outs.append(tok)
+            hidden = h
+        bk.drafts = torch.stack(outs, dim=1)
+        vb = StepInputs(torch.cat([bk.tok0[:, None], bk.drafts], dim=1).reshape(-1), bk.pos_v, bk.rows_v, bk.lanes,
+                        bk.cu_v, bk.start_v, bk.logit_rows_v, list(range(B)), list(range(0, B * (k + 1) + 1, k + 1)),
+                        [0] * B, m.max_seq)
+        vb.verify = True
+        m._vsave = {}
+        h = m._forward(vb)
+        bk.am = ops.argmax_rows(m.logits(h))[1].view(B, k + 1)
+        bk.vb, bk.vsave, bk.h_all = vb, m._vsave, m.last_h_all
+        m._vsave = {}
+
+    def prepare_speculative(self, buckets=None) -> None:
+        """Capture one speculative-round graph per bucket (draft + verify; accept and the
+        DeltaNet commit stay eager). Every rank must call this in the same order."""
+        m = self.model
+        if not self.enabled or m.device.type != "cuda" or m.mtp is None:
+            return
+        m.begin(self.pad_lane)
+        m.attach_blocks(self.pad_lane, [])
+        k = m.mtp.k
+        lim = self.max_batch
+        for B in sorted((b for b in (buckets or self.buckets) if b <= lim), reverse=True):
+            bk = _SpecBucket(m, B, k)
+            self._spec_fill(bk, [], [], [])
+            st = torch.cuda.Stream()
+            st.wait_stream(torch.cuda.current_stream())
+            with torch.inference_mode(), torch.cuda.stream(st):
+                for _ in range(2):
+                    self._spec_run(bk)
+            torch.cuda.current_stream().wait_stream(st)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.inference_mode(), torch.cuda.graph(g, pool=self.pool):
+                self._spec_run(bk)
+            bk.graph = g
+            self._spec[B] = bk
+        torch.cuda.synchronize()
+
+    def speculative_decode(self, lanes, tokens, positions, budgets, stops):
+        """One MTP round per lane replayed from the smallest captured bucket that holds the batch
+        (eager when none does); same results as ``Model.speculative_decode``."""
+        m = self.model
+        n = len(lanes)
+        B = next((b for b in sorted(self._spec) if b >= n), None)
+        if B is None:
+            return m.speculative_decode(lanes, tokens, positions, budgets, stops)
+        bk, mtp, k = self._spec[B], m.mtp, m.mtp.k
+        with torch.inference_mode():
+            self._spec_fill(bk, lanes, tokens, positions)
+            bk.graph.replay()
+            m._gpu_mark("out")
+            am_h, dr_h = bk.am[:n].tolist(), bk.drafts[:n].tolist()  # the round's one host sync
+            m._d2h += 8 * n * (2 * k + 1)
+            ns = [mtp.accept(dr_h[i], am_h[i]) for i in range(n)]
+            mtp.rounds += n
+            mtp.accepted += sum(ns)
+            mtp.drafted += n * k
+            m._vsave, m.last_h_all = bk.vsave, bk.h_all
+            m._commit_verify(bk.vb, lanes, positions, ns, k)
+        self.replays += 1
+        out = []
+        for i in range(n):
+            toks = dr_h[i][:ns[i]] + [am_h[i][ns[i]]]
+            st = set(stops[i])
+            cut = next((j for j, t in enumerate(toks) if t in st), None)
+            if cut is not None:
+                toks = toks[:cut + 1]
+            out.append(toks[:max(1, budgets[i])])
+        return out
+
     def attribution(self, B: int, replays: int = 10, detail: bool = False) -> dict[str, float]:
         """Device time per layer part (ms) of one captured ``B``-row decode step.
 
@@ -163,6 +319,9 @@ class GraphRunner:
             bk.graph = None
             bk.out = None
         self._b.clear()
+        for sb in self._spec.values():
+            sb.graph = None
+        self._spec.clear()
 
     # ------------------------------------------------------------------ runner
     def decode(self, lanes, tokens, positions):

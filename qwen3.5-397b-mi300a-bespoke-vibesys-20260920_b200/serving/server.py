@@ -52,6 +52,11 @@ def parse(argv=None):
     ap.add_argument("--device", default="auto", choices=["auto", "cuda", "cpu"])
     ap.add_argument("--dtype", default="auto", choices=["auto", "bf16", "fp32"])
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--mtp-k", type=int, default=0,
+                    help="MTP speculative decoding with this draft depth (0: off; the checkpoint needs mtp.*)")
+    ap.add_argument("--mtp-forced-accept", type=float, default=None,
+                    help="accept each draft position with this probability instead of greedy (benchmarking)")
+    ap.add_argument("--mixed", action="store_true", help="decode steps also carry prefill chunks")
     return ap.parse_args(argv)
 
 
@@ -85,8 +90,19 @@ def _build(args, device):
 
     spec = PoolSpec(lanes=args.max_batch, max_seq=args.max_seq_len, kv_tokens=args.kv_tokens,
                     snapshots=args.snapshots)
+    mtp_k = getattr(args, "mtp_k", 0)
     model, _ = build_model(args.model_path, args.rank, args.tp, device, spec, dtype=_dtype(args, device),
-                           seed=args.seed)
+                           seed=args.seed, with_mtp=mtp_k > 0)
+    if mtp_k > 0:
+        from ..models import mtp as mtpmod
+
+        inner = getattr(model, "model", model)  # the Model under a GraphRunner
+        head = mtpmod.attach(inner, k=mtp_k, forced_accept=getattr(args, "mtp_forced_accept", None))
+        if head is None:
+            raise SystemExit("--mtp-k needs a checkpoint with an mtp block")
+        head.rng.seed(args.seed)  # identical forced-acceptance draws on every rank
+        if hasattr(model, "prepare_speculative"):
+            model.prepare_speculative()
     group = command_group(args.tp)
     pool_handshake(model)
     return model, group
@@ -131,7 +147,8 @@ class Engine:
             cache = SessionCache(BlockAllocator(model.num_blocks, model.block_size), model.block_size,
                                  model.num_snapshots)
             self.sched = Scheduler(self.runner, cache, prefill_chunk=self.args.prefill_chunk,
-                                   token_budget=self.args.token_budget)
+                                   token_budget=self.args.token_budget, mixed=getattr(self.args, "mixed", False),
+                                   speculative=getattr(self.args, "mtp_k", 0) > 0)
             path = self.args.model_path if os.path.isdir(str(self.args.model_path)) else None
             self.tok = load_tokenizer(path, model.cfg.vocab, model.cfg.eos_token_id)
             self.ready = True

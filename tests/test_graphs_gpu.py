@@ -94,3 +94,39 @@ def test_graph_attribution_tiny():
     assert att["total"] > 0
     parts = sum(v for k, v in att.items() if k != "total")
     assert abs(parts - att["total"]) < 1e-6 + 1e-6 * att["total"]
+
+
+def test_speculative_round_graph_matches_eager():
+    """Captured speculative rounds (draft + wide verify in one graph, eager accept and commit)
+    emit the same tokens as the eager rounds on identical lane states."""
+    from qwen35_b200.models import mtp as mtpmod
+    from qwen35_b200.models.config import tiny_config
+    from qwen35_b200.models.qwen35 import Model
+    from qwen35_b200.models.weights import random_weights
+    from qwen35_b200.parallel.plan import plan
+    from qwen35_b200.serving.graphs import GraphRunner
+
+    dev = torch.device("cuda")
+    cfg = tiny_config()
+    p = plan(cfg, 0, 1)
+    m = Model(cfg, random_weights(cfg, p, dev, torch.bfloat16, seed=5, with_mtp=True), p, device=dev,
+              max_batch=5, max_seq=512)
+    head = mtpmod.attach(m, k=2)
+    g = GraphRunner(m, buckets=(1, 2, 4))
+    g.prepare_speculative()
+    assert set(g._spec) == {1, 2, 4}
+    prompts = [list(range(7, 60)), list(range(100, 141))]
+    for i, ids in enumerate(prompts * 2):  # lanes 0,1 (graph) and 2,3 (eager) hold the same history
+        m.begin(i)
+        m.attach_blocks(i, list(range(1 + 12 * i, 13 + 12 * i)))
+        m.prefill(i, ids, 0)
+    toks, pos = [9, 11], [len(prompts[0]), len(prompts[1])]
+    for _ in range(4):
+        a = g.speculative_decode([0, 1], toks, pos, [64, 64], [[], []])
+        b = m.speculative_decode([2, 3], toks, pos, [64, 64], [[], []])
+        torch.cuda.synchronize()
+        assert a == b, (a, b)
+        pos = [x + len(t) for x, t in zip(pos, a)]
+        toks = [t[-1] for t in a]
+    assert g.replays == 4 and head.rounds == 16
+    g.release()

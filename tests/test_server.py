@@ -23,12 +23,12 @@ def free_port():
     return p
 
 
-def start(tp=1, env_extra=None, model="tiny"):
+def start(tp=1, env_extra=None, model="tiny", extra_args=()):
     port = free_port()
     env = dict(os.environ, PYTHONPATH=ROOT, OMP_NUM_THREADS="2", **(env_extra or {}))
     cmd = [sys.executable, "-m", "qwen35_b200.serving.server", "--model-path", model, "--port", str(port),
            "--tp", str(tp), "--device", "cpu", "--max-batch", "4", "--max-seq-len", "2048", "--kv-tokens", "16384",
-           "--master-port", str(free_port())]
+           "--master-port", str(free_port()), *extra_args]
     proc = subprocess.Popen(cmd, cwd=ROOT, env=env, stdout=subprocess.DEVNULL, stderr=subprocess.DEVNULL,
                             start_new_session=True)
     url = f"http://127.0.0.1:{port}"
@@ -136,3 +136,17 @@ def test_fault_endpoint_changes_output_and_tp2_matches_tp1(tiny_dir):
         assert tp2["choices"][0]["token_ids"] == base["choices"][0]["token_ids"]
     finally:
         stop(p2)
+
+
+def test_mtp_speculative_server_matches_plain(server):
+    """``--mtp-k 2``: decode steps are speculative rounds (draft, wide verify, accept, commit);
+    greedy acceptance keeps the emitted tokens identical to plain decoding."""
+    ids = [random.Random(7).randrange(3000) for _ in range(40)]
+    body = {"prompt": ids, "max_tokens": 16, "ignore_eos": True}
+    plain = requests.post(server + "/v1/completions", json=body).json()["choices"][0]["token_ids"]
+    proc, url = start(extra_args=("--mtp-k", "2"))
+    try:
+        spec = requests.post(url + "/v1/completions", json=body).json()["choices"][0]["token_ids"]
+    finally:
+        stop(proc)
+    assert len(spec) == 16 and spec == plain
