@@ -30,7 +30,7 @@ __global__ void conv_out_kernel(const bf16* x, long ldx, const bf16* state, long
                                 const int* seg_lane, const int* cu, int S, int C, bf16* out) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int t = blockIdx.y;
-  if (c >= C) return;
+  if (c >= C || t >= cu[S]) return;  // rows past the last segment: padding of a fixed-size batch
   const int s = seg_of(cu, S, t);
   const int t0 = cu[s];
   const bf16* st = state + (long)seg_lane[s] * lane_stride + (long)c * (K - 1);

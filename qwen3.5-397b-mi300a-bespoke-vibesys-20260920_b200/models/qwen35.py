@@ -445,6 +445,45 @@ class Model:
             ab_in.tokens = b.tokens.index_select(0, it)
             self.mtp.catch_up(ab_in, self.last_h_all.index_select(0, it))
 
+    def _commit_verify_device(self, b: StepInputs, n: torch.Tensor, k: int) -> None:
+        """``_commit_verify`` with fixed shapes, for a captured graph: ``n`` [B] (device, int64)
+        accepted drafts per lane of the verify batch ``b`` (B segments of k+1 rows). The accepted
+        rows are compacted on the device into a full-size batch whose tail is padding (the kernels
+        bound their work by the device segment table); the MTP catch-up runs over all k+1 rows of
+        every lane (KV rows past the accepted prefix are rewritten before any read) and the seed
+        hidden of each lane becomes the one of its last accepted row."""
+        B = n.shape[0]
+        R = B * (k + 1)
+        dev = self.device
+        cu = torch.zeros(B + 1, dtype=torch.int64, device=dev)
+        cu[1:] = torch.cumsum(n + 1, 0)
+        r = torch.arange(R, device=dev)
+        lane_of = torch.searchsorted(cu[1:], r, right=True).clamp_(max=B - 1)
+        src = (lane_of * (k + 1) + (r - cu[lane_of])).clamp_(0, R - 1)
+        cu32 = cu.to(torch.int32)
+        cfg = self.cfg
+        for i, L in enumerate(self.w["layers"]):
+            if L["kind"] == FULL:
+                continue
+            j = self.lin_slot[i]
+            conv_in, ab = self._vsave[j]
+            qkv = ops.causal_conv_varlen(conv_in.index_select(0, src), self.conv_state[j], L["conv_w"], b.seg_lane,
+                                         cu32, b.seg_lane_h, b.cu_h, commit=True)
+            ops.gated_delta_varlen(qkv, ab.index_select(0, src), L["A_log"], L["dt_bias"], self.rec_state[j],
+                                   b.seg_lane, cu32, self.nk, self.nv, cfg.dn_k_dim, cfg.dn_v_dim, b.seg_lane_h,
+                                   b.cu_h, commit=True)
+        self._vsave = {}
+        mtp = self.mtp
+        if mtp is not None:
+            h_all = self.last_h_all
+            first = torch.arange(0, R, k + 1, device=dev)
+            prev = torch.empty_like(h_all)
+            prev[1:] = h_all[:-1]
+            lanes = b.seg_lane.long()
+            prev[first] = mtp.seed_h.index_select(0, lanes)
+            mtp.layer(mtp.combine(b.tokens, prev), b)
+            mtp.seed_h.index_copy_(0, lanes, h_all.index_select(0, first + n))
+
     def prefill(self, lane: int, ids: Sequence[int], start: int):
         return self.forward([(lane, ids, start)])[0:1]
 

@@ -58,9 +58,9 @@ class _SpecBucket:
         i32 = dict(dtype=torch.int32, device=dev)
         self.B, self.k = B, k
         R = B * (k + 1)
-        self.n_host = B + 2 * k * B + 2 * R + B  # lanes | draft pos, rows | verify pos, rows | starts
-        self.packed_host = torch.zeros(self.n_host, dtype=torch.int32).pin_memory()
-        self.packed_dev = torch.zeros(self.n_host, **i32)
+        self.n_packed = B + 2 * k * B + 2 * R + B  # lanes | draft pos, rows | verify pos, rows | starts
+        self.packed_host = torch.zeros(self.n_packed, dtype=torch.int32).pin_memory()
+        self.packed_dev = torch.zeros(self.n_packed, **i32)
         self.tok_host = torch.zeros(B, dtype=torch.int64).pin_memory()
         self.tok0 = torch.zeros(B, dtype=torch.int64, device=dev)
         self.lanes = torch.zeros(B, **i32)
@@ -73,7 +73,9 @@ class _SpecBucket:
         self.cu_v = torch.arange(0, R + 1, k + 1, **i32)
         self.logit_rows_d = torch.arange(B, dtype=torch.int64, device=dev)
         self.logit_rows_v = torch.arange(R, dtype=torch.int64, device=dev)
-        self.graph = None
+        self.n_host = torch.zeros(B, dtype=torch.int64).pin_memory()  # accepted drafts per lane
+        self.n_dev = torch.zeros(B, dtype=torch.int64, device=dev)
+        self.graph = self.commit_graph = None
         self.drafts = self.am = self.vb = self.vsave = self.h_all = None
 
     def unpack(self) -> None:
@@ -189,7 +191,7 @@ class GraphRunner:
         bk.packed_dev.copy_(bk.packed_host, non_blocking=True)
         bk.tok0.copy_(bk.tok_host, non_blocking=True)
         bk.unpack()
-        m._h2d += bk.n_host * 4 + B * 8
+        m._h2d += bk.n_packed * 4 + B * 8
         m._sync_tables()
 
     def _spec_run(self, bk: _SpecBucket) -> None:
@@ -218,9 +220,16 @@ class GraphRunner:
         bk.vb, bk.vsave, bk.h_all = vb, m._vsave, m.last_h_all
         m._vsave = {}
 
+    def _spec_commit(self, bk: _SpecBucket) -> None:
+        m = self.model
+        m._vsave = bk.vsave
+        m.last_h_all = bk.h_all
+        m._commit_verify_device(bk.vb, bk.n_dev, bk.k)
+
     def prepare_speculative(self, buckets=None) -> None:
-        """Capture one speculative-round graph per bucket (draft + verify; accept and the
-        DeltaNet commit stay eager). Every rank must call this in the same order."""
+        """Capture two graphs per bucket: the round (draft + wide verify + argmax) and its commit
+        (DeltaNet state over the accepted rows, MTP catch-up), between which the host reads the
+        argmax and decides the accepted lengths. Every rank must call this in the same order."""
         m = self.model
         if not self.enabled or m.device.type != "cuda" or m.mtp is None:
             return
@@ -233,15 +242,21 @@ class GraphRunner:
             self._spec_fill(bk, [], [], [])
             st = torch.cuda.Stream()
             st.wait_stream(torch.cuda.current_stream())
+            # warm-up and capture run on the pad lane only: the commit advances its state, which
+            # nothing reads
             with torch.inference_mode(), torch.cuda.stream(st):
                 for _ in range(2):
                     self._spec_run(bk)
+                    self._spec_commit(bk)
             torch.cuda.current_stream().wait_stream(st)
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             with torch.inference_mode(), torch.cuda.graph(g, pool=self.pool):
                 self._spec_run(bk)
-            bk.graph = g
+            gc = torch.cuda.CUDAGraph()
+            with torch.inference_mode(), torch.cuda.graph(gc, pool=self.pool):
+                self._spec_commit(bk)
+            bk.graph, bk.commit_graph = g, gc
             self._spec[B] = bk
         torch.cuda.synchronize()
 
@@ -264,8 +279,11 @@ class GraphRunner:
             mtp.rounds += n
             mtp.accepted += sum(ns)
             mtp.drafted += n * k
-            m._vsave, m.last_h_all = bk.vsave, bk.h_all
-            m._commit_verify(bk.vb, lanes, positions, ns, k)
+            bk.n_host[:n] = torch.tensor(ns, dtype=torch.int64)
+            bk.n_host[n:] = 0
+            bk.n_dev.copy_(bk.n_host, non_blocking=True)
+            m._h2d += 8 * B
+            bk.commit_graph.replay()
         self.replays += 1
         out = []
         for i in range(n):
@@ -320,7 +338,7 @@ class GraphRunner:
             bk.out = None
         self._b.clear()
         for sb in self._spec.values():
-            sb.graph = None
+            sb.graph = sb.commit_graph = None
         self._spec.clear()
 
     # ------------------------------------------------------------------ runner

@@ -120,13 +120,22 @@ def test_speculative_round_graph_matches_eager():
         m.begin(i)
         m.attach_blocks(i, list(range(1 + 12 * i, 13 + 12 * i)))
         m.prefill(i, ids, 0)
-    toks, pos = [9, 11], [len(prompts[0]), len(prompts[1])]
-    for _ in range(4):
-        a = g.speculative_decode([0, 1], toks, pos, [64, 64], [[], []])
-        b = m.speculative_decode([2, 3], toks, pos, [64, 64], [[], []])
-        torch.cuda.synchronize()
-        assert a == b, (a, b)
-        pos = [x + len(t) for x, t in zip(pos, a)]
-        toks = [t[-1] for t in a]
+    # each side runs its own rounds; the emitted streams must agree (acceptance lengths may differ
+    # where a draft flips on a near-tie, the emitted tokens are the target's greedy tokens)
+    streams = {}
+    for name, runner, lanes in (("graph", g, [0, 1]), ("eager", m, [2, 3])):
+        toks, pos = [9, 11], [len(prompts[0]), len(prompts[1])]
+        out = [[], []]
+        for _ in range(4):
+            got = runner.speculative_decode(lanes, toks, pos, [64, 64], [[], []])
+            for i in range(2):
+                out[i].extend(got[i])
+            pos = [x + len(t) for x, t in zip(pos, got)]
+            toks = [t[-1] for t in got]
+        streams[name] = out
+    torch.cuda.synchronize()
+    for i in range(2):
+        n = min(len(streams["graph"][i]), len(streams["eager"][i]))
+        assert n >= 4 and streams["graph"][i][:n] == streams["eager"][i][:n], (i, streams)
     assert g.replays == 4 and head.rounds == 16
     g.release()
