@@ -356,16 +356,15 @@ Tensor moe_routed_bf16(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor w2
 }
 
 // Block-scaled path: weights' e8m0 scales pre-arranged in 512-byte chunks (s13c / s2c).
-Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
-                     int64_t first, int64_t count, bool tiled) {
+void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
+                        int64_t first, int64_t count, bool tiled, Tensor out) {
   CHECK_BF16(h);
-  TORCH_CHECK(h.is_contiguous(), "moe: h contiguous");
+  TORCH_CHECK(h.is_contiguous() && out.is_contiguous(), "moe: h and out contiguous");
   const int T = h.size(0), H = h.size(1), k = topi.size(1);
   const int n13 = w13.size(1), I = n13 / 2;
   const int cap = T * k;
   auto i32 = h.options().dtype(at::kInt);
-  Tensor out = at::empty_like(h);
-  if (T == 0) return out;
+  if (T == 0) return;
   Tensor meta = at::empty({2 * count + 3 * cap + 1 + count + 1}, i32);
   int* counts = meta.data_ptr<int>();
   int* offsets = counts + count;
@@ -398,7 +397,52 @@ Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c
   LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w2.data_ptr<uint8_t>(), s2c.data_ptr<uint8_t>(), H, I, offsets,
                          counts, tstart, count, BN, 0, y2.data_ptr(), H, err_ptr(h), stream(), tiled));
   LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream()));
+}
+
+Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
+                     int64_t first, int64_t count, bool tiled) {
+  Tensor out = at::empty_like(h);
+  moe_routed_mx_into(h, topw, topi, w13, s13c, w2, s2c, first, count, tiled, out);
   return out;
+}
+
+// Expert-parallel MoE (ep.cu): dispatch this rank's token rows to the ranks owning their experts,
+// run this rank's experts on the rows it received (into its symmetric y area), combine the
+// weighted partial outputs of this rank's tokens from every rank.
+Tensor ep_moe(std::vector<int64_t> bases, int64_t rank, Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c,
+              Tensor w2, Tensor s2c, int64_t first, int64_t count, bool tiled, int64_t cap, int64_t experts_per_rank,
+              int64_t par, Tensor state, double timeout_s) {
+  CHECK_BF16(h);
+  TORCH_CHECK(h.is_contiguous() && topi.is_contiguous() && topw.is_contiguous(), "ep_moe: contiguous inputs");
+  TORCH_CHECK(topi.scalar_type() == at::kInt && topw.scalar_type() == at::kFloat, "ep_moe: int32 ids, fp32 weights");
+  const int world = bases.size(), T = h.size(0), H = h.size(1), k = topi.size(1);
+  TORCH_CHECK(T <= cap, "ep_moe: more tokens than the receive areas hold");
+  std::vector<void*> b(world);
+  for (int r = 0; r < world; ++r) b[r] = reinterpret_cast<void*>(bases[r]);
+  const unsigned long long tns = (unsigned long long)(timeout_s * 1e9);
+  Tensor slots = at::empty({T > 0 ? T : 1, world}, h.options().dtype(at::kInt));
+  Tensor counts = at::empty({world}, h.options().dtype(at::kInt));
+  LAUNCH(qb::ep_dispatch(b.data(), world, rank, cap, H, k, experts_per_rank, h.data_ptr(), H,
+                         topi.data_ptr<int>(), topw.data_ptr<float>(), T, slots.data_ptr<int>(),
+                         counts.data_ptr<int>(), state.data_ptr<int>(), tns, err_ptr(h), stream()));
+  long xo, io, wo, yo;
+  qb::ep_offsets(world, cap, H, k, (int)par, &xo, &io, &wo, &yo);
+  char* own = reinterpret_cast<char*>(b[rank]);
+  auto opt = h.options();
+  const long rows = (long)world * cap;
+  Tensor rx = at::from_blob(own + xo, {rows, H}, opt);
+  Tensor ri = at::from_blob(own + io, {rows, k}, opt.dtype(at::kInt));
+  Tensor rw = at::from_blob(own + wo, {rows, k}, opt.dtype(at::kFloat));
+  Tensor ry = at::from_blob(own + yo, {rows, H}, opt);
+  moe_routed_mx_into(rx, rw, ri, w13, s13c, w2, s2c, first, count, tiled, ry);
+  Tensor out = at::empty({T, H}, opt);
+  LAUNCH(qb::ep_combine(b.data(), world, rank, cap, H, k, slots.data_ptr<int>(), T, out.data_ptr(), H,
+                        state.data_ptr<int>(), tns, err_ptr(h), stream()));
+  return out;
+}
+
+int64_t ep_region_bytes(int64_t world, int64_t cap, int64_t H, int64_t k) {
+  return qb::ep_region_bytes(world, cap, H, k);
 }
 
 Tensor moe_routed_fp4(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13, Tensor w2, Tensor s2, int64_t first,
@@ -500,6 +544,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     return t;
   });
   m.def("deltanet_decode", &deltanet_decode);
+  m.def("ep_moe", &ep_moe);
+  m.def("ep_region_bytes", &ep_region_bytes);
   m.def("gated_delta_chunked", &gated_delta_chunked);
   m.def("causal_conv_varlen", &causal_conv_varlen);
   m.def("gated_delta_varlen", &gated_delta_varlen);

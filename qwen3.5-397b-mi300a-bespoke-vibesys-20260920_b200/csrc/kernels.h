@@ -57,6 +57,14 @@ long gated_delta_chunked_scratch(int T, int n_chunks, int nk, int nv, int dk);
 int deltanet_decode(const void* proj, long ldp, void* conv_state, long cls, const void* conv_w, const float* a_log,
                     const float* dt_bias, float* state, long sls, const void* norm_w, const int* seg_lane, int T,
                     int nk, int nv, int dk, int dv, int K, float eps, void* out, cudaStream_t s);
+// expert-parallel MoE over peer memory (ep.cu)
+long ep_region_bytes(int world, int cap, int H, int k);
+int ep_dispatch(void* const* bases, int world, int rank, int cap, int H, int k, int experts_per_rank, const void* x,
+                long ldx, const int* topi, const float* topw, int T, int* slots, int* counts, int* state,
+                unsigned long long timeout_ns, int* err, cudaStream_t s);
+int ep_combine(void* const* bases, int world, int rank, int cap, int H, int k, const int* slots, int T, void* out,
+               long ldo, const int* state, unsigned long long timeout_ns, int* err, cudaStream_t s);
+void ep_offsets(int world, int cap, int H, int k, int par, long* x, long* i, long* w, long* y);
 // in-graph clock stamp (elementwise.cu): buf[slot] = %globaltimer
 int stamp(unsigned long long* buf, int slot, cudaStream_t s);
 // block-scaled MoE (moe_mx.cu): token tile width, tile prefix, activation split, expert GEMM

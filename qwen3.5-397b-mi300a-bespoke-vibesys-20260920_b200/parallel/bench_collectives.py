@@ -10,6 +10,13 @@ microseconds per call, bus bandwidth (2 (N-1)/N x bytes / time, the NCCL convent
 fraction of the NVLink roofline of `fused`: an all-reduce without in-switch reduction must move
 2 (N-1)/N x the message bytes through every GPU's links, at 770 GB/s measured per-direction
 peer bandwidth.
+
+``--case ep``: expert-parallel MoE (dispatch -> block-scaled expert GEMMs -> combine over peer
+memory, ``parallel.ep``) at the full geometry (512 experts top-10, hidden 4096, expert width
+1024, random MXFP4 codes, uniform random routing) against the replicated form the tensor-parallel
+model uses (NCCL all-gather of the tokens, every rank's experts on all tokens, NCCL reduce-scatter
+of the partial sums). Roofline of a call: the slower of this rank's active expert weights over
+HBM (measured copy bandwidth) and its dispatch + combine bytes over NVLink (770 GB/s).
 """
 
 from __future__ import annotations
@@ -24,11 +31,85 @@ import torch.distributed as dist
 PEER_GBS = 770.0
 
 
+def ep_sweep(args, rank, world, dev) -> list[dict]:
+    from ..ops import core as ops
+    from ..ops.kbench import peaks
+    from .ep import EPComm
+
+    E, k, H, I = 512, 10, args.hidden, 1024
+    per = E // world
+    g = torch.Generator(device=dev).manual_seed(11 + rank)
+    u8 = dict(dtype=torch.uint8, device=dev)
+    experts = {"w13": torch.randint(0, 256, (per, 2 * I, H // 2), generator=g, **u8),
+               "s13": torch.full((per, 2 * I, H // 32), 120, **u8),
+               "w2": torch.randint(0, 256, (per, H, I // 2), generator=g, **u8),
+               "s2": torch.full((per, H, I // 32), 120, **u8)}
+    ops.prepare_experts(experts)
+    cap = max(max(args.tokens) // world, 1)
+    ep = EPComm(rank, world, dev, cap=cap, hidden=H, top_k=k, experts=E)
+    hbm = peaks()["hbm_gbs"]
+    rows = []
+    for N in args.tokens:
+        T = max(N // world, 1)
+        h = torch.randn(T, H, device=dev, generator=g).bfloat16()
+        tw, ti = ops.router_topk(torch.randn(T, E, device=dev, generator=g).bfloat16(), k)
+
+        def ep_call():
+            ep.moe(h, tw, ti, experts)
+
+        def replicated():
+            hs = torch.empty(T * world, H, device=dev, dtype=torch.bfloat16)
+            dist.all_gather_into_tensor(hs, h)
+            ws = torch.empty(T * world, k, device=dev)
+            dist.all_gather_into_tensor(ws, tw)
+            iss = torch.empty(T * world, k, device=dev, dtype=torch.int32)
+            dist.all_gather_into_tensor(iss, ti)
+            y = ops.moe_routed(hs, ws, iss, experts, rank * per, per).float()
+            out = torch.empty(T, H, device=dev)
+            dist.reduce_scatter_tensor(out, y)
+
+        out = {"case": "ep", "tokens": T * world, "tokens_per_rank": T, "n_gpus": world}
+        for name, fn in (("ep", ep_call), ("replicated", replicated)):
+            for _ in range(3):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(args.ep_iters):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            us = torch.tensor([s.elapsed_time(e) * 1e3 / args.ep_iters], device=dev)
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+            out[name + "_us"] = round(us.item(), 1)
+        # bytes: rows this rank sends to other ranks (dispatch) and reads back (combine)
+        owner = ti.long() // per
+        sent = sum(int(((owner == d).any(dim=1)).sum()) for d in range(world) if d != rank)
+        link_bytes = 2 * sent * H * 2
+        # this rank's active experts: any token of any rank may route to them (uniform routing)
+        hits = torch.zeros(E, dtype=torch.int64, device=dev)
+        ti_all = torch.empty(T * world, k, device=dev, dtype=torch.int32)
+        dist.all_gather_into_tensor(ti_all, ti)
+        hits.index_add_(0, ti_all.long().flatten(), torch.ones(ti_all.numel(), dtype=torch.int64, device=dev))
+        active = int((hits[rank * per:(rank + 1) * per] > 0).sum())
+        wbytes = active * (3 * H * I // 2) * (1 + 1 / 16)
+        roof_us = max(wbytes / (hbm * 1e3), link_bytes / (PEER_GBS * 1e3))
+        out.update(link_bytes=link_bytes, active_experts=active, roofline_us=round(roof_us, 1),
+                   ep_busbw_gbs=round(link_bytes / out["ep_us"] / 1e3, 1),
+                   ep_frac_of_roofline=round(roof_us / out["ep_us"], 3))
+        rows.append(out)
+    ep.close()
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, nargs="*", default=[1, 4, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096])
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--hidden", type=int, default=4096)
+    ap.add_argument("--case", default="allreduce", choices=["allreduce", "ep"])
+    ap.add_argument("--ep-iters", type=int, default=20)
     args = ap.parse_args()
     from ..ops import core as ops
     from . import comm as commmod
@@ -36,6 +117,15 @@ def main():
 
     rank, world = commmod.init("nccl")
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    if args.case == "ep":
+        if args.tokens == ap.get_default("tokens"):
+            args.tokens = [8, 64, 512, 2048, 8192]
+        rows = ep_sweep(args, rank, world, dev)
+        if rank == 0:
+            for r in rows:
+                print(json.dumps(r))
+        dist.destroy_process_group()
+        return
     H = args.hidden
     symm = SymmComm(rank, world, dev, max_rows=min(512, max(args.tokens)), hidden=H, sp_rows=max(args.tokens))
     w = torch.ones(H, device=dev)

@@ -22,6 +22,26 @@ MAX_BLOCKS = 296  # one-shot kernel: two CTAs per SM on a 148-SM B200
 SP_MAX_BLOCKS = 296  # sequence-parallel kernel: one row per CTA; more CTAs measured slower
 
 
+def alloc_region(rank: int, world: int, device, nbytes: int, group=None) -> tuple[list[int], int, list[int]]:
+    """Allocate this rank's region (``cudaMalloc``, zeroed), export it and map every peer's.
+    Returns (every rank's base address as seen here, own pointer, opened peer pointers); every
+    rank must call this together (it all-gathers the IPC handles)."""
+    with torch.cuda.device(device):
+        ptr, handle = ext().symm_alloc(nbytes)
+    handles = [None] * world
+    dist.all_gather_object(handles, handle, group=group)
+    bases, opened = [], []
+    for r in range(world):
+        if r == rank:
+            bases.append(ptr)
+        else:
+            with torch.cuda.device(device):
+                p = ext().symm_open(handles[r])
+            opened.append(p)
+            bases.append(p)
+    return bases, ptr, opened
+
+
 class SymmComm:
     """One-shot region (``max_rows`` rows) for decode-sized messages and, when ``sp_rows`` > 0, a
     sequence-parallel region for prefill-sized ones (reduce-scatter + add + RMSNorm +
@@ -61,20 +81,9 @@ class SymmComm:
         """Allocate and export this rank's region, map every peer's (or use given bases)."""
         if bases is not None:
             return list(bases)
-        with torch.cuda.device(self.device):
-            ptr, handle = ext().symm_alloc(nbytes)
+        out, ptr, opened = alloc_region(self.rank, self.world, self.device, nbytes, group)
         self.own.append(ptr)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, handle, group=group)
-        out = []
-        for r in range(self.world):
-            if r == self.rank:
-                out.append(ptr)
-            else:
-                with torch.cuda.device(self.device):
-                    p = ext().symm_open(handles[r])
-                self.opened.append(p)
-                out.append(p)
+        self.opened.extend(opened)
         return out
 
     @staticmethod

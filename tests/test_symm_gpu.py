@@ -54,3 +54,76 @@ def test_two_gpu_fused_equals_nccl():
     procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "symm_rank.py"), str(r), "2", str(port)], env=env)
              for r in range(2)]
     assert [p.wait(timeout=300) for p in procs] == [0, 0]
+
+
+def test_expert_parallel_one_rank_equals_local_moe():
+    """Expert-parallel dispatch / experts / combine with one rank (every token's row goes to
+    itself through the receive area) equals the local routed-expert op, over consecutive calls
+    (parity halves reused) and token counts from 0 to the area's capacity."""
+    from qwen35_b200.ops import core as ops
+    from qwen35_b200.ops._ext import ext
+    from qwen35_b200.parallel.ep import EPComm
+    from qwen35_b200.utils import mxfp4
+
+    dev = torch.device("cuda", 0)
+    E, k, H, I = 16, 4, 512, 256
+    g = torch.Generator(device=dev).manual_seed(3)
+    w13, s13 = mxfp4.quantize(torch.randn(E, 2 * I, H, device=dev, generator=g) * 0.02)
+    w2, s2 = mxfp4.quantize(torch.randn(E, H, I, device=dev, generator=g) * 0.02)
+    full = {"w13": w13, "s13": s13, "w2": w2, "s2": s2}
+    ep = EPComm(0, 1, dev, cap=128, hidden=H, top_k=k, experts=E)
+    ext().clear_status(torch.empty(1, device=dev))
+    for T in (5, 128, 0, 77, 1):
+        h = torch.randn(T, H, device=dev, generator=g).bfloat16()
+        tw, ti = ops.router_topk(torch.randn(T, E, device=dev, generator=g).bfloat16(), k)
+        y = ep.moe(h, tw, ti, {kk: v.clone() for kk, v in full.items()})
+        ref = ops.moe_routed(h, tw, ti, {kk: v.clone() for kk, v in full.items()}, 0, E)
+        torch.cuda.synchronize()
+        assert y.shape == (T, H)
+        if T:
+            assert (y.float() - ref.float()).abs().max().item() <= 1e-2 * ref.float().abs().max().item() + 1e-3
+    assert ext().status(torch.empty(1, device=dev)).tolist()[0] == 0
+    ep.close()
+
+
+def test_expert_parallel_silent_peer_times_out_cleanly():
+    """A peer that never dispatches: the receive and combine waits give up within the bound,
+    the status word says ERR_PEER_WAIT, the output is finite and the GPU stays usable."""
+    from qwen35_b200.ops import core as ops
+    from qwen35_b200.ops._ext import ext
+    from qwen35_b200.parallel.ep import EPComm
+    from qwen35_b200.utils import mxfp4
+
+    dev = torch.device("cuda", 0)
+    E, k, H, I = 16, 2, 256, 128
+    nbytes = ext().ep_region_bytes(2, 32, H, k)
+    own, _ = ext().symm_alloc(nbytes)
+    fake_peer, _ = ext().symm_alloc(nbytes)  # a local region standing in for a silent peer
+    ep = EPComm(0, 2, dev, cap=32, hidden=H, top_k=k, experts=E, bases=[own, fake_peer], timeout_s=0.05)
+    w13, s13 = mxfp4.quantize(torch.randn(E // 2, 2 * I, H, device=dev) * 0.02)
+    w2, s2 = mxfp4.quantize(torch.randn(E // 2, H, I, device=dev) * 0.02)
+    ext().clear_status(torch.empty(1, device=dev))
+    h = torch.randn(8, H, device=dev).bfloat16()
+    tw, ti = ops.router_topk(torch.randn(8, E, device=dev).bfloat16(), k)
+    y = ep.moe(h, tw, ti, {"w13": w13, "s13": s13, "w2": w2, "s2": s2})
+    torch.cuda.synchronize()
+    assert ext().status(torch.empty(1, device=dev)).tolist()[0] == 5  # ERR_PEER_WAIT
+    ext().clear_status(torch.empty(1, device=dev))
+    assert torch.isfinite(y.float()).all()
+    z = ops.rmsnorm(h, torch.ones(H, device=dev), 1e-6)  # the context is still usable
+    torch.cuda.synchronize()
+    assert torch.isfinite(z.float()).all()
+    ext().symm_free(own)
+    ext().symm_free(fake_peer)
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_expert_parallel_equals_local():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ep_rank.py"), str(r), "2", str(port)], env=env)
+             for r in range(2)]
+    assert [p.wait(timeout=300) for p in procs] == [0, 0]
