@@ -388,8 +388,10 @@ void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s
   Tensor y2 = at::empty({cap, H}, h.options());
   uint8_t *hp = hl.data_ptr<uint8_t>(), *lp = hp + plane;
   uint8_t *shp = sf.data_ptr<uint8_t>(), *slp = merged ? shp : shp + sf_plane;
-  LAUNCH(qb::mx_quant(h.data_ptr(), perm_tok, n_assign, cap, H, offsets, counts, tstart, count, BN, hp, lp, shp, slp,
-                      stream(), merged));
+  // each token quantised once, then expanded into its assignments' rows (k x fewer conversions)
+  Tensor qs = at::empty({(long)T * (2 * H + H / 32)}, u8);
+  LAUNCH(qb::mx_quant_expand(h.data_ptr(), T, perm_tok, n_assign, cap, H, offsets, tstart, count, BN,
+                             qs.data_ptr<uint8_t>(), hp, lp, shp, slp, stream(), merged));
   LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w13.data_ptr<uint8_t>(), s13c.data_ptr<uint8_t>(), n13, H, offsets,
                          counts, tstart, count, BN, 1, inter.data_ptr(), I, err_ptr(h), stream(), tiled));
   LAUNCH(qb::mx_quant(inter.data_ptr(), nullptr, n_assign, cap, I, offsets, counts, tstart, count, BN, hp, lp, shp,

@@ -75,6 +75,11 @@ int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, 
              cudaStream_t s, bool merged = false);
 // diagnostic wait-cycle counters of the block-scaled MoE kernel (QB_MX_PROBE=1), read and cleared
 int mx_probe_read(unsigned long long* out);
+// the routed MoE input quantised once per token (scratch: T x (2K + K/32) bytes), then expanded
+// into the expert-sorted rows and tile scale chunks (same bytes as mx_quant with a permutation)
+int mx_quant_expand(const void* x, int T, const int* perm, const int* n_rows, int cap, int K, const int* offsets,
+                    const int* tstart, int count, int BN, uint8_t* qscratch, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi,
+                    uint8_t* sf_lo, cudaStream_t s, bool merged = false);
 // merged activation buffers are used (tiled codes with one TMA box per operand)
 bool mx_merged(bool tiled, int BN);
 int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, const uint8_t* sf_lo, int cap,

@@ -590,6 +590,84 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
   }
 }
 
+// Each token once: rows of x [T, K] -> hi / lo e4m3 bytes [T, K] and one exponent byte (E + 127)
+// per 32-element block [T, K/32], with the same per-lane code as mx_quant_kernel (identical
+// bytes). mx_expand_kernel then places every (token, expert) assignment's row and scales into the
+// expert-sorted tiles: the routed MoE input is quantised T times instead of T x k times.
+__global__ void mx_quant_rows_kernel(const bf16* x, int T, int K, int wpr, uint8_t* hi, uint8_t* lo,
+                                     uint8_t* exps) {
+  const int lane = threadIdx.x % 32;
+  const int w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  const int a = w / wpr, part = w % wpr;
+  if (a >= T) return;
+  const int kseg = K / wpr, kbeg = part * kseg, kend = kbeg + kseg;
+  const bf16* src = x + (long)a * K;
+  for (int kbase = kbeg; kbase < kend; kbase += 256) {
+    const int k0 = kbase + lane * 8;
+    const bool valid = k0 < kend;
+    const uint4 raw = valid ? *reinterpret_cast<const uint4*>(src + k0) : make_uint4(0, 0, 0, 0);
+    const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&raw);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(p2[i]);
+      v[2 * i] = f.x;
+      v[2 * i + 1] = f.y;
+    }
+    uint32_t mb = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mb = max(mb, __float_as_uint(fabsf(v[i])));
+    mb = max(mb, __shfl_xor_sync(0xffffffff, mb, 1));
+    mb = max(mb, __shfl_xor_sync(0xffffffff, mb, 2));
+    const int E = mx_block_exponent(mb);
+    uint32_t hw[2] = {0, 0}, lw[2] = {0, 0};
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint8_t ch, cl;
+      mx_split(v[i], E, ch, cl);
+      hw[i / 4] |= (uint32_t)ch << (8 * (i % 4));
+      lw[i / 4] |= (uint32_t)cl << (8 * (i % 4));
+    }
+    if (!valid) continue;
+    *reinterpret_cast<uint2*>(hi + (long)a * K + k0) = make_uint2(hw[0], hw[1]);
+    *reinterpret_cast<uint2*>(lo + (long)a * K + k0) = make_uint2(lw[0], lw[1]);
+    if ((lane & 3) == 0) exps[(long)a * (K / 32) + k0 / 32] = (uint8_t)(E + 127);
+  }
+}
+
+// One warp per assignment row a < *n_rows: the hi / lo bytes of token perm[a] and its block
+// exponents, into row a and the chunk of row a's token tile (as mx_quant_kernel writes them).
+__global__ void mx_expand_kernel(const uint8_t* qhi, const uint8_t* qlo, const uint8_t* exps, const int* perm,
+                                 const int* n_rows, int K, const int* offsets, const int* tstart, int count, int BN,
+                                 uint8_t* hi, uint8_t* lo, uint8_t* sf_hi, uint8_t* sf_lo, int cstride, int lo_rows) {
+  const int lane = threadIdx.x % 32;
+  const int a = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
+  if (a >= *n_rows) return;
+  int lo_e = 0, hi_e = count - 1;
+  while (lo_e < hi_e) {
+    const int mid = (lo_e + hi_e + 1) >> 1;
+    if (offsets[mid] <= a) lo_e = mid; else hi_e = mid - 1;
+  }
+  const int r_e = a - offsets[lo_e];
+  const int tt = tstart[lo_e] + r_e / BN, rr = r_e % BN;
+  const long src = perm[a];
+  const uint4* sh = reinterpret_cast<const uint4*>(qhi + src * K);
+  const uint4* sl = reinterpret_cast<const uint4*>(qlo + src * K);
+  uint4* dh = reinterpret_cast<uint4*>(hi + (long)a * K);
+  uint4* dl = reinterpret_cast<uint4*>(lo + (long)a * K);
+  for (int v = lane; v < K / 16; v += 32) {
+    dh[v] = sh[v];
+    dl[v] = sl[v];
+  }
+  const long sf_tile = (long)tt * (K / MX_SK) * cstride;
+  for (int kb = lane; kb < K / 32; kb += 32) {
+    const uint8_t eb = exps[src * (K / 32) + kb];
+    const long cb = sf_tile + (long)(kb / 4) * cstride;
+    sf_hi[cb + mx_chunk_offset(rr, kb % 4)] = eb;
+    sf_lo[cb + mx_chunk_offset(rr + lo_rows, kb % 4)] = (uint8_t)(eb - 4);
+  }
+}
+
 // tstart[e] = sum over e' < e of ceil(counts[e'] / BN), tstart[count] = total token tiles.
 __global__ void mx_tile_prefix_kernel(const int* counts, int count, int BN, int* tstart) {
   const int lane = threadIdx.x;
@@ -717,6 +795,23 @@ int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, 
   mx_quant_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const bf16*)x, perm, n_rows, K, wpr, offsets, tstart,
                                                                count, BN, hi, lo, sf_hi, sf_lo, MX_CHUNK,
                                                                merged ? BN : 0);
+  return (int)cudaGetLastError();
+}
+
+int mx_quant_expand(const void* x, int T, const int* perm, const int* n_rows, int cap, int K, const int* offsets,
+                    const int* tstart, int count, int BN, uint8_t* qscratch, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi,
+                    uint8_t* sf_lo, cudaStream_t s, bool merged) {
+  if (!cap || !T) return 0;
+  if (K % MX_SK) return -1;
+  uint8_t* qhi = qscratch;
+  uint8_t* qlo = qhi + (long)T * K;
+  uint8_t* exps = qlo + (long)T * K;
+  int wpr = 1;
+  while ((long)T * wpr < 2048 && (K / (wpr * 2)) % 256 == 0) wpr *= 2;
+  const long warps = (long)T * wpr;
+  mx_quant_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const bf16*)x, T, K, wpr, qhi, qlo, exps);
+  mx_expand_kernel<<<(unsigned)((cap + 7) / 8), 256, 0, s>>>(qhi, qlo, exps, perm, n_rows, K, offsets, tstart, count,
+                                                             BN, hi, lo, sf_hi, sf_lo, MX_CHUNK, merged ? BN : 0);
   return (int)cudaGetLastError();
 }
 
