@@ -274,7 +274,10 @@ def fa_plan(q, k_cache, cu_h, block_size, max_ctx):
         _fa_tiles_cache[key] = tiles
     base = tiles.shape[0] * k_cache.shape[1]
     splits = 1
-    if base < _FA_SMS:
+    forced = flags.get("QB_FA_SPLITS")
+    if forced > 0:
+        splits = max(1, min(forced, (int(max_ctx) + 63) // 64, 128))
+    elif base < _FA_SMS:
         splits = max(1, min(_FA_SMS // base, (int(max_ctx) + 63) // 64, 128))
     return tiles, splits
 

@@ -49,6 +49,8 @@ _def("QB_MOE_BN_MAX", int, 64, "largest token tile of the f16-decode MoE kernel"
 _def("QB_MOE_SMEM_A", bool, False, "f16-decode MoE: stage decoded weights in shared memory", native=True)
 _def("QB_FA", bool, True, "tcgen05 flash attention for full-attention layers (else the CUDA-core kernel)",
      lockstep=True)
+_def("QB_FA_SPLITS", int, 0, "flash attention: key-range splits per tile (0: enough CTAs for one wave)",
+     lockstep=True)
 _def("QB_DN_CHUNKED", bool, False, "chunked (WY) DeltaNet prefill instead of the token recurrence",
      lockstep=True)
 _def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
