@@ -356,8 +356,10 @@ Tensor moe_routed_bf16(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor w2
 }
 
 // Block-scaled path: weights' e8m0 scales pre-arranged in 512-byte chunks (s13c / s2c).
+// sparse_rows: many rows are routed nowhere (expert ids -1, an expert-parallel receive area):
+// they are neither quantised nor written.
 void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
-                        int64_t first, int64_t count, bool tiled, Tensor out) {
+                        int64_t first, int64_t count, bool tiled, Tensor out, bool sparse_rows = false) {
   CHECK_BF16(h);
   TORCH_CHECK(h.is_contiguous() && out.is_contiguous(), "moe: h and out contiguous");
   const int T = h.size(0), H = h.size(1), k = topi.size(1);
@@ -391,14 +393,16 @@ void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s
   // each token quantised once, then expanded into its assignments' rows (k x fewer conversions)
   Tensor qs = at::empty({(long)T * (2 * H + H / 32)}, u8);
   LAUNCH(qb::mx_quant_expand(h.data_ptr(), T, perm_tok, n_assign, cap, H, offsets, tstart, count, BN,
-                             qs.data_ptr<uint8_t>(), hp, lp, shp, slp, stream(), merged));
+                             qs.data_ptr<uint8_t>(), hp, lp, shp, slp, stream(), merged,
+                             sparse_rows ? topi_c.data_ptr<int>() : nullptr, k));
   LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w13.data_ptr<uint8_t>(), s13c.data_ptr<uint8_t>(), n13, H, offsets,
                          counts, tstart, count, BN, 1, inter.data_ptr(), I, err_ptr(h), stream(), tiled));
   LAUNCH(qb::mx_quant(inter.data_ptr(), nullptr, n_assign, cap, I, offsets, counts, tstart, count, BN, hp, lp, shp,
                       slp, stream(), merged));
   LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w2.data_ptr<uint8_t>(), s2c.data_ptr<uint8_t>(), H, I, offsets,
                          counts, tstart, count, BN, 0, y2.data_ptr(), H, err_ptr(h), stream(), tiled));
-  LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream()));
+  LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream(),
+                         sparse_rows));
 }
 
 Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
@@ -436,7 +440,7 @@ Tensor ep_moe(std::vector<int64_t> bases, int64_t rank, Tensor h, Tensor topw, T
   Tensor ri = at::from_blob(own + io, {rows, k}, opt.dtype(at::kInt));
   Tensor rw = at::from_blob(own + wo, {rows, k}, opt.dtype(at::kFloat));
   Tensor ry = at::from_blob(own + yo, {rows, H}, opt);
-  moe_routed_mx_into(rx, rw, ri, w13, s13c, w2, s2c, first, count, tiled, ry);
+  moe_routed_mx_into(rx, rw, ri, w13, s13c, w2, s2c, first, count, tiled, ry, true);
   Tensor out = at::empty({T, H}, opt);
   LAUNCH(qb::ep_combine(b.data(), world, rank, cap, H, k, slots.data_ptr<int>(), T, out.data_ptr(), H,
                         state.data_ptr<int>(), tns, err_ptr(h), stream()));

@@ -79,7 +79,8 @@ int mx_probe_read(unsigned long long* out);
 // into the expert-sorted rows and tile scale chunks (same bytes as mx_quant with a permutation)
 int mx_quant_expand(const void* x, int T, const int* perm, const int* n_rows, int cap, int K, const int* offsets,
                     const int* tstart, int count, int BN, uint8_t* qscratch, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi,
-                    uint8_t* sf_lo, cudaStream_t s, bool merged = false);
+                    uint8_t* sf_lo, cudaStream_t s, bool merged = false, const int* skip_ids = nullptr,
+                    int k = 0);
 // merged activation buffers are used (tiled codes with one TMA box per operand)
 bool mx_merged(bool tiled, int BN);
 int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, const uint8_t* sf_lo, int cap,
@@ -103,7 +104,8 @@ int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8
                     int count, int cap, int act, void* out, int out_cols, int* err, cudaStream_t s, int max_ctas);
 int moe_gather_bf16(const void* h, const int* perm_tok, const int* n_assign, int cap, int H, void* xh,
                     cudaStream_t s);
-int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s);
+int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s,
+                bool skip_empty = false);
 int moe_expert_gemm_bf16(const void* xin, int in_cols, const void* w, int n_rows, int k_cols, long w_expert_stride,
                          const int* offsets, const int* counts, int count, int cap, int act, void* out, int out_cols,
                          cudaStream_t s);

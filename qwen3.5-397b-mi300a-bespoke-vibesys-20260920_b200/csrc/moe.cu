@@ -160,8 +160,14 @@ int moe_gather_bf16(const void* h, const int* perm_tok, const int* n_assign, int
 }
 
 // out[t, :] = sum_j topw[t, j] * y2[inv[t, j], :] over local assignments (fp32, rounded once)
-__global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* topw, int k, int H, bf16* out) {
+__global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* topw, int k, int H, bf16* out,
+                                   bool skip_empty) {
   const long t = blockIdx.x;
+  if (skip_empty) {  // rows no expert of this rank serves are left unwritten (nobody reads them)
+    bool any = false;
+    for (int j = 0; j < k; ++j) any |= inv[t * k + j] >= 0;
+    if (!any) return;
+  }
   // blockIdx.y splits the row so that small batches still spread over the SMs
   const int per = (H + gridDim.y - 1) / gridDim.y;
   const int i0 = blockIdx.y * per, i1 = min(H, i0 + per);
@@ -184,11 +190,12 @@ __global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* 
   }
 }
 
-int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s) {
+int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s,
+                bool skip_empty) {
   if (!T) return 0;
   int split = 1;  // row chunks of at least 1024 columns (multiples of 8) until ~2 blocks per SM
   while (T * split < 296 && H / (split * 2) >= 1024 && (H / (split * 2)) % 8 == 0) split *= 2;
-  moe_combine_kernel<<<dim3(T, split), 128, 0, s>>>((const bf16*)y2, inv, topw, k, H, (bf16*)out);
+  moe_combine_kernel<<<dim3(T, split), 128, 0, s>>>((const bf16*)y2, inv, topw, k, H, (bf16*)out, skip_empty);
   return (int)cudaGetLastError();
 }
 

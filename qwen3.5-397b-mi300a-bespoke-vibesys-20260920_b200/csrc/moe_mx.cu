@@ -595,11 +595,12 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
 // bytes). mx_expand_kernel then places every (token, expert) assignment's row and scales into the
 // expert-sorted tiles: the routed MoE input is quantised T times instead of T x k times.
 __global__ void mx_quant_rows_kernel(const bf16* x, int T, int K, int wpr, uint8_t* hi, uint8_t* lo,
-                                     uint8_t* exps) {
+                                     uint8_t* exps, const int* ids, int k) {
   const int lane = threadIdx.x % 32;
   const int w = blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int a = w / wpr, part = w % wpr;
   if (a >= T) return;
+  if (ids && ids[(long)a * k] < 0) return;  // a row routed nowhere (unused receive-area row)
   const int kseg = K / wpr, kbeg = part * kseg, kend = kbeg + kseg;
   const bf16* src = x + (long)a * K;
   for (int kbase = kbeg; kbase < kend; kbase += 256) {
@@ -800,7 +801,7 @@ int mx_quant(const void* x, const int* perm, const int* n_rows, int cap, int K, 
 
 int mx_quant_expand(const void* x, int T, const int* perm, const int* n_rows, int cap, int K, const int* offsets,
                     const int* tstart, int count, int BN, uint8_t* qscratch, uint8_t* hi, uint8_t* lo, uint8_t* sf_hi,
-                    uint8_t* sf_lo, cudaStream_t s, bool merged) {
+                    uint8_t* sf_lo, cudaStream_t s, bool merged, const int* skip_ids, int k) {
   if (!cap || !T) return 0;
   if (K % MX_SK) return -1;
   uint8_t* qhi = qscratch;
@@ -809,7 +810,8 @@ int mx_quant_expand(const void* x, int T, const int* perm, const int* n_rows, in
   int wpr = 1;
   while ((long)T * wpr < 2048 && (K / (wpr * 2)) % 256 == 0) wpr *= 2;
   const long warps = (long)T * wpr;
-  mx_quant_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const bf16*)x, T, K, wpr, qhi, qlo, exps);
+  mx_quant_rows_kernel<<<(unsigned)((warps + 7) / 8), 256, 0, s>>>((const bf16*)x, T, K, wpr, qhi, qlo, exps,
+                                                                   skip_ids, k);
   mx_expand_kernel<<<(unsigned)((cap + 7) / 8), 256, 0, s>>>(qhi, qlo, exps, perm, n_rows, K, offsets, tstart, count,
                                                              BN, hi, lo, sf_hi, sf_lo, MX_CHUNK, merged ? BN : 0);
   return (int)cudaGetLastError();
