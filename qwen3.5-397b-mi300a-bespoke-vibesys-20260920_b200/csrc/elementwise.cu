@@ -378,15 +378,18 @@ __global__ void router_topk_kernel(const bf16* logits, long ld, int T, int E, in
         bi = oi;
       }
     }
-    tw[r] = bv;
-    ti[r] = bi;
-    tot += bv;
-    if ((bi % 32) == lane) p[bi / 32] = -1.f;
+    // a row whose probabilities are NaN selects nothing (bi stays out of range): it gets no
+    // expert (id -1, weight 0) instead of an index past the array
+    const bool found = bi < E;
+    tw[r] = found ? bv : 0.f;
+    ti[r] = found ? bi : -1;
+    tot += tw[r];
+    if (found && (bi % 32) == lane) p[bi / 32] = -1.f;
   }
   if (lane == 0) {
     for (int r = 0; r < k; ++r) {
       // renormalised weight, rounded through the logits dtype like the reference (.to(bf16))
-      wout[t * k + r] = rbf(tw[r] / tot);
+      wout[t * k + r] = ti[r] >= 0 ? rbf(tw[r] / tot) : 0.f;
       iout[t * k + r] = ti[r];
     }
   }

@@ -91,7 +91,10 @@ __global__ void __launch_bounds__(1024) ep_route_kernel(const int* topi, int T, 
     int c = 0;
     for (int t = t0; t < t1; ++t) {
       bool hit = false;
-      for (int j = 0; j < k; ++j) hit |= topi[(long)t * k + j] / per_rank == d;
+      for (int j = 0; j < k; ++j) {
+        const int e = topi[(long)t * k + j];
+        hit |= e >= 0 && e / per_rank == d;  // id -1: no expert
+      }
       c += hit;
     }
     // exclusive block scan of c
@@ -117,7 +120,10 @@ __global__ void __launch_bounds__(1024) ep_route_kernel(const int* topi, int T, 
     int pos = v - c + (wid > 0 ? wsum[wid - 1] : 0);
     for (int t = t0; t < t1; ++t) {
       bool hit = false;
-      for (int j = 0; j < k; ++j) hit |= topi[(long)t * k + j] / per_rank == d;
+      for (int j = 0; j < k; ++j) {
+        const int e = topi[(long)t * k + j];
+        hit |= e >= 0 && e / per_rank == d;
+      }
       slots[(long)t * world + d] = hit ? pos++ : -1;
     }
     if (tid == 0) counts[d] = base_d;

@@ -216,6 +216,22 @@ def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, 
 DN_CHUNK = 64
 DN_CHUNK_MIN = 64
 _dn_chunk_cache: dict = {}
+# Device tables read by a captured CUDA graph must outlive it: entries used during a capture are
+# kept here for good, the bounded caches evict only tables no graph refers to.
+_captured_tables: dict = {}
+
+
+def _capturing() -> bool:
+    return torch.cuda.is_available() and torch.cuda.is_current_stream_capturing()
+
+
+def _cache_put(cache: dict, tag: tuple, key, value) -> None:
+    if _capturing():
+        _captured_tables[tag + key] = value
+        return
+    if len(cache) >= 256:
+        cache.pop(next(iter(cache)))
+    cache[key] = value
 
 
 def dn_chunk_plan(cu_h, dk, dv, device):
@@ -232,7 +248,7 @@ def dn_chunk_plan(cu_h, dk, dv, device):
     if not lens or max(lens) < DN_CHUNK_MIN:
         return None
     key = (tuple(cu_h), device)
-    hit = _dn_chunk_cache.get(key)
+    hit = _dn_chunk_cache.get(key) or _captured_tables.get(("dn",) + key)
     if hit is None:
         rows, seg0 = [], [0]
         for s, n in enumerate(lens):
@@ -240,9 +256,9 @@ def dn_chunk_plan(cu_h, dk, dv, device):
                 rows.append([s, cu_h[s] + r, min(DN_CHUNK, n - r)])
             seg0.append(len(rows))
         hit = (torch.tensor(rows, dtype=torch.int32).to(device), torch.tensor(seg0, dtype=torch.int32).to(device))
-        if len(_dn_chunk_cache) >= 256:
-            _dn_chunk_cache.pop(next(iter(_dn_chunk_cache)))
-        _dn_chunk_cache[key] = hit
+        _cache_put(_dn_chunk_cache, ("dn",), key, hit)
+    elif _capturing():
+        _captured_tables[("dn",) + key] = hit
     return hit
 
 
@@ -267,11 +283,13 @@ def fa_plan(q, k_cache, cu_h, block_size, max_ctx):
     key = (tuple(cu_h), g, q.device)
     tiles = _fa_tiles_cache.get(key)
     if tiles is None:
+        tiles = _captured_tables.get(("fa",) + key)
+    if tiles is None:
         host = torch.tensor(fa_tiles(cu_h, g), dtype=torch.int32)
         tiles = host.to(q.device)
-        if len(_fa_tiles_cache) >= 256:
-            _fa_tiles_cache.pop(next(iter(_fa_tiles_cache)))
-        _fa_tiles_cache[key] = tiles
+        _cache_put(_fa_tiles_cache, ("fa",), key, tiles)
+    elif _capturing():
+        _captured_tables[("fa",) + key] = tiles
     base = tiles.shape[0] * k_cache.shape[1]
     splits = 1
     forced = flags.get("QB_FA_SPLITS")

@@ -477,3 +477,27 @@ def test_deltanet_decode_fused(nk, nv, lanes):
     assert (st1 - st2).abs().max().item() < 1e-4 * st2.abs().max().item() + 1e-6
     close(out, exp, rtol=2e-2, atol=2e-2)
     status_ok()
+
+
+def test_router_topk_nan_rows_select_no_expert():
+    """A row of NaN router logits (padding rows of a fixed-width captured prefill are not
+    initialised) gets expert id -1 and weight 0 instead of an index past the expert array;
+    the other rows are unaffected and the routed-expert op writes zeros for such rows."""
+    E, k = 64, 4
+    lg = rnd(6, E, seed=9)
+    lg[2] = float("nan")
+    lg[4, :] = float("nan")
+    w, i = ops.router_topk(lg, k)
+    torch.cuda.synchronize()
+    assert (i[2] == -1).all() and (i[4] == -1).all() and (w[2] == 0).all() and (w[4] == 0).all()
+    ok = [0, 1, 3, 5]
+    rw, ri = ref.router_topk(lg[ok], k)
+    assert torch.equal(i[ok].long().sort(-1).values, ri.long().sort(-1).values)
+    H, I = 256, 128
+    w13, s13 = mxfp4.quantize(torch.randn(E, 2 * I, H, device=DEV) * 0.02)
+    w2, s2 = mxfp4.quantize(torch.randn(E, H, I, device=DEV) * 0.02)
+    h = rnd(6, H, seed=10)
+    y = ops.moe_routed(h, w, i, {"w13": w13, "s13": s13, "w2": w2, "s2": s2}, 0, E)
+    torch.cuda.synchronize()
+    assert torch.isfinite(y.float()).all() and y[2].abs().sum() == 0 and y[4].abs().sum() == 0
+    status_ok()
