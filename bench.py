@@ -36,7 +36,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "p95 TTFT turns>=2 (ms), multi-turn chat"
-BASELINE_MS = None  # BASELINE.md publishes no like-for-like B200 number for this workload
+BASELINE_MS = None  # the reference publishes no like-for-like B200 number for this workload
 
 
 def parse():
@@ -64,8 +64,8 @@ def reference_unavailable(args) -> None:
     rank = int(os.environ.get("RANK", "0"))
     if rank == 0:
         print(json.dumps({"impl": "reference", "unavailable":
-                          "the reference tree has no setup.py/pyproject.toml, so `pip install --target "
-                          "baseline/_ref /root/reference` fails (not installable)"}))
+                          "the reference tree has no setup.py/pyproject.toml, so installing it with pip "
+                          "into baseline/_ref fails (not installable)"}))
 
 
 class ClockSampler:
