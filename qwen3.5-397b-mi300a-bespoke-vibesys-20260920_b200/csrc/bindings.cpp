@@ -280,7 +280,7 @@ Tensor deltanet_decode(Tensor proj, Tensor conv_state, Tensor conv_w, Tensor a_l
   LAUNCH(qb::deltanet_decode(proj.data_ptr(), proj.stride(0), conv_state.data_ptr(), conv_state.stride(0),
                              conv_w.data_ptr(), a_log.data_ptr<float>(), dt_bias.data_ptr<float>(),
                              state.data_ptr<float>(), state.stride(0), norm_w.data_ptr(), seg_lane.data_ptr<int>(), T,
-                             nk, nv, dk, dv, conv_w.size(1), (float)eps, out.data_ptr(), stream()));
+                             nk, nv, dk, dv, conv_w.size(1), (float)eps, out.data_ptr(), stream(), err_ptr(proj)));
   return out;
 }
 

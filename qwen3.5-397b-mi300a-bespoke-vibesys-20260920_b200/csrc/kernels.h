@@ -56,7 +56,7 @@ long gated_delta_chunked_scratch(int T, int n_chunks, int nk, int nv, int dk);
 // DeltaNet token mixer for one token per lane (conv, l2norm, gated delta step, gated RMSNorm)
 int deltanet_decode(const void* proj, long ldp, void* conv_state, long cls, const void* conv_w, const float* a_log,
                     const float* dt_bias, float* state, long sls, const void* norm_w, const int* seg_lane, int T,
-                    int nk, int nv, int dk, int dv, int K, float eps, void* out, cudaStream_t s);
+                    int nk, int nv, int dk, int dv, int K, float eps, void* out, cudaStream_t s, int* err = nullptr);
 // expert-parallel MoE over peer memory (ep.cu)
 long ep_region_bytes(int world, int cap, int H, int k);
 int ep_dispatch(void* const* bases, int world, int rank, int cap, int H, int k, int experts_per_rank, const void* x,

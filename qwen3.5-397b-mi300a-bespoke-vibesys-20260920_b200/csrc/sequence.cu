@@ -420,9 +420,189 @@ __global__ void __launch_bounds__(256, 2)
   }
 }
 
+template <int DK, int DV>
+__global__ void __launch_bounds__(256, 3)
+    delta_decode_sm_kernel(const bf16* proj, long ldp, bf16* cstate, long cls, const bf16* cw, const float* a_log,
+                        const float* dt_bias, float* state, long sls, const bf16* norm_w, const int* seg_lane, int nk,
+                        int nv, float eps, bf16* out, int* err) {
+  constexpr int K = 4, RPW = DK / 8;
+  static_assert(DV == 128 && DK % 32 == 0, "one float4 of columns per lane");
+  __shared__ float qs[DK], ks[DK], vs[DV], os[DV];
+  __shared__ __align__(16) float red_kv[8][DV];
+  __shared__ __align__(16) float red_o[8][DV];
+  __shared__ float gsh[2];
+  const int h = blockIdx.x, t = blockIdx.y;  // value head, token (one token = one lane's segment)
+  const int lane_id = seg_lane[t];
+  const int warp = threadIdx.x / 32, l = threadIdx.x % 32;
+  const int hk = h / (nv / nk);
+  const bool qk_owner = cluster_ctarank() == 0;  // the cluster is this key head's value heads
+  float* st = state + (long)lane_id * sls + (long)h * DK * DV;
+  // the state [DK][DV] fp32 comes into shared memory by one bulk copy that overlaps the conv
+  extern __shared__ __align__(128) uint8_t dsm[];
+  float4* S4 = reinterpret_cast<float4*>(dsm);
+  __shared__ __align__(8) uint64_t sbar;
+  constexpr uint32_t SBYTES = DK * DV * 4;
+  if (threadIdx.x == 0) {
+    mbar_init(&sbar, 1);
+    fence_barrier_init();
+    mbar_expect_tx(&sbar, SBYTES);
+    bulk_g2s_s(smem_u32(dsm), st, SBYTES, smem_u32(&sbar));
+  }
+
+  const bf16* row = proj + (long)t * ldp;
+  bf16* cs = cstate + (long)lane_id * cls;
+  const int C = 2 * nk * DK + nv * DV;
+  // causal conv (K = 4) of channel c: the K-1 saved inputs then this token, SiLU of the bf16 sum
+  auto conv = [&](int c, bf16 (&win)[K]) -> float {
+    const bf16* sc = cs + (long)c * (K - 1);
+    const bf16* wc = cw + (long)c * K;
+    win[0] = sc[0];
+    win[1] = sc[1];
+    win[2] = sc[2];
+    win[3] = row[c];
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < K; ++j) acc += __bfloat162float(wc[j]) * __bfloat162float(win[j]);
+    const float a = rbf2(acc);
+    return __bfloat162float(__float2bfloat16(a / (1.f + expf(-a))));
+  };
+  bf16 qkwin[DK / 32][K];  // warps 0/1: this lane's q/k channels' windows (written by the owner)
+  bf16 vwin[K];
+  if (warp < 2) {  // l2-normalised q (times dk^-0.5) or k of key head hk
+    const bool isq = warp == 0;
+    const int c0 = (isq ? 0 : nk * DK) + hk * DK;
+    float v[DK / 32], ss = 0.f;
+#pragma unroll
+    for (int m = 0; m < DK / 32; ++m) {
+      v[m] = conv(c0 + l + 32 * m, qkwin[m]);
+      ss += rbf2(v[m] * v[m]);
+    }
+    ss = warp_sum(ss);
+    const float inv = rbf2(rsqrtf(rbf2(rbf2(ss) + 1e-6f)));
+    const float scale = rsqrtf((float)DK);
+#pragma unroll
+    for (int m = 0; m < DK / 32; ++m) {
+      const float y = rbf2(v[m] * inv);
+      if (isq) qs[l + 32 * m] = y * scale; else ks[l + 32 * m] = y;
+    }
+  } else if (warp < 6) {  // v channels of value head h
+    const int j = (warp - 2) * 32 + l;
+    vs[j] = conv(2 * nk * DK + h * DV + j, vwin);
+  } else if (warp == 6 && l == 0) {
+    const float b = __bfloat162float(row[C + nv * DV + h]);
+    const float a = __bfloat162float(row[C + nv * DV + nv + h]);
+    const float g = -expf(a_log[h]) * softplus(a + dt_bias[h]);
+    gsh[0] = expf(g);
+    gsh[1] = rbf2(1.f / (1.f + expf(-b)));
+  }
+  cluster_arrive_release();  // this CTA has read the shared q/k windows
+  __syncthreads();  // also makes the barrier's initialisation visible before anyone waits on it
+  const bool have = mbar_wait(&sbar, 0, err, ERR_TMA_WAIT, nullptr);  // the state has arrived
+  const float decay = gsh[0], beta = gsh[1];
+  // kv = S^T k over this warp's rows, then across warps
+  float4 kp = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const float k = ks[warp + 8 * r];
+    const float4 sv = S4[(warp + 8 * r) * (DV / 4) + l];
+    kp.x += sv.x * k;
+    kp.y += sv.y * k;
+    kp.z += sv.z * k;
+    kp.w += sv.w * k;
+  }
+  *reinterpret_cast<float4*>(&red_kv[warp][4 * l]) = kp;
+  __syncthreads();
+  float4 kv = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int w = 0; w < 8; ++w) {
+    const float4 p = *reinterpret_cast<const float4*>(&red_kv[w][4 * l]);
+    kv.x += p.x;
+    kv.y += p.y;
+    kv.z += p.z;
+    kv.w += p.w;
+  }
+  const float4 vv = *reinterpret_cast<const float4*>(&vs[4 * l]);
+  const float4 dl = make_float4((vv.x - decay * kv.x) * beta, (vv.y - decay * kv.y) * beta,
+                                (vv.z - decay * kv.z) * beta, (vv.w - decay * kv.w) * beta);
+  float4 op = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+  for (int r = 0; r < RPW; ++r) {
+    const float k = ks[warp + 8 * r], q = qs[warp + 8 * r];
+    float4 sv = S4[(warp + 8 * r) * (DV / 4) + l];
+    sv.x = sv.x * decay + k * dl.x;
+    sv.y = sv.y * decay + k * dl.y;
+    sv.z = sv.z * decay + k * dl.z;
+    sv.w = sv.w * decay + k * dl.w;
+    S4[(warp + 8 * r) * (DV / 4) + l] = sv;
+    op.x += sv.x * q;
+    op.y += sv.y * q;
+    op.z += sv.z * q;
+    op.w += sv.w * q;
+  }
+  // the updated state goes back by one bulk store (generic-proxy writes made visible to it first)
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  *reinterpret_cast<float4*>(&red_o[warp][4 * l]) = op;
+  __syncthreads();
+  if (threadIdx.x == 0 && have) {
+    asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(st), "r"(smem_u32(dsm)),
+                 "r"(SBYTES)
+                 : "memory");
+    asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+  }
+  if (warp == 0) {
+    float4 o = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int w = 0; w < 8; ++w) {
+      const float4 p = *reinterpret_cast<const float4*>(&red_o[w][4 * l]);
+      o.x += p.x;
+      o.y += p.y;
+      o.z += p.z;
+      o.w += p.w;
+    }
+    os[4 * l] = rbf2(o.x);  // the recurrence's output is bf16
+    os[4 * l + 1] = rbf2(o.y);
+    os[4 * l + 2] = rbf2(o.z);
+    os[4 * l + 3] = rbf2(o.w);
+    __syncwarp();
+    // gated RMSNorm over the head (same order as the separate norm kernel)
+    float ss = 0.f;
+    for (int i = l; i < DV; i += 32) ss += os[i] * os[i];
+    ss = warp_sum(ss);
+    const float inv = rsqrtf(ss / DV + eps);
+    const bf16* zr = row + C + (long)h * DV;
+    bf16* orow = out + ((long)t * nv + h) * DV;
+    for (int i = l; i < DV; i += 32) {
+      float y = rbf2(os[i] * inv);
+      y = rbf2(__bfloat162float(norm_w[i]) * y);
+      const float zz = __bfloat162float(zr[i]);
+      orow[i] = __float2bfloat16(y * (zz / (1.f + expf(-zz))));
+    }
+  }
+  // conv windows shift by this token: v channels by their own head, q/k after every head of the
+  // cluster has read them
+  if (warp >= 2 && warp < 6) {
+    bf16* sc = cs + (long)(2 * nk * DK + h * DV + (warp - 2) * 32 + l) * (K - 1);
+    sc[0] = vwin[1];
+    sc[1] = vwin[2];
+    sc[2] = vwin[3];
+  }
+  if (threadIdx.x == 0 && have) asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
+  cluster_wait_acquire();
+  if (warp < 2 && qk_owner) {
+    const int c0 = (warp == 0 ? 0 : nk * DK) + hk * DK;
+#pragma unroll
+    for (int m = 0; m < DK / 32; ++m) {
+      bf16* sc = cs + (long)(c0 + l + 32 * m) * (K - 1);
+      sc[0] = qkwin[m][1];
+      sc[1] = qkwin[m][2];
+      sc[2] = qkwin[m][3];
+    }
+  }
+}
+
 int deltanet_decode(const void* proj, long ldp, void* conv_state, long cls, const void* conv_w, const float* a_log,
                     const float* dt_bias, float* state, long sls, const void* norm_w, const int* seg_lane, int T,
-                    int nk, int nv, int dk, int dv, int K, float eps, void* out, cudaStream_t s) {
+                    int nk, int nv, int dk, int dv, int K, float eps, void* out, cudaStream_t s, int* err) {
   if (!T) return 0;
   const int rep = nk > 0 ? nv / nk : 0;
   if (dk != 128 || dv != 128 || K != 4 || rep < 1 || rep > 8 || nv % nk) return -1;
@@ -437,6 +617,23 @@ int deltanet_decode(const void* proj, long ldp, void* conv_state, long cls, cons
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  // state path: shared memory by bulk copies from 16 lanes up (3 CTAs per SM keep more state in
+  // flight: 0.070 vs 0.079 ms at 32 lanes), registers below (fewer CTAs than slots: the register
+  // form's shorter per-CTA latency wins, 0.024 vs 0.027 ms at 8 lanes); QB_DN_DECODE=reg|sm forces
+  static const char* mode = getenv("QB_DN_DECODE");
+  const bool sm = mode && mode[0] ? mode[0] == 's' : T >= 16;
+  if (sm) {
+    auto k = delta_decode_sm_kernel<128, 128>;
+    static bool attr_set = false;
+    if (!attr_set) {
+      cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, 128 * 128 * 4);
+      attr_set = true;
+    }
+    cfg.dynamicSmemBytes = 128 * 128 * 4;
+    return (int)cudaLaunchKernelEx(&cfg, k, (const bf16*)proj, ldp, (bf16*)conv_state, cls, (const bf16*)conv_w,
+                                   a_log, dt_bias, state, sls, (const bf16*)norm_w, seg_lane, nk, nv, eps,
+                                   (bf16*)out, err);
+  }
   return (int)cudaLaunchKernelEx(&cfg, delta_decode_kernel<128, 128>, (const bf16*)proj, ldp, (bf16*)conv_state, cls,
                                  (const bf16*)conv_w, a_log, dt_bias, state, sls, (const bf16*)norm_w, seg_lane, nk,
                                  nv, eps, (bf16*)out);

@@ -51,6 +51,8 @@ _def("QB_FA", bool, True, "tcgen05 flash attention for full-attention layers (el
      lockstep=True)
 _def("QB_FA_SPLITS", int, 0, "flash attention: key-range splits per tile (0: enough CTAs for one wave)",
      lockstep=True)
+_def("QB_DN_DECODE", str, "", "DeltaNet decode mixer state path: reg (registers), sm (shared memory by bulk copies); "
+     "empty: sm from 16 lanes up", native=True)
 _def("QB_DN_CHUNKED", bool, False, "chunked (WY) DeltaNet prefill instead of the token recurrence",
      lockstep=True)
 _def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
