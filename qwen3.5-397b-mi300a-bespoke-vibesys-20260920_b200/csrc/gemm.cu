@@ -50,6 +50,8 @@ struct GemmArgs {
   int T, N, K;
   int act;  // 0: none, 1: silu(g)*u over row pairs (g rows [0,64), u rows [64,128) of each tile)
   int* err;
+  int bn;      // token columns per tile actually used (<= BN, a multiple of 16): prefill token
+               // counts are split evenly over the tiles instead of filling all but the last
   int ctas;    // stream-K: CTAs sharing the (tile, K-block) space (0: whole tiles per CTA)
   float* ws;   // stream-K: [ctas][2][128][BN] fp32 partials (a CTA's first and last segment)
   int* cnt;    // stream-K: [tiles] arrival counters, zero between calls
@@ -113,7 +115,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_tiles = (a.N + 127) / 128;
-  const int t_tiles = (a.T + BN - 1) / BN;
+  const int t_tiles = (a.T + a.bn - 1) / a.bn;
   const int tiles = n_tiles * t_tiles;
   const int kblocks = (a.K + BK - 1) / BK;
 
@@ -154,7 +156,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       int s = 0;
       uint32_t ph = 1;  // a first-round stage waits on the parity that passes at once
       while (!*abort_flag && sg.next(tile, k0, k1)) {
-        const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
+        const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * a.bn;
         bool ok = true;
         for (int kx = k0 * BK; kx < k1 * BK; kx += BK, ++it) {
           if (!mbar_wait_s(empty0 + 8 * s, ph, a.err, ERR_TMA_WAIT, abort_flag)) {
@@ -162,7 +164,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             break;
           }
           const uint32_t st = st0 + s * C::STAGE, fb = full0 + 8 * s;
-          mbar_expect_tx_s(fb, C::STAGE);
+          mbar_expect_tx_s(fb, C::A_BYTES + a.bn * BK * 2);
           tma_load_2d_s(st, &tmW, fb, kx, n0);
           tma_load_2d_s(st + C::A_BYTES, &tmX, fb, kx, t0);
           *issued_p = it + 1;
@@ -239,7 +241,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int idx = et; idx < CH * 64; idx += 128) {
           const int j = idx / 64, r = idx % 64;
           const int t = t0 + c0 + j, n = n0 / 2 + r;
-          if (t < a.T && n < a.N / 2) {
+          if (t < a.T && c0 + j < a.bn && n < a.N / 2) {
             uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
             float g = to_f<OutT>(*reinterpret_cast<OutT*>(&gb)), u = to_f<OutT>(*reinterpret_cast<OutT*>(&ub));
             Y[(long)t * a.ldy + n] = from_f<OutT>(silu(g) * u);
@@ -250,7 +252,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int idx = et; idx < CH * 16; idx += 128) {
           const int j = idx / 16, q = idx % 16;
           const int t = t0 + c0 + j, n = n0 + q * 8;
-          if (t < a.T) {
+          if (t < a.T && c0 + j < a.bn) {
             const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
             OutT* dst = Y + (long)t * a.ldy + n;
             if (n + 8 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
@@ -270,12 +272,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int first_tile = a.ctas ? (int)(sg.pos / kblocks) : -1;  // tile of this CTA's first segment
     int tile, k0, k1;
     for (; sg.next(tile, k0, k1); ++ti) {
-      const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * BN;
+      const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * a.bn;
       const int acc = ti & 1;
       if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) break;
       tc_fence_after();
       if (k0 == 0 && k1 == kblocks) {  // a whole tile
-        for (int c0 = 0; c0 < BN; c0 += CH) {
+        for (int c0 = 0; c0 < a.bn; c0 += CH) {
           float v[32];
           const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
           if constexpr (CH == 32) tmem_ld32(taddr, v); else tmem_ld16(taddr, v);
@@ -401,10 +403,10 @@ static int launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArg
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr = true;
   }
-  const int tiles = ((a.N + 127) / 128) * ((a.T + BN - 1) / BN);
+  const int tiles = ((a.N + 127) / 128) * ((a.T + a.bn - 1) / a.bn);
   int grid = a.ctas ? a.ctas : tiles < max_ctas ? tiles : max_ctas;
   if (grid < 1) grid = 1;
-  k<<<grid, GEMM_THREADS, C::SMEM, st>>>(tw, tx, a, idesc_f16(128, BN, bf16));
+  k<<<grid, GEMM_THREADS, C::SMEM, st>>>(tw, tx, a, idesc_f16(128, a.bn, bf16));
   return (int)cudaGetLastError();
 }
 
@@ -437,13 +439,19 @@ int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy,
             int act, int* err, cudaStream_t stream, int max_ctas, float* ws, int* cnt) {
   if (T <= 0 || N <= 0) return 0;
   int BN = gemm_bn(T);
+  // the widest tile: the tokens split evenly over its tile count (800 -> 4 x 208, not 3 x 256 + 32)
+  int bn = BN;
+  if (BN == 256) {
+    const int tt = (T + 255) / 256;
+    bn = ((T + tt - 1) / tt + 15) / 16 * 16;
+  }
   CUtensorMap tw, tx;
   int r = make_tmap_2d(&tw, w, 2, N, K, ldw, 128, BK, true);
   if (r) return 1000 + r;
-  r = make_tmap_2d(&tx, x, 2, T, K, ldx, BN, BK, true);
+  r = make_tmap_2d(&tx, x, 2, T, K, ldx, bn, BK, true);
   if (r) return 2000 + r;
   const int ctas = (ws && cnt) ? gemm_streamk_ctas(T, N, K) : 0;
-  GemmArgs a{y, ldy, T, N, K, act, err, ctas, ws, cnt};
+  GemmArgs a{y, ldy, T, N, K, act, err, bn, ctas, ws, cnt};
   if (max_ctas <= 0) max_ctas = num_sms();
   switch (BN) {
     case 16: return bf16 ? launch_bn<16, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)

@@ -35,7 +35,8 @@ def status_ok():
 
 
 @pytest.mark.parametrize("T,N,K", [(1, 128, 64), (7, 200, 256), (16, 384, 4096), (33, 256, 512), (100, 1024, 1024),
-                                   (300, 640, 4096), (1000, 256, 128), (64, 4096, 4096)])
+                                   (300, 640, 4096), (1000, 256, 128), (64, 4096, 4096), (800, 384, 1024),
+                                   (513, 256, 512)])
 def test_linear(T, N, K):
     x = rnd(T, K, scale=1.0, seed=T)
     w = rnd(N, K, scale=0.05, seed=N + K)
