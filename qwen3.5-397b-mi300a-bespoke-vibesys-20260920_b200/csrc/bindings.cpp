@@ -519,6 +519,50 @@ void symm_sp_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor par
                                  (unsigned long long)(timeout_s * 1e9), stream()));
 }
 
+// GEMM -> reduce-scatter + residual add + RMSNorm + all-gather: the row-parallel projection
+// x @ w^T stores its rows straight into the owner ranks' partial slots, then the pushed variant
+// of the sequence-parallel kernel reduces them. Same bits as linear + symm_sp_ar_add_rmsnorm.
+void symm_linear_sp_ar_add_rmsnorm(Tensor x, Tensor w, std::vector<int64_t> bases, int64_t rank, Tensor res,
+                                   Tensor w1p, Tensor out, double eps, int64_t slot_elems, int64_t max_blocks,
+                                   Tensor epoch, double timeout_s) {
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(res);
+  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "symm_linear_sp: shape mismatch");
+  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1 && (x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0,
+              "symm_linear_sp: layouts");
+  TORCH_CHECK(res.is_contiguous() && out.is_contiguous(), "symm_linear_sp: layouts");
+  const int H = res.size(-1);
+  const int rows = res.numel() / H;
+  TORCH_CHECK(w.size(0) == H && x.size(0) == rows, "symm_linear_sp: output is [rows, hidden]");
+  const int world = (int)bases.size();
+  TORCH_CHECK(world >= 1 && world <= 8, "symm_linear_sp: 1..8 ranks");
+  const int per = (rows + world - 1) / world;
+  int* ep = epoch.data_ptr<int>();
+  qb::GemmPush push{};
+  for (int r = 0; r < world; ++r) push.base[r] = reinterpret_cast<void*>(bases[r]);
+  push.world = world;
+  push.rank = (int)rank;
+  push.per = per;
+  push.epoch = ep;
+  push.slot_stride = 3 * slot_elems;  // a slot: partial [rows, H] then results [rows, 2H]
+  TORCH_CHECK((long)per * world * H <= slot_elems, "symm_linear_sp: rows exceed the region");
+  const int T = rows, N = H, K = x.size(1);
+  const long wsf = qb::gemm_split_ws_floats(T, N, K);
+  Tensor ws, cnt;
+  if (wsf) {
+    ws = at::empty({wsf}, x.options().dtype(at::kFloat));
+    cnt = gemm_counters(x, (long)((N + 127) / 128) * ((T + 15) / 16));
+  }
+  LAUNCH(qb::gemm_ws(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), nullptr, N, T, N, K, true, 0, err_ptr(x),
+                     stream(), 0, wsf ? ws.data_ptr<float>() : nullptr, wsf ? cnt.data_ptr<int>() : nullptr, &push));
+  std::vector<void*> b(world);
+  for (int i = 0; i < world; ++i) b[i] = reinterpret_cast<void*>(bases[i]);
+  LAUNCH(qb::symm_sp_rs_add_rmsnorm(b.data(), world, (int)rank, per, res.data_ptr(), w1p.data_ptr<float>(),
+                                    out.data_ptr(), rows, H, (float)eps, slot_elems, (int)max_blocks, ep, ep + 1,
+                                    err_ptr(res), (unsigned long long)(timeout_s * 1e9), stream()));
+}
+
 // ------------------------------------------------------------------ status
 int64_t launches() { return g_launches.load(); }
 // graph replays launch the captured kernels without passing through these bindings
@@ -564,6 +608,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &symm_free);
   m.def("symm_ar_add_rmsnorm", &symm_ar_add_rmsnorm);
   m.def("symm_sp_ar_add_rmsnorm", &symm_sp_ar_add_rmsnorm);
+  m.def("symm_linear_sp_ar_add_rmsnorm", &symm_linear_sp_ar_add_rmsnorm);
   m.def("launches", &launches, "number of kernels launched through the bindings so far");
   m.def("add_launches", &add_launches, "account kernels launched by a CUDA-graph replay");
   m.def("clear_status", &clear_status);

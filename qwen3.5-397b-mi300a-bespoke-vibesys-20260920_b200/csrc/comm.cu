@@ -171,6 +171,10 @@ __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
 //   C. block b waits for flag B[b] of every peer and copies their units' result rows.
 // Same bits as the one-shot kernel (and as NCCL all-reduce + add + RMSNorm); each rank moves
 // about 3 (W-1)/W of the bf16 payload over NVLink instead of (W-1) copies of it.
+// PUSHED: the projection GEMM before this kernel already stored its rows into the owners' slots
+// (gemm.cu, GemmPush): rank o owns rows [o per, (o+1) per), and its partial slot holds rank p's
+// rows of that range at rows p per + (t - o per). Phase A then only publishes (the GEMM's stores
+// completed with that kernel) and phase B sums local rows.
 __device__ __forceinline__ bool wait_peers(const SymmPtrs& ptrs, long flag_off, int b, int e, int* err,
                                            unsigned long long timeout_ns) {
   int ok = 1;
@@ -188,9 +192,11 @@ __device__ __forceinline__ bool wait_peers(const SymmPtrs& ptrs, long flag_off, 
   return __syncthreads_and(ok);
 }
 
+template <bool PUSHED>
 __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
     SymmPtrs ptrs, const bf16* partial, long ldp, bf16* res, const float* w1p, bf16* out, int rows, int H,
-    float eps, long slot_elems, int max_blocks, int* epoch, int* done, int* err, unsigned long long timeout_ns) {
+    float eps, long slot_elems, int max_blocks, int* epoch, int* done, int* err, unsigned long long timeout_ns,
+    int per) {
   __shared__ float red[32];
   __shared__ int s_epoch;
   if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile int*>(epoch) + 1;
@@ -204,8 +210,13 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
   auto part_of = [&](int r) { return reinterpret_cast<bf16*>(ptrs.data[r]) + slot * slot_stride; };
   auto result_of = [&](int r) { return reinterpret_cast<bf16*>(ptrs.data[r]) + slot * slot_stride + slot_elems; };
   auto range = [&](int r, int& r0, int& r1) {
-    r0 = (int)((long)rows * r / W);
-    r1 = (int)((long)rows * (r + 1) / W);
+    if (PUSHED) {
+      r0 = min(rows, r * per);
+      r1 = min(rows, (r + 1) * per);
+    } else {
+      r0 = (int)((long)rows * r / W);
+      r1 = (int)((long)rows * (r + 1) / W);
+    }
   };
   auto publish = [&](long off) {
     __syncthreads();
@@ -216,7 +227,7 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
   };
   // A. stage this block's rows of every owner's range
   bf16* mine = part_of(me);
-  for (int r = 0; r < W; ++r) {
+  for (int r = 0; r < (PUSHED ? 0 : W); ++r) {
     int r0, r1;
     range(r, r0, r1);
     for (int row = r0 + b; row < r1; row += G)
@@ -242,7 +253,9 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
           uint4 raw[8];
 #pragma unroll
           for (int p = 0; p < 8; ++p)
-            if (p < W) raw[p] = __ldcv(reinterpret_cast<const uint4*>(part_of(p) + (long)row * H + i));
+            if (p < W)
+              raw[p] = PUSHED ? __ldcv(reinterpret_cast<const uint4*>(mine + ((long)p * per + row - r0) * H + i))
+                              : __ldcv(reinterpret_cast<const uint4*>(part_of(p) + (long)row * H + i));
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
             if (p < W) {
@@ -332,9 +345,27 @@ int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* 
   int per = (rows + world - 1) / world;  // rows of one rank's range: one block per row, up to max_blocks
   int grid = per < max_blocks ? per : max_blocks;
   if (grid < 1) grid = 1;
-  sp_ar_add_rmsnorm_kernel<<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res, w1p, (bf16*)out,
-                                                       rows, H, eps, slot_elems, max_blocks, epoch, done, err,
-                                                       timeout_ns);
+  sp_ar_add_rmsnorm_kernel<false><<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res, w1p,
+                                                              (bf16*)out, rows, H, eps, slot_elems, max_blocks,
+                                                              epoch, done, err, timeout_ns, 0);
+  return (int)cudaGetLastError();
+}
+
+int symm_sp_rs_add_rmsnorm(void* const* bases, int world, int rank, int per, void* res, const float* w1p, void* out,
+                           int rows, int H, float eps, long slot_elems, int max_blocks, int* epoch, int* done,
+                           int* err, unsigned long long timeout_ns, cudaStream_t s) {
+  if (world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || per < 1 || (long)per * world < rows ||
+      (long)per * world * H > slot_elems)
+    return -1;
+  SymmPtrs p{};
+  for (int r = 0; r < world; ++r) p.data[r] = bases[r];
+  p.world = world;
+  p.rank = rank;
+  int grid = per < max_blocks ? per : max_blocks;
+  if (grid < 1) grid = 1;
+  sp_ar_add_rmsnorm_kernel<true><<<grid, AR_THREADS, 0, s>>>(p, nullptr, 0, (bf16*)res, w1p, (bf16*)out, rows, H,
+                                                             eps, slot_elems, max_blocks, epoch, done, err,
+                                                             timeout_ns, per);
   return (int)cudaGetLastError();
 }
 

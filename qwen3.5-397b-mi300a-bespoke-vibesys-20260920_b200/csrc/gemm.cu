@@ -20,6 +20,13 @@
 // that arrives last adds the tile's partials (a handful, loaded two at a time) and runs the
 // normal epilogue, then re-arms the counter. Segments in between cover whole tiles and take the
 // normal epilogue directly.
+//
+// GEMM -> reduce-scatter (``push``): for a row-parallel projection followed by the
+// sequence-parallel all-reduce, the epilogue stores each output row straight into the symmetric
+// region of the rank that owns the row (rows [o per, (o+1) per) belong to rank o), at row
+// rank * per + (t - o per) of the owner's partial slot; the slot is (device epoch + 1) & 1, read
+// at entry. The transfer over NVLink thus runs tile by tile under the MMAs of the next tiles,
+// and the reduce kernel that follows (comm.cu) reads only local memory.
 #include "common.cuh"
 #include "kernels.h"
 #include <cudaTypedefs.h>
@@ -55,6 +62,7 @@ struct GemmArgs {
   int ctas;    // stream-K: CTAs sharing the (tile, K-block) space (0: whole tiles per CTA)
   float* ws;   // stream-K: [ctas][2][128][BN] fp32 partials (a CTA's first and last segment)
   int* cnt;    // stream-K: [tiles] arrival counters, zero between calls
+  GemmPush push;  // push.world > 0: rows go to the owner ranks' slots instead of y
 };
 
 // The sequence of (tile, K-block range) segments one CTA works through, identical for its
@@ -226,6 +234,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int row = ew * 32 + lane;      // accumulator row = weight row within the tile
     const int et = threadIdx.x - 64;     // 0..127
     OutT* Y = reinterpret_cast<OutT*>(a.y);
+    const bool push = a.push.world > 0;
+    const long push_off = push ? (long)((*reinterpret_cast<volatile const int*>(a.push.epoch) + 1) & 1) *
+                                     a.push.slot_stride : 0;
     constexpr int CH = BN < 32 ? BN : 32;
     // stage one chunk of CH token columns (fp32 values of this thread's weight row) and store it
     auto emit = [&](int n0, int t0, int c0, const float* v) {
@@ -254,7 +265,14 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           const int t = t0 + c0 + j, n = n0 + q * 8;
           if (t < a.T && c0 + j < a.bn) {
             const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
-            OutT* dst = Y + (long)t * a.ldy + n;
+            OutT* dst;
+            if (push) {
+              const int o = t / a.push.per;
+              dst = reinterpret_cast<OutT*>(a.push.base[o]) + push_off +
+                    (long)(a.push.rank * a.push.per + t - o * a.push.per) * a.ldy + n;
+            } else {
+              dst = Y + (long)t * a.ldy + n;
+            }
             if (n + 8 <= a.N && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0)) {
               *reinterpret_cast<uint4*>(dst) = val;
             } else {
@@ -436,8 +454,9 @@ long gemm_split_ws_floats(int T, int N, int K) {
 }
 
 int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
-            int act, int* err, cudaStream_t stream, int max_ctas, float* ws, int* cnt) {
+            int act, int* err, cudaStream_t stream, int max_ctas, float* ws, int* cnt, const GemmPush* push) {
   if (T <= 0 || N <= 0) return 0;
+  if (push && (act || push->world < 1 || push->world > 8 || push->per < 1 || ldy != N)) return -1;
   int BN = gemm_bn(T);
   // the widest tile: the tokens split evenly over its tile count (800 -> 4 x 208, not 3 x 256 + 32)
   int bn = BN;
@@ -451,7 +470,7 @@ int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy,
   r = make_tmap_2d(&tx, x, 2, T, K, ldx, bn, BK, true);
   if (r) return 2000 + r;
   const int ctas = (ws && cnt) ? gemm_streamk_ctas(T, N, K) : 0;
-  GemmArgs a{y, ldy, T, N, K, act, err, bn, ctas, ws, cnt};
+  GemmArgs a{y, ldy, T, N, K, act, err, bn, ctas, ws, cnt, push ? *push : GemmPush{}};
   if (max_ctas <= 0) max_ctas = num_sms();
   switch (BN) {
     case 16: return bf16 ? launch_bn<16, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)

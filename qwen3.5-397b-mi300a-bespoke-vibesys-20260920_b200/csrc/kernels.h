@@ -14,9 +14,20 @@ enum DType : int { DT_BF16 = 0, DT_F16 = 1, DT_F32 = 2 };
 int make_tmap_2d(CUtensorMap* map, const void* base, int elem_bytes, long rows, long cols, long ld_elems,
                  int box_rows, int box_cols, bool swizzle128);
 
-// Y[T,N] = X[T,K] @ W[N,K]^T ; act 1 = silu(gate)*up over 64-row halves of each 128-row tile
+// GEMM -> reduce-scatter target: every rank's symmetric sequence-parallel region (comm.cu layout)
+struct GemmPush {
+  void* base[8];       // region bases as mapped on this rank (own entry local)
+  int world, rank;     // world == 0: no push
+  int per;             // rows owned per rank (the last rank may own fewer)
+  const int* epoch;    // the reduce kernel's device epoch; the slot is (epoch + 1) & 1
+  long slot_stride;    // elements per slot of a region
+};
+
+// Y[T,N] = X[T,K] @ W[N,K]^T ; act 1 = silu(gate)*up over 64-row halves of each 128-row tile;
+// with `push`, row t is stored into the owner rank's partial slot instead of Y (ldy must be N)
 int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
-            int act, int* err, cudaStream_t stream, int max_ctas = 0, float* ws = nullptr, int* cnt = nullptr);
+            int act, int* err, cudaStream_t stream, int max_ctas = 0, float* ws = nullptr, int* cnt = nullptr,
+            const GemmPush* push = nullptr);
 // stream-K workspace (fp32 floats; 0 = whole tiles per CTA) and CTA count; counters: one per tile
 long gemm_split_ws_floats(int T, int N, int K);
 int gemm_streamk_ctas(int T, int N, int K);
@@ -117,5 +128,9 @@ int symm_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* par
 int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                         const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
                         int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s);
+// the same after a GEMM that pushed its rows into the owners' slots (GemmPush, per rows a rank)
+int symm_sp_rs_add_rmsnorm(void* const* bases, int world, int rank, int per, void* res, const float* w1p, void* out,
+                           int rows, int H, float eps, long slot_elems, int max_blocks, int* epoch, int* done,
+                           int* err, unsigned long long timeout_ns, cudaStream_t s);
 
 }  // namespace qb

@@ -16,7 +16,7 @@ Per-layer dataflow (``Model._forward``), with the TP collective fused into the n
     x = embed(tokens); h = rmsnorm(x, in_norm[0])
     for each layer:
         partial = deltanet(h) | gated_attention(h)        # row-parallel partial sums
-        x, h = allreduce_add_rmsnorm(partial, x, post_norm)
+        x, h = allreduce_add_rmsnorm(partial, x, post_norm)   # prefill: out_proj GEMM fused in
         partial = moe(h)                                   # EP experts + TP shared expert
         x, h = allreduce_add_rmsnorm(partial, x, next in_norm | final_norm)
     logits = lm_head(h[logit rows])                        # vocab parallel, all-gathered
@@ -41,6 +41,14 @@ from ..parallel.plan import Plan
 from .config import FULL, Qwen35Config
 
 RESERVED_BLOCK = 0
+
+
+@dataclass
+class _Deferred:
+    """A mixer's output projection not yet run: ``x @ w^T`` is fused into the all-reduce."""
+
+    x: torch.Tensor
+    w: torch.Tensor
 
 
 @dataclass
@@ -117,6 +125,7 @@ class Model:
         self._d2h = 0  # bytes read back device -> host (sampled ids)
         self.gpu_marks = None  # list -> CUDA events at each input upload ("in") and result read ("out")
         self.stamps = None  # utils.telemetry.Stamps -> in-graph clock stamps at layer boundaries
+        self._defer_out = False  # set inside _layers while the out projections fuse into the all-reduce
 
     def _gpu_mark(self, tag: str) -> None:
         """Stream-ordered event where a step's device work starts (input upload) or ends (the
@@ -271,7 +280,7 @@ class Model:
                                          self.rec_state[j], L["norm_w"], b.seg_lane, nk, nv, dk, dv, cfg.eps,
                                          b.seg_lane_h)
             self._dstamp("dn.decode_mixer")
-            return ops.linear(normed, L["w_out"])
+            return self._out_proj(normed, L["w_out"])
         commit = not b.verify
         if b.verify:  # keep the per-row inputs: the accepted prefix is committed later
             self._vsave[j] = (proj[:, :c].clone(), proj[:, c + nv * dv:].clone())
@@ -288,13 +297,14 @@ class Model:
         else:
             normed = ops.gated_rmsnorm(core, z.reshape(-1, nv, dv), L["norm_w"], cfg.eps).reshape(-1, nv * dv)
         self._dstamp("dn.gated_norm")
-        return ops.linear(normed, L["w_out"])
+        return self._out_proj(normed, L["w_out"])
 
     def _attention(self, i: int, L: dict, h: torch.Tensor, b: StepInputs) -> torch.Tensor:
         j = self.full_slot[i]
-        return self._attention_core(L, h, b, self.k_cache[j], self.v_cache[j])
+        return self._attention_core(L, h, b, self.k_cache[j], self.v_cache[j], j)
 
-    def _attention_core(self, L: dict, h: torch.Tensor, b: StepInputs, k_cache, v_cache) -> torch.Tensor:
+    def _attention_core(self, L: dict, h: torch.Tensor, b: StepInputs, k_cache, v_cache,
+                        j: int | None = None) -> torch.Tensor:
         cfg = self.cfg
         hd, nq, nkv = cfg.head_dim, self.nq, self.nkv
         qkv = ops.linear(h, L["w_qkv"])
@@ -307,14 +317,27 @@ class Model:
         theta = float(self.fault.get("rope_base", cfg.rope_theta))
         q = ops.qk_norm_rope_kv_write(q, k, v, L["q_norm"], L["k_norm"], b.positions, b.rows,
                                       k_cache, v_cache, cfg.rotary_dim, theta, cfg.eps)
+        if j is not None and self.fault.get("fp8_kv_no_scale"):
+            rows = b.rows.long()  # the rows just written, truncated through e4m3 without a scale
+            k_cache[rows] = k_cache[rows].to(torch.float8_e4m3fn).to(k_cache.dtype)
+            v_cache[rows] = v_cache[rows].to(torch.float8_e4m3fn).to(v_cache.dtype)
         self._dstamp("attn.norm_rope_kv")
         o = ops.attention_varlen(q, k_cache, v_cache, self.table_dev, b.seg_lane, b.cu,
                                  b.seg_start, self.block_size, b.seg_lane_h, b.cu_h, b.seg_start_h,
-                                 self.tables if h.device.type == "cpu" else None, b.positions, b.max_ctx)
+                                 self.tables if h.device.type == "cpu" else None, b.positions, b.max_ctx,
+                                 causal=not (j is not None and self.fault.get("flip_causal_mask")
+                                             and j == int(self.fault.get("flip_causal_mask_layer", 0))))
         self._dstamp("attn.core")
         o = ops.sigmoid_gate_mul(o.reshape(t, nq * hd), gate.reshape(t, nq * hd))
         self._dstamp("attn.gate")
-        return ops.linear(o, L["w_o"])
+        return self._out_proj(o, L["w_o"])
+
+    def _out_proj(self, x: torch.Tensor, w: torch.Tensor):
+        """The mixer's row-parallel output projection, or (x, w) left for the all-reduce that
+        follows when it fuses the two (GEMM -> reduce-scatter over peer memory)."""
+        if self._defer_out:
+            return _Deferred(x, w)
+        return ops.linear(x, w)
 
     def _moe(self, L: dict, h: torch.Tensor) -> torch.Tensor:
         cfg, p = self.cfg, self.plan
@@ -341,11 +364,19 @@ class Model:
         cfg, comm, layers = self.cfg, self.comm, self.w["layers"]
         h = ops.rmsnorm(x, layers[0]["in_norm"], cfg.eps)
         self._stamp("embed")
+        fuse_out = hasattr(comm, "fuses_linear") and comm.fuses_linear(x.shape[0])
         for i, L in enumerate(layers):
             full = L["kind"] == FULL
-            mix = self._attention(i, L, h, b) if full else self._deltanet(i, L, h, b)
+            self._defer_out = fuse_out
+            try:
+                mix = self._attention(i, L, h, b) if full else self._deltanet(i, L, h, b)
+            finally:
+                self._defer_out = False
             self._stamp("attention" if full else "deltanet")
-            x, h = comm.allreduce_add_rmsnorm(mix, x, L["post_norm"], cfg.eps)
+            if isinstance(mix, _Deferred):
+                x, h = comm.linear_allreduce_add_rmsnorm(mix.x, mix.w, x, L["post_norm"], cfg.eps)
+            else:
+                x, h = comm.allreduce_add_rmsnorm(mix, x, L["post_norm"], cfg.eps)
             self._stamp("allreduce")
             m = self._moe(L, h)
             self._stamp("moe")

@@ -184,11 +184,14 @@ def qk_norm_rope_kv_write(q, k, v, q_norm, k_norm, positions, rows, k_cache, v_c
 
 
 def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, block_size,
-                     seg_lane_h=None, cu_h=None, seg_start_h=None, tables_h=None, positions=None, max_ctx=None):
+                     seg_lane_h=None, cu_h=None, seg_start_h=None, tables_h=None, positions=None, max_ctx=None,
+                     causal=True):
     """Causal GQA attention of each segment's queries over its lane's paged context
     ``[0, seg_start + len)``. ``q`` [T, Hq, D]; caches [rows, Hkv, D]. Returns [T, Hq, D].
-    On CUDA ``positions`` ([T] absolute positions) and ``max_ctx`` (longest context) are used."""
-    if _cuda(q):
+    On CUDA ``positions`` ([T] absolute positions) and ``max_ctx`` (longest context) are used.
+    ``causal=False`` (the ``flip_causal_mask`` calibration fault) runs the PyTorch form with every
+    key of the segment's context visible."""
+    if _cuda(q) and causal:
         plan = fa_plan(q, k_cache, cu_h, block_size, max_ctx)
         if plan is not None:
             tiles, splits = plan
@@ -209,7 +212,7 @@ def attention_varlen(q, k_cache, v_cache, block_table, seg_lane, cu, seg_start, 
         nb = (n + block_size - 1) // block_size
         rows = torch.tensor([blk * block_size + o for blk in blocks[:nb] for o in range(block_size)][:n],
                             dtype=torch.long, device=q.device)
-        out[a:b] = ref.attention_prefix(q[a:b], k_cache[rows], v_cache[rows], starts[s])
+        out[a:b] = ref.attention_prefix(q[a:b], k_cache[rows], v_cache[rows], starts[s], causal)
     return out
 
 

@@ -78,7 +78,8 @@ def apply_partial_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) ->
 
 
 # ----------------------------------------------------------------------------- attention
-def attention_prefix(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_start: int) -> torch.Tensor:
+def attention_prefix(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_start: int,
+                     causal: bool = True) -> torch.Tensor:
     """Causal GQA attention of ``q`` [Tq, Hq, D] at positions ``q_start..`` over ``k``/``v``
     [Tk, Hkv, D] at positions ``0..Tk-1`` (``Tk == q_start + Tq``). Softmax in fp32; the
     probabilities are rounded to the input dtype before the value product (HF eager path)."""
@@ -90,7 +91,8 @@ def attention_prefix(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_start:
     s = torch.einsum("qhd,khd->hqk", q.float(), kk.float()) / math.sqrt(d)
     qpos = torch.arange(q_start, q_start + tq, device=q.device)[:, None]
     kpos = torch.arange(tk, device=q.device)[None, :]
-    s = s.masked_fill((kpos > qpos)[None], float("-inf"))
+    if causal:  # (False: every key of the context visible, a calibration fault)
+        s = s.masked_fill((kpos > qpos)[None], float("-inf"))
     p = torch.softmax(s, dim=-1).to(q.dtype)
     return torch.einsum("hqk,khd->qhd", p.float(), vv.float()).to(q.dtype)
 

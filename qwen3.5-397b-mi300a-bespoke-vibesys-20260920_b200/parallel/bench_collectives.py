@@ -17,6 +17,13 @@ memory, ``parallel.ep``) at the full geometry (512 experts top-10, hidden 4096, 
 model uses (NCCL all-gather of the tokens, every rank's experts on all tokens, NCCL reduce-scatter
 of the partial sums). Roofline of a call: the slower of this rank's active expert weights over
 HBM (measured copy bandwidth) and its dispatch + combine bytes over NVLink (770 GB/s).
+
+``--case sp_gemm``: the prefill out-projection (o_proj, K = 8192 / N per rank) with its
+all-reduce + residual + RMSNorm: the fused GEMM -> reduce-scatter (the GEMM epilogue stores rows
+into their owners' symmetric slots, then the sequence-parallel kernel reduces and gathers)
+against the GEMM followed by the sequence-parallel kernel and by NCCL. Roofline of a call: the
+slower of the GEMM's FLOPs at the measured bf16 peak and the 3 (N-1)/N x message bytes every GPU
+takes in over NVLink (partials, then the result rows) at 770 GB/s.
 """
 
 from __future__ import annotations
@@ -103,12 +110,66 @@ def ep_sweep(args, rank, world, dev) -> list[dict]:
     return rows
 
 
+def sp_gemm_sweep(args, rank, world, dev) -> list[dict]:
+    from ..ops import core as ops
+    from ..ops.kbench import peaks
+    from .symm import SymmComm
+
+    H, K = args.hidden, 8192 // world
+    tokens = [t for t in args.tokens if t % world == 0]
+    symm = SymmComm(rank, world, dev, max_rows=512, hidden=H, sp_rows=max(tokens))
+    g = torch.Generator(device=dev).manual_seed(5 + rank)
+    wo = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
+    w = torch.ones(H, device=dev)
+    tflops = peaks()["bf16_tflops"]
+    rows = []
+    for T in tokens:
+        x = torch.randn(T, K, device=dev, generator=g).bfloat16()
+        res = torch.zeros(T, H, device=dev).bfloat16()
+
+        def fused():
+            symm.linear_allreduce_add_rmsnorm(x, wo, res, w, 1e-6)
+
+        def gemm_sp():
+            symm.allreduce_add_rmsnorm(ops.linear(x, wo), res, w, 1e-6, kind="sp")
+
+        def gemm_nccl():
+            y = ops.linear(x, wo).float()
+            dist.all_reduce(y)
+            ops.add_rmsnorm(y.bfloat16(), res, w, 1e-6)
+
+        def gemm():
+            ops.linear(x, wo)
+
+        out = {"case": "sp_gemm", "tokens": T, "K": K, "n_gpus": world, "fused_path": symm.fuses_linear(T)}
+        for name, fn in (("fused", fused), ("gemm_sp", gemm_sp), ("gemm_nccl", gemm_nccl), ("gemm_only", gemm)):
+            for _ in range(5):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(args.ep_iters):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            us = torch.tensor([s.elapsed_time(e) * 1e3 / args.ep_iters], device=dev)
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+            out[name + "_us"] = round(us.item(), 1)
+        link_bytes = 3 * (world - 1) / world * T * H * 2
+        roof_us = max(2 * T * H * K / (tflops * 1e6), link_bytes / (PEER_GBS * 1e3))
+        out.update(roofline_us=round(roof_us, 1), fused_frac_of_roofline=round(roof_us / out["fused_us"], 3))
+        rows.append(out)
+    symm.close()
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, nargs="*", default=[1, 4, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096])
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--hidden", type=int, default=4096)
-    ap.add_argument("--case", default="allreduce", choices=["allreduce", "ep"])
+    ap.add_argument("--case", default="allreduce", choices=["allreduce", "ep", "sp_gemm"])
     ap.add_argument("--ep-iters", type=int, default=20)
     args = ap.parse_args()
     from ..ops import core as ops
@@ -117,10 +178,10 @@ def main():
 
     rank, world = commmod.init("nccl")
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
-    if args.case == "ep":
+    if args.case in ("ep", "sp_gemm"):
         if args.tokens == ap.get_default("tokens"):
-            args.tokens = [8, 64, 512, 2048, 8192]
-        rows = ep_sweep(args, rank, world, dev)
+            args.tokens = [8, 64, 512, 2048, 8192] if args.case == "ep" else [1024, 2048, 4096, 8192, 16384]
+        rows = (ep_sweep if args.case == "ep" else sp_gemm_sweep)(args, rank, world, dev)
         if rank == 0:
             for r in rows:
                 print(json.dumps(r))

@@ -68,6 +68,7 @@ class Comm:
         self.device = device
         self.symm = symm  # parallel.symm.SymmComm for the fused CUDA kernels, or None
         self.mode = flags.get("QB_COMM")
+        self.sp_gemm = flags.get("QB_SP_GEMM")
 
     # ------------------------------------------------------------------ primitives
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
@@ -110,6 +111,21 @@ class Comm:
                 return got
         summed = self.all_reduce(partial)
         return ops.add_rmsnorm(summed, residual, w1p, eps)
+
+    def fuses_linear(self, rows: int) -> bool:
+        """True when ``linear_allreduce_add_rmsnorm`` runs the projection and the all-reduce as
+        the fused GEMM -> reduce-scatter pair (multi-rank, fused comm, prefill-sized rows)."""
+        return (self.world > 1 and self.symm is not None and self.mode == "fused" and self.sp_gemm
+                and str(self.device).startswith("cuda") and self.symm.fuses_linear(rows))
+
+    def linear_allreduce_add_rmsnorm(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
+                                     w1p: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
+        """``residual + sum_ranks(x @ w^T)`` and its RMSNorm, for a row-parallel projection."""
+        if x.is_cuda and self.fuses_linear(residual.numel() // residual.shape[-1]):
+            got = self.symm.linear_allreduce_add_rmsnorm(x, w, residual, w1p, eps)
+            if got is not None:
+                return got
+        return self.allreduce_add_rmsnorm(ops.linear(x, w), residual, w1p, eps)
 
     def argmax_gather(self, local_logits: torch.Tensor, vocab_start: int) -> torch.Tensor:
         """Greedy token ids [B] over vocab-parallel logits (ties: lowest global index)."""

@@ -117,6 +117,29 @@ class SymmComm:
                                   self.max_blocks, self.epoch, self.timeout_s)
         return residual, normed
 
+    def fuses_linear(self, rows: int) -> bool:
+        """Whether ``linear_allreduce_add_rmsnorm`` takes the fused GEMM -> reduce-scatter path
+        for ``rows`` (the sizes the sequence-parallel kernel takes, with the owners' ranges of
+        ceil(rows / world) rows fitting the region)."""
+        if self.sp_bases is None or rows < 1:
+            return False
+        per = -(-rows // self.world)
+        return per * self.world <= self.sp_rows and (rows > self.max_rows
+                                                     or rows * (self.world - 1) > self.ONESHOT_ROW_BUDGET)
+
+    def linear_allreduce_add_rmsnorm(self, x, w, residual, w1p, eps):
+        """``residual += sum_ranks(x @ w^T)`` (in place) and returns (residual, rmsnorm(residual)):
+        the projection's epilogue stores every row into the symmetric region of the rank that owns
+        it, then the sequence-parallel kernel reduces, normalises and gathers. None when
+        ``fuses_linear`` is false (the caller runs the projection and the all-reduce apart)."""
+        rows = residual.numel() // residual.shape[-1]
+        if not self.fuses_linear(rows):
+            return None
+        normed = torch.empty_like(residual)
+        ext().symm_linear_sp_ar_add_rmsnorm(x, w, self.sp_bases, self.rank, residual, w1p, normed, float(eps),
+                                            self.sp_slot_elems, SP_MAX_BLOCKS, self.sp_epoch, self.timeout_s)
+        return residual, normed
+
     def close(self) -> None:
         for p in self.opened:
             ext().symm_close(p)

@@ -266,7 +266,7 @@ class GraphRunner:
         m = self.model
         n = len(lanes)
         B = next((b for b in sorted(self._spec) if b >= n), None)
-        if B is None:
+        if B is None or m.fault:  # a calibration fault acts on the eager path only
             return m.speculative_decode(lanes, tokens, positions, budgets, stops)
         bk, mtp, k = self._spec[B], m.mtp, m.mtp.k
         with torch.inference_mode():
@@ -345,7 +345,7 @@ class GraphRunner:
     def decode(self, lanes, tokens, positions):
         n = len(lanes)
         B = next((b for b in self.buckets if b >= n), None)
-        if not self._b or B is None or B not in self._b or self.model.mtp is not None:
+        if not self._b or B is None or B not in self._b or self.model.mtp is not None or self.model.fault:
             return self.model.decode(lanes, tokens, positions)
         bk = self._b[B]
         with torch.inference_mode():

@@ -41,6 +41,20 @@ def main(rank, world, port):
         torch.cuda.synchronize()
         assert torch.equal(r1, r2), (it, (r1.float() - r2.float()).abs().max().item())
         assert (n1.float() - n2.float()).abs().max().item() < 1e-2 * n2.float().abs().max().item() + 1e-3
+    # the projection fused in (GEMM -> reduce-scatter over peer memory): same bits as the
+    # projection followed by the sequence-parallel kernel, over consecutive calls of both kinds
+    K = 1024
+    wo = (torch.randn(H, K, device=dev, generator=g) * 0.02).bfloat16()
+    for it, rows in enumerate((1000, 2047, 513, 2048, 1001)):
+        assert s.fuses_linear(rows), rows
+        xo = torch.randn(rows, K, device=dev, generator=g).bfloat16()
+        base = torch.randn(rows, H, device=dev, generator=torch.Generator(device=dev).manual_seed(50 + it)).bfloat16()
+        r1, n1 = s.linear_allreduce_add_rmsnorm(xo, wo, base.clone(), w, 1e-6)
+        r2, n2 = s.allreduce_add_rmsnorm(ops.linear(xo, wo), base.clone(), w, 1e-6, kind="sp")
+        torch.cuda.synchronize()
+        assert torch.equal(r1, r2), (rows, (r1.float() - r2.float()).abs().max().item())
+        assert torch.equal(n1, n2), (rows, (n1.float() - n2.float()).abs().max().item())
+    assert not s.fuses_linear(100)
     # graph capture + replay
     x = torch.randn(16, H, device=dev, generator=g).bfloat16()
     res = torch.zeros(16, H, device=dev).bfloat16()

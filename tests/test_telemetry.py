@@ -169,3 +169,4 @@ def test_mx_tile_codes_layout():
                         else:
                             src = nt * 128 + r
                         assert torch.equal(t[e, nt, ks, r], w[e, src, ks * 64:(ks + 1) * 64])
+
