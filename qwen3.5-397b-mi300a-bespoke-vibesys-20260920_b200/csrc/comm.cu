@@ -159,22 +159,27 @@ __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
 }
 
 // ------------------------------------------------------------------ sequence-parallel variant
-// Reduce-scatter + residual add + RMSNorm + all-gather, for prefill-sized messages. Rank r owns
-// rows [r R / W, (r+1) R / W); inside every rank's range, block b handles rows b, b + G, ... (the
-// same (rank, block) units on every rank). Region per rank and slot: the staged partial
-// [R_max, H] and the results [R_max, 2H] (new residual row, normed row); then phase-A and
-// phase-B flags [2 slots][max_blocks] each.
-//   A. block b stages, for every owner rank, its unit's rows of the local partial; flag A[b] = e
+// Reduce-scatter + residual add + RMSNorm + all-gather, for prefill-sized messages. Rank o owns
+// rows [o per, (o+1) per) with per = ceil(R / W) (the last ranks may own fewer or none); inside
+// every rank's range, block b handles rows b, b + G, ... (the same (rank, block) units on every
+// rank). Region per rank and slot: the partial slot [W per, H], where rank p's rows of the
+// owner's range sit at rows p per + (t - o per), and the results [R_max, 2H] (new residual row,
+// normed row); then phase-A and phase-B flags [2 slots][max_blocks] each.
+//   A. block b stores, for every owner rank, its unit's rows of the local partial into the
+//      owner's partial slot (posted stores over NVLink); flag A[b] = e
 //   B. block b waits for flag A[b] of every peer (one thread per peer), then for its own unit:
 //      rank-order fp32 sum of the W partial rows, bf16 round, + residual, RMSNorm; writes the
-//      results to its slot and to the local tensors; flag B[b] = e
-//   C. block b waits for flag B[b] of every peer and copies their units' result rows.
+//      results to the local tensors and stores them into every peer's result area (stores are
+//      posted, so the all-gather costs no round trips); flag B[b] = e
+//   C. block b waits for flag B[b] of every peer and copies the peers' units' result rows, now
+//      in its own result area, into the local tensors.
+// Slot reuse: rank o writes rank p's result area of slot s for call e + 2 only after its block b
+// saw p's flag A[b] for e + 2, which p's block b raised after p's whole kernel for call e ended.
 // Same bits as the one-shot kernel (and as NCCL all-reduce + add + RMSNorm); each rank moves
 // about 3 (W-1)/W of the bf16 payload over NVLink instead of (W-1) copies of it.
 // PUSHED: the projection GEMM before this kernel already stored its rows into the owners' slots
-// (gemm.cu, GemmPush): rank o owns rows [o per, (o+1) per), and its partial slot holds rank p's
-// rows of that range at rows p per + (t - o per). Phase A then only publishes (the GEMM's stores
-// completed with that kernel) and phase B sums local rows.
+// (gemm.cu, GemmPush), so phase A only publishes (the GEMM's stores completed with that kernel).
+// Either way phase B reads local memory only.
 __device__ __forceinline__ bool wait_peers(const SymmPtrs& ptrs, long flag_off, int b, int e, int* err,
                                            unsigned long long timeout_ns) {
   int ok = 1;
@@ -210,13 +215,8 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
   auto part_of = [&](int r) { return reinterpret_cast<bf16*>(ptrs.data[r]) + slot * slot_stride; };
   auto result_of = [&](int r) { return reinterpret_cast<bf16*>(ptrs.data[r]) + slot * slot_stride + slot_elems; };
   auto range = [&](int r, int& r0, int& r1) {
-    if (PUSHED) {
-      r0 = min(rows, r * per);
-      r1 = min(rows, (r + 1) * per);
-    } else {
-      r0 = (int)((long)rows * r / W);
-      r1 = (int)((long)rows * (r + 1) / W);
-    }
+    r0 = min(rows, r * per);
+    r1 = min(rows, (r + 1) * per);
   };
   auto publish = [&](long off) {
     __syncthreads();
@@ -225,14 +225,15 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
       st_release_sys(reinterpret_cast<int*>(reinterpret_cast<char*>(ptrs.data[me]) + off) + b, e);
     }
   };
-  // A. stage this block's rows of every owner's range
+  // A. store this block's rows of every owner's range into the owner's partial slot
   bf16* mine = part_of(me);
   for (int r = 0; r < (PUSHED ? 0 : W); ++r) {
     int r0, r1;
     range(r, r0, r1);
+    bf16* dst = part_of(r) + (long)me * per * H;
     for (int row = r0 + b; row < r1; row += G)
       for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8)
-        *reinterpret_cast<uint4*>(mine + (long)row * H + i) =
+        *reinterpret_cast<uint4*>(dst + (long)(row - r0) * H + i) =
             *reinterpret_cast<const uint4*>(partial + (long)row * ldp + i);
   }
   publish(flagA);
@@ -240,7 +241,9 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
   if (wait_peers(ptrs, flagA, b, e, err, timeout_ns)) {
     int r0, r1;
     range(me, r0, r1);
-    bf16* myres = result_of(me);
+    bf16* peer_res[8];
+#pragma unroll
+    for (int p = 0; p < 8; ++p) peer_res[p] = p < W ? result_of(p) : nullptr;
     const int nper = (H + AR_THREADS * 8 - 1) / (AR_THREADS * 8);  // chunks of 8 per thread (<= 2)
     for (int row = r0 + b; row < r1; row += G) {
       float acc[16];
@@ -253,9 +256,7 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
           uint4 raw[8];
 #pragma unroll
           for (int p = 0; p < 8; ++p)
-            if (p < W)
-              raw[p] = PUSHED ? __ldcv(reinterpret_cast<const uint4*>(mine + ((long)p * per + row - r0) * H + i))
-                              : __ldcv(reinterpret_cast<const uint4*>(part_of(p) + (long)row * H + i));
+            if (p < W) raw[p] = __ldcv(reinterpret_cast<const uint4*>(mine + ((long)p * per + row - r0) * H + i));
 #pragma unroll
           for (int p = 0; p < 8; ++p) {
             if (p < W) {
@@ -276,7 +277,9 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
             ss += acc[c * 8 + u] * acc[c * 8 + u];
           }
           *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr;
-          *reinterpret_cast<uint4*>(myres + (long)row * 2 * H + i) = nr;
+#pragma unroll
+          for (int p = 0; p < 8; ++p)
+            if (p < W && p != me) *reinterpret_cast<uint4*>(peer_res[p] + (long)row * 2 * H + i) = nr;
         }
       }
       ss = warp_sum(ss);
@@ -299,25 +302,39 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
 #pragma unroll
           for (int u = 0; u < 8; ++u) ov[u] = __float2bfloat16(acc[c * 8 + u] * inv * w1p[i + u]);
           *reinterpret_cast<uint4*>(out + (long)row * H + i) = o;
-          *reinterpret_cast<uint4*>(myres + (long)row * 2 * H + H + i) = o;
+#pragma unroll
+          for (int p = 0; p < 8; ++p)
+            if (p < W && p != me) *reinterpret_cast<uint4*>(peer_res[p] + (long)row * 2 * H + H + i) = o;
         }
       }
     }
     publish(flagB);
-    // C. gather the peers' result rows of this block's units
+    // C. the peers' result rows of this block's units, stored into this rank's result area
     if (wait_peers(ptrs, flagB, b, e, err, timeout_ns)) {
+      const bf16* pr = result_of(me);
       for (int p = 0; p < W; ++p) {
         if (p == me) continue;
         int q0, q1;
         range(p, q0, q1);
-        const bf16* pr = result_of(p);
-        for (int row = q0 + b; row < q1; row += G)
-          for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8) {
-            const uint4 nr = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + i));
-            const uint4 o = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + H + i));
-            *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr;
-            *reinterpret_cast<uint4*>(out + (long)row * H + i) = o;
+        for (int row = q0 + b; row < q1; row += G) {
+          uint4 nr[2], o[2];  // every load of the row in flight before the stores
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int i = (threadIdx.x + c * AR_THREADS) * 8;
+            if (i < H) {
+              nr[c] = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + i));
+              o[c] = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + H + i));
+            }
           }
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            const int i = (threadIdx.x + c * AR_THREADS) * 8;
+            if (i < H) {
+              *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr[c];
+              *reinterpret_cast<uint4*>(out + (long)row * H + i) = o[c];
+            }
+          }
+        }
       }
     }
   }
@@ -337,17 +354,17 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
 int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                            const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
                            int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s) {
-  if (world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || (long)rows * H > slot_elems) return -1;
+  const int per = (rows + world - 1) / world;  // rows of one rank's range: one block per row, up to max_blocks
+  if (world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || (long)per * world * H > slot_elems) return -1;
   SymmPtrs p{};
   for (int r = 0; r < world; ++r) p.data[r] = bases[r];
   p.world = world;
   p.rank = rank;
-  int per = (rows + world - 1) / world;  // rows of one rank's range: one block per row, up to max_blocks
   int grid = per < max_blocks ? per : max_blocks;
   if (grid < 1) grid = 1;
   sp_ar_add_rmsnorm_kernel<false><<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res, w1p,
                                                               (bf16*)out, rows, H, eps, slot_elems, max_blocks,
-                                                              epoch, done, err, timeout_ns, 0);
+                                                              epoch, done, err, timeout_ns, per);
   return (int)cudaGetLastError();
 }
 

@@ -66,10 +66,11 @@ class SymmComm:
         self.bases = self._region(2 * self.slot_elems * 2 + 2 * self.max_blocks * 4, group, bases)
         self.epoch = torch.zeros(2, dtype=torch.int32, device=self.device)  # [epoch, finished blocks]
         self.sp_rows = sp_rows
-        self.sp_slot_elems = sp_rows * hidden
+        # partial slots hold whole per-rank ranges: world x ceil(rows / world) rows
+        self.sp_slot_elems = -(-sp_rows // world) * world * hidden
         self.sp_bases = None
         if sp_rows > 0:
-            self.sp_bases = self._region(self.sp_region_bytes(sp_rows, hidden), group, sp_bases)
+            self.sp_bases = self._region(self.sp_region_bytes(-(-sp_rows // world) * world, hidden), group, sp_bases)
             self.sp_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
 
     @staticmethod
@@ -119,13 +120,10 @@ class SymmComm:
 
     def fuses_linear(self, rows: int) -> bool:
         """Whether ``linear_allreduce_add_rmsnorm`` takes the fused GEMM -> reduce-scatter path
-        for ``rows`` (the sizes the sequence-parallel kernel takes, with the owners' ranges of
-        ceil(rows / world) rows fitting the region)."""
+        for ``rows`` (the sizes the automatic choice gives the sequence-parallel kernel)."""
         if self.sp_bases is None or rows < 1:
             return False
-        per = -(-rows // self.world)
-        return per * self.world <= self.sp_rows and (rows > self.max_rows
-                                                     or rows * (self.world - 1) > self.ONESHOT_ROW_BUDGET)
+        return rows <= self.sp_rows and (rows > self.max_rows or rows * (self.world - 1) > self.ONESHOT_ROW_BUDGET)
 
     def linear_allreduce_add_rmsnorm(self, x, w, residual, w1p, eps):
         """``residual += sum_ranks(x @ w^T)`` (in place) and returns (residual, rmsnorm(residual)):

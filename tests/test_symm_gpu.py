@@ -56,6 +56,20 @@ def test_two_gpu_fused_equals_nccl():
     assert [p.wait(timeout=300) for p in procs] == [0, 0]
 
 
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_model_out_proj_fused_equals_unfused():
+    """Tiny model, 2 ranks: a 1500-token prefill with the attention / DeltaNet out projections
+    fused into the sequence-parallel all-reduce gives the same logits bit for bit."""
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "sp_model_rank.py"), str(r), "2", str(port)],
+                              env=env) for r in range(2)]
+    assert [p.wait(timeout=300) for p in procs] == [0, 0]
+
+
 def test_expert_parallel_one_rank_equals_local_moe():
     """Expert-parallel dispatch / experts / combine with one rank (every token's row goes to
     itself through the receive area) equals the local routed-expert op, over consecutive calls
