@@ -1,4 +1,4 @@
-"""the tiny model at TP=4 over gloo (4 CPU processes, the real scheduler,
+"""Greedy-token parity: the tiny model at TP=4 over gloo (4 CPU processes, the real scheduler,
 session cache and SPMD driver) reproduces the HuggingFace oracle's greedy tokens, turn by turn,
 for 2 chat sessions x 3 turns with 32 new tokens each."""
 

@@ -1,4 +1,4 @@
-"""One rank of the tensor-parallel CPU parity run.
+"""One rank of the tensor-parallel CPU parity run (tiny model, TP=4 over gloo).
 
 Every rank loads its shard of the tiny checkpoint in fp32 and joins a gloo group; rank 0 runs
 the real scheduler + session cache through ``Broadcaster`` while the other ranks run
