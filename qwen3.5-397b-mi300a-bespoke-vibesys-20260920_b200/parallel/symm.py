@@ -22,24 +22,71 @@ MAX_BLOCKS = 296  # one-shot kernel: two CTAs per SM on a 148-SM B200
 SP_MAX_BLOCKS = 296  # sequence-parallel kernel: one row per CTA; more CTAs measured slower
 
 
-def alloc_region(rank: int, world: int, device, nbytes: int, group=None) -> tuple[list[int], int, list[int]]:
+class SymmUnavailable(RuntimeError):
+    """Raised on every rank together when any rank could not set up its symmetric region."""
+
+
+def vote_or_raise(ok: bool, err: Exception | None, device, what: str, group=None) -> None:
+    """Every rank reports whether its local step worked (``dist.all_reduce`` MIN of a 0/1 flag);
+    when any rank failed, every rank raises ``SymmUnavailable`` at this same point, so they all
+    fall back to NCCL together instead of some waiting in a collective the others never reach.
+    Reference behaviour: ``allreduce_custom.py:932-953`` (``_vote_or_raise``)."""
+    flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=device)
+    dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+    if int(flag.item()) == 0:
+        raise SymmUnavailable(f"{what} failed on at least one rank (this rank: {err!r})")
+
+
+def alloc_region(rank: int, world: int, device, nbytes: int, group=None, alloc=None, open_=None, close=None,
+                 free=None, vote_device=None) -> tuple[list[int], int, list[int]]:
     """Allocate this rank's region (``cudaMalloc``, zeroed), export it and map every peer's.
     Returns (every rank's base address as seen here, own pointer, opened peer pointers); every
-    rank must call this together (it all-gathers the IPC handles)."""
-    with torch.cuda.device(device):
-        ptr, handle = ext().symm_alloc(nbytes)
+    rank must call this together (it all-gathers the IPC handles). A failure on any rank, in the
+    allocation or in mapping a peer, raises ``SymmUnavailable`` on every rank after a vote, with
+    this rank's own mappings undone. ``alloc``/``open_``/``close``/``free`` default to the CUDA
+    extension (tests pass host fakes)."""
+    alloc = alloc or (lambda n: ext().symm_alloc(n))
+    open_ = open_ or (lambda h: ext().symm_open(h))
+    close = close or (lambda p: ext().symm_close(p))
+    free = free or (lambda p: ext().symm_free(p))
+    vdev = vote_device if vote_device is not None else device
+    ptr = handle = err = None
+    try:
+        with torch.cuda.device(device) if torch.device(device).type == "cuda" else _nullctx():
+            ptr, handle = alloc(nbytes)
+    except Exception as e:  # noqa: BLE001 - reported through the vote
+        err = e
+    vote_or_raise(err is None, err, vdev, "symmetric region allocation", group)
     handles = [None] * world
     dist.all_gather_object(handles, handle, group=group)
     bases, opened = [], []
-    for r in range(world):
-        if r == rank:
-            bases.append(ptr)
-        else:
-            with torch.cuda.device(device):
-                p = ext().symm_open(handles[r])
-            opened.append(p)
-            bases.append(p)
+    try:
+        for r in range(world):
+            if r == rank:
+                bases.append(ptr)
+            else:
+                with torch.cuda.device(device) if torch.device(device).type == "cuda" else _nullctx():
+                    p = open_(handles[r])
+                opened.append(p)
+                bases.append(p)
+    except Exception as e:  # noqa: BLE001 - reported through the vote
+        err = e
+    try:
+        vote_or_raise(err is None, err, vdev, "peer region mapping", group)
+    except SymmUnavailable:
+        for p in opened:
+            close(p)
+        free(ptr)
+        raise
     return bases, ptr, opened
+
+
+class _nullctx:
+    def __enter__(self):
+        return None
+
+    def __exit__(self, *a):
+        return False
 
 
 class SymmComm:
@@ -70,7 +117,12 @@ class SymmComm:
         self.sp_slot_elems = -(-sp_rows // world) * world * hidden
         self.sp_bases = None
         if sp_rows > 0:
-            self.sp_bases = self._region(self.sp_region_bytes(-(-sp_rows // world) * world, hidden), group, sp_bases)
+            try:
+                self.sp_bases = self._region(self.sp_region_bytes(-(-sp_rows // world) * world, hidden), group,
+                                             sp_bases)
+            except SymmUnavailable:
+                self.close()  # the one-shot region is undone on every rank alike
+                raise
             self.sp_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
 
     @staticmethod

@@ -77,11 +77,15 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
     if comm is None:
         comm = Comm(rank, world, None, device)
         if world > 1 and device.type == "cuda" and comm.mode == "fused":
-            from ..parallel.symm import SymmComm
+            from ..parallel.symm import SymmComm, SymmUnavailable
 
             rows = flags.get("QB_SYMM_MAX_ROWS")
             sp_rows = flags.get("QB_SP_MAX_ROWS")  # prefill-sized messages: sequence-parallel kernel
-            comm.symm = SymmComm(rank, world, device, max_rows=rows, hidden=cfg.hidden, sp_rows=sp_rows)
+            try:
+                comm.symm = SymmComm(rank, world, device, max_rows=rows, hidden=cfg.hidden, sp_rows=sp_rows)
+            except SymmUnavailable as e:  # raised on every rank together: all fall back to NCCL
+                print(f"[rank {rank}] fused collectives unavailable, using NCCL: {e}", flush=True)
+                comm.symm = None
     m = Model(cfg, w, p, comm, device=device, dtype=dtype,
               max_batch=spec.lanes + (1 if graphs else 0), max_seq=spec.max_seq, block_size=spec.block_size,
               num_blocks=num_blocks, num_snapshots=spec.snapshots or 2 * spec.lanes + 16)

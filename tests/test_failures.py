@@ -103,3 +103,57 @@ def test_ranks_with_different_lockstep_flags_refuse_to_serve():
     for p in ps:
         p.join(timeout=60)
     assert res == {0: "mismatch", 1: "mismatch"}
+
+
+def _region_rank(rank, port, fail_stage, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), RANK=str(rank), WORLD_SIZE="2")
+    import datetime
+
+    import torch.distributed as dist
+
+    from qwen35_b200.parallel.symm import SymmUnavailable, alloc_region
+
+    dist.init_process_group("gloo", rank=rank, world_size=2, timeout=datetime.timedelta(seconds=60))
+    freed, closed = [], []
+
+    def alloc(n):
+        if fail_stage == "alloc" and rank == 1:
+            raise RuntimeError("out of device memory")
+        return 1000 + rank, f"handle{rank}"
+
+    def open_(h):
+        if fail_stage == "open" and rank == 0:
+            raise RuntimeError("peer access refused")
+        return 2000 + int(h[-1])
+
+    try:
+        bases, own, opened = alloc_region(rank, 2, "cpu", 64, alloc=alloc, open_=open_, close=closed.append,
+                                          free=freed.append)
+        q.put((rank, "ok", bases))
+    except SymmUnavailable:
+        q.put((rank, "unavailable", (freed, closed)))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("fail_stage", ["none", "alloc", "open"])
+def test_symmetric_region_failure_on_one_rank_is_raised_on_every_rank(fail_stage):
+    """A rank that cannot allocate or map the peer regions makes every rank raise at the same
+    vote (so all fall back to NCCL together), with its own mappings undone; nobody waits."""
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_region_rank, args=(r, port, fail_stage, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {r: (st, info) for r, st, info in (q.get(timeout=120) for _ in ps)}
+    for p in ps:
+        p.join(timeout=60)
+    if fail_stage == "none":
+        assert res == {0: ("ok", [1000, 2001]), 1: ("ok", [2000, 1001])}
+    elif fail_stage == "alloc":
+        assert {r: st for r, (st, _) in res.items()} == {0: "unavailable", 1: "unavailable"}
+    else:
+        assert res[0] == ("unavailable", ([1000], [])) and res[1] == ("unavailable", ([1001], [2000]))
