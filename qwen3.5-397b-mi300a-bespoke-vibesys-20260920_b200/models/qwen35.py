@@ -126,6 +126,7 @@ class Model:
         self.gpu_marks = None  # list -> CUDA events at each input upload ("in") and result read ("out")
         self.stamps = None  # utils.telemetry.Stamps -> in-graph clock stamps at layer boundaries
         self._defer_out = False  # set inside _layers while the out projections fuse into the all-reduce
+        self.status_watch = None  # utils.devstatus.StatusWatch (CUDA): polled by the scheduler / workers
 
     def _gpu_mark(self, tag: str) -> None:
         """Stream-ordered event where a step's device work starts (input upload) or ends (the

@@ -130,14 +130,21 @@ def apply(model, op: Op, args: tuple):
     raise ValueError(f"unknown op {op}")
 
 
+STEP_OPS = (Op.PREFILL_BATCH, Op.DECODE, Op.DECODE_MIXED, Op.SPECULATIVE_DECODE, Op.SCORE)
+
+
 def serve_worker(model, channel: Channel) -> int:
-    """Apply rank 0's commands until SHUTDOWN; returns the number of commands applied."""
+    """Apply rank 0's commands until SHUTDOWN; returns the number of commands applied. A nonzero
+    device status word (``utils.devstatus``) ends the worker with ``DeviceStatusError``."""
     n = 0
+    watch = getattr(model, "status_watch", None)
     while True:
         op, args = channel.recv()
         if op == Op.SHUTDOWN:
             return n
         apply(model, op, args)
+        if watch is not None and op in STEP_OPS:
+            watch.step()
         n += 1
 
 
@@ -150,6 +157,10 @@ class Broadcaster:
         self.max_batch = model.max_batch
         self.max_seq = model.max_seq
         self.block_size = model.block_size
+
+    @property
+    def status_watch(self):
+        return getattr(self.model, "status_watch", None)
 
     def _send(self, op: Op, *args):
         if self.channel is not None:

@@ -90,6 +90,10 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
               max_batch=spec.lanes + (1 if graphs else 0), max_seq=spec.max_seq, block_size=spec.block_size,
               num_blocks=num_blocks, num_snapshots=spec.snapshots or 2 * spec.lanes + 16)
     memtimeline.mark("pools", device)
+    if device.type == "cuda":
+        from ..utils.devstatus import StatusWatch
+
+        m.status_watch = StatusWatch(device, flags.get("QB_STATUS_EVERY"))
     if device.type == "cuda" and flags.get("QB_RANK_BW_PROBE"):
         from ..utils.hostinfo import probe
 

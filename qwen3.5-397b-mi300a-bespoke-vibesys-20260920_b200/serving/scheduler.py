@@ -199,11 +199,13 @@ class Scheduler:
                     self._prefill_step()
                     self.burst += 1
                 self.steps += 1
+                self._watch_status()
                 return True
             if self.decoding:
                 self._decode_step()
                 self.burst = 0
                 self.steps += 1
+                self._watch_status()
                 return True
             return False
         except Exception as e:  # abort everything in flight, keep serving
@@ -212,6 +214,12 @@ class Scheduler:
             traceback.print_exc()
             self._abort_all(msg)
             return True
+
+    def _watch_status(self) -> None:
+        """Poll the device status word (raises ``DeviceStatusError``: the step's caller aborts)."""
+        watch = getattr(self.runner, "status_watch", None)
+        if watch is not None:
+            watch.step()
 
     # ================================================================== admission
     def _live_parents(self) -> list[Node]:

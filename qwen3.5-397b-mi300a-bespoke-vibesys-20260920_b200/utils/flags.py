@@ -65,6 +65,8 @@ _def("QB_SP_GEMM", bool, True, "prefill: fuse the mixers' output projection into
      "(GEMM epilogue stores rows into their owners' peer slots)", lockstep=True)
 _def("QB_CMD_CHANNEL", str, "shm", "leader -> worker command channel: shm (shared-memory ring) or gloo (broadcast)",
      lockstep=True)
+_def("QB_STATUS_EVERY", int, 64, "read the kernels' device status word every n model steps (0: never); a "
+     "nonzero code aborts the requests in flight (rank 0) or ends the worker")
 # ---- diagnostics (off by default; none of them changes a number)
 _def("QB_STEP_TIMING", int, 0, "log a [step-timing] line every n scheduler steps (0: off)")
 _def("QB_SERVICE_TRACE", str, "", "append one JSON record per scheduler step to this path")
