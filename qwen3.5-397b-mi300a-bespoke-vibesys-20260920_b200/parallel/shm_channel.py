@@ -36,7 +36,17 @@ class ShmChannel:
             self.shm = shared_memory.SharedMemory(name=name, create=True, size=HEADER + size)
             self.shm.buf[:HEADER] = bytes(HEADER)
         else:
-            self.shm = shared_memory.SharedMemory(name=name)
+            # only the creator owns the segment: a reader attaches without registering it with
+            # the resource tracker, which would otherwise unlink it at the reader's exit too (and
+            # warn about a "leaked" segment the creator already removed)
+            from multiprocessing import resource_tracker
+
+            register = resource_tracker.register
+            resource_tracker.register = lambda *a, **k: None
+            try:
+                self.shm = shared_memory.SharedMemory(name=name)
+            finally:
+                resource_tracker.register = register
         self.ctr = np.ndarray((1 + world,), dtype=np.uint64, buffer=self.shm.buf[:8 * (1 + world)])
         self.ring = self.shm.buf[HEADER:HEADER + size]
         self._closed = False
