@@ -128,6 +128,9 @@ class Engine:
         self.sched = None
         self.runner = None
         self.tok = None
+        from .chat_history import ChatHistory
+
+        self.history = ChatHistory()  # exact ids of the replies this server generated
         self.model_name = os.path.basename(str(args.model_path).rstrip("/")) or "qwen3.5"
         self.thread = threading.Thread(target=self._boot, daemon=True)
         self.thread.start()
@@ -219,7 +222,7 @@ def make_app(engine: Engine):
     async def models(_):
         return web.json_response({"object": "list", "data": [{"id": engine.model_name, "object": "model"}]})
 
-    async def generate(request, prompt_ids, suffix_len, has_history, body, chat: bool):
+    async def generate(request, prompt_ids, suffix_len, has_history, body, chat: bool, on_done=None):
         max_new = int(body.get("max_tokens") or body.get("max_completion_tokens") or 256)
         temp = float(body.get("temperature", 0.0) or 0.0)
         stream = bool(body.get("stream", False))
@@ -264,6 +267,8 @@ def make_app(engine: Engine):
                 tail = detok.flush()
                 if tail:
                     await send(chunk(tail))
+                if on_done is not None:
+                    on_done(out_ids)
                 reason = "stop" if end[0] == "stop" else "length"
                 await send(chunk(None, reason))
                 if usage_opt:
@@ -280,6 +285,8 @@ def make_app(engine: Engine):
         if err is not None:
             return web.json_response({"error": {"message": err, "type": "server_error"}}, status=500)
         text = engine.tok.decode(out_ids)
+        if on_done is not None:
+            on_done(out_ids)
         reason = "stop" if end[0] == "stop" else "length"
         if chat:
             choice = {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
@@ -302,9 +309,21 @@ def make_app(engine: Engine):
         body = await request.json()
         msgs = body.get("messages") or []
         kw = body.get("chat_template_kwargs") or {}
-        ids, suffix = engine.tok.render_chat(msgs, enable_thinking=bool(kw.get("enable_thinking", False)))
         has_history = any(m.get("role") == "assistant" for m in msgs)
-        return await generate(request, ids, suffix, has_history, body, chat=True)
+        eos = engine.tok.eos_token_id
+        stop_ids = {eos} if eos is not None else set()
+        if getattr(engine.tok, "template", None) is not None:
+            stop_ids.add(engine.tok.template.im_end)
+        spliced = engine.history.splice(engine.tok, msgs, kw, stop_ids) if has_history else None
+        if spliced is not None:
+            ids, suffix = spliced
+        else:
+            ids, suffix = engine.tok.render_chat(msgs, enable_thinking=bool(kw.get("enable_thinking", False)))
+
+        def remember(out_ids):
+            engine.history.record(msgs, kw, engine.tok.decode(out_ids), ids, out_ids)
+
+        return await generate(request, ids, suffix, has_history, body, chat=True, on_done=remember)
 
     @routes.post("/v1/completions")
     async def completions(request):

@@ -37,6 +37,14 @@ class ByteTokenizer:
         msgs = [(m["role"], self.encode(str(m.get("content") or ""))) for m in messages]
         return self.template.render(msgs, True, enable_thinking)
 
+    def render_tail(self, messages: list[dict], enable_thinking: bool = False) -> tuple[list[int], int]:
+        """Ids after the content of the assistant message ``messages[-2]`` (its closing tokens,
+        the later turns, the generation prompt) and the prompt's ``suffix_len``."""
+        t = self.template
+        rest = [(m["role"], self.encode(str(m.get("content") or ""))) for m in messages[-1:]]
+        ids, suffix = t.render(rest, True, enable_thinking)
+        return [t.im_end, t.nl] + ids, suffix
+
 
 class HFTokenizer:
     """A HuggingFace tokenizer with Qwen's chat template."""
@@ -52,6 +60,34 @@ class HFTokenizer:
 
     def decode(self, ids) -> str:
         return self.tok.decode(ids, skip_special_tokens=True)
+
+    PLACEHOLDER = "\u2063qb-reply-placeholder\u2063"
+
+    def render_tail(self, messages: list[dict], enable_thinking: bool = False) -> tuple[list[int], int] | None:
+        """Ids after the content of the assistant message ``messages[-2]`` and the prompt's
+        ``suffix_len``: the template is rendered with a placeholder reply and split there. None
+        when the template changes the reply text or the tail does not open with a special token
+        (the ids could not be joined at that point)."""
+        reply = messages[-2].get("content")
+        if not isinstance(reply, str) or any(self.PLACEHOLDER in str(m.get("content")) for m in messages):
+            return None
+        marked = [*messages[:-2], {**messages[-2], "content": self.PLACEHOLDER}, messages[-1]]
+        try:
+            text = self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=True,
+                                                enable_thinking=enable_thinking)
+            mtext = self.tok.apply_chat_template(marked, tokenize=False, add_generation_prompt=True,
+                                                 enable_thinking=enable_thinking)
+        except Exception:  # noqa: BLE001 - an unfamiliar template: ordinary prompt
+            return None
+        if mtext.count(self.PLACEHOLDER) != 1:
+            return None
+        head, tail = mtext.split(self.PLACEHOLDER)
+        if text != head + reply.strip() + tail:
+            return None
+        if not tail or not any(tail.startswith(s) for s in self.tok.all_special_tokens):
+            return None
+        _, suffix = self.render_chat(messages, enable_thinking)
+        return self.encode(tail), suffix
 
     def render_chat(self, messages: list[dict], enable_thinking: bool = False) -> tuple[list[int], int]:
         text = self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=True,

@@ -1,0 +1,67 @@
+"""Chat history with the exact generated ids (CPU): a recorded reply sent back as history is
+spliced in as the generated ids, so the next prompt extends the cached sequence."""
+
+from qwen35_b200.serving.chat_history import ChatHistory
+from qwen35_b200.serving.tokenizer import ByteTokenizer, HFTokenizer
+
+
+def test_splice_with_the_token_template():
+    tok = ByteTokenizer(4096, 4095)
+    t = tok.template
+    h = ChatHistory()
+    first = [{"role": "user", "content": "hi"}]
+    prompt, _ = tok.render_chat(first)
+    out = tok.encode("hello there") + [tok.eos_token_id]
+    h.record(first, {}, tok.decode(out), prompt, out)
+    nxt = first + [{"role": "assistant", "content": "hello there"}, {"role": "user", "content": "more"}]
+    ids, suffix = h.splice(tok, nxt, {}, {tok.eos_token_id, t.im_end})
+    tail = [t.im_end, t.nl] + t.turn("user", tok.encode("more")) + t.generation_suffix(False)
+    assert ids == prompt + out[:-1] + tail
+    assert suffix == tok.render_chat(nxt)[1]
+    assert ids[:len(prompt) + len(out) - 1] == prompt + out[:-1]  # the cached sequence, token for token
+    # another reply text, other history or other template options: ordinary prompt
+    assert h.splice(tok, first + [{"role": "assistant", "content": "hello"}, nxt[-1]], {}) is None
+    assert h.splice(tok, [{"role": "user", "content": "yo"}] + nxt[1:], {}) is None
+    assert h.splice(tok, nxt, {"enable_thinking": True}) is None
+    assert h.splice(tok, nxt[:2], {}) is None  # does not end with a user message
+    assert h.stats["spliced"] == 1
+
+
+def test_lru_capacity():
+    h = ChatHistory(capacity=2)
+    for i in range(3):
+        h.record([{"role": "user", "content": str(i)}], {}, "r", [i], [i])
+    assert len(h._recs) == 2
+
+
+class _FakeHF:
+    """A Qwen-like text template over a character-level encoding."""
+
+    all_special_tokens = ["<|im_start|>", "<|im_end|>"]
+
+    def apply_chat_template(self, messages, tokenize=False, add_generation_prompt=True, enable_thinking=False):
+        out = ""
+        for m in messages:
+            out += f"<|im_start|>{m['role']}\n{str(m['content']).strip()}<|im_end|>\n"
+        if add_generation_prompt:
+            out += "<|im_start|>assistant\n" + ("" if enable_thinking else "<think>\n\n</think>\n\n")
+        return out
+
+    def encode(self, text, add_special_tokens=False):
+        return [ord(c) for c in text]
+
+
+def test_hf_tail_found_by_placeholder():
+    tok = object.__new__(HFTokenizer)
+    tok.tok = _FakeHF()
+    tok.eos_token_id = None
+    msgs = [{"role": "user", "content": "hi"}, {"role": "assistant", "content": " hello "},
+            {"role": "user", "content": "more"}]
+    tail, suffix = tok.render_tail(msgs)
+    assert "".join(map(chr, tail)) == "<|im_end|>\n<|im_start|>user\nmore<|im_end|>\n<|im_start|>assistant\n" \
+                                      "<think>\n\n</think>\n\n"
+    assert suffix == tok.render_chat(msgs)[1] > 0
+    # a template that rewrites the reply cannot be split: ordinary prompt
+    tok.tok.apply_chat_template = lambda m, **k: _FakeHF.apply_chat_template(
+        tok.tok, [{**x, "content": str(x["content"]).upper()} for x in m], **k)
+    assert tok.render_tail(msgs) is None
