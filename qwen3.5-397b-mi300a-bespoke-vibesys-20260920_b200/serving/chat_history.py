@@ -60,7 +60,7 @@ class ChatHistory:
             return None
         tail, suffix = got
         prompt, out = rec
-        if out and out[-1] in stop_ids:
+        if out and (out[-1] in stop_ids or (tail and out[-1] == tail[0])):
             out = out[:-1]  # the tail opens with the template's own closing token
         self._recs.move_to_end(self.key(list(messages[:-2]), reply, options))
         self.stats["spliced"] += 1

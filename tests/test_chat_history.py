@@ -25,6 +25,11 @@ def test_splice_with_the_token_template():
     assert h.splice(tok, nxt, {"enable_thinking": True}) is None
     assert h.splice(tok, nxt[:2], {}) is None  # does not end with a user message
     assert h.stats["spliced"] == 1
+    # a reply that ended on the template's closing token itself: that token is not doubled
+    out2 = tok.encode("ok") + [t.im_end]
+    h.record(first, {"x": 1}, tok.decode(out2), prompt, out2)
+    ids2, _ = h.splice(tok, first + [{"role": "assistant", "content": "ok"}, nxt[-1]], {"x": 1})
+    assert ids2 == prompt + out2[:-1] + tail
 
 
 def test_lru_capacity():
