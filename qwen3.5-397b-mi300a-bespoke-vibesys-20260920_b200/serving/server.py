@@ -343,23 +343,55 @@ def make_app(engine: Engine):
 
     @routes.post("/v1/score")
     async def score(request):
+        """Teacher-forced log-probabilities of a continuation. Two request forms:
+        ``{"prompt": [ids], "continuation_start": i, "top_k": k}`` scores ``prompt[i:]`` and
+        answers ``{"object": "token_scores", "scores": [{token_id, logprob, top_logprobs}]}`` (the
+        reference's form, ``server.py:723-880`` there); ``{"prompt": ..., "continuation": ...}``
+        (ids or text) answers ``{"logprobs": [...], "tokens": [...]}``."""
+        if not engine.healthy():
+            return web.json_response({"error": {"message": "not ready"}}, status=503)
         body = await request.json()
-        p = body.get("prompt", [])
-        c = body.get("continuation", [])
-        pids = [int(x) for x in p] if isinstance(p, list) else engine.tok.encode(p)
-        cids = [int(x) for x in c] if isinstance(c, list) else engine.tok.encode(c)
+        ref_form = "continuation_start" in body
+        top_k = 0
+        if ref_form:
+            ids = body.get("prompt")
+            cs = body.get("continuation_start")
+            top_k = body.get("top_k", 5)
+            if not isinstance(ids, list) or not all(isinstance(x, int) and not isinstance(x, bool) for x in ids):
+                return web.json_response({"error": "prompt must be a list of token ids"}, status=400)
+            if not isinstance(cs, int) or isinstance(cs, bool) or not 0 < cs < len(ids):
+                return web.json_response({"error": f"continuation_start must satisfy 0 < continuation_start < "
+                                                   f"len(prompt) ({len(ids)}), got {cs!r}"}, status=400)
+            if not isinstance(top_k, int) or isinstance(top_k, bool) or top_k < 1:
+                return web.json_response({"error": "top_k must be a positive integer"}, status=400)
+            pids, cids = ids[:cs], ids[cs:]
+        else:
+            p = body.get("prompt", [])
+            c = body.get("continuation", [])
+            pids = [int(x) for x in p] if isinstance(p, list) else engine.tok.encode(p)
+            cids = [int(x) for x in c] if isinstance(c, list) else engine.tok.encode(c)
         ids = pids + cids
 
         def finish(logits):
             lp = torch.log_softmax(logits.float(), dim=-1)
             tgt = torch.tensor(cids, device=lp.device)
-            return lp[torch.arange(len(cids), device=lp.device), tgt].tolist()
+            picked = lp[torch.arange(len(cids), device=lp.device), tgt].tolist()
+            if not ref_form:
+                return picked
+            vals, tops = lp.topk(min(top_k, lp.shape[-1]), dim=-1)
+            return [{"token_id": t, "logprob": v,
+                     "top_logprobs": [{"token_id": i, "logprob": x} for x, i in zip(vr, ir)]}
+                    for t, v, vr, ir in zip(cids, picked, vals.tolist(), tops.tolist())]
 
         job = ScoreJob(ids, len(pids), finish)
         engine.sched.score(job)
         await asyncio.get_running_loop().run_in_executor(None, job.done.wait, 600)
         if job.error:
             return web.json_response({"error": {"message": job.error}}, status=500)
+        if ref_form:
+            return web.json_response({"id": f"score-{uuid.uuid4().hex}", "object": "token_scores",
+                                      "model": body.get("model") or engine.model_name, "prompt_tokens": len(ids),
+                                      "continuation_start": len(pids), "scores": job.result})
         return web.json_response({"logprobs": job.result, "tokens": cids})
 
     @routes.post("/debug/fault")

@@ -117,6 +117,16 @@ def test_reset_score_health(server):
     assert "evicted" in ev
     s = requests.post(server + "/v1/score", json={"prompt": [5, 6, 7, 8], "continuation": [9, 10, 11]}).json()
     assert len(s["logprobs"]) == 3 and all(x <= 0 for x in s["logprobs"])
+    # the reference's request form: the same positions, with top-k alternatives
+    r = requests.post(server + "/v1/score", json={"prompt": [5, 6, 7, 8, 9, 10, 11], "continuation_start": 4,
+                                                   "top_k": 3}).json()
+    assert r["object"] == "token_scores" and r["continuation_start"] == 4 and r["prompt_tokens"] == 7
+    assert [x["token_id"] for x in r["scores"]] == [9, 10, 11]
+    for x, lp in zip(r["scores"], s["logprobs"]):
+        assert abs(x["logprob"] - lp) < 1e-4 and len(x["top_logprobs"]) == 3
+        assert x["top_logprobs"][0]["logprob"] >= x["logprob"] - 1e-6
+    bad = requests.post(server + "/v1/score", json={"prompt": [5, 6], "continuation_start": 2})
+    assert bad.status_code == 400
     assert requests.post(server + "/debug/fault", json={"name": "rope_base", "value": 10}).status_code == 404
 
 
