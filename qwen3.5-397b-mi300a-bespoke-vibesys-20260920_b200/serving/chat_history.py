@@ -31,6 +31,9 @@ class ChatHistory:
         self._recs: OrderedDict[str, tuple[list[int], list[int]]] = OrderedDict()
         self.stats: Counter = Counter()
 
+    def clear(self) -> None:
+        self._recs.clear()
+
     @staticmethod
     def key(history: list[dict], reply_text: str, options: dict) -> str:
         raw = json.dumps([history, reply_text.strip(), options], sort_keys=True, ensure_ascii=False, default=str)

@@ -338,8 +338,13 @@ def make_app(engine: Engine):
 
     @routes.post("/reset_prefix_cache")
     async def reset(_):
+        """Drop every cached prefix no request is using, and the recorded chat replies, so a
+        benchmark point cannot reuse what an earlier point sent."""
+        if not engine.healthy():
+            return web.json_response({"error": {"message": "not ready"}}, status=503)
         n = await asyncio.get_running_loop().run_in_executor(None, engine.sched.reset_prefix_cache)
-        return web.json_response({"evicted": n})
+        engine.history.clear()
+        return web.json_response({"status": "ok", "cleared_slots": n, "evicted": n})
 
     @routes.post("/v1/score")
     async def score(request):

@@ -114,7 +114,7 @@ def test_reset_score_health(server):
     assert requests.get(server + "/health").status_code == 200
     assert requests.get(server + "/v1/models").json()["data"]
     ev = requests.post(server + "/reset_prefix_cache").json()
-    assert "evicted" in ev
+    assert "evicted" in ev and ev["status"] == "ok" and "cleared_slots" in ev
     s = requests.post(server + "/v1/score", json={"prompt": [5, 6, 7, 8], "continuation": [9, 10, 11]}).json()
     assert len(s["logprobs"]) == 3 and all(x <= 0 for x in s["logprobs"])
     # the reference's request form: the same positions, with top-k alternatives
