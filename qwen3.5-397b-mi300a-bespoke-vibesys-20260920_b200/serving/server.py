@@ -332,8 +332,21 @@ def make_app(engine: Engine):
         body = await request.json()
         prompt = body.get("prompt")
         if isinstance(prompt, list) and prompt and isinstance(prompt[0], list):
+            if len(prompt) != 1:
+                return web.json_response({"error": "one prompt per request (no batches)"}, status=400)
             prompt = prompt[0]
-        ids = [int(x) for x in prompt] if isinstance(prompt, list) else engine.tok.encode(str(prompt))
+        if isinstance(prompt, list):
+            if not all(isinstance(x, int) and not isinstance(x, bool) for x in prompt):
+                return web.json_response({"error": "prompt must be an array of integer token ids (one prompt)"},
+                                         status=400)
+            ids = list(prompt)
+        else:
+            ids = engine.tok.encode(str(prompt or ""))
+        if not ids:
+            return web.json_response({"error": "prompt must not be empty"}, status=400)
+        if len(ids) >= engine.args.max_seq_len:
+            return web.json_response({"error": f"prompt has {len(ids)} tokens, max_seq_len is "
+                                               f"{engine.args.max_seq_len}"}, status=400)
         return await generate(request, ids, 0, False, body, chat=False)
 
     @routes.post("/reset_prefix_cache")
