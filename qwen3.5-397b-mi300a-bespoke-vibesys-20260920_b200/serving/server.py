@@ -307,7 +307,9 @@ def make_app(engine: Engine):
         if not engine.healthy():
             return web.json_response({"error": {"message": "not ready"}}, status=503)
         body = await request.json()
-        msgs = body.get("messages") or []
+        msgs = body.get("messages")
+        if not isinstance(msgs, list) or not msgs or not all(isinstance(m, dict) and "role" in m for m in msgs):
+            return web.json_response({"error": "messages must be a non-empty array of {role, content}"}, status=400)
         kw = body.get("chat_template_kwargs") or {}
         has_history = any(m.get("role") == "assistant" for m in msgs)
         eos = engine.tok.eos_token_id
@@ -319,6 +321,10 @@ def make_app(engine: Engine):
             ids, suffix = spliced
         else:
             ids, suffix = engine.tok.render_chat(msgs, enable_thinking=bool(kw.get("enable_thinking", False)))
+
+        if len(ids) >= engine.args.max_seq_len:
+            return web.json_response({"error": f"prompt has {len(ids)} tokens, max_seq_len is "
+                                               f"{engine.args.max_seq_len}"}, status=400)
 
         def remember(out_ids):
             engine.history.record(msgs, kw, engine.tok.decode(out_ids), ids, out_ids)

@@ -127,6 +127,8 @@ def test_reset_score_health(server):
         assert x["top_logprobs"][0]["logprob"] >= x["logprob"] - 1e-6
     bad = requests.post(server + "/v1/score", json={"prompt": [5, 6], "continuation_start": 2})
     assert bad.status_code == 400
+    for bad in ({}, {"messages": []}, {"messages": ["hi"]}, {"messages": [{"role": "user", "content": "x" * 100000}]}):
+        assert requests.post(server + "/v1/chat/completions", json=bad).status_code == 400, bad
     for bad_prompt in ([], [1.5, 2], [[1, 2], [3]], [7] * 100000):
         r = requests.post(server + "/v1/completions", json={"prompt": bad_prompt, "max_tokens": 2})
         assert r.status_code == 400, (bad_prompt[:3], r.status_code)
