@@ -216,7 +216,7 @@ def make_app(engine: Engine):
     async def health(_):
         if engine.healthy():
             return web.json_response({"status": "ok"})
-        return web.json_response({"status": "unavailable", "error": engine.error}, status=503)
+        return web.json_response({"status": "loading", "error": engine.error}, status=503)  # body as the reference gives it
 
     @routes.get("/v1/models")
     async def models(_):
