@@ -430,7 +430,11 @@ def make_app(engine: Engine):
             return web.json_response({"error": {"message": f"unknown fault {name}"}}, status=400)
         value = body.get("value")
         engine.sched.control(lambda: engine.runner.set_fault(name, value))
-        return web.json_response({"fault": name, "value": value})
+        m = engine.runner
+        while not hasattr(m, "fault") and hasattr(m, "model"):
+            m = m.model
+        state = {n: getattr(m, "fault", {}).get(n) for n in sorted(FAULTS)}
+        return web.json_response({"fault": name, "value": value, "faults": state})
 
     app = web.Application(client_max_size=64 * 1024 * 1024)
     app.add_routes(routes)

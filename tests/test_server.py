@@ -141,7 +141,9 @@ def test_fault_endpoint_changes_output_and_tp2_matches_tp1(tiny_dir):
     p1, u1 = start(env_extra={"QB_FAULT_ENDPOINT": "1"}, model=tiny_dir)
     try:
         base = requests.post(u1 + "/v1/completions", json={"prompt": ids, "max_tokens": 10, "ignore_eos": True}).json()
-        assert requests.post(u1 + "/debug/fault", json={"name": "drop_expert", "value": 3}).status_code == 200
+        r = requests.post(u1 + "/debug/fault", json={"name": "drop_expert", "value": 3})
+        assert r.status_code == 200 and r.json()["faults"]["drop_expert"] == 3
+        assert r.json()["faults"]["flip_causal_mask"] is None
         requests.post(u1 + "/reset_prefix_cache")
         assert requests.post(u1 + "/debug/fault", json={"name": "rope_base", "value": 10.0}).status_code == 200
         hurt = requests.post(u1 + "/v1/completions", json={"prompt": ids, "max_tokens": 10, "ignore_eos": True}).json()
