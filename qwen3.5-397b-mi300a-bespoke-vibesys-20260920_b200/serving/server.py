@@ -35,6 +35,22 @@ import torch
 from ..utils import flags
 
 
+def stop_ids(model_dir: str | None, cfg_eos: int, tok) -> frozenset[int]:
+    """Ids that end a generation: the config's eos, every ``eos_token_id`` of the checkpoint's
+    ``generation_config.json`` (chat checkpoints list the end-of-turn token there too) and the
+    tokenizer's eos."""
+    ids = {int(cfg_eos)}
+    if model_dir:
+        gen = os.path.join(model_dir, "generation_config.json")
+        if os.path.exists(gen):
+            with open(gen) as f:
+                eos = json.load(f).get("eos_token_id", [])
+            ids |= {int(eos)} if isinstance(eos, int) else {int(e) for e in eos}
+    if getattr(tok, "eos_token_id", None) is not None:
+        ids.add(int(tok.eos_token_id))
+    return frozenset(ids)
+
+
 def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--model-path", default=os.environ.get("MODEL_PATH", "tiny"))
@@ -128,6 +144,7 @@ class Engine:
         self.sched = None
         self.runner = None
         self.tok = None
+        self.stop_ids: frozenset[int] = frozenset()
         from .chat_history import ChatHistory
 
         self.history = ChatHistory()  # exact ids of the replies this server generated
@@ -154,6 +171,7 @@ class Engine:
                                    speculative=getattr(self.args, "mtp_k", 0) > 0)
             path = self.args.model_path if os.path.isdir(str(self.args.model_path)) else None
             self.tok = load_tokenizer(path, model.cfg.vocab, model.cfg.eos_token_id)
+            self.stop_ids = stop_ids(path, model.cfg.eos_token_id, self.tok)
             self.ready = True
             self.sched.run()
         except Exception as e:  # surfaced through /health
@@ -199,8 +217,7 @@ def make_app(engine: Engine):
         return q
 
     def stops(body):
-        eos = engine.tok.eos_token_id
-        return set() if body.get("ignore_eos", False) or eos is None else {int(eos)}
+        return set() if body.get("ignore_eos", False) else set(engine.stop_ids)
 
     async def stream_tokens(q, on_token):
         while True:
@@ -224,6 +241,7 @@ def make_app(engine: Engine):
 
     async def generate(request, prompt_ids, suffix_len, has_history, body, chat: bool, on_done=None):
         max_new = int(body.get("max_tokens") or body.get("max_completion_tokens") or 256)
+        max_new = max(1, min(max_new, engine.args.max_seq_len - len(prompt_ids)))  # clamped to the context
         temp = float(body.get("temperature", 0.0) or 0.0)
         stream = bool(body.get("stream", False))
         usage_opt = bool((body.get("stream_options") or {}).get("include_usage", False))
@@ -312,8 +330,7 @@ def make_app(engine: Engine):
             return web.json_response({"error": "messages must be a non-empty array of {role, content}"}, status=400)
         kw = body.get("chat_template_kwargs") or {}
         has_history = any(m.get("role") == "assistant" for m in msgs)
-        eos = engine.tok.eos_token_id
-        stop_ids = {eos} if eos is not None else set()
+        stop_ids = set(engine.stop_ids)
         if getattr(engine.tok, "template", None) is not None:
             stop_ids.add(engine.tok.template.im_end)
         spliced = engine.history.splice(engine.tok, msgs, kw, stop_ids) if has_history else None

@@ -70,3 +70,14 @@ def test_hf_tail_found_by_placeholder():
     tok.tok.apply_chat_template = lambda m, **k: _FakeHF.apply_chat_template(
         tok.tok, [{**x, "content": str(x["content"]).upper()} for x in m], **k)
     assert tok.render_tail(msgs) is None
+
+
+def test_stop_ids_from_config_generation_config_and_tokenizer(tmp_path):
+    import json
+
+    from qwen35_b200.serving.server import stop_ids
+
+    tok = ByteTokenizer(4096, 4095)
+    assert stop_ids(None, 7, tok) == {7, 4095}
+    (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [11, 12]}))
+    assert stop_ids(str(tmp_path), 7, tok) == {7, 11, 12, 4095}
