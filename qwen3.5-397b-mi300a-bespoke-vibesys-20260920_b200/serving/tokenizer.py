@@ -54,6 +54,29 @@ class HFTokenizer:
 
         self.tok = AutoTokenizer.from_pretrained(path)
         self.eos_token_id = self.tok.eos_token_id
+        self.enable_prompt_cache()
+
+    PROBES = ([{"role": "user", "content": "Hello! How are you today?"}],
+              [{"role": "system", "content": "Be brief."}, {"role": "user", "content": "2+2?"},
+               {"role": "assistant", "content": "4"}, {"role": "user", "content": "And 3+3, explained?"}])
+
+    def enable_prompt_cache(self, capacity: int = 256) -> bool:
+        """Tokenize chat prompts incrementally (``PromptCache``) if, on a few probe
+        conversations, that gives exactly the ids of full tokenization; else encode in full."""
+        self.prompts = PromptCache(self, capacity)
+        try:
+            samples = [self.tok.apply_chat_template(list(m), tokenize=False, add_generation_prompt=True)
+                       for m in self.PROBES]
+            samples += [s2 for s in samples for s2 in (s, s + "<|im_start|>user\nmore<|im_end|>\n")]
+            ok = self.prompts.selfcheck(samples)
+        except Exception:  # noqa: BLE001 - a template the probes do not fit: full encoding
+            ok = False
+        if not ok:
+            self.prompts = None
+        return ok
+
+    def encode_prompt(self, text: str) -> list[int]:
+        return self.prompts.encode(text) if getattr(self, "prompts", None) is not None else self.encode(text)
 
     def encode(self, text: str) -> list[int]:
         return self.tok.encode(text, add_special_tokens=False)
@@ -92,7 +115,7 @@ class HFTokenizer:
     def render_chat(self, messages: list[dict], enable_thinking: bool = False) -> tuple[list[int], int]:
         text = self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=True,
                                             enable_thinking=enable_thinking)
-        ids = self.encode(text)
+        ids = self.encode_prompt(text)
         suffix = 0
         if not enable_thinking:
             bare = self.tok.apply_chat_template(messages, tokenize=False, add_generation_prompt=True,

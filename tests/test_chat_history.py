@@ -81,3 +81,24 @@ def test_stop_ids_from_config_generation_config_and_tokenizer(tmp_path):
     assert stop_ids(None, 7, tok) == {7, 4095}
     (tmp_path / "generation_config.json").write_text(json.dumps({"eos_token_id": [11, 12]}))
     assert stop_ids(str(tmp_path), 7, tok) == {7, 11, 12, 4095}
+
+
+def test_hf_prompts_tokenized_incrementally_after_selfcheck():
+    tok = object.__new__(HFTokenizer)
+    tok.tok = _FakeHF()
+    tok.eos_token_id = None
+    assert tok.enable_prompt_cache()
+    msgs = [{"role": "user", "content": "hi"}, {"role": "assistant", "content": "hello"},
+            {"role": "user", "content": "more"}]
+    ids, _ = tok.render_chat(msgs)
+    full = tok.encode(tok.tok.apply_chat_template(msgs, tokenize=False, add_generation_prompt=True))
+    assert ids == full and tok.prompts.entries  # the prefix up to the last turn end is cached
+
+    class _Merging(_FakeHF):  # an encoder whose ids depend on text before the boundary
+        def encode(self, text, add_special_tokens=False):
+            return [len(text)] + [ord(c) for c in text]
+
+    tok.tok = _Merging()
+    assert not tok.enable_prompt_cache() and tok.prompts is None
+    assert tok.render_chat(msgs)[0] == tok.encode(tok.tok.apply_chat_template(msgs, tokenize=False,
+                                                                               add_generation_prompt=True))
