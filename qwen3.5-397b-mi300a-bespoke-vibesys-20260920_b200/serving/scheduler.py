@@ -234,6 +234,7 @@ class Scheduler:
                                f"context limit {self.runner.max_seq}"))
             return True
         node = self.cache.lookup(req.prompt)
+        self.cache.classify(req.prompt, node)  # counted in cache.admissions (diagnostics)
         lane = self.free_lanes[-1]
         protect = [node] + self._live_parents()
         try:

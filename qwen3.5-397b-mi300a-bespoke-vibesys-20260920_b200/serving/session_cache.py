@@ -26,6 +26,7 @@ Reference behaviour: ``session_cache.py:1-614`` (``Node``, ``SessionCache.lookup
 from __future__ import annotations
 
 import itertools
+from collections import Counter, OrderedDict
 from collections.abc import Sequence
 from dataclasses import dataclass, field
 
@@ -45,6 +46,7 @@ class Node:
     snapshot: int
     children: dict[int, list[Node]] = field(default_factory=dict)
     used: int = 0
+    reclaimed: bool = False  # its snapshot was taken back to free a slot
     adopted: bool = False
     superseded: bool = False
 
@@ -82,6 +84,9 @@ class SessionCache:
         self.reclaims = 0
         self.hits = 0
         self.misses = 0
+        self.admissions: Counter = Counter()  # classify() results
+        self._evicted: OrderedDict = OrderedDict()  # (first tokens, depth) of evicted boundaries, LRU
+        self._evicted_by_key: dict[tuple, dict[int, int]] = {}  # first tokens -> depth -> path hash
 
     # ------------------------------------------------------------------ lookup
     def _walk(self, prompt: Sequence[int]):
@@ -120,12 +125,51 @@ class SessionCache:
             last = n
         return last
 
+    EVICTED_INDEX = 4096  # remembered evicted boundaries (diagnostics only)
+    EVICTED_KEY = 16  # leading tokens that bucket them
+
+    def _note_evicted(self, node: Node) -> None:
+        """Remember that a boundary with state at ``node`` was evicted (for ``classify``)."""
+        edges = []
+        n = node
+        while n is not None and not n.is_root():
+            edges.append(n.edge)
+            n = n.parent
+        path = tuple(t for e in reversed(edges) for t in e)
+        if len(path) < self.EVICTED_KEY:
+            return
+        ent = (path[: self.EVICTED_KEY], node.depth)
+        self._evicted[ent] = None
+        self._evicted.move_to_end(ent)
+        self._evicted_by_key.setdefault(ent[0], {})[node.depth] = hash(path)
+        while len(self._evicted) > self.EVICTED_INDEX:
+            (k, d), _ = self._evicted.popitem(last=False)
+            by_depth = self._evicted_by_key[k]
+            by_depth.pop(d, None)
+            if not by_depth:
+                del self._evicted_by_key[k]
+
     def classify(self, prompt: Sequence[int], node: Node) -> str:
-        if node.is_root():
-            return "miss"
-        if node.depth == len(prompt):
-            return "exact"
-        return "hit"
+        """Why an admission of ``prompt`` resumes at ``node`` (from ``lookup``), for the cache
+        statistics: ``exact`` / ``hit`` (nothing deeper was cached that this cache remembers),
+        ``short_reclaimed`` / ``miss_reclaimed`` (a deeper boundary matches but its snapshot was
+        reclaimed), ``short_evicted`` / ``miss_evicted`` (a deeper boundary matching the prompt
+        was evicted), ``miss_cold`` (nothing matches, now or before). Reference behaviour:
+        ``session_cache.py:209-227`` (``classify``)."""
+        kind = "miss" if node.is_root() else "short"
+        if any(n.reclaimed and n.depth > node.depth for n in self._walk(prompt)):
+            cls = kind + "_reclaimed"
+        else:
+            cls = None
+            by_depth = self._evicted_by_key.get(tuple(prompt[: self.EVICTED_KEY]), {})
+            for d, digest in by_depth.items():
+                if node.depth < d <= len(prompt) and hash(tuple(prompt[:d])) == digest:
+                    cls = kind + "_evicted"
+                    break
+            if cls is None:
+                cls = "miss_cold" if node.is_root() else ("exact" if node.depth == len(prompt) else "hit")
+        self.admissions[cls] += 1
+        return cls
 
     # ------------------------------------------------------------------ adoption
     def needs_cow(self, node: Node) -> bool:
@@ -182,7 +226,7 @@ class SessionCache:
         nb = blocks_for(depth, self.block_size)
         if parent.depth == depth and not parent.is_root():
             if parent.snapshot < 0:
-                parent.snapshot = snapshot
+                parent.snapshot, parent.reclaimed = snapshot, False
             else:
                 self.release_snapshot(snapshot)
             self._touch(parent)
@@ -239,6 +283,7 @@ class SessionCache:
         victim = min(cands, key=lambda n: n.used)
         self.release_snapshot(victim.snapshot)
         victim.snapshot = -1
+        victim.reclaimed = True
         self.reclaims += 1
         return True
 
@@ -251,6 +296,7 @@ class SessionCache:
                 del parent.children[node.edge[0]]
             self.alloc.decref(node.blocks)
             if node.snapshot >= 0:
+                self._note_evicted(node)
                 self.release_snapshot(node.snapshot)
             node = parent if (parent is not None and not parent.is_root() and parent.snapshot < 0) else None
 

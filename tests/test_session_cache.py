@@ -65,3 +65,25 @@ def test_evict_all_respects_protect():
     c.publish([3] * 8, 8, b2, c.reserve_snapshot())
     assert c.evict_all(protect=[n]) == 1
     assert c.node_count() == 1
+
+
+def test_classify_cold_hit_evicted_reclaimed():
+    c = mk(blocks=12, bs=4, snaps=8)
+    p1 = list(range(100, 120))
+    assert c.classify(p1, c.lookup(p1)) == "miss_cold"
+    b = c.reserve_blocks(5)
+    c.publish(p1, 20, b, c.reserve_snapshot())
+    c.release_lane_blocks(b)
+    assert c.classify(p1 + [1, 2], c.lookup(p1 + [1, 2])) == "hit"
+    assert c.classify(p1, c.lookup(p1)) == "exact"
+    c.evict_all()
+    assert c.classify(p1 + [1], c.lookup(p1 + [1])) == "miss_evicted"
+    assert c.classify(list(range(300, 330)), c.root) == "miss_cold"
+    # a deeper boundary whose snapshot was reclaimed
+    b = c.reserve_blocks(5)
+    n = c.publish(p1, 20, b, c.reserve_snapshot())
+    c.release_lane_blocks(b)
+    c.release_snapshot(n.snapshot)
+    n.snapshot, n.reclaimed = -1, True  # as _reclaim_one_internal leaves a node
+    assert c.classify(p1 + [3], c.lookup(p1 + [3])) == "miss_reclaimed"
+    assert c.admissions["miss_cold"] == 2 and c.admissions["hit"] == 1
