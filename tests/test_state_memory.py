@@ -38,6 +38,7 @@ def test_no_block_or_snapshot_leaks_over_many_turns():
     assert len(s.free_lanes) == 4
     st = cache.stats()
     assert st.evictions > 0 and st.hits > 0  # the pools were tight and the cache was used
+    assert sum(st.admissions.values()) == 12 * 20 and st.admissions.get("miss_cold", 0) >= 12
     cache.evict_all()
     assert alloc.free_count() == blocks - 1
     assert cache.free_snapshot_count() == snaps
