@@ -3,23 +3,30 @@
 synthetic multi-turn chat workload, full Qwen3.5-397B-A17B geometry, random-init weights.
 
     python bench.py --gpus N --steps K --warmup W            # N=1 directly, N>1 under torchrun
+    python bench.py --impl reference --gpus N ...            # the reference engine, same workload
 
 One process per GPU (tensor + expert parallel over N). Rank 0 runs the scheduler and the
 closed-loop client; the other ranks mirror every model call (``parallel.driver``). Phases:
 
-1. setup (untimed): the first ``concurrency`` sessions run their opening turn (2000-8000-token
-   prompt, 200-500 generated tokens), which fills the session cache;
-2. ``W`` warm-up scheduler steps of the closed loop (turns >= 2 start here);
-3. ``K`` timed scheduler steps, bracketed by a barrier and ``torch.cuda.synchronize()`` on every
-   rank; every step is also bracketed by CUDA events on rank 0.
+1. warm-up (untimed): ``W`` scheduler steps of a short side workload with its own seed (both
+   step kinds, every kernel and captured graph touched), drained, then its cache entries evicted;
+2. the timed closed loop: ALL ``sessions`` x ``turns`` turns of the workload (256 x 6 by
+   default: turn 1 = 2000-8000 random ids, each later turn appends 200-1000 ids to the full
+   history, 200-500 greedy tokens per turn, EOS ignored, no think time, seed 0), from the first
+   submission to the last token, bracketed by a barrier + ``torch.cuda.synchronize()`` on every
+   rank. The window is reported as ``K`` equal steps (``steps x ms_per_step`` = the whole timed
+   loop; ``scheduler_steps`` gives the number of model steps inside it).
 
-``value`` = p95 TTFT of turns >= 2 whose first token landed in the timed window, device-timed:
-the sum, over the steps from the one that admitted the request to the one that produced its
-first token, of each step's device interval (CUDA event at the step's first input upload to the
-event just before its last result read). ``e2e`` = the same metric on the host clock through the
-public ``Scheduler.submit`` API: it also counts the host's scheduling work between steps (every
-step copies its inputs host->device from pinned memory and reads the sampled ids back). The weights stream from HBM every step (far larger than L2), so no
-extra L2 flush is needed between steps.
+``value`` = p95 TTFT over EVERY turn >= 2 of the loop (no survivorship filter: the loop runs
+until each has finished), device-timed: for each turn, the sum over the scheduler steps from the
+one that admitted it to the one that produced its first token of each step's device interval
+(CUDA event at the step's first input upload to the event just before its last result read);
+host gaps between steps are excluded. Fewer than 200 samples give no value. ``decode_tok_s`` =
+every token generated in the loop (each counted once, when emitted) / the loop's device window
+(max over ranks). ``e2e`` = the same two metrics on the host clock through the public
+``Scheduler.submit`` API: every step copies its inputs host->device from pinned memory and reads
+the sampled ids back (bytes per reported step in ``h2d_bytes_per_step`` / ``d2h_bytes_per_step``).
+The weights stream from HBM every step (far larger than L2), so no extra L2 flush is needed.
 """
 
 from __future__ import annotations
@@ -37,13 +44,14 @@ sys.path.insert(0, ROOT)
 
 METRIC = "p95 TTFT turns>=2 (ms), multi-turn chat"
 BASELINE_MS = None  # the reference publishes no like-for-like B200 number for this workload
+MIN_SAMPLES = 200
 
 
-def parse():
+def parse(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=300)
-    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=20, help="the timed loop is reported as this many equal steps")
+    ap.add_argument("--warmup", type=int, default=5, help="untimed scheduler steps of the warm-up workload")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--model", default="full", choices=["full", "tiny"])
     ap.add_argument("--concurrency", type=int, default=32)
@@ -52,20 +60,14 @@ def parse():
     ap.add_argument("--max-seq", type=int, default=16384)
     ap.add_argument("--prefill-chunk", type=int, default=2048)
     ap.add_argument("--token-budget", type=int, default=2048)
+    ap.add_argument("--mixed", type=int, default=None, help="decode steps carry prefill chunks (default: flag QB_MIXED)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--first-len", type=int, nargs=2, default=(2000, 8000))
     ap.add_argument("--user-len", type=int, nargs=2, default=(200, 1000))
     ap.add_argument("--gen-len", type=int, nargs=2, default=(200, 500))
+    ap.add_argument("--max-seconds", type=float, default=1500.0, help="safety stop of the timed loop (host clock)")
     ap.add_argument("--out", default=None)
-    return ap.parse_args()
-
-
-def reference_unavailable(args) -> None:
-    rank = int(os.environ.get("RANK", "0"))
-    if rank == 0:
-        print(json.dumps({"impl": "reference", "unavailable":
-                          "the reference tree has no setup.py/pyproject.toml, so installing it with pip "
-                          "into baseline/_ref fails (not installable)"}))
+    return ap.parse_args(argv)
 
 
 class ClockSampler:
@@ -99,29 +101,36 @@ class ClockSampler:
                 self.proc.wait(timeout=5)
             except Exception:
                 self.proc.kill()
-        sm, mx, reasons = [], 0.0, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                idx = int(parts[0])
-            except ValueError:
-                continue
-            if idx not in self.gpus:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = max(mx, float(parts[2]))
-            except ValueError:
-                pass
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        sm.sort()
-        return {"sm_mhz": sm[len(sm) // 2] if sm else None, "sm_max_mhz": mx or None, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        return summarize_clocks(self.lines, self.gpus)
+
+
+def summarize_clocks(lines, gpus) -> dict:
+    """Median SM clock over the samples taken under load (power above 300 W, or all samples when
+    none is), the max clock, and every throttle reason seen active."""
+    rows, mx, reasons = [], 0.0, set()
+    names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+    for ln in lines:
+        parts = [p.strip() for p in ln.split(",")]
+        if len(parts) < 9:
+            continue
+        try:
+            idx = int(parts[0])
+        except ValueError:
+            continue
+        if idx not in gpus:
+            continue
+        try:
+            sm, power = float(parts[1]), float(parts[3])
+            mx = max(mx, float(parts[2]))
+        except ValueError:
+            continue
+        rows.append((sm, power))
+        for n, v in zip(names, parts[5:9]):
+            if v.lower() == "active":
+                reasons.add(n)
+    loaded = sorted(s for s, p in rows if p > 300.0) or sorted(s for s, _ in rows)
+    return {"sm_mhz": loaded[len(loaded) // 2] if loaded else None, "sm_max_mhz": mx or None,
+            "reasons": sorted(reasons), "samples": len(rows), "samples_under_load": len(loaded)}
 
 
 def _elapsed_ms(a, b) -> float:
@@ -129,6 +138,94 @@ def _elapsed_ms(a, b) -> float:
     if isinstance(a, float):
         return (b - a) * 1e3
     return a.elapsed_time(b)
+
+
+def ttft_lists(records, step_ms, first_turn: int = 1):
+    """Device and host TTFT (ms) of every turn >= ``first_turn + 1`` that produced a first token.
+    ``step_ms[i]`` = device ms of scheduler step ``i`` of the timed loop (``None`` when the step
+    had no device work); a turn's device TTFT sums the steps from its admission to its first
+    token. Returns ``(device, host, missing)``; ``missing`` counts turns with no first token."""
+    prefix = [0.0]
+    for v in step_ms:
+        prefix.append(prefix[-1] + (v or 0.0))
+    dev, host, missing = [], [], 0
+    for r in records:
+        if r.turn < first_turn:
+            continue
+        if r.first_step < 0:
+            missing += 1
+            continue
+        i0, i1 = r.submit_step, r.first_step
+        dev.append(prefix[min(i1 + 1, len(step_ms))] - prefix[min(i0, len(step_ms))])
+        host.append((r.t_first - r.t_submit) * 1e3)
+    return dev, host, missing
+
+
+def report(args, *, impl, world, window_ms, host_s, records, step_ms, kinds_summary, clocks, h2d, d2h,
+           launches, sched_steps, boot_s, warm_s, cfg_desc, expert_storage, extra=None) -> dict:
+    """The benchmark's JSON line (shared by both arms)."""
+    from qwen35_b200.serving.workload import percentile
+
+    dev, host, missing = ttft_lists(records, step_ms)
+    samples = dev if any(v is not None for v in step_ms) and dev else host
+    gen = sum(r.generated for r in records)
+    turns_total = args.sessions * args.turns
+    done = sum(1 for r in records if r.end_step >= 0 and r.error is None)
+    ok = len(samples) >= MIN_SAMPLES
+    K = max(1, args.steps)
+    res = {
+        "metric": METRIC,
+        "value": round(percentile(samples, 95), 2) if ok else None,
+        "unit": "ms",
+        "n_gpus": world,
+        "steps": K,
+        "warmup": args.warmup,
+        "ms_per_step": round(window_ms / K, 3),
+        "higher_is_better": False,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (random token ids, random-init weights)",
+        "impl": impl,
+        "config": {
+            "model": cfg_desc,
+            "global_batch": args.concurrency, "seq_len": args.max_seq,
+            "parallelism": f"tp{world}+ep{world}",
+            "workload": f"{args.sessions} sessions, C{args.concurrency}, {args.turns} turns, first "
+                        f"{args.first_len[0]}-{args.first_len[1]}, user {args.user_len[0]}-{args.user_len[1]}, "
+                        f"gen {args.gen_len[0]}-{args.gen_len[1]}, seed {args.seed}, EOS ignored, no think time",
+            "expert_storage": expert_storage,
+            "l2": "no flush: every step streams the weights (>> 126 MB L2)",
+            "step": "the whole timed closed loop split into `steps` equal parts (steps x ms_per_step = loop window)",
+        },
+        "ttft_samples": len(samples),
+        "ttft_missing": missing,
+        "p50_ttft_ms": round(percentile(samples, 50), 2) if samples else None,
+        "p99_ttft_ms": round(percentile(samples, 99), 2) if samples else None,
+        "decode_tok_s": round(gen / (window_ms / 1e3), 1) if window_ms else None,
+        "tokens_generated": gen,
+        "turns_done": done,
+        "turns_total": turns_total,
+        "clocks": clocks,
+        "e2e": {"value": round(percentile(host, 95), 2) if len(host) >= MIN_SAMPLES else None,
+                "unit": "ms (p95 TTFT turns>=2, host clock, Scheduler.submit API)",
+                "p50": round(percentile(host, 50), 2) if host else None,
+                "h2d_bytes_per_step": int(h2d / K), "d2h_bytes_per_step": int(d2h / K),
+                "decode_tok_s": round(gen / host_s, 1) if host_s else None},
+        "gpu_launches": int(launches),
+        "scheduler_steps": sched_steps,
+        "loop_s": round(window_ms / 1e3, 2),
+        "boot_s": round(boot_s, 1),
+        "warmup_s": round(warm_s, 1),
+        "step_kinds": kinds_summary,
+    }
+    if not ok:
+        res["invalid"] = f"only {len(samples)} turn>=2 samples (< {MIN_SAMPLES}): no value"
+    if done < turns_total:
+        res["incomplete"] = f"{done} of {turns_total} turns finished"
+    if extra:
+        res.update(extra)
+    return res
 
 
 def build_model(args, rank, world, device):
@@ -142,11 +239,14 @@ def build_model(args, rank, world, device):
     return runner.cfg, runner, distinct
 
 
-def main():
-    args = parse()
-    if args.impl == "reference":
-        reference_unavailable(args)
-        return
+def warmup_spec(args, vocab):
+    from qwen35_b200.serving.workload import ChatSpec
+
+    return ChatSpec(sessions=min(4, args.concurrency), concurrency=min(4, args.concurrency), turns=2,
+                    seed=args.seed + 7919, vocab=vocab, first_len=(256, 1024), user_len=(64, 256), gen_len=(24, 48))
+
+
+def main_ours(args):
     import torch
     import torch.distributed as dist
 
@@ -156,7 +256,8 @@ def main():
     from qwen35_b200.serving.block_pool import BlockAllocator
     from qwen35_b200.serving.scheduler import Scheduler
     from qwen35_b200.serving.session_cache import SessionCache
-    from qwen35_b200.serving.workload import ChatSpec, ClosedLoop, percentile
+    from qwen35_b200.serving.workload import ChatSpec, ClosedLoop
+    from qwen35_b200.utils import flags
 
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     if world_env != args.gpus:
@@ -206,25 +307,22 @@ def main():
     runner = Broadcaster(model, channel)
     alloc = BlockAllocator(model.num_blocks, model.block_size)  # the runner's max_batch excludes the pad lane
     cache = SessionCache(alloc, model.block_size, model.num_snapshots)
-    sched = Scheduler(runner, cache, prefill_chunk=args.prefill_chunk, token_budget=args.token_budget)
-    spec = ChatSpec(sessions=args.sessions, concurrency=args.concurrency, turns=args.turns, seed=args.seed,
-                    vocab=min(151000, cfg.vocab - 16), first_len=tuple(args.first_len),
-                    user_len=tuple(args.user_len), gen_len=tuple(args.gen_len))
-    step_no = [0]
-    loop = ClosedLoop(sched, spec, step_index=lambda: step_no[0])
-
+    mixed = bool(flags.get("QB_MIXED")) if args.mixed is None else bool(args.mixed)
+    sched = Scheduler(runner, cache, prefill_chunk=args.prefill_chunk, token_budget=args.token_budget, mixed=mixed)
+    vocab = min(151000, cfg.vocab - 16)
     inner = getattr(model, "model", model)  # the Model under a GraphRunner
+    on_gpu = device.type == "cuda"
+    step_no = [0]
 
-    def one_step(events=None):
-        """One scheduler step. With ``events``, append the step's device interval: from the
+    def one_step(loop, step_ms=None):
+        """One scheduler step. With ``step_ms``, append the step's device interval (ms): from the
         event at its first input upload to the event before its last result read (or, for a
-        step that reads nothing back, an event after its last launch); host gaps between steps
-        are outside every interval."""
-        if events is not None:
+        step that reads nothing back, an event after its last launch); ``None`` when the step
+        launched nothing. Host gaps between steps are outside every interval."""
+        if step_ms is not None:
             inner.gpu_marks = []
-            sched.timer.last_kind = None
         sched.step()
-        if events is not None:
+        if step_ms is not None:
             marks = inner.gpu_marks
             inner.gpu_marks = None
             end = torch.cuda.Event(enable_timing=True)
@@ -232,30 +330,30 @@ def main():
             first_in = next((ev for tag, ev in marks if tag == "in"), None)
             last_in = max((i for i, (tag, _) in enumerate(marks) if tag == "in"), default=-1)
             outs = [ev for i, (tag, ev) in enumerate(marks) if tag == "out" and i > last_in]
-            events.append((first_in, outs[-1] if outs else end) if first_in is not None else None)
-            kinds.append(sched.timer.last_kind)
+            step_ms.append((first_in, outs[-1] if outs else end) if first_in is not None else None)
         step_no[0] += 1
         loop.pump()
 
-    # ---- setup: opening turns of the first `concurrency` sessions
+    # ---- warm-up: a short side workload (own seed), W steps and drained, then its cache evicted
     t0 = time.perf_counter()
-    loop.start()
-    first_wave = set(range(min(args.concurrency, args.sessions)))
-    last_log = time.perf_counter()
-    while any(r.turn == 0 and r.session in first_wave and r.end_step < 0 for r in loop.records):
-        one_step()
-        if time.perf_counter() - last_log > 15:
-            last_log = time.perf_counter()
-            done = sum(1 for r in loop.records if r.turn == 0 and r.end_step >= 0)
-            print(f"[bench] setup step {step_no[0]}: {done}/{len(first_wave)} opening turns done, "
-                  f"{sched.timer.summary()}", file=sys.stderr, flush=True)
-    setup_s = time.perf_counter() - t0
-    print(f"[bench] setup done in {setup_s:.1f}s ({step_no[0]} steps)", file=sys.stderr, flush=True)
-    # ---- warm-up
-    for _ in range(args.warmup):
-        one_step()
-    # ---- timed window
-    launches0 = _ext.ext().launches() if device.type == "cuda" else 0
+    wloop = ClosedLoop(sched, warmup_spec(args, vocab), step_index=lambda: step_no[0])
+    wloop.start()
+    n_warm = 0
+    while n_warm < max(args.warmup, 3) or wloop.active:
+        one_step(wloop)
+        n_warm += 1
+    sched.cache.evict_all([])
+    warm_s = time.perf_counter() - t0
+    print(f"[bench] warm-up: {n_warm} steps in {warm_s:.1f}s", file=sys.stderr, flush=True)
+
+    # ---- the timed closed loop
+    spec = ChatSpec(sessions=args.sessions, concurrency=args.concurrency, turns=args.turns, seed=args.seed,
+                    vocab=vocab, first_len=tuple(args.first_len), user_len=tuple(args.user_len),
+                    gen_len=tuple(args.gen_len))
+    step_no[0] = 0
+    loop = ClosedLoop(sched, spec, step_index=lambda: step_no[0])
+    sched.timer = type(sched.timer)()  # step kinds of the timed loop only
+    launches0 = _ext.ext().launches() if on_gpu else 0
     h2d0, d2h0 = model.io_bytes()
     cvd = os.environ.get("CUDA_VISIBLE_DEVICES", "")
     phys = [int(x) for x in cvd.split(",") if x.strip().isdigit()] if cvd else list(range(8))
@@ -264,20 +362,24 @@ def main():
     if world > 1:
         channel.send(Op.CALL, ("bench_mark", ("start",), {}))
     ev_start = mark("start")
-    step0 = step_no[0]
     t_host0 = time.perf_counter()
-    events, kinds = [], []
-    gen0 = sum(r.generated for r in loop.records if r.end_step >= 0)
-    for _ in range(args.steps):
-        one_step(events if device.type == "cuda" else None)
+    marks: list = []
+    loop.start()
+    last_log = t_host0
+    while loop.active and time.perf_counter() - t_host0 < args.max_seconds:
+        one_step(loop, marks if on_gpu else None)
+        if time.perf_counter() - last_log > 30:
+            last_log = time.perf_counter()
+            done = sum(1 for r in loop.records if r.end_step >= 0)
+            print(f"[bench] {time.perf_counter() - t_host0:.0f}s step {step_no[0]}: {done} turns done, "
+                  f"{loop.finished_sessions} sessions", file=sys.stderr, flush=True)
     if world > 1:
         channel.send(Op.CALL, ("bench_mark", ("end",), {}))
     ev_end = mark("end")
     t_host1 = time.perf_counter()
     clk = clocks.stop()
-    launches = (_ext.ext().launches() - launches0) if device.type == "cuda" else 0
+    launches = (_ext.ext().launches() - launches0) if on_gpu else 0
     h2d1, d2h1 = model.io_bytes()
-    step1 = step_no[0]
     window_ms = _elapsed_ms(ev_start, ev_end)
     if world > 1:
         runner.shutdown()
@@ -286,66 +388,20 @@ def main():
         gathered = [None] * world
         dist.all_gather_object(gathered, window_ms)
         window_ms = max(gathered)
-    # ---- metrics
-    ttft_dev, ttft_host, tokens_in_window = [], [], 0
-    for r in loop.records:
-        if r.turn >= 1 and r.submit_step >= step0 and 0 <= r.first_step < step1:
-            i0, i1 = r.submit_step - step0, r.first_step - step0
-            if device.type == "cuda":  # device time of the steps from admission to first token
-                ttft_dev.append(sum(ev[0].elapsed_time(ev[1]) for ev in events[i0:i1 + 1] if ev is not None))
-            ttft_host.append((r.t_first - r.t_submit) * 1e3)
-    # tokens generated inside the window: every emitted token of every turn, counted by step
-    done_now = sum(r.generated for r in loop.records if r.end_step >= 0)
-    inflight = sum(len(getattr(f, "out_ids", [])) for f in sched.decoding)
-    tokens_in_window = max(0, done_now + inflight - gen0)
-    p95_dev = percentile(ttft_dev, 95) if ttft_dev else percentile(ttft_host, 95)
+    step_ms = [ev[0].elapsed_time(ev[1]) if ev is not None else None for ev in marks] if on_gpu else \
+        [None] * step_no[0]
     by_kind: dict = {}
-    for ev, kind in zip(events, kinds):  # device time of one step, by the step's kind
-        if ev is not None and kind is not None:
-            by_kind.setdefault(kind, []).append(ev[0].elapsed_time(ev[1]))
-    device_ms_by_kind = {k: round(sum(v) / len(v), 3) for k, v in by_kind.items()}
-    n_steps = step1 - step0
-    res = {
-        "metric": METRIC,
-        "value": round(p95_dev, 2),
-        "unit": "ms",
-        "n_gpus": world,
-        "steps": n_steps,
-        "warmup": args.warmup,
-        "ms_per_step": round(window_ms / max(1, n_steps), 3),
-        "higher_is_better": False,
-        "scaling": "strong",
-        "vs_baseline": None if BASELINE_MS is None else round(p95_dev / BASELINE_MS, 3),
-        "dtype": "bf16",
-        "data": "synthetic (random token ids, random-init weights)",
-        "impl": "ours",
-        "config": {
-            "model": f"Qwen3.5-397B-A17B geometry ({cfg.layers} layers, {cfg.experts} experts MXFP4)"
-            if args.model == "full" else "tiny parity model",
-            "global_batch": args.concurrency, "seq_len": args.max_seq,
-            "parallelism": f"tp{world}+ep{world}",
-            "workload": f"{args.sessions} sessions, C{args.concurrency}, {args.turns} turns, first "
-                        f"{args.first_len[0]}-{args.first_len[1]}, user {args.user_len[0]}-{args.user_len[1]}, "
-                        f"gen {args.gen_len[0]}-{args.gen_len[1]}, seed {args.seed}",
-            "expert_storage": "all layers distinct" if distinct is None else
-            f"{distinct} distinct expert layers, the other {cfg.layers - distinct} reuse their storage "
-            f"(205 GB of MXFP4 experts exceed one GPU); per-layer work and HBM traffic unchanged",
-            "l2": "no flush: every step streams the weights (>> 126 MB L2)",
-        },
-        "ttft_samples": len(ttft_dev) or len(ttft_host),
-        "p50_ttft_ms": round(percentile(ttft_dev or ttft_host, 50), 2),
-        "decode_tok_s": round(tokens_in_window / (window_ms / 1e3), 1) if window_ms else None,
-        "clocks": clk,
-        "e2e": {"value": round(percentile(ttft_host, 95), 2), "unit": "ms (p95 TTFT turns>=2, host clock, "
-                "Scheduler.submit API)", "h2d_bytes_per_step": int((h2d1 - h2d0) / max(1, n_steps)),
-                "d2h_bytes_per_step": int((d2h1 - d2h0) / max(1, n_steps)), "decode_tok_s":
-                round(tokens_in_window / (t_host1 - t_host0), 1)},
-        "gpu_launches": int(launches),
-        "setup_s": round(setup_s, 1),
-        "boot_s": round(boot_s, 1),
-        "step_kinds": sched.timer.summary(),
-        "device_ms_per_step": device_ms_by_kind,
-    }
+    kinds = sched.timer.summary()
+    storage = "all layers distinct" if distinct is None else \
+        (f"{distinct} distinct expert layers, the other {cfg.layers - distinct} reuse their storage "
+         f"(205 GB of MXFP4 experts exceed one GPU); per-layer work and HBM traffic unchanged")
+    res = report(args, impl="ours", world=world, window_ms=window_ms, host_s=t_host1 - t_host0,
+                 records=loop.records, step_ms=step_ms, kinds_summary=kinds, clocks=clk,
+                 h2d=h2d1 - h2d0, d2h=d2h1 - d2h0, launches=launches, sched_steps=step_no[0], boot_s=boot_s,
+                 warm_s=warm_s, cfg_desc=(f"Qwen3.5-397B-A17B geometry ({cfg.layers} layers, {cfg.experts} "
+                                          f"experts MXFP4)" if args.model == "full" else "tiny parity model"),
+                 expert_storage=storage, extra={"mixed": mixed})
+    del by_kind
     line = json.dumps(res)
     print(line, flush=True)
     if args.out:
@@ -355,6 +411,17 @@ def main():
         if hasattr(model, "release"):
             model.release()
         dist.destroy_process_group()
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        sys.path.insert(0, os.path.join(ROOT, "baseline"))
+        import reference_arm
+
+        reference_arm.main(args, report)
+        return
+    main_ours(args)
 
 
 if __name__ == "__main__":

@@ -45,11 +45,11 @@ def init(backend: str | None = None, rank: int | None = None, world: int | None 
         backend = "nccl" if torch.cuda.is_available() else "gloo"
     if backend == "nccl":
         torch.cuda.set_device(local)
-        from ..utils.hostinfo import apply_for_device
+        from ..utils.affinity import pin_device
 
-        note = apply_for_device(local)  # host threads and pages next to this rank's GPU
+        note = pin_device(local)  # host threads on the CPUs next to this rank's GPU
         if note:
-            print(f"[host-numa] rank {rank}: {note}", flush=True)
+            print(f"[cpu-affinity] rank {rank}: {note}", flush=True)
     os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
     os.environ.setdefault("MASTER_PORT", "29500")
     kw = {}

@@ -18,7 +18,8 @@ from ..models.qwen35 import Model
 from ..models.weights import expert_bytes_per_layer, load_weights, random_weights
 from ..parallel.comm import Comm
 from ..parallel.plan import plan
-from ..utils import flags, memtimeline
+from ..utils import flags
+from ..utils.memreport import BootMemory, pool_plan
 
 
 @dataclass
@@ -49,10 +50,8 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
     every rank must call this in the same order, since capture runs the collectives."""
     if graphs is None:
         graphs = device.type == "cuda" and flags.get("QB_GRAPHS")
-    if device.type == "cuda":
-        memtimeline.set_rank(rank)
-        memtimeline.preflight()
-        memtimeline.mark("start", device)
+    mem = BootMemory(rank, device)
+    mem.phase("start")
     if model in ("full", "tiny"):
         cfg = full_config() if model == "full" else tiny_config()
     else:
@@ -73,7 +72,7 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
         w = random_weights(cfg, p, device, dtype, seed=seed, with_mtp=with_mtp, distinct_expert_layers=distinct)
     else:
         w = load_weights(model, cfg, p, device, dtype, with_mtp=with_mtp)
-    memtimeline.mark("weights", device)
+    mem.phase("weights")
     if comm is None:
         comm = Comm(rank, world, None, device)
         if world > 1 and device.type == "cuda" and comm.mode == "fused":
@@ -89,21 +88,18 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
     m = Model(cfg, w, p, comm, device=device, dtype=dtype,
               max_batch=spec.lanes + (1 if graphs else 0), max_seq=spec.max_seq, block_size=spec.block_size,
               num_blocks=num_blocks, num_snapshots=spec.snapshots or 2 * spec.lanes + 16)
-    memtimeline.mark("pools", device)
+    mem.phase("pools")
     if device.type == "cuda":
         from ..utils.devstatus import StatusWatch
 
         m.status_watch = StatusWatch(device, flags.get("QB_STATUS_EVERY"))
-    if device.type == "cuda" and flags.get("QB_RANK_BW_PROBE"):
-        from ..utils.hostinfo import probe
-
-        probe(rank, device)
     if graphs:
         from .graphs import GraphRunner
 
         g = GraphRunner(m)
         g.prepare()
-        memtimeline.report(g, device)
+        mem.phase("graphs")
+        pool_plan(m, rank)
         return g, distinct
-    memtimeline.report(m, device)
+    pool_plan(m, rank)
     return m, distinct

@@ -56,6 +56,7 @@ _def("QB_DN_DECODE", str, "", "DeltaNet decode mixer state path: reg (registers)
 _def("QB_DN_CHUNKED", bool, False, "chunked (WY) DeltaNet prefill instead of the token recurrence",
      lockstep=True)
 _def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
+_def("QB_MIXED", bool, False, "scheduler: decode steps also carry prefill chunks in the same forward")
 # ---- collectives and multi-rank plumbing
 _def("QB_COMM", str, "fused", "tensor-parallel all-reduce: fused (peer-memory kernels) or nccl", lockstep=True)
 _def("QB_SYMM_MAX_ROWS", int, 512, "rows of the one-shot fused all-reduce buffers", lockstep=True)
@@ -71,14 +72,12 @@ _def("QB_STATUS_EVERY", int, 64, "read the kernels' device status word every n m
 _def("QB_STEP_TIMING", int, 0, "log a [step-timing] line every n scheduler steps (0: off)")
 _def("QB_SERVICE_TRACE", str, "", "append one JSON record per scheduler step to this path")
 _def("QB_STAMPS", bool, False, "in-graph %globaltimer stamps at layer boundaries")
-_def("QB_MEM_TIMELINE", bool, False, "print a [mem] line at each boot phase and a [mem-cls] report")
-_def("QB_MEM_TIMELINE_DIR", str, "", "also write every allocator segment of the timeline as JSON here")
-_def("QB_BOOT_MEM_PREFLIGHT_GIB", float, 0.0, "before boot, wait until the device has this much free memory")
-_def("QB_BOOT_MEM_PREFLIGHT_WAIT_S", float, 300.0, "how long the preflight waits before it fails")
-_def("QB_RANK_BW_PROBE", bool, False, "print a [rank-bw] line (HBM read and pinned copy bandwidth) at boot",
-     lockstep=True)
-_def("QB_HOST_CPU_NODES", str, "", "run this process's threads on these NUMA nodes' CPUs (auto: the GPU's node)")
-_def("QB_HOST_MEM_NODES", str, "", "interleave this process's host pages over these NUMA nodes (auto: the GPU's)")
+_def("QB_MEM_REPORT", bool, False, "print a [mem] line at each boot phase and a [pool-plan] line (bytes per "
+     "static pool)")
+_def("QB_CPU_AFFINITY", bool, False, "restrict each rank's host threads to the CPUs local to its GPU (sysfs "
+     "local_cpulist)")
+_def("QB_CACHE_STATS", int, 0, "log a [cache-stats] line (session-cache admissions, hit tokens) every n finished "
+     "requests (0: off)")
 _def("QB_FAULT_ENDPOINT", bool, False, "expose POST /debug/fault (accuracy-gate calibration faults)")
 
 

@@ -1,4 +1,4 @@
-"""Flag registry, host NUMA placement, memory preflight and clock stamps (CPU parts)."""
+"""Flag registry, GPU-local CPU affinity, the boot memory report and clock stamps (CPU parts)."""
 
 import re
 from pathlib import Path
@@ -6,7 +6,7 @@ from pathlib import Path
 import pytest
 import torch
 
-from qwen35_b200.utils import flags, hostinfo, memtimeline
+from qwen35_b200.utils import affinity, flags, memreport
 from qwen35_b200.utils.telemetry import Stamps
 
 PKG = Path(__file__).resolve().parent.parent / "qwen3.5-397b-mi300a-bespoke-vibesys-20260920_b200"
@@ -54,69 +54,50 @@ def test_flag_parsing_and_signature():
     assert "QB_MOE_IMPL" in flags.describe()
 
 
-def test_parse_nodes_and_node_cpus(tmp_path):
-    assert hostinfo.parse_nodes("") == []
-    assert hostinfo.parse_nodes("1,2,3") == [1, 2, 3]
-    assert hostinfo.parse_nodes("3,1-2, 2") == [1, 2, 3]
-    (tmp_path / "node1").mkdir()
-    (tmp_path / "node1" / "cpulist").write_text("24-26,120\n")
-    assert hostinfo.node_cpus(1, root=tmp_path) == {24, 25, 26, 120}
+def test_parse_cpulist():
+    assert affinity.parse_cpulist("") == set()
+    assert affinity.parse_cpulist("0-3,8,10-11\n") == {0, 1, 2, 3, 8, 10, 11}
+    with pytest.raises(ValueError):
+        affinity.parse_cpulist("5-2")
 
 
-def test_gpu_numa_node_from_sysfs(tmp_path):
+def test_gpu_local_cpus_from_sysfs(tmp_path):
     d = tmp_path / "0000:1b:00.0"
     d.mkdir()
-    (d / "numa_node").write_text("1\n")
-    assert hostinfo.gpu_numa_node("0000:1B:00.0", root=tmp_path) == 1
-    assert hostinfo.gpu_numa_node("0000:99:00.0", root=tmp_path) == -1
+    (d / "local_cpulist").write_text("24-26,120\n")
+    # CUDA's bus id form (8-digit domain, upper case) maps to the sysfs name
+    assert affinity.gpu_local_cpus("00000000:1B:00.0", root=str(tmp_path)) == {24, 25, 26, 120}
+    assert affinity.gpu_local_cpus("00000000:99:00.0", root=str(tmp_path)) == set()
 
 
-def test_apply_placement_with_fakes(tmp_path):
-    for n, cpus in ((0, "0-3"), (1, "4-7")):
-        (tmp_path / f"node{n}").mkdir()
-        (tmp_path / f"node{n}" / "cpulist").write_text(cpus)
-    calls = {}
-
-    def aff(pid, cpus):
-        calls["cpus"] = cpus
-
-    def pol(nodes):
-        calls["mem"] = nodes
-
-    assert hostinfo.apply({}, 1, tmp_path, aff, pol) == ""
-    assert not calls
-    note = hostinfo.apply({"QB_HOST_CPU_NODES": "auto", "QB_HOST_MEM_NODES": "auto"}, 1, tmp_path, aff, pol)
-    assert calls == {"cpus": {4, 5, 6, 7}, "mem": [1]} and "mem_bind=[1]" in note
+def test_pin_to_gpu_with_fakes(tmp_path):
+    d = tmp_path / "0000:1b:00.0"
+    d.mkdir()
+    (d / "local_cpulist").write_text("4-7")
+    calls = []
+    allowed = {0, 1, 2, 3, 4, 5}
+    kw = dict(root=str(tmp_path), setter=calls.append, getter=lambda: allowed)
+    assert affinity.pin_to_gpu("00000000:1B:00.0", {}, **kw) == "" and not calls  # off by default
+    note = affinity.pin_to_gpu("00000000:1B:00.0", {"QB_CPU_AFFINITY": "1"}, **kw)
+    assert calls == [{4, 5}] and "2 CPUs" in note  # only CPUs the process may use
     calls.clear()
-    note = hostinfo.apply({"QB_HOST_MEM_NODES": "0-1"}, -1, tmp_path, aff, pol)
-    assert calls == {"mem": [0, 1]} and "mem_interleave" in note
-    calls.clear()
-    # auto with an unknown GPU node does nothing
-    assert hostinfo.apply({"QB_HOST_CPU_NODES": "auto"}, -1, tmp_path, aff, pol) == "" and not calls
+    assert affinity.pin_to_gpu("00000000:99:00.0", {"QB_CPU_AFFINITY": "1"}, **kw) == "" and not calls
 
 
-def test_node_meminfo(tmp_path):
-    (tmp_path / "node0").mkdir()
-    (tmp_path / "node0" / "meminfo").write_text(
-        "Node 0 MemTotal:       1048576 kB\nNode 0 MemFree:         524288 kB\nNode 0 MemUsed:  524288 kB\n")
-    assert hostinfo.node_meminfo_gib(tmp_path) == {"node0": {"MemFree": 0.5, "MemUsed": 0.5}}
+def test_mem_report_off_by_default_and_pool_plan_on_cpu():
+    from qwen35_b200.serving.engine import PoolSpec, build_model
 
-
-def test_preflight_waits_then_fails_or_passes():
-    t = [0.0]
-    free = iter([10.0, 20.0, 60.0])
-    logs = []
-    memtimeline.preflight(50.0, 30.0, read=lambda: next(free), sleep=lambda s: t.__setitem__(0, t[0] + s),
-                          clock=lambda: t[0], sink=logs.append)
-    assert logs and "ok" in logs[0]
-    with pytest.raises(RuntimeError, match="another process"):
-        memtimeline.preflight(50.0, 5.0, read=lambda: 1.0, sleep=lambda s: t.__setitem__(0, t[0] + s),
-                              clock=lambda: t[0], sink=logs.append)
-    memtimeline.preflight(0.0, 5.0, read=lambda: 0.0)  # off: returns at once
-
-
-def test_mem_timeline_is_off_by_default():
-    assert memtimeline.mark("x", torch.device("cpu")) is None
+    assert memreport.BootMemory(0, torch.device("cpu")).phase("x") is None
+    m, _ = build_model("tiny", 0, 1, torch.device("cpu"), PoolSpec(lanes=2, max_seq=64, kv_tokens=128),
+                       dtype=torch.float32, graphs=False)
+    assert memreport.pool_plan(m) is None  # off unless QB_MEM_REPORT
+    lines = []
+    rec = memreport.pool_plan(m, sink=lines.append, force=True)
+    assert lines and lines[0].startswith("[pool-plan]")
+    b = memreport.pool_bytes_of(m)
+    kv = sum(t.numel() * t.element_size() for t in m.k_cache + m.v_cache)
+    assert b["kv_cache"] == kv and b["experts"] > 0 and b["deltanet"] > 0 and b["attention"] > 0
+    assert rec["kv_tokens"] == m.num_blocks * m.block_size and rec["lanes"] == m.max_batch
 
 
 def test_stamps_on_cpu():
