@@ -29,6 +29,8 @@
 #define QB_NOALLOC_ERR_TOO_LARGE (-2)
 #define QB_NOALLOC_ERR_ARGS (-3)
 #define QB_NOALLOC_ERR_SYMBOL (-4)
+// Query heads per KV head handled by one CTA of the split kernel (4 warps x 4 heads).
+#define QB_NOALLOC_MAX_GQA_GROUP 16
 
 #ifdef __cplusplus
 extern "C" {
@@ -40,8 +42,16 @@ extern "C" {
 // bf16; block_table [lanes, max_blocks] int32; positions [rows] int32 (absolute position of each
 // query row, causal context is 0..position); seg_lane [segments] and cu [segments + 1] int32
 // describe which lane each row belongs to; out [rows, nq, head_dim] bf16.
-// Returns QB_NOALLOC_OK, QB_NOALLOC_ERR_TOO_LARGE, QB_NOALLOC_ERR_ARGS, QB_NOALLOC_ERR_SYMBOL
-// or a CUDA error code from the launch.
+// Returns one of:
+//   QB_NOALLOC_OK             launched (or nothing to do when num_rows == 0);
+//   QB_NOALLOC_ERR_TOO_LARGE  splits > 1 and the scratch the call needs exceeds the array;
+//   QB_NOALLOC_ERR_ARGS       a bad argument: num_rows < 0, num_segments <= 0, nq or nkv <= 0,
+//                             nq % nkv != 0, nq / nkv > QB_NOALLOC_MAX_GQA_GROUP (16),
+//                             head_dim not 64, 128 or 256, block_size <= 0, splits outside 1..64,
+//                             or a current device index >= 64;
+//   QB_NOALLOC_ERR_SYMBOL     the scratch array's device address could not be looked up;
+//   a positive cudaError_t    the launch failed (the value of cudaGetLastError()).
+// Nothing is launched on any of the negative codes.
 int qb_attention_varlen_noalloc(const void* q, const void* k_cache, const void* v_cache, const int* block_table,
                                 int max_blocks, const int* positions, const int* seg_lane, const int* cu,
                                 int num_segments, int num_rows, int nq, int nkv, int head_dim, int block_size,

@@ -860,7 +860,7 @@ extern "C" __attribute__((visibility("default"))) int qb_attention_varlen_noallo
     const int* positions, const int* seg_lane, const int* cu, int num_segments, int num_rows, int nq, int nkv,
     int head_dim, int block_size, int splits, void* out, cudaStream_t stream) {
   if (num_rows < 0 || num_segments <= 0 || nq <= 0 || nkv <= 0 || splits < 1 || splits > 64 || block_size <= 0 ||
-      nq % nkv != 0 || (head_dim != 64 && head_dim != 128 && head_dim != 256))
+      nq % nkv != 0 || nq / nkv > QB_NOALLOC_MAX_GQA_GROUP || (head_dim != 64 && head_dim != 128 && head_dim != 256))
     return QB_NOALLOC_ERR_ARGS;
   if (num_rows == 0) return QB_NOALLOC_OK;
   const size_t need = (size_t)num_rows * nq * splits * (head_dim + 2) * sizeof(float);

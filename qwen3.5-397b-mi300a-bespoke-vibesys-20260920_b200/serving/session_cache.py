@@ -86,8 +86,9 @@ class SessionCache:
         self.hits = 0
         self.misses = 0
         self.admissions: Counter = Counter()  # classify() results
-        self._evicted: OrderedDict = OrderedDict()  # (first tokens, depth) of evicted boundaries, LRU
-        self._evicted_by_key: dict[tuple, dict[int, int]] = {}  # first tokens -> depth -> path hash
+        self._evicted: OrderedDict = OrderedDict()  # (first tokens, depth, digest) of evicted boundaries, LRU
+        self._evicted_by_key: dict[tuple, dict[int, set]] = {}  # first tokens -> depth -> prefix digests
+        self._lookup_memo: tuple | None = None  # (prompt, node, deepest reclaimed depth) of the last lookup
 
     # ------------------------------------------------------------------ lookup
     def _walk(self, prompt: Sequence[int]):
@@ -107,11 +108,16 @@ class SessionCache:
             yield node
 
     def lookup(self, prompt: Sequence[int]) -> Node:
-        """Deepest node with a resumable state whose span is a prefix of ``prompt``."""
-        best = self.root
+        """Deepest node with a resumable state whose span is a prefix of ``prompt``. The same
+        walk notes the deepest matching boundary whose snapshot was reclaimed, which
+        ``classify`` reuses instead of walking again."""
+        best, reclaimed = self.root, -1
         for n in self._walk(prompt):
             if n.has_state():
                 best = n
+            elif n.reclaimed:
+                reclaimed = n.depth
+        self._lookup_memo = (prompt, best, reclaimed)
         if best.is_root():
             self.misses += 1
         else:
@@ -129,8 +135,27 @@ class SessionCache:
     EVICTED_INDEX = 4096  # remembered evicted boundaries (diagnostics only)
     EVICTED_KEY = 16  # leading tokens that bucket them
 
+    @staticmethod
+    def _prefix_digests(tokens: Sequence[int], depths) -> dict[int, int]:
+        """Digest of ``tokens[:d]`` for each ``d`` in ``depths``: a polynomial hash mod 2^64
+        computed for every prefix in one vectorised pass (one walk of the longest prefix,
+        however many depths are asked)."""
+        import numpy as np
+
+        depths = [d for d in depths if 0 < d <= len(tokens)]
+        if not depths:
+            return {}
+        n = max(depths)
+        t = np.asarray(tokens[:n], dtype=np.uint64) + np.uint64(1)
+        powers = np.cumprod(np.full(n, 1_000_003, dtype=np.uint64), dtype=np.uint64)
+        with np.errstate(over="ignore"):
+            cs = np.cumsum(t * powers, dtype=np.uint64)
+        return {d: int(cs[d - 1]) for d in depths}
+
     def _note_evicted(self, node: Node) -> None:
-        """Remember that a boundary with state at ``node`` was evicted (for ``classify``)."""
+        """Remember that a boundary with state at ``node`` was evicted (for ``classify``). Several
+        sessions that share their first tokens may lose boundaries at the same depth: each
+        keeps its own digest."""
         edges = []
         n = node
         while n is not None and not n.is_root():
@@ -139,14 +164,17 @@ class SessionCache:
         path = tuple(t for e in reversed(edges) for t in e)
         if len(path) < self.EVICTED_KEY:
             return
-        ent = (path[: self.EVICTED_KEY], node.depth)
+        digest = self._prefix_digests(path, [len(path)])[len(path)]
+        ent = (path[: self.EVICTED_KEY], node.depth, digest)
         self._evicted[ent] = None
         self._evicted.move_to_end(ent)
-        self._evicted_by_key.setdefault(ent[0], {})[node.depth] = hash(path)
+        self._evicted_by_key.setdefault(ent[0], {}).setdefault(node.depth, set()).add(digest)
         while len(self._evicted) > self.EVICTED_INDEX:
-            (k, d), _ = self._evicted.popitem(last=False)
+            (k, d, dg), _ = self._evicted.popitem(last=False)
             by_depth = self._evicted_by_key[k]
-            by_depth.pop(d, None)
+            by_depth[d].discard(dg)
+            if not by_depth[d]:
+                del by_depth[d]
             if not by_depth:
                 del self._evicted_by_key[k]
 
@@ -158,15 +186,21 @@ class SessionCache:
         was evicted), ``miss_cold`` (nothing matches, now or before). Reference behaviour:
         ``session_cache.py:209-227`` (``classify``)."""
         kind = "miss" if node.is_root() else "short"
-        if any(n.reclaimed and n.depth > node.depth for n in self._walk(prompt)):
+        memo = self._lookup_memo
+        if memo is not None and memo[0] is prompt and memo[1] is node:
+            reclaimed = memo[2]
+        else:
+            reclaimed = max((n.depth for n in self._walk(prompt) if n.reclaimed), default=-1)
+        if reclaimed > node.depth:
             cls = kind + "_reclaimed"
         else:
             cls = None
             by_depth = self._evicted_by_key.get(tuple(prompt[: self.EVICTED_KEY]), {})
-            for d, digest in by_depth.items():
-                if node.depth < d <= len(prompt) and hash(tuple(prompt[:d])) == digest:
+            cand = [d for d in by_depth if node.depth < d <= len(prompt)]
+            if cand:
+                got = self._prefix_digests(prompt, cand)
+                if any(got[d] in by_depth[d] for d in cand):
                     cls = kind + "_evicted"
-                    break
             if cls is None:
                 cls = "miss_cold" if node.is_root() else ("exact" if node.depth == len(prompt) else "hit")
         self.admissions[cls] += 1

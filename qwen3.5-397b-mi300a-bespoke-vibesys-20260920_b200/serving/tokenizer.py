@@ -173,23 +173,28 @@ class PromptCache:
         self.entries: OrderedDict[str, list[int]] = OrderedDict()
 
     def encode(self, text: str) -> list[int]:
+        """Ids of ``text``: the cached ids of its longest cached prefix that ends at a turn
+        boundary, plus the encoding of the rest. The prefix up to ``text``'s own last boundary
+        is cached for the next turn, built from the same pieces, so each call encodes only the
+        characters after the longest cached prefix."""
         best = ""
         for k in self.entries:
             if len(k) > len(best) and text.startswith(k):
                 best = k
+        head = list(self.entries[best]) if best else []
         if best:
-            ids = list(self.entries[best]) + self.tok.encode(text[len(best):])
             self.entries.move_to_end(best)
-        else:
-            ids = self.tok.encode(text)
         cut = text.rfind(self.boundary)
-        if cut > 0:
-            key = text[: cut + len(self.boundary)]
-            if key not in self.entries:
-                self.entries[key] = self.tok.encode(key)
-                if len(self.entries) > self.capacity:
-                    self.entries.popitem(last=False)
-        return ids
+        end = cut + len(self.boundary) if cut >= 0 else 0
+        if end > len(best):  # a new boundary past the cached prefix: extend and cache it
+            head = head + self.tok.encode(text[len(best):end])
+            key = text[:end]
+            self.entries[key] = head
+            self.entries.move_to_end(key)
+            if len(self.entries) > self.capacity:
+                self.entries.popitem(last=False)
+            best = key
+        return list(head) + (self.tok.encode(text[len(best):]) if len(text) > len(best) else [])
 
     def selfcheck(self, samples: list[str]) -> bool:
         """Incremental ids equal full tokenization for every sample (run at boot)."""

@@ -102,3 +102,33 @@ def test_hf_prompts_tokenized_incrementally_after_selfcheck():
     assert not tok.enable_prompt_cache() and tok.prompts is None
     assert tok.render_chat(msgs)[0] == tok.encode(tok.tok.apply_chat_template(msgs, tokenize=False,
                                                                                add_generation_prompt=True))
+
+
+class _CountingTok:
+    """Whitespace-free byte tokenizer stand-in that records every ``encode`` input length."""
+
+    def __init__(self):
+        self.lengths = []
+
+    def encode(self, text):
+        self.lengths.append(len(text))
+        return [ord(c) for c in text]
+
+
+def test_prompt_cache_encodes_each_turn_incrementally():
+    from qwen35_b200.serving.tokenizer import PromptCache
+
+    tok = _CountingTok()
+    pc = PromptCache(tok, capacity=8)
+    conv = "<|im_start|>system\nbe brief<|im_end|>\n"
+    cached = 0  # length of the longest cached boundary prefix
+    for turn in range(6):
+        conv += f"<|im_start|>user\nquestion number {turn}<|im_end|>\n<|im_start|>assistant\n"
+        tok.lengths.clear()
+        ids = pc.encode(conv)
+        assert ids == [ord(c) for c in conv]
+        # only the characters after the previous turn's cached boundary are encoded, once
+        assert sum(tok.lengths) == len(conv) - cached, (turn, tok.lengths)
+        cached = conv.rfind("<|im_end|>") + len("<|im_end|>")
+        conv += f"answer {turn}<|im_end|>\n"
+    assert len(pc.entries) <= 8

@@ -87,3 +87,34 @@ def test_classify_cold_hit_evicted_reclaimed():
     n.snapshot, n.reclaimed = -1, True  # as _reclaim_one_internal leaves a node
     assert c.classify(p1 + [3], c.lookup(p1 + [3])) == "miss_reclaimed"
     assert c.admissions["miss_cold"] == 2 and c.admissions["hit"] == 1
+
+
+def test_classify_remembers_each_evicted_session_sharing_a_prefix():
+    """Two sessions with the same first 20 tokens lose boundaries at the same depth: both are
+    reported as evicted, not only the last one evicted."""
+    c = mk(blocks=40, bs=4, snaps=8)
+    shared = list(range(500, 520))
+    a, b = shared + [1] * 8, shared + [2] * 8
+    for p in (a, b):
+        blk = c.reserve_blocks(7)
+        c.publish(p, 28, blk, c.reserve_snapshot())
+        c.release_lane_blocks(blk)
+    c.evict_all()
+    for p in (a, b):
+        assert c.classify(p + [7], c.lookup(p + [7])) == "miss_evicted"
+    assert c.classify(shared + [3] * 8, c.root) == "miss_cold"
+    # the memo of the last lookup is used only for that same prompt object
+    q = a + [9]
+    node = c.lookup(q)
+    assert c._lookup_memo[0] is q and c.classify(q, node) == "miss_evicted"
+
+
+def test_prefix_digests_match_per_prefix():
+    from qwen35_b200.serving.session_cache import SessionCache
+
+    toks = [5, 0, 7, 7, 123456, 3]
+    all_d = SessionCache._prefix_digests(toks, range(1, 7))
+    for d in range(1, 7):
+        assert SessionCache._prefix_digests(toks[:d], [d])[d] == all_d[d]
+    assert len(set(all_d.values())) == 6
+    assert SessionCache._prefix_digests(toks, [0, 9]) == {}
