@@ -20,8 +20,9 @@ closed-loop client; the other ranks mirror every model call (``parallel.driver``
 ``value`` = p95 TTFT over EVERY turn >= 2 of the loop (no survivorship filter: the loop runs
 until each has finished), device-timed: for each turn, the sum over the scheduler steps from the
 one that admitted it to the one that produced its first token of each step's device interval
-(CUDA event at the step's first input upload to the event just before its last result read);
-host gaps between steps are excluded. Fewer than 200 samples give no value. ``decode_tok_s`` =
+(CUDA events recorded on the launching stream just before and just after the step; host gaps
+between steps are excluded). The reference arm (``baseline/reference_arm.py``) is timed the same
+way. Fewer than 200 samples give no value. ``decode_tok_s`` =
 every token generated in the loop (each counted once, when emitted) / the loop's device window
 (max over ranks). ``e2e`` = the same two metrics on the host clock through the public
 ``Scheduler.submit`` API: every step copies its inputs host->device from pinned memory and reads
@@ -161,11 +162,19 @@ def ttft_lists(records, step_ms, first_turn: int = 1):
     return dev, host, missing
 
 
+def percentile(xs, q: float) -> float:
+    """Linear-interpolated percentile (numpy's default method)."""
+    if not xs:
+        return float("nan")
+    s = sorted(xs)
+    k = (len(s) - 1) * q / 100.0
+    lo, hi = int(k), min(int(k) + 1, len(s) - 1)
+    return s[lo] + (s[hi] - s[lo]) * (k - lo)
+
+
 def report(args, *, impl, world, window_ms, host_s, records, step_ms, kinds_summary, clocks, h2d, d2h,
            launches, sched_steps, boot_s, warm_s, cfg_desc, expert_storage, extra=None) -> dict:
     """The benchmark's JSON line (shared by both arms)."""
-    from qwen35_b200.serving.workload import percentile
-
     dev, host, missing = ttft_lists(records, step_ms)
     samples = dev if any(v is not None for v in step_ms) and dev else host
     gen = sum(r.generated for r in records)
@@ -314,23 +323,17 @@ def main_ours(args):
     on_gpu = device.type == "cuda"
     step_no = [0]
 
-    def one_step(loop, step_ms=None):
-        """One scheduler step. With ``step_ms``, append the step's device interval (ms): from the
-        event at its first input upload to the event before its last result read (or, for a
-        step that reads nothing back, an event after its last launch); ``None`` when the step
-        launched nothing. Host gaps between steps are outside every interval."""
-        if step_ms is not None:
-            inner.gpu_marks = []
+    def one_step(loop, brackets=None):
+        """One scheduler step; with ``brackets``, a CUDA event before and one after it on the
+        launching stream (the step's device interval; host gaps between steps fall outside)."""
+        if brackets is not None:
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
         sched.step()
-        if step_ms is not None:
-            marks = inner.gpu_marks
-            inner.gpu_marks = None
-            end = torch.cuda.Event(enable_timing=True)
-            end.record()
-            first_in = next((ev for tag, ev in marks if tag == "in"), None)
-            last_in = max((i for i, (tag, _) in enumerate(marks) if tag == "in"), default=-1)
-            outs = [ev for i, (tag, ev) in enumerate(marks) if tag == "out" and i > last_in]
-            step_ms.append((first_in, outs[-1] if outs else end) if first_in is not None else None)
+        if brackets is not None:
+            ev1 = torch.cuda.Event(enable_timing=True)
+            ev1.record()
+            brackets.append((ev0, ev1))
         step_no[0] += 1
         loop.pump()
 
@@ -388,9 +391,7 @@ def main_ours(args):
         gathered = [None] * world
         dist.all_gather_object(gathered, window_ms)
         window_ms = max(gathered)
-    step_ms = [ev[0].elapsed_time(ev[1]) if ev is not None else None for ev in marks] if on_gpu else \
-        [None] * step_no[0]
-    by_kind: dict = {}
+    step_ms = [a.elapsed_time(b) for a, b in marks] if on_gpu else [None] * step_no[0]
     kinds = sched.timer.summary()
     storage = "all layers distinct" if distinct is None else \
         (f"{distinct} distinct expert layers, the other {cfg.layers - distinct} reuse their storage "
@@ -401,7 +402,6 @@ def main_ours(args):
                  warm_s=warm_s, cfg_desc=(f"Qwen3.5-397B-A17B geometry ({cfg.layers} layers, {cfg.experts} "
                                           f"experts MXFP4)" if args.model == "full" else "tiny parity model"),
                  expert_storage=storage, extra={"mixed": mixed})
-    del by_kind
     line = json.dumps(res)
     print(line, flush=True)
     if args.out:

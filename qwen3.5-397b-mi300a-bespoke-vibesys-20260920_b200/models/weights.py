@@ -412,3 +412,105 @@ def write_tiny_checkpoint(path: str, cfg: Qwen35Config, seed: int = 0, shards: i
           "qwen35_b200": json.loads(cfg.to_json())}
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(hf, f, indent=1)
+
+
+# ============================================================================ full-size checkpoint
+def _layer_specs(prefix: str, kind: str, cfg: Qwen35Config) -> list[tuple[str, str, tuple[int, ...]]]:
+    """(name, kind, shape) of one decoder layer's tensors in the published layout; kind is
+    ``bf16``, ``codes`` (packed e2m1, uint8) or ``scales`` (e8m0, uint8)."""
+    h = cfg.hidden
+    out = [(prefix + "input_layernorm.weight", "bf16", (h,)),
+           (prefix + "post_attention_layernorm.weight", "bf16", (h,))]
+    if kind == FULL:
+        hd = cfg.head_dim
+        out += [(prefix + "self_attn.q_proj.weight", "bf16", (cfg.q_heads * hd * 2, h)),
+                (prefix + "self_attn.k_proj.weight", "bf16", (cfg.kv_heads * hd, h)),
+                (prefix + "self_attn.v_proj.weight", "bf16", (cfg.kv_heads * hd, h)),
+                (prefix + "self_attn.o_proj.weight", "bf16", (h, cfg.q_heads * hd)),
+                (prefix + "self_attn.q_norm.weight", "bf16", (hd,)),
+                (prefix + "self_attn.k_norm.weight", "bf16", (hd,))]
+    else:
+        out += [(prefix + "linear_attn.in_proj_qkv.weight", "bf16", (cfg.dn_conv_dim, h)),
+                (prefix + "linear_attn.in_proj_z.weight", "bf16", (cfg.dn_value_dim, h)),
+                (prefix + "linear_attn.in_proj_b.weight", "bf16", (cfg.dn_v_heads, h)),
+                (prefix + "linear_attn.in_proj_a.weight", "bf16", (cfg.dn_v_heads, h)),
+                (prefix + "linear_attn.conv1d.weight", "bf16", (cfg.dn_conv_dim, 1, cfg.conv_kernel)),
+                (prefix + "linear_attn.A_log", "bf16", (cfg.dn_v_heads,)),
+                (prefix + "linear_attn.dt_bias", "bf16", (cfg.dn_v_heads,)),
+                (prefix + "linear_attn.norm.weight", "bf16", (cfg.dn_v_dim,)),
+                (prefix + "linear_attn.out_proj.weight", "bf16", (h, cfg.dn_value_dim))]
+    out += [(prefix + "mlp.gate.weight", "bf16", (cfg.experts, h)),
+            (prefix + "mlp.shared_expert_gate.weight", "bf16", (1, h)),
+            (prefix + "mlp.shared_expert.gate_proj.weight", "bf16", (cfg.shared_inter, h)),
+            (prefix + "mlp.shared_expert.up_proj.weight", "bf16", (cfg.shared_inter, h)),
+            (prefix + "mlp.shared_expert.down_proj.weight", "bf16", (h, cfg.shared_inter))]
+    for e in range(cfg.experts):
+        b = f"{prefix}mlp.experts.{e}."
+        for name, (rows, cols) in (("gate_proj", (cfg.moe_inter, h)), ("up_proj", (cfg.moe_inter, h)),
+                                   ("down_proj", (h, cfg.moe_inter))):
+            out.append((b + name + ".weight", "codes", (rows, cols // 2)))
+            out.append((b + name + ".weight_scale", "scales", (rows, cols // 32)))
+    return out
+
+
+def checkpoint_shards(cfg: Qwen35Config) -> list[list[tuple[str, str, tuple[int, ...]]]]:
+    """Tensor specs per shard of ``write_random_checkpoint``: shard 0 holds the embedding, the
+    final norm and the LM head; shard ``1 + i`` holds decoder layer ``i``."""
+    h = cfg.hidden
+    shards = [[(PREFIX + "embed_tokens.weight", "bf16", (cfg.vocab, h)), (PREFIX + "norm.weight", "bf16", (h,)),
+               ("lm_head.weight", "bf16", (cfg.vocab, h))]]
+    for i, kind in enumerate(cfg.layer_types):
+        shards.append(_layer_specs(f"{PREFIX}layers.{i}.", kind, cfg))
+    return shards
+
+
+def write_random_checkpoint(path: str, cfg: Qwen35Config, seed: int = 0, only: list[int] | None = None,
+                            device: str | torch.device = "cpu", write_config: bool = True) -> list[str]:
+    """Write a random-init checkpoint of ``cfg`` (any size, the full geometry included) in the
+    published naming and layout, one safetensors file per shard of ``checkpoint_shards``:
+    bf16 tensors N(0, 0.02); routed experts as packed e2m1 codes (uniform random bytes) with
+    e8m0 scales 2^-7 .. 2^-5 (the block scales an N(0, 0.02) matrix quantises to). Tensors are
+    generated one at a time on ``device`` and streamed to the file, so host memory stays at one
+    tensor. ``only`` restricts the call to those shard indices (ranks can split the work); the
+    shard's own seed makes its bytes independent of which process writes it. Returns the paths
+    written."""
+    import struct
+
+    os.makedirs(path, exist_ok=True)
+    shards = checkpoint_shards(cfg)
+    n = len(shards)
+    written = []
+    dev = torch.device(device)
+    for s in (range(n) if only is None else only):
+        specs = shards[s]
+        gen = torch.Generator(device=dev).manual_seed(seed * 100_003 + s)
+        header, off = {}, 0
+        for name, kind, shape in specs:
+            nbytes = int(torch.Size(shape).numel()) * (2 if kind == "bf16" else 1)
+            header[name] = {"dtype": "BF16" if kind == "bf16" else "U8", "shape": list(shape),
+                            "data_offsets": [off, off + nbytes]}
+            off += nbytes
+        hb = json.dumps(header, separators=(",", ":")).encode()
+        hb += b" " * ((8 - len(hb) % 8) % 8)
+        fn = os.path.join(path, f"model-{s + 1:05d}-of-{n:05d}.safetensors")
+        tmp = fn + ".part"
+        with open(tmp, "wb") as f:
+            f.write(struct.pack("<Q", len(hb)))
+            f.write(hb)
+            for name, kind, shape in specs:
+                if kind == "bf16":
+                    t = (torch.randn(*shape, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+                elif kind == "codes":
+                    t = torch.randint(0, 256, shape, generator=gen, device=dev, dtype=torch.uint8)
+                else:
+                    t = torch.randint(120, 123, shape, generator=gen, device=dev, dtype=torch.uint8)
+                f.write(t.contiguous().view(torch.uint8).cpu().numpy().tobytes())
+        os.replace(tmp, fn)
+        written.append(fn)
+    if write_config:
+        hf = {"architectures": ["Qwen3_5MoeForConditionalGeneration"], "model_type": "qwen3_5_moe",
+              "text_config": to_hf_text_config(cfg), "tie_word_embeddings": False,
+              "qwen35_b200": json.loads(cfg.to_json())}
+        with open(os.path.join(path, "config.json"), "w") as f:
+            json.dump(hf, f, indent=1)
+    return written

@@ -15,7 +15,12 @@ import random
 import time
 from dataclasses import dataclass, field
 
-from .scheduler import Request
+
+
+def _our_request(prompt, max_new, emit, has_history):
+    from .scheduler import Request
+
+    return Request(prompt, max_new, emit, temperature=0.0, has_history=has_history)
 
 
 @dataclass(frozen=True)
@@ -59,10 +64,14 @@ class _Session:
 class ClosedLoop:
     """Keeps ``spec.concurrency`` sessions in flight; a session's next turn is submitted as soon
     as its previous turn ends. ``step_index`` is read from the caller (the index of the next
-    scheduler step) so device-side step events can be matched to each turn."""
+    scheduler step) so device-side step events can be matched to each turn. ``make_request``
+    builds the scheduler's request object from ``(prompt, max_new, emit, has_history)`` (this
+    package's ``Request`` by default; another engine's scheduler can be driven the same way)."""
 
-    def __init__(self, scheduler, spec: ChatSpec, step_index=lambda: 0, max_turn: int | None = None):
+    def __init__(self, scheduler, spec: ChatSpec, step_index=lambda: 0, max_turn: int | None = None,
+                 make_request=None):
         self.sched = scheduler
+        self.make_request = make_request or _our_request
         self.spec = spec
         self.step_index = step_index
         self.max_turn = max_turn or spec.turns
@@ -107,7 +116,7 @@ class ClosedLoop:
                 rec.end_step = self.step_index()
                 self._done.append((sess, rec, toks))
 
-        self.sched.submit(Request(list(sess.history), glen, emit, temperature=0.0, has_history=sess.turn > 0))
+        self.sched.submit(self.make_request(list(sess.history), glen, emit, sess.turn > 0))
 
     def start(self) -> None:
         while len(self.active) < self.spec.concurrency and self.next_sid < self.spec.sessions:
