@@ -401,7 +401,12 @@ def main_ours(args):
                  h2d=h2d1 - h2d0, d2h=d2h1 - d2h0, launches=launches, sched_steps=step_no[0], boot_s=boot_s,
                  warm_s=warm_s, cfg_desc=(f"Qwen3.5-397B-A17B geometry ({cfg.layers} layers, {cfg.experts} "
                                           f"experts MXFP4)" if args.model == "full" else "tiny parity model"),
-                 expert_storage=storage, extra={"mixed": mixed})
+                 expert_storage=storage,
+                 extra={"mixed": mixed, "prefill_order": sched.prefill_order,
+                        "cache": {"admissions": dict(cache.admissions), "evictions": cache.evictions,
+                                  "reclaims": cache.reclaims,
+                                  "prefill_tokens": (kinds.get("prefill", {}).get("tokens", 0)
+                                                     + kinds.get("mixed", {}).get("tokens", 0))}})
     line = json.dumps(res)
     print(line, flush=True)
     if args.out:

@@ -1,8 +1,8 @@
 """Continuous-batching scheduler with the cross-turn prefix/session cache (host only).
 
 Iteration model: one ``step()`` is either one packed prefill call (several requests' prompt
-chunks concatenated, up to ``token_budget`` tokens) or one batched decode step over every lane
-past prefill; prefill wins ties for at most ``max_prefill_burst`` consecutive steps while
+chunks concatenated, up to ``token_budget`` tokens; packed shortest pending prompt first by
+default, ``QB_PREFILL_ORDER``) or one batched decode step over every lane past prefill; prefill wins ties for at most ``max_prefill_burst`` consecutive steps while
 lanes are decoding (reference ``scheduler.py:865-948``). With ``mixed=True`` a decode step
 also carries prefill chunks in the same forward (Sarathi-style), and with an MTP-capable runner
 decode steps are speculative rounds (draft, verify, accept).
@@ -46,6 +46,7 @@ Event = tuple[str, Any]
 PREFILL_CHUNK = 512
 PREFILL_TOKEN_BUDGET = 2048
 MAX_PREFILL_BURST = 4
+MAX_PREFILL_SKIPS = 8  # shortest-first: a flight passed over this many prefill steps goes first
 
 
 @dataclass
@@ -76,6 +77,7 @@ class _Flight:
     blocks: list[int]
     boundary: int
     next_token: int | None = None
+    skipped: int = 0  # prefill steps that ran without this flight (shortest-first aging)
     generated: int = 0
     out_ids: list[int] = field(default_factory=list)
     last_logits: Any = None
@@ -102,7 +104,8 @@ class _Control:
 class Scheduler:
     def __init__(self, runner, cache: SessionCache, prefill_chunk: int = PREFILL_CHUNK,
                  token_budget: int = PREFILL_TOKEN_BUDGET, max_prefill_burst: int = MAX_PREFILL_BURST,
-                 mixed: bool = False, speculative: bool = False, timer: StepTimer | None = None) -> None:
+                 mixed: bool = False, speculative: bool = False, timer: StepTimer | None = None,
+                 prefill_order: str | None = None, max_skips: int = MAX_PREFILL_SKIPS) -> None:
         self.runner = runner
         self.cache = cache
         self.block_size = cache.block_size
@@ -111,6 +114,14 @@ class Scheduler:
         self.max_prefill_burst = max_prefill_burst
         self.mixed = mixed
         self.speculative = speculative
+        if prefill_order is None:
+            from ..utils import flags
+
+            prefill_order = flags.get("QB_PREFILL_ORDER")
+        if prefill_order not in ("fifo", "shortest"):
+            raise ValueError(f"prefill_order must be fifo or shortest, got {prefill_order!r}")
+        self.prefill_order = prefill_order
+        self.max_skips = max_skips
         self.free_lanes: list[int] = list(range(runner.max_batch - 1, -1, -1))
         self.incoming: queue.Queue = queue.Queue()
         self.waiting: deque[Request] = deque()
@@ -277,9 +288,19 @@ class Scheduler:
             self.runner.extend_blocks(grants)
 
     # ================================================================== prefill
+    def _prefill_queue(self) -> list[_Flight]:
+        """Prefill flights in the order a step packs them. ``fifo``: admission order.
+        ``shortest``: fewest pending prompt tokens first, so a follow-up turn's few hundred new
+        tokens are not queued behind another session's long opening prompt; a flight passed
+        over ``max_skips`` prefill steps in a row goes first (no starvation)."""
+        q = list(self.prefilling)
+        if self.prefill_order == "shortest":
+            q.sort(key=lambda f: (f.skipped < self.max_skips, len(f.pending)))
+        return q
+
     def _select_prefill(self) -> list[tuple[_Flight, list[int]]]:
         batch, budget = [], self.token_budget
-        for f in self.prefilling:
+        for f in self._prefill_queue():
             n = min(len(f.pending), self.prefill_chunk, budget)
             if f.boundary > f.pos:
                 n = min(n, f.boundary - f.pos)
@@ -289,6 +310,9 @@ class Scheduler:
             budget -= n
             if budget <= 0:
                 break
+        chosen = {id(f) for f, _ in batch}
+        for f in self.prefilling:
+            f.skipped = 0 if id(f) in chosen else f.skipped + 1
         return batch
 
     def _prefill_step(self) -> None:
@@ -390,7 +414,9 @@ class Scheduler:
             return
         self.runner.save_snapshot(f.lane, snap)
         self.runner.cache_node_logits(snap, logits)
-        node = self.cache.publish(tokens, depth, f.blocks, snap, resumed_from=f.resumed_from)
+        # the node this flight last extended (its admission node, or its own turn-open node when
+        # the turn closes) is now behind the conversation: superseded, its snapshot reclaimable
+        node = self.cache.publish(tokens, depth, f.blocks, snap, resumed_from=f.parent)
         f.parent = node
 
     def _finish(self, f: _Flight, reason: str) -> None:

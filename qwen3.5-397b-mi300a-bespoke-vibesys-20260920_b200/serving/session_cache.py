@@ -307,7 +307,11 @@ class SessionCache:
         return True
 
     def _reclaim_one_internal(self, protect: Sequence[Node] = ()) -> bool:
-        prot = self._protected(protect)
+        """Take the snapshot slot of one internal node (superseded ones first, then any, least
+        recently used first). Only the nodes in ``protect`` themselves are spared: an internal
+        node's blocks are part of its descendants' context, but its snapshot is needed only by
+        an admission that resumes exactly there, and a live lane already loaded its own."""
+        prot = {id(p) for p in protect}
         cands = [n for n in self._iter() if not n.is_leaf() and not n.is_root() and n.snapshot >= 0
                  and n.superseded and id(n) not in prot]
         if not cands:

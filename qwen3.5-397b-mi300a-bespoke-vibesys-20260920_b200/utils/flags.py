@@ -56,6 +56,8 @@ _def("QB_DN_DECODE", str, "", "DeltaNet decode mixer state path: reg (registers)
 _def("QB_DN_CHUNKED", bool, False, "chunked (WY) DeltaNet prefill instead of the token recurrence",
      lockstep=True)
 _def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
+_def("QB_PREFILL_ORDER", str, "shortest", "scheduler: order prefill flights are packed in: shortest (fewest "
+     "pending prompt tokens first, with aging) or fifo (admission order)")
 _def("QB_MIXED", bool, False, "scheduler: decode steps also carry prefill chunks in the same forward")
 # ---- collectives and multi-rank plumbing
 _def("QB_COMM", str, "fused", "tensor-parallel all-reduce: fused (peer-memory kernels) or nccl", lockstep=True)

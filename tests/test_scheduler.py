@@ -128,3 +128,46 @@ def test_runner_exception_aborts_inflight_and_recovers():
     s.submit(Request([1, 2, 3], 4, ev2.append))
     s.run_until_idle()
     assert ev2[-1][0] == "end" and len(s.free_lanes) == 2
+
+
+@pytest.mark.parametrize("order", ["fifo", "shortest"])
+def test_prefill_order_same_tokens(order):
+    """Both prefill orders give every turn exactly its uncached greedy tokens."""
+    r = FakeRunner(max_batch=3, num_snapshots=6, block_size=4)
+    s = Scheduler(r, SessionCache(BlockAllocator(400, 4), 4, 6), prefill_chunk=8, token_budget=12,
+                  prefill_order=order)
+    for turn, prompt, toks, ends in run_sessions(s, 5, 3, 7, random.Random(5)):
+        assert toks == greedy(prompt, 7)
+
+
+def test_shortest_first_runs_a_short_prompt_before_a_long_one_and_ages():
+    """With a long prompt already prefilling, a short one admitted later gets its first token
+    first under ``shortest``; under ``fifo`` it waits for the long one. A flight passed over
+    ``max_skips`` steps is packed first."""
+    def first_token_order(order, max_skips=8):
+        r = FakeRunner(max_batch=3, num_snapshots=6, block_size=4)
+        s = Scheduler(r, SessionCache(BlockAllocator(400, 4), 4, 6), prefill_chunk=8, token_budget=8,
+                      prefill_order=order, max_skips=max_skips)
+        seen = []
+        s.submit(Request(list(range(1, 80)), 2, lambda e: seen.append("long") if e[0] == "tok" and "long" not in seen else None))
+        s.step()  # the long prompt starts prefilling
+        s.submit(Request(list(range(200, 206)), 2, lambda e: seen.append("short") if e[0] == "tok" and "short" not in seen else None))
+        s.run_until_idle()
+        return seen
+
+    assert first_token_order("shortest") == ["short", "long"]
+    assert first_token_order("fifo") == ["long", "short"]
+    r = FakeRunner(max_batch=3, num_snapshots=6, block_size=4)
+    s = Scheduler(r, SessionCache(BlockAllocator(400, 4), 4, 6), prefill_chunk=8, token_budget=8,
+                  prefill_order="shortest", max_skips=2)
+    s.submit(Request(list(range(1, 80)), 1, lambda e: None))
+    s.step()
+    for k in range(3):  # a stream of short prompts cannot starve the long one past max_skips
+        s.submit(Request(list(range(300 + 10 * k, 306 + 10 * k)), 1, lambda e: None))
+    skips = []
+    for _ in range(6):
+        s.step()
+        long_f = [f for f in s.prefilling if len(f.req.prompt) == 79]
+        if long_f:
+            skips.append(long_f[0].skipped)
+    assert max(skips) <= 2
