@@ -519,6 +519,25 @@ void symm_sp_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor par
                                  (unsigned long long)(timeout_s * 1e9), stream()));
 }
 
+// NVLS all-reduce + residual add + RMSNorm: `uc`/`mc` are this rank's unicast and multicast
+// addresses of one symmetric region bound to an NVSwitch multicast object.
+void nvls_ar_add_rmsnorm(int64_t uc, int64_t mc, int64_t world, int64_t rank, Tensor partial, Tensor res, Tensor w1p,
+                         Tensor out, double eps, int64_t slot_elems, int64_t grid, Tensor epoch, double timeout_s) {
+  CHECK_BF16(partial);
+  CHECK_BF16(res);
+  TORCH_CHECK(res.is_contiguous() && out.is_contiguous() && partial.stride(-1) == 1 &&
+                  (partial.stride(0) * 2) % 16 == 0, "nvls_ar: layouts");
+  const int H = res.size(-1);
+  const int rows = res.numel() / H;
+  int* ep = epoch.data_ptr<int>();
+  LAUNCH(qb::nvls_ar_add_rmsnorm(reinterpret_cast<void*>(uc), reinterpret_cast<void*>(mc), (int)world, (int)rank,
+                                 partial.data_ptr(), partial.stride(0), res.data_ptr(), w1p.data_ptr<float>(),
+                                 out.data_ptr(), rows, H, (float)eps, slot_elems, (int)grid, ep, ep + 1, err_ptr(res),
+                                 (unsigned long long)(timeout_s * 1e9), stream()));
+}
+
+int64_t nvls_region_bytes(int64_t slot_elems) { return qb::nvls_region_bytes(slot_elems); }
+
 // GEMM -> reduce-scatter + residual add + RMSNorm + all-gather: the row-parallel projection
 // x @ w^T stores its rows straight into the owner ranks' partial slots, then the pushed variant
 // of the sequence-parallel kernel reduces them. Same bits as linear + symm_sp_ar_add_rmsnorm.
@@ -609,6 +628,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_ar_add_rmsnorm", &symm_ar_add_rmsnorm);
   m.def("symm_sp_ar_add_rmsnorm", &symm_sp_ar_add_rmsnorm);
   m.def("symm_linear_sp_ar_add_rmsnorm", &symm_linear_sp_ar_add_rmsnorm);
+  m.def("nvls_ar_add_rmsnorm", &nvls_ar_add_rmsnorm);
+  m.def("nvls_region_bytes", &nvls_region_bytes);
   m.def("launches", &launches, "number of kernels launched through the bindings so far");
   m.def("add_launches", &add_launches, "account kernels launched by a CUDA-graph replay");
   m.def("clear_status", &clear_status);

@@ -401,4 +401,184 @@ int symm_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* par
   return (int)cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------------------------
+// NVLS (NVLink SHARP) all-reduce + residual add + RMSNorm for large messages.
+//
+// The region is one symmetric allocation bound to an NVSwitch multicast object: `uc` is this
+// rank's own (unicast) mapping, `mc` the multicast address of the same bytes on every rank.
+// Layout: two slots (call parity) of [partial | x | h], each [rows_cap, H] bf16, then two
+// monotonically increasing u32 arrival counters. A call with index e (device epoch + 1):
+//   A. every CTA copies its rows of the local partial into slot e&1 (unicast stores), then one
+//      thread adds 1 to counter 0 on EVERY rank at once (multimem.red.release) and waits,
+//      bounded, until its local copy reaches e * world * grid (all ranks' CTAs arrived);
+//   B. rank r owns rows [r*per, (r+1)*per): for each, multimem.ld_reduce makes the switch return
+//      the sum over all ranks (fp32 accumulation, one bf16 rounding), the kernel adds the
+//      residual, normalises, and multimem.st writes the new residual row and its norm into
+//      every rank's x/h areas with one store each;
+//   C. counter 1 the same way, then every CTA copies the rows from the local x/h areas into the
+//      output tensors.
+// Each rank's rows are reduced and normalised by one rank only, so every rank ends with
+// identical bits. The counters wrap safely (signed distance). Slot e&1 is rewritten at call
+// e+2, after every rank passed counter 1 of call e+1, so no rank still reads it. Accesses
+// through the multicast and unicast addresses of the same memory are ordered with
+// fence.proxy.alias. No TMA and no cluster multicast are involved.
+// ---------------------------------------------------------------------------------------------
+__device__ __forceinline__ void mc_red_add_release(unsigned* mc_addr, unsigned v) {
+  asm volatile("multimem.red.release.sys.global.add.u32 [%0], %1;" ::"l"(mc_addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned ld_acquire_sys_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_proxy_alias() { asm volatile("fence.proxy.alias;" ::: "memory"); }
+__device__ __forceinline__ uint4 mc_ld_reduce_bf16x8(const void* mc_addr) {
+  uint4 r;
+  asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
+               : "l"(mc_addr)
+               : "memory");
+  return r;
+}
+__device__ __forceinline__ void mc_st_16(void* mc_addr, uint4 v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc_addr),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
+
+// One thread per CTA: arrive on every rank's counter `c`, then wait until this rank's copy shows
+// all `target` arrivals. Returns false (and records ERR_PEER_WAIT) when the wait runs out.
+__device__ __forceinline__ bool nvls_barrier(unsigned* mc_cnt, const unsigned* uc_cnt, unsigned target, int* err,
+                                             unsigned long long timeout_ns) {
+  __threadfence_system();
+  fence_proxy_alias();
+  mc_red_add_release(mc_cnt, 1u);
+  const uint64_t t0 = globaltimer();
+  while ((int)(ld_acquire_sys_u32(uc_cnt) - target) < 0) {
+    if (globaltimer() - t0 > timeout_ns) {
+      atomicCAS(err, 0, ERR_PEER_WAIT);
+      return false;
+    }
+  }
+  fence_proxy_alias();
+  return true;
+}
+
+__global__ void __launch_bounds__(AR_THREADS) nvls_ar_add_rmsnorm_kernel(
+    char* uc, char* mc, int world, int rank, const bf16* partial, long ldp, bf16* res, const float* w1p, bf16* out,
+    int rows, int H, float eps, long slot_elems, int* epoch, int* done, int* err, unsigned long long timeout_ns) {
+  __shared__ float red[32];
+  __shared__ int s_epoch, s_ok;
+  if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile int*>(epoch) + 1;
+  __syncthreads();
+  const int e = s_epoch;
+  const int slot = e & 1;
+  const long slot_bytes = 3 * slot_elems * 2;
+  bf16* part_uc = reinterpret_cast<bf16*>(uc + slot * slot_bytes);
+  bf16* part_mc = reinterpret_cast<bf16*>(mc + slot * slot_bytes);
+  bf16* x_uc = part_uc + slot_elems;
+  bf16* x_mc = part_mc + slot_elems;
+  bf16* h_uc = part_uc + 2 * slot_elems;
+  bf16* h_mc = part_mc + 2 * slot_elems;
+  unsigned* cnt_uc = reinterpret_cast<unsigned*>(uc + 2 * slot_bytes);
+  unsigned* cnt_mc = reinterpret_cast<unsigned*>(mc + 2 * slot_bytes);
+  const unsigned target = (unsigned)e * (unsigned)world * gridDim.x;
+  const int G = gridDim.x, b = blockIdx.x;
+  // A. stage the local partial (all rows: every rank's slice is read by its owner via the switch)
+  for (int r = b; r < rows; r += G)
+    for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8)
+      *reinterpret_cast<uint4*>(part_uc + (long)r * H + i) = *reinterpret_cast<const uint4*>(partial + (long)r * ldp + i);
+  __syncthreads();
+  if (threadIdx.x == 0) s_ok = nvls_barrier(cnt_mc, cnt_uc, target, err, timeout_ns);
+  __syncthreads();
+  if (s_ok) {
+    // B. this rank's rows: switch-reduced sum, residual add, RMSNorm, multicast the results
+    const int per = (rows + world - 1) / world;
+    const int r0 = rank * per, r1 = min(rows, r0 + per);
+    for (int r = r0 + b; r < r1; r += G) {
+      float acc[16];
+      float ss = 0.f;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int i = (threadIdx.x + c * AR_THREADS) * 8;
+        if (i < H) {
+          const uint4 sm = mc_ld_reduce_bf16x8(part_mc + (long)r * H + i);
+          const uint4 rr = *reinterpret_cast<const uint4*>(res + (long)r * H + i);
+          const bf16* sv = reinterpret_cast<const bf16*>(&sm);
+          const bf16* rv = reinterpret_cast<const bf16*>(&rr);
+          uint4 nr;
+          bf16* nv = reinterpret_cast<bf16*>(&nr);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            nv[u] = __float2bfloat16(__bfloat162float(rv[u]) + __bfloat162float(sv[u]));
+            acc[c * 8 + u] = __bfloat162float(nv[u]);
+            ss += acc[c * 8 + u] * acc[c * 8 + u];
+          }
+          mc_st_16(x_mc + (long)r * H + i, nr);
+        }
+      }
+      ss = warp_sum(ss);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+      __syncthreads();
+      if (threadIdx.x < 32) {
+        float t = threadIdx.x < AR_THREADS / 32 ? red[threadIdx.x] : 0.f;
+        t = warp_sum(t);
+        if (threadIdx.x == 0) red[0] = t;
+      }
+      __syncthreads();
+      const float inv = rsqrtf(red[0] / H + eps);
+      __syncthreads();
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        const int i = (threadIdx.x + c * AR_THREADS) * 8;
+        if (i < H) {
+          uint4 o;
+          bf16* ov = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) ov[u] = __float2bfloat16(acc[c * 8 + u] * inv * w1p[i + u]);
+          mc_st_16(h_mc + (long)r * H + i, o);
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) s_ok = nvls_barrier(cnt_mc + 1, cnt_uc + 1, target, err, timeout_ns);
+    __syncthreads();
+    // C. every row's results, from this rank's own copy of the x/h areas
+    if (s_ok) {
+      for (int r = b; r < rows; r += G)
+        for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8) {
+          const uint4 xv = __ldcv(reinterpret_cast<const uint4*>(x_uc + (long)r * H + i));
+          const uint4 hv = __ldcv(reinterpret_cast<const uint4*>(h_uc + (long)r * H + i));
+          *reinterpret_cast<uint4*>(res + (long)r * H + i) = xv;
+          *reinterpret_cast<uint4*>(out + (long)r * H + i) = hv;
+        }
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int d = atomicAdd(done, 1);
+    if (d == (int)gridDim.x - 1) {
+      *done = 0;
+      __threadfence();
+      atomicExch(epoch, e);
+    }
+  }
+}
+
+long nvls_region_bytes(long slot_elems) { return 2 * 3 * slot_elems * 2 + 256; }
+
+int nvls_ar_add_rmsnorm(void* uc, void* mc, int world, int rank, const void* partial, long ldp, void* res,
+                        const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int grid,
+                        int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s) {
+  if (world < 1 || world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || (long)rows * H > slot_elems || grid < 1 ||
+      (reinterpret_cast<uintptr_t>(uc) | reinterpret_cast<uintptr_t>(mc)) % 16)
+    return -1;
+  nvls_ar_add_rmsnorm_kernel<<<grid, AR_THREADS, 0, s>>>((char*)uc, (char*)mc, world, rank, (const bf16*)partial, ldp,
+                                                         (bf16*)res, w1p, (bf16*)out, rows, H, eps, slot_elems, epoch,
+                                                         done, err, timeout_ns);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace qb
