@@ -55,22 +55,27 @@ def _by_path(name: str, path: str):
     return mod
 
 
-def _ckpt_dir(args, need_bytes: int) -> str:
-    """Where the random checkpoint lives on this box: ``QB_REF_CKPT_DIR`` if set, else the
-    first of /dev/shm, /tmp and the repository's parent with room for it."""
+def _ckpt_dir(args, need_bytes: int, dense_bytes: int) -> tuple[str, bool]:
+    """Where the random checkpoint lives on this box, and whether its expert codes must be file
+    holes: ``QB_REF_CKPT_DIR`` if set, else the first of /tmp, the repository's parent and
+    /dev/shm with room for all of it (random codes), else the first with room for everything but
+    the codes (zero codes as holes)."""
     env = os.environ.get("QB_REF_CKPT_DIR")
     if env:
-        return env
-    name = f"qb_ref_ckpt_{args.model}_s{args.seed}"
-    for base in ("/dev/shm", "/tmp", os.path.dirname(ROOT)):
-        try:
-            have = os.path.exists(os.path.join(base, name))
-            free = shutil.disk_usage(base).free
-        except OSError:
-            continue
-        if have or free > need_bytes * 1.05:
-            return os.path.join(base, name)
-    raise RuntimeError(f"no filesystem has {need_bytes / 1e9:.0f} GB free for the random checkpoint")
+        return env, False
+    bases = ("/tmp", os.path.dirname(ROOT), "/dev/shm")
+    for zero in (False, True):
+        name = f"qb_ref_ckpt_{args.model}_s{args.seed}" + ("_zc" if zero else "")
+        need = dense_bytes if zero else need_bytes
+        for base in bases:
+            try:
+                have = os.path.exists(os.path.join(base, name))
+                free = shutil.disk_usage(base).free
+            except OSError:
+                continue
+            if have or free > need * 1.1 + 8e9:
+                return os.path.join(base, name), zero
+    raise RuntimeError(f"no filesystem has {dense_bytes / 1e9:.0f} GB free for the random checkpoint")
 
 
 def prepare_checkpoint(args, rank: int, world: int, device, timeout_s: float = 1200.0) -> str:
@@ -85,17 +90,18 @@ def prepare_checkpoint(args, rank: int, world: int, device, timeout_s: float = 1
     cfg = full_config() if args.model == "full" else tiny_config()
     cfg = type(cfg)(**{**cfg.__dict__, "mtp_layers": 0})  # MTP is off in this configuration
     shards = wmod.checkpoint_shards(cfg)
-    sizes = []
+    sizes, dense = [], 0
     for specs in shards:
         sizes.append(sum(int(torch.Size(s).numel()) * (2 if k == "bf16" else 1) for _, k, s in specs))
-    path = _ckpt_dir(args, sum(sizes))
+        dense += sum(int(torch.Size(s).numel()) * (2 if k == "bf16" else 1) for _, k, s in specs if k != "codes")
+    path, zero = _ckpt_dir(args, sum(sizes), dense)
     n = len(shards)
     files = [os.path.join(path, f"model-{i + 1:05d}-of-{n:05d}.safetensors") for i in range(n)]
     mine = [i for i in range(n) if i % world == rank and not os.path.exists(files[i])]
     t0 = time.perf_counter()
     if mine:
         wmod.write_random_checkpoint(path, cfg, seed=args.seed, only=mine, device=device,
-                                     write_config=(rank == 0))
+                                     write_config=(rank == 0), zero_codes=zero)
     elif rank == 0 and not os.path.exists(os.path.join(path, "config.json")):
         wmod.write_random_checkpoint(path, cfg, seed=args.seed, only=[], device=device, write_config=True)
     while not (all(os.path.exists(f) for f in files) and os.path.exists(os.path.join(path, "config.json"))):
@@ -103,8 +109,10 @@ def prepare_checkpoint(args, rank: int, world: int, device, timeout_s: float = 1
             raise RuntimeError("timed out waiting for the other ranks' checkpoint shards")
         time.sleep(0.5)
     if rank == 0:
-        print(f"[reference] checkpoint {path}: {sum(sizes) / 1e9:.1f} GB in {n} shards, "
+        print(f"[reference] checkpoint {path}: {sum(sizes) / 1e9:.1f} GB in {n} shards"
+              f"{' (expert codes as zero-filled holes: no room for random codes)' if zero else ''}, "
               f"{time.perf_counter() - t0:.0f}s", file=sys.stderr, flush=True)
+    args.ref_zero_codes = zero
     return path
 
 
@@ -261,7 +269,10 @@ def main(args, report) -> None:
                            f"engine (stock SEED_* defaults, graph capture on)" if args.model == "full"
                            else "tiny parity model, reference engine"),
                  expert_storage="all layers distinct",
-                 extra={"reference_tree": "baseline/_ref (plain copy of the reference)", "checkpoint": ckpt})
+                 extra={"reference_tree": "baseline/_ref (plain copy of the reference)", "checkpoint": ckpt,
+                        "checkpoint_expert_codes": "zeros (file holes; the box's disk cannot hold the random "
+                        "codes; every byte is still read and multiplied)" if getattr(args, "ref_zero_codes", False)
+                        else "random"})
     res["e2e"]["h2d_bytes_per_step"] = None  # the reference's copies are not counted here
     res["e2e"]["d2h_bytes_per_step"] = None
     print(json.dumps(res), flush=True)

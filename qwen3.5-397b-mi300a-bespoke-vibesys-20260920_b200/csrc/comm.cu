@@ -406,19 +406,19 @@ int symm_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* par
 //
 // The region is one symmetric allocation bound to an NVSwitch multicast object: `uc` is this
 // rank's own (unicast) mapping, `mc` the multicast address of the same bytes on every rank.
-// Layout: two slots (call parity) of [partial | x | h], each [rows_cap, H] bf16, then two
+// Layout: two slots (call parity) of [partial | x], each [rows_cap, H] bf16, then two
 // monotonically increasing u32 arrival counters. A call with index e (device epoch + 1):
 //   A. every CTA copies its rows of the local partial into slot e&1 (unicast stores), then one
 //      thread adds 1 to counter 0 on EVERY rank at once (multimem.red.release) and waits,
 //      bounded, until its local copy reaches e * world * grid (all ranks' CTAs arrived);
 //   B. rank r owns rows [r*per, (r+1)*per): for each, multimem.ld_reduce makes the switch return
 //      the sum over all ranks (fp32 accumulation, one bf16 rounding), the kernel adds the
-//      residual, normalises, and multimem.st writes the new residual row and its norm into
-//      every rank's x/h areas with one store each;
-//   C. counter 1 the same way, then every CTA copies the rows from the local x/h areas into the
-//      output tensors.
-// Each rank's rows are reduced and normalised by one rank only, so every rank ends with
-// identical bits. The counters wrap safely (signed distance). Slot e&1 is rewritten at call
+//      residual and multimem.st writes the new residual row into every rank's x area with one
+//      store;
+//   C. counter 1 the same way, then every CTA takes rows from the local x area: the new
+//      residual, and its RMSNorm computed locally.
+// Each row is reduced by one rank only, so every rank ends with identical bits, and the norm is
+// recomputed from those bits rather than sent (NVLink carries the partials once and x once). The counters wrap safely (signed distance). Slot e&1 is rewritten at call
 // e+2, after every rank passed counter 1 of call e+1, so no rank still reads it. Accesses
 // through the multicast and unicast addresses of the same memory are ordered with
 // fence.proxy.alias. No TMA and no cluster multicast are involved.
@@ -474,13 +474,11 @@ __global__ void __launch_bounds__(AR_THREADS) nvls_ar_add_rmsnorm_kernel(
   __syncthreads();
   const int e = s_epoch;
   const int slot = e & 1;
-  const long slot_bytes = 3 * slot_elems * 2;
+  const long slot_bytes = 2 * slot_elems * 2;
   bf16* part_uc = reinterpret_cast<bf16*>(uc + slot * slot_bytes);
   bf16* part_mc = reinterpret_cast<bf16*>(mc + slot * slot_bytes);
-  bf16* x_uc = part_uc + slot_elems;
+  const bf16* x_uc = part_uc + slot_elems;
   bf16* x_mc = part_mc + slot_elems;
-  bf16* h_uc = part_uc + 2 * slot_elems;
-  bf16* h_mc = part_mc + 2 * slot_elems;
   unsigned* cnt_uc = reinterpret_cast<unsigned*>(uc + 2 * slot_bytes);
   unsigned* cnt_mc = reinterpret_cast<unsigned*>(mc + 2 * slot_bytes);
   const unsigned target = (unsigned)e * (unsigned)world * gridDim.x;
@@ -493,66 +491,66 @@ __global__ void __launch_bounds__(AR_THREADS) nvls_ar_add_rmsnorm_kernel(
   if (threadIdx.x == 0) s_ok = nvls_barrier(cnt_mc, cnt_uc, target, err, timeout_ns);
   __syncthreads();
   if (s_ok) {
-    // B. this rank's rows: switch-reduced sum, residual add, RMSNorm, multicast the results
+    // B. this rank's rows: switch-reduced sum (one bf16 rounding), residual add, and the new
+    //    residual row multicast into every rank's x area
     const int per = (rows + world - 1) / world;
     const int r0 = rank * per, r1 = min(rows, r0 + per);
-    for (int r = r0 + b; r < r1; r += G) {
-      float acc[16];
-      float ss = 0.f;
+    for (int r = r0 + b; r < r1; r += G)
+      for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8) {
+        const uint4 sm = mc_ld_reduce_bf16x8(part_mc + (long)r * H + i);
+        const uint4 rr = *reinterpret_cast<const uint4*>(res + (long)r * H + i);
+        const bf16* sv = reinterpret_cast<const bf16*>(&sm);
+        const bf16* rv = reinterpret_cast<const bf16*>(&rr);
+        uint4 nr;
+        bf16* nv = reinterpret_cast<bf16*>(&nr);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int i = (threadIdx.x + c * AR_THREADS) * 8;
-        if (i < H) {
-          const uint4 sm = mc_ld_reduce_bf16x8(part_mc + (long)r * H + i);
-          const uint4 rr = *reinterpret_cast<const uint4*>(res + (long)r * H + i);
-          const bf16* sv = reinterpret_cast<const bf16*>(&sm);
-          const bf16* rv = reinterpret_cast<const bf16*>(&rr);
-          uint4 nr;
-          bf16* nv = reinterpret_cast<bf16*>(&nr);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) {
-            nv[u] = __float2bfloat16(__bfloat162float(rv[u]) + __bfloat162float(sv[u]));
-            acc[c * 8 + u] = __bfloat162float(nv[u]);
-            ss += acc[c * 8 + u] * acc[c * 8 + u];
-          }
-          mc_st_16(x_mc + (long)r * H + i, nr);
-        }
+        for (int u = 0; u < 8; ++u) nv[u] = __float2bfloat16(__bfloat162float(rv[u]) + __bfloat162float(sv[u]));
+        mc_st_16(x_mc + (long)r * H + i, nr);
       }
-      ss = warp_sum(ss);
-      if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
-      __syncthreads();
-      if (threadIdx.x < 32) {
-        float t = threadIdx.x < AR_THREADS / 32 ? red[threadIdx.x] : 0.f;
-        t = warp_sum(t);
-        if (threadIdx.x == 0) red[0] = t;
-      }
-      __syncthreads();
-      const float inv = rsqrtf(red[0] / H + eps);
-      __syncthreads();
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        const int i = (threadIdx.x + c * AR_THREADS) * 8;
-        if (i < H) {
-          uint4 o;
-          bf16* ov = reinterpret_cast<bf16*>(&o);
-#pragma unroll
-          for (int u = 0; u < 8; ++u) ov[u] = __float2bfloat16(acc[c * 8 + u] * inv * w1p[i + u]);
-          mc_st_16(h_mc + (long)r * H + i, o);
-        }
-      }
-    }
     __syncthreads();
     if (threadIdx.x == 0) s_ok = nvls_barrier(cnt_mc + 1, cnt_uc + 1, target, err, timeout_ns);
     __syncthreads();
-    // C. every row's results, from this rank's own copy of the x/h areas
+    // C. every row from this rank's own copy of the x area: the new residual and its RMSNorm
+    //    (each rank normalises locally from identical bits, so the norms agree too)
     if (s_ok) {
-      for (int r = b; r < rows; r += G)
-        for (int i = threadIdx.x * 8; i < H; i += AR_THREADS * 8) {
-          const uint4 xv = __ldcv(reinterpret_cast<const uint4*>(x_uc + (long)r * H + i));
-          const uint4 hv = __ldcv(reinterpret_cast<const uint4*>(h_uc + (long)r * H + i));
-          *reinterpret_cast<uint4*>(res + (long)r * H + i) = xv;
-          *reinterpret_cast<uint4*>(out + (long)r * H + i) = hv;
+      for (int r = b; r < rows; r += G) {
+        uint4 xv[2];
+        float ss = 0.f;
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int i = (threadIdx.x + c * AR_THREADS) * 8;
+          if (i < H) {
+            xv[c] = __ldcv(reinterpret_cast<const uint4*>(x_uc + (long)r * H + i));
+            const bf16* v = reinterpret_cast<const bf16*>(&xv[c]);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) ss += __bfloat162float(v[u]) * __bfloat162float(v[u]);
+            *reinterpret_cast<uint4*>(res + (long)r * H + i) = xv[c];
+          }
         }
+        ss = warp_sum(ss);
+        if ((threadIdx.x & 31) == 0) red[threadIdx.x / 32] = ss;
+        __syncthreads();
+        if (threadIdx.x < 32) {
+          float t = threadIdx.x < AR_THREADS / 32 ? red[threadIdx.x] : 0.f;
+          t = warp_sum(t);
+          if (threadIdx.x == 0) red[0] = t;
+        }
+        __syncthreads();
+        const float inv = rsqrtf(red[0] / H + eps);
+        __syncthreads();
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          const int i = (threadIdx.x + c * AR_THREADS) * 8;
+          if (i < H) {
+            const bf16* v = reinterpret_cast<const bf16*>(&xv[c]);
+            uint4 o;
+            bf16* ov = reinterpret_cast<bf16*>(&o);
+#pragma unroll
+            for (int u = 0; u < 8; ++u) ov[u] = __float2bfloat16(__bfloat162float(v[u]) * inv * w1p[i + u]);
+            *reinterpret_cast<uint4*>(out + (long)r * H + i) = o;
+          }
+        }
+      }
     }
   }
   __syncthreads();
@@ -567,7 +565,7 @@ __global__ void __launch_bounds__(AR_THREADS) nvls_ar_add_rmsnorm_kernel(
   }
 }
 
-long nvls_region_bytes(long slot_elems) { return 2 * 3 * slot_elems * 2 + 256; }
+long nvls_region_bytes(long slot_elems) { return 2 * 2 * slot_elems * 2 + 256; }
 
 int nvls_ar_add_rmsnorm(void* uc, void* mc, int world, int rank, const void* partial, long ldp, void* res,
                         const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int grid,

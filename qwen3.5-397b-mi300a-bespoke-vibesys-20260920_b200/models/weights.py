@@ -465,15 +465,17 @@ def checkpoint_shards(cfg: Qwen35Config) -> list[list[tuple[str, str, tuple[int,
 
 
 def write_random_checkpoint(path: str, cfg: Qwen35Config, seed: int = 0, only: list[int] | None = None,
-                            device: str | torch.device = "cpu", write_config: bool = True) -> list[str]:
+                            device: str | torch.device = "cpu", write_config: bool = True,
+                            zero_codes: bool = False) -> list[str]:
     """Write a random-init checkpoint of ``cfg`` (any size, the full geometry included) in the
     published naming and layout, one safetensors file per shard of ``checkpoint_shards``:
     bf16 tensors N(0, 0.02); routed experts as packed e2m1 codes (uniform random bytes) with
     e8m0 scales 2^-7 .. 2^-5 (the block scales an N(0, 0.02) matrix quantises to). Tensors are
     generated one at a time on ``device`` and streamed to the file, so host memory stays at one
     tensor. ``only`` restricts the call to those shard indices (ranks can split the work); the
-    shard's own seed makes its bytes independent of which process writes it. Returns the paths
-    written."""
+    shard's own seed makes its bytes independent of which process writes it. ``zero_codes``
+    leaves the routed experts' code bytes as file holes (zeros, no disk blocks) for a disk that
+    cannot hold ~190 GB of codes; readers still read every byte. Returns the paths written."""
     import struct
 
     os.makedirs(path, exist_ok=True)
@@ -500,11 +502,15 @@ def write_random_checkpoint(path: str, cfg: Qwen35Config, seed: int = 0, only: l
             for name, kind, shape in specs:
                 if kind == "bf16":
                     t = (torch.randn(*shape, generator=gen, device=dev) * 0.02).to(torch.bfloat16)
+                elif kind == "codes" and zero_codes:
+                    f.seek(int(torch.Size(shape).numel()), os.SEEK_CUR)  # a hole: reads as zeros
+                    continue
                 elif kind == "codes":
                     t = torch.randint(0, 256, shape, generator=gen, device=dev, dtype=torch.uint8)
                 else:
                     t = torch.randint(120, 123, shape, generator=gen, device=dev, dtype=torch.uint8)
                 f.write(t.contiguous().view(torch.uint8).cpu().numpy().tobytes())
+            f.truncate(f.tell())  # a trailing hole still counts toward the file size
         os.replace(tmp, fn)
         written.append(fn)
     if write_config:

@@ -9,7 +9,9 @@ Times each variant with CUDA events over many back-to-back calls (max over ranks
 microseconds per call, bus bandwidth (2 (N-1)/N x bytes / time, the NCCL convention) and the
 fraction of the NVLink roofline of `fused`: an all-reduce without in-switch reduction must move
 2 (N-1)/N x the message bytes through every GPU's links, at 770 GB/s measured per-direction
-peer bandwidth.
+peer bandwidth. `nvls` (when the fabric has multicast): the switch-reduced kernel, whose
+roofline is (1 + 1/N) x the message bytes into every GPU (its reduced rows, then every result
+row).
 
 ``--case ep``: expert-parallel MoE (dispatch -> block-scaled expert GEMMs -> combine over peer
 memory, ``parallel.ep``) at the full geometry (512 experts top-10, hidden 4096, expert width
@@ -189,6 +191,7 @@ def main():
         return
     H = args.hidden
     symm = SymmComm(rank, world, dev, max_rows=min(512, max(args.tokens)), hidden=H, sp_rows=max(args.tokens))
+    have_nvls = symm.enable_nvls(rows_cap=max(args.tokens), min_rows=1 << 30)  # only when asked by kind
     w = torch.ones(H, device=dev)
     rows_out = []
     for T in args.tokens:
@@ -209,8 +212,13 @@ def main():
             dist.all_reduce(y)
             ops.add_rmsnorm(y.bfloat16(), res, w, 1e-6)
 
+        def nvls():
+            symm.allreduce_add_rmsnorm(x, res, w, 1e-6, kind="nvls")
+
         out = {"tokens": T, "bytes": T * H * 2}
         variants = [("fused", fused), ("nccl", nccl), ("sp", sp)]
+        if have_nvls:
+            variants.append(("nvls", nvls))
         if T <= symm.max_rows:
             variants.append(("oneshot", oneshot))
         for name, fn in variants:
@@ -234,6 +242,10 @@ def main():
         roof_us = 2 * (world - 1) / world * out["bytes"] / (PEER_GBS * 1e3)
         out["roofline_us"] = round(roof_us, 2)
         out["fused_frac_of_roofline"] = round(roof_us / out["fused_us"], 3)
+        if have_nvls:  # with in-switch reduction a GPU takes in its reduced rows and every result row
+            nv_roof = (1 + 1 / world) * out["bytes"] / (PEER_GBS * 1e3)
+            out["nvls_roofline_us"] = round(nv_roof, 2)
+            out["nvls_frac_of_roofline"] = round(nv_roof / out["nvls_us"], 3)
         rows_out.append(out)
     if rank == 0:
         for r in rows_out:

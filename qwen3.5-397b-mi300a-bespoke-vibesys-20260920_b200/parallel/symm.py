@@ -89,6 +89,66 @@ class _nullctx:
         return False
 
 
+class NvlsRegion:
+    """A symmetric region bound to an NVSwitch multicast object (NVLS), for the switch-reduced
+    all-reduce + residual add + RMSNorm of large messages (``csrc/comm.cu``,
+    ``nvls_ar_add_rmsnorm_kernel``). The memory comes from PyTorch's symmetric-memory allocator
+    (``torch.distributed._symmetric_memory``: one physical allocation per rank, every peer's
+    mapped, plus the multicast address when the fabric supports it); the kernels are this
+    package's. Every rank must construct it together; when any rank gets no multicast address
+    all of them raise ``SymmUnavailable`` (``vote_or_raise``). Reference counterpart: none (the
+    reference's MI300A fabric has no in-switch reduction); its large-message path is the
+    row-sharded reduce-scatter + norm + all-gather family.
+
+    The grid is fixed per region (the arrival counters count ``world x grid`` arrivals per
+    call), and so is ``rows_cap``."""
+
+    GRID = 148
+
+    def __init__(self, rank: int, world: int, device, rows_cap: int, hidden: int, group=None,
+                 timeout_s: float = 10.0):
+        self.rank, self.world, self.device = rank, world, torch.device(device)
+        self.rows_cap, self.hidden, self.timeout_s = rows_cap, hidden, timeout_s
+        self.slot_elems = rows_cap * hidden
+        self.buf = None
+        err = None
+        mc = 0
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+
+            pg = group or dist.group.WORLD
+            name = pg.group_name
+            if hasattr(symm_mem, "enable_symm_mem_for_group"):
+                try:
+                    symm_mem.enable_symm_mem_for_group(name)
+                except Exception:  # noqa: BLE001 - newer releases need no enabling
+                    pass
+            nbytes = int(ext().nvls_region_bytes(self.slot_elems))
+            self.buf = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
+            self.hdl = symm_mem.rendezvous(self.buf, name)
+            mc = int(getattr(self.hdl, "multicast_ptr", 0) or 0)
+            if mc == 0:
+                raise RuntimeError("no multicast address (NVLS unsupported on this fabric or driver)")
+            self.buf.zero_()
+            torch.cuda.synchronize(self.device)
+        except Exception as e:  # noqa: BLE001 - reported through the vote
+            err = e
+        vote_or_raise(err is None, err, self.device, "NVLS multicast region", group)
+        dist.barrier(group=group)  # every rank's counters are zero before any rank arrives
+        self.uc = self.buf.data_ptr()
+        self.mc = mc
+        self.epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
+
+    def allreduce_add_rmsnorm(self, partial, residual, w1p, eps):
+        rows = residual.numel() // residual.shape[-1]
+        if rows > self.rows_cap:
+            return None
+        normed = torch.empty_like(residual)
+        ext().nvls_ar_add_rmsnorm(self.uc, self.mc, self.world, self.rank, partial, residual, w1p, normed,
+                                  float(eps), self.slot_elems, self.GRID, self.epoch, self.timeout_s)
+        return residual, normed
+
+
 class SymmComm:
     """One-shot region (``max_rows`` rows) for decode-sized messages and, when ``sp_rows`` > 0, a
     sequence-parallel region for prefill-sized ones (reduce-scatter + add + RMSNorm +
@@ -124,6 +184,21 @@ class SymmComm:
                 self.close()  # the one-shot region is undone on every rank alike
                 raise
             self.sp_epoch = torch.zeros(2, dtype=torch.int32, device=self.device)
+        self.nvls = None
+        self.nvls_min_rows = 1 << 30
+
+    def enable_nvls(self, rows_cap: int, min_rows: int, group=None) -> bool:
+        """Add the NVLS region (every rank together); messages of ``min_rows`` rows and more
+        then take the switch-reduced kernel. False, on every rank, when the fabric has no
+        multicast support."""
+        try:
+            self.nvls = NvlsRegion(self.rank, self.world, self.device, rows_cap, self.hidden, group,
+                                   self.timeout_s)
+        except SymmUnavailable:
+            self.nvls = None
+            return False
+        self.nvls_min_rows = min_rows
+        return True
 
     @staticmethod
     def sp_region_bytes(sp_rows: int, hidden: int) -> int:
@@ -153,6 +228,14 @@ class SymmComm:
         one); None when the message fits neither region."""
         rows = residual.numel() // residual.shape[-1]
         normed = torch.empty_like(residual)
+        nvls = getattr(self, "nvls", None)
+        if kind == "nvls" or (kind == "auto" and nvls is not None and rows >= self.nvls_min_rows):
+            if nvls is not None:
+                out = nvls.allreduce_add_rmsnorm(partial, residual, w1p, eps)
+                if out is not None:
+                    return out
+            if kind == "nvls":
+                return None
         fits_sp = self.sp_bases is not None and rows <= self.sp_rows
         if kind == "sp":
             use_sp = fits_sp
@@ -174,6 +257,8 @@ class SymmComm:
         """Whether ``linear_allreduce_add_rmsnorm`` takes the fused GEMM -> reduce-scatter path
         for ``rows`` (the sizes the automatic choice gives the sequence-parallel kernel)."""
         if self.sp_bases is None or rows < 1:
+            return False
+        if self.nvls is not None and rows >= self.nvls_min_rows and rows <= self.nvls.rows_cap:
             return False
         return rows <= self.sp_rows and (rows > self.max_rows or rows * (self.world - 1) > self.ONESHOT_ROW_BUDGET)
 

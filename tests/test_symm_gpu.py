@@ -44,30 +44,52 @@ def test_peer_that_never_signals_times_out_cleanly():
     ext().symm_free(fake_peer)
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_two_gpu_fused_equals_nccl():
+def _world() -> int:
+    """Ranks for the multi-GPU checks: every visible GPU, up to 8."""
+    return min(torch.cuda.device_count(), 8)
+
+
+def _port() -> int:
     s = socket.socket()
     s.bind(("127.0.0.1", 0))
     port = s.getsockname()[1]
     s.close()
+    return port
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_multi_gpu_nvls_equals_nccl():
+    """NVLS switch-reduced all-reduce + add + RMSNorm on every visible GPU (up to 8) against NCCL
+    all-reduce + add + RMSNorm; skips when the fabric offers no multicast object."""
+    world, port = _world(), _port()
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "nvls_rank.py"), str(r), str(world), str(port)])
+             for r in range(world)]
+    rcs = [p.wait(timeout=300) for p in procs]
+    if all(rc == 3 for rc in rcs):
+        pytest.skip("no NVLS multicast support on this fabric")
+    assert rcs == [0] * world, rcs
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_two_gpu_fused_equals_nccl():
+    """Every visible GPU (up to 8): the one-shot and sequence-parallel kernels against NCCL."""
+    world, port = _world(), _port()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "symm_rank.py"), str(r), "2", str(port)], env=env)
-             for r in range(2)]
-    assert [p.wait(timeout=300) for p in procs] == [0, 0]
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "symm_rank.py"), str(r), str(world), str(port)],
+                              env=env) for r in range(world)]
+    assert [p.wait(timeout=300) for p in procs] == [0] * world
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_gpu_model_out_proj_fused_equals_unfused():
-    """Tiny model, 2 ranks: a 1500-token prefill with the attention / DeltaNet out projections
-    fused into the sequence-parallel all-reduce gives the same logits bit for bit."""
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
+    """Tiny model on 2 or 4 ranks (its 4 DeltaNet key heads bound the split): a 1500-token
+    prefill with the attention / DeltaNet out projections fused into the sequence-parallel
+    all-reduce gives the same logits bit for bit."""
+    world, port = (4 if _world() >= 4 else 2), _port()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "sp_model_rank.py"), str(r), "2", str(port)],
-                              env=env) for r in range(2)]
-    assert [p.wait(timeout=300) for p in procs] == [0, 0]
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "sp_model_rank.py"), str(r), str(world), str(port)],
+                              env=env) for r in range(world)]
+    assert [p.wait(timeout=300) for p in procs] == [0] * world
 
 
 def test_expert_parallel_one_rank_equals_local_moe():
@@ -133,11 +155,8 @@ def test_expert_parallel_silent_peer_times_out_cleanly():
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_gpu_expert_parallel_equals_local():
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
+    world, port = _world(), _port()
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ep_rank.py"), str(r), "2", str(port)], env=env)
-             for r in range(2)]
-    assert [p.wait(timeout=300) for p in procs] == [0, 0]
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ep_rank.py"), str(r), str(world), str(port)],
+                              env=env) for r in range(world)]
+    assert [p.wait(timeout=300) for p in procs] == [0] * world
