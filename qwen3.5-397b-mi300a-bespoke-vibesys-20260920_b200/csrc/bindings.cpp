@@ -303,6 +303,26 @@ Tensor gated_delta_chunked(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, 
   return out;
 }
 
+// chunked gated delta rule on tcgen05 (state in TMEM): same contract as gated_delta_chunked
+Tensor gated_delta_tc(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, Tensor state, Tensor seg_lane, Tensor chunks,
+                      Tensor seg_chunk0, int64_t nk, int64_t nv, int64_t dk, int64_t dv, bool commit) {
+  CHECK_BF16(qkv);
+  TORCH_CHECK(state.scalar_type() == at::kFloat, "delta_tc: fp32 state");
+  TORCH_CHECK(state.stride(3) == 1 && state.stride(2) == dv && state.stride(1) == dk * dv, "delta_tc: state layout");
+  TORCH_CHECK(chunks.dim() == 2 && chunks.size(1) == 3, "delta_tc: chunks [n, 3]");
+  TORCH_CHECK(qkv.stride(1) == 1 && qkv.stride(0) % 8 == 0, "delta_tc: qkv rows 16-byte aligned");
+  const int T = qkv.size(0), n_chunks = chunks.size(0);
+  Tensor out = at::empty({T, nv, dv}, qkv.options());
+  Tensor scratch = at::empty({qb::gated_delta_tc_scratch(T, n_chunks, nk, nv)}, qkv.options().dtype(at::kFloat));
+  LAUNCH(qb::gated_delta_tc(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0), a_log.data_ptr<float>(),
+                            dt_bias.data_ptr<float>(), state.data_ptr<float>(), state.stride(0),
+                            seg_lane.data_ptr<int>(), chunks.data_ptr<int>(), n_chunks, seg_chunk0.data_ptr<int>(),
+                            seg_lane.size(0), T, nk, nv, dk, dv, scratch.data_ptr<float>(), out.data_ptr(), commit,
+                            err_ptr(qkv), stream()));
+  g_launches.fetch_add(2, std::memory_order_relaxed);  // glue prep + chunk prep + state kernels
+  return out;
+}
+
 // ------------------------------------------------------------------ moe
 Tensor moe_routed_impl(Tensor h, Tensor topw, Tensor topi, Tensor w13, c10::optional<Tensor> s13, Tensor w2,
                        c10::optional<Tensor> s2, int64_t first, int64_t count) {
@@ -616,6 +636,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_moe", &ep_moe);
   m.def("ep_region_bytes", &ep_region_bytes);
   m.def("gated_delta_chunked", &gated_delta_chunked);
+  m.def("gated_delta_tc", &gated_delta_tc);
   m.def("causal_conv_varlen", &causal_conv_varlen);
   m.def("gated_delta_varlen", &gated_delta_varlen);
   m.def("moe_routed_fp4", &moe_routed_fp4);

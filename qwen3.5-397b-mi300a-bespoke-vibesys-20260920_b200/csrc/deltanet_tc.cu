@@ -1,0 +1,507 @@
+// Chunked gated delta rule for prefill segments with the state on the 5th-generation tensor
+// cores (tcgen05 + TMEM), for key/value head size 128.
+//
+// Same chunkwise (WY) identities as deltanet.cu (Yang et al., "Parallelizing Linear Transformers
+// with the Delta Rule over Sequence Length", NeurIPS 2024; "Gated Delta Networks", ICLR 2025):
+// with G the cumulative log decay inside a chunk of C = 64 tokens and S0 [dk, dv] the state
+// entering it,
+//   T = (I + A)^-1,  A_ts = beta_t (k_t . k_s) e^(G_t - G_s)  (s < t)
+//   U = T diag(beta) V,  W = T diag(beta e^G) K
+//   Delta = U - W S0
+//   O     = diag(e^G) Q S0 + Mq Delta,     Mq_ts = (q_t . k_s) e^(G_t - G_s)  (s <= t)
+//   S     = e^(G_last) S0 + (diag(e^(G_last - G)) K)^T Delta
+//
+// dn_tc_prep (grid: chunk x value head, every chunk at once, CUDA cores in fp32): the two 64x64
+// Gram products, the unit lower-triangular inverse T by forward substitution (one column per
+// four threads), U and W, and a per-(chunk, head) record in exactly the shared-memory image the
+// state kernel's MMAs read: U fp32, then W, Q e^G, Mq (bf16, K-major, 128-byte swizzle) and
+// K e^(G_last - G) (bf16, M-major), and e^(G_last).
+//
+// dn_tc_state (grid: segment x value head, 128 threads): walks the segment's chunks in order with
+// the fp32 state S in tensor memory (lane = key row, 128 columns). Per chunk, after one bulk copy
+// of the record: S is read once (tcgen05.ld) to a bf16 MN-major operand and written back scaled
+// by e^(G_last); MMA  D1 = W S;  threads form Delta = U - D1 (bf16 operand);  MMAs
+// D2 = (Q e^G) S + Mq Delta  and  S += (K e^(G_last-G))^T Delta  (accumulating in TMEM); threads
+// write O = D2. All MMAs are kind::f16 (bf16 operands, fp32 accumulate), M = 128 (the 64-token
+// operands are padded with zero rows), N = 128. The serial depth of a segment is its number of
+// chunks instead of its number of tokens. Waits are bounded (common.cuh) and every wait is
+// followed by a block-wide vote, so all threads leave the chunk loop together and TMEM is
+// released on every path (a wait that runs out only leaves the status word set). Any
+// copies or MMAs still in flight after such a give-up are drained before the release.
+//
+// Reference behaviour: `deltanet_prefill_chunked.py` (the reference's chunked prefill, same
+// published algorithm, fp32 Triton dots), `model.delta_rule_chunked`.
+#include "common.cuh"
+#include "kernels.h"
+
+namespace qb {
+
+using bf16 = __nv_bfloat16;
+
+namespace dntc {
+constexpr int C = 64;      // tokens per chunk
+constexpr int D = 128;     // key and value head size
+constexpr int KP = 132;    // fp32 row pitch of the prep kernel's operand tiles
+constexpr int AP = 65;     // fp32 row pitch of its 64 x 64 tiles
+// record of one (chunk, value head), bytes
+constexpr int R_U = 0;            // [64][128] fp32
+constexpr int R_EGL = 32768;      // e^(G_last), 16 bytes
+constexpr int R_W = 32784;        // 2 K-atoms x [64 rows][128 B]
+constexpr int R_QG = R_W + 16384;
+constexpr int R_M = R_QG + 16384;  // 1 K-atom x [64 rows][128 B]
+constexpr int R_KG = R_M + 8192;   // 2 M-atoms x [64 K-rows][128 B]
+constexpr int R_END = R_KG + 16384;
+constexpr int REC = (R_END + 127) / 128 * 128;
+// state kernel shared memory (offsets from a 1024-byte aligned base)
+constexpr int S_W = 0;            // 2 x 16 KB (128-row K-atoms, rows 64..127 zero)
+constexpr int S_QG = 32768;
+constexpr int S_M = 65536;        // 16 KB (rows 64..127 zero)
+constexpr int S_KG = 81920;       // 16 KB
+constexpr int S_U = 98304;        // U fp32 + e^(G_last)
+constexpr int S_S = 132096;       // S as bf16 MN-major B operand: 2 N-atoms x [128 K-rows][128 B]
+constexpr int S_D = 164864;       // Delta as bf16 MN-major B operand: 2 N-atoms x [64 K-rows][128 B]
+constexpr int S_BAR = 181248;
+constexpr int S_BYTES = S_BAR + 64 + 1024;
+constexpr int PREP_SMEM = (3 * C * KP + 3 * C * AP + 3 * C) * 4;
+constexpr int TM_S = 0, TM_D1 = 128, TM_D2 = 256;
+}  // namespace dntc
+
+__device__ __forceinline__ uint64_t desc_sw128_mn_dn(uint32_t saddr, uint32_t lbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ uint4 pack8(const float* v) {
+  uint4 r;
+  __nv_bfloat162* p = reinterpret_cast<__nv_bfloat162*>(&r);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) p[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+  return r;
+}
+
+// byte offset of element chunk `ch` (8 bf16) of row `r` in a 128-byte swizzled atom
+__device__ __forceinline__ int swz(int r, int ch) { return r * 128 + ((ch ^ (r & 7)) << 4); }
+
+__global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const float* kn, const float* gb,
+                                                         const bf16* qkv, long ldqkv, const int* chunks, int nk,
+                                                         int nv, uint8_t* rec_all) {
+  using namespace dntc;
+  extern __shared__ float sm[];
+  float* Ks = sm;
+  float* Qs = Ks + C * KP;
+  float* Vs = Qs + C * KP;
+  float* A = Vs + C * KP;
+  float* Mq = A + C * AP;
+  float* Tm = Mq + C * AP;
+  float* G = Tm + C * AP;
+  float* Bt = G + C;
+  float* EG = Bt + C;
+  const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int row0 = chunks[c * 3 + 1], rows = chunks[c * 3 + 2];
+  const int hk = h / (nv / nk);
+  uint8_t* rec = rec_all + ((long)c * nv + h) * REC;
+  // ---- operands (rows >= `rows` are zero: they change nothing)
+  for (int idx = tid; idx < C * 32; idx += 256) {
+    const int t = idx >> 5, i = (idx & 31) * 4;
+    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
+    if (t < rows) {
+      const long base = ((long)(row0 + t) * nk + hk) * D + i;
+      kv = *reinterpret_cast<const float4*>(kn + base);
+      qv = *reinterpret_cast<const float4*>(qn + base);
+    }
+    *reinterpret_cast<float4*>(Ks + t * KP + i) = kv;
+    *reinterpret_cast<float4*>(Qs + t * KP + i) = qv;
+  }
+  for (int idx = tid; idx < C * 16; idx += 256) {
+    const int t = idx >> 4, j = (idx & 15) * 8;
+    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    if (t < rows) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(qkv + (long)(row0 + t) * ldqkv + 2L * nk * D + (long)h * D + j);
+      const bf16* e = reinterpret_cast<const bf16*>(&raw);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __bfloat162float(e[u]);
+    }
+    *reinterpret_cast<float4*>(Vs + t * KP + j) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(Vs + t * KP + j + 4) = make_float4(v[4], v[5], v[6], v[7]);
+  }
+  if (tid < C) {
+    const float4 g4 = tid < rows ? *reinterpret_cast<const float4*>(gb + ((long)(row0 + tid) * nv + h) * 4)
+                                 : make_float4(1.f, 0.f, 0.f, 0.f);
+    Bt[tid] = g4.y;
+    G[tid] = g4.z;
+  }
+  __syncthreads();
+  if (tid < 32) {  // inclusive scan of the log decays, two per lane
+    const float a0 = G[2 * tid], a1 = G[2 * tid + 1];
+    float s = a0 + a1;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const float n = __shfl_up_sync(0xffffffffu, s, o);
+      if (tid >= o) s += n;
+    }
+    const float ex = s - (a0 + a1);
+    G[2 * tid] = ex + a0;
+    G[2 * tid + 1] = s;
+  }
+  __syncthreads();
+  if (tid < C) EG[tid] = expf(G[tid]);
+  // ---- A (strictly lower) and Mq (lower incl. diagonal): 4 x 4 outputs per thread
+  {
+    const int ty = tid >> 4, tx = tid & 15;
+    float aa[4][4], mm[4][4];
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int s = 0; s < 4; ++s) aa[r][s] = mm[r][s] = 0.f;
+    for (int i = 0; i < D; i += 4) {
+      float4 kt[4], qt[4], ks[4];
+#pragma unroll
+      for (int r = 0; r < 4; ++r) {
+        kt[r] = *reinterpret_cast<const float4*>(Ks + (4 * ty + r) * KP + i);
+        qt[r] = *reinterpret_cast<const float4*>(Qs + (4 * ty + r) * KP + i);
+        ks[r] = *reinterpret_cast<const float4*>(Ks + (4 * tx + r) * KP + i);
+      }
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int s = 0; s < 4; ++s) {
+          aa[r][s] += kt[r].x * ks[s].x + kt[r].y * ks[s].y + kt[r].z * ks[s].z + kt[r].w * ks[s].w;
+          mm[r][s] += qt[r].x * ks[s].x + qt[r].y * ks[s].y + qt[r].z * ks[s].z + qt[r].w * ks[s].w;
+        }
+    }
+    __syncthreads();  // G and EG complete
+#pragma unroll
+    for (int r = 0; r < 4; ++r)
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int t = 4 * ty + r, u = 4 * tx + s;
+        const float dec = u <= t ? expf(G[t] - G[u]) : 0.f;
+        A[t * AP + u] = u < t ? Bt[t] * aa[r][s] * dec : 0.f;
+        Mq[t * AP + u] = u <= t ? mm[r][s] * dec : 0.f;
+      }
+  }
+  __syncthreads();
+  // ---- T = (I + A)^-1 by forward substitution: column cc by four threads (one warp = 8 columns)
+  {
+    const int cc = tid >> 2, part = tid & 3;
+    for (int t = part; t < C; t += 4) Tm[t * AP + cc] = t == cc ? 1.f : 0.f;
+    __syncwarp();
+    for (int t = 1; t < C; ++t) {
+      float sum = 0.f;
+      if (t > cc)
+        for (int s = cc + part; s < t; s += 4) sum += A[t * AP + s] * Tm[s * AP + cc];
+      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+      if (t > cc && part == 0) Tm[t * AP + cc] = -sum;
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  // ---- U = T diag(beta) V (fp32 record), W = T diag(beta e^G) K (bf16 K-major image): 8 x 8 per thread
+  {
+    const int gy = tid >> 5, gx = tid & 31;
+    const bool isU = gx < 16;
+    const float* src = isU ? Vs + gx * 8 : Ks + (gx - 16) * 8;
+    float acc[8][8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
+    for (int s = 0; s < C; ++s) {
+      const float sc = isU ? Bt[s] : Bt[s] * EG[s];
+      const float4 r0 = *reinterpret_cast<const float4*>(src + s * KP);
+      const float4 r1 = *reinterpret_cast<const float4*>(src + s * KP + 4);
+      const float rv[8] = {r0.x * sc, r0.y * sc, r0.z * sc, r0.w * sc, r1.x * sc, r1.y * sc, r1.z * sc, r1.w * sc};
+#pragma unroll
+      for (int r = 0; r < 8; ++r) {
+        const float tv = Tm[(8 * gy + r) * AP + s];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[r][e] += tv * rv[e];
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const int t = 8 * gy + r;
+      if (isU) {
+        float* u = reinterpret_cast<float*>(rec + R_U) + t * D + gx * 8;
+        *reinterpret_cast<float4*>(u) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+        *reinterpret_cast<float4*>(u + 4) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+      } else {
+        const int i = (gx - 16) * 8;
+        *reinterpret_cast<uint4*>(rec + R_W + (i >> 6) * 8192 + swz(t, (i & 63) >> 3)) = pack8(acc[r]);
+      }
+    }
+  }
+  // ---- Q e^G (K-major), K e^(G_last - G) (M-major: the same byte image), Mq (K-major), e^G_last
+  const int last = rows > 0 ? rows - 1 : 0;
+  const float Gl = G[last];
+  for (int idx = tid; idx < C * 16; idx += 256) {
+    const int t = idx >> 4, ch = idx & 15;
+    const float eg = EG[t], ekg = t < rows ? expf(Gl - G[t]) : 0.f;
+    float q8[8], k8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      q8[u] = Qs[t * KP + ch * 8 + u] * eg;
+      k8[u] = Ks[t * KP + ch * 8 + u] * ekg;
+    }
+    const int off = (ch >> 3) * 8192 + swz(t, ch & 7);
+    *reinterpret_cast<uint4*>(rec + R_QG + off) = pack8(q8);
+    *reinterpret_cast<uint4*>(rec + R_KG + off) = pack8(k8);
+  }
+  for (int idx = tid; idx < C * 8; idx += 256) {
+    const int t = idx >> 3, ch = idx & 7;
+    float m8[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) m8[u] = Mq[t * AP + ch * 8 + u];
+    *reinterpret_cast<uint4*>(rec + R_M + swz(t, ch)) = pack8(m8);
+  }
+  if (tid == 0) *reinterpret_cast<float4*>(rec + R_EGL) = make_float4(expf(Gl), 0.f, 0.f, 0.f);
+}
+
+__global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_all, const int* chunks,
+                                                             const int* seg_chunk0, const int* seg_lane, float* state,
+                                                             long lane_stride, int nv, bf16* out, int commit, int* err) {
+  using namespace dntc;
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t base_u = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  uint8_t* base = smem_raw + (base_u - smem_u32(smem_raw));
+  uint64_t* bar_rec = reinterpret_cast<uint64_t*>(base + S_BAR);
+  uint64_t* bar_mma = bar_rec + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_rec + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_rec + 3);
+  const int seg = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+  const int c_begin = seg_chunk0[seg], c_end = seg_chunk0[seg + 1];
+  if (c_begin >= c_end) return;
+  // zero the pad rows (64..127) of the 64-token A operands, once
+  for (int i = tid; i < 8192 / 16; i += 128) {
+    const uint4 z = make_uint4(0, 0, 0, 0);
+    reinterpret_cast<uint4*>(base + S_W + 8192)[i] = z;
+    reinterpret_cast<uint4*>(base + S_W + 16384 + 8192)[i] = z;
+    reinterpret_cast<uint4*>(base + S_QG + 8192)[i] = z;
+    reinterpret_cast<uint4*>(base + S_QG + 16384 + 8192)[i] = z;
+    reinterpret_cast<uint4*>(base + S_M + 8192)[i] = z;
+  }
+  if (tid == 0) {
+    mbar_init(bar_rec, 1);
+    mbar_init(bar_mma, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t lane_t = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lanes
+  // ---- initial state: thread tid = key row
+  float* st = state + (long)seg_lane[seg] * lane_stride + (long)h * D * D + (long)tid * D;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    uint32_t r[32];
+#pragma unroll
+    for (int i = 0; i < 32; i += 4) {
+      const float4 v = *reinterpret_cast<const float4*>(st + 32 * q + i);
+      r[i] = __float_as_uint(v.x);
+      r[i + 1] = __float_as_uint(v.y);
+      r[i + 2] = __float_as_uint(v.z);
+      r[i + 3] = __float_as_uint(v.w);
+    }
+    tmem_st32(lane_t + TM_S + 32 * q, r);
+  }
+  tmem_wait_st();
+  auto load_rec = [&](int c) {
+    const uint8_t* rec = rec_all + ((long)c * nv + h) * REC;
+    const uint32_t bar = smem_u32(bar_rec);
+    mbar_expect_tx_s(bar, (uint32_t)(R_END));
+    bulk_g2s_s(base_u + S_U, rec + R_U, 32784, bar);
+    bulk_g2s_s(base_u + S_W, rec + R_W, 8192, bar);
+    bulk_g2s_s(base_u + S_W + 16384, rec + R_W + 8192, 8192, bar);
+    bulk_g2s_s(base_u + S_QG, rec + R_QG, 8192, bar);
+    bulk_g2s_s(base_u + S_QG + 16384, rec + R_QG + 8192, 8192, bar);
+    bulk_g2s_s(base_u + S_M, rec + R_M, 8192, bar);
+    bulk_g2s_s(base_u + S_KG, rec + R_KG, 16384, bar);
+  };
+  int rec_issued = 0, rec_done = 0, mma_issued = 0, mma_done = 0;  // issue counts kept by thread 0
+  if (tid == 0) {
+    fence_proxy_async_smem();
+    load_rec(c_begin);
+    ++rec_issued;
+  }
+  const uint32_t idesc = idesc_f16(128, 128, true) | (1u << 16);  // A K-major, B MN-major
+  const uint32_t idesc_mn = idesc | (1u << 15);                    // A MN-major too
+  uint32_t ph_rec = 0, ph_mma = 0;
+  bool ok = true;
+  for (int c = c_begin; c < c_end && ok; ++c) {
+    const int row0 = chunks[c * 3 + 1], rows = chunks[c * 3 + 2];
+    // 1. the record has landed
+    if (!__syncthreads_and(mbar_wait(bar_rec, ph_rec, err, ERR_TMA_WAIT, abort_flag))) { ok = false; break; }
+    ph_rec ^= 1;
+    ++rec_done;
+    // 2. S -> bf16 MN-major operand (row tid), and S *= e^(G_last) in place
+    {
+      const float egl = *reinterpret_cast<const float*>(base + S_U + R_EGL);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[32];
+        tmem_ld32(lane_t + TM_S + 32 * q, v);
+        uint8_t* row = base + S_S + (q >> 1) * 16384 + tid * 128;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int ch = (q & 1) * 4 + k;
+          *reinterpret_cast<uint4*>(row + ((ch ^ (tid & 7)) << 4)) = pack8(v + 8 * k);
+        }
+        uint32_t r[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i] * egl);
+        tmem_st32(lane_t + TM_S + 32 * q, r);
+      }
+      tmem_wait_st();
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // 3. D1 = W S
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + TM_D1, desc_sw128(base_u + S_W + a * 16384) + 2 * kk,
+                     desc_sw128_mn_dn(base_u + S_S + (a * 4 + kk) * 2048, 16384), idesc, (a | kk) != 0);
+      mma_commit(bar_mma);
+      ++mma_issued;
+    }
+    if (!__syncthreads_and(mbar_wait(bar_mma, ph_mma, err, ERR_MMA_WAIT, abort_flag))) { ok = false; break; }
+    ph_mma ^= 1;
+    ++mma_done;
+    tc_fence_after();
+    // 4. Delta = U - D1 (token rows 0..63: warps 0 and 1) -> bf16 MN-major operand
+    if (warp < 2) {
+      const float* u = reinterpret_cast<const float*>(base + S_U) + tid * D;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[32];
+        tmem_ld32(lane_t + TM_D1 + 32 * q, v);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] = u[32 * q + i] - v[i];
+        uint8_t* row = base + S_D + (q >> 1) * 8192 + tid * 128;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int ch = (q & 1) * 4 + k;
+          *reinterpret_cast<uint4*>(row + ((ch ^ (tid & 7)) << 4)) = pack8(v + 8 * k);
+        }
+      }
+    }
+    fence_proxy_async_smem();
+    tc_fence_before();
+    __syncthreads();
+    // 5. D2 = (Q e^G) S + Mq Delta;  S += (K e^(G_last - G))^T Delta
+    if (tid == 0) {
+      tc_fence_after();
+#pragma unroll
+      for (int a = 0; a < 2; ++a)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_f16_ss(tmem + TM_D2, desc_sw128(base_u + S_QG + a * 16384) + 2 * kk,
+                     desc_sw128_mn_dn(base_u + S_S + (a * 4 + kk) * 2048, 16384), idesc, (a | kk) != 0);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss(tmem + TM_D2, desc_sw128(base_u + S_M) + 2 * kk,
+                   desc_sw128_mn_dn(base_u + S_D + kk * 2048, 8192), idesc, 1);
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_f16_ss(tmem + TM_S, desc_sw128_mn_dn(base_u + S_KG + kk * 2048, 8192),
+                   desc_sw128_mn_dn(base_u + S_D + kk * 2048, 8192), idesc_mn, 1);
+      mma_commit(bar_mma);
+      ++mma_issued;
+    }
+    if (!__syncthreads_and(mbar_wait(bar_mma, ph_mma, err, ERR_MMA_WAIT, abort_flag))) { ok = false; break; }
+    ph_mma ^= 1;
+    ++mma_done;
+    tc_fence_after();
+    // 6. the next record streams in while the outputs of this chunk go out
+    if (tid == 0 && c + 1 < c_end) {
+      fence_proxy_async_smem();
+      load_rec(c + 1);
+      ++rec_issued;
+    }
+    if (warp < 2 && tid < rows) {
+      bf16* o = out + ((long)(row0 + tid) * nv + h) * D;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        float v[32];
+        tmem_ld32(lane_t + TM_D2 + 32 * q, v);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(o + 32 * q + 8 * k) = pack8(v + 8 * k);
+      }
+    }
+  }
+  // ---- after a give-up: let this CTA's own copies and MMAs in flight finish (bounded) before
+  // its shared memory and tensor memory are released
+  if (!ok && tid == 0) {
+    for (; rec_done < rec_issued; ++rec_done, ph_rec ^= 1)
+      if (!mbar_wait(bar_rec, ph_rec, err, ERR_DRAIN, nullptr)) break;
+    for (; mma_done < mma_issued; ++mma_done, ph_mma ^= 1)
+      if (!mbar_wait(bar_mma, ph_mma, err, ERR_DRAIN, nullptr)) break;
+  }
+  // ---- final state (fp32) back to the lane
+  if (ok && commit) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v[32];
+      tmem_ld32(lane_t + TM_S + 32 * q, v);
+#pragma unroll
+      for (int i = 0; i < 32; i += 4)
+        *reinterpret_cast<float4*>(st + 32 * q + i) = make_float4(v[i], v[i + 1], v[i + 2], v[i + 3]);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+long gated_delta_tc_scratch(int T, int n_chunks, int nk, int nv) {
+  // floats: qn, kn, gate record, then 128-byte aligned chunk records
+  return (long)T * (2L * nk * dntc::D + 4L * nv) + 32 + (long)n_chunks * nv * dntc::REC / 4;
+}
+
+int gated_delta_tc(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log, const float* dt_bias,
+                   float* state, long lane_stride, const int* seg_lane, const int* chunks, int n_chunks,
+                   const int* seg_chunk0, int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out,
+                   bool commit, int* err, cudaStream_t s) {
+  using namespace dntc;
+  if (!S || !T || !n_chunks) return 0;
+  if (dk != D || dv != D || nv % nk || ldqkv % 8) return -1;
+  float* qn = scratch;
+  float* kn = qn + (long)T * nk * D;
+  float* gb = kn + (long)T * nk * D;
+  uint8_t* rec = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(gb + (long)T * nv * 4) + 127) & ~uintptr_t(127));
+  int r = delta_prep(qkv, ldqkv, ab, ldab, a_log, dt_bias, T, nk, nv, dk, qn, kn, gb, s);
+  if (r) return r;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(dn_tc_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
+    cudaFuncSetAttribute(dn_tc_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_BYTES);
+    attr = true;
+  }
+  dn_tc_prep_kernel<<<dim3(n_chunks, nv), 256, PREP_SMEM, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, chunks, nk, nv,
+                                                               rec);
+  dn_tc_state_kernel<<<dim3(S, nv), 128, S_BYTES, s>>>(rec, chunks, seg_chunk0, seg_lane, state, lane_stride, nv,
+                                                       (bf16*)out, commit ? 1 : 0, err);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace qb

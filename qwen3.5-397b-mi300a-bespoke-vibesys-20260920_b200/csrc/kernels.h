@@ -64,6 +64,12 @@ int gated_delta_chunked(const void* qkv, long ldqkv, const void* ab, long ldab, 
                         const int* chunks, int n_chunks, const int* seg_chunk0, int S, int T, int nk, int nv, int dk,
                         int dv, float* scratch, void* out, bool commit, cudaStream_t s);
 long gated_delta_chunked_scratch(int T, int n_chunks, int nk, int nv, int dk);
+// chunked gated delta rule with the state in tensor memory (tcgen05), head size 128
+int gated_delta_tc(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log, const float* dt_bias,
+                   float* state, long lane_stride, const int* seg_lane, const int* chunks, int n_chunks,
+                   const int* seg_chunk0, int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out,
+                   bool commit, int* err, cudaStream_t s);
+long gated_delta_tc_scratch(int T, int n_chunks, int nk, int nv);
 // DeltaNet token mixer for one token per lane (conv, l2norm, gated delta step, gated RMSNorm)
 int deltanet_decode(const void* proj, long ldp, void* conv_state, long cls, const void* conv_w, const float* a_log,
                     const float* dt_bias, float* state, long sls, const void* norm_w, const int* seg_lane, int T,

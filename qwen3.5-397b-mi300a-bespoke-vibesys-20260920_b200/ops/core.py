@@ -142,8 +142,8 @@ def gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv,
         plan = dn_chunk_plan(cu_h, dk, dv, qkv.device)
         if plan is not None:
             chunks, seg0 = plan
-            return ext().gated_delta_chunked(qkv, ab, a_log, dt_bias, rec_state, seg_lane, chunks, seg0, nk, nv, dk,
-                                             dv, commit)
+            fn = ext().gated_delta_tc if flags.get("QB_DN_PREFILL") == "tc" else ext().gated_delta_chunked
+            return fn(qkv, ab, a_log, dt_bias, rec_state, seg_lane, chunks, seg0, nk, nv, dk, dv, commit)
         return ext().gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv, dk, dv, commit)
     t = qkv.shape[0]
     q = qkv[:, : nk * dk].reshape(t, nk, dk)
@@ -241,11 +241,13 @@ def dn_chunk_plan(cu_h, dk, dv, device):
     """(device chunk table [n, 3] = (segment, first row, rows), device first-chunk index per
     segment [S + 1]) for the chunked delta rule, or None (the token-serial kernel runs).
 
-    Opt-in (``QB_DN_CHUNKED=1``): on fp32 CUDA cores the chunked form does about as many FLOPs
-    as the token recurrence (it buys parallelism, not work), and measured slower than the
-    latency-tuned token kernel; it serves as the exact fp32 formulation for a tensor-core
-    version. Only batches whose longest segment reaches a chunk, and head size 128."""
-    if cu_h is None or dk != 128 or dv != 128 or not flags.get("QB_DN_CHUNKED"):
+    ``QB_DN_PREFILL``: ``tc`` (default) runs the chunked form with the state in tensor memory
+    and its products on tcgen05 (serial depth: chunks, not tokens); ``chunked_fp32`` the same
+    identities on CUDA cores in fp32 (exact formulation, slower than the token kernel);
+    ``recurrence`` always the fp32 token recurrence. Only batches whose longest segment reaches
+    a chunk, and head size 128."""
+    mode = flags.get("QB_DN_PREFILL")
+    if cu_h is None or dk != 128 or dv != 128 or mode not in ("tc", "chunked_fp32"):
         return None
     lens = [cu_h[i + 1] - cu_h[i] for i in range(len(cu_h) - 1)]
     if not lens or max(lens) < DN_CHUNK_MIN:
