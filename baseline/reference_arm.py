@@ -6,7 +6,9 @@ own stock serving path from the plain copy of its tree in ``baseline/_ref``: per
 ``server.build_runner`` (its captured decode graphs, as ``--enable-graph-capture`` gives), then on
 rank 0 the same sequence ``server.Engine`` runs (``tp_driver.Broadcaster``, ``warmup``,
 ``pool_handshake``, ``session_cache.SessionCache``, ``scheduler.Scheduler``) and on the other
-ranks ``tp_driver.serve_worker``. Every ``SEED_*`` flag keeps its default. The closed-loop client
+ranks ``tp_driver.serve_worker``. Every ``SEED_*`` flag keeps its default except
+``SEED_BLAS_TUNE=0``: the reference's boot-time cuBLAS solution search calls
+``torch.cuda.tunable.write_file``, which this PyTorch release does not have. The closed-loop client
 is the same token-id generator as our arm (256 sessions x 6 turns, C32, seed 0), submitting the
 reference's own ``scheduler.Request`` objects through ``Scheduler.submit`` and stepping its
 ``Scheduler.step``. Nothing of this repository's model, kernels or engine is imported on this path
@@ -143,6 +145,10 @@ def main(args, report) -> None:
     ckpt = prepare_checkpoint(args, rank, world, dev)
     wl = _by_path("qb_bench_workload", os.path.join(PKG_DIR, "serving", "workload.py"))
 
+    # The reference's boot GEMM search (blas_tune, TunableOp) ends in torch.cuda.tunable.write_file,
+    # which this PyTorch release no longer has; its own switch SEED_BLAS_TUNE=0 skips the search
+    # (cuBLAS keeps its default heuristic), the one flag this arm sets.
+    os.environ.setdefault("SEED_BLAS_TUNE", "0")
     sys.path.insert(0, REF_DIR)
     import server as ref_server  # the reference's own modules from here on
     import tp_driver

@@ -305,6 +305,9 @@ def main(argv=None):
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--lanes", type=int, default=None)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--heads", type=int, nargs=2, default=None, metavar=("NK", "NV"),
+                    help="deltanet cases: key and value heads (default the full geometry's 16 64; one "
+                         "rank of N-way tensor parallelism has 16/N and 64/N)")
     a = ap.parse_args(argv)
     if not torch.cuda.is_available():
         raise SystemExit("kbench needs a CUDA device")
@@ -328,7 +331,8 @@ def main(argv=None):
     if a.case in ("deltanet_decode", "all"):
         run.append(case_deltanet_decode(a.lanes or 32, a.iters, pk))
     if a.case in ("deltanet", "all"):
-        run.append(case_deltanet(a.tokens or 1, a.lanes or 32, a.iters, pk))
+        hk = dict(nk=a.heads[0], nv=a.heads[1]) if a.heads else {}
+        run.append(case_deltanet(a.tokens or 1, a.lanes or 32, a.iters, pk, **hk))
         if a.case == "all":
             run.append(case_deltanet(800, 1, a.iters, pk))
     return run
