@@ -438,14 +438,16 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
       load_rec(c + 1);
       ++rec_issued;
     }
-    if (warp < 2 && tid < rows) {
+    if (warp < 2) {  // whole warps: tcgen05.ld is warp-collective; only the stores are per row
       bf16* o = out + ((long)(row0 + tid) * nv + h) * D;
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
         float v[32];
         tmem_ld32(lane_t + TM_D2 + 32 * q, v);
+        if (tid < rows) {
 #pragma unroll
-        for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(o + 32 * q + 8 * k) = pack8(v + 8 * k);
+          for (int k = 0; k < 4; ++k) *reinterpret_cast<uint4*>(o + 32 * q + 8 * k) = pack8(v + 8 * k);
+        }
       }
     }
   }
