@@ -1,11 +1,23 @@
-"""Builds the HuggingFace ``Qwen3_5MoeForCausalLM`` oracle from one of our checkpoints.
+"""Builds the ``Qwen3_5MoeForCausalLM`` oracle from one of our checkpoints.
 
-The oracle is transformers' own ``qwen3_5_moe`` modeling code (the same code as the
-reference's ``reference/modeling_qwen3_5_moe.py``). Routed experts are dequantized from
-MXFP4 into HF's fused ``gate_up_proj`` [E, 2I, H] / ``down_proj`` [E, H, I] parameters."""
+Two sources of the modeling code: ``reference="ref"`` loads the reference repository's own
+``reference/modeling_qwen3_5_moe.py`` (from the plain copy of the reference tree in
+``baseline/_ref``; the test skips when that copy is absent), the oracle its parity tests and its
+pins were made with; ``reference="hf"`` uses the installed transformers' ``qwen3_5_moe`` code.
+The reference file was written against a slightly different transformers release: it is
+loaded as a module of transformers' ``qwen3_5_moe`` package, and the one helper it imports
+that this release lacks are supplied for its vision parts only (``accepts_precomputed_kwargs``,
+a decorator on its vision methods, as a pass-through; the ``vision_utils`` helpers of its vision
+tower as functions that raise), so its text model runs as written. Routed experts are dequantized from MXFP4 into the
+fused ``gate_up_proj`` [E, 2I, H] / ``down_proj`` [E, H, I] parameters."""
 
 from __future__ import annotations
 
+import importlib.util
+import os
+import sys
+
+import pytest
 import torch
 
 from qwen35_b200.models.config import load_config, to_hf_text_config
@@ -14,9 +26,47 @@ from qwen35_b200.utils import mxfp4
 from qwen35_b200.utils.safetensors_io import Checkpoint
 
 
-def build_hf(model_dir: str, dtype=torch.float32):
+REF_MODELING = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "baseline", "_ref",
+                            "reference", "modeling_qwen3_5_moe.py")
+
+
+def reference_modeling():
+    """The reference repository's modeling module (skips the calling test when absent)."""
+    name = "transformers.models.qwen3_5_moe.modeling_qwen3_5_moe_reference"
+    if name in sys.modules:
+        return sys.modules[name]
+    if not os.path.exists(REF_MODELING):
+        pytest.skip("the reference tree is not present in baseline/_ref")
+    import transformers.models.qwen3_5_moe  # noqa: F401  (the package its relative imports resolve in)
+    import transformers.utils.generic as generic
+
+    if not hasattr(generic, "accepts_precomputed_kwargs"):
+        generic.accepts_precomputed_kwargs = lambda **kw: (lambda f: f)
+    if importlib.util.find_spec("transformers.vision_utils") is None:  # vision-tower helpers only
+        import types
+
+        vu = types.ModuleType("transformers.vision_utils")
+
+        def _vision_only(*a, **k):
+            raise NotImplementedError("vision tower helper (not used by the text model)")
+
+        for n in ("get_vision_bilinear_indices_and_weights", "get_vision_cu_seqlens", "get_vision_position_ids"):
+            setattr(vu, n, _vision_only)
+        sys.modules["transformers.vision_utils"] = vu
+    spec = importlib.util.spec_from_file_location(name, REF_MODELING)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def build_hf(model_dir: str, dtype=torch.float32, reference: str = "hf"):
     from transformers.models.qwen3_5_moe.configuration_qwen3_5_moe import Qwen3_5MoeTextConfig
-    from transformers.models.qwen3_5_moe.modeling_qwen3_5_moe import Qwen3_5MoeForCausalLM
+
+    if reference == "ref":
+        Qwen3_5MoeForCausalLM = reference_modeling().Qwen3_5MoeForCausalLM
+    else:
+        from transformers.models.qwen3_5_moe.modeling_qwen3_5_moe import Qwen3_5MoeForCausalLM
 
     cfg = load_config(model_dir)
     hcfg = Qwen3_5MoeTextConfig(**{k: v for k, v in to_hf_text_config(cfg).items()

@@ -1,6 +1,7 @@
 """Greedy-token parity: the tiny model at TP=4 over gloo (4 CPU processes, the real scheduler,
-session cache and SPMD driver) reproduces the HuggingFace oracle's greedy tokens, turn by turn,
-for 2 chat sessions x 3 turns with 32 new tokens each."""
+session cache and SPMD driver) reproduces the oracle's greedy tokens, turn by turn, for 2 chat
+sessions x 3 turns with 32 new tokens each. The oracle is the reference repository's own
+``reference/modeling_qwen3_5_moe.py`` forward (``hf_oracle.build_hf(..., reference="ref")``)."""
 
 import json
 import os
@@ -25,7 +26,7 @@ def test_tp4_gloo_multiturn_matches_hf(tiny_dir, tmp_path):
     assert codes == [0, 0, 0, 0], codes
     res = json.load(open(out))
     assert res["hits"] > 0  # later turns resumed from cached boundaries
-    model, _ = build_hf(tiny_dir)
+    model, _ = build_hf(tiny_dir, reference="ref")
     exact = 0
     for t in res["turns"]:
         exact += t["out"] == hf_greedy(model, t["prompt"], 32)
@@ -62,6 +63,6 @@ def test_single_process_matches_hf(tiny_dir):
     p = plan(cfg, 0, 1)
     m = Model(cfg, load_weights(tiny_dir, cfg, p, "cpu", torch.float32), p, device="cpu", dtype=torch.float32,
               max_batch=2, max_seq=512)
-    model, _ = build_hf(tiny_dir)
+    model, _ = build_hf(tiny_dir, reference="ref")
     ids = list(range(10, 140))
     assert m.generate(ids, 16) == hf_greedy(model, ids, 16)
