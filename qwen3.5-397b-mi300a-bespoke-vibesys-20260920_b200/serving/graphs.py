@@ -150,7 +150,10 @@ class GraphRunner:
         m.attach_blocks(self.pad_lane, [])
         from ..ops import _ext
 
+        import time
+
         for B in sorted(self.buckets, reverse=True):
+            t0 = time.perf_counter()
             bk = _Bucket(m, B, self.pool)
             self._fill(bk, [], [], [])
             s = torch.cuda.Stream()
@@ -167,6 +170,9 @@ class GraphRunner:
             self.launch_per_replay[B] = _ext.ext().launches() - l0
             bk.graph = g
             self._b[B] = bk
+            if flags.get("QB_GRAPH_LOG"):
+                print(f"[graph-capture] decode bucket {B}: {self.launch_per_replay[B]} kernels, "
+                      f"{time.perf_counter() - t0:.2f}s", flush=True)
         torch.cuda.synchronize()
 
     # ------------------------------------------------------------------ speculative rounds

@@ -122,6 +122,10 @@ class Scheduler:
             raise ValueError(f"prefill_order must be fifo or shortest, got {prefill_order!r}")
         self.prefill_order = prefill_order
         self.max_skips = max_skips
+        from ..utils import flags as _flags
+
+        self.cache_stats_every = int(_flags.get("QB_CACHE_STATS"))
+        self.finished = 0
         self.free_lanes: list[int] = list(range(runner.max_batch - 1, -1, -1))
         self.incoming: queue.Queue = queue.Queue()
         self.waiting: deque[Request] = deque()
@@ -428,6 +432,17 @@ class Scheduler:
             self._publish(f, full, f.pos, f.last_logits)
         self._release(f)
         f.req.emit(("end", (reason, f.generated, f.reused)))
+        self.finished += 1
+        if self.cache_stats_every and self.finished % self.cache_stats_every == 0:
+            self._log_cache_stats()
+
+    def _log_cache_stats(self) -> None:
+        """One ``[cache-stats]`` line: admissions by class, hit rate, snapshot and block use."""
+        st = self.cache.stats()
+        adm = " ".join(f"{k}={v}" for k, v in sorted(st.admissions.items()))
+        print(f"[cache-stats] finished={self.finished} {adm} nodes={st.nodes} snapshots={st.snapshots_used}/"
+              f"{st.snapshots_capacity} free_blocks={st.free_blocks} evictions={st.evictions} "
+              f"reclaims={st.reclaims} hits={st.hits} misses={st.misses}", flush=True)
 
     def _release(self, f: _Flight) -> None:
         if f in self.decoding:

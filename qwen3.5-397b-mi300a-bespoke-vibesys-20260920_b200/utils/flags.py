@@ -79,6 +79,7 @@ _def("QB_MEM_REPORT", bool, False, "print a [mem] line at each boot phase and a 
      "static pool)")
 _def("QB_CPU_AFFINITY", bool, False, "restrict each rank's host threads to the CPUs local to its GPU (sysfs "
      "local_cpulist)")
+_def("QB_GRAPH_LOG", bool, False, "print a [graph-capture] line per captured decode bucket (kernels, seconds)")
 _def("QB_CACHE_STATS", int, 0, "log a [cache-stats] line (session-cache admissions, hit tokens) every n finished "
      "requests (0: off)")
 _def("QB_FAULT_ENDPOINT", bool, False, "expose POST /debug/fault (accuracy-gate calibration faults)")

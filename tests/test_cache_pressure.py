@@ -67,3 +67,17 @@ def test_follow_up_turns_resume_from_the_previous_close_with_few_snapshots():
                                                            for x in recs if x.turn > 0)
     assert cache.reclaims > 0
     assert loop.sched.runner.prefill_tokens == expect
+
+
+def test_cache_stats_line(monkeypatch, capsys):
+    monkeypatch.setenv("QB_CACHE_STATS", "2")
+    r = CountingRunner(2, 6, 16, 4096)
+    s = Scheduler(r, SessionCache(BlockAllocator(600, 16), 16, 6))
+    loop = ClosedLoop(s, ChatSpec(sessions=2, concurrency=2, turns=2, first_len=(40, 60), user_len=(5, 9),
+                                  gen_len=(3, 5), vocab=500, seed=1))
+    loop.start()
+    while loop.active:
+        s.step()
+        loop.pump()
+    lines = [ln for ln in capsys.readouterr().out.splitlines() if ln.startswith("[cache-stats]")]
+    assert len(lines) == 2 and "finished=4" in lines[-1] and "hit=2" in lines[-1]
