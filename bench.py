@@ -322,6 +322,7 @@ def main_ours(args):
     inner = getattr(model, "model", model)  # the Model under a GraphRunner
     on_gpu = device.type == "cuda"
     step_no = [0]
+    step_kind: list = []
 
     def one_step(loop, brackets=None):
         """One scheduler step; with ``brackets``, a CUDA event before and one after it on the
@@ -329,11 +330,13 @@ def main_ours(args):
         if brackets is not None:
             ev0 = torch.cuda.Event(enable_timing=True)
             ev0.record()
+            sched.timer.last_kind = None
         sched.step()
         if brackets is not None:
             ev1 = torch.cuda.Event(enable_timing=True)
             ev1.record()
             brackets.append((ev0, ev1))
+            step_kind.append(sched.timer.last_kind)
         step_no[0] += 1
         loop.pump()
 
@@ -392,6 +395,10 @@ def main_ours(args):
         dist.all_gather_object(gathered, window_ms)
         window_ms = max(gathered)
     step_ms = [a.elapsed_time(b) for a, b in marks] if on_gpu else [None] * step_no[0]
+    dev_by_kind: dict = {}
+    for ms_, k in zip(step_ms, step_kind[-len(step_ms):] if on_gpu else []):
+        if ms_ is not None and k is not None:
+            dev_by_kind.setdefault(k, []).append(ms_)
     kinds = sched.timer.summary()
     storage = "all layers distinct" if distinct is None else \
         (f"{distinct} distinct expert layers, the other {cfg.layers - distinct} reuse their storage "
@@ -403,6 +410,7 @@ def main_ours(args):
                                           f"experts MXFP4)" if args.model == "full" else "tiny parity model"),
                  expert_storage=storage,
                  extra={"mixed": mixed, "prefill_order": sched.prefill_order,
+                        "device_ms_per_step": {k: round(sum(v) / len(v), 3) for k, v in dev_by_kind.items()},
                         "cache": {"admissions": dict(cache.admissions), "evictions": cache.evictions,
                                   "reclaims": cache.reclaims,
                                   "prefill_tokens": (kinds.get("prefill", {}).get("tokens", 0)
