@@ -174,6 +174,51 @@ class GraphRunner:
                 print(f"[graph-capture] decode bucket {B}: {self.launch_per_replay[B]} kernels, "
                       f"{time.perf_counter() - t0:.2f}s", flush=True)
         torch.cuda.synchronize()
+        self.validate()
+
+    def validate(self, tol: float = 5e-2) -> bool:
+        """Boot check of every captured bucket: from the same pad-lane state, a replay and an
+        eager run of the same step must give the same logits (max abs difference within
+        ``tol`` of the logits' scale: the two run the same kernels, and the margin only admits
+        rounding-order differences of the reductions that finish in arrival order, while a replay
+        reading a stale or freed table gives garbage far outside it). Every rank reports its verdict and the ranks agree on
+        the minimum (an all-reduce over the model's group), so either every rank serves from its
+        graphs or none does. Returns whether the graphs stay on. Reference behaviour:
+        ``graph_decode.py`` (``validate``, ``all_ranks``)."""
+        m = self.model
+        pad = self.pad_lane
+        ok = True
+        worst = 0.0
+        with torch.inference_mode():
+            for B, bk in sorted(self._b.items()):
+                conv = m.conv_state[:, pad].clone()
+                rec = m.rec_state[:, pad].clone()
+                bk.graph.replay()
+                got = bk.out.float().clone()
+                m.conv_state[:, pad].copy_(conv)
+                m.rec_state[:, pad].copy_(rec)
+                exp = self._run(bk).float()
+                m.conv_state[:, pad].copy_(conv)
+                m.rec_state[:, pad].copy_(rec)
+                err = (got - exp).abs().max().item()
+                scale = exp.abs().max().item() + 1e-6
+                worst = max(worst, err / scale)
+                if not (err <= tol * scale) or not torch.isfinite(got).all():
+                    ok = False
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=m.device)
+        world = getattr(m.comm, "world", 1)
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        agreed = bool(int(flag.item()))
+        if flags.get("QB_GRAPH_LOG") or not agreed:
+            print(f"[graph-capture] validation: this rank {'ok' if ok else 'MISMATCH'} (worst relative "
+                  f"{worst:.2e}), all ranks {'ok' if agreed else 'disagree: decode runs eagerly'}", flush=True)
+        if not agreed:
+            self.release()
+        self.validated = agreed
+        return agreed
 
     # ------------------------------------------------------------------ speculative rounds
     def _spec_fill(self, bk: _SpecBucket, lanes, tokens, positions) -> None:

@@ -20,6 +20,7 @@ def test_graph_decode_matches_eager():
               max_batch=5, max_seq=512)
     g = GraphRunner(m, buckets=(1, 2, 4))
     g.prepare()
+    assert g.validated and g._b  # boot replay-vs-eager check passed, graphs stay on
     assert set(g._b) == {1, 2, 4}
     prompts = [list(range(3, 40)), list(range(50, 130))]
     for i, ids in enumerate(prompts * 2):  # lanes 0,1 (graph) and 2,3 (eager) hold the same history
