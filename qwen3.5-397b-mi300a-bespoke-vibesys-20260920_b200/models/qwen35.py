@@ -528,6 +528,61 @@ class Model:
     def decode(self, lanes: Sequence[int], tokens: Sequence[int], positions: Sequence[int]):
         return self.forward([(l, [t], p) for l, t, p in zip(lanes, tokens, positions)])
 
+    # ------------------------------------------------------------------ one-step overlap
+    @torch.inference_mode()
+    def decode_launch(self, lanes, tokens, positions, src_rows, keep_rows=()):
+        """A decode step whose result is read later (``decode_collect``): a token of -1 takes the
+        previous launch's greedy id at row ``src_rows[i]`` on the device, so the host never has to
+        see it first. The step's greedy ids are copied to pinned host memory behind an event; the
+        logits rows in ``keep_rows`` are kept (the node logits of lanes that finish here)."""
+        host = [int(t) if t >= 0 else 0 for t in tokens]
+        b = self.make_inputs([(l, [t], p) for l, t, p in zip(lanes, host, positions)])
+        self._feed_back(b.tokens, tokens, src_rows)
+        lg = self.logits(self._forward(b))
+        if self.mtp is not None:
+            self.mtp.catch_up(b, self.last_h_all)
+        return self._launch_tail(lg, len(lanes), keep_rows)
+
+    def _dev_index(self, xs) -> torch.Tensor:
+        t = torch.tensor(list(xs), dtype=torch.long)
+        if self.device.type == "cuda":
+            return t.pin_memory().to(self.device, non_blocking=True)
+        return t
+
+    def _feed_back(self, tokens_dev: torch.Tensor, tokens, src_rows) -> None:
+        rows = [i for i, t in enumerate(tokens) if t < 0]
+        if not rows:
+            return
+        src = [src_rows[i] for i in rows]
+        self._h2d += 16 * len(rows)
+        tokens_dev.index_copy_(0, self._dev_index(rows), self._launch_ids.index_select(0, self._dev_index(src)))
+
+    def _launch_tail(self, lg: torch.Tensor, n: int, keep_rows):
+        ids = ops.argmax_rows(lg)[1]
+        self._launch_ids = ids
+        kept = {}
+        if keep_rows:
+            sel = lg.index_select(0, self._dev_index(keep_rows))
+            kept = {r: sel[i:i + 1] for i, r in enumerate(keep_rows)}
+        if self.device.type == "cuda":
+            host = torch.empty(n, dtype=torch.int64).pin_memory()
+            host.copy_(ids, non_blocking=True)
+            ev = torch.cuda.Event()
+            ev.record()
+        else:
+            host, ev = ids, None
+        return (host, ev, kept, n)
+
+    def decode_collect(self, handle) -> list[int]:
+        host, ev, _, n = handle
+        if ev is not None:
+            ev.synchronize()
+        self._d2h += 8 * n
+        return [int(x) for x in host.tolist()]
+
+    def decode_kept(self, handle) -> dict:
+        return handle[2]
+
     def decode_mixed(self, lanes, tokens, positions, prefill_calls):
         segs = [(l, [t], p) for l, t, p in zip(lanes, tokens, positions)] + list(prefill_calls)
         lg = self.forward(segs)

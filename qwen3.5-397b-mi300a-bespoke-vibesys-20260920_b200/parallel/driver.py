@@ -40,6 +40,7 @@ class Op(enum.IntEnum):
     SET_FAULT = 13
     CALL = 14  # generic named method (rarely used control calls)
     SHUTDOWN = 15
+    DECODE_LAUNCH = 16
 
 
 class PoolMismatchError(RuntimeError):
@@ -111,6 +112,8 @@ def apply(model, op: Op, args: tuple):
         return model.decode(*args)
     if op == Op.DECODE_MIXED:
         return model.decode_mixed(*args)
+    if op == Op.DECODE_LAUNCH:
+        return model.decode_launch(*args)
     if op == Op.SPECULATIVE_DECODE:
         return model.speculative_decode(*args)
     if op == Op.SCORE:
@@ -130,7 +133,7 @@ def apply(model, op: Op, args: tuple):
     raise ValueError(f"unknown op {op}")
 
 
-STEP_OPS = (Op.PREFILL_BATCH, Op.DECODE, Op.DECODE_MIXED, Op.SPECULATIVE_DECODE, Op.SCORE)
+STEP_OPS = (Op.PREFILL_BATCH, Op.DECODE, Op.DECODE_MIXED, Op.SPECULATIVE_DECODE, Op.SCORE, Op.DECODE_LAUNCH)
 
 
 def serve_worker(model, channel: Channel) -> int:
@@ -205,6 +208,17 @@ class Broadcaster:
         lanes, tokens, positions = list(lanes), [int(t) for t in tokens], list(positions)
         self._send(Op.DECODE, lanes, tokens, positions)
         return self.model.decode(lanes, tokens, positions)
+
+    def decode_launch(self, lanes, tokens, positions, src_rows, keep_rows=()):
+        args = (list(lanes), [int(t) for t in tokens], list(positions), list(src_rows), list(keep_rows))
+        self._send(Op.DECODE_LAUNCH, *args)
+        return self.model.decode_launch(*args)
+
+    def decode_collect(self, handle):
+        return self.model.decode_collect(handle)
+
+    def decode_kept(self, handle):
+        return self.model.decode_kept(handle)
 
     def decode_mixed(self, lanes, tokens, positions, calls):
         lanes, tokens, positions = list(lanes), [int(t) for t in tokens], list(positions)

@@ -35,9 +35,13 @@ class _Bucket:
         self.lanes = torch.zeros(B, dtype=torch.int32, device=dev)
         self.cu = torch.arange(B + 1, dtype=torch.int32, device=dev)
         self.logit_rows = torch.arange(B, dtype=torch.int64, device=dev)
-        self.packed_host = torch.zeros(4 * B, dtype=torch.int32).pin_memory()
+        # two pinned input sets used alternately: with the one-step overlap the host fills step
+        # n+1 while step n's input copies may still be queued
+        self._hosts = [(torch.zeros(4 * B, dtype=torch.int32).pin_memory(),
+                        torch.zeros(B, dtype=torch.int64).pin_memory()) for _ in range(2)]
+        self._flip = 0
+        self.packed_host, self.tok_host = self._hosts[0]
         self.packed_dev = torch.zeros(4 * B, dtype=torch.int32, device=dev)
-        self.tok_host = torch.zeros(B, dtype=torch.int64).pin_memory()
         self.graph = None
         self.out = None
         self.pool = pool
@@ -118,6 +122,8 @@ class GraphRunner:
     def _fill(self, bk: _Bucket, lanes, tokens, positions):
         m = self.model
         m._gpu_mark("in")
+        bk._flip ^= 1
+        bk.packed_host, bk.tok_host = bk._hosts[bk._flip]
         B, n = bk.B, len(lanes)
         pos = list(positions) + [0] * (B - n)
         ln = list(lanes) + [self.pad_lane] * (B - n)
@@ -407,6 +413,27 @@ class GraphRunner:
 
         _ext.ext().add_launches(self.launch_per_replay.get(B, 0))
         return bk.out[:n]
+
+    def decode_launch(self, lanes, tokens, positions, src_rows, keep_rows=()):
+        """``Model.decode_launch`` replayed from the smallest captured bucket that holds the
+        batch: the host tokens go in with the bucket's inputs, the fed-back rows are then
+        overwritten on the device from the previous launch's ids, and the argmax and its
+        read-back run after the replay."""
+        n = len(lanes)
+        B = next((b for b in self.buckets if b >= n), None)
+        m = self.model
+        if not self._b or B is None or B not in self._b or m.mtp is not None or m.fault:
+            return m.decode_launch(lanes, tokens, positions, src_rows, keep_rows)
+        bk = self._b[B]
+        with torch.inference_mode():
+            self._fill(bk, lanes, [int(t) if t >= 0 else 0 for t in tokens], positions)
+            m._feed_back(bk.tokens, tokens, src_rows)
+            bk.graph.replay()
+            self.replays += 1
+            from ..ops import _ext
+
+            _ext.ext().add_launches(self.launch_per_replay.get(B, 0))
+            return m._launch_tail(bk.out[:n], n, keep_rows)
 
     def __getattr__(self, name):
         return getattr(self.model, name)

@@ -85,6 +85,15 @@ class _Flight:
 
 
 @dataclass
+class _Inflight:
+    """A decode step launched but not yet read back (one-step overlap)."""
+
+    handle: Any
+    flights: list  # the step's flights, in row order
+    finishing: set  # ids of flights whose last token this step produces
+
+
+@dataclass
 class ScoreJob:
     ids: list[int]
     continuation_start: int
@@ -105,7 +114,8 @@ class Scheduler:
     def __init__(self, runner, cache: SessionCache, prefill_chunk: int = PREFILL_CHUNK,
                  token_budget: int = PREFILL_TOKEN_BUDGET, max_prefill_burst: int = MAX_PREFILL_BURST,
                  mixed: bool = False, speculative: bool = False, timer: StepTimer | None = None,
-                 prefill_order: str | None = None, max_skips: int = MAX_PREFILL_SKIPS) -> None:
+                 prefill_order: str | None = None, max_skips: int = MAX_PREFILL_SKIPS,
+                 overlap: bool | None = None) -> None:
         self.runner = runner
         self.cache = cache
         self.block_size = cache.block_size
@@ -126,6 +136,10 @@ class Scheduler:
 
         self.cache_stats_every = int(_flags.get("QB_CACHE_STATS"))
         self.finished = 0
+        if overlap is None:
+            overlap = bool(_flags.get("QB_OVERLAP"))
+        self.overlap = overlap and hasattr(runner, "decode_launch")
+        self.inflight: _Inflight | None = None
         self.free_lanes: list[int] = list(range(runner.max_batch - 1, -1, -1))
         self.incoming: queue.Queue = queue.Queue()
         self.waiting: deque[Request] = deque()
@@ -156,7 +170,8 @@ class Scheduler:
         return c.result
 
     def idle(self) -> bool:
-        return not (self.waiting or self.prefilling or self.decoding) and self.incoming.empty()
+        return (not (self.waiting or self.prefilling or self.decoding) and self.inflight is None
+                and self.incoming.empty())
 
     def stop(self) -> None:
         self._stop.set()
@@ -208,6 +223,7 @@ class Scheduler:
                     break
                 self.waiting.popleft()
             if self.prefilling and (not self.decoding or self.burst < self.max_prefill_burst):
+                self._complete_inflight()  # a prefill or mixed step starts from a quiet pipeline
                 if self.mixed and self.decoding:
                     self._decode_step(with_prefill=True)
                 else:
@@ -216,7 +232,7 @@ class Scheduler:
                 self.steps += 1
                 self._watch_status()
                 return True
-            if self.decoding:
+            if self.decoding or self.inflight is not None:
                 self._decode_step()
                 self.burst = 0
                 self.steps += 1
@@ -350,6 +366,13 @@ class Scheduler:
     # ================================================================== decode
     def _decode_step(self, with_prefill: bool = False) -> None:
         flights = list(self.decoding)
+        if self.overlap and not with_prefill and not self.speculative and \
+                all(not f.req.temperature for f in flights):
+            return self._overlap_step()
+        self._complete_inflight()
+        flights = list(self.decoding)
+        if not flights and not with_prefill:
+            return
         if self.speculative and not with_prefill and self._spec_ok(flights):
             return self._speculative_step(flights)
         pre = self._select_prefill() if with_prefill else []
@@ -370,6 +393,52 @@ class Scheduler:
         if pre:
             self._finish_prefill(pre, plog)
         self.timer.record("mixed" if pre else "decode", len(flights), time.perf_counter() - t0)
+
+    # ------------------------------------------------------------------ one-step overlap
+    def _overlap_step(self) -> None:
+        """Launch the next decode step before reading the previous one back: rows of lanes that
+        were in the in-flight step take their input token from its on-device argmax, so the host's
+        read-back, emission and bookkeeping of step n run while the GPU computes step n+1. A lane
+        whose last token (by length) the in-flight step produces is left out of the new launch, so
+        its state at read-back is exactly its history and its turn-close node can be published;
+        a lane that stops on a stop token rides one extra step whose token is dropped, and publishes
+        no turn-close node (its state already holds that token). Greedy lanes only; anything else
+        drains the pipeline first. Reference behaviour: ``scheduler.py:1850-1948`` (overlap)."""
+        prev = self.inflight
+        in_prev = {id(f): i for i, f in enumerate(prev.flights)} if prev is not None else {}
+        fin_prev = prev.finishing if prev is not None else set()
+        launch = [f for f in self.decoding if id(f) not in fin_prev and not f.done]
+        t0 = time.perf_counter()
+        new = None
+        if launch:
+            self._grow(launch, [f.pos + 1 for f in launch])
+            toks = [-1 if id(f) in in_prev else f.next_token for f in launch]
+            src = [in_prev.get(id(f), 0) for f in launch]
+            finishing = {id(f) for f in launch
+                         if f.generated + (1 if id(f) in in_prev else 0) + 1 >= f.req.max_new}
+            keep = [i for i, f in enumerate(launch) if id(f) in finishing]
+            handle = self.runner.decode_launch([f.lane for f in launch], toks, [f.pos for f in launch], src, keep)
+            for f in launch:
+                f.pos += 1
+            new = _Inflight(handle, launch, finishing)
+        self.inflight = new
+        if prev is not None:
+            self._collect(prev)
+        self.timer.record("decode", len(launch), time.perf_counter() - t0)
+
+    def _collect(self, inf: _Inflight) -> None:
+        ids = self.runner.decode_collect(inf.handle)
+        kept = self.runner.decode_kept(inf.handle)
+        for i, (f, t) in enumerate(zip(inf.flights, ids)):
+            if f.done:  # stopped at the previous step: this token is past its end
+                continue
+            f.last_logits = kept.get(i) if id(f) in inf.finishing else None
+            self._emit(f, int(t))
+
+    def _complete_inflight(self) -> None:
+        inf, self.inflight = self.inflight, None
+        if inf is not None:
+            self._collect(inf)
 
     def _spec_ok(self, flights: Sequence[_Flight]) -> bool:
         k1 = self.runner.decode_tokens_per_step()
@@ -454,6 +523,7 @@ class Scheduler:
         self.free_lanes.append(f.lane)
 
     def _abort_all(self, msg: str) -> None:
+        self.inflight = None
         for f in list(self.prefilling) + list(self.decoding):
             f.done = True
             try:

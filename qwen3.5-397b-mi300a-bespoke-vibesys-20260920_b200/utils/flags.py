@@ -59,6 +59,8 @@ _def("QB_DN_PREFILL", str, "tc", "DeltaNet prefill segments: tc (chunked WY form
 _def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
 _def("QB_PREFILL_ORDER", str, "shortest", "scheduler: order prefill flights are packed in: shortest (fewest "
      "pending prompt tokens first, with aging) or fifo (admission order)")
+_def("QB_OVERLAP", bool, True, "scheduler: launch decode step n+1 (tokens fed back on the device) before reading "
+     "step n back", lockstep=True)
 _def("QB_MIXED", bool, False, "scheduler: decode steps also carry prefill chunks in the same forward")
 # ---- collectives and multi-rank plumbing
 _def("QB_COMM", str, "fused", "tensor-parallel all-reduce: fused (peer-memory kernels) or nccl", lockstep=True)

@@ -94,6 +94,23 @@ class FakeRunner:
         self.calls.append(("decode", len(lanes)))
         return Logits([self._fwd(l, [t], p) for l, t, p in zip(lanes, tokens, positions)])
 
+    def decode_launch(self, lanes, tokens, positions, src_rows, keep_rows=()):
+        """One-step overlap form of ``decode``: a token of -1 means "the previous launch's
+        sampled id at row ``src_rows[i]``" (the device feedback of the real runner)."""
+        self.calls.append(("launch", len(lanes)))
+        prev = getattr(self, "_launched_ids", None)
+        toks = [prev[s] if t < 0 else t for t, s in zip(tokens, src_rows)]
+        rows = [self._fwd(l, [t], p) for l, t, p in zip(lanes, toks, positions)]
+        ids = [next_token(h) for h in rows]
+        self._launched_ids = ids
+        return (ids, {i: Logits([rows[i]]) for i in keep_rows})
+
+    def decode_collect(self, handle):
+        return list(handle[0])
+
+    def decode_kept(self, handle):
+        return handle[1]
+
     def decode_mixed(self, lanes, tokens, positions, calls):
         d = self.decode(lanes, tokens, positions)
         return d, self.prefill_batch(calls)

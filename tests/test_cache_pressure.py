@@ -39,11 +39,28 @@ class CountingRunner:
         return [7] * len(temps)
 
 
-def test_follow_up_turns_resume_from_the_previous_close_with_few_snapshots():
+class CountingLaunchRunner(CountingRunner):
+    """The same, with the one-step overlap entry points."""
+
+    def decode_launch(self, lanes, tokens, positions, src_rows, keep_rows=()):
+        return ([7] * len(lanes), {i: [0] for i in keep_rows})
+
+    def decode_collect(self, h):
+        return h[0]
+
+    def decode_kept(self, h):
+        return h[1]
+
+
+import pytest
+
+
+@pytest.mark.parametrize("runner_cls", [CountingRunner, CountingLaunchRunner])
+def test_follow_up_turns_resume_from_the_previous_close_with_few_snapshots(runner_cls):
     lanes, snaps = 6, 2 * 6 + 2
     spec = ChatSpec(sessions=24, concurrency=lanes, turns=5, first_len=(200, 600), user_len=(20, 80),
                     gen_len=(20, 60), vocab=5000, seed=3)
-    r = CountingRunner(lanes, snaps, 16, 8192)
+    r = runner_cls(lanes, snaps, 16, 8192)
     cache = SessionCache(BlockAllocator(lanes * 8192 // 16 + 1, 16), 16, snaps)
     s = Scheduler(r, cache, prefill_chunk=256, token_budget=512)
     loop = ClosedLoop(s, spec)

