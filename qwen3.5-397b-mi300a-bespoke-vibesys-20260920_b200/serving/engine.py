@@ -85,6 +85,13 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
             except SymmUnavailable as e:  # raised on every rank together: all fall back to NCCL
                 print(f"[rank {rank}] fused collectives unavailable, using NCCL: {e}", flush=True)
                 comm.symm = None
+            nvls_min = flags.get("QB_NVLS_MIN_ROWS")
+            if comm.symm is not None and nvls_min > 0 and sp_rows > 0:
+                # messages of nvls_min rows and more take the switch-reduced kernel; all ranks
+                # keep the peer-memory kernels together when the fabric has no multicast
+                if not comm.symm.enable_nvls(rows_cap=sp_rows, min_rows=nvls_min):
+                    print(f"[rank {rank}] NVLS unavailable: large messages stay on the peer-memory kernel",
+                          flush=True)
     m = Model(cfg, w, p, comm, device=device, dtype=dtype,
               max_batch=spec.lanes + (1 if graphs else 0), max_seq=spec.max_seq, block_size=spec.block_size,
               num_blocks=num_blocks, num_snapshots=spec.snapshots or 2 * spec.lanes + 16)

@@ -67,6 +67,8 @@ _def("QB_COMM", str, "fused", "tensor-parallel all-reduce: fused (peer-memory ke
 _def("QB_SYMM_MAX_ROWS", int, 512, "rows of the one-shot fused all-reduce buffers", lockstep=True)
 _def("QB_SP_MAX_ROWS", int, 4096, "rows of the sequence-parallel fused all-reduce buffers (0: off)",
      lockstep=True)
+_def("QB_NVLS_MIN_ROWS", int, 0, "all-reduce messages of at least this many rows use the NVLS (multimem) kernel "
+     "(0: never)", lockstep=True)
 _def("QB_SP_GEMM", bool, True, "prefill: fuse the mixers' output projection into the sequence-parallel all-reduce "
      "(GEMM epilogue stores rows into their owners' peer slots)", lockstep=True)
 _def("QB_CMD_CHANNEL", str, "shm", "leader -> worker command channel: shm (shared-memory ring) or gloo (broadcast)",
