@@ -25,6 +25,85 @@ from ..utils import flags
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
 
 
+def _host(t: torch.Tensor) -> torch.Tensor:
+    """Page-locked when a CUDA device is present (async input copies), plain memory otherwise."""
+    return t.pin_memory() if torch.cuda.is_available() else t
+
+
+class CudaGraphs:
+    """Capture backend: CUDA graphs in one shared memory pool (the serving backend)."""
+
+    def __init__(self):
+        self._pool = None
+
+    def pool(self):
+        if self._pool is None:
+            self._pool = torch.cuda.graph_pool_handle()
+        return self._pool
+
+    def capture(self, fn, warmups: int = 2, pool=True):
+        """Runs ``fn`` ``warmups`` times on a side stream, then captures it; returns (graph, the
+        captured call's output)."""
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for _ in range(warmups):
+                fn()
+        torch.cuda.current_stream().wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self.pool() if pool else None):
+            out = fn()
+        return g, out
+
+    def sync(self):
+        torch.cuda.synchronize()
+
+    def count_launches(self) -> int:
+        from ..ops import _ext
+
+        return _ext.ext().launches()
+
+    def add_launches(self, n: int) -> None:
+        from ..ops import _ext
+
+        _ext.ext().add_launches(n)
+
+
+class _HostGraph:
+    def __init__(self, fn, out):
+        self.fn, self.out = fn, out
+
+    def replay(self):
+        self.out.copy_(self.fn())
+
+
+class HostGraphs(CudaGraphs):
+    """Capture backend without a GPU: "capture" keeps the step function and its output tensor,
+    "replay" re-runs the function on the same static input buffers and writes the result into
+    that output in place, as a CUDA-graph replay updates its captured output. Everything the
+    runner does around a replay (bucket choice, padding with the pad lane, input packing, the
+    overlap feedback, validation and the rank vote) then runs on CPU ranks in tests."""
+
+    def pool(self):
+        return None
+
+    def capture(self, fn, warmups: int = 2, pool=True):
+        for _ in range(warmups):
+            fn()
+        out = fn()
+        return _HostGraph(fn, out), out
+
+    def sync(self):
+        pass
+
+    def count_launches(self) -> int:
+        return 0
+
+    def add_launches(self, n: int) -> None:
+        pass
+
+
 class _Bucket:
     def __init__(self, model, B: int, pool):
         dev = model.device
@@ -37,8 +116,8 @@ class _Bucket:
         self.logit_rows = torch.arange(B, dtype=torch.int64, device=dev)
         # two pinned input sets used alternately: with the one-step overlap the host fills step
         # n+1 while step n's input copies may still be queued
-        self._hosts = [(torch.zeros(4 * B, dtype=torch.int32).pin_memory(),
-                        torch.zeros(B, dtype=torch.int64).pin_memory()) for _ in range(2)]
+        self._hosts = [(_host(torch.zeros(4 * B, dtype=torch.int32)),
+                        _host(torch.zeros(B, dtype=torch.int64))) for _ in range(2)]
         self._flip = 0
         self.packed_host, self.tok_host = self._hosts[0]
         self.packed_dev = torch.zeros(4 * B, dtype=torch.int32, device=dev)
@@ -47,9 +126,14 @@ class _Bucket:
         self.pool = pool
 
     def inputs(self, model) -> StepInputs:
+        """The bucket's static device inputs. The host lists are what the last fill put there (the
+        CUDA kernels read only the device tensors and take nothing but the segment count from
+        these; the host reference ops of a CPU rank read the lanes and starts)."""
         B = self.B
+        lanes = getattr(self, "lanes_h", None) or [model.max_batch - 1] * B
+        starts = getattr(self, "pos_h", None) or [0] * B
         return StepInputs(self.tokens, self.pos, self.rows, self.lanes, self.cu, self.pos, self.logit_rows,
-                          list(range(B)), list(range(B + 1)), [0] * B, model.max_seq)
+                          list(lanes), list(range(B + 1)), list(starts), model.max_seq)
 
 
 class _SpecBucket:
@@ -101,8 +185,9 @@ class _SpecBucket:
 class GraphRunner:
     """Runner that replays captured decode graphs; see the module docstring."""
 
-    def __init__(self, model, buckets=None):
+    def __init__(self, model, buckets=None, backend=None):
         self.model = model
+        self.backend = backend or (CudaGraphs() if model.device.type == "cuda" else HostGraphs())
         self.max_batch = model.max_batch - 1  # the model is built with one spare lane: the pad lane
         self.max_seq = model.max_seq
         self.block_size = model.block_size
@@ -111,7 +196,7 @@ class GraphRunner:
         self.buckets = sorted(b for b in (buckets or DEFAULT_BUCKETS) if b <= lim) or [lim]
         if self.buckets[-1] < lim:
             self.buckets.append(lim)
-        self.pool = torch.cuda.graph_pool_handle()
+        self.pool = self.backend.pool()
         self._b = {}
         self._spec: dict[int, _SpecBucket] = {}
         self.enabled = flags.get("QB_GRAPHS")
@@ -134,6 +219,7 @@ class GraphRunner:
         ph[2 * B:3 * B] = torch.tensor(ln, dtype=torch.int32)
         bk.tok_host[:n] = torch.tensor([int(t) for t in tokens], dtype=torch.int64)
         bk.tok_host[n:] = 0
+        bk.lanes_h, bk.pos_h = ln, pos
         bk.packed_dev.copy_(ph, non_blocking=True)
         bk.tokens.copy_(bk.tok_host, non_blocking=True)
         bk.pos.copy_(bk.packed_dev[:B])
@@ -149,67 +235,65 @@ class GraphRunner:
     def prepare(self) -> None:
         """Capture every bucket (largest first, sharing one memory pool). Must run on every rank
         in the same order, before serving starts."""
-        if not self.enabled or self.model.device.type != "cuda":
+        if not self.enabled or (self.model.device.type != "cuda" and not isinstance(self.backend, HostGraphs)):
             return
         m = self.model
         m.begin(self.pad_lane)
         m.attach_blocks(self.pad_lane, [])
-        from ..ops import _ext
-
         import time
 
         for B in sorted(self.buckets, reverse=True):
             t0 = time.perf_counter()
             bk = _Bucket(m, B, self.pool)
             self._fill(bk, [], [], [])
-            s = torch.cuda.Stream()
-            s.wait_stream(torch.cuda.current_stream())
-            with torch.cuda.stream(s):
-                for _ in range(2):
-                    self._run(bk)
-            torch.cuda.current_stream().wait_stream(s)
-            torch.cuda.synchronize()
-            g = torch.cuda.CUDAGraph()
-            l0 = _ext.ext().launches()
-            with torch.cuda.graph(g, pool=self.pool):
-                bk.out = self._run(bk)
-            self.launch_per_replay[B] = _ext.ext().launches() - l0
+            l0 = self.backend.count_launches()
+            g, bk.out = self.backend.capture(lambda bk=bk: self._run(bk))
+            self.launch_per_replay[B] = (self.backend.count_launches() - l0) // 3  # warm-ups + capture
             bk.graph = g
             self._b[B] = bk
             if flags.get("QB_GRAPH_LOG"):
                 print(f"[graph-capture] decode bucket {B}: {self.launch_per_replay[B]} kernels, "
                       f"{time.perf_counter() - t0:.2f}s", flush=True)
-        torch.cuda.synchronize()
+        self.backend.sync()
         self.validate()
 
     def validate(self, tol: float = 5e-2) -> bool:
-        """Boot check of every captured bucket: from the same pad-lane state, a replay and an
-        eager run of the same step must give the same logits (max abs difference within
-        ``tol`` of the logits' scale: the two run the same kernels, and the margin only admits
+        """Boot check of every captured bucket: a replay and an eager run of the same step, from
+        the same lane states, must give the same logits (max abs difference within ``tol`` of
+        the logits' scale: the two run the same kernels, and the margin only admits
         rounding-order differences of the reductions that finish in arrival order, while a replay
-        reading a stale or freed table gives garbage far outside it). Every rank reports its verdict and the ranks agree on
-        the minimum (an all-reduce over the model's group), so either every rank serves from its
-        graphs or none does. Returns whether the graphs stay on. Reference behaviour:
-        ``graph_decode.py`` (``validate``, ``all_ranks``)."""
+        reading a stale or freed table gives garbage far outside it). The step puts one token on
+        each of B distinct lanes (lane i at position 0 of block 1 + i; nothing is being served
+        yet), so rows do not share state as the pad rows of a padded batch do. Every rank reports
+        its verdict and the ranks agree on the minimum (an all-reduce over the model's group), so
+        either every rank serves from its graphs or none does. Returns whether the graphs stay
+        on. Reference behaviour: ``graph_decode.py`` (``validate``, ``all_ranks``)."""
         m = self.model
-        pad = self.pad_lane
         ok = True
         worst = 0.0
         with torch.inference_mode():
             for B, bk in sorted(self._b.items()):
-                conv = m.conv_state[:, pad].clone()
-                rec = m.rec_state[:, pad].clone()
+                lanes = list(range(B))
+
+                def reset():
+                    for ln in lanes:
+                        m.begin(ln)
+                        m.attach_blocks(ln, [1 + ln])
+
+                reset()
+                self._fill(bk, lanes, [(7 * ln + 11) % 1000 for ln in lanes], [0] * B)
                 bk.graph.replay()
                 got = bk.out.float().clone()
-                m.conv_state[:, pad].copy_(conv)
-                m.rec_state[:, pad].copy_(rec)
+                reset()
+                m._sync_tables()
                 exp = self._run(bk).float()
-                m.conv_state[:, pad].copy_(conv)
-                m.rec_state[:, pad].copy_(rec)
+                for ln in lanes:
+                    m.begin(ln)
+                    m.attach_blocks(ln, [])
                 err = (got - exp).abs().max().item()
                 scale = exp.abs().max().item() + 1e-6
                 worst = max(worst, err / scale)
-                if not (err <= tol * scale) or not torch.isfinite(got).all():
+                if not (err <= tol * scale) or not bool(torch.isfinite(got).all()):
                     ok = False
         flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=m.device)
         world = getattr(m.comm, "world", 1)
@@ -409,9 +493,7 @@ class GraphRunner:
             self._fill(bk, lanes, tokens, positions)
             bk.graph.replay()
         self.replays += 1
-        from ..ops import _ext
-
-        _ext.ext().add_launches(self.launch_per_replay.get(B, 0))
+        self.backend.add_launches(self.launch_per_replay.get(B, 0))
         return bk.out[:n]
 
     def decode_launch(self, lanes, tokens, positions, src_rows, keep_rows=()):
@@ -430,9 +512,7 @@ class GraphRunner:
             m._feed_back(bk.tokens, tokens, src_rows)
             bk.graph.replay()
             self.replays += 1
-            from ..ops import _ext
-
-            _ext.ext().add_launches(self.launch_per_replay.get(B, 0))
+            self.backend.add_launches(self.launch_per_replay.get(B, 0))
             return m._launch_tail(bk.out[:n], n, keep_rows)
 
     def __getattr__(self, name):

@@ -53,8 +53,9 @@ _def("QB_FA_SPLITS", int, 0, "flash attention: key-range splits per tile (0: eno
      lockstep=True)
 _def("QB_DN_DECODE", str, "", "DeltaNet decode mixer state path: reg (registers), sm (shared memory by bulk copies); "
      "empty: sm from 16 lanes up", native=True)
-_def("QB_DN_PREFILL", str, "tc", "DeltaNet prefill segments: tc (chunked WY form, state in tensor memory, "
-     "tcgen05 products), recurrence (fp32 token recurrence), chunked_fp32 (chunked WY form on CUDA cores)",
+_def("QB_DN_PREFILL", str, "auto", "DeltaNet prefill segments: tc (chunked WY form, state in tensor memory, "
+     "tcgen05 products), recurrence (fp32 token recurrence), chunked_fp32 (chunked WY form on CUDA cores), auto "
+     "(tc up to 32 value heads per rank, else recurrence)",
      lockstep=True)
 _def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
 _def("QB_PREFILL_ORDER", str, "shortest", "scheduler: order prefill flights are packed in: shortest (fewest "

@@ -434,7 +434,7 @@ def test_chunked_delta_rule_matches_recurrence(monkeypatch, mode):
     rs = torch.randn(lanes, nv, dk, dv, device=DEV) * 0.1
     rs2 = rs.clone().cpu()
     i32 = dict(dtype=torch.int32, device=DEV)
-    assert ops.dn_chunk_plan(cu, dk, dv, qkv.device) is not None
+    assert ops.dn_chunk_plan(cu, dk, dv, qkv.device, mode) is not None
     o = ops.gated_delta_varlen(qkv, ab, a_log, dtb, rs, torch.tensor(ln, **i32), torch.tensor(cu, **i32), nk, nv, dk,
                                dv, ln, cu)
     torch.cuda.synchronize()
