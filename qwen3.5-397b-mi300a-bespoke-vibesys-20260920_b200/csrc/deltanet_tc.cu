@@ -11,9 +11,10 @@
 //   O     = diag(e^G) Q S0 + Mq Delta,     Mq_ts = (q_t . k_s) e^(G_t - G_s)  (s <= t)
 //   S     = e^(G_last) S0 + (diag(e^(G_last - G)) K)^T Delta
 //
-// dn_tc_prep (grid: chunk x value head, every chunk at once, CUDA cores in fp32): the two 64x64
-// Gram products, the unit lower-triangular inverse T by forward substitution (one column per
-// four threads), U and W, and a per-(chunk, head) record in exactly the shared-memory image the
+// dn_tc_prep (grid: chunk x key head, every chunk at once, CUDA cores in fp32): the two 64x64
+// Gram products once per key head, then for each value head sharing it the decays, the unit
+// lower-triangular inverse T by forward substitution (one column per four threads), U and W,
+// and a per-(chunk, value head) record in exactly the shared-memory image the
 // state kernel's MMAs read: U fp32, then W, Q e^G, Mq (bf16, K-major, 128-byte swizzle) and
 // K e^(G_last - G) (bf16, M-major), and e^(G_last).
 //
@@ -62,7 +63,7 @@ constexpr int S_S = 132096;       // S as bf16 MN-major B operand: 2 N-atoms x [
 constexpr int S_D = 164864;       // Delta as bf16 MN-major B operand: 2 N-atoms x [64 K-rows][128 B]
 constexpr int S_BAR = 181248;
 constexpr int S_BYTES = S_BAR + 64 + 1024;
-constexpr int PREP_SMEM = (3 * C * KP + 3 * C * AP + 3 * C) * 4;
+constexpr int PREP_SMEM = (3 * C * KP + 4 * C * AP + 3 * C) * 4;
 constexpr int TM_S = 0, TM_D1 = 128, TM_D2 = 256;
 }  // namespace dntc
 
@@ -94,69 +95,48 @@ __device__ __forceinline__ int swz(int r, int ch) { return r * 128 + ((ch ^ (r &
 __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const float* kn, const float* gb,
                                                          const bf16* qkv, long ldqkv, const int* chunks, int nk,
                                                          int nv, uint8_t* rec_all) {
+  // one CTA per (chunk, key head): the Gram products K K^T and Q K^T depend on the key head only
+  // and are computed once for the nv / nk value heads that share it
   using namespace dntc;
   extern __shared__ float sm[];
-  float* Ks = sm;
-  float* Qs = Ks + C * KP;
-  float* Vs = Qs + C * KP;
-  float* A = Vs + C * KP;
-  float* Mq = A + C * AP;
-  float* Tm = Mq + C * AP;
+  float* Ks = sm;              // [64][KP]
+  float* Qs = Ks + C * KP;     // [64][KP]
+  float* Vs = Qs + C * KP;     // [64][KP] (one value head at a time)
+  float* Kg = Vs + C * KP;     // [64][AP] raw k_t . k_s
+  float* Qg = Kg + C * AP;     // [64][AP] raw q_t . k_s
+  float* A = Qg + C * AP;      // [64][AP]
+  float* Tm = A + C * AP;      // [64][AP]
   float* G = Tm + C * AP;
   float* Bt = G + C;
   float* EG = Bt + C;
-  const int c = blockIdx.x, h = blockIdx.y, tid = threadIdx.x;
+  const int c = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
   const int row0 = chunks[c * 3 + 1], rows = chunks[c * 3 + 2];
-  const int hk = h / (nv / nk);
-  uint8_t* rec = rec_all + ((long)c * nv + h) * REC;
-  // ---- operands (rows >= `rows` are zero: they change nothing)
-  for (int idx = tid; idx < C * 32; idx += 256) {
-    const int t = idx >> 5, i = (idx & 31) * 4;
-    float4 kv = make_float4(0.f, 0.f, 0.f, 0.f), qv = kv;
-    if (t < rows) {
-      const long base = ((long)(row0 + t) * nk + hk) * D + i;
-      kv = *reinterpret_cast<const float4*>(kn + base);
-      qv = *reinterpret_cast<const float4*>(qn + base);
-    }
-    *reinterpret_cast<float4*>(Ks + t * KP + i) = kv;
-    *reinterpret_cast<float4*>(Qs + t * KP + i) = qv;
-  }
-  for (int idx = tid; idx < C * 16; idx += 256) {
-    const int t = idx >> 4, j = (idx & 15) * 8;
-    float v[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    if (t < rows) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(qkv + (long)(row0 + t) * ldqkv + 2L * nk * D + (long)h * D + j);
-      const bf16* e = reinterpret_cast<const bf16*>(&raw);
-#pragma unroll
-      for (int u = 0; u < 8; ++u) v[u] = __bfloat162float(e[u]);
-    }
-    *reinterpret_cast<float4*>(Vs + t * KP + j) = make_float4(v[0], v[1], v[2], v[3]);
-    *reinterpret_cast<float4*>(Vs + t * KP + j + 4) = make_float4(v[4], v[5], v[6], v[7]);
-  }
-  if (tid < C) {
-    const float4 g4 = tid < rows ? *reinterpret_cast<const float4*>(gb + ((long)(row0 + tid) * nv + h) * 4)
-                                 : make_float4(1.f, 0.f, 0.f, 0.f);
-    Bt[tid] = g4.y;
-    G[tid] = g4.z;
-  }
-  __syncthreads();
-  if (tid < 32) {  // inclusive scan of the log decays, two per lane
-    const float a0 = G[2 * tid], a1 = G[2 * tid + 1];
-    float s = a0 + a1;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const float n = __shfl_up_sync(0xffffffffu, s, o);
-      if (tid >= o) s += n;
-    }
-    const float ex = s - (a0 + a1);
-    G[2 * tid] = ex + a0;
-    G[2 * tid + 1] = s;
-  }
-  __syncthreads();
-  if (tid < C) EG[tid] = expf(G[tid]);
-  // ---- A (strictly lower) and Mq (lower incl. diagonal): 4 x 4 outputs per thread
+  const int R = nv / nk;
+  // ---- K and Q of the key head (rows >= `rows` are zero: they change nothing); all loads of a
+  // thread are issued before its shared-memory stores
   {
-    const int ty = tid >> 4, tx = tid & 15;
+    float4 kv[8], qv[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = tid + u * 256, t = idx >> 5, i = (idx & 31) * 4;
+      kv[u] = qv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (t < rows) {
+        const long base = ((long)(row0 + t) * nk + hk) * D + i;
+        kv[u] = *reinterpret_cast<const float4*>(kn + base);
+        qv[u] = *reinterpret_cast<const float4*>(qn + base);
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const int idx = tid + u * 256, t = idx >> 5, i = (idx & 31) * 4;
+      *reinterpret_cast<float4*>(Ks + t * KP + i) = kv[u];
+      *reinterpret_cast<float4*>(Qs + t * KP + i) = qv[u];
+    }
+  }
+  __syncthreads();
+  // ---- raw Gram products, 4 x 4 outputs per thread
+  const int ty = tid >> 4, tx = tid & 15;
+  {
     float aa[4][4], mm[4][4];
 #pragma unroll
     for (int r = 0; r < 4; ++r)
@@ -178,93 +158,149 @@ __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const 
           mm[r][s] += qt[r].x * ks[s].x + qt[r].y * ks[s].y + qt[r].z * ks[s].z + qt[r].w * ks[s].w;
         }
     }
-    __syncthreads();  // G and EG complete
 #pragma unroll
     for (int r = 0; r < 4; ++r)
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        const int t = 4 * ty + r, u = 4 * tx + s;
-        const float dec = u <= t ? expf(G[t] - G[u]) : 0.f;
-        A[t * AP + u] = u < t ? Bt[t] * aa[r][s] * dec : 0.f;
-        Mq[t * AP + u] = u <= t ? mm[r][s] * dec : 0.f;
+        Kg[(4 * ty + r) * AP + 4 * tx + s] = aa[r][s];
+        Qg[(4 * ty + r) * AP + 4 * tx + s] = mm[r][s];
       }
   }
-  __syncthreads();
-  // ---- T = (I + A)^-1 by forward substitution: column cc by four threads (one warp = 8 columns)
-  {
-    const int cc = tid >> 2, part = tid & 3;
-    for (int t = part; t < C; t += 4) Tm[t * AP + cc] = t == cc ? 1.f : 0.f;
-    __syncwarp();
-    for (int t = 1; t < C; ++t) {
-      float sum = 0.f;
-      if (t > cc)
-        for (int s = cc + part; s < t; s += 4) sum += A[t * AP + s] * Tm[s * AP + cc];
-      sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-      sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-      if (t > cc && part == 0) Tm[t * AP + cc] = -sum;
-      __syncwarp();
+  const int last = rows > 0 ? rows - 1 : 0;
+  for (int rr = 0; rr < R; ++rr) {
+    const int h = hk * R + rr;
+    uint8_t* rec = rec_all + ((long)c * nv + h) * REC;
+    __syncthreads();  // the previous value head is done with Vs, A, Tm, G
+    // ---- V of this value head, gates
+    {
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = tid + u * 256, t = idx >> 4, j = (idx & 15) * 8;
+        raw[u] = make_uint4(0, 0, 0, 0);
+        if (t < rows)
+          raw[u] = *reinterpret_cast<const uint4*>(qkv + (long)(row0 + t) * ldqkv + 2L * nk * D + (long)h * D + j);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int idx = tid + u * 256, t = idx >> 4, j = (idx & 15) * 8;
+        const bf16* e = reinterpret_cast<const bf16*>(&raw[u]);
+        *reinterpret_cast<float4*>(Vs + t * KP + j) = make_float4(__bfloat162float(e[0]), __bfloat162float(e[1]),
+                                                                  __bfloat162float(e[2]), __bfloat162float(e[3]));
+        *reinterpret_cast<float4*>(Vs + t * KP + j + 4) = make_float4(__bfloat162float(e[4]), __bfloat162float(e[5]),
+                                                                      __bfloat162float(e[6]), __bfloat162float(e[7]));
+      }
     }
-  }
-  __syncthreads();
-  // ---- U = T diag(beta) V (fp32 record), W = T diag(beta e^G) K (bf16 K-major image): 8 x 8 per thread
-  {
-    const int gy = tid >> 5, gx = tid & 31;
-    const bool isU = gx < 16;
-    const float* src = isU ? Vs + gx * 8 : Ks + (gx - 16) * 8;
-    float acc[8][8];
+    if (tid < C) {
+      const float4 g4 = tid < rows ? *reinterpret_cast<const float4*>(gb + ((long)(row0 + tid) * nv + h) * 4)
+                                   : make_float4(1.f, 0.f, 0.f, 0.f);
+      Bt[tid] = g4.y;
+      G[tid] = g4.z;
+    }
+    __syncthreads();
+    if (tid < 32) {  // inclusive scan of the log decays, two per lane
+      const float a0 = G[2 * tid], a1 = G[2 * tid + 1];
+      float s = a0 + a1;
 #pragma unroll
-    for (int r = 0; r < 8; ++r)
+      for (int o = 1; o < 32; o <<= 1) {
+        const float n = __shfl_up_sync(0xffffffffu, s, o);
+        if (tid >= o) s += n;
+      }
+      const float ex = s - (a0 + a1);
+      G[2 * tid] = ex + a0;
+      G[2 * tid + 1] = s;
+    }
+    __syncthreads();
+    if (tid < C) EG[tid] = expf(G[tid]);
+    // ---- A (strictly lower) into shared memory; Mq (lower incl. diagonal) straight to the record
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
-    for (int s = 0; s < C; ++s) {
-      const float sc = isU ? Bt[s] : Bt[s] * EG[s];
-      const float4 r0 = *reinterpret_cast<const float4*>(src + s * KP);
-      const float4 r1 = *reinterpret_cast<const float4*>(src + s * KP + 4);
-      const float rv[8] = {r0.x * sc, r0.y * sc, r0.z * sc, r0.w * sc, r1.x * sc, r1.y * sc, r1.z * sc, r1.w * sc};
+    for (int r = 0; r < 4; ++r) {
+      const int t = 4 * ty + r;
+      float m4[4];
+#pragma unroll
+      for (int s = 0; s < 4; ++s) {
+        const int u = 4 * tx + s;
+        const float dec = u <= t ? expf(G[t] - G[u]) : 0.f;
+        A[t * AP + u] = u < t ? Bt[t] * Kg[t * AP + u] * dec : 0.f;
+        m4[s] = u <= t ? Qg[t * AP + u] * dec : 0.f;
+      }
+      __nv_bfloat162 p0 = __floats2bfloat162_rn(m4[0], m4[1]), p1 = __floats2bfloat162_rn(m4[2], m4[3]);
+      uint2 w;
+      w.x = *reinterpret_cast<uint32_t*>(&p0);
+      w.y = *reinterpret_cast<uint32_t*>(&p1);
+      const int u0 = 4 * tx;
+      *reinterpret_cast<uint2*>(rec + R_M + swz(t, u0 >> 3) + (u0 & 7) * 2) = w;
+    }
+    __syncthreads();
+    // ---- T = (I + A)^-1 by forward substitution: column cc by four threads (one warp = 8 columns)
+    {
+      const int cc = tid >> 2, part = tid & 3;
+      for (int t = part; t < C; t += 4) Tm[t * AP + cc] = t == cc ? 1.f : 0.f;
+      __syncwarp();
+      for (int t = 1; t < C; ++t) {
+        float sum = 0.f;
+        if (t > cc)
+          for (int s = cc + part; s < t; s += 4) sum += A[t * AP + s] * Tm[s * AP + cc];
+        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+        if (t > cc && part == 0) Tm[t * AP + cc] = -sum;
+        __syncwarp();
+      }
+    }
+    __syncthreads();
+    // ---- U = T diag(beta) V (fp32 record), W = T diag(beta e^G) K (bf16 K-major image): 8 x 8 per thread
+    {
+      const int gy = tid >> 5, gx = tid & 31;
+      const bool isU = gx < 16;
+      const float* src = isU ? Vs + gx * 8 : Ks + (gx - 16) * 8;
+      float acc[8][8];
+#pragma unroll
+      for (int r = 0; r < 8; ++r)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[r][e] = 0.f;
+      for (int s = 0; s < C; ++s) {
+        const float sc = isU ? Bt[s] : Bt[s] * EG[s];
+        const float4 r0 = *reinterpret_cast<const float4*>(src + s * KP);
+        const float4 r1 = *reinterpret_cast<const float4*>(src + s * KP + 4);
+        const float rv[8] = {r0.x * sc, r0.y * sc, r0.z * sc, r0.w * sc, r1.x * sc, r1.y * sc, r1.z * sc, r1.w * sc};
+#pragma unroll
+        for (int r = 0; r < 8; ++r) {
+          const float tv = Tm[(8 * gy + r) * AP + s];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[r][e] += tv * rv[e];
+        }
+      }
 #pragma unroll
       for (int r = 0; r < 8; ++r) {
-        const float tv = Tm[(8 * gy + r) * AP + s];
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[r][e] += tv * rv[e];
+        const int t = 8 * gy + r;
+        if (isU) {
+          float* u = reinterpret_cast<float*>(rec + R_U) + t * D + gx * 8;
+          *reinterpret_cast<float4*>(u) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
+          *reinterpret_cast<float4*>(u + 4) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
+        } else {
+          const int i = (gx - 16) * 8;
+          *reinterpret_cast<uint4*>(rec + R_W + (i >> 6) * 8192 + swz(t, (i & 63) >> 3)) = pack8(acc[r]);
+        }
       }
     }
+    // ---- Q e^G (K-major), K e^(G_last - G) (M-major: the same byte image), e^G_last
+    const float Gl = G[last];
 #pragma unroll
-    for (int r = 0; r < 8; ++r) {
-      const int t = 8 * gy + r;
-      if (isU) {
-        float* u = reinterpret_cast<float*>(rec + R_U) + t * D + gx * 8;
-        *reinterpret_cast<float4*>(u) = make_float4(acc[r][0], acc[r][1], acc[r][2], acc[r][3]);
-        *reinterpret_cast<float4*>(u + 4) = make_float4(acc[r][4], acc[r][5], acc[r][6], acc[r][7]);
-      } else {
-        const int i = (gx - 16) * 8;
-        *reinterpret_cast<uint4*>(rec + R_W + (i >> 6) * 8192 + swz(t, (i & 63) >> 3)) = pack8(acc[r]);
+    for (int u = 0; u < 4; ++u) {
+      const int idx = tid + u * 256, t = idx >> 4, ch = idx & 15;
+      const float eg = EG[t], ekg = t < rows ? expf(Gl - G[t]) : 0.f;
+      float q8[8], k8[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        q8[e] = Qs[t * KP + ch * 8 + e] * eg;
+        k8[e] = Ks[t * KP + ch * 8 + e] * ekg;
       }
+      const int off = (ch >> 3) * 8192 + swz(t, ch & 7);
+      *reinterpret_cast<uint4*>(rec + R_QG + off) = pack8(q8);
+      *reinterpret_cast<uint4*>(rec + R_KG + off) = pack8(k8);
     }
+    if (tid == 0) *reinterpret_cast<float4*>(rec + R_EGL) = make_float4(expf(Gl), 0.f, 0.f, 0.f);
   }
-  // ---- Q e^G (K-major), K e^(G_last - G) (M-major: the same byte image), Mq (K-major), e^G_last
-  const int last = rows > 0 ? rows - 1 : 0;
-  const float Gl = G[last];
-  for (int idx = tid; idx < C * 16; idx += 256) {
-    const int t = idx >> 4, ch = idx & 15;
-    const float eg = EG[t], ekg = t < rows ? expf(Gl - G[t]) : 0.f;
-    float q8[8], k8[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) {
-      q8[u] = Qs[t * KP + ch * 8 + u] * eg;
-      k8[u] = Ks[t * KP + ch * 8 + u] * ekg;
-    }
-    const int off = (ch >> 3) * 8192 + swz(t, ch & 7);
-    *reinterpret_cast<uint4*>(rec + R_QG + off) = pack8(q8);
-    *reinterpret_cast<uint4*>(rec + R_KG + off) = pack8(k8);
-  }
-  for (int idx = tid; idx < C * 8; idx += 256) {
-    const int t = idx >> 3, ch = idx & 7;
-    float m8[8];
-#pragma unroll
-    for (int u = 0; u < 8; ++u) m8[u] = Mq[t * AP + ch * 8 + u];
-    *reinterpret_cast<uint4*>(rec + R_M + swz(t, ch)) = pack8(m8);
-  }
-  if (tid == 0) *reinterpret_cast<float4*>(rec + R_EGL) = make_float4(expf(Gl), 0.f, 0.f, 0.f);
 }
 
 __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_all, const int* chunks,
@@ -499,7 +535,7 @@ int gated_delta_tc(const void* qkv, long ldqkv, const void* ab, long ldab, const
     cudaFuncSetAttribute(dn_tc_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_BYTES);
     attr = true;
   }
-  dn_tc_prep_kernel<<<dim3(n_chunks, nv), 256, PREP_SMEM, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, chunks, nk, nv,
+  dn_tc_prep_kernel<<<dim3(n_chunks, nk), 256, PREP_SMEM, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, chunks, nk, nv,
                                                                rec);
   dn_tc_state_kernel<<<dim3(S, nv), 128, S_BYTES, s>>>(rec, chunks, seg_chunk0, seg_lane, state, lane_stride, nv,
                                                        (bf16*)out, commit ? 1 : 0, err);
