@@ -68,6 +68,7 @@ def parse(argv=None):
     ap.add_argument("--gen-len", type=int, nargs=2, default=(200, 500))
     ap.add_argument("--max-seconds", type=float, default=1500.0, help="safety stop of the timed loop (host clock)")
     ap.add_argument("--out", default=None)
+    ap.add_argument("--records", default=None, help="also write one JSON line per turn (TTFT, lengths, steps)")
     return ap.parse_args(argv)
 
 
@@ -235,6 +236,26 @@ def report(args, *, impl, world, window_ms, host_s, records, step_ms, kinds_summ
     if extra:
         res.update(extra)
     return res
+
+
+def write_records(path, records, step_ms, kinds) -> None:
+    """One JSON line per turn: session, turn, prompt length, reused tokens, generated tokens,
+    admission and first-token step, device TTFT (sum of step intervals) and the kinds of the
+    steps it spanned, host TTFT."""
+    prefix = [0.0]
+    for v in step_ms:
+        prefix.append(prefix[-1] + (v or 0.0))
+    with open(path, "w") as f:
+        for r in records:
+            rec = {"session": r.session, "turn": r.turn, "prompt_len": r.prompt_len, "reused": r.reused,
+                   "generated": r.generated, "submit_step": r.submit_step, "first_step": r.first_step}
+            if r.first_step >= 0:
+                i0, i1 = min(r.submit_step, len(step_ms)), min(r.first_step + 1, len(step_ms))
+                rec["ttft_dev_ms"] = round(prefix[i1] - prefix[i0], 3)
+                rec["ttft_host_ms"] = round((r.t_first - r.t_submit) * 1e3, 3)
+                ks = [k for k in kinds[i0:i1] if k]
+                rec["steps"] = {k: ks.count(k) for k in set(ks)}
+            f.write(json.dumps(rec) + "\n")
 
 
 def build_model(args, rank, world, device):
@@ -420,6 +441,8 @@ def main_ours(args):
     if args.out:
         with open(args.out, "w") as f:
             f.write(line + "\n")
+    if args.records:
+        write_records(args.records, loop.records, step_ms, step_kind)
     if world > 1:
         if hasattr(model, "release"):
             model.release()
