@@ -115,7 +115,7 @@ class Scheduler:
                  token_budget: int = PREFILL_TOKEN_BUDGET, max_prefill_burst: int = MAX_PREFILL_BURST,
                  mixed: bool = False, speculative: bool = False, timer: StepTimer | None = None,
                  prefill_order: str | None = None, max_skips: int = MAX_PREFILL_SKIPS,
-                 overlap: bool | None = None) -> None:
+                 overlap: bool | None = None, prefill_pack: str | None = None) -> None:
         self.runner = runner
         self.cache = cache
         self.block_size = cache.block_size
@@ -132,6 +132,13 @@ class Scheduler:
             raise ValueError(f"prefill_order must be fifo or shortest, got {prefill_order!r}")
         self.prefill_order = prefill_order
         self.max_skips = max_skips
+        if prefill_pack is None:
+            from ..utils import flags
+
+            prefill_pack = flags.get("QB_PREFILL_PACK")
+        if prefill_pack not in ("fill", "finish"):
+            raise ValueError(f"prefill_pack must be fill or finish, got {prefill_pack!r}")
+        self.prefill_pack = prefill_pack
         from ..utils import flags as _flags
 
         self.cache_stats_every = int(_flags.get("QB_CACHE_STATS"))
@@ -320,13 +327,18 @@ class Scheduler:
 
     def _select_prefill(self) -> list[tuple[_Flight, list[int]]]:
         batch, budget = [], self.token_budget
+        completing = False  # the batch already gives some request its first token
         for f in self._prefill_queue():
             n = min(len(f.pending), self.prefill_chunk, budget)
             if f.boundary > f.pos:
                 n = min(n, f.boundary - f.pos)
             if n <= 0:
                 break
+            done = n == len(f.pending)
+            if completing and self.prefill_pack == "finish" and not done:
+                continue  # would only lengthen the step that delivers those first tokens
             batch.append((f, f.pending[:n]))
+            completing |= done
             budget -= n
             if budget <= 0:
                 break

@@ -60,6 +60,8 @@ _def("QB_DN_PREFILL", str, "auto", "DeltaNet prefill segments: tc (chunked WY fo
 _def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
 _def("QB_PREFILL_ORDER", str, "shortest", "scheduler: order prefill flights are packed in: shortest (fewest "
      "pending prompt tokens first, with aging) or fifo (admission order)")
+_def("QB_PREFILL_PACK", str, "fill", "scheduler: fill (pack prefill chunks up to the token budget) or finish "
+     "(once a step gives some request its first token, add only requests whose prompt also completes in it)")
 _def("QB_OVERLAP", bool, True, "scheduler: launch decode step n+1 (tokens fed back on the device) before reading "
      "step n back", lockstep=True)
 _def("QB_MIXED", bool, False, "scheduler: decode steps also carry prefill chunks in the same forward")

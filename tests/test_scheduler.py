@@ -217,3 +217,26 @@ def test_overlap_random_interleavings_match_greedy(seed):
     # nothing but the trie holds blocks once idle
     held = sum(len(node.blocks) for node in cache._iter() if not node.is_root())
     assert cache.alloc.free_count() + held >= 0
+
+
+@pytest.mark.parametrize("pack", ["fill", "finish"])
+def test_prefill_pack_modes_match_greedy_and_finish_keeps_steps_short(pack):
+    """Both packing modes give every turn its uncached greedy tokens. With ``finish``, a step that
+    completes a short prompt carries no chunk of a long prompt that would not complete."""
+    r = FakeRunner(max_batch=3, num_snapshots=6, block_size=4)
+    s = Scheduler(r, SessionCache(BlockAllocator(400, 4), 4, 6), prefill_chunk=64, token_budget=64,
+                  prefill_pack=pack)
+    for turn, prompt, toks, ends in run_sessions(s, 5, 3, 6, random.Random(9)):
+        assert toks == greedy(prompt, 6)
+    r2 = FakeRunner(max_batch=3, block_size=4)
+    s2 = Scheduler(r2, SessionCache(BlockAllocator(400, 4), 4, 6), prefill_chunk=64, token_budget=64,
+                   prefill_pack=pack)
+    sizes = []
+    orig = r2.prefill_batch
+    r2.prefill_batch = lambda calls: (sizes.append([len(i) for _, i, _ in calls]), orig(calls))[1]
+    s2.submit(Request(list(range(1, 200)), 1, lambda e: None))
+    s2.submit(Request(list(range(300, 310)), 1, lambda e: None))
+    s2.step()
+    first = sizes[0]
+    assert first[0] == 10  # the short prompt first (shortest-first order)
+    assert (len(first) == 1) == (pack == "finish")
