@@ -94,9 +94,10 @@ __device__ __forceinline__ int swz(int r, int ch) { return r * 128 + ((ch ^ (r &
 
 __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const float* kn, const float* gb,
                                                          const bf16* qkv, long ldqkv, const int* chunks, int nk,
-                                                         int nv, uint8_t* rec_all) {
-  // one CTA per (chunk, key head): the Gram products K K^T and Q K^T depend on the key head only
-  // and are computed once for the nv / nk value heads that share it
+                                                         int nv, int hpc, uint8_t* rec_all) {
+  // one CTA per (chunk, key head, group of hpc value heads): the Gram products K K^T and Q K^T
+  // depend on the key head only and are computed once for the value heads of the group (all
+  // nv / nk of them when the grid has enough CTAs, one per CTA when it would not fill the GPU)
   using namespace dntc;
   extern __shared__ float sm[];
   float* Ks = sm;              // [64][KP]
@@ -112,6 +113,7 @@ __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const 
   const int c = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
   const int row0 = chunks[c * 3 + 1], rows = chunks[c * 3 + 2];
   const int R = nv / nk;
+  const int h0 = hk * R + blockIdx.z * hpc;
   // ---- K and Q of the key head (rows >= `rows` are zero: they change nothing); all loads of a
   // thread are issued before its shared-memory stores
   {
@@ -167,8 +169,8 @@ __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const 
       }
   }
   const int last = rows > 0 ? rows - 1 : 0;
-  for (int rr = 0; rr < R; ++rr) {
-    const int h = hk * R + rr;
+  for (int rr = 0; rr < hpc; ++rr) {
+    const int h = h0 + rr;
     uint8_t* rec = rec_all + ((long)c * nv + h) * REC;
     __syncthreads();  // the previous value head is done with Vs, A, Tm, G
     // ---- V of this value head, gates
@@ -535,8 +537,12 @@ int gated_delta_tc(const void* qkv, long ldqkv, const void* ab, long ldab, const
     cudaFuncSetAttribute(dn_tc_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_BYTES);
     attr = true;
   }
-  dn_tc_prep_kernel<<<dim3(n_chunks, nk), 256, PREP_SMEM, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, chunks, nk, nv,
-                                                               rec);
+  // value heads per prep CTA: a key head's whole group while that still gives a full wave of
+  // CTAs (the Gram products are shared), else one (more CTAs in flight for short segments)
+  const int R = nv / nk;
+  const int hpc = (long)n_chunks * nk >= 148 ? R : 1;
+  dn_tc_prep_kernel<<<dim3(n_chunks, nk, R / hpc), 256, PREP_SMEM, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, chunks,
+                                                                       nk, nv, hpc, rec);
   dn_tc_state_kernel<<<dim3(S, nv), 128, S_BYTES, s>>>(rec, chunks, seg_chunk0, seg_lane, state, lane_stride, nv,
                                                        (bf16*)out, commit ? 1 : 0, err);
   return (int)cudaGetLastError();

@@ -73,6 +73,7 @@ def build_hf(model_dir: str, dtype=torch.float32, reference: str = "hf"):
                                    if k not in ("model_type", "attn_output_gate", "full_attention_interval",
                                                 "mtp_num_hidden_layers")})
     hcfg._attn_implementation = "eager"
+    hcfg._experts_implementation = "eager"  # the plain loop over experts (no GPU kernels on host tensors)
     model = Qwen3_5MoeForCausalLM(hcfg).to(dtype).eval()
     ck = Checkpoint(model_dir)
     sd = {}
