@@ -139,7 +139,7 @@ def gated_delta_varlen(qkv, ab, a_log, dt_bias, rec_state, seg_lane, cu, nk, nv,
     q/k l2-normalised, ``q *= dk**-0.5``, key heads repeated to value heads. ``rec_state``
     [lanes, nv, dk, dv] fp32 is continued and updated. Returns [T, nv, dv] in ``qkv.dtype``."""
     if _cuda(qkv):
-        mode = dn_prefill_mode(nv)
+        mode = dn_prefill_mode(nv, cu_h)
         plan = dn_chunk_plan(cu_h, dk, dv, qkv.device, mode)
         if plan is not None:
             chunks, seg0 = plan
@@ -239,17 +239,21 @@ def _cache_put(cache: dict, tag: tuple, key, value) -> None:
 
 
 DN_TC_MAX_HEADS = 32
+DN_TC_MIN_TOKENS = 1024
 
 
-def dn_prefill_mode(nv: int) -> str:
-    """The DeltaNet prefill path for ``nv`` value heads on this rank (``QB_DN_PREFILL``; ``auto``:
-    the tensor-core chunked form up to ``DN_TC_MAX_HEADS`` heads, i.e. from 2-way tensor
-    parallelism on, where it measured 2-2.6x faster than the token recurrence at 8 heads; at the
-    full 64 heads of one GPU the two measured equal, 0.40 vs 0.36 ms for 800 tokens, and the
-    exact fp32 recurrence is kept)."""
+def dn_prefill_mode(nv: int, cu_h=None) -> str:
+    """The DeltaNet prefill path for ``nv`` value heads on this rank (``QB_DN_PREFILL``). ``auto``:
+    the tensor-core chunked form up to ``DN_TC_MAX_HEADS`` heads (from 2-way tensor parallelism
+    on; at 8 heads it measured 1.2-3x faster than the token recurrence) and, at more heads, for
+    batches whose longest segment has at least ``DN_TC_MIN_TOKENS`` tokens (64 heads: 1.37 vs
+    1.79 ms for 4096 tokens, 0.375 vs 0.358 ms for 800, where the exact fp32 recurrence is kept)."""
     mode = flags.get("QB_DN_PREFILL")
     if mode == "auto":
-        return "tc" if nv <= DN_TC_MAX_HEADS else "recurrence"
+        if nv <= DN_TC_MAX_HEADS:
+            return "tc"
+        longest = max((cu_h[i + 1] - cu_h[i] for i in range(len(cu_h) - 1)), default=0) if cu_h else 0
+        return "tc" if longest >= DN_TC_MIN_TOKENS else "recurrence"
     return mode
 
 
