@@ -66,7 +66,9 @@ def parse(argv=None):
     ap.add_argument("--first-len", type=int, nargs=2, default=(2000, 8000))
     ap.add_argument("--user-len", type=int, nargs=2, default=(200, 1000))
     ap.add_argument("--gen-len", type=int, nargs=2, default=(200, 500))
-    ap.add_argument("--max-seconds", type=float, default=1500.0, help="safety stop of the timed loop (host clock)")
+    ap.add_argument("--max-seconds", type=float, default=780.0,
+                    help="safety stop of the timed loop (host clock): past it the loop ends, the line says "
+                         "'incomplete' and the value covers the turns >= 2 that got their first token")
     ap.add_argument("--out", default=None)
     ap.add_argument("--records", default=None, help="also write one JSON line per turn (TTFT, lengths, steps)")
     return ap.parse_args(argv)
