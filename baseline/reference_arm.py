@@ -246,7 +246,10 @@ def main(args, report) -> None:
     brackets = []
     loop.start()
     last_log = t_host0
-    while loop.active and time.perf_counter() - t_host0 < args.max_seconds:
+    from bench import loop_seconds
+
+    limit_s = loop_seconds(args)
+    while loop.active and time.perf_counter() - t_host0 < limit_s:
         s = stamp()
         sched.step()
         brackets.append((s, stamp()))
@@ -274,7 +277,7 @@ def main(args, report) -> None:
                  cfg_desc=(f"Qwen3.5-397B-A17B geometry ({len(model.layers)} layers, MXFP4 experts), reference "
                            f"engine (stock SEED_* defaults, graph capture on)" if args.model == "full"
                            else "tiny parity model, reference engine"),
-                 expert_storage="all layers distinct",
+                 expert_storage="all layers distinct", t_end=t_host1,
                  extra={"reference_tree": "baseline/_ref (plain copy of the reference)", "checkpoint": ckpt,
                         "checkpoint_expert_codes": "zeros (file holes; the box's disk cannot hold the random "
                         "codes; every byte is still read and multiplied)" if getattr(args, "ref_zero_codes", False)

@@ -42,10 +42,11 @@ def main(rank, world, port):
         dist.all_reduce(y)
         r2, n2 = ops.add_rmsnorm(y.bfloat16(), base.clone(), w, 1e-6)
         torch.cuda.synchronize()
-        # the switch sums in fp32 in its own order: at most one bf16 rounding step apart
+        # the switch sums in fp32 and returns the sum as bf16 with its own rounding: the sum may be
+        # one bf16 step of itself away from NCCL's, and the residual add rounds once more
         d = (r1.float() - r2.float()).abs()
-        tol = 2 ** -7 * r2.float().abs() + 2 ** -7 * y.abs().max().item() * 2 ** -7 + 1e-6
-        assert bool((d <= tol + 1e-2).all()), (rows, d.max().item())
+        tol = 2 ** -7 * (y.abs() + r2.float().abs()) + 1e-6
+        assert bool((d <= tol).all()), (rows, d.max().item())
         worst = max(worst, d.max().item())
         assert (n1.float() - n2.float()).abs().max().item() < 2e-2 * n2.float().abs().max().item() + 1e-3
         # every rank holds identical bits
