@@ -82,6 +82,8 @@ class _Flight:
     out_ids: list[int] = field(default_factory=list)
     last_logits: Any = None
     done: bool = False
+    forced: list[int] = field(default_factory=list)  # folded suffix ids still to feed after next_token
+    queued_at: float = field(default_factory=time.perf_counter)  # entered the prefill queue
 
 
 @dataclass
@@ -115,7 +117,8 @@ class Scheduler:
                  token_budget: int = PREFILL_TOKEN_BUDGET, max_prefill_burst: int = MAX_PREFILL_BURST,
                  mixed: bool = False, speculative: bool = False, timer: StepTimer | None = None,
                  prefill_order: str | None = None, max_skips: int = MAX_PREFILL_SKIPS,
-                 overlap: bool | None = None, prefill_pack: str | None = None) -> None:
+                 overlap: bool | None = None, prefill_pack: str | None = None, fold_suffix: bool | None = None,
+                 prefill_accum: bool | None = None) -> None:
         self.runner = runner
         self.cache = cache
         self.block_size = cache.block_size
@@ -142,6 +145,12 @@ class Scheduler:
         from ..utils import flags as _flags
 
         self.cache_stats_every = int(_flags.get("QB_CACHE_STATS"))
+        self.fold_suffix = bool(_flags.get("QB_FOLD_SUFFIX")) if fold_suffix is None else fold_suffix
+        self.prefill_accum = bool(_flags.get("QB_PREFILL_ACCUM")) if prefill_accum is None else prefill_accum
+        self.accum_tokens = int(_flags.get("QB_PREFILL_ACCUM_TOKENS"))
+        self.accum_wait_s = float(_flags.get("QB_PREFILL_ACCUM_WAIT_MS")) / 1e3
+        self.accum_min_decode = int(_flags.get("QB_PREFILL_ACCUM_MIN_DECODE"))
+        self.held_steps = 0  # steps on which queued prefill was held back (accumulation)
         self.finished = 0
         if overlap is None:
             overlap = bool(_flags.get("QB_OVERLAP"))
@@ -229,7 +238,8 @@ class Scheduler:
                 if not self._admit(self.waiting[0]):
                     break
                 self.waiting.popleft()
-            if self.prefilling and (not self.decoding or self.burst < self.max_prefill_burst):
+            if self.prefilling and (not self.decoding or self.burst < self.max_prefill_burst) \
+                    and not self._hold_prefill():
                 self._complete_inflight()  # a prefill or mixed step starts from a quiet pipeline
                 if self.mixed and self.decoding:
                     self._decode_step(with_prefill=True)
@@ -252,6 +262,22 @@ class Scheduler:
             traceback.print_exc()
             self._abort_all(msg)
             return True
+
+    def _hold_prefill(self) -> bool:
+        """Prefill accumulation: while many lanes decode, a prefill step costs nearly the same
+        for few tokens as for a full budget (it streams every layer's experts either way), so
+        queued prefill waits until ``accum_tokens`` tokens can be packed into one step or its
+        oldest flight has waited ``accum_wait_s``; decode steps run meanwhile. Reference
+        behaviour: ``scheduler.py:107-128`` (``SEED_PREFILL_ACCUM``)."""
+        if not (self.prefill_accum and len(self.decoding) >= max(1, self.accum_min_decode)):
+            return False
+        packable = sum(min(len(f.pending), self.prefill_chunk) for f in self.prefilling)
+        oldest = min(f.queued_at for f in self.prefilling)
+        if packable >= min(self.accum_tokens, self.token_budget) or \
+                time.perf_counter() - oldest >= self.accum_wait_s:
+            return False
+        self.held_steps += 1
+        return True
 
     def _watch_status(self) -> None:
         """Poll the device status word (raises ``DeviceStatusError``: the step's caller aborts)."""
@@ -361,6 +387,13 @@ class Scheduler:
             f.pending = f.pending[len(ids):]
             if f.pos == f.boundary:
                 self._publish(f, f.req.prompt, f.pos, lg)
+                if self.fold_suffix and f.pending and f.req.max_new > 0:
+                    # the suffix rides the next decode steps as forced input ids
+                    self.prefilling.remove(f)
+                    f.next_token, f.forced, f.pending = f.pending[0], list(f.pending[1:]), []
+                    f.last_logits = lg
+                    self.decoding.append(f)
+                    continue
             if not f.pending:
                 self.prefilling.remove(f)
                 self._first_token(f, lg)
@@ -379,7 +412,7 @@ class Scheduler:
     def _decode_step(self, with_prefill: bool = False) -> None:
         flights = list(self.decoding)
         if self.overlap and not with_prefill and not self.speculative and \
-                all(not f.req.temperature for f in flights):
+                all(not f.req.temperature and not f.forced for f in flights):
             return self._overlap_step()
         self._complete_inflight()
         flights = list(self.decoding)
@@ -401,6 +434,9 @@ class Scheduler:
         for i, (f, t) in enumerate(zip(flights, sampled)):
             f.pos += 1
             f.last_logits = self.runner.decode_row(logits, i)
+            if f.forced:  # a folded suffix id is still to be fed: the sample is not output
+                f.next_token = f.forced.pop(0)
+                continue
             self._emit(f, t)
         if pre:
             self._finish_prefill(pre, plog)
@@ -454,7 +490,7 @@ class Scheduler:
 
     def _spec_ok(self, flights: Sequence[_Flight]) -> bool:
         k1 = self.runner.decode_tokens_per_step()
-        return k1 > 1 and all(f.pos + k1 <= self.runner.max_seq for f in flights)
+        return k1 > 1 and all(f.pos + k1 <= self.runner.max_seq and not f.forced for f in flights)
 
     def _speculative_step(self, flights: list[_Flight]) -> None:
         k1 = self.runner.decode_tokens_per_step()

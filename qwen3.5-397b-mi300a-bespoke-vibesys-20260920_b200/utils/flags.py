@@ -64,6 +64,14 @@ _def("QB_PREFILL_PACK", str, "fill", "scheduler: fill (pack prefill chunks up to
      "(once a step gives some request its first token, add only requests whose prompt also completes in it)")
 _def("QB_OVERLAP", bool, True, "scheduler: launch decode step n+1 (tokens fed back on the device) before reading "
      "step n back", lockstep=True)
+_def("QB_FOLD_SUFFIX", bool, False, "scheduler: the chat template's generation suffix after the turn-open boundary "
+     "is fed through the following decode steps (their sampled ids discarded) instead of a prefill step of its own")
+_def("QB_PREFILL_ACCUM", bool, False, "scheduler: while at least QB_PREFILL_ACCUM_MIN_DECODE lanes decode, hold "
+     "queued prefill until QB_PREFILL_ACCUM_TOKENS tokens are packable or the oldest has waited "
+     "QB_PREFILL_ACCUM_WAIT_MS")
+_def("QB_PREFILL_ACCUM_TOKENS", int, 1024, "scheduler: packable prefill tokens that fire a held prefill step")
+_def("QB_PREFILL_ACCUM_WAIT_MS", float, 400.0, "scheduler: longest hold of a queued prefill (host clock)")
+_def("QB_PREFILL_ACCUM_MIN_DECODE", int, 48, "scheduler: decoding lanes below which prefill fires at once")
 _def("QB_MIXED", bool, False, "scheduler: decode steps also carry prefill chunks in the same forward")
 # ---- collectives and multi-rank plumbing
 _def("QB_COMM", str, "fused", "tensor-parallel all-reduce: fused (peer-memory kernels) or nccl", lockstep=True)

@@ -43,6 +43,7 @@ class FakeRunner:
         self.snaps = {}
         self.node_logits = {}
         self.calls = []
+        self.prefill_tokens = 0
         self.mtp_k = mtp_k
 
     def begin(self, lane):
@@ -85,6 +86,7 @@ class FakeRunner:
 
     def prefill_batch(self, calls):
         self.calls.append(("prefill", len(calls)))
+        self.prefill_tokens += sum(len(ids) for _, ids, _ in calls)
         return [Logits([self._fwd(l, ids, s)]) for l, ids, s in calls]
 
     def prefill(self, lane, ids, start):

@@ -240,3 +240,98 @@ def test_prefill_pack_modes_match_greedy_and_finish_keeps_steps_short(pack):
     first = sizes[0]
     assert first[0] == 10  # the short prompt first (shortest-first order)
     assert (len(first) == 1) == (pack == "finish")
+
+
+def _chat_sessions(sched, sessions, turns, max_new, rng, suffix):
+    """Like ``run_sessions`` but every prompt ends with a ``suffix``-token generation suffix."""
+    hist = {s: [rng.randrange(1000) for _ in range(rng.randint(8, 30))] for s in range(sessions)}
+    log = []
+    for turn in range(turns):
+        res = {}
+        for s in range(sessions):
+            prompt = hist[s] + [900 + i for i in range(suffix)]
+            toks, ends = [], []
+            res[s] = (prompt, toks, ends)
+            sched.submit(Request(list(prompt), max_new, lambda e, toks=toks, ends=ends:
+                                 toks.append(e[1]) if e[0] == "tok" else ends.append(e), suffix_len=suffix))
+        sched.run_until_idle()
+        for s in range(sessions):
+            prompt, toks, ends = res[s]
+            log.append((turn, prompt, toks, ends))
+            hist[s] = prompt[:len(prompt) - suffix] + toks + [rng.randrange(1000) for _ in range(rng.randint(5, 20))]
+    return log
+
+
+@pytest.mark.parametrize("overlap", [False, True])
+@pytest.mark.parametrize("mixed", [False, True])
+def test_folded_suffix_same_tokens_and_no_suffix_prefill(mixed, overlap):
+    """QB_FOLD_SUFFIX: the generation suffix after the turn-open boundary rides the following
+    decode steps as forced input ids. Every turn's output equals uncached greedy on the full
+    prompt, no prefill call ends at the suffix, and the boundary node is still published."""
+    out = {}
+    for fold in (False, True):
+        r = FakeRunner(max_batch=3, num_snapshots=8, block_size=4)
+        cache = SessionCache(BlockAllocator(600, 4), 4, 8)
+        s = Scheduler(r, cache, prefill_chunk=16, token_budget=32, mixed=mixed, overlap=overlap, fold_suffix=fold)
+        log = _chat_sessions(s, 3, 3, 7, random.Random(5), suffix=5)
+        for turn, prompt, toks, ends in log:
+            assert ends[0][0] == "end", ends
+            assert toks == greedy(prompt, 7), (fold, turn)
+        pre_tokens = r.prefill_tokens
+        out[fold] = (pre_tokens, sum(1 for c in r.calls if c[0] == "prefill"))
+        assert cache.hits > 0
+    assert out[True][0] == out[False][0] - 5 * 9  # the 9 turns' suffixes were decoded, not prefilled
+    assert out[True][1] < out[False][1]
+
+
+def test_prefill_accumulation_holds_until_enough_tokens():
+    """QB_PREFILL_ACCUM: with enough lanes decoding, a short queued prefill waits (decode steps
+    run) until the packable tokens reach the threshold; outputs stay greedy-exact."""
+    r = FakeRunner(max_batch=4, num_snapshots=8, block_size=4)
+    cache = SessionCache(BlockAllocator(600, 4), 4, 8)
+    s = Scheduler(r, cache, prefill_chunk=64, token_budget=64, prefill_accum=True, overlap=False)
+    s.accum_min_decode, s.accum_tokens, s.accum_wait_s = 2, 40, 1e9
+    ev = {}
+
+    def sub(i, prompt, n):
+        ev[i] = ([], [])
+        s.submit(Request(prompt, n, lambda e, i=i: ev[i][0].append(e[1]) if e[0] == "tok" else ev[i][1].append(e)))
+
+    rng = random.Random(2)
+    prompts = [[rng.randrange(1000) for _ in range(12)] for _ in range(4)]
+    sub(0, prompts[0], 30)
+    sub(1, prompts[1], 30)
+    for _ in range(6):  # both decoding
+        s.step()
+    assert len(s.decoding) == 2
+    sub(2, prompts[2], 5)  # 12 pending tokens < 40: held
+    for _ in range(3):
+        s.step()
+    assert s.held_steps >= 3 and len(s.prefilling) == 1
+    sub(3, prompts[3], 5)  # still 24 < 40
+    s.step()
+    assert len(s.prefilling) == 2
+    s.accum_tokens = 20  # 24 >= 20: fires
+    s.step()
+    assert not s.prefilling
+    s.run_until_idle()
+    for i in range(4):
+        assert ev[i][0] == greedy(prompts[i], 30 if i < 2 else 5), i
+
+
+def test_prefill_accumulation_fires_after_the_wait_and_below_min_decode():
+    r = FakeRunner(max_batch=3, num_snapshots=8, block_size=4)
+    cache = SessionCache(BlockAllocator(400, 4), 4, 8)
+    s = Scheduler(r, cache, prefill_accum=True, overlap=False)
+    s.accum_min_decode, s.accum_tokens, s.accum_wait_s = 1, 10**6, 0.0
+    toks = []
+    s.submit(Request([1, 2, 3, 4, 5], 4, lambda e: toks.append(e[1]) if e[0] == "tok" else None))
+    s.run_until_idle()
+    assert toks == greedy([1, 2, 3, 4, 5], 4) and s.held_steps == 0  # no lane decoding: fires at once
+    s.accum_wait_s = 0.0
+    s.submit(Request([7] * 9, 20, lambda e: None))
+    s.step()
+    s.step()
+    s.submit(Request([8] * 5, 3, lambda e: None))
+    s.run_until_idle()  # the wait bound (0 s) fires it on the next step
+    assert s.idle()
