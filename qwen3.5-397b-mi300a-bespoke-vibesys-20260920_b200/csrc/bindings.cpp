@@ -38,10 +38,45 @@ Tensor& status_tensor(const at::Device& dev) {
   static std::unordered_map<int, Tensor> m;
   std::lock_guard<std::mutex> g(mu);
   auto it = m.find(dev.index());
-  if (it == m.end()) it = m.emplace(dev.index(), at::zeros({4}, at::TensorOptions().dtype(at::kInt).device(dev))).first;
+  if (it == m.end()) {
+    it = m.emplace(dev.index(), at::zeros({4}, at::TensorOptions().dtype(at::kInt).device(dev))).first;
+    // debug build: the bounds checks of every translation unit record into this word
+    c10::cuda::CUDAGuard g(dev.index());
+    int* word = it->second.data_ptr<int>();
+    TORCH_CHECK(qb::bounds_install_elementwise(word) == 0 && qb::bounds_install_sequence(word) == 0,
+                "bounds-check status word install failed");
+  }
   return it->second;
 }
 int* err_ptr(const Tensor& like) { return status_tensor(like.device()).data_ptr<int>(); }
+
+// Scratch buffers: in the debug build (-DQB_BOUNDS) each gets CANARY_BYTES of CANARY_BYTE after
+// its end, compared by a check kernel after the launch that used it (bounds.cuh); in the release
+// build a plain allocation.
+struct Scratch {
+  Tensor t;      // the buffer the kernel uses
+  Tensor bytes;  // debug build: the allocation including the canary
+  long nbytes = 0;
+  int site = 0;
+};
+
+Scratch scratch_empty(long n, const at::TensorOptions& opt, int site) {
+  Scratch sc;
+  sc.site = site;
+  if (!qb::bounds_build()) {
+    sc.t = at::empty({n}, opt);
+    return sc;
+  }
+  sc.nbytes = n * (long)c10::elementSize(c10::typeMetaToScalarType(opt.dtype()));
+  sc.bytes = at::empty({sc.nbytes + qb::CANARY_BYTES}, opt.dtype(at::kByte));
+  cudaMemsetAsync(sc.bytes.data_ptr<uint8_t>() + sc.nbytes, qb::CANARY_BYTE, qb::CANARY_BYTES, stream());
+  sc.t = sc.bytes.narrow(0, 0, sc.nbytes).view(c10::typeMetaToScalarType(opt.dtype()));
+  return sc;
+}
+
+void scratch_check(const Scratch& sc) {
+  if (qb::bounds_build() && sc.bytes.defined()) qb::canary_check(sc.bytes.data_ptr<uint8_t>() + sc.nbytes, sc.site, stream());
+}
 
 long row_stride(const Tensor& t) { return t.dim() >= 2 ? t.stride(0) : t.size(-1); }
 
@@ -79,14 +114,16 @@ Tensor linear(Tensor x, Tensor w, c10::optional<Tensor> out) {
   TORCH_CHECK((x.stride(0) * 2) % 16 == 0 && (w.stride(0) * 2) % 16 == 0, "linear: row strides must be 16B multiples");
   // stream-K workspace when the tiles do not divide evenly over the SMs (decode projections)
   const long wsf = qb::gemm_split_ws_floats(T, N, K);
-  Tensor ws, cnt;
+  Scratch ws;
+  Tensor cnt;
   if (wsf) {
-    ws = at::empty({wsf}, x.options().dtype(at::kFloat));
+    ws = scratch_empty(wsf, x.options().dtype(at::kFloat), qb::BS_CANARY_GEMM_WS);
     cnt = gemm_counters(x, (long)((N + 127) / 128) * ((T + 15) / 16));
   }
   LAUNCH(qb::gemm_ws(x.data_ptr(), x.stride(0), w.data_ptr(), w.stride(0), y.data_ptr(), y.stride(0), T, N, K, bf, 0,
-                     err_ptr(x), stream(), 0, wsf ? ws.data_ptr<float>() : nullptr,
+                     err_ptr(x), stream(), 0, wsf ? ws.t.data_ptr<float>() : nullptr,
                      wsf ? cnt.data_ptr<int>() : nullptr));
+  scratch_check(ws);
   return y;
 }
 
@@ -133,7 +170,8 @@ Tensor silu_mul(Tensor gu) {
 Tensor embed(Tensor tok, Tensor table) {
   TORCH_CHECK(tok.scalar_type() == at::kLong, "embed: int64 tokens");
   Tensor out = at::empty({tok.size(0), table.size(1)}, table.options());
-  LAUNCH(qb::embed(tok.data_ptr<int64_t>(), table.data_ptr(), out.data_ptr(), tok.size(0), table.size(1), stream()));
+  LAUNCH(qb::embed(tok.data_ptr<int64_t>(), table.data_ptr(), out.data_ptr(), tok.size(0), table.size(1),
+                         table.size(0), stream()));
   return out;
 }
 
@@ -190,7 +228,8 @@ Tensor qk_norm_rope_kv_write(Tensor q, Tensor k, Tensor v, Tensor qn, Tensor kn,
   Tensor qout = at::empty({T, nq, hd}, q.options());
   LAUNCH(qb::qk_norm_rope_kv_write(q.data_ptr(), q.stride(0), nq, nkv, hd, qn.data_ptr<float>(), kn.data_ptr<float>(),
                                    pos.data_ptr<int>(), rows.data_ptr<int>(), kc.data_ptr(), vc.data_ptr(),
-                                   qout.data_ptr(), T, rot, (float)theta, (float)eps, stream()));
+                                   qout.data_ptr(), T, rot, (float)theta, (float)eps, kc.numel() / ((long)nkv * hd),
+                                   stream()));
   return qout;
 }
 
@@ -209,12 +248,13 @@ Tensor attention_varlen(Tensor q, Tensor kc, Tensor vc, Tensor table, Tensor seg
   if (splits < 1) splits = 1;
   if (splits > 64) splits = 64;
   Tensor out = at::empty_like(q);
-  Tensor ws;
-  if (splits > 1) ws = at::empty({(long)T * nq * splits * (hd + 2)}, q.options().dtype(at::kFloat));
+  Scratch ws;
+  if (splits > 1) ws = scratch_empty((long)T * nq * splits * (hd + 2), q.options().dtype(at::kFloat), qb::BS_CANARY_ATTN_WS);
   LAUNCH(qb::attention_varlen(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), table.data_ptr<int>(), table.size(1),
                               pos.data_ptr<int>(), seg_lane.data_ptr<int>(), cu.data_ptr<int>(), S, T, nq, nkv, hd,
-                              block_size, splits, splits > 1 ? ws.data_ptr<float>() : nullptr, out.data_ptr(),
+                              block_size, splits, splits > 1 ? ws.t.data_ptr<float>() : nullptr, out.data_ptr(),
                               stream()));
+  scratch_check(ws);
   if (splits > 1) g_launches.fetch_add(1, std::memory_order_relaxed);  // the split-combine kernel
   return out;
 }
@@ -226,12 +266,13 @@ Tensor attention_fa(Tensor q, Tensor kc, Tensor vc, Tensor table, Tensor seg_lan
   TORCH_CHECK(tiles.dim() == 2 && tiles.size(1) == 3 && tiles.scalar_type() == at::kInt, "attention_fa: tiles [n, 3]");
   const int T = q.size(0), nq = q.size(1), hd = q.size(2), nkv = kc.size(1);
   Tensor out = at::empty_like(q);
-  Tensor ws;
-  if (splits > 1) ws = at::empty({(long)T * nq * splits * (hd + 4)}, q.options().dtype(at::kFloat));
+  Scratch ws;
+  if (splits > 1) ws = scratch_empty((long)T * nq * splits * (hd + 4), q.options().dtype(at::kFloat), qb::BS_CANARY_ATTN_WS);
   LAUNCH(qb::fa_prefill(q.data_ptr(), kc.data_ptr(), vc.data_ptr(), kc.size(0), table.data_ptr<int>(), table.size(1),
                         pos.data_ptr<int>(), seg_lane.data_ptr<int>(), tiles.data_ptr<int>(), tiles.size(0), T, nq,
-                        nkv, hd, block_size, (int)splits, splits > 1 ? ws.data_ptr<float>() : nullptr,
+                        nkv, hd, block_size, (int)splits, splits > 1 ? ws.t.data_ptr<float>() : nullptr,
                         out.data_ptr(), err_ptr(q), stream()));
+  scratch_check(ws);
   if (splits > 1) g_launches.fetch_add(1, std::memory_order_relaxed);  // the combine kernel
   return out;
 }
@@ -244,7 +285,7 @@ Tensor causal_conv_varlen(Tensor x, Tensor state, Tensor w, Tensor seg_lane, Ten
   Tensor out = at::empty({T, C}, x.options());
   LAUNCH(qb::causal_conv_varlen_t(x.data_ptr(), x.stride(0), state.data_ptr(), state.stride(0), w.data_ptr(),
                                   seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), T, C, K,
-                                  out.data_ptr(), commit, stream()));
+                                  out.data_ptr(), commit, (int)state.size(0), stream()));
   g_launches.fetch_add(1, std::memory_order_relaxed);  // output + state kernels
   return out;
 }
@@ -256,11 +297,13 @@ Tensor gated_delta_varlen(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, T
   TORCH_CHECK(state.stride(3) == 1 && state.stride(2) == dv && state.stride(1) == dk * dv, "delta: state layout");
   const int T = qkv.size(0);
   Tensor out = at::empty({T, nv, dv}, qkv.options());
-  Tensor scratch = at::empty({(long)T * (2 * nk * dk + 4 * nv)}, qkv.options().dtype(at::kFloat));
+  Scratch scratch = scratch_empty((long)T * (2 * nk * dk + 4 * nv), qkv.options().dtype(at::kFloat),
+                                  qb::BS_CANARY_DN_SCRATCH);
   LAUNCH(qb::gated_delta_varlen_t(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0),
                                   a_log.data_ptr<float>(), dt_bias.data_ptr<float>(), state.data_ptr<float>(),
                                   state.stride(0), seg_lane.data_ptr<int>(), cu.data_ptr<int>(), seg_lane.size(0), T,
-                                  nk, nv, dk, dv, scratch.data_ptr<float>(), out.data_ptr(), commit, stream()));
+                                  nk, nv, dk, dv, scratch.t.data_ptr<float>(), out.data_ptr(), commit, stream()));
+  scratch_check(scratch);
   g_launches.fetch_add(1, std::memory_order_relaxed);  // prep + recurrence kernels
   return out;
 }
@@ -293,12 +336,14 @@ Tensor gated_delta_chunked(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, 
   TORCH_CHECK(chunks.dim() == 2 && chunks.size(1) == 3, "delta: chunks [n, 3]");
   const int T = qkv.size(0), n_chunks = chunks.size(0);
   Tensor out = at::empty({T, nv, dv}, qkv.options());
-  Tensor scratch = at::empty({qb::gated_delta_chunked_scratch(T, n_chunks, nk, nv, dk)}, qkv.options().dtype(at::kFloat));
+  Scratch scratch = scratch_empty(qb::gated_delta_chunked_scratch(T, n_chunks, nk, nv, dk),
+                                  qkv.options().dtype(at::kFloat), qb::BS_CANARY_DN_SCRATCH);
   LAUNCH(qb::gated_delta_chunked(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0), a_log.data_ptr<float>(),
                                  dt_bias.data_ptr<float>(), state.data_ptr<float>(), state.stride(0),
                                  seg_lane.data_ptr<int>(), chunks.data_ptr<int>(), n_chunks,
                                  seg_chunk0.data_ptr<int>(), seg_lane.size(0), T, nk, nv, dk, dv,
-                                 scratch.data_ptr<float>(), out.data_ptr(), commit, stream()));
+                                 scratch.t.data_ptr<float>(), out.data_ptr(), commit, stream()));
+  scratch_check(scratch);
   g_launches.fetch_add(2, std::memory_order_relaxed);  // prep + chunk prep + chunk state kernels
   return out;
 }
@@ -313,12 +358,14 @@ Tensor gated_delta_tc(Tensor qkv, Tensor ab, Tensor a_log, Tensor dt_bias, Tenso
   TORCH_CHECK(qkv.stride(1) == 1 && qkv.stride(0) % 8 == 0, "delta_tc: qkv rows 16-byte aligned");
   const int T = qkv.size(0), n_chunks = chunks.size(0);
   Tensor out = at::empty({T, nv, dv}, qkv.options());
-  Tensor scratch = at::empty({qb::gated_delta_tc_scratch(T, n_chunks, nk, nv)}, qkv.options().dtype(at::kFloat));
+  Scratch scratch = scratch_empty(qb::gated_delta_tc_scratch(T, n_chunks, nk, nv), qkv.options().dtype(at::kFloat),
+                                  qb::BS_CANARY_DN_SCRATCH);
   LAUNCH(qb::gated_delta_tc(qkv.data_ptr(), qkv.stride(0), ab.data_ptr(), ab.stride(0), a_log.data_ptr<float>(),
                             dt_bias.data_ptr<float>(), state.data_ptr<float>(), state.stride(0),
                             seg_lane.data_ptr<int>(), chunks.data_ptr<int>(), n_chunks, seg_chunk0.data_ptr<int>(),
-                            seg_lane.size(0), T, nk, nv, dk, dv, scratch.data_ptr<float>(), out.data_ptr(), commit,
+                            seg_lane.size(0), T, nk, nv, dk, dv, scratch.t.data_ptr<float>(), out.data_ptr(), commit,
                             err_ptr(qkv), stream()));
+  scratch_check(scratch);
   g_launches.fetch_add(2, std::memory_order_relaxed);  // glue prep + chunk prep + state kernels
   return out;
 }
@@ -387,8 +434,8 @@ void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s
   const int cap = T * k;
   auto i32 = h.options().dtype(at::kInt);
   if (T == 0) return;
-  Tensor meta = at::empty({2 * count + 3 * cap + 1 + count + 1}, i32);
-  int* counts = meta.data_ptr<int>();
+  Scratch meta = scratch_empty(2 * count + 3 * cap + 1 + count + 1, i32, qb::BS_CANARY_MOE_META);
+  int* counts = meta.t.data_ptr<int>();
   int* offsets = counts + count;
   int* perm_tok = offsets + count;
   int* perm_slot = perm_tok + cap;
@@ -405,11 +452,12 @@ void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s
   // hi plane then lo plane; scale chunks either hi then lo regions, or (merged) per chunk hi|lo
   const bool merged = qb::mx_merged(tiled, BN);
   const long plane = ((long)cap * KM + 127) / 128 * 128, sf_plane = tiles * (KM / 128) * 512;
-  Tensor hl = at::empty({2 * plane}, u8), sf = at::empty({2 * sf_plane}, u8);
+  Scratch hl = scratch_empty(2 * plane, u8, qb::BS_CANARY_MOE_SCRATCH);
+  Scratch sf = scratch_empty(2 * sf_plane, u8, qb::BS_CANARY_MOE_SCRATCH);
   Tensor inter = at::empty({cap, I}, h.options());
   Tensor y2 = at::empty({cap, H}, h.options());
-  uint8_t *hp = hl.data_ptr<uint8_t>(), *lp = hp + plane;
-  uint8_t *shp = sf.data_ptr<uint8_t>(), *slp = merged ? shp : shp + sf_plane;
+  uint8_t *hp = hl.t.data_ptr<uint8_t>(), *lp = hp + plane;
+  uint8_t *shp = sf.t.data_ptr<uint8_t>(), *slp = merged ? shp : shp + sf_plane;
   // each token quantised once, then expanded into its assignments' rows (k x fewer conversions)
   Tensor qs = at::empty({(long)T * (2 * H + H / 32)}, u8);
   LAUNCH(qb::mx_quant_expand(h.data_ptr(), T, perm_tok, n_assign, cap, H, offsets, tstart, count, BN,
@@ -423,6 +471,9 @@ void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s
                          counts, tstart, count, BN, 0, y2.data_ptr(), H, err_ptr(h), stream(), tiled));
   LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream(),
                          sparse_rows));
+  scratch_check(meta);
+  scratch_check(hl);
+  scratch_check(sf);
 }
 
 Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,

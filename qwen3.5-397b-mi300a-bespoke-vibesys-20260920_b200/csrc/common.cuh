@@ -27,6 +27,8 @@ enum ErrCode : int {
   ERR_EPI_WAIT = 4,
   ERR_PEER_WAIT = 5,
   ERR_DRAIN = 6,
+  ERR_BOUNDS = 7,  // debug build: an index read from memory was out of range (bounds.cuh)
+  ERR_CANARY = 8,  // debug build: a scratch buffer's trailing canary changed (bounds.cuh)
 };
 
 __device__ __forceinline__ uint64_t globaltimer() {

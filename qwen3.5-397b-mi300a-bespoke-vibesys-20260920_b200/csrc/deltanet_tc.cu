@@ -13,7 +13,8 @@
 //
 // dn_tc_prep (grid: chunk x key head, every chunk at once, CUDA cores in fp32): the two 64x64
 // Gram products once per key head, then for each value head sharing it the decays, the unit
-// lower-triangular inverse T by forward substitution (one column per four threads), U and W,
+// lower-triangular inverse T in 16 x 16 blocks (diagonal blocks by substitution from registers,
+// then three block rows of small products), U and W,
 // and a per-(chunk, value head) record in exactly the shared-memory image the
 // state kernel's MMAs read: U fp32, then W, Q e^G, Mq (bf16, K-major, 128-byte swizzle) and
 // K e^(G_last - G) (bf16, M-major), and e^(G_last).
@@ -63,7 +64,8 @@ constexpr int S_S = 132096;       // S as bf16 MN-major B operand: 2 N-atoms x [
 constexpr int S_D = 164864;       // Delta as bf16 MN-major B operand: 2 N-atoms x [64 K-rows][128 B]
 constexpr int S_BAR = 181248;
 constexpr int S_BYTES = S_BAR + 64 + 1024;
-constexpr int PREP_SMEM = (3 * C * KP + 4 * C * AP + 3 * C) * 4;
+constexpr int PP = 3 * 16 + 1;     // fp32 row pitch of the inverse's block-row partial products
+constexpr int PREP_SMEM = (3 * C * KP + 4 * C * AP + 3 * C + 16 * PP) * 4;
 constexpr int TM_S = 0, TM_D1 = 128, TM_D2 = 256;
 }  // namespace dntc
 
@@ -110,6 +112,7 @@ __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const 
   float* G = Tm + C * AP;
   float* Bt = G + C;
   float* EG = Bt + C;
+  float* Pb = EG + C;          // [16][PP] block-row partial products of the inverse
   const int c = blockIdx.x, hk = blockIdx.y, tid = threadIdx.x;
   const int row0 = chunks[c * 3 + 1], rows = chunks[c * 3 + 2];
   const int R = nv / nk;
@@ -150,7 +153,8 @@ __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const 
       for (int r = 0; r < 4; ++r) {
         kt[r] = *reinterpret_cast<const float4*>(Ks + (4 * ty + r) * KP + i);
         qt[r] = *reinterpret_cast<const float4*>(Qs + (4 * ty + r) * KP + i);
-        ks[r] = *reinterpret_cast<const float4*>(Ks + (4 * tx + r) * KP + i);
+        // key rows tx + 16 r: the 8 threads of a quarter warp read 8 distinct 4-bank groups
+        ks[r] = *reinterpret_cast<const float4*>(Ks + (tx + 16 * r) * KP + i);
       }
 #pragma unroll
       for (int r = 0; r < 4; ++r)
@@ -164,8 +168,8 @@ __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const 
     for (int r = 0; r < 4; ++r)
 #pragma unroll
       for (int s = 0; s < 4; ++s) {
-        Kg[(4 * ty + r) * AP + 4 * tx + s] = aa[r][s];
-        Qg[(4 * ty + r) * AP + 4 * tx + s] = mm[r][s];
+        Kg[(4 * ty + r) * AP + tx + 16 * s] = aa[r][s];
+        Qg[(4 * ty + r) * AP + tx + 16 * s] = mm[r][s];
       }
   }
   const int last = rows > 0 ? rows - 1 : 0;
@@ -234,19 +238,52 @@ __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const 
       *reinterpret_cast<uint2*>(rec + R_M + swz(t, u0 >> 3) + (u0 & 7) * 2) = w;
     }
     __syncthreads();
-    // ---- T = (I + A)^-1 by forward substitution: column cc by four threads (one warp = 8 columns)
+    // ---- T = (I + A)^-1 (A strictly lower triangular) in 16 x 16 blocks T_ij:
+    //   (1) diagonal blocks D_i = (I + A_ii)^-1 by forward substitution, one thread per (block,
+    //       column) holding its column in registers: no barrier inside, depth 15;
+    //   (2) block rows i = 1, 2, 3 in order: P_ij = sum_{k=j}^{i-1} A_ik T_kj, then T_ij = -D_i P_ij
+    //       (from (I + A) T = I restricted to block row i). Blocks above the diagonal are zero.
     {
-      const int cc = tid >> 2, part = tid & 3;
-      for (int t = part; t < C; t += 4) Tm[t * AP + cc] = t == cc ? 1.f : 0.f;
-      __syncwarp();
-      for (int t = 1; t < C; ++t) {
-        float sum = 0.f;
-        if (t > cc)
-          for (int s = cc + part; s < t; s += 4) sum += A[t * AP + s] * Tm[s * AP + cc];
-        sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-        sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-        if (t > cc && part == 0) Tm[t * AP + cc] = -sum;
-        __syncwarp();
+      if (tid < 64) {
+        const int o = (tid >> 4) * 16, cc = tid & 15;
+        float col[16];
+#pragma unroll
+        for (int t = 0; t < 16; ++t) {
+          float acc = t == cc ? 1.f : 0.f;
+#pragma unroll
+          for (int u = 0; u < t; ++u) acc -= A[(o + t) * AP + o + u] * col[u];
+          col[t] = t < cc ? 0.f : acc;
+        }
+#pragma unroll
+        for (int t = 0; t < 16; ++t) Tm[(o + t) * AP + o + cc] = col[t];
+      } else {
+        // the six blocks above the diagonal: (0,1..3), (1,2..3), (2,3)
+        for (int e = tid - 64; e < 6 * 256; e += 192) {
+          const int b = e >> 8, r = (e >> 4) & 15, q = e & 15;
+          const int bi = b < 3 ? 0 : (b < 5 ? 1 : 2);
+          const int bj = b < 3 ? b + 1 : (b < 5 ? b - 1 : 3);
+          Tm[(16 * bi + r) * AP + 16 * bj + q] = 0.f;
+        }
+      }
+      const int r = tid >> 4, q = tid & 15;
+      for (int bi = 1; bi < 4; ++bi) {
+        __syncthreads();  // block rows < bi of T (and the diagonal blocks) are complete
+        for (int bj = 0; bj < bi; ++bj) {
+          float acc = 0.f;
+          for (int k = bj; k < bi; ++k) {
+#pragma unroll
+            for (int u = 0; u < 16; ++u)
+              acc += A[(16 * bi + r) * AP + 16 * k + u] * Tm[(16 * k + u) * AP + 16 * bj + q];
+          }
+          Pb[r * PP + 16 * bj + q] = acc;
+        }
+        __syncthreads();
+        for (int bj = 0; bj < bi; ++bj) {
+          float acc = 0.f;
+#pragma unroll
+          for (int u = 0; u < 16; ++u) acc += Tm[(16 * bi + r) * AP + 16 * bi + u] * Pb[u * PP + 16 * bj + q];
+          Tm[(16 * bi + r) * AP + 16 * bj + q] = -acc;
+        }
       }
     }
     __syncthreads();

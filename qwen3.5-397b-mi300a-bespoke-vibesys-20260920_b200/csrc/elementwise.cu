@@ -3,6 +3,7 @@
 // rounding points of the HuggingFace modeling code (an op whose PyTorch statement produces a
 // bf16 tensor rounds to bf16 at the same place here), so greedy decoding agrees with it.
 #include "common.cuh"
+#include "bounds.cuh"
 #include "kernels.h"
 
 namespace qb {
@@ -157,18 +158,19 @@ int silu_mul(const void* gu, long ldg, void* out, long ldo, int T, int n, cudaSt
   return (int)cudaGetLastError();
 }
 
-__global__ void embed_kernel(const int64_t* tok, const bf16* table, bf16* out, int H) {
+__global__ void embed_kernel(const int64_t* tok, const bf16* table, bf16* out, int H, long V) {
   const long t = blockIdx.x;
   const int64_t id = tok[t];
+  if (!bounds_ok(BS_EMBED_TOKEN, id, V)) return;
   const uint4* src = reinterpret_cast<const uint4*>(table + id * H);
   uint4* dst = reinterpret_cast<uint4*>(out + t * H);
   for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
 }
 
-int embed(const int64_t* tok, const void* table, void* out, int T, int H, cudaStream_t s) {
+int embed(const int64_t* tok, const void* table, void* out, int T, int H, long V, cudaStream_t s) {
   if (!T) return 0;
   if (H % 8) return -1;
-  embed_kernel<<<T, 128, 0, s>>>(tok, (const bf16*)table, (bf16*)out, H);
+  embed_kernel<<<T, 128, 0, s>>>(tok, (const bf16*)table, (bf16*)out, H, V);
   return (int)cudaGetLastError();
 }
 
@@ -267,7 +269,7 @@ int shared_gate_combine(const void* routed, const void* shared, const void* gl, 
 // k heads and the v heads are written to the paged cache at physical row rows[t].
 __global__ void qk_norm_rope_kernel(const bf16* qkv, long ldqkv, int nq, int nkv, int hd, const float* qn,
                                     const float* kn, const int* pos, const int* rows, bf16* kc, bf16* vc, bf16* qout,
-                                    int rot, float theta, float eps) {
+                                    int rot, float theta, float eps, long kv_rows) {
   extern __shared__ float sh[];  // [warps][hd] normalised head + [rot/2] cos + [rot/2] sin
   const int t = blockIdx.x;
   const int warps = blockDim.x / 32, w = threadIdx.x / 32, lane = threadIdx.x % 32;
@@ -284,6 +286,7 @@ __global__ void qk_norm_rope_kernel(const bf16* qkv, long ldqkv, int nq, int nkv
   __syncthreads();
   const bf16* row = qkv + (long)t * ldqkv;
   const long prow = rows[t];
+  const bool kv_ok = bounds_ok(BS_KV_ROW, prow, kv_rows);  // debug build: a bad row skips the KV write
   float* buf = sh + w * hd;
   for (int hh = w; hh < nq + nkv; hh += warps) {
     const bool isq = hh < nq;
@@ -299,6 +302,7 @@ __global__ void qk_norm_rope_kernel(const bf16* qkv, long ldqkv, int nq, int nkv
     const float inv = rsqrtf(ss / hd + eps);
     for (int i = lane; i < hd; i += 32) buf[i] = rbf(buf[i] * inv * wt[i]);
     __syncwarp();
+    if (!isq && !kv_ok) continue;
     bf16* dst = isq ? qout + ((long)t * nq + hh) * hd : kc + (prow * nkv + (hh - nq)) * hd;
     for (int i = lane; i < hd; i += 32) {
       float o;
@@ -316,17 +320,18 @@ __global__ void qk_norm_rope_kernel(const bf16* qkv, long ldqkv, int nq, int nkv
   // values: plain copy into the paged cache
   const bf16* vsrc = row + (long)nq * 2 * hd + (long)nkv * hd;
   bf16* vdst = vc + prow * nkv * hd;
-  for (int i = threadIdx.x; i < nkv * hd; i += blockDim.x) vdst[i] = vsrc[i];
+  if (kv_ok)
+    for (int i = threadIdx.x; i < nkv * hd; i += blockDim.x) vdst[i] = vsrc[i];
 }
 
 int qk_norm_rope_kv_write(const void* qkv, long ldqkv, int nq, int nkv, int hd, const float* qn, const float* kn,
                           const int* pos, const int* rows, void* kc, void* vc, void* qout, int T, int rot,
-                          float theta, float eps, cudaStream_t s) {
+                          float theta, float eps, long kv_rows, cudaStream_t s) {
   if (!T) return 0;
   const int threads = 256, warps = threads / 32;
   const size_t smem = (size_t)(warps * hd + rot) * sizeof(float);
   qk_norm_rope_kernel<<<T, threads, smem, s>>>((const bf16*)qkv, ldqkv, nq, nkv, hd, qn, kn, pos, rows, (bf16*)kc,
-                                               (bf16*)vc, (bf16*)qout, rot, theta, eps);
+                                               (bf16*)vc, (bf16*)qout, rot, theta, eps, kv_rows);
   return (int)cudaGetLastError();
 }
 
@@ -410,6 +415,32 @@ __global__ void stamp_kernel(unsigned long long* buf, int slot) { buf[slot] = gl
 int stamp(unsigned long long* buf, int slot, cudaStream_t s) {
   stamp_kernel<<<1, 1, 0, s>>>(buf, slot);
   return (int)cudaGetLastError();
+}
+
+// ------------------------------------------------------------------ debug build: canaries
+__global__ void canary_check_kernel(const unsigned char* tail, int site) {
+  for (int i = threadIdx.x; i < CANARY_BYTES; i += blockDim.x)
+    if (tail[i] != CANARY_BYTE) {
+#ifdef QB_BOUNDS
+      bounds_record(ERR_CANARY, site, i, CANARY_BYTES);
+#endif
+      return;
+    }
+}
+
+int canary_check(const void* tail, int site, cudaStream_t s) {
+  canary_check_kernel<<<1, 128, 0, s>>>((const unsigned char*)tail, site);
+  return (int)cudaGetLastError();
+}
+
+QB_BOUNDS_INSTALL(bounds_install_elementwise)
+
+bool bounds_build() {
+#ifdef QB_BOUNDS
+  return true;
+#else
+  return false;
+#endif
 }
 
 }  // namespace qb

@@ -39,16 +39,36 @@ int add_rmsnorm(const void* x, long ldx, void* res, long ldr, const float* w1p, 
 int gated_rmsnorm(const void* core, const void* z, long ldz_row, const void* w, void* out, int T, int heads, int dv,
                   float eps, cudaStream_t s);
 int silu_mul(const void* gu, long ldg, void* out, long ldo, int T, int n, cudaStream_t s);
-int embed(const int64_t* tok, const void* table, void* out, int T, int H, cudaStream_t s);
+int embed(const int64_t* tok, const void* table, void* out, int T, int H, long V, cudaStream_t s);
 int argmax_rows(const void* x, long ldx, int dtype, int R, int V, float* val, int64_t* idx, cudaStream_t s);
 int sigmoid_gate_mul(const void* x, long ldx, const void* g, long ldg, void* out, int T, int D, cudaStream_t s);
 int shared_gate_combine(const void* routed, const void* shared, const void* gl, long ldgl, void* out, int T, int H,
                         cudaStream_t s);
 int qk_norm_rope_kv_write(const void* qkv, long ldqkv, int nq, int nkv, int hd, const float* qn, const float* kn,
                           const int* pos, const int* rows, void* kc, void* vc, void* qout, int T, int rot,
-                          float theta, float eps, cudaStream_t s);
+                          float theta, float eps, long kv_rows, cudaStream_t s);
 int causal_conv_varlen_t(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
-                         const int* cu, int S, int T, int C, int K, void* out, bool commit, cudaStream_t s);
+                         const int* cu, int S, int T, int C, int K, void* out, bool commit, int lanes,
+                         cudaStream_t s);
+// debug build (-DQB_BOUNDS, bounds.cuh): check sites recorded in the status word, the scratch
+// canary, the status-word pointer installs (one per translation unit with checks; no-ops in the
+// release build) and the canary check
+enum BoundsSite : int {
+  BS_EMBED_TOKEN = 1,
+  BS_KV_ROW = 2,
+  BS_LANE = 4,
+  BS_CANARY_GEMM_WS = 11,
+  BS_CANARY_ATTN_WS = 12,
+  BS_CANARY_DN_SCRATCH = 13,
+  BS_CANARY_MOE_META = 14,
+  BS_CANARY_MOE_SCRATCH = 15,
+};
+constexpr int CANARY_BYTES = 256;
+constexpr unsigned char CANARY_BYTE = 0xA5;
+bool bounds_build();
+int bounds_install_elementwise(int* word);
+int bounds_install_sequence(int* word);
+int canary_check(const void* tail, int site, cudaStream_t s);
 int gated_delta_varlen_t(const void* qkv, long ldqkv, const void* ab, long ldab, const float* a_log,
                          const float* dt_bias, float* state, long lane_stride, const int* seg_lane, const int* cu,
                          int S, int T, int nk, int nv, int dk, int dv, float* scratch, void* out, bool commit,

@@ -5,6 +5,7 @@
 //   attention_varlen     causal GQA attention over the paged KV cache, split-K (flash-decoding)
 // Rounding follows the HuggingFace modeling code (see elementwise.cu).
 #include "common.cuh"
+#include "bounds.cuh"
 #include "kernels.h"
 
 namespace qb {
@@ -27,12 +28,13 @@ __device__ __forceinline__ int seg_of(const int* cu, int S, int t) {
 // the last K-1 inputs of the segment (old window entries when the segment is shorter).
 template <int K>
 __global__ void conv_out_kernel(const bf16* x, long ldx, const bf16* state, long lane_stride, const bf16* w,
-                                const int* seg_lane, const int* cu, int S, int C, bf16* out) {
+                                const int* seg_lane, const int* cu, int S, int C, bf16* out, int lanes) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int t = blockIdx.y;
   if (c >= C || t >= cu[S]) return;  // rows past the last segment: padding of a fixed-size batch
   const int s = seg_of(cu, S, t);
   const int t0 = cu[s];
+  if (!bounds_ok(BS_LANE, seg_lane[s], lanes)) return;
   const bf16* st = state + (long)seg_lane[s] * lane_stride + (long)c * (K - 1);
   float acc = 0.f;
 #pragma unroll
@@ -47,10 +49,11 @@ __global__ void conv_out_kernel(const bf16* x, long ldx, const bf16* state, long
 
 template <int K>
 __global__ void conv_state_kernel(const bf16* x, long ldx, bf16* state, long lane_stride, const int* seg_lane,
-                                  const int* cu, int C) {
+                                  const int* cu, int C, int lanes) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
   const int s = blockIdx.y;
   if (c >= C) return;
+  if (!bounds_ok(BS_LANE, seg_lane[s], lanes)) return;
   const int t0 = cu[s], len = cu[s + 1] - cu[s];
   bf16* st = state + (long)seg_lane[s] * lane_stride + (long)c * (K - 1);
 #pragma unroll
@@ -61,14 +64,15 @@ __global__ void conv_state_kernel(const bf16* x, long ldx, bf16* state, long lan
 }
 
 int causal_conv_varlen_t(const void* x, long ldx, void* state, long lane_stride, const void* w, const int* seg_lane,
-                         const int* cu, int S, int T, int C, int K, void* out, bool commit, cudaStream_t s) {
+                         const int* cu, int S, int T, int C, int K, void* out, bool commit, int lanes,
+                         cudaStream_t s) {
   if (!S || !T) return 0;
   if (K != 4) return -1;
   conv_out_kernel<4><<<dim3((C + 127) / 128, T), 128, 0, s>>>((const bf16*)x, ldx, (const bf16*)state, lane_stride,
-                                                               (const bf16*)w, seg_lane, cu, S, C, (bf16*)out);
+                                                               (const bf16*)w, seg_lane, cu, S, C, (bf16*)out, lanes);
   if (commit)
     conv_state_kernel<4><<<dim3((C + 127) / 128, S), 128, 0, s>>>((const bf16*)x, ldx, (bf16*)state, lane_stride,
-                                                                   seg_lane, cu, C);
+                                                                   seg_lane, cu, C, lanes);
   return (int)cudaGetLastError();
 }
 
@@ -817,6 +821,10 @@ int attention_varlen(const void* q, const void* kc, const void* vc, const int* t
   return (int)cudaGetLastError();
 }
 
+}  // namespace qb
+
+namespace qb {
+QB_BOUNDS_INSTALL(bounds_install_sequence)
 }  // namespace qb
 
 // ------------------------------------------------------------------ allocation-free entry point

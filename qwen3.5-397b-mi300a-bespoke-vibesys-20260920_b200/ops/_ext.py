@@ -17,6 +17,7 @@ import torch
 
 _PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 BUILD_DIR = os.path.join(_PKG, "_build")
+BOUNDS_BUILD_DIR = os.path.join(_PKG, "_build_bounds")  # debug build (-DQB_BOUNDS), loaded when QB_BOUNDS=1
 MODULE_NAME = "qwen35_b200_C"
 
 _lock = threading.Lock()
@@ -24,7 +25,10 @@ _mod = None
 
 
 def so_path() -> str | None:
-    hits = sorted(glob.glob(os.path.join(BUILD_DIR, MODULE_NAME + "*.so")))
+    from ..utils import flags
+
+    d = BOUNDS_BUILD_DIR if flags.get("QB_BOUNDS") else BUILD_DIR
+    hits = sorted(glob.glob(os.path.join(d, MODULE_NAME + "*.so")))
     return hits[0] if hits else None
 
 

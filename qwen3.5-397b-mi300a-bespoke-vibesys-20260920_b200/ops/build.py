@@ -10,7 +10,7 @@ from __future__ import annotations
 import glob
 import os
 
-from ._ext import BUILD_DIR, MODULE_NAME
+from ._ext import BOUNDS_BUILD_DIR, BUILD_DIR, MODULE_NAME
 
 PKG = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 CSRC = os.path.join(PKG, "csrc")
@@ -27,19 +27,33 @@ def sources() -> list[str]:
     return sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + sorted(glob.glob(os.path.join(CSRC, "*.cpp")))
 
 
-def build(verbose: bool = False):
+def build(verbose: bool = False, bounds: bool = False):
+    """The release extension, or with ``bounds=True`` the debug build (``-DQB_BOUNDS``: index checks
+    and scratch canaries that record into the device status word, ``csrc/bounds.cuh``) in
+    ``_build_bounds/``, which ``ops._ext`` loads instead when ``QB_BOUNDS=1``."""
     import torch.utils.cpp_extension as ce
 
-    os.makedirs(BUILD_DIR, exist_ok=True)
+    build_dir = BOUNDS_BUILD_DIR if bounds else BUILD_DIR
+    os.makedirs(build_dir, exist_ok=True)
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
     os.environ.setdefault("MAX_JOBS", str(min(8, os.cpu_count() or 4)))
     return ce.load(
         name=MODULE_NAME,
         sources=sources(),
-        extra_cflags=["-O3", "-std=c++17"],
-        extra_cuda_cflags=CUDA_FLAGS,
+        extra_cflags=["-O3", "-std=c++17"] + (["-DQB_BOUNDS"] if bounds else []),
+        extra_cuda_cflags=CUDA_FLAGS + (["-DQB_BOUNDS"] if bounds else []),
         extra_include_paths=[CSRC],
-        build_directory=BUILD_DIR,
+        build_directory=build_dir,
         verbose=verbose,
         with_cuda=True,
     )
+
+
+if __name__ == "__main__":
+    import argparse
+
+    ap = argparse.ArgumentParser(description="build the sm_100a extension in-tree")
+    ap.add_argument("--bounds", action="store_true", help="the debug build with bounds checks and canaries")
+    ap.add_argument("--verbose", action="store_true")
+    a = ap.parse_args()
+    build(verbose=a.verbose, bounds=a.bounds)

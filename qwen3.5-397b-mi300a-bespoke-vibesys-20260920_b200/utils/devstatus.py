@@ -15,7 +15,11 @@ collective's spin bound ran out); here one word covers every kernel family.
 from __future__ import annotations
 
 ERR_NAMES = {1: "tma_wait", 2: "mma_wait", 3: "accumulator_wait", 4: "epilogue_wait", 5: "peer_wait",
-             6: "drain"}
+             6: "drain", 7: "bounds", 8: "canary"}
+# debug build (QB_BOUNDS): words 1..3 of the status hold the failing check's site, value and capacity
+BOUNDS_SITES = {1: "embed token id", 2: "paged KV row", 4: "DeltaNet lane", 11: "GEMM stream-K workspace",
+                12: "attention split workspace", 13: "DeltaNet scratch", 14: "MoE dispatch metadata",
+                15: "MoE activation planes"}
 
 
 class DeviceStatusError(RuntimeError):

@@ -38,6 +38,8 @@ def _def(name, kind, default, doc, lockstep=False, native=False) -> None:
 
 
 # ---- kernels and numerics
+_def("QB_BOUNDS", bool, False, "load the debug build of the extension (_build_bounds: index checks and scratch "
+     "canaries recorded in the device status word; build it with python -m qwen35_b200.ops.build --bounds)")
 _def("QB_MOE_IMPL", str, "mx", "routed-expert kernel: mx (block-scaled fp8 tcgen05), f16 (fp4 decoded to "
      "f16 in TMEM), bf16 (dequantised weights)", lockstep=True)
 _def("QB_MX_BN_MAX", int, 64, "largest token tile of the block-scaled MoE kernel", native=True)
