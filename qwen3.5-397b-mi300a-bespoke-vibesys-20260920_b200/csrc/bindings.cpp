@@ -575,7 +575,8 @@ void symm_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor partia
 }
 
 void symm_sp_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor partial, Tensor res, Tensor w1p, Tensor out,
-                         double eps, int64_t slot_elems, int64_t max_blocks, Tensor epoch, double timeout_s) {
+                         double eps, int64_t slot_elems, int64_t max_blocks, Tensor epoch, double timeout_s,
+                         bool own) {
   CHECK_BF16(partial);
   CHECK_BF16(res);
   TORCH_CHECK(res.is_contiguous() && out.is_contiguous() && partial.stride(-1) == 1, "symm_sp_ar: layouts");
@@ -587,7 +588,39 @@ void symm_sp_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor par
   LAUNCH(qb::symm_sp_ar_add_rmsnorm(b.data(), (int)b.size(), (int)rank, partial.data_ptr(), partial.stride(0),
                                  res.data_ptr(), w1p.data_ptr<float>(), out.data_ptr(), rows, H, (float)eps,
                                  slot_elems, (int)max_blocks, ep, ep + 1, err_ptr(res),
-                                 (unsigned long long)(timeout_s * 1e9), stream()));
+                                 (unsigned long long)(timeout_s * 1e9), stream(), own));
+}
+
+// All-gather -> GEMM after the owner-only sequence-parallel call (own=true above): y[rows, N] =
+// gathered normed rows @ w^T, each owner's rows pulled by TMA from its result area (comm.cu).
+Tensor symm_gemm_ag(std::vector<int64_t> bases, int64_t rank, Tensor w, int64_t rows, int64_t hidden,
+                    int64_t slot_elems, int64_t max_blocks, Tensor epoch, double timeout_s) {
+  CHECK_BF16(w);
+  TORCH_CHECK(w.dim() == 2 && w.size(1) == hidden && w.stride(1) == 1 && (w.stride(0) * 2) % 16 == 0,
+              "symm_gemm_ag: w [N, hidden] with 16-byte rows");
+  const int world = (int)bases.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world, "symm_gemm_ag: 1..8 ranks");
+  const int per = (int)((rows + world - 1) / world);
+  TORCH_CHECK((long)per * world * hidden <= slot_elems, "symm_gemm_ag: rows exceed the region");
+  const long slot_stride = 3 * slot_elems;                  // elements per slot
+  const long flags_base = 2 * slot_stride * 2;              // bytes
+  const long ready_off = flags_base + 4L * max_blocks * 4;  // the owner-only call's ready word
+  std::vector<const void*> src(world);
+  qb::GemmGather g{};
+  for (int o = 0; o < world; ++o) {
+    char* base = reinterpret_cast<char*>(bases[o]);
+    src[o] = base + (slot_elems + hidden) * 2;  // slot 0 result area, normed half of each row
+    g.ready[o] = reinterpret_cast<const int*>(base + ready_off);
+  }
+  g.epoch = epoch.data_ptr<int>();
+  g.world = world;
+  g.rank = (int)rank;
+  g.per = per;
+  g.timeout_ns = (unsigned long long)(timeout_s * 1e9);
+  Tensor y = at::empty({rows, w.size(0)}, w.options());
+  LAUNCH(qb::gemm_ag(src.data(), 2 * hidden, slot_stride, w.data_ptr(), w.stride(0), y.data_ptr(), y.stride(0),
+                     (int)rows, (int)w.size(0), (int)hidden, g, err_ptr(w), stream()));
+  return y;
 }
 
 // NVLS all-reduce + residual add + RMSNorm: `uc`/`mc` are this rank's unicast and multicast
@@ -698,7 +731,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
   m.def("symm_ar_add_rmsnorm", &symm_ar_add_rmsnorm);
-  m.def("symm_sp_ar_add_rmsnorm", &symm_sp_ar_add_rmsnorm);
+  m.def("symm_sp_ar_add_rmsnorm", &symm_sp_ar_add_rmsnorm, py::arg("bases"), py::arg("rank"), py::arg("partial"),
+        py::arg("res"), py::arg("w1p"), py::arg("out"), py::arg("eps"), py::arg("slot_elems"), py::arg("max_blocks"),
+        py::arg("epoch"), py::arg("timeout_s"), py::arg("own") = false);
+  m.def("symm_gemm_ag", &symm_gemm_ag);
   m.def("symm_linear_sp_ar_add_rmsnorm", &symm_linear_sp_ar_add_rmsnorm);
   m.def("nvls_ar_add_rmsnorm", &nvls_ar_add_rmsnorm);
   m.def("nvls_region_bytes", &nvls_region_bytes);

@@ -180,6 +180,15 @@ __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
 // PUSHED: the projection GEMM before this kernel already stored its rows into the owners' slots
 // (gemm.cu, GemmPush), so phase A only publishes (the GEMM's stores completed with that kernel).
 // Either way phase B reads local memory only.
+// OWN (all-gather left to the next GEMM): phase B writes the new residual and normed rows of this
+// rank's range to the local tensors only, and the normed rows also into this rank's own result
+// area; there is no phase C. The last block to finish raises this rank's ready word to e (after
+// every block's system-scope fence), and the next projection's GEMM (gemm.cu, gemm_ag) pulls each
+// owner's normed rows from that owner's result area once its ready word reaches e. The rows of
+// `res` outside this rank's range keep stale values: the next sequence-parallel call reads and
+// writes only this rank's range of them. Slot reuse is as above: the result area of slot s is
+// written again at call e + 2 only after every peer's flag A of e + 2, which each peer raised
+// after its gathering GEMM of call e had ended (stream order).
 __device__ __forceinline__ bool wait_peers(const SymmPtrs& ptrs, long flag_off, int b, int e, int* err,
                                            unsigned long long timeout_ns) {
   int ok = 1;
@@ -197,7 +206,7 @@ __device__ __forceinline__ bool wait_peers(const SymmPtrs& ptrs, long flag_off, 
   return __syncthreads_and(ok);
 }
 
-template <bool PUSHED>
+template <bool PUSHED, bool OWN>
 __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
     SymmPtrs ptrs, const bf16* partial, long ldp, bf16* res, const float* w1p, bf16* out, int rows, int H,
     float eps, long slot_elems, int max_blocks, int* epoch, int* done, int* err, unsigned long long timeout_ns,
@@ -277,9 +286,11 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
             ss += acc[c * 8 + u] * acc[c * 8 + u];
           }
           *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr;
+          if (!OWN) {
 #pragma unroll
-          for (int p = 0; p < 8; ++p)
-            if (p < W && p != me) *reinterpret_cast<uint4*>(peer_res[p] + (long)row * 2 * H + i) = nr;
+            for (int p = 0; p < 8; ++p)
+              if (p < W && p != me) *reinterpret_cast<uint4*>(peer_res[p] + (long)row * 2 * H + i) = nr;
+          }
         }
       }
       ss = warp_sum(ss);
@@ -302,15 +313,19 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
 #pragma unroll
           for (int u = 0; u < 8; ++u) ov[u] = __float2bfloat16(acc[c * 8 + u] * inv * w1p[i + u]);
           *reinterpret_cast<uint4*>(out + (long)row * H + i) = o;
+          if (OWN) {
+            *reinterpret_cast<uint4*>(peer_res[me] + (long)row * 2 * H + H + i) = o;
+          } else {
 #pragma unroll
-          for (int p = 0; p < 8; ++p)
-            if (p < W && p != me) *reinterpret_cast<uint4*>(peer_res[p] + (long)row * 2 * H + H + i) = o;
+            for (int p = 0; p < 8; ++p)
+              if (p < W && p != me) *reinterpret_cast<uint4*>(peer_res[p] + (long)row * 2 * H + H + i) = o;
+          }
         }
       }
     }
-    publish(flagB);
+    if (!OWN) publish(flagB);
     // C. the peers' result rows of this block's units, stored into this rank's result area
-    if (wait_peers(ptrs, flagB, b, e, err, timeout_ns)) {
+    if (!OWN && wait_peers(ptrs, flagB, b, e, err, timeout_ns)) {
       const bf16* pr = result_of(me);
       for (int p = 0; p < W; ++p) {
         if (p == me) continue;
@@ -341,11 +356,16 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
   // the last block to finish advances the epoch (every block already read it at entry)
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
+    if (OWN)
+      __threadfence_system();  // this block's result rows before the ready word (below)
+    else
+      __threadfence();
     const int d = atomicAdd(done, 1);
     if (d == (int)gridDim.x - 1) {
       *done = 0;
-      __threadfence();
+      __threadfence_system();
+      if (OWN) st_release_sys(reinterpret_cast<int*>(reinterpret_cast<char*>(ptrs.data[me]) + flags_base +
+                                                     4L * max_blocks * 4), e);
       atomicExch(epoch, e);
     }
   }
@@ -353,7 +373,7 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
 
 int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                            const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
-                           int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s) {
+                           int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s, bool own) {
   const int per = (rows + world - 1) / world;  // rows of one rank's range: one block per row, up to max_blocks
   if (world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || (long)per * world * H > slot_elems) return -1;
   SymmPtrs p{};
@@ -362,9 +382,14 @@ int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* 
   p.rank = rank;
   int grid = per < max_blocks ? per : max_blocks;
   if (grid < 1) grid = 1;
-  sp_ar_add_rmsnorm_kernel<false><<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res, w1p,
-                                                              (bf16*)out, rows, H, eps, slot_elems, max_blocks,
-                                                              epoch, done, err, timeout_ns, per);
+  if (own)
+    sp_ar_add_rmsnorm_kernel<false, true><<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res, w1p,
+                                                                     (bf16*)out, rows, H, eps, slot_elems, max_blocks,
+                                                                     epoch, done, err, timeout_ns, per);
+  else
+    sp_ar_add_rmsnorm_kernel<false, false><<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res,
+                                                                      w1p, (bf16*)out, rows, H, eps, slot_elems,
+                                                                      max_blocks, epoch, done, err, timeout_ns, per);
   return (int)cudaGetLastError();
 }
 
@@ -380,7 +405,7 @@ int symm_sp_rs_add_rmsnorm(void* const* bases, int world, int rank, int per, voi
   p.rank = rank;
   int grid = per < max_blocks ? per : max_blocks;
   if (grid < 1) grid = 1;
-  sp_ar_add_rmsnorm_kernel<true><<<grid, AR_THREADS, 0, s>>>(p, nullptr, 0, (bf16*)res, w1p, (bf16*)out, rows, H,
+  sp_ar_add_rmsnorm_kernel<true, false><<<grid, AR_THREADS, 0, s>>>(p, nullptr, 0, (bf16*)res, w1p, (bf16*)out, rows, H,
                                                              eps, slot_elems, max_blocks, epoch, done, err,
                                                              timeout_ns, per);
   return (int)cudaGetLastError();

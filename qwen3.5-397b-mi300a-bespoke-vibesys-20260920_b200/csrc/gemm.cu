@@ -36,6 +36,12 @@
 namespace qb {
 
 constexpr int GEMM_THREADS = 192;
+
+__device__ __forceinline__ int ld_acquire_sys_g(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
 constexpr int BK = 64;  // K elements per stage (one 128-byte swizzle atom of 16-bit values)
 
 template <int BN>
@@ -63,6 +69,30 @@ struct GemmArgs {
   float* ws;   // stream-K: [ctas][2][128][BN] fp32 partials (a CTA's first and last segment)
   int* cnt;    // stream-K: [tiles] arrival counters, zero between calls
   GemmPush push;  // push.world > 0: rows go to the owner ranks' slots instead of y
+  GemmGather gather;  // the all-gather -> GEMM kernel only: owners of the token rows
+};
+
+// Token tile `tt` -> its rows [t0, tend). Plain GEMM: tiles of bn rows over [0, T). All-gather
+// GEMM: ceil(per / bn) tiles per owner, so no tile spans two owners; a tile of an owner with fewer
+// rows may be empty (tend <= t0: computed from whatever the area holds, never stored).
+struct TokTiles {
+  int bn, T, per, tpo;
+  bool g;
+  __device__ TokTiles(const GemmArgs& a, bool gather) : bn(a.bn), T(a.T), per(a.gather.per), g(gather) {
+    tpo = g ? (per + bn - 1) / bn : 0;
+  }
+  __device__ int count(int world) const { return g ? world * tpo : (T + bn - 1) / bn; }
+  __device__ void rows(int tt, int& t0, int& tend, int& owner) const {
+    if (!g) {
+      owner = -1;
+      t0 = tt * bn;
+      tend = min(T, t0 + bn);
+      return;
+    }
+    owner = tt / tpo;
+    t0 = owner * per + (tt % tpo) * bn;
+    tend = min(min(T, (owner + 1) * per), t0 + bn);
+  }
 };
 
 // The sequence of (tile, K-block range) segments one CTA works through, identical for its
@@ -101,10 +131,13 @@ struct SegIter {
 // Stream-K: the CTA whose share contains position p of the (tile, K-block) space of size W.
 __device__ __forceinline__ int sk_owner(long p, long W, int ctas) { return (int)(((p + 1) * ctas - 1) / W); }
 
-template <int BN, typename OutT>
-__global__ void __launch_bounds__(GEMM_THREADS, 1)
-    gemm_ws_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GemmArgs a,
-                   uint32_t idesc) {
+struct GatherMaps {
+  CUtensorMap m[8];  // owner o's gather area: 3-D [slot][row][K] boxes of BK x bn x 1
+};
+
+template <int BN, typename OutT, bool G>
+__device__ __forceinline__ void gemm_ws_body(const CUtensorMap* tmW, const CUtensorMap* tmX, const CUtensorMap* gmaps,
+                                             const GemmArgs& a, uint32_t idesc) {
   using C = GemmCfg<BN>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -123,7 +156,8 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 
   const int warp = threadIdx.x / 32, lane = threadIdx.x % 32;
   const int n_tiles = (a.N + 127) / 128;
-  const int t_tiles = (a.T + a.bn - 1) / a.bn;
+  const TokTiles tokt(a, G);
+  const int t_tiles = tokt.count(a.gather.world);
   const int tiles = n_tiles * t_tiles;
   const int kblocks = (a.K + BK - 1) / BK;
 
@@ -141,8 +175,12 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     *issued_p = 0;
     *consumed_p = 0;
     fence_barrier_init();
-    prefetch_tmap(&tmW);
-    prefetch_tmap(&tmX);
+    prefetch_tmap(tmW);
+    if constexpr (G) {
+      for (int o = 0; o < a.gather.world; ++o) prefetch_tmap(gmaps + o);
+    } else {
+      prefetch_tmap(tmX);
+    }
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, C::TMEM_COLS);
@@ -163,8 +201,35 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       const uint32_t st0 = smem_u32(stages), full0 = smem_u32(full), empty0 = smem_u32(empty);
       int s = 0;
       uint32_t ph = 1;  // a first-round stage waits on the parity that passes at once
+      int e_src = 0, ready_mask = 0;
+      if constexpr (G) {
+        e_src = *reinterpret_cast<volatile const int*>(a.gather.epoch);
+        ready_mask = 1 << a.gather.rank;  // own rows: written by the previous kernel on this stream
+      }
       while (!*abort_flag && sg.next(tile, k0, k1)) {
-        const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * a.bn;
+        const int n0 = (tile / t_tiles) * 128;
+        int t0, tend, owner;
+        tokt.rows(tile % t_tiles, t0, tend, owner);
+        if constexpr (G) {
+          if (!((ready_mask >> owner) & 1)) {
+            // owner's rows for this call are complete once its ready word reaches the epoch
+            // (system-scope acquire); then order the async-proxy (TMA) reads after it
+            const int* f = a.gather.ready[owner];
+            const uint64_t w0 = globaltimer();
+            bool got = true;
+            while (ld_acquire_sys_g(f) < e_src) {
+              if (globaltimer() - w0 > a.gather.timeout_ns) {
+                atomicCAS(a.err, 0, ERR_PEER_WAIT);
+                *abort_flag = 1;
+                got = false;
+                break;
+              }
+            }
+            if (!got) break;
+            asm volatile("fence.proxy.async.global;" ::: "memory");
+            ready_mask |= 1 << owner;
+          }
+        }
         bool ok = true;
         for (int kx = k0 * BK; kx < k1 * BK; kx += BK, ++it) {
           if (!mbar_wait_s(empty0 + 8 * s, ph, a.err, ERR_TMA_WAIT, abort_flag)) {
@@ -173,8 +238,11 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           }
           const uint32_t st = st0 + s * C::STAGE, fb = full0 + 8 * s;
           mbar_expect_tx_s(fb, C::A_BYTES + a.bn * BK * 2);
-          tma_load_2d_s(st, &tmW, fb, kx, n0);
-          tma_load_2d_s(st + C::A_BYTES, &tmX, fb, kx, t0);
+          tma_load_2d_s(st, tmW, fb, kx, n0);
+          if constexpr (G)
+            tma_load_3d_s(st + C::A_BYTES, gmaps + owner, fb, kx, t0, e_src & 1);
+          else
+            tma_load_2d_s(st + C::A_BYTES, tmX, fb, kx, t0);
           *issued_p = it + 1;
           if (++s == C::STAGES) {
             s = 0;
@@ -239,7 +307,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
                                      a.push.slot_stride : 0;
     constexpr int CH = BN < 32 ? BN : 32;
     // stage one chunk of CH token columns (fp32 values of this thread's weight row) and store it
-    auto emit = [&](int n0, int t0, int c0, const float* v) {
+    auto emit = [&](int n0, int t0, int tend, int c0, const float* v) {
 #pragma unroll
       for (int j = 0; j < CH; ++j) {  // staging[j][row]: token column j, weight row `row`
         OutT o = from_f<OutT>(v[j]);
@@ -252,7 +320,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int idx = et; idx < CH * 64; idx += 128) {
           const int j = idx / 64, r = idx % 64;
           const int t = t0 + c0 + j, n = n0 / 2 + r;
-          if (t < a.T && c0 + j < a.bn && n < a.N / 2) {
+          if (t < tend && n < a.N / 2) {
             uint16_t gb = staging[j * 128 + r], ub = staging[j * 128 + 64 + r];
             float g = to_f<OutT>(*reinterpret_cast<OutT*>(&gb)), u = to_f<OutT>(*reinterpret_cast<OutT*>(&ub));
             Y[(long)t * a.ldy + n] = from_f<OutT>(silu(g) * u);
@@ -263,7 +331,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         for (int idx = et; idx < CH * 16; idx += 128) {
           const int j = idx / 16, q = idx % 16;
           const int t = t0 + c0 + j, n = n0 + q * 8;
-          if (t < a.T && c0 + j < a.bn) {
+          if (t < tend) {
             const uint4 val = *reinterpret_cast<const uint4*>(&staging[j * 128 + q * 8]);
             OutT* dst;
             if (push) {
@@ -290,7 +358,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int first_tile = a.ctas ? (int)(sg.pos / kblocks) : -1;  // tile of this CTA's first segment
     int tile, k0, k1;
     for (; sg.next(tile, k0, k1); ++ti) {
-      const int n0 = (tile / t_tiles) * 128, t0 = (tile % t_tiles) * a.bn;
+      const int n0 = (tile / t_tiles) * 128;
+      int t0, tend, owner;
+      tokt.rows(tile % t_tiles, t0, tend, owner);
       const int acc = ti & 1;
       if (!mbar_wait(&acc_full[acc], (ti >> 1) & 1, a.err, ERR_EPI_WAIT, abort_flag)) break;
       tc_fence_after();
@@ -299,7 +369,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
           float v[32];
           const uint32_t taddr = tmem + acc * BN + c0 + ((uint32_t)(ew * 32) << 16);
           if constexpr (CH == 32) tmem_ld32(taddr, v); else tmem_ld16(taddr, v);
-          emit(n0, t0, c0, v);
+          emit(n0, t0, tend, c0, v);
         }
         tc_fence_before();
         mbar_arrive(&acc_empty[acc]);
@@ -354,7 +424,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
             v[4 * j + 3] += f0[j].w + f1[j].w;
           }
         }
-        emit(n0, t0, c0, v);
+        emit(n0, t0, tend, c0, v);
       }
       if (et == 0) a.cnt[tile] = 0;  // re-armed for the next call on this stream
     }
@@ -371,6 +441,21 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+}
+
+template <int BN, typename OutT>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_ws_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmX, GemmArgs a,
+                   uint32_t idesc) {
+  gemm_ws_body<BN, OutT, false>(&tmW, &tmX, nullptr, a, idesc);
+}
+
+// all-gather -> GEMM: token tiles from the owners' gather areas (bf16)
+template <int BN>
+__global__ void __launch_bounds__(GEMM_THREADS, 1)
+    gemm_ag_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ GatherMaps gm, GemmArgs a,
+                   uint32_t idesc) {
+  gemm_ws_body<BN, __nv_bfloat16, true>(&tmW, nullptr, gm.m, a, idesc);
 }
 
 // ------------------------------------------------------------------ host side
@@ -483,6 +568,68 @@ int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy,
                           : launch_bn<128, __half>(tw, tx, a, bf16, max_ctas, stream);
     default: return bf16 ? launch_bn<256, __nv_bfloat16>(tw, tx, a, bf16, max_ctas, stream)
                          : launch_bn<256, __half>(tw, tx, a, bf16, max_ctas, stream);
+  }
+}
+
+// 3-D [2 slots][rows][K] view of one owner's gather area (16-bit elements), box [1][bn][BK]
+static int make_tmap_gather(CUtensorMap* map, const void* base, long rows, long K, long ld_elems, long slot_elems,
+                            int bn) {
+  auto fn = encode_fn();
+  if (!fn) return -1;
+  cuuint64_t dims[3] = {(cuuint64_t)K, (cuuint64_t)rows, 2};
+  cuuint64_t strides[2] = {(cuuint64_t)(ld_elems * 2), (cuuint64_t)(slot_elems * 2)};
+  cuuint32_t box[3] = {(cuuint32_t)BK, (cuuint32_t)bn, 1};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+template <int BN>
+static int launch_ag(const CUtensorMap& tw, const GatherMaps& gm, const GemmArgs& a, cudaStream_t st) {
+  using C = GemmCfg<BN>;
+  auto k = gemm_ag_kernel<BN>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+    attr = true;
+  }
+  const int tpo = (a.gather.per + a.bn - 1) / a.bn;
+  const int tiles = ((a.N + 127) / 128) * a.gather.world * tpo;
+  const int grid = std::max(1, std::min(tiles, num_sms()));
+  k<<<grid, GEMM_THREADS, C::SMEM, st>>>(tw, gm, a, idesc_f16(128, a.bn, true));
+  return (int)cudaGetLastError();
+}
+
+int gemm_ag(const void* const* src, long src_ld, long slot_stride, const void* w, long ldw, void* y, long ldy, int T,
+            int N, int K, const GemmGather& g, int* err, cudaStream_t stream) {
+  if (T <= 0 || N <= 0) return 0;
+  if (g.world < 1 || g.world > 8 || g.rank < 0 || g.rank >= g.world || g.per < 1 || (long)g.per * g.world < T ||
+      K % BK)
+    return -1;
+  // token tiles per owner: its `per` rows split evenly (as the plain GEMM splits T)
+  const int BN = gemm_bn(g.per);
+  int bn = BN;
+  if (BN == 256) {
+    const int tt = (g.per + 255) / 256;
+    bn = ((g.per + tt - 1) / tt + 15) / 16 * 16;
+  }
+  CUtensorMap tw;
+  int r = make_tmap_2d(&tw, w, 2, N, K, ldw, 128, BK, true);
+  if (r) return 1000 + r;
+  GatherMaps gm{};
+  for (int o = 0; o < g.world; ++o) {
+    r = make_tmap_gather(&gm.m[o], src[o], (long)g.per * g.world, K, src_ld, slot_stride, bn);
+    if (r) return 2000 + r;
+  }
+  GemmArgs a{y, ldy, T, N, K, 0, err, bn, 0, nullptr, nullptr, GemmPush{}, g};
+  switch (BN) {
+    case 16: return launch_ag<16>(tw, gm, a, stream);
+    case 32: return launch_ag<32>(tw, gm, a, stream);
+    case 64: return launch_ag<64>(tw, gm, a, stream);
+    case 128: return launch_ag<128>(tw, gm, a, stream);
+    default: return launch_ag<256>(tw, gm, a, stream);
   }
 }
 

@@ -23,11 +23,27 @@ struct GemmPush {
   long slot_stride;    // elements per slot of a region
 };
 
+// All-gather -> GEMM: the token rows are owned by the ranks in contiguous ranges (owner o holds
+// rows [o per, min(T, (o+1) per))), each in its own symmetric gather area; the GEMM's producer
+// loads owner o's token tiles by TMA straight from that area (a peer's memory over NVLink, no
+// multicast) after owner o's ready word has reached the producing kernel's epoch.
+struct GemmGather {
+  const int* ready[8];  // owner o's ready word as mapped on this rank (own entry unused)
+  const int* epoch;     // the producing kernel's device epoch e: slot e & 1, ready when word >= e
+  int world, rank, per;
+  unsigned long long timeout_ns;
+};
+
 // Y[T,N] = X[T,K] @ W[N,K]^T ; act 1 = silu(gate)*up over 64-row halves of each 128-row tile;
 // with `push`, row t is stored into the owner rank's partial slot instead of Y (ldy must be N)
 int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy, int T, int N, int K, bool bf16,
             int act, int* err, cudaStream_t stream, int max_ctas = 0, float* ws = nullptr, int* cnt = nullptr,
             const GemmPush* push = nullptr);
+// Y[T,N] = gathered X[T,K] @ W[N,K]^T, X row t read from owner t / per's gather area:
+// src[o] = owner o's area for slot 0 as mapped here, rows `src_ld` elements apart, slot 1 at
+// + slot_stride elements (bf16 only, no activation)
+int gemm_ag(const void* const* src, long src_ld, long slot_stride, const void* w, long ldw, void* y, long ldy, int T,
+            int N, int K, const GemmGather& g, int* err, cudaStream_t stream);
 // stream-K workspace (fp32 floats; 0 = whole tiles per CTA) and CTA count; counters: one per tile
 long gemm_split_ws_floats(int T, int N, int K);
 int gemm_streamk_ctas(int T, int N, int K);
@@ -151,9 +167,11 @@ int moe_expert_gemm_bf16(const void* xin, int in_cols, const void* w, int n_rows
 int symm_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                         const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
                         int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s);
+// own: the owner-only form (no all-gather; the next GEMM gathers, see comm.cu and gemm_ag)
 int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                         const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
-                        int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s);
+                        int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s,
+                        bool own = false);
 // the same after a GEMM that pushed its rows into the owners' slots (GemmPush, per rows a rank)
 // NVLS: switch-reduced all-reduce + residual add + RMSNorm over a multicast-bound region.
 long nvls_region_bytes(long slot_elems);

@@ -382,7 +382,10 @@ class Model:
             m = self._moe(L, h)
             self._stamp("moe")
             nxt = layers[i + 1]["in_norm"] if i + 1 < len(layers) else self.w["final_norm"]
-            x, h = comm.allreduce_add_rmsnorm(m, x, nxt, cfg.eps)
+            # before another layer, h only feeds its input projection: that GEMM may do the
+            # all-gather itself (QB_AG_GEMM; the residual then stays on this rank's rows until the
+            # next all-reduce, which reads only those)
+            x, h = comm.allreduce_add_rmsnorm(m, x, nxt, cfg.eps, gather_out=i + 1 < len(layers))
             self._stamp("allreduce")
         return x, h
 

@@ -50,7 +50,12 @@ def gated_rmsnorm(x, z, w, eps):
 
 # ----------------------------------------------------------------------------- dense
 def linear(x, w, out=None):
-    """``x @ w.T`` (fp32 accumulate). CUDA: tcgen05 GEMM with the weight as the M operand."""
+    """``x @ w.T`` (fp32 accumulate). CUDA: tcgen05 GEMM with the weight as the M operand. ``x``
+    may be the owner-only rows of a sequence-parallel all-reduce (``parallel.symm.GatheredRows``):
+    then the GEMM gathers them from every rank over NVLink itself."""
+    if getattr(x, "gathered", False):
+        assert out is None
+        return x.linear(w)
     if _cuda(x):
         return ext().linear(x, w, out)
     y = ref.linear(x, w)

@@ -20,6 +20,10 @@ model uses (NCCL all-gather of the tokens, every rank's experts on all tokens, N
 of the partial sums). Roofline of a call: the slower of this rank's active expert weights over
 HBM (measured copy bandwidth) and its dispatch + combine bytes over NVLink (770 GB/s).
 
+``--case ag_gemm``: the all-reduce after the MoE with the next layer's input projection: the
+owner-only all-reduce + the GEMM that gathers the rows over NVLink itself, against the full
+sequence-parallel all-reduce + plain GEMM and NCCL + GEMM.
+
 ``--case sp_gemm``: the prefill out-projection (o_proj, K = 8192 / N per rank) with its
 all-reduce + residual + RMSNorm: the fused GEMM -> reduce-scatter (the GEMM epilogue stores rows
 into their owners' symmetric slots, then the sequence-parallel kernel reduces and gathers)
@@ -166,12 +170,76 @@ def sp_gemm_sweep(args, rank, world, dev) -> list[dict]:
     return rows
 
 
+def ag_gemm_sweep(args, rank, world, dev) -> list[dict]:
+    """All-reduce + add + RMSNorm followed by the next layer's input projection (DeltaNet in_proj,
+    K = hidden, N = its 20608 output columns / N ranks): the owner-only all-reduce with the
+    gathering GEMM (rows pulled over NVLink inside the GEMM) against the full sequence-parallel
+    all-reduce (push all-gather) + the plain GEMM, and NCCL all-reduce + norm + GEMM."""
+    from ..ops import core as ops
+    from ..ops.kbench import peaks
+    from .symm import SymmComm
+
+    H = args.hidden
+    N = (20608 // world + 127) // 128 * 128
+    tokens = list(args.tokens)
+    symm = SymmComm(rank, world, dev, max_rows=512, hidden=H, sp_rows=max(tokens))
+    g = torch.Generator(device=dev).manual_seed(9 + rank)
+    wi = (torch.randn(N, H, device=dev, generator=g) * 0.02).bfloat16()
+    w = torch.ones(H, device=dev)
+    tflops = peaks()["bf16_tflops"]
+    rows = []
+    for T in tokens:
+        x = torch.randn(T, H, device=dev, generator=g).bfloat16()
+        res = torch.zeros(T, H, device=dev).bfloat16()
+
+        def fused():
+            _, gat = symm.allreduce_add_rmsnorm(x, res, w, 1e-6, kind="sp", gather_out=True)
+            ops.linear(gat, wi)
+
+        def sp_then_gemm():
+            _, h = symm.allreduce_add_rmsnorm(x, res, w, 1e-6, kind="sp")
+            ops.linear(h, wi)
+
+        def nccl_then_gemm():
+            y = x.float()
+            dist.all_reduce(y)
+            _, h = ops.add_rmsnorm(y.bfloat16(), res, w, 1e-6)
+            ops.linear(h, wi)
+
+        def gemm():
+            ops.linear(x, wi)
+
+        out = {"case": "ag_gemm", "tokens": T, "N": N, "n_gpus": world}
+        for name, fn in (("fused", fused), ("sp_gemm", sp_then_gemm), ("nccl_gemm", nccl_then_gemm),
+                         ("gemm_only", gemm)):
+            for _ in range(5):
+                fn()
+            torch.cuda.synchronize()
+            dist.barrier()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(args.ep_iters):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            us = torch.tensor([s.elapsed_time(e) * 1e3 / args.ep_iters], device=dev)
+            dist.all_reduce(us, op=dist.ReduceOp.MAX)
+            out[name + "_us"] = round(us.item(), 1)
+        # bytes into each GPU over NVLink: its share of the reduce-scatter and the gathered rows
+        link_bytes = 2 * (world - 1) / world * T * H * 2
+        roof_us = max(2 * T * H * N / (tflops * 1e6), link_bytes / (PEER_GBS * 1e3))
+        out.update(roofline_us=round(roof_us, 1), fused_frac_of_roofline=round(roof_us / out["fused_us"], 3))
+        rows.append(out)
+    symm.close()
+    return rows
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--tokens", type=int, nargs="*", default=[1, 4, 16, 32, 64, 128, 256, 512, 1024, 2048, 4096])
     ap.add_argument("--iters", type=int, default=200)
     ap.add_argument("--hidden", type=int, default=4096)
-    ap.add_argument("--case", default="allreduce", choices=["allreduce", "ep", "sp_gemm"])
+    ap.add_argument("--case", default="allreduce", choices=["allreduce", "ep", "sp_gemm", "ag_gemm"])
     ap.add_argument("--ep-iters", type=int, default=20)
     args = ap.parse_args()
     from ..ops import core as ops
@@ -183,7 +251,7 @@ def main():
     if args.case in ("ep", "sp_gemm"):
         if args.tokens == ap.get_default("tokens"):
             args.tokens = [8, 64, 512, 2048, 8192] if args.case == "ep" else [1024, 2048, 4096, 8192, 16384]
-        rows = (ep_sweep if args.case == "ep" else sp_gemm_sweep)(args, rank, world, dev)
+        rows = {"ep": ep_sweep, "sp_gemm": sp_gemm_sweep, "ag_gemm": ag_gemm_sweep}[args.case](args, rank, world, dev)
         if rank == 0:
             for r in rows:
                 print(json.dumps(r))

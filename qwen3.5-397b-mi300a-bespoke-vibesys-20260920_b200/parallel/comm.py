@@ -69,6 +69,7 @@ class Comm:
         self.symm = symm  # parallel.symm.SymmComm for the fused CUDA kernels, or None
         self.mode = flags.get("QB_COMM")
         self.sp_gemm = flags.get("QB_SP_GEMM")
+        self.ag_gemm = flags.get("QB_AG_GEMM")
 
     # ------------------------------------------------------------------ primitives
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
@@ -103,10 +104,16 @@ class Comm:
 
     # ------------------------------------------------------------------ fused
     def allreduce_add_rmsnorm(self, partial: torch.Tensor, residual: torch.Tensor, w1p: torch.Tensor,
-                              eps: float) -> tuple[torch.Tensor, torch.Tensor]:
-        """``residual + sum_ranks(partial)`` and its RMSNorm; returns (residual, normed)."""
+                              eps: float, gather_out: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+        """``residual + sum_ranks(partial)`` and its RMSNorm; returns (residual, normed). With
+        ``gather_out`` (the caller's only use of ``normed`` is one projection) and
+        ``QB_AG_GEMM``, sequence-parallel sizes return the owner-only form: ``residual`` valid on
+        this rank's rows only and ``normed`` a ``GatheredRows`` whose ``linear`` gathers inside
+        the GEMM."""
         if self.world > 1 and partial.is_cuda and self.symm is not None and self.mode == "fused":
-            got = self.symm.allreduce_add_rmsnorm(partial, residual, w1p, eps)
+            rows = residual.numel() // residual.shape[-1]
+            own = gather_out and self.ag_gemm and self.symm.gathers(rows)
+            got = self.symm.allreduce_add_rmsnorm(partial, residual, w1p, eps, gather_out=own)
             if got is not None:
                 return got
         summed = self.all_reduce(partial)

@@ -203,7 +203,8 @@ class SymmComm:
     @staticmethod
     def sp_region_bytes(sp_rows: int, hidden: int) -> int:
         # two slots of [partial | result residual + normed] = 3 x rows x hidden bf16, then A and B flags
-        return 2 * 3 * sp_rows * hidden * 2 + 4 * SP_MAX_BLOCKS * 4
+        # and the owner-only call's ready word
+        return 2 * 3 * sp_rows * hidden * 2 + 4 * SP_MAX_BLOCKS * 4 + 64
 
     def _region(self, nbytes: int, group, bases):
         """Allocate and export this rank's region, map every peer's (or use given bases)."""
@@ -221,7 +222,7 @@ class SymmComm:
     def fits(self, rows: int) -> bool:
         return rows <= self.max_rows or rows <= self.sp_rows
 
-    def allreduce_add_rmsnorm(self, partial, residual, w1p, eps, kind: str = "auto"):
+    def allreduce_add_rmsnorm(self, partial, residual, w1p, eps, kind: str = "auto", gather_out: bool = False):
         """``residual += sum_ranks(partial)`` (in place) and returns (residual, rmsnorm(residual)).
         One-shot kernel while ``rows * (world - 1)`` is within ``ONESHOT_ROW_BUDGET`` (one peer
         round trip), the sequence-parallel kernel above that (``kind`` = "oneshot" / "sp" forces
@@ -245,13 +246,21 @@ class SymmComm:
             use_sp = fits_sp and (rows > self.max_rows or rows * (self.world - 1) > self.ONESHOT_ROW_BUDGET)
         if use_sp:
             ext().symm_sp_ar_add_rmsnorm(self.sp_bases, self.rank, partial, residual, w1p, normed, float(eps),
-                                         self.sp_slot_elems, SP_MAX_BLOCKS, self.sp_epoch, self.timeout_s)
+                                         self.sp_slot_elems, SP_MAX_BLOCKS, self.sp_epoch, self.timeout_s,
+                                         gather_out)
+            if gather_out:  # this rank's rows only: the next projection gathers (GatheredRows.linear)
+                return residual, GatheredRows(self, rows, residual.shape[-1], residual.device, normed)
             return residual, normed
         if rows > self.max_rows:
             return None
         ext().symm_ar_add_rmsnorm(self.bases, self.rank, partial, residual, w1p, normed, float(eps), self.slot_elems,
                                   self.max_blocks, self.epoch, self.timeout_s)
         return residual, normed
+
+    def gathers(self, rows: int) -> bool:
+        """Whether ``allreduce_add_rmsnorm(..., gather_out=True)`` leaves the all-gather of ``rows``
+        rows to the next projection (the sizes that take the sequence-parallel kernel)."""
+        return self.fuses_linear(rows)
 
     def fuses_linear(self, rows: int) -> bool:
         """Whether ``linear_allreduce_add_rmsnorm`` takes the fused GEMM -> reduce-scatter path
@@ -282,3 +291,25 @@ class SymmComm:
         for p in self.own:
             ext().symm_free(p)
         self.own.clear()
+
+
+class GatheredRows:
+    """The normed rows of an owner-only sequence-parallel all-reduce: this rank holds its own
+    range (``local``, other rows unset); every rank's range sits in that rank's symmetric result
+    area. ``linear(w)`` is the all-gather -> GEMM: ``gathered @ w^T`` with each owner's token
+    tiles loaded by TMA from its area once its ready word shows this call (csrc/gemm.cu
+    ``gemm_ag``). It stands in for the normed tensor where its only consumer is the next layer's
+    input projection."""
+
+    gathered = True
+    is_cuda = True
+    dtype = torch.bfloat16
+
+    def __init__(self, symm: "SymmComm", rows: int, hidden: int, device, local: torch.Tensor):
+        self.symm, self.rows, self.hidden, self.device, self.local = symm, rows, hidden, device, local
+        self.shape = (rows, hidden)
+
+    def linear(self, w: torch.Tensor) -> torch.Tensor:
+        s = self.symm
+        return ext().symm_gemm_ag(s.sp_bases, s.rank, w, self.rows, self.hidden, s.sp_slot_elems, SP_MAX_BLOCKS,
+                                  s.sp_epoch, s.timeout_s)

@@ -82,6 +82,9 @@ _def("QB_SP_MAX_ROWS", int, 4096, "rows of the sequence-parallel fused all-reduc
      lockstep=True)
 _def("QB_NVLS_MIN_ROWS", int, 0, "all-reduce messages of at least this many rows use the NVLS (multimem) kernel "
      "(0: never)", lockstep=True)
+_def("QB_AG_GEMM", bool, False, "prefill: the all-reduce after the MoE leaves the all-gather to the next layer's "
+     "input projection, which pulls every rank's normed rows over NVLink inside its GEMM (sequence-parallel sizes)",
+     lockstep=True)
 _def("QB_SP_GEMM", bool, True, "prefill: fuse the mixers' output projection into the sequence-parallel all-reduce "
      "(GEMM epilogue stores rows into their owners' peer slots)", lockstep=True)
 _def("QB_CMD_CHANNEL", str, "shm", "leader -> worker command channel: shm (shared-memory ring) or gloo (broadcast)",

@@ -81,6 +81,17 @@ def test_two_gpu_fused_equals_nccl():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_multi_gpu_allgather_gemm_equals_allreduce_then_gemm():
+    """Every visible GPU (up to 8): owner-only sequence-parallel all-reduce + the GEMM that pulls
+    every rank's rows over NVLink against the full all-reduce + the plain GEMM."""
+    world, port = _world(), _port()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    procs = [subprocess.Popen([sys.executable, os.path.join(HERE, "ag_rank.py"), str(r), str(world), str(port)],
+                              env=env) for r in range(world)]
+    assert [p.wait(timeout=300) for p in procs] == [0] * world
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_gpu_model_out_proj_fused_equals_unfused():
     """Tiny model on 2 or 4 ranks (its 4 DeltaNet key heads bound the split): a 1500-token
     prefill with the attention / DeltaNet out projections fused into the sequence-parallel
