@@ -55,7 +55,8 @@ def ext():
                 "run `python -c 'import __graft_entry__ as g; g.build()'`"
             )
         torch.cuda.init() if torch.cuda.is_available() else None
-        spec = importlib.util.spec_from_file_location(MODULE_NAME, path)
+        # the module's own name: the file stem (the debug build is qwen35_b200_C_bounds)
+        spec = importlib.util.spec_from_file_location(os.path.basename(path).split(".")[0], path)
         mod = importlib.util.module_from_spec(spec)
         spec.loader.exec_module(mod)
         _mod = mod

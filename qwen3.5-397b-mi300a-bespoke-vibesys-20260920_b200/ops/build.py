@@ -38,7 +38,7 @@ def build(verbose: bool = False, bounds: bool = False):
     os.environ.setdefault("TORCH_CUDA_ARCH_LIST", "10.0a")
     os.environ.setdefault("MAX_JOBS", str(min(8, os.cpu_count() or 4)))
     return ce.load(
-        name=MODULE_NAME,
+        name=MODULE_NAME + ("_bounds" if bounds else ""),
         sources=sources(),
         extra_cflags=["-O3", "-std=c++17"] + (["-DQB_BOUNDS"] if bounds else []),
         extra_cuda_cflags=CUDA_FLAGS + (["-DQB_BOUNDS"] if bounds else []),

@@ -277,13 +277,16 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
 
     g = GraphRunner(m, buckets=(lanes,))
     g.prepare()
+    for lane in range(lanes):  # capture and validation ran on reset lanes: attach the blocks again
+        m.begin(lane)
+        m.attach_blocks(lane, list(range(1 + lane * per, 1 + (lane + 1) * per)))
     pos = [max(ctx, 2048) + lane for lane in range(lanes)]
     ms = _time(lambda: g.decode(list(range(lanes)), [5] * lanes, pos), 5)
-    replay_ms = _time(lambda: g._b[lanes].graph.replay(), 5)
+    replay_ms = _time(lambda: g._b[lanes].graph.replay(), 5) if lanes in g._b else None
     att = g.attribution(lanes, replays=5)
     tot = att.get("total", 0.0) or 1.0
     row = {"case": "model_decode_graph", "lanes": lanes, "ctx": max(ctx, 2048), "ms": round(ms, 2),
-           "replay_ms": round(replay_ms, 2),
+           "replay_ms": round(replay_ms, 2) if replay_ms is not None else None,
            "parts_ms": {k: round(v, 3) for k, v in sorted(att.items())},
            "parts_share": {k: round(v / tot, 3) for k, v in sorted(att.items()) if k != "total"}}
     print(json.dumps(row), flush=True)
