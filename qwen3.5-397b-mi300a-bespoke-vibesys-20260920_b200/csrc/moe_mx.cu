@@ -135,10 +135,17 @@ __device__ __forceinline__ int mx_cols(int rest) {
   return n < BN ? n : BN;
 }
 
+// Wide path: the hi|lo planes of a token tile by boxes of exactly the tile's rows rounded up to
+// 16 (m[i] loads 16 (i + 1) rows of each plane), so a tile of an expert with fewer tokens than BN
+// moves and multiplies only those rows.
+struct MxPlanes {
+  CUtensorMap m[4];
+};
+
 template <int BN, bool W>
 __global__ void __launch_bounds__(MX_THREADS, 1)
     moe_mx_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmH,
-                  const __grid_constant__ CUtensorMap tmL, MxArgs a) {
+                  const __grid_constant__ CUtensorMap tmL, const __grid_constant__ MxPlanes pl, MxArgs a) {
   using C = MxCfg<BN, W>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -216,11 +223,14 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
       long long pw = 0, pi = 0, w1 = 0;
       const long long p0 = clock64();
       int e = 0;
-      constexpr uint32_t TX = C::A / 2 + 2 * BN * MX_SK + 2 * MX_CHUNK;
       for (int u = blockIdx.x; u < units && !*abort_flag; u += gridDim.x) {
         int nt, tt;
         unit(u, e, nt, tt);
-        const int row_b = offs[e] + (tt - tstart[e]) * BN;
+        const int m0 = (tt - tstart[e]) * BN;
+        const int row_b = offs[e] + m0;
+        const int ne = mx_cols<BN>(cnts[e] - m0);  // the tile's rows, rounded up to 16
+        const CUtensorMap* tmP = &pl.m[ne / 16 - 1];
+        const uint32_t TX = C::A / 2 + 2 * ne * MX_SK + 2 * MX_CHUNK;
         const int wtile = e * n_tiles + nt;
         int trow = wtile * kstages * 128;  // < 2^31: 512 experts x 32 tiles x 32 stages x 128
         const uint8_t* sfw = a.sfa + (long)wtile * kstages * MX_CHUNK;
@@ -235,7 +245,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
           const uint32_t fb = full0 + 8 * s, st = st0 + s * C::STAGE, sf = sf0 + s * C::SF;
           mbar_expect_tx_s(fb, TX);
           tma_load_2d_s(st, &tmW, fb, 0, trow);
-          tma_load_3d_s(st + C::A, &tmH, fb, kx, row_b, 0);  // hi then lo plane
+          tma_load_3d_s(st + C::A, tmP, fb, kx, row_b, 0);  // ne hi rows, then ne lo rows
           bulk_g2s_s(sf, sfw, MX_CHUNK, fb);
           bulk_g2s_s(sf + MX_CHUNK, sfb, MX_CHUNK, fb);
           trow += 128;
@@ -329,13 +339,16 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
                      acce0 = smem_u32(acc_empty);
       const uint64_t da0 = desc_sw128(smem_u32(stages)), db0 = desc_sw128(smem_u32(stages) + C::A);
       const uint32_t sf_s0 = smem_u32(sfs);
-      const uint32_t idesc = idesc_mxf8f6f4(2 * BN);  // hi | lo rows: one N = 2 BN operand
-      int s = 0, ti = 0;
+      int s = 0, ti = 0, e = 0;
       uint32_t ph = 0;
       bool ok = true;
       long long mw = 0, aw = 0, mi = 0, m1 = 0;
       const long long m0c = clock64();
       for (int u = blockIdx.x; u < units && ok && !*abort_flag; u += gridDim.x, ++ti) {
+        int nt, tt;
+        unit(u, e, nt, tt);
+        // hi | lo rows of the tile: one N = 2 ne operand (lo products in columns [ne, 2 ne))
+        const uint32_t idesc = idesc_mxf8f6f4(2 * mx_cols<BN>(cnts[e] - (tt - tstart[e]) * BN));
         const int acc = ti & 1;
         const long long a0 = a.probe ? clock64() : 0;
         if (!mbar_wait_s(acce0 + 8 * acc, ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
@@ -476,9 +489,9 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         float v[16];
         const uint32_t ta = tmem + acc * C::ACC + c0 + ((uint32_t)(ew * 32) << 16);
         tmem_ld16(ta, v);
-        if (W) {  // hi products in columns [0, BN), lo products in [BN, 2 BN)
+        if (W) {  // hi products in columns [0, ne), lo products in [ne, 2 ne)
           float vl[16];
-          tmem_ld16(ta + BN, vl);
+          tmem_ld16(ta + ne, vl);
 #pragma unroll
           for (int j = 0; j < 16; ++j) v[j] += vl[j];
         }
@@ -527,6 +540,15 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
 }
 
 // ------------------------------------------------------------------ activation split
+// Rows of the token tile holding row r_e of expert e (tiles of BN rows from the expert's first
+// row), rounded up to 16: the tile's hi | lo MMA operand is 2 x this many rows.
+__device__ __forceinline__ int mx_tile_rows(const int* offsets, int count, int n_rows, int e, int r_e, int BN) {
+  const int cnt = (e + 1 < count ? offsets[e + 1] : n_rows) - offsets[e];
+  const int m0 = r_e / BN * BN;
+  const int n = (cnt - m0 + 15) & ~15;
+  return n < BN ? n : BN;
+}
+
 // One warp per row: rows `a < *n_rows` of x (row a read from x[perm[a]] when perm is given) ->
 // hi / lo e4m3 bytes [cap, K] and their scales, written straight into the per-tile chunks (the
 // token tile of row a is the tile of its expert's run; tiles of BN rows). Each lane holds 8
@@ -548,6 +570,9 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
   }
   const int r_e = a - offsets[lo_e];
   const int tt = tstart[lo_e] + r_e / BN, rr = r_e % BN;
+  // merged layout: the lo scales follow the tile's own rows (rounded up to 16), the rows of its
+  // one hi | lo MMA operand
+  const int lo_off = lo_rows ? mx_tile_rows(offsets, count, *n_rows, lo_e, r_e, BN) : 0;
   const bf16* src = x + (long)(perm ? perm[a] : a) * K;
   uint8_t* hrow = hi + (long)a * K;
   uint8_t* lrow = lo + (long)a * K;
@@ -585,7 +610,7 @@ __global__ void mx_quant_kernel(const bf16* x, const int* perm, const int* n_row
       const int kb = k0 / 32;
       const long cb = sf_tile + (long)(kb / 4) * cstride;
       sf_hi[cb + mx_chunk_offset(rr, kb % 4)] = (uint8_t)(E + 127);
-      sf_lo[cb + mx_chunk_offset(rr + lo_rows, kb % 4)] = (uint8_t)(E - 4 + 127);
+      sf_lo[cb + mx_chunk_offset(rr + lo_off, kb % 4)] = (uint8_t)(E - 4 + 127);
     }
   }
 }
@@ -651,6 +676,7 @@ __global__ void mx_expand_kernel(const uint8_t* qhi, const uint8_t* qlo, const u
   }
   const int r_e = a - offsets[lo_e];
   const int tt = tstart[lo_e] + r_e / BN, rr = r_e % BN;
+  const int lo_off = lo_rows ? mx_tile_rows(offsets, count, *n_rows, lo_e, r_e, BN) : 0;
   const long src = perm[a];
   const uint4* sh = reinterpret_cast<const uint4*>(qhi + src * K);
   const uint4* sl = reinterpret_cast<const uint4*>(qlo + src * K);
@@ -665,7 +691,7 @@ __global__ void mx_expand_kernel(const uint8_t* qhi, const uint8_t* qlo, const u
     const uint8_t eb = exps[src * (K / 32) + kb];
     const long cb = sf_tile + (long)(kb / 4) * cstride;
     sf_hi[cb + mx_chunk_offset(rr, kb % 4)] = eb;
-    sf_lo[cb + mx_chunk_offset(rr + lo_rows, kb % 4)] = (uint8_t)(eb - 4);
+    sf_lo[cb + mx_chunk_offset(rr + lo_off, kb % 4)] = (uint8_t)(eb - 4);
   }
 }
 
@@ -736,7 +762,8 @@ int mx_probe_read(unsigned long long* out) {
 
 // Merged activation layout (wide boxes over tiled codes, token tiles of at most 64): the lo plane
 // right after the hi plane, and one scale chunk per (token tile, K stage) holding the hi scales in
-// rows [0, BN) and the lo scales in rows [BN, 2 BN), the rows of the one N = 2 BN MMA operand.
+// rows [0, n) and the lo scales in rows [n, 2 n), n = the tile's rows rounded up to 16: the rows of
+// its one N = 2 n MMA operand.
 bool mx_merged(bool tiled, int BN) {
   static const bool wide_env = !getenv("QB_MX_WIDE") || atoi(getenv("QB_MX_WIDE")) != 0;
   return tiled && wide_env && BN <= 64;
@@ -753,8 +780,8 @@ static int mx_sms() {
 }
 
 template <int BN, bool W>
-static int mx_launch(const CUtensorMap& tw, const CUtensorMap& th, const CUtensorMap& tl, const MxArgs& a,
-                     cudaStream_t st) {
+static int mx_launch(const CUtensorMap& tw, const CUtensorMap& th, const CUtensorMap& tl, const MxPlanes& pl,
+                     const MxArgs& a, cudaStream_t st) {
   using C = MxCfg<BN, W>;
   auto k = moe_mx_kernel<BN, W>;
   static bool attr = false;
@@ -762,7 +789,7 @@ static int mx_launch(const CUtensorMap& tw, const CUtensorMap& th, const CUtenso
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
     attr = true;
   }
-  k<<<mx_sms(), MX_THREADS, C::SMEM, st>>>(tw, th, tl, a);
+  k<<<mx_sms(), MX_THREADS, C::SMEM, st>>>(tw, th, tl, pl, a);
   return (int)cudaGetLastError();
 }
 
@@ -837,14 +864,19 @@ int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, cons
   if (r) return 2000 + r;
   r = mx_tmap(&tl, lo, cap, K, K, 16, false);
   if (r) return 3000 + r;
+  MxPlanes pl{};
+  for (int i = 0; wide && i < BN / 16; ++i) {
+    r = mx_tmap_planes(&pl.m[i], hi, cap, K, lo - hi, 16 * (i + 1));
+    if (r) return 4000 + r;
+  }
   static const int probe = getenv("QB_MX_PROBE") ? atoi(getenv("QB_MX_PROBE")) : 0;
   MxArgs a{sfa, sf_hi, sf_lo, offsets, counts, tstart, out, out_cols, n_rows, K, count, act, err, tiled ? 1 : 0,
            wide ? 1 : 0, probe};
   switch (BN) {
-    case 16: return wide ? mx_launch<16, true>(tw, th, tl, a, s) : mx_launch<16, false>(tw, th, tl, a, s);
-    case 32: return wide ? mx_launch<32, true>(tw, th, tl, a, s) : mx_launch<32, false>(tw, th, tl, a, s);
-    case 64: return wide ? mx_launch<64, true>(tw, th, tl, a, s) : mx_launch<64, false>(tw, th, tl, a, s);
-    default: return mx_launch<128, false>(tw, th, tl, a, s);
+    case 16: return wide ? mx_launch<16, true>(tw, th, tl, pl, a, s) : mx_launch<16, false>(tw, th, tl, pl, a, s);
+    case 32: return wide ? mx_launch<32, true>(tw, th, tl, pl, a, s) : mx_launch<32, false>(tw, th, tl, pl, a, s);
+    case 64: return wide ? mx_launch<64, true>(tw, th, tl, pl, a, s) : mx_launch<64, false>(tw, th, tl, pl, a, s);
+    default: return mx_launch<128, false>(tw, th, tl, pl, a, s);
   }
 }
 

@@ -146,7 +146,8 @@ class _SpecBucket:
         i32 = dict(dtype=torch.int32, device=dev)
         self.B, self.k = B, k
         R = B * (k + 1)
-        self.n_packed = B + 2 * k * B + 2 * R + B  # lanes | draft pos, rows | verify pos, rows | starts
+        # lanes | draft pos, rows | verify pos, rows | starts | real-row flags
+        self.n_packed = B + 2 * k * B + 2 * R + B + B
         self.packed_host = torch.zeros(self.n_packed, dtype=torch.int32).pin_memory()
         self.packed_dev = torch.zeros(self.n_packed, **i32)
         self.tok_host = torch.zeros(B, dtype=torch.int64).pin_memory()
@@ -157,13 +158,14 @@ class _SpecBucket:
         self.pos_v = torch.zeros(R, **i32)
         self.rows_v = torch.zeros(R, **i32)
         self.start_v = torch.zeros(B, **i32)
+        self.real = torch.zeros(B, dtype=torch.int64, device=dev)  # 1 for a lane's row, 0 for padding
         self.cu_d = torch.arange(B + 1, **i32)
         self.cu_v = torch.arange(0, R + 1, k + 1, **i32)
         self.logit_rows_d = torch.arange(B, dtype=torch.int64, device=dev)
         self.logit_rows_v = torch.arange(R, dtype=torch.int64, device=dev)
         self.n_host = torch.zeros(B, dtype=torch.int64).pin_memory()  # accepted drafts per lane
         self.n_dev = torch.zeros(B, dtype=torch.int64, device=dev)
-        self.graph = self.commit_graph = None
+        self.graph = self.commit_graph = self.round_graph = None
         self.drafts = self.am = self.vb = self.vsave = self.h_all = None
 
     def unpack(self) -> None:
@@ -180,6 +182,7 @@ class _SpecBucket:
         self.pos_v.copy_(pd[o:o + R])
         self.rows_v.copy_(pd[o + R:o + 2 * R])
         self.start_v.copy_(pd[o + 2 * R:o + 2 * R + B])
+        self.real.copy_(pd[o + 2 * R + B:o + 2 * R + 2 * B])
 
 
 class GraphRunner:
@@ -326,6 +329,7 @@ class GraphRunner:
         vals.extend(p + j for p in pos for j in range(k + 1))
         vals.extend(m._row(l, p + j) if r else 0 for l, p, r in zip(ln, pos, real) for j in range(k + 1))
         vals.extend(pos)
+        vals.extend(1 if r else 0 for r in real)
         bk.packed_host.copy_(torch.tensor(vals, dtype=torch.int32))
         bk.tok_host[:n] = torch.tensor([int(t) for t in tokens], dtype=torch.int64)
         bk.tok_host[n:] = 0
@@ -361,6 +365,17 @@ class GraphRunner:
         bk.vb, bk.vsave, bk.h_all = vb, m._vsave, m.last_h_all
         m._vsave = {}
 
+    def _spec_accept(self, bk: _SpecBucket) -> None:
+        """Accepted drafts per lane on the device: the leading drafts that equal the verify argmax
+        (``MTPHead.accept``), or with forced acceptance each further draft with probability p
+        from the device generator; padding rows accept none."""
+        mtp, k = self.model.mtp, bk.k
+        if mtp.forced_accept is None:
+            hit = bk.drafts.eq(bk.am[:, :k])
+        else:
+            hit = torch.rand(bk.B, k, device=bk.drafts.device) < mtp.forced_accept
+        bk.n_dev.copy_(hit.to(torch.int64).cumprod(dim=1).sum(dim=1) * bk.real)
+
     def _spec_commit(self, bk: _SpecBucket) -> None:
         m = self.model
         m._vsave = bk.vsave
@@ -368,9 +383,11 @@ class GraphRunner:
         m._commit_verify_device(bk.vb, bk.n_dev, bk.k)
 
     def prepare_speculative(self, buckets=None) -> None:
-        """Capture two graphs per bucket: the round (draft + wide verify + argmax) and its commit
-        (DeltaNet state over the accepted rows, MTP catch-up), between which the host reads the
-        argmax and decides the accepted lengths. Every rank must call this in the same order."""
+        """Capture per bucket the whole round as one graph (draft + wide verify + argmax, the
+        accepted lengths on the device, the commit: DeltaNet state over the accepted rows, MTP
+        catch-up), read back once after it; with ``QB_MTP_DEVICE_ACCEPT=0`` two graphs instead,
+        between which the host reads the argmax and decides the accepted lengths. Every rank
+        must call this in the same order."""
         m = self.model
         if not self.enabled or m.device.type != "cuda" or m.mtp is None:
             return
@@ -398,6 +415,13 @@ class GraphRunner:
             with torch.inference_mode(), torch.cuda.graph(gc, pool=self.pool):
                 self._spec_commit(bk)
             bk.graph, bk.commit_graph = g, gc
+            if flags.get("QB_MTP_DEVICE_ACCEPT"):
+                gr = torch.cuda.CUDAGraph()
+                with torch.inference_mode(), torch.cuda.graph(gr, pool=self.pool):
+                    self._spec_run(bk)
+                    self._spec_accept(bk)
+                    self._spec_commit(bk)
+                bk.round_graph = gr
             self._spec[B] = bk
         torch.cuda.synchronize()
 
@@ -410,6 +434,21 @@ class GraphRunner:
         if B is None or m.fault:  # a calibration fault acts on the eager path only
             return m.speculative_decode(lanes, tokens, positions, budgets, stops)
         bk, mtp, k = self._spec[B], m.mtp, m.mtp.k
+        if bk.round_graph is not None:
+            with torch.inference_mode():
+                self._spec_fill(bk, lanes, tokens, positions)
+                bk.round_graph.replay()
+                m._gpu_mark("out")
+                res = torch.cat([bk.n_dev[:, None], bk.drafts, bk.am], dim=1)[:n].tolist()  # one host sync
+            m._d2h += 8 * n * (2 * k + 2)
+            ns = [int(r[0]) for r in res]
+            dr_h = [r[1:1 + k] for r in res]
+            am_h = [r[1 + k:] for r in res]
+            mtp.rounds += n
+            mtp.accepted += sum(ns)
+            mtp.drafted += n * k
+            self.replays += 1
+            return self._spec_tokens(n, ns, dr_h, am_h, budgets, stops)
         with torch.inference_mode():
             self._spec_fill(bk, lanes, tokens, positions)
             bk.graph.replay()
@@ -426,6 +465,12 @@ class GraphRunner:
             m._h2d += 8 * B
             bk.commit_graph.replay()
         self.replays += 1
+        return self._spec_tokens(n, ns, dr_h, am_h, budgets, stops)
+
+    @staticmethod
+    def _spec_tokens(n, ns, dr_h, am_h, budgets, stops):
+        """Each lane's committed tokens: its accepted drafts and the verify argmax after them, cut
+        at a stop id and at its budget."""
         out = []
         for i in range(n):
             toks = dr_h[i][:ns[i]] + [am_h[i][ns[i]]]

@@ -66,6 +66,8 @@ _def("QB_PREFILL_PACK", str, "fill", "scheduler: fill (pack prefill chunks up to
      "(once a step gives some request its first token, add only requests whose prompt also completes in it)")
 _def("QB_OVERLAP", bool, True, "scheduler: launch decode step n+1 (tokens fed back on the device) before reading "
      "step n back", lockstep=True)
+_def("QB_MTP_DEVICE_ACCEPT", bool, True, "speculative rounds: accepted lengths computed on the device and the whole "
+     "round (draft, verify, accept, commit) replayed as one graph, read back once", lockstep=True)
 _def("QB_FOLD_SUFFIX", bool, False, "scheduler: the chat template's generation suffix after the turn-open boundary "
      "is fed through the following decode steps (their sampled ids discarded) instead of a prefill step of its own")
 _def("QB_PREFILL_ACCUM", bool, False, "scheduler: while at least QB_PREFILL_ACCUM_MIN_DECODE lanes decode, hold "

@@ -97,9 +97,12 @@ def test_graph_attribution_tiny():
     assert abs(parts - att["total"]) < 1e-6 + 1e-6 * att["total"]
 
 
-def test_speculative_round_graph_matches_eager():
-    """Captured speculative rounds (draft + wide verify in one graph, eager accept and commit)
-    emit the same tokens as the eager rounds on identical lane states."""
+@pytest.mark.parametrize("device_accept", ["1", "0"])
+def test_speculative_round_graph_matches_eager(device_accept, monkeypatch):
+    """Captured speculative rounds emit the same tokens as the eager rounds on identical lane
+    states: the whole round as one graph with the accepted lengths computed on the device, or
+    (QB_MTP_DEVICE_ACCEPT=0) draft + verify in one graph, host accept, then the commit graph."""
+    monkeypatch.setenv("QB_MTP_DEVICE_ACCEPT", device_accept)
     from qwen35_b200.models import mtp as mtpmod
     from qwen35_b200.models.config import tiny_config
     from qwen35_b200.models.qwen35 import Model
@@ -116,6 +119,7 @@ def test_speculative_round_graph_matches_eager():
     g = GraphRunner(m, buckets=(1, 2, 4))
     g.prepare_speculative()
     assert set(g._spec) == {1, 2, 4}
+    assert all((bk.round_graph is not None) == (device_accept == "1") for bk in g._spec.values())
     prompts = [list(range(7, 60)), list(range(100, 141))]
     for i, ids in enumerate(prompts * 2):  # lanes 0,1 (graph) and 2,3 (eager) hold the same history
         m.begin(i)
