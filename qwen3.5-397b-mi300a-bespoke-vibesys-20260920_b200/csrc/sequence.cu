@@ -23,28 +23,60 @@ __device__ __forceinline__ int seg_of(const int* cu, int S, int t) {
 }
 
 // ------------------------------------------------------------------ causal conv
-// Output kernel: one thread per (token, channel); the K-1 inputs before a segment's first
-// token come from the lane's saved window. State kernel (launched after): the window becomes
-// the last K-1 inputs of the segment (old window entries when the segment is shorter).
+// Output kernel: one thread per (channel, run of CONV_RUN consecutive tokens); the thread keeps
+// the K-1 previous inputs in registers, so every input is read once, and takes the K-1 inputs
+// before a segment's first token from the lane's saved window. State kernel (launched after): the
+// window becomes the last K-1 inputs of the segment (old window entries when the segment is
+// shorter).
+constexpr int CONV_RUN = 16;
+
 template <int K>
 __global__ void conv_out_kernel(const bf16* x, long ldx, const bf16* state, long lane_stride, const bf16* w,
                                 const int* seg_lane, const int* cu, int S, int C, bf16* out, int lanes) {
   const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  const int t = blockIdx.y;
-  if (c >= C || t >= cu[S]) return;  // rows past the last segment: padding of a fixed-size batch
-  const int s = seg_of(cu, S, t);
-  const int t0 = cu[s];
-  if (!bounds_ok(BS_LANE, seg_lane[s], lanes)) return;
-  const bf16* st = state + (long)seg_lane[s] * lane_stride + (long)c * (K - 1);
-  float acc = 0.f;
+  const int T = cu[S];
+  const int tb = blockIdx.y * CONV_RUN;
+  if (c >= C || tb >= T) return;  // rows past the last segment: padding of a fixed-size batch
+  const int te = min(T, tb + CONV_RUN);
+  float wk[K];
 #pragma unroll
-  for (int j = 0; j < K; ++j) {
-    const int src = t - (K - 1) + j;  // absolute row of input j
-    const float xv = src >= t0 ? __bfloat162float(x[(long)src * ldx + c]) : __bfloat162float(st[src - t0 + K - 1]);
-    acc += __bfloat162float(w[(long)c * K + j]) * xv;
+  for (int j = 0; j < K; ++j) wk[j] = __bfloat162float(w[(long)c * K + j]);
+  int s = seg_of(cu, S, tb);
+  int t0 = cu[s], t1 = cu[s + 1];
+  // win[i]: the input at row t - (K-1) + i for the current t
+  float win[K - 1];
+  auto load_window = [&](int t) -> bool {
+    const int ln = seg_lane[s];
+    if (!bounds_ok(BS_LANE, ln, lanes)) return false;
+    const bf16* st = state + (long)ln * lane_stride + (long)c * (K - 1);
+#pragma unroll
+    for (int i = 0; i < K - 1; ++i) {
+      const int src = t - (K - 1) + i;
+      win[i] = src >= t0 ? __bfloat162float(x[(long)src * ldx + c]) : __bfloat162float(st[src - t0 + K - 1]);
+    }
+    return true;
+  };
+  if (!load_window(tb)) return;
+  for (int t = tb; t < te; ++t) {
+    if (t >= t1) {  // the next (non-empty) segment starts: its window comes from its lane's state
+      while (t >= t1) {
+        ++s;
+        t0 = t1;
+        t1 = cu[s + 1];
+      }
+      if (!load_window(t)) return;
+    }
+    const float xt = __bfloat162float(x[(long)t * ldx + c]);
+    float acc = 0.f;
+#pragma unroll
+    for (int j = 0; j < K - 1; ++j) acc += wk[j] * win[j];
+    acc += wk[K - 1] * xt;
+    const float a = rbf2(acc);
+    out[(long)t * C + c] = __float2bfloat16(a / (1.f + expf(-a)));
+#pragma unroll
+    for (int i = 0; i < K - 2; ++i) win[i] = win[i + 1];
+    win[K - 2] = xt;
   }
-  const float a = rbf2(acc);
-  out[(long)t * C + c] = __float2bfloat16(a / (1.f + expf(-a)));
 }
 
 template <int K>
@@ -68,8 +100,8 @@ int causal_conv_varlen_t(const void* x, long ldx, void* state, long lane_stride,
                          cudaStream_t s) {
   if (!S || !T) return 0;
   if (K != 4) return -1;
-  conv_out_kernel<4><<<dim3((C + 127) / 128, T), 128, 0, s>>>((const bf16*)x, ldx, (const bf16*)state, lane_stride,
-                                                               (const bf16*)w, seg_lane, cu, S, C, (bf16*)out, lanes);
+  conv_out_kernel<4><<<dim3((C + 127) / 128, (T + CONV_RUN - 1) / CONV_RUN), 128, 0, s>>>(
+      (const bf16*)x, ldx, (const bf16*)state, lane_stride, (const bf16*)w, seg_lane, cu, S, C, (bf16*)out, lanes);
   if (commit)
     conv_state_kernel<4><<<dim3((C + 127) / 128, S), 128, 0, s>>>((const bf16*)x, ldx, (bf16*)state, lane_stride,
                                                                    seg_lane, cu, C, lanes);
