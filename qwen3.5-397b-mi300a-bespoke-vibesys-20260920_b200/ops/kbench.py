@@ -267,8 +267,12 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
                 agg[ev.name.split("(")[0][:60]][1] += getattr(ev, "device_time_total", 0.0)
         tot = sum(v[1] for v in agg.values()) or 1.0
         top = sorted(agg.items(), key=lambda kv: -kv[1][1])[:12]
+        # kernel_ms: the step's kernels back to back; ms - kernel_ms: device idle inside the step
+        # (host launch cost the GPU waited for)
         row = {"case": f"model_{f.__name__}", "tokens": tokens if f is prefill else lanes, "ctx": ctx,
-               "ms": round(ms, 2), "kernels": [(k, n, round(t / tot, 3)) for k, (n, t) in top]}
+               "ms": round(ms, 2), "kernel_ms": round(tot / 1e3, 2),
+               "launches": sum(n for n, _ in agg.values()),
+               "kernels": [(k, n, round(t / tot, 3)) for k, (n, t) in top]}
         print(json.dumps(row), flush=True)
         res[f.__name__] = row
     # the same decode step replayed from a CUDA graph, and its per-part device time from clock
