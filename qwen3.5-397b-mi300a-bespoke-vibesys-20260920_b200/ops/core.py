@@ -128,6 +128,8 @@ def causal_conv_varlen(x, conv_state, w, seg_lane, cu, seg_lane_h=None, cu_h=Non
     cus = cu_h if cu_h is not None else cu.tolist()
     for s, lane in enumerate(lanes):
         a, b = cus[s], cus[s + 1]
+        if b == a:  # an empty segment leaves its lane's window as it is
+            continue
         o, st = ref.causal_conv(x[a:b], conv_state[lane], w)
         out[a:b] = o
         if commit:

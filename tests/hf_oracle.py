@@ -60,13 +60,27 @@ def reference_modeling():
     return mod
 
 
+def _torch_paths_only(mod) -> None:
+    """The oracle runs on host tensors: drop the modeling module's optional GPU kernels (the
+    flash-linear-attention and causal-conv1d packages, which it picks whenever they import, as
+    they do on a GPU box), so its own PyTorch implementations run."""
+    for n in ("causal_conv1d_fn", "causal_conv1d_update", "chunk_gated_delta_rule", "fused_recurrent_gated_delta_rule",
+              "FusedRMSNormGated"):
+        if hasattr(mod, n):
+            setattr(mod, n, None)
+    if hasattr(mod, "is_fast_path_available"):
+        mod.is_fast_path_available = False
+
+
 def build_hf(model_dir: str, dtype=torch.float32, reference: str = "hf"):
     from transformers.models.qwen3_5_moe.configuration_qwen3_5_moe import Qwen3_5MoeTextConfig
 
     if reference == "ref":
-        Qwen3_5MoeForCausalLM = reference_modeling().Qwen3_5MoeForCausalLM
+        mod = reference_modeling()
     else:
-        from transformers.models.qwen3_5_moe.modeling_qwen3_5_moe import Qwen3_5MoeForCausalLM
+        import transformers.models.qwen3_5_moe.modeling_qwen3_5_moe as mod
+    _torch_paths_only(mod)
+    Qwen3_5MoeForCausalLM = mod.Qwen3_5MoeForCausalLM
 
     cfg = load_config(model_dir)
     hcfg = Qwen3_5MoeTextConfig(**{k: v for k, v in to_hf_text_config(cfg).items()
