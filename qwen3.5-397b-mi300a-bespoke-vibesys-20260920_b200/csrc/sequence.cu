@@ -57,7 +57,14 @@ __global__ void conv_out_kernel(const bf16* x, long ldx, const bf16* state, long
     return true;
   };
   if (!load_window(tb)) return;
-  for (int t = tb; t < te; ++t) {
+  // every input of the run in flight at once (the loop below then only waits for the first)
+  float xs[CONV_RUN];
+#pragma unroll
+  for (int i = 0; i < CONV_RUN; ++i) xs[i] = tb + i < te ? __bfloat162float(x[(long)(tb + i) * ldx + c]) : 0.f;
+#pragma unroll
+  for (int i = 0; i < CONV_RUN; ++i) {
+    const int t = tb + i;
+    if (t >= te) break;
     if (t >= t1) {  // the next (non-empty) segment starts: its window comes from its lane's state
       while (t >= t1) {
         ++s;
@@ -66,7 +73,7 @@ __global__ void conv_out_kernel(const bf16* x, long ldx, const bf16* state, long
       }
       if (!load_window(t)) return;
     }
-    const float xt = __bfloat162float(x[(long)t * ldx + c]);
+    const float xt = xs[i];
     float acc = 0.f;
 #pragma unroll
     for (int j = 0; j < K - 1; ++j) acc += wk[j] * win[j];
@@ -74,7 +81,7 @@ __global__ void conv_out_kernel(const bf16* x, long ldx, const bf16* state, long
     const float a = rbf2(acc);
     out[(long)t * C + c] = __float2bfloat16(a / (1.f + expf(-a)));
 #pragma unroll
-    for (int i = 0; i < K - 2; ++i) win[i] = win[i + 1];
+    for (int q = 0; q < K - 2; ++q) win[q] = win[q + 1];
     win[K - 2] = xt;
   }
 }

@@ -246,7 +246,7 @@ def _cache_put(cache: dict, tag: tuple, key, value) -> None:
 
 
 DN_TC_MAX_HEADS = 32
-DN_TC_MIN_TOKENS = 256
+DN_TC_MIN_TOKENS = 128
 
 
 def dn_prefill_mode(nv: int, cu_h=None) -> str:
@@ -254,8 +254,8 @@ def dn_prefill_mode(nv: int, cu_h=None) -> str:
     the tensor-core chunked form up to ``DN_TC_MAX_HEADS`` heads (from 2-way tensor parallelism
     on; at 8 heads it measured 2.5-3.3x faster than the token recurrence for 800-4096 tokens) and,
     at more heads, for batches whose longest segment has at least ``DN_TC_MIN_TOKENS`` tokens
-    (64 heads: 0.95 vs 1.79 ms for 4096 tokens, 0.26 vs 0.36 ms for 800; below a few chunks the
-    prep kernel's latency leaves the two about even and the fp32 recurrence is kept)."""
+    (64 heads: 0.95 vs 1.79 ms for 4096 tokens, 0.26 vs 0.36 for 800, 0.097 vs 0.123 for 256,
+    0.061 vs 0.069 for 128; shorter segments keep the fp32 recurrence)."""
     mode = flags.get("QB_DN_PREFILL")
     if mode == "auto":
         if nv <= DN_TC_MAX_HEADS:
