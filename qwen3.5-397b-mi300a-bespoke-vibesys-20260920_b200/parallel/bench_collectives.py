@@ -248,7 +248,7 @@ def main():
 
     rank, world = commmod.init("nccl")
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
-    if args.case in ("ep", "sp_gemm"):
+    if args.case in ("ep", "sp_gemm", "ag_gemm"):
         if args.tokens == ap.get_default("tokens"):
             args.tokens = [8, 64, 512, 2048, 8192] if args.case == "ep" else [1024, 2048, 4096, 8192, 16384]
         rows = {"ep": ep_sweep, "sp_gemm": sp_gemm_sweep, "ag_gemm": ag_gemm_sweep}[args.case](args, rank, world, dev)

@@ -217,13 +217,13 @@ def test_causal_conv_and_delta_rule():
     exp = ops.causal_conv_varlen(x.cpu(), st2, w.cpu(), torch.tensor(ln), torch.tensor(cu), ln, cu)
     close(out.cpu(), exp, atol=2e-2)
     close(st.cpu(), st2, atol=0)
-    # runs of tokens crossing several segments, an empty segment among them
-    segs_b = [(0, 37), (1, 0), (2, 20), (1, 3)]
+    # runs of tokens crossing several segments, an empty segment among them (one lane per segment)
+    segs_b = [(0, 37), (1, 0), (2, 20), (3, 3)]
     cub = [0]
     for _, n in segs_b:
         cub.append(cub[-1] + n)
     xb = rnd(cub[-1], C, seed=31)
-    stb = rnd(lanes, C, K - 1, seed=32)
+    stb = rnd(len(segs_b), C, K - 1, seed=32)
     stb2 = stb.clone().cpu()
     lnb = [l for l, _ in segs_b]
     outb = ops.causal_conv_varlen(xb, stb, w, torch.tensor(lnb, **i32), torch.tensor(cub, **i32))
