@@ -34,8 +34,9 @@ def test_tp4_gloo_multiturn_matches_hf(tiny_dir, tmp_path):
     assert exact >= len(res["turns"]) // 2, exact
 
 
-def check_teacher_forced(model, prompt, ours, tol=2e-2):
-    """Every generated token is the HF model's top-1 for our own prefix, up to ``tol``.
+def check_teacher_forced(model, prompt, ours, tol=2e-2, flips=0, flip_tol=None):
+    """Every generated token is the HF model's top-1 for our own prefix, up to ``tol`` (at most
+    ``flips`` positions up to ``flip_tol``).
 
     On a random-weight model the router's top-k has near-ties, and a tie flipped by summation
     order changes later logits by ~1e-2; HF's own cached ``generate`` and its uncached forward
@@ -48,7 +49,9 @@ def check_teacher_forced(model, prompt, ours, tol=2e-2):
     top = lg.max(dim=-1).values
     got = lg[torch.arange(len(ours)), torch.tensor(ours)]
     bad = (got < top - tol).nonzero().flatten().tolist()
-    assert not bad, [(i, ours[i], got[i].item(), top[i].item()) for i in bad]
+    info = [(i, ours[i], got[i].item(), top[i].item()) for i in bad]
+    assert len(bad) <= flips, info
+    assert all(top[i] - got[i] <= (flip_tol or tol) for i in bad), info
 
 
 def test_single_process_matches_hf(tiny_dir):
