@@ -201,6 +201,25 @@ def case_deltanet(tokens: int, lanes: int, iters: int, pk: dict, nk: int = 16, n
     return _report(f"deltanet_T{tokens}_B{lanes}", ms, bytes_, flops, pk)
 
 
+def case_conv(tokens: int, iters: int, pk: dict) -> dict:
+    """The DeltaNet causal conv + SiLU of a prefill over ``tokens`` rows of one lane: the conv
+    channels (2 x 16 x 128 + 64 x 128) read as a column slice of the input projection's output
+    rows, as in the model."""
+    C, W = 2 * 16 * 128 + 64 * 128, 20608
+    g = torch.Generator(device="cuda").manual_seed(3)
+    proj = torch.randn(tokens, W, device="cuda", generator=g).to(torch.bfloat16)
+    w = (0.3 * torch.randn(C, 4, device="cuda", generator=g)).to(torch.bfloat16)
+    st = torch.zeros(2, C, 3, device="cuda", dtype=torch.bfloat16)
+    seg = torch.tensor([0], dtype=torch.int32, device="cuda")
+    cu = torch.tensor([0, tokens], dtype=torch.int32, device="cuda")
+    ms = _time(lambda: ops.causal_conv_varlen(proj[:, :C], st, w, seg, cu, [0], [0, tokens], commit=False), iters)
+    byts = 2 * tokens * C * 2  # inputs read once, outputs written once
+    row = {"case": f"conv_T{tokens}", "ms": round(ms, 4), "GB_s": round(byts / ms / 1e6, 1),
+           "hbm_frac": round(byts / ms / 1e6 / pk["hbm_gbs"], 3), "peaks": pk["source"]}
+    print(json.dumps(row), flush=True)
+    return row
+
+
 def case_deltanet_decode(lanes: int, iters: int, pk: dict, nk: int = 16, nv: int = 64, dk: int = 128,
                          dv: int = 128, layers: int = 8) -> dict:
     """The fused one-token-per-lane DeltaNet mixer (conv, l2norm, gated delta step, gated
@@ -307,7 +326,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--case", default="all",
                     choices=["moe", "gemm", "gemm_shapes", "attn_prefill", "attn_decode", "deltanet",
-                             "deltanet_decode", "model", "all"])
+                             "deltanet_decode", "model", "conv", "all"])
     ap.add_argument("--tokens", type=int, default=None)
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--lanes", type=int, default=None)
@@ -333,6 +352,8 @@ def main(argv=None):
         run.append(case_attn_prefill(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.iters, pk))
     if a.case in ("attn_decode", "all"):
         run.append(case_attn_decode(a.lanes or 32, a.ctx or 6000, a.iters, pk))
+    if a.case == "conv":
+        return [case_conv(a.tokens or 2048, a.iters, pk)]
     if a.case == "model":
         return case_model(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.lanes or 32)
     if a.case in ("deltanet_decode", "all"):
