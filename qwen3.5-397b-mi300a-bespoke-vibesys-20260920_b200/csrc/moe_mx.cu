@@ -49,13 +49,16 @@ constexpr int MX_MAX_EXPERTS = 512;  // experts per rank (the model has 512)
 
 // W: the wide path (tiled codes, one box per operand, one hi|lo MMA operand, two scale chunks
 // per stage: weight and activation); else three chunks (weight, hi, lo).
-template <int BN, bool W>
+// KA (wide path only): 128-K atoms per pipeline stage. Two halve the copies, barrier round trips
+// and scale copies per byte (one 256-row weight box, the two atoms' scale chunks in one bulk copy
+// each) for the same bytes in flight.
+template <int BN, bool W, int KA = 1>
 struct MxCfg {
   static constexpr int A = 128 * MX_SK;          // fp4 tile, one byte per code in shared memory
   static constexpr int B = BN * MX_SK;           // one e4m3 token tile (hi or lo)
-  static constexpr int STAGE = A + 2 * B;        // multiple of 1024
-  static constexpr int SF = (W ? 2 : 3) * MX_CHUNK;  // scale chunks per stage
-  static constexpr int SF_COLS = W ? 8 : 12;     // their tensor-memory columns
+  static constexpr int STAGE = KA * (A + 2 * B);  // multiple of 1024: KA weight atoms, then KA hi|lo tiles
+  static constexpr int SF = KA * (W ? 2 : 3) * MX_CHUNK;  // scale chunks per stage
+  static constexpr int SF_COLS = KA * (W ? 8 : 12);       // their tensor-memory columns
   static constexpr int STAGING = BN * 128 * 2;   // one output tile (bf16)
   // token-tile prefix, counts and offsets of the experts in shared memory (16-byte multiple: the
   // mbarriers after it stay aligned)
@@ -142,11 +145,12 @@ struct MxPlanes {
   CUtensorMap m[4];
 };
 
-template <int BN, bool W>
+template <int BN, bool W, int KA = 1>
 __global__ void __launch_bounds__(MX_THREADS, 1)
     moe_mx_kernel(const __grid_constant__ CUtensorMap tmW, const __grid_constant__ CUtensorMap tmH,
                   const __grid_constant__ CUtensorMap tmL, const __grid_constant__ MxPlanes pl, MxArgs a) {
-  using C = MxCfg<BN, W>;
+  using C = MxCfg<BN, W, KA>;
+  static_assert(KA == 1 || W, "two-atom stages: wide path only");
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* stages = smem;
@@ -230,12 +234,12 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         const int row_b = offs[e] + m0;
         const int ne = mx_cols<BN>(cnts[e] - m0);  // the tile's rows, rounded up to 16
         const CUtensorMap* tmP = &pl.m[ne / 16 - 1];
-        const uint32_t TX = C::A / 2 + 2 * ne * MX_SK + 2 * MX_CHUNK;
+        const uint32_t TX = KA * (C::A / 2 + 2 * ne * MX_SK + 2 * MX_CHUNK);
         const int wtile = e * n_tiles + nt;
         int trow = wtile * kstages * 128;  // < 2^31: 512 experts x 32 tiles x 32 stages x 128
         const uint8_t* sfw = a.sfa + (long)wtile * kstages * MX_CHUNK;
         const uint8_t* sfb = a.sfb_hi + (long)tt * kstages * MX_CHUNK;
-        for (int kx = 0; kx < kstages * MX_SK; kx += MX_SK, ++it) {
+        for (int kx = 0; kx < kstages * MX_SK; kx += KA * MX_SK, ++it) {
           const long long w0 = a.probe ? clock64() : 0;
           if (!mbar_wait_s(empty0 + 8 * s, ph, a.err, ERR_TMA_WAIT, abort_flag)) goto prod_done_w;
           if (a.probe) {
@@ -244,13 +248,15 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
           }
           const uint32_t fb = full0 + 8 * s, st = st0 + s * C::STAGE, sf = sf0 + s * C::SF;
           mbar_expect_tx_s(fb, TX);
-          tma_load_2d_s(st, &tmW, fb, 0, trow);
-          tma_load_3d_s(st + C::A, tmP, fb, kx, row_b, 0);  // ne hi rows, then ne lo rows
-          bulk_g2s_s(sf, sfw, MX_CHUNK, fb);
-          bulk_g2s_s(sf + MX_CHUNK, sfb, MX_CHUNK, fb);
-          trow += 128;
-          sfw += MX_CHUNK;
-          sfb += MX_CHUNK;
+          tma_load_2d_s(st, &tmW, fb, 0, trow);  // KA consecutive 128-row blocks of the tile
+#pragma unroll
+          for (int j = 0; j < KA; ++j)  // atom j: ne hi rows, then ne lo rows
+            tma_load_3d_s(st + KA * C::A + j * 2 * ne * MX_SK, tmP, fb, kx + j * MX_SK, row_b, 0);
+          bulk_g2s_s(sf, sfw, KA * MX_CHUNK, fb);  // the atoms' chunks are consecutive in memory
+          bulk_g2s_s(sf + KA * MX_CHUNK, sfb, KA * MX_CHUNK, fb);
+          trow += KA * 128;
+          sfw += KA * MX_CHUNK;
+          sfb += KA * MX_CHUNK;
           *issued_p = it + 1;
           if (a.probe) pi += clock64() - w1;
           if (++s == C::STAGES) {
@@ -337,7 +343,7 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
     if (W && elect_one()) {
       const uint32_t full0 = smem_u32(full), empty0 = smem_u32(empty), accf0 = smem_u32(acc_full),
                      acce0 = smem_u32(acc_empty);
-      const uint64_t da0 = desc_sw128(smem_u32(stages)), db0 = desc_sw128(smem_u32(stages) + C::A);
+      const uint64_t da0 = desc_sw128(smem_u32(stages));
       const uint32_t sf_s0 = smem_u32(sfs);
       int s = 0, ti = 0, e = 0;
       uint32_t ph = 0;
@@ -348,14 +354,15 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
         int nt, tt;
         unit(u, e, nt, tt);
         // hi | lo rows of the tile: one N = 2 ne operand (lo products in columns [ne, 2 ne))
-        const uint32_t idesc = idesc_mxf8f6f4(2 * mx_cols<BN>(cnts[e] - (tt - tstart[e]) * BN));
+        const int ne = mx_cols<BN>(cnts[e] - (tt - tstart[e]) * BN);
+        const uint32_t idesc = idesc_mxf8f6f4(2 * ne);
         const int acc = ti & 1;
         const long long a0 = a.probe ? clock64() : 0;
         if (!mbar_wait_s(acce0 + 8 * acc, ((ti >> 1) & 1) ^ 1, a.err, ERR_ACC_WAIT, abort_flag)) break;
         if (a.probe) aw += clock64() - a0;
         tc_fence_after();
         const uint32_t d = tmem + acc * C::ACC;
-        for (int ks = 0; ks < kstages; ++ks) {
+        for (int ks = 0; ks < kstages; ks += KA) {
           const long long w0 = a.probe ? clock64() : 0;
           if (!mbar_wait_s(full0 + 8 * s, ph, a.err, ERR_MMA_WAIT, abort_flag)) {
             ok = false;
@@ -368,14 +375,20 @@ __global__ void __launch_bounds__(MX_THREADS, 1)
           tc_fence_after();
           const uint32_t sf_t = tmem + C::SF_COL + s * C::SF_COLS, sf_s = sf_s0 + s * C::SF;
           const uint64_t so = (uint64_t)((s * C::STAGE) >> 4);  // descriptor address field: bytes / 16
-          const uint64_t da = da0 + so, dh = db0 + so;
-          tmem_cp_chunk(sf_t, sf_s);
-          tmem_cp_chunk(sf_t + 4, sf_s + MX_CHUNK);
+          const uint64_t da = da0 + so, dh = da0 + so + (uint64_t)((KA * C::A) >> 4);
+          // KA weight scale chunks, then KA activation chunks: 4 tensor-memory columns each
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {  // K-block j: hi | lo products into accumulator columns [0, 2 BN)
-            const uint32_t id_j = idesc | ((uint32_t)j << 29) | ((uint32_t)j << 4);
-            const uint32_t bsel = (uint32_t)j << 30;
-            mma_mx(d, da + 2 * j, dh + 2 * j, id_j, (sf_t) | bsel, (sf_t + 4) | bsel, (ks | j) != 0);
+          for (int c = 0; c < 2 * KA; ++c) tmem_cp_chunk(sf_t + 4 * c, sf_s + c * MX_CHUNK);
+#pragma unroll
+          for (int at = 0; at < KA; ++at) {
+            const uint64_t dat = da + (uint64_t)((at * C::A) >> 4), dht = dh + (uint64_t)((at * 2 * ne * MX_SK) >> 4);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {  // K-block j: hi | lo products into accumulator columns [0, 2 ne)
+              const uint32_t id_j = idesc | ((uint32_t)j << 29) | ((uint32_t)j << 4);
+              const uint32_t bsel = (uint32_t)j << 30;
+              mma_mx(d, dat + 2 * j, dht + 2 * j, id_j, (sf_t + 4 * at) | bsel, (sf_t + 4 * KA + 4 * at) | bsel,
+                     (ks | at | j) != 0);
+            }
           }
           mma_commit_s(empty0 + 8 * s);
           if (a.probe) mi += clock64() - m1;
@@ -779,11 +792,11 @@ static int mx_sms() {
   return n;
 }
 
-template <int BN, bool W>
+template <int BN, bool W, int KA = 1>
 static int mx_launch(const CUtensorMap& tw, const CUtensorMap& th, const CUtensorMap& tl, const MxPlanes& pl,
                      const MxArgs& a, cudaStream_t st) {
-  using C = MxCfg<BN, W>;
-  auto k = moe_mx_kernel<BN, W>;
+  using C = MxCfg<BN, W, KA>;
+  auto k = moe_mx_kernel<BN, W, KA>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
@@ -857,7 +870,10 @@ int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, cons
   // row-major codes [count * n_rows][K/2 bytes], or tiled: [count * n_rows * K/128][64 bytes]
   const bool wide = mx_merged(tiled, BN);
   if (wide && (lo <= hi || ((lo - hi) & 15))) return -3;
-  int r = tiled ? mx_tmap(&tw, wq, (long)count * n_rows * (K / MX_SK), MX_SK, MX_SK / 2, wide ? 128 : 64, true)
+  // two 128-K atoms per stage (QB_MX_K2=1, wide path, an even number of atoms)
+  static const bool k2_env = getenv("QB_MX_K2") && atoi(getenv("QB_MX_K2")) != 0;
+  const int ka = (wide && k2_env && (K / MX_SK) % 2 == 0) ? 2 : 1;
+  int r = tiled ? mx_tmap(&tw, wq, (long)count * n_rows * (K / MX_SK), MX_SK, MX_SK / 2, wide ? 128 * ka : 64, true)
                 : mx_tmap(&tw, wq, (long)count * n_rows, K, K / 2, 64, true);
   if (r) return 1000 + r;
   r = wide ? mx_tmap_planes(&th, hi, cap, K, lo - hi, BN) : mx_tmap(&th, hi, cap, K, K, 16, false);
@@ -873,9 +889,12 @@ int moe_mx_gemm(const uint8_t* hi, const uint8_t* lo, const uint8_t* sf_hi, cons
   MxArgs a{sfa, sf_hi, sf_lo, offsets, counts, tstart, out, out_cols, n_rows, K, count, act, err, tiled ? 1 : 0,
            wide ? 1 : 0, probe};
   switch (BN) {
-    case 16: return wide ? mx_launch<16, true>(tw, th, tl, pl, a, s) : mx_launch<16, false>(tw, th, tl, pl, a, s);
-    case 32: return wide ? mx_launch<32, true>(tw, th, tl, pl, a, s) : mx_launch<32, false>(tw, th, tl, pl, a, s);
-    case 64: return wide ? mx_launch<64, true>(tw, th, tl, pl, a, s) : mx_launch<64, false>(tw, th, tl, pl, a, s);
+    case 16: return !wide ? mx_launch<16, false>(tw, th, tl, pl, a, s)
+                 : ka == 2 ? mx_launch<16, true, 2>(tw, th, tl, pl, a, s) : mx_launch<16, true>(tw, th, tl, pl, a, s);
+    case 32: return !wide ? mx_launch<32, false>(tw, th, tl, pl, a, s)
+                 : ka == 2 ? mx_launch<32, true, 2>(tw, th, tl, pl, a, s) : mx_launch<32, true>(tw, th, tl, pl, a, s);
+    case 64: return !wide ? mx_launch<64, false>(tw, th, tl, pl, a, s)
+                 : ka == 2 ? mx_launch<64, true, 2>(tw, th, tl, pl, a, s) : mx_launch<64, true>(tw, th, tl, pl, a, s);
     default: return mx_launch<128, false>(tw, th, tl, pl, a, s);
   }
 }
