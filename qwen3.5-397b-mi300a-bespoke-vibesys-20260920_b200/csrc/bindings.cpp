@@ -426,7 +426,9 @@ Tensor moe_routed_bf16(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor w2
 // sparse_rows: many rows are routed nowhere (expert ids -1, an expert-parallel receive area):
 // they are neither quantised nor written.
 void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
-                        int64_t first, int64_t count, bool tiled, Tensor out, bool sparse_rows = false) {
+                        int64_t first, int64_t count, bool tiled, Tensor out, bool sparse_rows = false,
+                        const c10::optional<Tensor>& shared = c10::nullopt,
+                        const c10::optional<Tensor>& gate = c10::nullopt) {
   CHECK_BF16(h);
   TORCH_CHECK(h.is_contiguous() && out.is_contiguous(), "moe: h and out contiguous");
   const int T = h.size(0), H = h.size(1), k = topi.size(1);
@@ -469,17 +471,24 @@ void moe_routed_mx_into(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s
                       slp, stream(), merged));
   LAUNCH(qb::moe_mx_gemm(hp, lp, shp, slp, cap, w2.data_ptr<uint8_t>(), s2c.data_ptr<uint8_t>(), H, I, offsets,
                          counts, tstart, count, BN, 0, y2.data_ptr(), H, err_ptr(h), stream(), tiled));
+  const bool with_shared = shared.has_value() && gate.has_value();
+  if (with_shared)
+    TORCH_CHECK(!sparse_rows && shared->is_contiguous() && shared->sizes() == h.sizes() && gate->dim() == 1 &&
+                    gate->size(0) == T && gate->scalar_type() == at::kBFloat16,
+                "moe: shared [T, H] contiguous and gate logits [T] bf16");
   LAUNCH(qb::moe_combine(y2.data_ptr(), inv, topw.contiguous().data_ptr<float>(), T, k, H, out.data_ptr(), stream(),
-                         sparse_rows));
+                         sparse_rows, with_shared ? shared->data_ptr() : nullptr,
+                         with_shared ? gate->data_ptr() : nullptr, with_shared ? gate->stride(0) : 0));
   scratch_check(meta);
   scratch_check(hl);
   scratch_check(sf);
 }
 
 Tensor moe_routed_mx(Tensor h, Tensor topw, Tensor topi, Tensor w13, Tensor s13c, Tensor w2, Tensor s2c,
-                     int64_t first, int64_t count, bool tiled) {
+                     int64_t first, int64_t count, bool tiled, c10::optional<Tensor> shared,
+                     c10::optional<Tensor> gate) {
   Tensor out = at::empty_like(h);
-  moe_routed_mx_into(h, topw, topi, w13, s13c, w2, s2c, first, count, tiled, out);
+  moe_routed_mx_into(h, topw, topi, w13, s13c, w2, s2c, first, count, tiled, out, false, shared, gate);
   return out;
 }
 
@@ -709,7 +718,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("qk_norm_rope_kv_write", &qk_norm_rope_kv_write);
   m.def("attention_varlen", &attention_varlen);
   m.def("attention_fa", &attention_fa);
-  m.def("moe_routed_mx", &moe_routed_mx);
+  m.def("moe_routed_mx", &moe_routed_mx, py::arg("h"), py::arg("topw"), py::arg("topi"), py::arg("w13"),
+        py::arg("s13c"), py::arg("w2"), py::arg("s2c"), py::arg("first"), py::arg("count"), py::arg("tiled"),
+        py::arg("shared") = py::none(), py::arg("gate") = py::none());
   m.def("stamp", &stamp);
   m.def("mx_probe", []() {
     Tensor t = at::zeros({8}, at::kLong);

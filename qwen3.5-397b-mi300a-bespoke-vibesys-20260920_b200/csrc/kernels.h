@@ -157,8 +157,9 @@ int moe_expert_gemm(const void* xin, int in_cols, const uint8_t* wq, const uint8
                     int count, int cap, int act, void* out, int out_cols, int* err, cudaStream_t s, int max_ctas);
 int moe_gather_bf16(const void* h, const int* perm_tok, const int* n_assign, int cap, int H, void* xh,
                     cudaStream_t s);
+// shared (optional, with gl / ldgl): add bf16(sigmoid(gate)) x shared to every combined row
 int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s,
-                bool skip_empty = false);
+                bool skip_empty = false, const void* shared = nullptr, const void* gl = nullptr, long ldgl = 0);
 int moe_expert_gemm_bf16(const void* xin, int in_cols, const void* w, int n_rows, int k_cols, long w_expert_stride,
                          const int* offsets, const int* counts, int count, int cap, int act, void* out, int out_cols,
                          cudaStream_t s);

@@ -160,8 +160,11 @@ int moe_gather_bf16(const void* h, const int* perm_tok, const int* n_assign, int
 }
 
 // out[t, :] = sum_j topw[t, j] * y2[inv[t, j], :] over local assignments (fp32, rounded once)
+// shared (optional): the shared expert's output rows and their gate logits (gl, ldgl apart): the
+// row becomes bf16(routed) + bf16(bf16(sigmoid(gate)) * shared), the same bits as
+// shared_gate_combine after the routed sum, without the extra pass over the rows.
 __global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* topw, int k, int H, bf16* out,
-                                   bool skip_empty) {
+                                   bool skip_empty, const bf16* shared, const bf16* gl, long ldgl) {
   const long t = blockIdx.x;
   if (skip_empty) {  // rows no expert of this rank serves are left unwritten (nobody reads them)
     bool any = false;
@@ -186,16 +189,28 @@ __global__ void moe_combine_kernel(const bf16* y2, const int* inv, const float* 
     bf16* oe = reinterpret_cast<bf16*>(&o);
 #pragma unroll
     for (int u = 0; u < 8; ++u) oe[u] = __float2bfloat16(acc[u]);
+    if (shared != nullptr) {
+      const float g = __bfloat162float(gl[t * ldgl]);
+      const float sg = __bfloat162float(__float2bfloat16(1.f / (1.f + expf(-g))));
+      const uint4 sr = *reinterpret_cast<const uint4*>(shared + t * H + i);
+      const bf16* se = reinterpret_cast<const bf16*>(&sr);
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const float sh = __bfloat162float(__float2bfloat16(sg * __bfloat162float(se[u])));
+        oe[u] = __float2bfloat16(__bfloat162float(oe[u]) + sh);
+      }
+    }
     *reinterpret_cast<uint4*>(out + t * H + i) = o;
   }
 }
 
 int moe_combine(const void* y2, const int* inv, const float* topw, int T, int k, int H, void* out, cudaStream_t s,
-                bool skip_empty) {
+                bool skip_empty, const void* shared, const void* gl, long ldgl) {
   if (!T) return 0;
   int split = 1;  // row chunks of at least 1024 columns (multiples of 8) until ~2 blocks per SM
   while (T * split < 296 && H / (split * 2) >= 1024 && (H / (split * 2)) % 8 == 0) split *= 2;
-  moe_combine_kernel<<<dim3(T, split), 128, 0, s>>>((const bf16*)y2, inv, topw, k, H, (bf16*)out, skip_empty);
+  moe_combine_kernel<<<dim3(T, split), 128, 0, s>>>((const bf16*)y2, inv, topw, k, H, (bf16*)out, skip_empty,
+                                                     (const bf16*)shared, (const bf16*)gl, ldgl);
   return (int)cudaGetLastError();
 }
 

@@ -353,13 +353,15 @@ class Model:
         drop = self.fault.get("drop_expert")
         if drop is not None:
             topw = torch.where(topi == int(drop), torch.zeros_like(topw), topw)
-        routed = ops.moe_routed(h, topw, topi, L["experts"], p.experts.start, p.experts.count)
-        self._dstamp("moe.routed")
         if g13 is None:
             g13 = ops.linear(h, L["w_sh13"])
         sh = ops.linear(ops.silu_mul(g13), L["w_sh2"])
         self._dstamp("moe.shared")
-        return ops.shared_gate_combine(routed, sh, rl[:, cfg.experts])
+        # routed experts; their combine also adds sigmoid(gate) x the shared expert's rows
+        out = ops.moe_routed(h, topw, topi, L["experts"], p.experts.start, p.experts.count, shared=sh,
+                             gate=rl[:, cfg.experts])
+        self._dstamp("moe.routed")
+        return out
 
     def _layers(self, x: torch.Tensor, b: StepInputs) -> tuple[torch.Tensor, torch.Tensor]:
         cfg, comm, layers = self.cfg, self.comm, self.w["layers"]

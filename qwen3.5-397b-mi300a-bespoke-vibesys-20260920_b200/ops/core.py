@@ -418,25 +418,29 @@ def moe_impl() -> str:
     return flags.get("QB_MOE_IMPL")
 
 
-def moe_routed(h, topw, topi, experts, first, count):
+def moe_routed(h, topw, topi, experts, first, count, shared=None, gate=None):
     """Sum of this rank's experts' weighted outputs for each row (zero for rows routed only to
-    other ranks' experts). fp32 accumulation, rounded once to ``h.dtype``."""
+    other ranks' experts). fp32 accumulation, rounded once to ``h.dtype``. With ``shared`` and
+    ``gate`` (the shared expert's rows and gate logits): ``+ sigmoid(gate) * shared``, as
+    ``shared_gate_combine`` gives it; the block-scaled path adds it in its combine kernel."""
     if _cuda(h):
         if "s13c" in experts and (moe_impl() == "mx" or "s13" not in experts):
-            if "w13t" in experts:
-                return ext().moe_routed_mx(h, topw, topi, experts["w13t"], experts["s13c"], experts["w2t"],
-                                           experts["s2c"], first, count, True)
-            return ext().moe_routed_mx(h, topw, topi, experts["w13"], experts["s13c"], experts["w2"],
-                                       experts["s2c"], first, count, bool(experts.get("tiled", False)))
+            w13, w2, tiled = (experts["w13t"], experts["w2t"], True) if "w13t" in experts else \
+                (experts["w13"], experts["w2"], bool(experts.get("tiled", False)))
+            return ext().moe_routed_mx(h, topw, topi, w13, experts["s13c"], w2, experts["s2c"], first, count,
+                                       tiled, shared, gate)
         if "s13" in experts and moe_impl() == "mx" and h.shape[1] % 128 == 0 \
                 and experts["w2"].shape[2] * 2 % 128 == 0:
             prepare_experts(experts, keep_rows=True)
-            return moe_routed(h, topw, topi, experts, first, count)
+            return moe_routed(h, topw, topi, experts, first, count, shared, gate)
+        if shared is not None:
+            return shared_gate_combine(moe_routed(h, topw, topi, experts, first, count), shared, gate)
         if "s13" in experts:
             return ext().moe_routed_fp4(h, topw, topi, experts["w13"], experts["s13"], experts["w2"], experts["s2"],
                                         first, count)
         return ext().moe_routed_bf16(h, topw, topi, experts["w13"], experts["w2"], first, count)
-    return ref.routed_experts(h, topw, topi.long(), experts, first, count)
+    routed = ref.routed_experts(h, topw, topi.long(), experts, first, count)
+    return routed if shared is None else shared_gate_combine(routed, shared, gate)
 
 
 def shared_gate_combine(routed, shared, gate_logit):

@@ -269,6 +269,13 @@ def test_moe_routed_mxfp4(T, E, k, H, I, impl, monkeypatch):
     torch.cuda.synchronize()
     exp = ref.routed_experts(h, topw, topi.long(), experts, first, count)
     close(out, exp, rtol=3e-2, atol=3e-3)
+    # the shared expert added in the combine: the same bits as the separate gate-and-add kernel
+    sh = rnd(T, H, seed=T + 2)
+    gl = rnd(T, 3, seed=T + 3)[:, 1]  # a strided column, as the router projection gives it
+    fused = ops.moe_routed(h, topw, topi, experts, first, count, shared=sh, gate=gl)
+    apart = ops.shared_gate_combine(ops.moe_routed(h, topw, topi, experts, first, count), sh, gl)
+    torch.cuda.synchronize()
+    assert torch.equal(fused, apart), (fused.float() - apart.float()).abs().max().item()
     status_ok()
 
 
