@@ -585,7 +585,7 @@ void symm_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor partia
 
 void symm_sp_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor partial, Tensor res, Tensor w1p, Tensor out,
                          double eps, int64_t slot_elems, int64_t max_blocks, Tensor epoch, double timeout_s,
-                         bool own) {
+                         bool own, bool res_local) {
   CHECK_BF16(partial);
   CHECK_BF16(res);
   TORCH_CHECK(res.is_contiguous() && out.is_contiguous() && partial.stride(-1) == 1, "symm_sp_ar: layouts");
@@ -597,7 +597,7 @@ void symm_sp_ar_add_rmsnorm(std::vector<int64_t> bases, int64_t rank, Tensor par
   LAUNCH(qb::symm_sp_ar_add_rmsnorm(b.data(), (int)b.size(), (int)rank, partial.data_ptr(), partial.stride(0),
                                  res.data_ptr(), w1p.data_ptr<float>(), out.data_ptr(), rows, H, (float)eps,
                                  slot_elems, (int)max_blocks, ep, ep + 1, err_ptr(res),
-                                 (unsigned long long)(timeout_s * 1e9), stream(), own));
+                                 (unsigned long long)(timeout_s * 1e9), stream(), own, res_local));
 }
 
 // All-gather -> GEMM after the owner-only sequence-parallel call (own=true above): y[rows, N] =
@@ -656,7 +656,7 @@ int64_t nvls_region_bytes(int64_t slot_elems) { return qb::nvls_region_bytes(slo
 // of the sequence-parallel kernel reduces them. Same bits as linear + symm_sp_ar_add_rmsnorm.
 void symm_linear_sp_ar_add_rmsnorm(Tensor x, Tensor w, std::vector<int64_t> bases, int64_t rank, Tensor res,
                                    Tensor w1p, Tensor out, double eps, int64_t slot_elems, int64_t max_blocks,
-                                   Tensor epoch, double timeout_s) {
+                                   Tensor epoch, double timeout_s, bool res_local) {
   CHECK_BF16(x);
   CHECK_BF16(w);
   CHECK_BF16(res);
@@ -692,7 +692,7 @@ void symm_linear_sp_ar_add_rmsnorm(Tensor x, Tensor w, std::vector<int64_t> base
   for (int i = 0; i < world; ++i) b[i] = reinterpret_cast<void*>(bases[i]);
   LAUNCH(qb::symm_sp_rs_add_rmsnorm(b.data(), world, (int)rank, per, res.data_ptr(), w1p.data_ptr<float>(),
                                     out.data_ptr(), rows, H, (float)eps, slot_elems, (int)max_blocks, ep, ep + 1,
-                                    err_ptr(res), (unsigned long long)(timeout_s * 1e9), stream()));
+                                    err_ptr(res), (unsigned long long)(timeout_s * 1e9), stream(), res_local));
 }
 
 // ------------------------------------------------------------------ status
@@ -744,9 +744,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_ar_add_rmsnorm", &symm_ar_add_rmsnorm);
   m.def("symm_sp_ar_add_rmsnorm", &symm_sp_ar_add_rmsnorm, py::arg("bases"), py::arg("rank"), py::arg("partial"),
         py::arg("res"), py::arg("w1p"), py::arg("out"), py::arg("eps"), py::arg("slot_elems"), py::arg("max_blocks"),
-        py::arg("epoch"), py::arg("timeout_s"), py::arg("own") = false);
+        py::arg("epoch"), py::arg("timeout_s"), py::arg("own") = false, py::arg("res_local") = false);
   m.def("symm_gemm_ag", &symm_gemm_ag);
-  m.def("symm_linear_sp_ar_add_rmsnorm", &symm_linear_sp_ar_add_rmsnorm);
+  m.def("symm_linear_sp_ar_add_rmsnorm", &symm_linear_sp_ar_add_rmsnorm, py::arg("x"), py::arg("w"), py::arg("bases"),
+        py::arg("rank"), py::arg("res"), py::arg("w1p"), py::arg("out"), py::arg("eps"), py::arg("slot_elems"),
+        py::arg("max_blocks"), py::arg("epoch"), py::arg("timeout_s"), py::arg("res_local") = false);
   m.def("nvls_ar_add_rmsnorm", &nvls_ar_add_rmsnorm);
   m.def("nvls_region_bytes", &nvls_region_bytes);
   m.def("launches", &launches, "number of kernels launched through the bindings so far");

@@ -180,6 +180,11 @@ __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
 // PUSHED: the projection GEMM before this kernel already stored its rows into the owners' slots
 // (gemm.cu, GemmPush), so phase A only publishes (the GEMM's stores completed with that kernel).
 // Either way phase B reads local memory only.
+// res_local (runtime): the residual stays sequence-parallel: phase B stores only the normed rows
+// into the peers' result areas and phase C copies only those, so every rank's `res` holds the new
+// residual on its own range only (the next sequence-parallel call reads and writes only that
+// range); half the gather traffic. The caller keeps it off for the last call of a forward, whose
+// residual rows are read elsewhere.
 // OWN (all-gather left to the next GEMM): phase B writes the new residual and normed rows of this
 // rank's range to the local tensors only, and the normed rows also into this rank's own result
 // area; there is no phase C. The last block to finish raises this rank's ready word to e (after
@@ -210,7 +215,7 @@ template <bool PUSHED, bool OWN>
 __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
     SymmPtrs ptrs, const bf16* partial, long ldp, bf16* res, const float* w1p, bf16* out, int rows, int H,
     float eps, long slot_elems, int max_blocks, int* epoch, int* done, int* err, unsigned long long timeout_ns,
-    int per) {
+    int per, bool res_local) {
   __shared__ float red[32];
   __shared__ int s_epoch;
   if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile int*>(epoch) + 1;
@@ -286,7 +291,7 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
             ss += acc[c * 8 + u] * acc[c * 8 + u];
           }
           *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr;
-          if (!OWN) {
+          if (!OWN && !res_local) {
 #pragma unroll
             for (int p = 0; p < 8; ++p)
               if (p < W && p != me) *reinterpret_cast<uint4*>(peer_res[p] + (long)row * 2 * H + i) = nr;
@@ -337,7 +342,7 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
           for (int c = 0; c < 2; ++c) {
             const int i = (threadIdx.x + c * AR_THREADS) * 8;
             if (i < H) {
-              nr[c] = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + i));
+              if (!res_local) nr[c] = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + i));
               o[c] = __ldcv(reinterpret_cast<const uint4*>(pr + (long)row * 2 * H + H + i));
             }
           }
@@ -345,7 +350,7 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
           for (int c = 0; c < 2; ++c) {
             const int i = (threadIdx.x + c * AR_THREADS) * 8;
             if (i < H) {
-              *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr[c];
+              if (!res_local) *reinterpret_cast<uint4*>(res + (long)row * H + i) = nr[c];
               *reinterpret_cast<uint4*>(out + (long)row * H + i) = o[c];
             }
           }
@@ -373,7 +378,8 @@ __global__ void __launch_bounds__(AR_THREADS) sp_ar_add_rmsnorm_kernel(
 
 int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                            const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
-                           int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s, bool own) {
+                           int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s, bool own,
+                           bool res_local) {
   const int per = (rows + world - 1) / world;  // rows of one rank's range: one block per row, up to max_blocks
   if (world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || (long)per * world * H > slot_elems) return -1;
   SymmPtrs p{};
@@ -385,17 +391,18 @@ int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* 
   if (own)
     sp_ar_add_rmsnorm_kernel<false, true><<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res, w1p,
                                                                      (bf16*)out, rows, H, eps, slot_elems, max_blocks,
-                                                                     epoch, done, err, timeout_ns, per);
+                                                                     epoch, done, err, timeout_ns, per, true);
   else
     sp_ar_add_rmsnorm_kernel<false, false><<<grid, AR_THREADS, 0, s>>>(p, (const bf16*)partial, ldp, (bf16*)res,
                                                                       w1p, (bf16*)out, rows, H, eps, slot_elems,
-                                                                      max_blocks, epoch, done, err, timeout_ns, per);
+                                                                      max_blocks, epoch, done, err, timeout_ns, per,
+                                                                      res_local);
   return (int)cudaGetLastError();
 }
 
 int symm_sp_rs_add_rmsnorm(void* const* bases, int world, int rank, int per, void* res, const float* w1p, void* out,
                            int rows, int H, float eps, long slot_elems, int max_blocks, int* epoch, int* done,
-                           int* err, unsigned long long timeout_ns, cudaStream_t s) {
+                           int* err, unsigned long long timeout_ns, cudaStream_t s, bool res_local) {
   if (world > 8 || H % 8 || H > 2 * AR_THREADS * 8 || per < 1 || (long)per * world < rows ||
       (long)per * world * H > slot_elems)
     return -1;
@@ -407,7 +414,7 @@ int symm_sp_rs_add_rmsnorm(void* const* bases, int world, int rank, int per, voi
   if (grid < 1) grid = 1;
   sp_ar_add_rmsnorm_kernel<true, false><<<grid, AR_THREADS, 0, s>>>(p, nullptr, 0, (bf16*)res, w1p, (bf16*)out, rows, H,
                                                              eps, slot_elems, max_blocks, epoch, done, err,
-                                                             timeout_ns, per);
+                                                             timeout_ns, per, res_local);
   return (int)cudaGetLastError();
 }
 

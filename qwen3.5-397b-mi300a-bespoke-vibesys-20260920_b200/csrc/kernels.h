@@ -172,7 +172,7 @@ int symm_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* par
 int symm_sp_ar_add_rmsnorm(void* const* bases, int world, int rank, const void* partial, long ldp, void* res,
                         const float* w1p, void* out, int rows, int H, float eps, long slot_elems, int max_blocks,
                         int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s,
-                        bool own = false);
+                        bool own = false, bool res_local = false);
 // the same after a GEMM that pushed its rows into the owners' slots (GemmPush, per rows a rank)
 // NVLS: switch-reduced all-reduce + residual add + RMSNorm over a multicast-bound region.
 long nvls_region_bytes(long slot_elems);
@@ -181,6 +181,6 @@ int nvls_ar_add_rmsnorm(void* uc, void* mc, int world, int rank, const void* par
                         int* epoch, int* done, int* err, unsigned long long timeout_ns, cudaStream_t s);
 int symm_sp_rs_add_rmsnorm(void* const* bases, int world, int rank, int per, void* res, const float* w1p, void* out,
                            int rows, int H, float eps, long slot_elems, int max_blocks, int* epoch, int* done,
-                           int* err, unsigned long long timeout_ns, cudaStream_t s);
+                           int* err, unsigned long long timeout_ns, cudaStream_t s, bool res_local = false);
 
 }  // namespace qb

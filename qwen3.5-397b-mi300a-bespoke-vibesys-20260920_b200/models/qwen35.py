@@ -37,6 +37,7 @@ import torch
 
 from ..ops import core as ops
 from ..parallel.comm import Comm
+from ..utils import flags
 from ..parallel.plan import Plan
 from .config import FULL, Qwen35Config
 
@@ -126,6 +127,7 @@ class Model:
         self.gpu_marks = None  # list -> CUDA events at each input upload ("in") and result read ("out")
         self.stamps = None  # utils.telemetry.Stamps -> in-graph clock stamps at layer boundaries
         self._defer_out = False  # set inside _layers while the out projections fuse into the all-reduce
+        self.fuse_shared = bool(flags.get("QB_MOE_FUSE_SHARED"))  # shared expert added in the routed combine
         self.status_watch = None  # utils.devstatus.StatusWatch (CUDA): polled by the scheduler / workers
 
     def _gpu_mark(self, tag: str) -> None:
@@ -357,6 +359,10 @@ class Model:
             g13 = ops.linear(h, L["w_sh13"])
         sh = ops.linear(ops.silu_mul(g13), L["w_sh2"])
         self._dstamp("moe.shared")
+        if not self.fuse_shared:
+            routed = ops.moe_routed(h, topw, topi, L["experts"], p.experts.start, p.experts.count)
+            self._dstamp("moe.routed")
+            return ops.shared_gate_combine(routed, sh, rl[:, cfg.experts])
         # routed experts; their combine also adds sigmoid(gate) x the shared expert's rows
         out = ops.moe_routed(h, topw, topi, L["experts"], p.experts.start, p.experts.count, shared=sh,
                              gate=rl[:, cfg.experts])
@@ -376,10 +382,12 @@ class Model:
             finally:
                 self._defer_out = False
             self._stamp("attention" if full else "deltanet")
+            # the residual after this all-reduce is read only by the next one (QB_SP_RES_LOCAL lets
+            # sequence-parallel sizes keep it on each rank's own rows)
             if isinstance(mix, _Deferred):
-                x, h = comm.linear_allreduce_add_rmsnorm(mix.x, mix.w, x, L["post_norm"], cfg.eps)
+                x, h = comm.linear_allreduce_add_rmsnorm(mix.x, mix.w, x, L["post_norm"], cfg.eps, res_local=True)
             else:
-                x, h = comm.allreduce_add_rmsnorm(mix, x, L["post_norm"], cfg.eps)
+                x, h = comm.allreduce_add_rmsnorm(mix, x, L["post_norm"], cfg.eps, res_local=True)
             self._stamp("allreduce")
             m = self._moe(L, h)
             self._stamp("moe")
@@ -387,7 +395,8 @@ class Model:
             # before another layer, h only feeds its input projection: that GEMM may do the
             # all-gather itself (QB_AG_GEMM; the residual then stays on this rank's rows until the
             # next all-reduce, which reads only those)
-            x, h = comm.allreduce_add_rmsnorm(m, x, nxt, cfg.eps, gather_out=i + 1 < len(layers))
+            last = i + 1 == len(layers)  # the forward's last residual is read as a whole (MTP seed rows)
+            x, h = comm.allreduce_add_rmsnorm(m, x, nxt, cfg.eps, gather_out=not last, res_local=not last)
             self._stamp("allreduce")
         return x, h
 

@@ -70,6 +70,7 @@ class Comm:
         self.mode = flags.get("QB_COMM")
         self.sp_gemm = flags.get("QB_SP_GEMM")
         self.ag_gemm = flags.get("QB_AG_GEMM")
+        self.sp_res_local = flags.get("QB_SP_RES_LOCAL")
 
     # ------------------------------------------------------------------ primitives
     def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
@@ -104,16 +105,20 @@ class Comm:
 
     # ------------------------------------------------------------------ fused
     def allreduce_add_rmsnorm(self, partial: torch.Tensor, residual: torch.Tensor, w1p: torch.Tensor,
-                              eps: float, gather_out: bool = False) -> tuple[torch.Tensor, torch.Tensor]:
+                              eps: float, gather_out: bool = False, res_local: bool = False
+                              ) -> tuple[torch.Tensor, torch.Tensor]:
         """``residual + sum_ranks(partial)`` and its RMSNorm; returns (residual, normed). With
         ``gather_out`` (the caller's only use of ``normed`` is one projection) and
         ``QB_AG_GEMM``, sequence-parallel sizes return the owner-only form: ``residual`` valid on
         this rank's rows only and ``normed`` a ``GatheredRows`` whose ``linear`` gathers inside
-        the GEMM."""
+        the GEMM. With ``res_local`` (the residual is next read only by another sequence-parallel
+        call) and ``QB_SP_RES_LOCAL``, the sequence-parallel kernel gathers only the normed rows and
+        ``residual`` stays valid on this rank's rows."""
         if self.world > 1 and partial.is_cuda and self.symm is not None and self.mode == "fused":
             rows = residual.numel() // residual.shape[-1]
             own = gather_out and self.ag_gemm and self.symm.gathers(rows)
-            got = self.symm.allreduce_add_rmsnorm(partial, residual, w1p, eps, gather_out=own)
+            got = self.symm.allreduce_add_rmsnorm(partial, residual, w1p, eps, gather_out=own,
+                                                  res_local=res_local and self.sp_res_local)
             if got is not None:
                 return got
         summed = self.all_reduce(partial)
@@ -126,13 +131,16 @@ class Comm:
                 and str(self.device).startswith("cuda") and self.symm.fuses_linear(rows))
 
     def linear_allreduce_add_rmsnorm(self, x: torch.Tensor, w: torch.Tensor, residual: torch.Tensor,
-                                     w1p: torch.Tensor, eps: float) -> tuple[torch.Tensor, torch.Tensor]:
-        """``residual + sum_ranks(x @ w^T)`` and its RMSNorm, for a row-parallel projection."""
+                                     w1p: torch.Tensor, eps: float, res_local: bool = False
+                                     ) -> tuple[torch.Tensor, torch.Tensor]:
+        """``residual + sum_ranks(x @ w^T)`` and its RMSNorm, for a row-parallel projection
+        (``res_local`` as in ``allreduce_add_rmsnorm``)."""
         if x.is_cuda and self.fuses_linear(residual.numel() // residual.shape[-1]):
-            got = self.symm.linear_allreduce_add_rmsnorm(x, w, residual, w1p, eps)
+            got = self.symm.linear_allreduce_add_rmsnorm(x, w, residual, w1p, eps,
+                                                         res_local=res_local and self.sp_res_local)
             if got is not None:
                 return got
-        return self.allreduce_add_rmsnorm(ops.linear(x, w), residual, w1p, eps)
+        return self.allreduce_add_rmsnorm(ops.linear(x, w), residual, w1p, eps, res_local=res_local)
 
     def argmax_gather(self, local_logits: torch.Tensor, vocab_start: int) -> torch.Tensor:
         """Greedy token ids [B] over vocab-parallel logits (ties: lowest global index)."""

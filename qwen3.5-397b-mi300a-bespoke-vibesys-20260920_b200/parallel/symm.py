@@ -222,7 +222,8 @@ class SymmComm:
     def fits(self, rows: int) -> bool:
         return rows <= self.max_rows or rows <= self.sp_rows
 
-    def allreduce_add_rmsnorm(self, partial, residual, w1p, eps, kind: str = "auto", gather_out: bool = False):
+    def allreduce_add_rmsnorm(self, partial, residual, w1p, eps, kind: str = "auto", gather_out: bool = False,
+                              res_local: bool = False):
         """``residual += sum_ranks(partial)`` (in place) and returns (residual, rmsnorm(residual)).
         One-shot kernel while ``rows * (world - 1)`` is within ``ONESHOT_ROW_BUDGET`` (one peer
         round trip), the sequence-parallel kernel above that (``kind`` = "oneshot" / "sp" forces
@@ -247,7 +248,7 @@ class SymmComm:
         if use_sp:
             ext().symm_sp_ar_add_rmsnorm(self.sp_bases, self.rank, partial, residual, w1p, normed, float(eps),
                                          self.sp_slot_elems, SP_MAX_BLOCKS, self.sp_epoch, self.timeout_s,
-                                         gather_out)
+                                         gather_out, res_local)
             if gather_out:  # this rank's rows only: the next projection gathers (GatheredRows.linear)
                 return residual, GatheredRows(self, rows, residual.shape[-1], residual.device, normed)
             return residual, normed
@@ -271,7 +272,7 @@ class SymmComm:
             return False
         return rows <= self.sp_rows and (rows > self.max_rows or rows * (self.world - 1) > self.ONESHOT_ROW_BUDGET)
 
-    def linear_allreduce_add_rmsnorm(self, x, w, residual, w1p, eps):
+    def linear_allreduce_add_rmsnorm(self, x, w, residual, w1p, eps, res_local: bool = False):
         """``residual += sum_ranks(x @ w^T)`` (in place) and returns (residual, rmsnorm(residual)):
         the projection's epilogue stores every row into the symmetric region of the rank that owns
         it, then the sequence-parallel kernel reduces, normalises and gathers. None when
@@ -281,7 +282,8 @@ class SymmComm:
             return None
         normed = torch.empty_like(residual)
         ext().symm_linear_sp_ar_add_rmsnorm(x, w, self.sp_bases, self.rank, residual, w1p, normed, float(eps),
-                                            self.sp_slot_elems, SP_MAX_BLOCKS, self.sp_epoch, self.timeout_s)
+                                            self.sp_slot_elems, SP_MAX_BLOCKS, self.sp_epoch, self.timeout_s,
+                                            res_local)
         return residual, normed
 
     def close(self) -> None:

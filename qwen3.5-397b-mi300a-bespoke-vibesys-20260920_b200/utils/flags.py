@@ -68,6 +68,8 @@ _def("QB_OVERLAP", bool, True, "scheduler: launch decode step n+1 (tokens fed ba
      "step n back", lockstep=True)
 _def("QB_MTP_DEVICE_ACCEPT", bool, True, "speculative rounds: accepted lengths computed on the device and the whole "
      "round (draft, verify, accept, commit) replayed as one graph, read back once", lockstep=True)
+_def("QB_MOE_FUSE_SHARED", bool, True, "MoE: the shared expert's gated rows are added in the routed combine kernel "
+     "(off: a separate gate-and-add kernel)", lockstep=True)
 _def("QB_FOLD_SUFFIX", bool, False, "scheduler: the chat template's generation suffix after the turn-open boundary "
      "is fed through the following decode steps (their sampled ids discarded) instead of a prefill step of its own")
 _def("QB_PREFILL_ACCUM", bool, False, "scheduler: while at least QB_PREFILL_ACCUM_MIN_DECODE lanes decode, hold "
@@ -84,6 +86,8 @@ _def("QB_SP_MAX_ROWS", int, 4096, "rows of the sequence-parallel fused all-reduc
      lockstep=True)
 _def("QB_NVLS_MIN_ROWS", int, 0, "all-reduce messages of at least this many rows use the NVLS (multimem) kernel "
      "(0: never)", lockstep=True)
+_def("QB_SP_RES_LOCAL", bool, False, "prefill: the sequence-parallel all-reduce keeps the residual on each rank's own "
+     "rows (only the normed rows are gathered) except in a forward's last all-reduce", lockstep=True)
 _def("QB_AG_GEMM", bool, False, "prefill: the all-reduce after the MoE leaves the all-gather to the next layer's "
      "input projection, which pulls every rank's normed rows over NVLink inside its GEMM (sequence-parallel sizes)",
      lockstep=True)

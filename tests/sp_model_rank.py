@@ -26,26 +26,28 @@ def main(rank, world, port):
     g = torch.Generator().manual_seed(7)
     ids = torch.randint(10, 4000, (1500,), generator=g).tolist()
     out = {}
-    # (out projection fused into the reduce-scatter, all-gather fused into the next input projection)
-    modes = ((False, False), (True, False), (True, True), (False, True))
-    for fused, ag in modes:
-        m.comm.sp_gemm, m.comm.ag_gemm = fused, ag
+    # (out projection fused into the reduce-scatter, all-gather fused into the next input projection,
+    # residual kept on each rank's own rows)
+    modes = ((False, False, False), (True, False, False), (True, True, False), (False, True, False),
+             (True, False, True), (False, False, True), (True, True, True))
+    for fused, ag, rl in modes:
+        m.comm.sp_gemm, m.comm.ag_gemm, m.comm.sp_res_local = fused, ag, rl
         assert m.comm.fuses_linear(len(ids)) == fused
         m.begin(0)
         m.attach_blocks(0, list(range(1, 1 + (len(ids) + 15) // 16)))
-        out[(fused, ag)] = m.forward([(0, ids, 0)]).clone()
+        out[(fused, ag, rl)] = m.forward([(0, ids, 0)]).clone()
         # a decode step after it (one-shot path, the fused flags do not apply)
-        out[(fused, ag, "d")] = m.forward([(0, [int(out[(fused, ag)].argmax())], len(ids))]).clone()
+        out[(fused, ag, rl, "d")] = m.forward([(0, [int(out[(fused, ag, rl)].argmax())], len(ids))]).clone()
     torch.cuda.synchronize()
-    base = out[(False, False)]
-    for fused, ag in modes[1:]:
-        got = out[(fused, ag)]
+    base = out[(False, False, False)]
+    for fused, ag, rl in modes[1:]:
+        got = out[(fused, ag, rl)]
         if ag:  # the gathering GEMM tiles tokens per owner: same products, equal up to accumulation
             assert (got.float() - base.float()).abs().max().item() <= 2e-2 * base.float().abs().max().item(), \
-                (fused, ag)
-        else:
-            assert torch.equal(base, got), (base - got).abs().max().item()
-            assert torch.equal(out[(False, False, "d")], out[(fused, ag, "d")])
+                (fused, ag, rl)
+        else:  # fewer copies, the same arithmetic: the same bits
+            assert torch.equal(base, got), ((fused, ag, rl), (base - got).abs().max().item())
+            assert torch.equal(out[(False, False, False, "d")], out[(fused, ag, rl, "d")])
     assert ext().status(torch.empty(1, device=dev)).tolist()[0] == 0
     m.comm.symm.close()
     dist.destroy_process_group()

@@ -55,6 +55,21 @@ def main(rank, world, port):
         assert torch.equal(r1, r2), (rows, (r1.float() - r2.float()).abs().max().item())
         assert torch.equal(n1, n2), (rows, (n1.float() - n2.float()).abs().max().item())
     assert not s.fuses_linear(100)
+    # residual kept on each rank's own rows: the normed rows equal the full gather's on every row,
+    # the residual on this rank's range, over consecutive calls of both kernels
+    for it, rows in enumerate((1000, 2047, 2048)):
+        x = torch.randn(rows, H, device=dev, generator=g).bfloat16()
+        base = torch.randn(rows, H, device=dev, generator=torch.Generator(device=dev).manual_seed(70 + it)).bfloat16()
+        r1, n1 = s.allreduce_add_rmsnorm(x, base.clone(), w, 1e-6, kind="sp")
+        r2, n2 = s.allreduce_add_rmsnorm(x, base.clone(), w, 1e-6, kind="sp", res_local=True)
+        xo = torch.randn(rows, K, device=dev, generator=g).bfloat16()
+        r3, n3 = s.linear_allreduce_add_rmsnorm(xo, wo, base.clone(), w, 1e-6)
+        r4, n4 = s.linear_allreduce_add_rmsnorm(xo, wo, base.clone(), w, 1e-6, res_local=True)
+        torch.cuda.synchronize()
+        per = -(-rows // world)
+        a, b = min(rows, rank * per), min(rows, (rank + 1) * per)
+        assert torch.equal(n1, n2) and torch.equal(r1[a:b], r2[a:b]), (rows, "sp")
+        assert torch.equal(n3, n4) and torch.equal(r3[a:b], r4[a:b]), (rows, "linear")
     # graph capture + replay
     x = torch.randn(16, H, device=dev, generator=g).bfloat16()
     res = torch.zeros(16, H, device=dev).bfloat16()

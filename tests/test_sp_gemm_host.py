@@ -37,9 +37,9 @@ class _FusingComm(Comm):
     def fuses_linear(self, rows):
         return True
 
-    def linear_allreduce_add_rmsnorm(self, x, w, residual, w1p, eps):
+    def linear_allreduce_add_rmsnorm(self, x, w, residual, w1p, eps, res_local=False):
         self.calls += 1
-        return self.allreduce_add_rmsnorm(ops.linear(x, w), residual, w1p, eps)
+        return self.allreduce_add_rmsnorm(ops.linear(x, w), residual, w1p, eps, res_local=res_local)
 
 
 def test_deferred_out_projection_gives_the_same_logits():
