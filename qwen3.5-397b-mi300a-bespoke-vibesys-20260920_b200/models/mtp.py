@@ -111,8 +111,7 @@ class MTPHead:
             b = m.make_inputs([(l, [0], p + i) for l, p in zip(lanes, positions)])
             b.tokens = tok
             h = self.layer(self.combine(tok, hidden), b)
-            logits = m.logits(h)
-            tok = ops.argmax_rows(logits)[1]
+            tok = m.greedy(h)[0]
             out.append(tok)
             hidden = h
         self.drafted += B * self.k

@@ -128,6 +128,7 @@ class Model:
         self.stamps = None  # utils.telemetry.Stamps -> in-graph clock stamps at layer boundaries
         self._defer_out = False  # set inside _layers while the out projections fuse into the all-reduce
         self.fuse_shared = bool(flags.get("QB_MOE_FUSE_SHARED"))  # shared expert added in the routed combine
+        self.greedy_head = bool(flags.get("QB_GREEDY_HEAD"))  # greedy ids from gathered (max, index) pairs
         self.status_watch = None  # utils.devstatus.StatusWatch (CUDA): polled by the scheduler / workers
 
     def _gpu_mark(self, tag: str) -> None:
@@ -417,6 +418,28 @@ class Model:
         self._stamp("lm_head")
         return out
 
+    def greedy(self, h: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Greedy next-token ids of the rows of ``h`` through the vocabulary-parallel head: every
+        rank takes the (max, index) of its own vocabulary slice and only those pairs cross the
+        ranks (8 bytes per row and rank instead of each row's full logits); the largest value
+        wins, the lowest index on a tie, which is exactly the argmax of the gathered rows.
+        Returns (ids [R] int64, this rank's logits slice [R, V / world]); ``full_rows`` gathers
+        the full logits of the rows that need them. With ``QB_GREEDY_HEAD=0`` the rows are
+        all-gathered first (the slice is then the full rows). Reference behaviour:
+        ``mtp.py:640-658`` (``greedy_token``)."""
+        if not self.greedy_head:
+            lg = self.logits(h)
+            return ops.argmax_rows(lg)[1], lg
+        local = ops.linear(h, self.w["lm_head"])
+        ids = self.comm.argmax_gather(local, self.plan.vocab.start)
+        self._stamp("lm_head")
+        return ids, local
+
+    def full_rows(self, local: torch.Tensor) -> torch.Tensor:
+        """Full-vocabulary logits of rows of a ``greedy`` slice (a collective: every rank calls
+        it with the same rows)."""
+        return self.comm.all_gather_last(local) if self.greedy_head else local
+
     # ================================================================== Runner: forwards
     @torch.inference_mode()
     def forward(self, segs, logit_rows=None) -> torch.Tensor:
@@ -442,8 +465,7 @@ class Model:
         b.verify = True
         self._vsave = {}
         h = self._forward(b)
-        logits = self.logits(h)
-        am = ops.argmax_rows(logits)[1].view(B, k + 1)
+        am = self.greedy(h)[0].view(B, k + 1)
         self._gpu_mark("out")
         am_h, dr_h = am.tolist(), drafts.tolist()  # the round's one host sync
         self._d2h += 8 * B * (2 * k + 1)
@@ -552,10 +574,10 @@ class Model:
         host = [int(t) if t >= 0 else 0 for t in tokens]
         b = self.make_inputs([(l, [t], p) for l, t, p in zip(lanes, host, positions)])
         self._feed_back(b.tokens, tokens, src_rows)
-        lg = self.logits(self._forward(b))
+        ids, local = self.greedy(self._forward(b))
         if self.mtp is not None:
             self.mtp.catch_up(b, self.last_h_all)
-        return self._launch_tail(lg, len(lanes), keep_rows)
+        return self._launch_tail(ids, local, len(lanes), keep_rows)
 
     def _dev_index(self, xs) -> torch.Tensor:
         t = torch.tensor(list(xs), dtype=torch.long)
@@ -571,20 +593,21 @@ class Model:
         self._h2d += 16 * len(rows)
         tokens_dev.index_copy_(0, self._dev_index(rows), self._launch_ids.index_select(0, self._dev_index(src)))
 
-    def _launch_tail(self, lg: torch.Tensor, n: int, keep_rows):
-        ids = ops.argmax_rows(lg)[1]
+    def _launch_tail(self, ids: torch.Tensor, local: torch.Tensor, n: int, keep_rows):
+        """Greedy ids of a launched step (``greedy``) to pinned host memory behind an event; the
+        full logits of the ``keep_rows`` gathered (a collective on every rank)."""
         self._launch_ids = ids
         kept = {}
         if keep_rows:
-            sel = lg.index_select(0, self._dev_index(keep_rows))
+            sel = self.full_rows(local.index_select(0, self._dev_index(keep_rows)))
             kept = {r: sel[i:i + 1] for i, r in enumerate(keep_rows)}
         if self.device.type == "cuda":
             host = torch.empty(n, dtype=torch.int64).pin_memory()
             host.copy_(ids, non_blocking=True)
             ev = torch.cuda.Event()
             ev.record()
-        else:
-            host, ev = ids, None
+        else:  # a copy: ids may be a replayed bucket's static output, which the next replay rewrites
+            host, ev = ids.clone(), None
         return (host, ev, kept, n)
 
     def decode_collect(self, handle) -> list[int]:

@@ -42,6 +42,17 @@ def pool_bytes(cfg: Qwen35Config, p, spec: PoolSpec) -> tuple[int, int, int]:
     return kv, (spec.lanes + snaps) * per_state, num_blocks
 
 
+def nvls_min_rows(flag: int, world: int) -> int:
+    """Smallest all-reduce (rows) that takes the NVLS kernel, 0 for never. ``flag`` -1 chooses by
+    world size from the collective sweep (hidden 4096, device time, max over ranks): at 8 ranks the
+    switch-reduced kernel beats the sequence-parallel one from 1024 rows (68 vs 71 us at 1024, 108
+    vs 126 at 2048, 353 vs 409 at 8192) and loses below (55 vs 51 us at 512); at 2 and 4 ranks it
+    never wins (each GPU's share of the reduction is already half or a quarter of the message)."""
+    if flag >= 0:
+        return flag
+    return 1024 if world >= 8 else 0
+
+
 def build_model(model: str, rank: int, world: int, device: torch.device, spec: PoolSpec,
                 dtype=torch.bfloat16, seed: int = 0, with_mtp: bool = False, comm: Comm | None = None,
                 reserve_bytes: float = 14e9, graphs: bool | None = None):
@@ -85,7 +96,7 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
             except SymmUnavailable as e:  # raised on every rank together: all fall back to NCCL
                 print(f"[rank {rank}] fused collectives unavailable, using NCCL: {e}", flush=True)
                 comm.symm = None
-            nvls_min = flags.get("QB_NVLS_MIN_ROWS")
+            nvls_min = nvls_min_rows(flags.get("QB_NVLS_MIN_ROWS"), world)
             if comm.symm is not None and nvls_min > 0 and sp_rows > 0:
                 # messages of nvls_min rows and more take the switch-reduced kernel; all ranks
                 # keep the peer-memory kernels together when the fabric has no multicast

@@ -19,7 +19,6 @@ from __future__ import annotations
 import torch
 
 from ..models.qwen35 import StepInputs
-from ..ops import core as ops
 from ..utils import flags
 
 DEFAULT_BUCKETS = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128)
@@ -75,7 +74,12 @@ class _HostGraph:
         self.fn, self.out = fn, out
 
     def replay(self):
-        self.out.copy_(self.fn())
+        res = self.fn()
+        if isinstance(self.out, tuple):
+            for o, r in zip(self.out, res):
+                o.copy_(r)
+        else:
+            self.out.copy_(res)
 
 
 class HostGraphs(CudaGraphs):
@@ -232,8 +236,10 @@ class GraphRunner:
         m._sync_tables()
 
     def _run(self, bk: _Bucket):
+        """The captured step: the forward and the vocabulary-parallel greedy head, whose output is
+        (greedy ids [B], this rank's logits slice [B, V / world])."""
         m = self.model
-        return m.logits(m._forward(bk.inputs(m)))
+        return m.greedy(m._forward(bk.inputs(m)))
 
     def prepare(self) -> None:
         """Capture every bucket (largest first, sharing one memory pool). Must run on every rank
@@ -286,10 +292,10 @@ class GraphRunner:
                 reset()
                 self._fill(bk, lanes, [(7 * ln + 11) % 1000 for ln in lanes], [0] * B)
                 bk.graph.replay()
-                got = bk.out.float().clone()
+                got = bk.out[1].float().clone()
                 reset()
                 m._sync_tables()
-                exp = self._run(bk).float()
+                exp = self._run(bk)[1].float()
                 for ln in lanes:
                     m.begin(ln)
                     m.attach_blocks(ln, [])
@@ -351,7 +357,7 @@ class GraphRunner:
             b = StepInputs(tok, bk.pos_d[i], bk.rows_d[i], bk.lanes, bk.cu_d, bk.pos_d[i], bk.logit_rows_d,
                            list(range(B)), list(range(B + 1)), [0] * B, m.max_seq)
             h = mtp.layer(mtp.combine(tok, hidden), b)
-            tok = ops.argmax_rows(m.logits(h))[1]
+            tok = m.greedy(h)[0]
             outs.append(tok)
             hidden = h
         bk.drafts = torch.stack(outs, dim=1)
@@ -361,7 +367,7 @@ class GraphRunner:
         vb.verify = True
         m._vsave = {}
         h = m._forward(vb)
-        bk.am = ops.argmax_rows(m.logits(h))[1].view(B, k + 1)
+        bk.am = m.greedy(h)[0].view(B, k + 1)
         bk.vb, bk.vsave, bk.h_all = vb, m._vsave, m.last_h_all
         m._vsave = {}
 
@@ -539,7 +545,7 @@ class GraphRunner:
             bk.graph.replay()
         self.replays += 1
         self.backend.add_launches(self.launch_per_replay.get(B, 0))
-        return bk.out[:n]
+        return self.model.full_rows(bk.out[1][:n])  # gathered after the replay, on every rank
 
     def decode_launch(self, lanes, tokens, positions, src_rows, keep_rows=()):
         """``Model.decode_launch`` replayed from the smallest captured bucket that holds the
@@ -558,7 +564,7 @@ class GraphRunner:
             bk.graph.replay()
             self.replays += 1
             self.backend.add_launches(self.launch_per_replay.get(B, 0))
-            return m._launch_tail(bk.out[:n], n, keep_rows)
+            return m._launch_tail(bk.out[0][:n], bk.out[1][:n], n, keep_rows)
 
     def __getattr__(self, name):
         return getattr(self.model, name)

@@ -70,6 +70,8 @@ _def("QB_OVERLAP", bool, True, "scheduler: launch decode step n+1 (tokens fed ba
      "step n back", lockstep=True)
 _def("QB_MTP_DEVICE_ACCEPT", bool, True, "speculative rounds: accepted lengths computed on the device and the whole "
      "round (draft, verify, accept, commit) replayed as one graph, read back once", lockstep=True)
+_def("QB_GREEDY_HEAD", bool, True, "greedy decode ids from each rank's (max, index) over its vocabulary slice, "
+     "gathered as 8-byte pairs (off: the full logits rows are all-gathered, then the argmax)", lockstep=True)
 _def("QB_MOE_FUSE_SHARED", bool, True, "MoE: the shared expert's gated rows are added in the routed combine kernel "
      "(off: a separate gate-and-add kernel)", lockstep=True)
 _def("QB_FOLD_SUFFIX", bool, False, "scheduler: the chat template's generation suffix after the turn-open boundary "
@@ -86,8 +88,9 @@ _def("QB_COMM", str, "fused", "tensor-parallel all-reduce: fused (peer-memory ke
 _def("QB_SYMM_MAX_ROWS", int, 512, "rows of the one-shot fused all-reduce buffers", lockstep=True)
 _def("QB_SP_MAX_ROWS", int, 4096, "rows of the sequence-parallel fused all-reduce buffers (0: off)",
      lockstep=True)
-_def("QB_NVLS_MIN_ROWS", int, 0, "all-reduce messages of at least this many rows use the NVLS (multimem) kernel "
-     "(0: never)", lockstep=True)
+_def("QB_NVLS_MIN_ROWS", int, -1, "all-reduce messages of at least this many rows use the NVLS (multimem) kernel "
+     "(0: never; -1: by world size, from 1024 rows at 8 ranks and more, where the switch reduction measured "
+     "ahead of the sequence-parallel kernel, never below)", lockstep=True)
 _def("QB_SP_RES_LOCAL", bool, False, "prefill: the sequence-parallel all-reduce keeps the residual on each rank's own "
      "rows (only the normed rows are gathered) except in a forward's last all-reduce", lockstep=True)
 _def("QB_AG_GEMM", bool, False, "prefill: the all-reduce after the MoE leaves the all-gather to the next layer's "

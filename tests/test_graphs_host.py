@@ -76,7 +76,8 @@ def test_host_graph_validation_failure_turns_graphs_off():
     class Broken(HostGraphs):
         def capture(self, fn, warmups=2, pool=True):
             g, out = super().capture(fn, warmups, pool)
-            g.fn = lambda: torch.full_like(out, 1e4)
+            ids, local = out  # (greedy ids, logits slice): the slice comes back as garbage
+            g.fn = lambda: (ids, torch.full_like(local, 1e4))
             return g, out
 
     m = _model()

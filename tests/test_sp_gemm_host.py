@@ -21,6 +21,14 @@ def test_fused_sizes_follow_the_sequence_parallel_choice():
     assert not _symm(2, sp_rows=0).fuses_linear(2048)
 
 
+def test_nvls_choice_by_world_size():
+    from qwen35_b200.serving.engine import nvls_min_rows
+
+    assert nvls_min_rows(-1, 8) == 1024  # measured ahead of the sequence-parallel kernel from 1024 rows
+    assert nvls_min_rows(-1, 4) == 0 and nvls_min_rows(-1, 2) == 0  # never ahead at 2 and 4 ranks
+    assert nvls_min_rows(0, 8) == 0 and nvls_min_rows(512, 2) == 512  # an explicit flag wins
+
+
 def test_partial_slots_hold_whole_rank_ranges():
     s = _symm(8, sp_rows=1001)
     per = -(-1001 // 8)
