@@ -25,6 +25,15 @@ constexpr int FA_THREADS = 192;
 constexpr int FA_S_COL = 0;      // S buffers: cols [0, 64) and [64, 128)
 constexpr int FA_O_COL = 256;    // O accumulator
 constexpr int FA_WS_HEAD = 4;    // partial record: max, sum, 2 pad words, then O (16-byte aligned)
+constexpr float FA_RESCALE_LOG2 = 8.f;  // running-max slack before O is rescaled (log2 units)
+
+// 2^x by the hardware's approximate base-2 exponential (MUFU; relative error ~2^-22, far below
+// the bf16 rounding P gets next); -inf gives 0.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // K-major SW128 descriptor is desc_sw128; MN-major SW128 needs explicit LBO (MN-atom stride) and
 // SBO (8-row K-group stride).
@@ -43,6 +52,17 @@ __device__ __forceinline__ void tmem_st_col32(uint32_t taddr, const float* v) {
 #pragma unroll
   for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(v[i]);
   tmem_st32(taddr, r);
+}
+
+// 64 consecutive fp32 columns of this warp's 32 TMEM lanes, one load and one wait.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t r[64];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]), "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]), "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]), "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]), "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; ++i) v[i] = __uint_as_float(r[i]);
 }
 
 template <int HD>
@@ -231,30 +251,43 @@ __global__ void __launch_bounds__(FA_THREADS, 1)
       }
       tc_fence_after();
       float sv[64];
-      tmem_ld32(tmem + lane_off + FA_S_COL + st * FA_KT, sv);
-      tmem_ld32(tmem + lane_off + FA_S_COL + st * FA_KT + 32, sv + 32);
+      tmem_ld64(tmem + lane_off + FA_S_COL + st * FA_KT, sv);
       tc_fence_before();
       mbar_arrive(&s_free[st]);
       const int k0 = (kt0 + i) * FA_KT;
-      float mx = -INFINITY;
+      // keys past the row's position (the diagonal tiles) and rows past the tile are masked; the
+      // softmax scale is applied inside the exponent (one FFMA per score)
+      if (!valid || k0 + FA_KT - 1 > qpos) {
 #pragma unroll
-      for (int jj = 0; jj < 64; ++jj) {
-        const bool keep = valid && (k0 + jj) <= qpos;
-        sv[jj] = keep ? sv[jj] * a.scale_log2 : -INFINITY;
-        mx = fmaxf(mx, sv[jj]);
+        for (int jj = 0; jj < 64; ++jj)
+          if (k0 + jj > qpos) sv[jj] = -INFINITY;  // qpos = -1 on invalid rows masks every key
       }
-      const float m_new = fmaxf(m, mx);
-      const float corr = (m == -INFINITY) ? (m_new == -INFINITY ? 1.f : 0.f) : exp2f(m - m_new);
-      float sum = 0.f;
+      // row max as eight independent chains (one dependent chain of 64 would expose its latency:
+      // a softmax warp is alone on its sub-partition)
+      float mx8[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) mx8[u] = sv[u];
+#pragma unroll
+      for (int jj = 8; jj < 64; ++jj) mx8[jj & 7] = fmaxf(mx8[jj & 7], sv[jj]);
+      const float mx = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                             fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7]))) * a.scale_log2;
+      // lazy rescale: the running max m moves only when a tile's max passes it by more than
+      // FA_RESCALE_LOG2, so O is rescaled in TMEM rarely; in between, p = 2^(s - m) <= 2^8, which
+      // fp32 and bf16 hold with full relative precision, and O and l stay relative to the same m
+      const float m_new = (mx > m + FA_RESCALE_LOG2) ? mx : m;
+      const float corr = (m_new == m) ? 1.f : (m == -INFINITY ? 0.f : ex2_approx(m - m_new));
+      const float nm = m_new == -INFINITY ? 0.f : -m_new;  // every score is -inf while m_new is
+      float s4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pw[32];
 #pragma unroll
       for (int u = 0; u < 32; ++u) {
-        const float p0 = m_new == -INFINITY ? 0.f : exp2f(sv[2 * u] - m_new);
-        const float p1 = m_new == -INFINITY ? 0.f : exp2f(sv[2 * u + 1] - m_new);
+        const float p0 = ex2_approx(fmaf(sv[2 * u], a.scale_log2, nm));
+        const float p1 = ex2_approx(fmaf(sv[2 * u + 1], a.scale_log2, nm));
         const __nv_bfloat162 pb = __floats2bfloat162_rn(p0, p1);
-        sum += __bfloat162float(pb.x) + __bfloat162float(pb.y);
+        s4[u & 3] += __bfloat162float(pb.x) + __bfloat162float(pb.y);
         pw[u] = *reinterpret_cast<const uint32_t*>(&pb);
       }
+      const float sum = (s4[0] + s4[1]) + (s4[2] + s4[3]);
       l = l * corr + sum;
       m = m_new;
       if (i > 0) {

@@ -129,6 +129,7 @@ class Model:
         self._defer_out = False  # set inside _layers while the out projections fuse into the all-reduce
         self.fuse_shared = bool(flags.get("QB_MOE_FUSE_SHARED"))  # shared expert added in the routed combine
         self.greedy_head = bool(flags.get("QB_GREEDY_HEAD"))  # greedy ids from gathered (max, index) pairs
+        self.route_log: list | None = None  # list -> every MoE call's top-k expert ids, in call order (tests)
         self.status_watch = None  # utils.devstatus.StatusWatch (CUDA): polled by the scheduler / workers
 
     def _gpu_mark(self, tag: str) -> None:
@@ -353,6 +354,8 @@ class Model:
         self._dstamp("moe.router_proj")
         topw, topi = ops.router_topk(rl[:, : cfg.experts], cfg.top_k)
         self._dstamp("moe.topk")
+        if self.route_log is not None:
+            self.route_log.append(topi)
         drop = self.fault.get("drop_expert")
         if drop is not None:
             topw = torch.where(topi == int(drop), torch.zeros_like(topw), topw)

@@ -8,8 +8,12 @@ positions with the two MoE kernel paths (both exact in their products, different
 orders), while the host model in fp32 stays within 2e-2 of the oracle (``test_tp_gloo_parity``).
 
 * logits: the next-token logits at every prompt position (one prefill through the real kernels)
-  against the oracle's over the same tokens: the median position's largest error within 5 % of
-  the logit scale and the 90th percentile within 20 % (a wrong kernel is off by the whole scale);
+  against the oracle's over the same tokens, with the oracle's routers made to pick the experts
+  our prefill picked (each router keeps its own softmax weights over them, renormalised): the
+  discrete choice is then the same on both sides and what remains is the continuous bf16 vs fp32
+  difference, so the median position's largest error must stay within 2 % of the logit scale and
+  every position's within 4 % (measured 0.9 % and 1.2 %; a near-tie flipped at an early position would otherwise perturb
+  every later position through attention and the DeltaNet state, whatever the kernels' accuracy);
 * tokens: 32 greedy tokens per prompt, teacher-forced through the oracle: our token is the
   oracle's top-1 up to 6e-2 at 85 % of positions and within 0.35 everywhere.
 """
@@ -21,6 +25,26 @@ from hf_oracle import build_hf
 from test_tp_gloo_parity import check_teacher_forced
 
 pytestmark = pytest.mark.gpu
+
+
+def _force_routing(oracle, routes):
+    """Makes every top-k router of the oracle (in layer order) take the given expert ids [T, k]
+    with its own fp32 softmax weights over them, renormalised as the router does; returns the
+    routers (``del r.forward`` restores one)."""
+    import torch.nn.functional as F
+
+    routers = [mod for mod in oracle.modules() if type(mod).__name__.endswith("TopKRouter")]
+    assert len(routers) <= len(routes), (len(routers), len(routes))
+    for r, idx in zip(routers, routes):
+        def forward(hidden_states, r=r, idx=idx.long().cpu()):
+            logits = F.linear(hidden_states, r.weight)
+            probs = torch.softmax(logits, dtype=torch.float, dim=-1)
+            top = probs.gather(-1, idx)
+            top = top / top.sum(dim=-1, keepdim=True)
+            return logits, top.to(logits.dtype), idx
+
+        r.forward = forward
+    return routers
 
 
 def test_tiny_gpu_matches_reference_modeling(tiny_dir):
@@ -40,15 +64,22 @@ def test_tiny_gpu_matches_reference_modeling(tiny_dir):
         # logits at every prompt position
         m.begin(0)
         m.attach_blocks(0, list(range(1, 1 + (len(ids) + 15) // 16)))
+        m.route_log = []
         ours = m.forward([(0, ids, 0)], logit_rows=list(range(len(ids)))).float().cpu()
-        with torch.inference_mode():
-            ref = oracle(torch.tensor([ids])).logits[0].float()
+        routes, m.route_log = m.route_log, None
+        routers = _force_routing(oracle, routes)
+        try:
+            with torch.inference_mode():
+                ref = oracle(torch.tensor([ids])).logits[0].float()
+        finally:
+            for r in routers:
+                del r.forward
         err = (ours - ref).abs().max(dim=-1).values  # per position
         scale = ref.abs().max().item()
-        print(f"logit error vs oracle: median {err.median().item():.4f} p90 {err.quantile(0.9).item():.4f} "
-              f"max {err.max().item():.4f} (logit scale {scale:.3f})")
-        assert err.median().item() <= 0.05 * scale, (err.median().item(), scale)
-        assert err.quantile(0.9).item() <= 0.2 * scale, (err.quantile(0.9).item(), scale)
+        print(f"logit error vs oracle (routing forced): median {err.median().item():.4f} "
+              f"p90 {err.quantile(0.9).item():.4f} max {err.max().item():.4f} (logit scale {scale:.3f})")
+        assert err.median().item() <= 0.02 * scale, (err.median().item(), scale)
+        assert err.max().item() <= 0.04 * scale, (err.max().item(), err.argmax().item(), scale)
         # greedy tokens, teacher-forced
         toks = m.generate(ids, 32)
         torch.cuda.synchronize()
