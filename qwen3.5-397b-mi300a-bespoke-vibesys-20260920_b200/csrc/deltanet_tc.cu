@@ -19,7 +19,7 @@
 // state kernel's MMAs read: U fp32, then W, Q e^G, Mq (bf16, K-major, 128-byte swizzle) and
 // K e^(G_last - G) (bf16, M-major), and e^(G_last).
 //
-// dn_tc_state (grid: segment x value head, 128 threads): walks the segment's chunks in order with
+// dn_tc_state (grid: segment x value head x value-column half, 128 threads): walks the segment's chunks in order with
 // the fp32 state S in tensor memory (lane = key row, 128 columns). Per chunk, after one bulk copy
 // of the record: S is read once (tcgen05.ld) to a bf16 MN-major operand and written back scaled
 // by e^(G_last); MMA  D1 = W S;  threads form Delta = U - D1 (bf16 operand);  MMAs
@@ -342,6 +342,7 @@ __global__ void __launch_bounds__(256) dn_tc_prep_kernel(const float* qn, const 
   }
 }
 
+template <int NS>
 __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_all, const int* chunks,
                                                              const int* seg_chunk0, const int* seg_lane, float* state,
                                                              long lane_stride, int nv, bf16* out, int commit, int* err) {
@@ -353,7 +354,12 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
   uint64_t* bar_mma = bar_rec + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_rec + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_rec + 3);
+  // NS value columns of the state per CTA (blockIdx.z picks which): the columns evolve
+  // independently (Delta, O and the update are column-wise in V), so a head can be split over
+  // CTAs by value columns; 64 columns are exactly one N-atom of the MN-major operands
+  constexpr int NQ = NS / 32;
   const int seg = blockIdx.x, h = blockIdx.y, tid = threadIdx.x, warp = tid >> 5;
+  const int col0 = blockIdx.z * NS;
   const int c_begin = seg_chunk0[seg], c_end = seg_chunk0[seg + 1];
   if (c_begin >= c_end) return;
   // zero the pad rows (64..127) of the 64-token A operands, once
@@ -381,9 +387,9 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
   const uint32_t tmem = *tmem_slot;
   const uint32_t lane_t = tmem + ((uint32_t)(warp * 32) << 16);  // this warp's TMEM lanes
   // ---- initial state: thread tid = key row
-  float* st = state + (long)seg_lane[seg] * lane_stride + (long)h * D * D + (long)tid * D;
+  float* st = state + (long)seg_lane[seg] * lane_stride + (long)h * D * D + (long)tid * D + col0;
 #pragma unroll
-  for (int q = 0; q < 4; ++q) {
+  for (int q = 0; q < NQ; ++q) {
     uint32_t r[32];
 #pragma unroll
     for (int i = 0; i < 32; i += 4) {
@@ -414,7 +420,7 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     load_rec(c_begin);
     ++rec_issued;
   }
-  const uint32_t idesc = idesc_f16(128, 128, true) | (1u << 16);  // A K-major, B MN-major
+  const uint32_t idesc = idesc_f16(128, NS, true) | (1u << 16);  // A K-major, B MN-major
   const uint32_t idesc_mn = idesc | (1u << 15);                    // A MN-major too
   uint32_t ph_rec = 0, ph_mma = 0;
   bool ok = true;
@@ -428,7 +434,7 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     {
       const float egl = *reinterpret_cast<const float*>(base + S_U + R_EGL);
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < NQ; ++q) {
         float v[32];
         tmem_ld32(lane_t + TM_S + 32 * q, v);
         uint8_t* row = base + S_S + (q >> 1) * 16384 + tid * 128;
@@ -465,9 +471,9 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     tc_fence_after();
     // 4. Delta = U - D1 (token rows 0..63: warps 0 and 1) -> bf16 MN-major operand
     if (warp < 2) {
-      const float* u = reinterpret_cast<const float*>(base + S_U) + tid * D;
+      const float* u = reinterpret_cast<const float*>(base + S_U) + tid * D + col0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < NQ; ++q) {
         float v[32];
         tmem_ld32(lane_t + TM_D1 + 32 * q, v);
 #pragma unroll
@@ -514,9 +520,9 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
       ++rec_issued;
     }
     if (warp < 2) {  // whole warps: tcgen05.ld is warp-collective; only the stores are per row
-      bf16* o = out + ((long)(row0 + tid) * nv + h) * D;
+      bf16* o = out + ((long)(row0 + tid) * nv + h) * D + col0;
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
+      for (int q = 0; q < NQ; ++q) {
         float v[32];
         tmem_ld32(lane_t + TM_D2 + 32 * q, v);
         if (tid < rows) {
@@ -537,7 +543,7 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
   // ---- final state (fp32) back to the lane
   if (ok && commit) {
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < NQ; ++q) {
       float v[32];
       tmem_ld32(lane_t + TM_S + 32 * q, v);
 #pragma unroll
@@ -571,7 +577,8 @@ int gated_delta_tc(const void* qkv, long ldqkv, const void* ab, long ldab, const
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(dn_tc_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
-    cudaFuncSetAttribute(dn_tc_state_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, S_BYTES);
+    cudaFuncSetAttribute(dn_tc_state_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_BYTES);
+    cudaFuncSetAttribute(dn_tc_state_kernel<64>, cudaFuncAttributeMaxDynamicSharedMemorySize, S_BYTES);
     attr = true;
   }
   // value heads per prep CTA: a key head's whole group while that still gives a full wave of
@@ -580,8 +587,21 @@ int gated_delta_tc(const void* qkv, long ldqkv, const void* ab, long ldab, const
   const int hpc = (long)n_chunks * nk >= 148 ? R : 1;
   dn_tc_prep_kernel<<<dim3(n_chunks, nk, R / hpc), 256, PREP_SMEM, s>>>(qn, kn, gb, (const bf16*)qkv, ldqkv, chunks,
                                                                        nk, nv, hpc, rec);
-  dn_tc_state_kernel<<<dim3(S, nv), 128, S_BYTES, s>>>(rec, chunks, seg_chunk0, seg_lane, state, lane_stride, nv,
-                                                       (bf16*)out, commit ? 1 : 0, err);
+  // state CTAs: one per (segment, value head), or two per head on 64 value columns each when that
+  // packs the waves better (few heads per rank, few segments: the serial chunk walk is latency
+  // bound, so half the columns per CTA is close to half the time). QB_DN_VSPLIT = 1 / 2 forces.
+  const char* vs_env = getenv("QB_DN_VSPLIT");
+  int vsplit = vs_env ? atoi(vs_env) : 0;
+  if (vsplit != 1 && vsplit != 2) {
+    const long ctas = (long)S * nv, w1 = (ctas + 147) / 148, w2 = (2 * ctas + 147) / 148;
+    vsplit = w2 < 2 * w1 ? 2 : 1;
+  }
+  if (vsplit == 2)
+    dn_tc_state_kernel<64><<<dim3(S, nv, 2), 128, S_BYTES, s>>>(rec, chunks, seg_chunk0, seg_lane, state, lane_stride,
+                                                                nv, (bf16*)out, commit ? 1 : 0, err);
+  else
+    dn_tc_state_kernel<128><<<dim3(S, nv, 1), 128, S_BYTES, s>>>(rec, chunks, seg_chunk0, seg_lane, state,
+                                                                 lane_stride, nv, (bf16*)out, commit ? 1 : 0, err);
   return (int)cudaGetLastError();
 }
 

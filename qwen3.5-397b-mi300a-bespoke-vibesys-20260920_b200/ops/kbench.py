@@ -248,19 +248,25 @@ def case_deltanet_decode(lanes: int, iters: int, pk: dict, nk: int = 16, nv: int
     return _report(f"deltanet_decode_B{lanes}", ms, bytes_, 4 * lanes * nv * dk * dv, pk)
 
 
-def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
+def case_model(tokens: int, ctx: int, lanes: int = 32, shard: int = 1) -> dict:
     """Whole-model steps at the full geometry on one GPU (random weights; experts of the first
     layers reused by the rest, as the one-GPU benchmark does): one prefill of ``tokens`` new
     tokens continuing ``ctx`` cached ones, and one ``lanes``-row decode step at context
     ``max(ctx, 2048)``. Prints the step times (CUDA events) and the per-kernel share of device
-    time (torch profiler, a separate run)."""
+    time (torch profiler, a separate run).
+
+    ``shard`` N > 1: rank 0's shard of N-way tensor + expert parallelism (its heads, its expert
+    range, its vocabulary slice, all layers' experts distinct) on this one GPU with every
+    collective replaced by the local identity: the per-rank compute of an N-GPU step, without
+    its NVLink traffic (``parallel.bench_collectives`` times that part)."""
     import collections
 
+    from ..parallel.comm import Comm
     from ..serving.engine import PoolSpec, build_model
 
     dev = torch.device("cuda", 0)
     spec = PoolSpec(lanes=lanes + 1, max_seq=16384, kv_tokens=(lanes + 1) * 9600, snapshots=8)  # + pad lane
-    m, _ = build_model("full", 0, 1, dev, spec, graphs=False)
+    m, _ = build_model("full", 0, shard, dev, spec, graphs=False, comm=Comm() if shard > 1 else None)
     per = 600
     for lane in range(lanes):
         m.begin(lane)
@@ -285,13 +291,13 @@ def case_model(tokens: int, ctx: int, lanes: int = 32) -> dict:
                 agg[ev.name.split("(")[0][:60]][0] += 1
                 agg[ev.name.split("(")[0][:60]][1] += getattr(ev, "device_time_total", 0.0)
         tot = sum(v[1] for v in agg.values()) or 1.0
-        top = sorted(agg.items(), key=lambda kv: -kv[1][1])[:12]
+        top = sorted(agg.items(), key=lambda kv: -kv[1][1])[:20]
         # kernel_ms: the step's kernels back to back; ms - kernel_ms: device idle inside the step
         # (host launch cost the GPU waited for)
-        row = {"case": f"model_{f.__name__}", "tokens": tokens if f is prefill else lanes, "ctx": ctx,
-               "ms": round(ms, 2), "kernel_ms": round(tot / 1e3, 2),
+        row = {"case": f"model_{f.__name__}", "shard": shard, "tokens": tokens if f is prefill else lanes,
+               "ctx": ctx, "ms": round(ms, 2), "kernel_ms": round(tot / 1e3, 2),
                "launches": sum(n for n, _ in agg.values()),
-               "kernels": [(k, n, round(t / tot, 3)) for k, (n, t) in top]}
+               "kernels": [(k, n, round(t / tot, 3), round(t / 1e3, 3)) for k, (n, t) in top]}
         print(json.dumps(row), flush=True)
         res[f.__name__] = row
     # the same decode step replayed from a CUDA graph, and its per-part device time from clock
@@ -331,6 +337,8 @@ def main(argv=None):
     ap.add_argument("--ctx", type=int, default=None)
     ap.add_argument("--lanes", type=int, default=None)
     ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--shard", type=int, default=1,
+                    help="model case: time rank 0's shard of N-way parallelism on this GPU (collectives local)")
     ap.add_argument("--heads", type=int, nargs=2, default=None, metavar=("NK", "NV"),
                     help="deltanet cases: key and value heads (default the full geometry's 16 64; one "
                          "rank of N-way tensor parallelism has 16/N and 64/N)")
@@ -355,7 +363,7 @@ def main(argv=None):
     if a.case == "conv":
         return [case_conv(a.tokens or 2048, a.iters, pk)]
     if a.case == "model":
-        return case_model(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.lanes or 32)
+        return case_model(a.tokens or 800, a.ctx if a.ctx is not None else 6000, a.lanes or 32, a.shard)
     if a.case in ("deltanet_decode", "all"):
         run.append(case_deltanet_decode(a.lanes or 32, a.iters, pk))
     if a.case in ("deltanet", "all"):

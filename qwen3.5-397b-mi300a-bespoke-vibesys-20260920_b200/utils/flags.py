@@ -45,6 +45,8 @@ _def("QB_MOE_IMPL", str, "mx", "routed-expert kernel: mx (block-scaled fp8 tcgen
 _def("QB_MX_BN_MAX", int, 64, "largest token tile of the block-scaled MoE kernel", native=True)
 _def("QB_MX_TILED", bool, True, "block-scaled MoE: expert codes re-laid tile-contiguous at load")
 _def("QB_MX_WIDE", bool, True, "block-scaled MoE, tiled codes: one TMA box per operand and stage", native=True)
+_def("QB_DN_VSPLIT", int, 0, "chunked DeltaNet state kernel: CTAs per value head (1: all 128 value columns, "
+     "2: 64 each; 0: two when that packs the waves better)", native=True)
 _def("QB_MX_K2", int, -1, "block-scaled MoE, wide path: two 128-K atoms per pipeline stage (1), one (0), "
      "or two for token tiles of at most 32 rows (-1)", native=True)
 _def("QB_MX_PROBE", bool, False, "block-scaled MoE: count the producer / MMA wait cycles (diagnostic)",

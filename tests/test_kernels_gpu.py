@@ -430,13 +430,15 @@ def test_flash_attention_decode_splits(nq, nkv, hd):
     status_ok()
 
 
-@pytest.mark.parametrize("mode", ["tc", "chunked_fp32"])
-def test_chunked_delta_rule_matches_recurrence(monkeypatch, mode):
+@pytest.mark.parametrize("mode,vsplit", [("tc", "1"), ("tc", "2"), ("tc", "0"), ("chunked_fp32", "0")])
+def test_chunked_delta_rule_matches_recurrence(monkeypatch, mode, vsplit):
     """Chunked (WY) delta rule on prefill-sized segments vs the fp32 token recurrence (PyTorch on
     the host): outputs and the carried state, several segments (one shorter than a chunk, one of
     a single row, one spanning four chunks). ``tc`` keeps the state in tensor memory and rounds
-    the MMA operands to bf16 (fp32 accumulate), hence its wider tolerance."""
+    the MMA operands to bf16 (fp32 accumulate), hence its wider tolerance; its state kernel runs
+    with whole heads per CTA and with heads split over two CTAs by value columns."""
     monkeypatch.setenv("QB_DN_PREFILL", mode)
+    monkeypatch.setenv("QB_DN_VSPLIT", vsplit)  # state CTAs per value head: 1, 2 (64 columns each), 0 auto
     nk, nv, dk, dv = 2, 8, 128, 128
     C = 2 * nk * dk + nv * dv
     lanes = 4
