@@ -338,36 +338,45 @@ int qk_norm_rope_kv_write(const void* qkv, long ldqkv, int nq, int nkv, int hd, 
 // ------------------------------------------------------------------ router softmax + top-k
 // One warp per token: fp32 softmax over E experts, k rounds of arg-max (ties -> lower
 // expert index), renormalised weights.
+// One warp per token row: fp32 softmax over the E router logits, then k rounds of a warp-wide
+// argmax (ties to the lower expert id), renormalised. PER = logits per lane (E <= 32 PER) is a
+// compile-time count and every loop over it and over the k <= 16 picks is unrolled, so the row
+// stays in registers (a runtime-indexed array would live in local memory).
+template <int PER>
 __global__ void router_topk_kernel(const bf16* logits, long ld, int T, int E, int k, float* wout, int* iout) {
   const long t = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (t >= T) return;
-  constexpr int MAXPER = 32;  // E <= 1024
-  float p[MAXPER];
-  const int per = (E + 31) / 32;
+  float p[PER];
   const bf16* row = logits + t * ld;
   float m = -INFINITY;
-  for (int i = 0; i < per; ++i) {
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
     p[i] = e < E ? __bfloat162float(row[e]) : -INFINITY;
     m = fmaxf(m, p[i]);
   }
   m = warp_max(m);
   float s = 0.f;
-  for (int i = 0; i < per; ++i) {
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
     p[i] = (lane + 32 * i) < E ? expf(p[i] - m) : 0.f;
     s += p[i];
   }
   s = warp_sum(s);
   const float invs = 1.f / s;
-  for (int i = 0; i < per; ++i) p[i] = (lane + 32 * i) < E ? p[i] * invs : -1.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) p[i] = (lane + 32 * i) < E ? p[i] * invs : -1.f;
   float tw[16];
   int ti[16];
   float tot = 0.f;
-  for (int r = 0; r < k; ++r) {
+#pragma unroll
+  for (int r = 0; r < 16; ++r) {
+    if (r >= k) break;
     float bv = -2.f;
     int bi = 0x7fffffff;
-    for (int i = 0; i < per; ++i) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
       const int e = lane + 32 * i;
       if (p[i] > bv || (p[i] == bv && e < bi)) {
         bv = p[i];
@@ -389,10 +398,14 @@ __global__ void router_topk_kernel(const bf16* logits, long ld, int T, int E, in
     tw[r] = found ? bv : 0.f;
     ti[r] = found ? bi : -1;
     tot += tw[r];
-    if (found && (bi % 32) == lane) p[bi / 32] = -1.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i)
+      if (found && lane + 32 * i == bi) p[i] = -1.f;
   }
   if (lane == 0) {
-    for (int r = 0; r < k; ++r) {
+#pragma unroll
+    for (int r = 0; r < 16; ++r) {
+      if (r >= k) break;
       // renormalised weight, rounded through the logits dtype like the reference (.to(bf16))
       wout[t * k + r] = ti[r] >= 0 ? rbf(tw[r] / tot) : 0.f;
       iout[t * k + r] = ti[r];
@@ -403,7 +416,20 @@ __global__ void router_topk_kernel(const bf16* logits, long ld, int T, int E, in
 int router_topk(const void* logits, long ld, int T, int E, int k, float* w, int* idx, cudaStream_t s) {
   if (!T) return 0;
   if (E > 1024 || k > 16) return -1;
-  router_topk_kernel<<<(T + 7) / 8, 256, 0, s>>>((const bf16*)logits, ld, T, E, k, w, idx);
+  const int per = (E + 31) / 32;
+  const dim3 grid((T + 7) / 8), block(256);
+  if (per <= 1)
+    router_topk_kernel<1><<<grid, block, 0, s>>>((const bf16*)logits, ld, T, E, k, w, idx);
+  else if (per <= 2)
+    router_topk_kernel<2><<<grid, block, 0, s>>>((const bf16*)logits, ld, T, E, k, w, idx);
+  else if (per <= 4)
+    router_topk_kernel<4><<<grid, block, 0, s>>>((const bf16*)logits, ld, T, E, k, w, idx);
+  else if (per <= 8)
+    router_topk_kernel<8><<<grid, block, 0, s>>>((const bf16*)logits, ld, T, E, k, w, idx);
+  else if (per <= 16)
+    router_topk_kernel<16><<<grid, block, 0, s>>>((const bf16*)logits, ld, T, E, k, w, idx);
+  else
+    router_topk_kernel<32><<<grid, block, 0, s>>>((const bf16*)logits, ld, T, E, k, w, idx);
   return (int)cudaGetLastError();
 }
 
