@@ -533,6 +533,41 @@ int gemm_streamk_ctas(int T, int N, int K) {
   return split < whole ? (int)ctas : 0;
 }
 
+// Token-tile width (a multiple of 16, at most 256) for more than 128 tokens. The tokens split
+// evenly over tt tiles; every (weight tile, token tile) pair is one work tile of the persistent
+// grid, so a step costs about waves(tt) x (bn + c0) token columns, c0 being a tile's fixed cost
+// (pipeline fill, epilogue), about 32 columns at K = 4096 and relatively more for shorter K.
+// Narrower tiles pay when the weight tiles alone leave the last wave ragged: 21 weight tiles x 8
+// tiles of 256 tokens = 168 tiles on 148 SMs run as two full-length waves, 21 x 13 tiles of 160
+// as two waves of shorter tiles. The cheapest width is taken only when the model has it 10 %
+// under the widest one: measured, 2048 tokens x 2576 x 4096 went 52.4 -> 45.8 us (160 wide), but
+// 800 x 20608 x 4096 lost 8 % at 160 wide for a modelled 4 % gain (with many waves the ragged last
+// one matters less than the narrower MMAs). QB_GEMM_BN_FIT=0: the widest width only (the tokens
+// split evenly over ceil(T / 256) tiles).
+int gemm_token_tile(int T, int N, int K) {
+  const int tt0 = (T + 255) / 256;
+  const int widest = ((T + tt0 - 1) / tt0 + 15) / 16 * 16;
+  static const int fit = getenv("QB_GEMM_BN_FIT") ? atoi(getenv("QB_GEMM_BN_FIT")) : 1;
+  if (!fit) return widest;
+  const int sms = num_sms();
+  const long wt = (N + 127) / 128;
+  const double c0 = 32.0 * 4096.0 / (K > 128 ? K : 128);
+  int best = widest;
+  double best_cost = 1e300, widest_cost = 0.0;
+  for (int tt = tt0;; ++tt) {
+    const int bn = ((T + tt - 1) / tt + 15) / 16 * 16;
+    const long tiles = wt * tt;
+    const double cost = (double)((tiles + sms - 1) / sms) * (bn + c0);
+    if (tt == tt0) widest_cost = cost;
+    if (cost < best_cost) {
+      best_cost = cost;
+      best = bn;
+    }
+    if (bn <= 64) break;
+  }
+  return best_cost < 0.9 * widest_cost ? best : widest;
+}
+
 long gemm_split_ws_floats(int T, int N, int K) {
   const int c = gemm_streamk_ctas(T, N, K);
   return c ? (long)c * 2 * 128 * gemm_bn(T) : 0;
@@ -545,10 +580,7 @@ int gemm_ws(const void* x, long ldx, const void* w, long ldw, void* y, long ldy,
   int BN = gemm_bn(T);
   // the widest tile: the tokens split evenly over its tile count (800 -> 4 x 208, not 3 x 256 + 32)
   int bn = BN;
-  if (BN == 256) {
-    const int tt = (T + 255) / 256;
-    bn = ((T + tt - 1) / tt + 15) / 16 * 16;
-  }
+  if (BN == 256) bn = gemm_token_tile(T, N, K);
   CUtensorMap tw, tx;
   int r = make_tmap_2d(&tw, w, 2, N, K, ldw, 128, BK, true);
   if (r) return 1000 + r;
