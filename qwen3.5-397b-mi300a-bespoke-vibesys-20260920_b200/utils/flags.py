@@ -63,7 +63,8 @@ _def("QB_DN_DECODE", str, "", "DeltaNet decode mixer state path: reg (registers)
      "empty: sm from 16 lanes up", native=True)
 _def("QB_DN_PREFILL", str, "auto", "DeltaNet prefill segments: tc (chunked WY form, state in tensor memory, "
      "tcgen05 products), recurrence (fp32 token recurrence), chunked_fp32 (chunked WY form on CUDA cores), auto "
-     "(tc up to 32 value heads per rank, else recurrence)",
+     "(tc up to 32 value heads per rank, and at more heads for batches whose longest segment has 128 tokens or more, "
+     "else recurrence)",
      lockstep=True)
 _def("QB_GRAPHS", bool, True, "capture decode steps in CUDA graphs", lockstep=True)
 _def("QB_PREFILL_ORDER", str, "shortest", "scheduler: order prefill flights are packed in: shortest (fewest "
