@@ -695,7 +695,23 @@ __global__ void mx_expand_kernel(const uint8_t* qhi, const uint8_t* qlo, const u
   const uint4* sl = reinterpret_cast<const uint4*>(qlo + src * K);
   uint4* dh = reinterpret_cast<uint4*>(hi + (long)a * K);
   uint4* dl = reinterpret_cast<uint4*>(lo + (long)a * K);
-  for (int v = lane; v < K / 16; v += 32) {
+  // eight 16-byte loads in flight per lane before their stores (the rows come from L2)
+  const int nv = K / 16;
+  int v = lane;
+  for (; v + 96 < nv; v += 128) {
+    uint4 h[4], l[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      h[u] = sh[v + 32 * u];
+      l[u] = sl[v + 32 * u];
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      dh[v + 32 * u] = h[u];
+      dl[v + 32 * u] = l[u];
+    }
+  }
+  for (; v < nv; v += 32) {
     dh[v] = sh[v];
     dl[v] = sl[v];
   }
