@@ -20,8 +20,9 @@
 // K e^(G_last - G) (bf16, M-major), and e^(G_last).
 //
 // dn_tc_state (grid: segment x value head x value-column half, 128 threads): walks the segment's chunks in order with
-// the fp32 state S in tensor memory (lane = key row, 128 columns). Per chunk, after one bulk copy
-// of the record: S is read once (tcgen05.ld) to a bf16 MN-major operand and written back scaled
+// the fp32 state S in tensor memory (lane = key row, 128 columns). Per chunk, once the chunk's record
+// has landed (bulk copies in three parts, each requested for the next chunk as soon as this
+// chunk has used its shared-memory region): S is read once (tcgen05.ld) to a bf16 MN-major operand and written back scaled
 // by e^(G_last); MMA  D1 = W S;  threads form Delta = U - D1 (bf16 operand);  MMAs
 // D2 = (Q e^G) S + Mq Delta  and  S += (K e^(G_last-G))^T Delta  (accumulating in TMEM); threads
 // write O = D2. All MMAs are kind::f16 (bf16 operands, fp32 accumulate), M = 128 (the 64-token
@@ -350,10 +351,15 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
   extern __shared__ uint8_t smem_raw[];
   const uint32_t base_u = (smem_u32(smem_raw) + 1023u) & ~1023u;
   uint8_t* base = smem_raw + (base_u - smem_u32(smem_raw));
-  uint64_t* bar_rec = reinterpret_cast<uint64_t*>(base + S_BAR);
-  uint64_t* bar_mma = bar_rec + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_rec + 2);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_rec + 3);
+  // the chunk record arrives in three parts, each with its barrier, so that the next chunk's part
+  // is requested as soon as this chunk has used its shared-memory region: W after the first MMA,
+  // U and e^(G_last) after Delta, the rest (Q e^G, Mq, K e^(G_last - G)) after the last MMAs
+  uint64_t* bar_w = reinterpret_cast<uint64_t*>(base + S_BAR);
+  uint64_t* bar_u = bar_w + 1;
+  uint64_t* bar_r = bar_w + 2;
+  uint64_t* bar_mma = bar_w + 3;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bar_w + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(bar_w + 5);
   // NS value columns of the state per CTA (blockIdx.z picks which): the columns evolve
   // independently (Delta, O and the update are column-wise in V), so a head can be split over
   // CTAs by value columns; 64 columns are exactly one N-atom of the MN-major operands
@@ -372,7 +378,9 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     reinterpret_cast<uint4*>(base + S_M + 8192)[i] = z;
   }
   if (tid == 0) {
-    mbar_init(bar_rec, 1);
+    mbar_init(bar_w, 1);
+    mbar_init(bar_u, 1);
+    mbar_init(bar_r, 1);
     mbar_init(bar_mma, 1);
     *abort_flag = 0;
     fence_barrier_init();
@@ -402,34 +410,47 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     tmem_st32(lane_t + TM_S + 32 * q, r);
   }
   tmem_wait_st();
-  auto load_rec = [&](int c) {
-    const uint8_t* rec = rec_all + ((long)c * nv + h) * REC;
-    const uint32_t bar = smem_u32(bar_rec);
-    mbar_expect_tx_s(bar, (uint32_t)(R_END));
-    bulk_g2s_s(base_u + S_U, rec + R_U, 32784, bar);
-    bulk_g2s_s(base_u + S_W, rec + R_W, 8192, bar);
-    bulk_g2s_s(base_u + S_W + 16384, rec + R_W + 8192, 8192, bar);
-    bulk_g2s_s(base_u + S_QG, rec + R_QG, 8192, bar);
-    bulk_g2s_s(base_u + S_QG + 16384, rec + R_QG + 8192, 8192, bar);
-    bulk_g2s_s(base_u + S_M, rec + R_M, 8192, bar);
-    bulk_g2s_s(base_u + S_KG, rec + R_KG, 16384, bar);
+  auto rec_of = [&](int c) { return rec_all + ((long)c * nv + h) * REC; };
+  auto load_w = [&](int c) {
+    const uint32_t bar = smem_u32(bar_w);
+    mbar_expect_tx_s(bar, 16384u);
+    bulk_g2s_s(base_u + S_W, rec_of(c) + R_W, 8192, bar);
+    bulk_g2s_s(base_u + S_W + 16384, rec_of(c) + R_W + 8192, 8192, bar);
   };
-  int rec_issued = 0, rec_done = 0, mma_issued = 0, mma_done = 0;  // issue counts kept by thread 0
+  auto load_u = [&](int c) {  // U, then e^(G_last)
+    const uint32_t bar = smem_u32(bar_u);
+    mbar_expect_tx_s(bar, 32784u);
+    bulk_g2s_s(base_u + S_U, rec_of(c) + R_U, 32784, bar);
+  };
+  auto load_r = [&](int c) {
+    const uint32_t bar = smem_u32(bar_r);
+    mbar_expect_tx_s(bar, 40960u);
+    bulk_g2s_s(base_u + S_QG, rec_of(c) + R_QG, 8192, bar);
+    bulk_g2s_s(base_u + S_QG + 16384, rec_of(c) + R_QG + 8192, 8192, bar);
+    bulk_g2s_s(base_u + S_M, rec_of(c) + R_M, 8192, bar);
+    bulk_g2s_s(base_u + S_KG, rec_of(c) + R_KG, 16384, bar);
+  };
+  // issue counts (kept by thread 0, which issues every copy and MMA): copies of each record part,
+  // MMA groups; `*_done` counts the completions every thread has waited for
+  int w_issued = 0, u_issued = 0, r_issued = 0, w_done = 0, u_done = 0, r_done = 0, mma_issued = 0, mma_done = 0;
   if (tid == 0) {
     fence_proxy_async_smem();
-    load_rec(c_begin);
-    ++rec_issued;
+    load_u(c_begin);
+    load_w(c_begin);
+    load_r(c_begin);
+    ++u_issued, ++w_issued, ++r_issued;
   }
   const uint32_t idesc = idesc_f16(128, NS, true) | (1u << 16);  // A K-major, B MN-major
   const uint32_t idesc_mn = idesc | (1u << 15);                    // A MN-major too
-  uint32_t ph_rec = 0, ph_mma = 0;
+  uint32_t ph_w = 0, ph_u = 0, ph_r = 0, ph_mma = 0;
   bool ok = true;
   for (int c = c_begin; c < c_end && ok; ++c) {
     const int row0 = chunks[c * 3 + 1], rows = chunks[c * 3 + 2];
-    // 1. the record has landed
-    if (!__syncthreads_and(mbar_wait(bar_rec, ph_rec, err, ERR_TMA_WAIT, abort_flag))) { ok = false; break; }
-    ph_rec ^= 1;
-    ++rec_done;
+    const bool more = c + 1 < c_end;
+    // 1. U and e^(G_last) of this chunk have landed
+    if (!__syncthreads_and(mbar_wait(bar_u, ph_u, err, ERR_TMA_WAIT, abort_flag))) { ok = false; break; }
+    ph_u ^= 1;
+    ++u_done;
     // 2. S -> bf16 MN-major operand (row tid), and S *= e^(G_last) in place
     {
       const float egl = *reinterpret_cast<const float*>(base + S_U + R_EGL);
@@ -453,7 +474,10 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
-    // 3. D1 = W S
+    // 3. D1 = W S (once W has landed)
+    if (!__syncthreads_and(mbar_wait(bar_w, ph_w, err, ERR_TMA_WAIT, abort_flag))) { ok = false; break; }
+    ph_w ^= 1;
+    ++w_done;
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -469,6 +493,11 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     ph_mma ^= 1;
     ++mma_done;
     tc_fence_after();
+    if (tid == 0 && more) {  // W has been read: the next chunk's W streams in from here on
+      fence_proxy_async_smem();
+      load_w(c + 1);
+      ++w_issued;
+    }
     // 4. Delta = U - D1 (token rows 0..63: warps 0 and 1) -> bf16 MN-major operand
     if (warp < 2) {
       const float* u = reinterpret_cast<const float*>(base + S_U) + tid * D + col0;
@@ -489,7 +518,15 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     fence_proxy_async_smem();
     tc_fence_before();
     __syncthreads();
-    // 5. D2 = (Q e^G) S + Mq Delta;  S += (K e^(G_last - G))^T Delta
+    if (tid == 0 && more) {  // U has been read (every thread passed the barrier): the next U
+      fence_proxy_async_smem();
+      load_u(c + 1);
+      ++u_issued;
+    }
+    // 5. D2 = (Q e^G) S + Mq Delta;  S += (K e^(G_last - G))^T Delta (once the rest has landed)
+    if (!__syncthreads_and(mbar_wait(bar_r, ph_r, err, ERR_TMA_WAIT, abort_flag))) { ok = false; break; }
+    ph_r ^= 1;
+    ++r_done;
     if (tid == 0) {
       tc_fence_after();
 #pragma unroll
@@ -513,11 +550,11 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
     ph_mma ^= 1;
     ++mma_done;
     tc_fence_after();
-    // 6. the next record streams in while the outputs of this chunk go out
-    if (tid == 0 && c + 1 < c_end) {
+    // 6. the rest of the next record streams in while the outputs of this chunk go out
+    if (tid == 0 && more) {
       fence_proxy_async_smem();
-      load_rec(c + 1);
-      ++rec_issued;
+      load_r(c + 1);
+      ++r_issued;
     }
     if (warp < 2) {  // whole warps: tcgen05.ld is warp-collective; only the stores are per row
       bf16* o = out + ((long)(row0 + tid) * nv + h) * D + col0;
@@ -535,8 +572,12 @@ __global__ void __launch_bounds__(128, 1) dn_tc_state_kernel(const uint8_t* rec_
   // ---- after a give-up: let this CTA's own copies and MMAs in flight finish (bounded) before
   // its shared memory and tensor memory are released
   if (!ok && tid == 0) {
-    for (; rec_done < rec_issued; ++rec_done, ph_rec ^= 1)
-      if (!mbar_wait(bar_rec, ph_rec, err, ERR_DRAIN, nullptr)) break;
+    for (; u_done < u_issued; ++u_done, ph_u ^= 1)
+      if (!mbar_wait(bar_u, ph_u, err, ERR_DRAIN, nullptr)) break;
+    for (; w_done < w_issued; ++w_done, ph_w ^= 1)
+      if (!mbar_wait(bar_w, ph_w, err, ERR_DRAIN, nullptr)) break;
+    for (; r_done < r_issued; ++r_done, ph_r ^= 1)
+      if (!mbar_wait(bar_r, ph_r, err, ERR_DRAIN, nullptr)) break;
     for (; mma_done < mma_issued; ++mma_done, ph_mma ^= 1)
       if (!mbar_wait(bar_mma, ph_mma, err, ERR_DRAIN, nullptr)) break;
   }
