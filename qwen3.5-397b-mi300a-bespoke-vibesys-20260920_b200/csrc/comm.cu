@@ -44,6 +44,7 @@ constexpr int AR_THREADS = 256;
 __global__ void __launch_bounds__(AR_THREADS) ar_add_rmsnorm_kernel(
     SymmPtrs ptrs, const bf16* partial, long ldp, bf16* res, const float* w1p, bf16* out, int rows, int H,
     float eps, long slot_elems, int max_blocks, int* epoch, int* done, int* err, unsigned long long timeout_ns) {
+  pdl_launch_dependents();  // the next projection (launched as a dependent) may start its prologue
   __shared__ float red[32];
   __shared__ int s_epoch;
   if (threadIdx.x == 0) s_epoch = *reinterpret_cast<volatile int*>(epoch) + 1;

@@ -37,6 +37,15 @@ __device__ __forceinline__ uint64_t globaltimer() {
   return t;
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic stream serialization
+// attribute may be scheduled before the previous kernel on its stream has finished; pdl_wait()
+// blocks until that kernel's grid has completed and its memory is visible (a no-op for a normal
+// launch), so every read of the predecessor's results and every global write comes after it.
+// pdl_launch_dependents() lets such a dependent be scheduled now: it still waits in pdl_wait()
+// for this grid's completion, so calling it at a kernel's entry is always safe.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }

@@ -37,6 +37,7 @@ constexpr int NORM_MAXV = 4;  // up to 4 x 8 elements per thread (H <= 8192)
 template <bool ADD>
 __global__ void __launch_bounds__(NORM_T) norm_kernel(const bf16* x, long ldx, bf16* res, long ldr, const float* w1p,
                                                       bf16* out, long ldo, int H, float eps) {
+  pdl_launch_dependents();  // the next projection (launched as a dependent) may start its prologue
   __shared__ float red[32];
   const long r = blockIdx.x;
   const bf16* xr = x + r * ldx;
@@ -108,6 +109,7 @@ int add_rmsnorm(const void* x, long ldx, void* res, long ldr, const float* w1p, 
 // One warp per (token, head): y = bf16(w * bf16(norm(x))) * silu(z), rounded to bf16.
 __global__ void gated_rmsnorm_kernel(const bf16* core, const bf16* z, long ldz, const bf16* w, bf16* out, int T,
                                      int heads, int dv, float eps) {
+  pdl_launch_dependents();  // the next projection (launched as a dependent) may start its prologue
   const long gw = (long)blockIdx.x * (blockDim.x / 32) + threadIdx.x / 32;
   const int lane = threadIdx.x % 32;
   if (gw >= (long)T * heads) return;
@@ -142,6 +144,7 @@ int gated_rmsnorm(const void* core, const void* z, long ldz_row, const void* w, 
 
 // ------------------------------------------------------------------ small elementwise ops
 __global__ void silu_mul_kernel(const bf16* gu, long ldg, bf16* out, long ldo, int T, int n) {
+  pdl_launch_dependents();  // the next projection (launched as a dependent) may start its prologue
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long)T * n) return;
   const long t = i / n;
@@ -225,6 +228,7 @@ int argmax_rows(const void* x, long ldx, int dtype, int R, int V, float* val, in
 }
 
 __global__ void sigmoid_gate_mul_kernel(const bf16* x, long ldx, const bf16* g, long ldg, bf16* out, int T, int D) {
+  pdl_launch_dependents();  // the next projection (launched as a dependent) may start its prologue
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long)T * D) return;
   const long t = i / D;

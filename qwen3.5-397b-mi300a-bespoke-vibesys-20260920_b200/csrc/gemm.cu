@@ -194,6 +194,10 @@ __device__ __forceinline__ void gemm_ws_body(const CUtensorMap* tmW, const CUten
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     if (elect_one()) {
+      // launched as a programmatic dependent, everything above overlapped the previous kernel;
+      // its results (the activations) are read from here on, and every write of this grid (the
+      // epilogue's, after the MMAs on these loads) comes later still
+      pdl_wait();
       int it = 0;
       SegIter sg(blockIdx.x, a.ctas, gridDim.x, tiles, kblocks);
       int tile, k0, k1;
@@ -496,6 +500,12 @@ static int num_sms() {
   return n;
 }
 
+// QB_PDL (default 1): dense GEMMs are launched as programmatic dependents of the previous kernel.
+static bool gemm_pdl() {
+  static const int on = getenv("QB_PDL") ? atoi(getenv("QB_PDL")) : 1;
+  return on != 0;
+}
+
 template <int BN, typename OutT>
 static int launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArgs& a, bool bf16, int max_ctas,
                      cudaStream_t st) {
@@ -509,7 +519,22 @@ static int launch_bn(const CUtensorMap& tw, const CUtensorMap& tx, const GemmArg
   const int tiles = ((a.N + 127) / 128) * ((a.T + a.bn - 1) / a.bn);
   int grid = a.ctas ? a.ctas : tiles < max_ctas ? tiles : max_ctas;
   if (grid < 1) grid = 1;
-  k<<<grid, GEMM_THREADS, C::SMEM, st>>>(tw, tx, a, idesc_f16(128, a.bn, bf16));
+  const uint32_t idesc = idesc_f16(128, a.bn, bf16);
+  if (gemm_pdl()) {  // programmatic dependent: the prologue overlaps the previous kernel's tail
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(GEMM_THREADS);
+    cfg.dynamicSmemBytes = C::SMEM;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = 1;
+    cudaLaunchKernelEx(&cfg, k, tw, tx, a, idesc);
+  } else {
+    k<<<grid, GEMM_THREADS, C::SMEM, st>>>(tw, tx, a, idesc);
+  }
   return (int)cudaGetLastError();
 }
 

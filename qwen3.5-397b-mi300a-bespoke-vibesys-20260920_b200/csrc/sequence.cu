@@ -307,6 +307,7 @@ __global__ void __launch_bounds__(256, 2)
     delta_decode_kernel(const bf16* proj, long ldp, bf16* cstate, long cls, const bf16* cw, const float* a_log,
                         const float* dt_bias, float* state, long sls, const bf16* norm_w, const int* seg_lane, int nk,
                         int nv, float eps, bf16* out) {
+  pdl_launch_dependents();  // the next projection (launched as a dependent) may start its prologue
   constexpr int K = 4, RPW = DK / 8;
   static_assert(DV == 128 && DK % 32 == 0, "one float4 of columns per lane");
   __shared__ float qs[DK], ks[DK], vs[DV], os[DV];
@@ -468,6 +469,7 @@ __global__ void __launch_bounds__(256, 3)
     delta_decode_sm_kernel(const bf16* proj, long ldp, bf16* cstate, long cls, const bf16* cw, const float* a_log,
                         const float* dt_bias, float* state, long sls, const bf16* norm_w, const int* seg_lane, int nk,
                         int nv, float eps, bf16* out, int* err) {
+  pdl_launch_dependents();  // the next projection (launched as a dependent) may start its prologue
   constexpr int K = 4, RPW = DK / 8;
   static_assert(DV == 128 && DK % 32 == 0, "one float4 of columns per lane");
   __shared__ float qs[DK], ks[DK], vs[DV], os[DV];
