@@ -41,6 +41,9 @@ def init(backend: str | None = None, rank: int | None = None, world: int | None 
     world = w if world is None else world
     if world <= 1 or dist.is_initialized():
         return (dist.get_rank(), dist.get_world_size()) if dist.is_initialized() else (0, 1)
+    # programmatic dependent launches of the GEMMs are measured and tested on one GPU; a
+    # multi-rank run keeps plain launches unless QB_PDL is set explicitly (every rank alike)
+    os.environ.setdefault("QB_PDL", "0")
     if backend is None:
         backend = "nccl" if torch.cuda.is_available() else "gloo"
     if backend == "nccl":

@@ -50,7 +50,8 @@ _def("QB_DN_VSPLIT", int, 0, "chunked DeltaNet state kernel: CTAs per value head
 _def("QB_GEMM_BN_FIT", int, 1, "dense GEMM above 128 tokens: token-tile width fitted to the SM waves (0: the widest "
      "width, the tokens split evenly over ceil(T / 256) tiles)", native=True)
 _def("QB_PDL", int, 1, "dense GEMMs launched as programmatic dependents (their prologue overlaps the previous "
-     "kernel, which signals early; 0: plain launches)", native=True)
+     "kernel, which signals early; 0: plain launches); a multi-rank process group sets 0 unless given",
+     lockstep=True, native=True)
 _def("QB_MX_K2", int, -1, "block-scaled MoE, wide path: two 128-K atoms per pipeline stage (1), one (0), "
      "or two for token tiles of at most 32 rows (-1)", native=True)
 _def("QB_MX_PROBE", bool, False, "block-scaled MoE: count the producer / MMA wait cycles (diagnostic)",
