@@ -42,6 +42,12 @@ def pool_bytes(cfg: Qwen35Config, p, spec: PoolSpec) -> tuple[int, int, int]:
     return kv, (spec.lanes + snaps) * per_state, num_blocks
 
 
+def prefill_graph_widths(flag: str) -> list[int]:
+    """Widths of the captured single-segment prefill steps from ``QB_PREFILL_GRAPHS`` ("512,2048"; empty:
+    none)."""
+    return [int(w) for w in str(flag or "").replace(" ", "").split(",") if w.strip().isdigit() and int(w) > 0]
+
+
 def nvls_min_rows(flag: int, world: int) -> int:
     """Smallest all-reduce (rows) that takes the NVLS kernel, 0 for never. ``flag`` -1 chooses by
     world size from the collective sweep (hidden 4096, device time, max over ranks): at 8 ranks the
@@ -116,6 +122,9 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
 
         g = GraphRunner(m)
         g.prepare()
+        widths = prefill_graph_widths(flags.get("QB_PREFILL_GRAPHS"))
+        if widths:
+            g.prepare_prefill(widths)
         mem.phase("graphs")
         pool_plan(m, rank)
         return g, distinct

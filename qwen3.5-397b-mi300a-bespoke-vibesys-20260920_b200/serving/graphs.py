@@ -11,6 +11,15 @@ snapshots, blocks) is delegated to the wrapped model.
 
 Reference behaviour: ``graph_decode.py:250-1725`` (``DEFAULT_BUCKET_SIZES``, ``GraphDecodeRunner``,
 ``fill``, ``prepare``, ``validate``), with its masked-row idea realised as a pad lane.
+
+Prefill steps (``prepare_prefill``, ``QB_PREFILL_GRAPHS``): one graph per width W replays a
+single-segment prefill of exactly W tokens on any lane at any start position. The lane, the start
+and every row's position and KV row are device inputs; the tables the host plans for a forward
+(flash-attention tiles, DeltaNet chunks) depend only on the segment lengths, here always (W,), so
+no padding is needed and nothing else changes between replays: the chunks of a long prompt cut at
+the prefill chunk size, and follow-up turns of a captured length, replay instead of issuing their
+~1250 launches. Batches of several segments and other lengths run eagerly. Reference behaviour:
+``graph_prefill.py:812`` (``PrefillGraphRunner``, captured rows x width shapes).
 """
 
 from __future__ import annotations
@@ -140,6 +149,36 @@ class _Bucket:
                           list(lanes), list(range(B + 1)), list(starts), model.max_seq)
 
 
+class _PrefillBucket:
+    """Static buffers of one captured single-segment prefill of exactly ``W`` tokens."""
+
+    def __init__(self, model, W: int):
+        dev = model.device
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.W = W
+        self.tokens = torch.zeros(W, dtype=torch.int64, device=dev)
+        self.packed_dev = torch.zeros(2 * W + 2, **i32)  # positions | KV rows | lane | start
+        self.pos = torch.zeros(W, **i32)
+        self.rows = torch.zeros(W, **i32)
+        self.lane = torch.zeros(1, **i32)
+        self.start = torch.zeros(1, **i32)
+        self.cu = torch.tensor([0, W], **i32)
+        self.logit_rows = torch.tensor([W - 1], dtype=torch.int64, device=dev)
+        # two pinned input sets used alternately (a fill never overwrites one whose copy may be queued)
+        self._hosts = [(_host(torch.zeros(2 * W + 2, dtype=torch.int32)), _host(torch.zeros(W, dtype=torch.int64)))
+                       for _ in range(2)]
+        self._flip = 0
+        self.lane_h, self.start_h = model.max_batch - 1, 0
+        self.graph = None
+        self.out = None
+
+    def inputs(self, model) -> StepInputs:
+        """The bucket's device inputs; the host lists are the last fill's lane and start (read only
+        by the host reference ops of a CPU rank) and the fixed segment length."""
+        return StepInputs(self.tokens, self.pos, self.rows, self.lane, self.cu, self.start, self.logit_rows,
+                          [self.lane_h], [0, self.W], [self.start_h], model.max_seq)
+
+
 class _SpecBucket:
     """Static buffers of one captured speculative round for ``B`` lanes and draft depth ``k``:
     the draft steps' positions and KV rows, the verify forward's ``B x (k+1)`` rows, and the
@@ -209,6 +248,9 @@ class GraphRunner:
         self.enabled = flags.get("QB_GRAPHS")
         self.replays = 0
         self.launch_per_replay: dict[int, int] = {}
+        self._pb: dict[int, _PrefillBucket] = {}  # captured prefill widths
+        self.prefill_replays = 0
+        self.prefill_validated = False
 
     # ------------------------------------------------------------------ capture
     def _fill(self, bk: _Bucket, lanes, tokens, positions):
@@ -318,6 +360,130 @@ class GraphRunner:
             self.release()
         self.validated = agreed
         return agreed
+
+    # ------------------------------------------------------------------ prefill steps
+    def _prefill_fill(self, bk: _PrefillBucket, lane: int, ids, start: int, rows=None) -> None:
+        m = self.model
+        W = bk.W
+        m._gpu_mark("in")
+        bk._flip ^= 1
+        ph, th = bk._hosts[bk._flip]
+        if rows is None:
+            rows = [m._row(lane, p) for p in range(start, start + W)]
+        ph[:W] = torch.arange(start, start + W, dtype=torch.int32)
+        ph[W:2 * W] = torch.tensor(rows, dtype=torch.int32)
+        ph[2 * W] = lane
+        ph[2 * W + 1] = start
+        th.copy_(torch.tensor([int(t) for t in ids], dtype=torch.int64))
+        bk.lane_h, bk.start_h = lane, start
+        bk.packed_dev.copy_(ph, non_blocking=True)
+        bk.tokens.copy_(th, non_blocking=True)
+        bk.pos.copy_(bk.packed_dev[:W])
+        bk.rows.copy_(bk.packed_dev[W:2 * W])
+        bk.lane.copy_(bk.packed_dev[2 * W:2 * W + 1])
+        bk.start.copy_(bk.packed_dev[2 * W + 1:])
+        m._h2d += ph.numel() * 4 + th.numel() * 8
+        m._sync_tables()
+
+    def _prefill_run(self, bk: _PrefillBucket):
+        """The captured step: the forward over the bucket's one segment and its last row's logits."""
+        m = self.model
+        return m.logits(m._forward(bk.inputs(m)))
+
+    def prepare_prefill(self, widths) -> None:
+        """Capture one single-segment prefill step per width (largest first, in the decode graphs'
+        memory pool) on the pad lane, whose KV rows all go to the reserved block, then check each
+        against an eager forward (``validate_prefill``). Every rank in the same order; skipped with
+        an MTP head (its catch-up follows every forward) or when graphs are off."""
+        m = self.model
+        widths = sorted({int(w) for w in widths if 0 < int(w) <= m.max_seq}, reverse=True)
+        if (not self.enabled or not widths or m.mtp is not None
+                or (m.device.type != "cuda" and not isinstance(self.backend, HostGraphs))):
+            return
+        import time
+
+        m.begin(self.pad_lane)
+        m.attach_blocks(self.pad_lane, [])
+        for W in widths:
+            t0 = time.perf_counter()
+            bk = _PrefillBucket(m, W)
+            self._prefill_fill(bk, self.pad_lane, [0] * W, 0, rows=[0] * W)
+            l0 = self.backend.count_launches()
+            with torch.inference_mode():
+                bk.graph, bk.out = self.backend.capture(lambda bk=bk: self._prefill_run(bk))
+            self.launch_per_replay[-W] = (self.backend.count_launches() - l0) // 3  # warm-ups + capture
+            self._pb[W] = bk
+            if flags.get("QB_GRAPH_LOG"):
+                print(f"[graph-capture] prefill width {W}: {self.launch_per_replay[-W]} kernels, "
+                      f"{time.perf_counter() - t0:.2f}s", flush=True)
+        self.backend.sync()
+        self.validate_prefill()
+
+    def validate_prefill(self, tol: float = 5e-2) -> bool:
+        """Boot check of every captured prefill width: W tokens on lane 0 (nothing is served yet)
+        through the replay and through an eager forward from the same reset state must give the
+        same logits within ``tol`` of their scale; the ranks agree on the minimum (as the decode
+        buckets do) and the prefill graphs are dropped on every rank if any disagrees."""
+        m = self.model
+        ok, worst, lane = True, 0.0, 0
+        with torch.inference_mode():
+            for W, bk in sorted(self._pb.items()):
+                blocks = list(range(1, 1 + -(-W // m.block_size)))
+                ids = [(13 * i + 7) % min(m.cfg.vocab, 1000) for i in range(W)]
+
+                def reset():
+                    m.begin(lane)
+                    m.attach_blocks(lane, blocks)
+
+                reset()
+                self._prefill_fill(bk, lane, ids, 0)
+                bk.graph.replay()
+                got = bk.out.float().clone()
+                reset()
+                exp = m.forward([(lane, ids, 0)]).float()
+                m.begin(lane)
+                m.attach_blocks(lane, [])
+                err = (got - exp).abs().max().item()
+                scale = exp.abs().max().item() + 1e-6
+                worst = max(worst, err / scale)
+                if not (err <= tol * scale) or not bool(torch.isfinite(got).all()):
+                    ok = False
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=m.device)
+        if getattr(m.comm, "world", 1) > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        agreed = bool(int(flag.item()))
+        if flags.get("QB_GRAPH_LOG") or not agreed:
+            print(f"[graph-capture] prefill validation: this rank {'ok' if ok else 'MISMATCH'} (worst relative "
+                  f"{worst:.2e}), all ranks {'ok' if agreed else 'disagree: prefill runs eagerly'}", flush=True)
+        if not agreed:
+            for bk in self._pb.values():
+                bk.graph = bk.out = None
+            self._pb.clear()
+        self.prefill_validated = agreed
+        return agreed
+
+    def prefill_batch(self, calls):
+        """``Model.prefill_batch``; one segment of a captured length is replayed from its graph (the
+        logits row is copied out: the session cache may keep it past the next replay)."""
+        calls = list(calls)
+        m = self.model
+        if len(calls) == 1 and self._pb and not m.fault and m.mtp is None:
+            lane, ids, start = calls[0]
+            bk = self._pb.get(len(ids))
+            if bk is not None and start + len(ids) <= m.max_seq:
+                with torch.inference_mode():
+                    self._prefill_fill(bk, lane, ids, start)
+                    bk.graph.replay()
+                    out = bk.out.clone()
+                self.prefill_replays += 1
+                self.backend.add_launches(self.launch_per_replay.get(-bk.W, 0))
+                return [out]
+        return m.prefill_batch(calls)
+
+    def prefill(self, lane, ids, start):
+        return self.prefill_batch([(lane, ids, start)])[0]
 
     # ------------------------------------------------------------------ speculative rounds
     def _spec_fill(self, bk: _SpecBucket, lanes, tokens, positions) -> None:
@@ -532,6 +698,9 @@ class GraphRunner:
         for sb in self._spec.values():
             sb.graph = sb.commit_graph = None
         self._spec.clear()
+        for pb in self._pb.values():
+            pb.graph = pb.out = None
+        self._pb.clear()
 
     # ------------------------------------------------------------------ runner
     def decode(self, lanes, tokens, positions):

@@ -78,6 +78,8 @@ _def("QB_OVERLAP", bool, True, "scheduler: launch decode step n+1 (tokens fed ba
      "step n back", lockstep=True)
 _def("QB_MTP_DEVICE_ACCEPT", bool, True, "speculative rounds: accepted lengths computed on the device and the whole "
      "round (draft, verify, accept, commit) replayed as one graph, read back once", lockstep=True)
+_def("QB_PREFILL_GRAPHS", str, "", "widths (comma-separated token counts) of captured single-segment prefill steps, "
+     "replayed for one segment of exactly that length (empty: prefill runs eagerly)", lockstep=True)
 _def("QB_GREEDY_HEAD", bool, True, "greedy decode ids from each rank's (max, index) over its vocabulary slice, "
      "gathered as 8-byte pairs (off: the full logits rows are all-gathered, then the argmax)", lockstep=True)
 _def("QB_MOE_FUSE_SHARED", bool, True, "MoE: the shared expert's gated rows are added in the routed combine kernel "

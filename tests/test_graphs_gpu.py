@@ -39,6 +39,50 @@ def test_graph_decode_matches_eager():
     assert g.replays == 3
 
 
+def test_prefill_graphs_match_eager():
+    """Captured single-segment prefill widths (QB_PREFILL_GRAPHS): a prompt and a continuation of
+    captured lengths replayed on one lane give the logits of the eager forwards on another lane
+    with the same history, and the decode steps that follow agree (KV, DeltaNet and conv state
+    written through the graphs)."""
+    from qwen35_b200.models.config import tiny_config
+    from qwen35_b200.models.qwen35 import Model
+    from qwen35_b200.models.weights import random_weights
+    from qwen35_b200.parallel.plan import plan
+    from qwen35_b200.serving.graphs import GraphRunner
+
+    dev = torch.device("cuda")
+    cfg = tiny_config()
+    p = plan(cfg, 0, 1)
+    m = Model(cfg, random_weights(cfg, p, dev, torch.bfloat16, seed=2, with_mtp=False), p, device=dev,
+              max_batch=4, max_seq=512)
+    g = GraphRunner(m, buckets=(1, 2))
+    g.prepare()
+    g.prepare_prefill([64, 128])
+    assert g.prefill_validated and set(g._pb) == {64, 128}
+    a, b = list(range(7, 135)), list(range(300, 364))
+    for lane in (0, 1):
+        m.begin(lane)
+        m.attach_blocks(lane, list(range(1 + 16 * lane, 17 + 16 * lane)))
+    ga = g.prefill_batch([(0, a, 0)])[0].float()
+    gb = g.prefill_batch([(0, b, 128)])[0].float()
+    ea = m.prefill_batch([(1, a, 0)])[0].float()
+    eb = m.prefill_batch([(1, b, 128)])[0].float()
+    torch.cuda.synchronize()
+    assert g.prefill_replays == 2
+    for x, y in ((ga, ea), (gb, eb)):
+        assert torch.equal(x.argmax(-1), y.argmax(-1))
+        assert (x - y).abs().max().item() < 2e-2 * y.abs().max().item() + 1e-2
+    toks, pos = [int(gb.argmax())] * 2, [192, 192]
+    for _ in range(3):
+        lg = m.decode([0, 1], toks, pos).float()
+        torch.cuda.synchronize()
+        assert torch.equal(lg[0].argmax(), lg[1].argmax())
+        assert (lg[0] - lg[1]).abs().max().item() < 2e-2 * lg[1].abs().max().item() + 1e-2
+        toks = [int(lg[0].argmax())] * 2
+        pos = [x + 1 for x in pos]
+    g.release()
+
+
 def test_stamps_inside_captured_graph():
     """%globaltimer stamps recorded inside a CUDA graph: segments are positive and their sum is
     the replay's device time (CUDA events around the replay)."""

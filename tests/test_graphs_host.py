@@ -87,3 +87,53 @@ def test_host_graph_validation_failure_turns_graphs_off():
     _lanes(m, [list(range(3, 12))], 0)
     out = g.decode([0], [5], [9])  # eager fallback
     assert torch.isfinite(out).all() and out.abs().max() < 1e3
+
+
+def test_host_prefill_graphs_match_eager_and_keep_lane_state():
+    """Captured single-segment prefill widths replay on any lane at any start: a 64-token prompt
+    and a 32-token continuation through the graphs leave the lane exactly as the eager forwards
+    do (logits, KV, DeltaNet and conv state: the decode steps that follow agree); other lengths
+    and multi-segment batches run eagerly."""
+    m = _model()
+    g = GraphRunner(m, buckets=(1, 2), backend=HostGraphs())
+    g.prepare()
+    g.prepare_prefill([32, 64])
+    assert g.prefill_validated and set(g._pb) == {32, 64}
+    a, b = list(range(5, 69)), list(range(100, 132))
+    for lane in (0, 1):
+        m.begin(lane)
+        m.attach_blocks(lane, list(range(1 + 8 * lane, 9 + 8 * lane)))
+    ga = g.prefill_batch([(0, a, 0)])[0]
+    gb = g.prefill_batch([(0, b, 64)])[0]
+    assert g.prefill_replays == 2
+    ea = m.prefill_batch([(1, a, 0)])[0]
+    eb = m.prefill_batch([(1, b, 64)])[0]
+    assert torch.allclose(ga, ea, atol=1e-4, rtol=1e-4) and torch.allclose(gb, eb, atol=1e-4, rtol=1e-4)
+    toks, pos = [int(gb.argmax())] * 2, [96, 96]
+    for _ in range(3):
+        lg = m.decode([0, 1], toks, pos)
+        assert torch.allclose(lg[0], lg[1], atol=1e-4, rtol=1e-4)
+        toks = [int(lg[0].argmax())] * 2
+        pos = [p + 1 for p in pos]
+    m.begin(2)
+    m.attach_blocks(2, list(range(17, 25)))
+    g.prefill_batch([(2, list(range(40)), 0)])  # not a captured width: eager
+    assert g.prefill_replays == 2
+
+
+def test_host_prefill_graph_validation_failure_drops_them():
+    class Broken(HostGraphs):
+        def capture(self, fn, warmups=2, pool=True):
+            g, out = super().capture(fn, warmups, pool)
+            if isinstance(out, torch.Tensor):  # the prefill step: garbage logits on replay
+                g.fn = lambda: torch.full_like(out, 1e4)
+            return g, out
+
+    m = _model()
+    g = GraphRunner(m, buckets=(1,), backend=Broken())
+    g.prepare_prefill([32])
+    assert not g.prefill_validated and not g._pb
+    m.begin(0)
+    m.attach_blocks(0, list(range(1, 9)))
+    out = g.prefill_batch([(0, list(range(32)), 0)])[0]  # eager
+    assert torch.isfinite(out).all() and out.abs().max() < 1e3 and g.prefill_replays == 0
