@@ -135,7 +135,7 @@ def save_file(tensors: dict[str, torch.Tensor], path: str, metadata: dict[str, s
     blobs = []
     for name in sorted(tensors):
         t = tensors[name].detach().to("cpu").contiguous()
-        raw = t.view(torch.uint8).numpy().tobytes() if t.numel() else b""
+        raw = t.reshape(-1).view(torch.uint8).numpy().tobytes() if t.numel() else b""  # 0-dim too
         header[name] = {"dtype": _NAMES[t.dtype], "shape": list(t.shape), "data_offsets": [off, off + len(raw)]}
         blobs.append(raw)
         off += len(raw)
