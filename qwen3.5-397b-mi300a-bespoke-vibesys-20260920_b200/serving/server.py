@@ -73,7 +73,14 @@ def parse(argv=None):
     ap.add_argument("--mtp-forced-accept", type=float, default=None,
                     help="accept each draft position with this probability instead of greedy (benchmarking)")
     ap.add_argument("--mixed", action="store_true", help="decode steps also carry prefill chunks")
-    return ap.parse_args(argv)
+    ap.add_argument("--prefill-graphs", default=None,
+                    help="widths (comma-separated token counts) of captured single-segment prefill steps, e.g. "
+                         "the prefill chunk size: a prompt chunk of exactly that length replays its graph "
+                         "(sets QB_PREFILL_GRAPHS on every rank)")
+    args = ap.parse_args(argv)
+    if args.prefill_graphs is not None:
+        os.environ["QB_PREFILL_GRAPHS"] = args.prefill_graphs  # read when the model and its graphs are built
+    return args
 
 
 def _device(args):

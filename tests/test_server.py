@@ -170,3 +170,14 @@ def test_mtp_speculative_server_matches_plain(server):
     finally:
         stop(proc)
     assert len(spec) == 16 and spec == plain
+
+
+def test_prefill_graphs_option_sets_the_flag(monkeypatch):
+    from qwen35_b200.serving import server
+    from qwen35_b200.utils import flags
+
+    monkeypatch.delenv("QB_PREFILL_GRAPHS", raising=False)
+    server.parse(["--model-path", "tiny"])
+    assert flags.get("QB_PREFILL_GRAPHS") == ""
+    server.parse(["--model-path", "tiny", "--prefill-graphs", "512,2048"])
+    assert flags.get("QB_PREFILL_GRAPHS") == "512,2048"
