@@ -176,7 +176,7 @@ def test_prefill_graphs_option_sets_the_flag(monkeypatch):
     from qwen35_b200.serving import server
     from qwen35_b200.utils import flags
 
-    monkeypatch.delenv("QB_PREFILL_GRAPHS", raising=False)
+    monkeypatch.setenv("QB_PREFILL_GRAPHS", "")  # restored after the test (parse writes os.environ)
     server.parse(["--model-path", "tiny"])
     assert flags.get("QB_PREFILL_GRAPHS") == ""
     server.parse(["--model-path", "tiny", "--prefill-graphs", "512,2048"])
