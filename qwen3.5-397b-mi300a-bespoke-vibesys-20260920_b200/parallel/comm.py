@@ -43,7 +43,7 @@ def init(backend: str | None = None, rank: int | None = None, world: int | None 
         return (dist.get_rank(), dist.get_world_size()) if dist.is_initialized() else (0, 1)
     # programmatic dependent launches of the GEMMs are measured and tested on one GPU; a
     # multi-rank run keeps plain launches unless QB_PDL is set explicitly (every rank alike)
-    os.environ.setdefault("QB_PDL", "0")
+    flags.put("QB_PDL", 0, only_if_unset=True)
     if backend is None:
         backend = "nccl" if torch.cuda.is_available() else "gloo"
     if backend == "nccl":

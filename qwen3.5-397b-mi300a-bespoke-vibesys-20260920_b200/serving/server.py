@@ -79,7 +79,7 @@ def parse(argv=None):
                          "(sets QB_PREFILL_GRAPHS on every rank)")
     args = ap.parse_args(argv)
     if args.prefill_graphs is not None:
-        os.environ["QB_PREFILL_GRAPHS"] = args.prefill_graphs  # read when the model and its graphs are built
+        flags.put("QB_PREFILL_GRAPHS", args.prefill_graphs)  # read when the model and its graphs are built
     return args
 
 

@@ -155,6 +155,21 @@ def get(name: str, env: dict | None = None):
         raise ValueError(f"{name}={raw!r}: expected {f.kind.__name__}") from e
 
 
+def put(name: str, value, only_if_unset: bool = False) -> None:
+    """Set a declared flag in this process's environment (which child processes inherit and the
+    native code reads), checking that the value parses; with ``only_if_unset`` an explicit
+    setting of the user wins."""
+    f = _FLAGS.get(name)
+    if f is None:
+        raise KeyError(f"undeclared flag {name}")
+    raw = str(int(value) if isinstance(value, bool) else value)
+    if raw:
+        _parse(f, raw)
+    if only_if_unset and os.environ.get(name) not in (None, ""):
+        return
+    os.environ[name] = raw
+
+
 def snapshot(env: dict | None = None, numerics_only: bool = True) -> dict:
     return {n: get(n, env) for n, f in sorted(_FLAGS.items()) if f.lockstep or not numerics_only}
 

@@ -24,7 +24,7 @@ def test_every_python_flag_read_is_declared():
             assert name in reg, (p.name, name)
         if p.name != "flags.py":
             # QB_* variables are read through the registry only
-            assert not re.search(r'environ(?:\.get)?[\[(]\s*"QB_', text), p.name
+            assert not re.search(r'environ(?:\.get|\.setdefault|\.pop)?[\[(]\s*"QB_', text), p.name
             assert not re.search(r'getenv\(\s*"QB_', text), p.name
 
 
@@ -36,6 +36,22 @@ def test_every_native_flag_read_is_declared():
             seen.add(name)
             assert name in reg and reg[name].native, (p.name, name)
     assert seen == {n for n, f in reg.items() if f.native}
+
+
+def test_flag_put_checks_name_and_value(monkeypatch):
+    monkeypatch.setenv("QB_PDL", "")
+    flags.put("QB_PDL", 0, only_if_unset=True)
+    assert flags.get("QB_PDL") == 0
+    flags.put("QB_PDL", 1, only_if_unset=True)  # already set: the explicit value wins
+    assert flags.get("QB_PDL") == 0
+    flags.put("QB_PDL", 1)
+    assert flags.get("QB_PDL") == 1
+    import pytest
+
+    with pytest.raises(KeyError):
+        flags.put("QB_NOT_A_FLAG", 1)
+    with pytest.raises(ValueError):
+        flags.put("QB_PDL", "many")
 
 
 def test_flag_parsing_and_signature():
