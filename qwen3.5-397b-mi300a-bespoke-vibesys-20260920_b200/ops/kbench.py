@@ -253,7 +253,9 @@ def case_model(tokens: int, ctx: int, lanes: int = 32, shard: int = 1) -> dict:
     layers reused by the rest, as the one-GPU benchmark does): one prefill of ``tokens`` new
     tokens continuing ``ctx`` cached ones, and one ``lanes``-row decode step at context
     ``max(ctx, 2048)``. Prints the step times (CUDA events) and the per-kernel share of device
-    time (torch profiler, a separate run).
+    time (torch profiler, a separate run). Every decode lane feeds the same token id, so the
+    routed experts of a decode step are those of one token (ten per layer): the step is a lower
+    bound of a chat decode step, whose distinct tokens reach ~240 experts per layer.
 
     ``shard`` N > 1: rank 0's shard of N-way tensor + expert parallelism (its heads, its expert
     range, its vocabulary slice, all layers' experts distinct) on this one GPU with every
