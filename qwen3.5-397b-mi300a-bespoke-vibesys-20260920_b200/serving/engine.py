@@ -48,6 +48,17 @@ def prefill_graph_widths(flag: str) -> list[int]:
     return [int(w) for w in str(flag or "").replace(" ", "").split(",") if w.strip().isdigit() and int(w) > 0]
 
 
+def mixed_graph_shapes(flag: str) -> list[tuple[int, int]]:
+    """(decode rows, prefill width) of the captured mixed steps from ``QB_MIXED_GRAPHS``
+    ("32:256,32:512"; empty: none)."""
+    out = []
+    for part in str(flag or "").replace(" ", "").split(","):
+        b, _, w = part.partition(":")
+        if b.isdigit() and w.isdigit() and int(b) > 0 and int(w) > 0:
+            out.append((int(b), int(w)))
+    return out
+
+
 def nvls_min_rows(flag: int, world: int) -> int:
     """Smallest all-reduce (rows) that takes the NVLS kernel, 0 for never. ``flag`` -1 chooses by
     world size from the collective sweep (hidden 4096, device time, max over ranks): at 8 ranks the
@@ -125,6 +136,9 @@ def build_model(model: str, rank: int, world: int, device: torch.device, spec: P
         widths = prefill_graph_widths(flags.get("QB_PREFILL_GRAPHS"))
         if widths:
             g.prepare_prefill(widths)
+        shapes = mixed_graph_shapes(flags.get("QB_MIXED_GRAPHS"))
+        if shapes:
+            g.prepare_mixed(shapes)
         mem.phase("graphs")
         pool_plan(m, rank)
         return g, distinct

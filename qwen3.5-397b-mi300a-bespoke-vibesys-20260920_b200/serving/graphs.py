@@ -20,6 +20,10 @@ no padding is needed and nothing else changes between replays: the chunks of a l
 the prefill chunk size, and follow-up turns of a captured length, replay instead of issuing their
 ~1250 launches. Batches of several segments and other lengths run eagerly. Reference behaviour:
 ``graph_prefill.py:812`` (``PrefillGraphRunner``, captured rows x width shapes).
+
+Mixed steps (``prepare_mixed``, ``QB_MIXED_GRAPHS``): the same for a decode batch of up to B
+lanes (padded with the pad lane) plus one prefill segment of exactly W tokens. Reference
+behaviour: ``graph_mixed.py:308`` (``MixedGraphRunner``).
 """
 
 from __future__ import annotations
@@ -179,6 +183,37 @@ class _PrefillBucket:
                           [self.lane_h], [0, self.W], [self.start_h], model.max_seq)
 
 
+class _MixedBucket:
+    """Static buffers of one captured mixed step: ``B`` one-token decode rows (padded with the pad
+    lane) followed by one prefill segment of exactly ``W`` tokens."""
+
+    def __init__(self, model, B: int, W: int):
+        dev = model.device
+        i32 = dict(dtype=torch.int32, device=dev)
+        self.B, self.W = B, W
+        T = B + W
+        self.tokens = torch.zeros(T, dtype=torch.int64, device=dev)
+        self.packed_dev = torch.zeros(2 * T + 2 * (B + 1), **i32)  # positions | rows | lanes | starts
+        self.pos = torch.zeros(T, **i32)
+        self.rows = torch.zeros(T, **i32)
+        self.lanes = torch.zeros(B + 1, **i32)
+        self.starts = torch.zeros(B + 1, **i32)
+        self.cu_h = list(range(B + 1)) + [T]
+        self.cu = torch.tensor(self.cu_h, **i32)
+        self.logit_rows = torch.tensor(list(range(B)) + [T - 1], dtype=torch.int64, device=dev)
+        self._hosts = [(_host(torch.zeros(2 * T + 2 * (B + 1), dtype=torch.int32)),
+                        _host(torch.zeros(T, dtype=torch.int64))) for _ in range(2)]
+        self._flip = 0
+        self.lanes_h = [model.max_batch - 1] * (B + 1)
+        self.starts_h = [0] * (B + 1)
+        self.graph = None
+        self.out = None
+
+    def inputs(self, model) -> StepInputs:
+        return StepInputs(self.tokens, self.pos, self.rows, self.lanes, self.cu, self.starts, self.logit_rows,
+                          list(self.lanes_h), list(self.cu_h), list(self.starts_h), model.max_seq)
+
+
 class _SpecBucket:
     """Static buffers of one captured speculative round for ``B`` lanes and draft depth ``k``:
     the draft steps' positions and KV rows, the verify forward's ``B x (k+1)`` rows, and the
@@ -249,6 +284,9 @@ class GraphRunner:
         self.replays = 0
         self.launch_per_replay: dict[int, int] = {}
         self._pb: dict[int, _PrefillBucket] = {}  # captured prefill widths
+        self._mb: dict[tuple[int, int], _MixedBucket] = {}  # captured (decode rows, prefill width)
+        self.mixed_replays = 0
+        self.mixed_validated = False
         self.prefill_replays = 0
         self.prefill_validated = False
 
@@ -485,6 +523,140 @@ class GraphRunner:
     def prefill(self, lane, ids, start):
         return self.prefill_batch([(lane, ids, start)])[0]
 
+    # ------------------------------------------------------------------ mixed steps
+    def _mixed_fill(self, bk: _MixedBucket, lanes, tokens, positions, call, capture: bool = False) -> None:
+        m = self.model
+        B, W, T = bk.B, bk.W, bk.B + bk.W
+        m._gpu_mark("in")
+        bk._flip ^= 1
+        ph, th = bk._hosts[bk._flip]
+        n = len(lanes)
+        plane, pids, pstart = call
+        ln = list(lanes) + [self.pad_lane] * (B - n)
+        pos = list(positions) + [0] * (B - n)
+        if capture:
+            rows = [0] * T
+        else:
+            rows = [m._row(l, p) for l, p in zip(lanes, positions)] + [0] * (B - n)
+            rows += [m._row(plane, p) for p in range(pstart, pstart + W)]
+        allpos = pos + list(range(pstart, pstart + W))
+        ph[:T] = torch.tensor(allpos, dtype=torch.int32)
+        ph[T:2 * T] = torch.tensor(rows, dtype=torch.int32)
+        ph[2 * T:2 * T + B + 1] = torch.tensor(ln + [plane], dtype=torch.int32)
+        ph[2 * T + B + 1:] = torch.tensor(pos + [pstart], dtype=torch.int32)
+        th[:n] = torch.tensor([int(t) for t in tokens], dtype=torch.int64)
+        th[n:B] = 0
+        th[B:] = torch.tensor([int(t) for t in pids], dtype=torch.int64)
+        bk.lanes_h, bk.starts_h = ln + [plane], pos + [pstart]
+        bk.packed_dev.copy_(ph, non_blocking=True)
+        bk.tokens.copy_(th, non_blocking=True)
+        bk.pos.copy_(bk.packed_dev[:T])
+        bk.rows.copy_(bk.packed_dev[T:2 * T])
+        bk.lanes.copy_(bk.packed_dev[2 * T:2 * T + B + 1])
+        bk.starts.copy_(bk.packed_dev[2 * T + B + 1:])
+        m._h2d += ph.numel() * 4 + th.numel() * 8
+        m._sync_tables()
+
+    def _mixed_run(self, bk: _MixedBucket):
+        m = self.model
+        return m.logits(m._forward(bk.inputs(m)))
+
+    def prepare_mixed(self, shapes) -> None:
+        """Capture one mixed step per (decode rows B, prefill width W) on the pad lane, then check
+        each against an eager mixed step (``validate_mixed``). The decode rows are padded up to B
+        with the pad lane, as the decode buckets do; the prefill segment must be exactly W tokens
+        (the segment lengths fix every host-planned table). Every rank in the same order."""
+        m = self.model
+        shapes = sorted({(int(b), int(w)) for b, w in shapes if 0 < int(b) <= self.max_batch - 1
+                         and 0 < int(w) <= m.max_seq}, reverse=True)
+        if (not self.enabled or not shapes or m.mtp is not None
+                or (m.device.type != "cuda" and not isinstance(self.backend, HostGraphs))):
+            return
+        m.begin(self.pad_lane)
+        m.attach_blocks(self.pad_lane, [])
+        for B, W in shapes:
+            bk = _MixedBucket(m, B, W)
+            self._mixed_fill(bk, [], [], [], (self.pad_lane, [0] * W, 0), capture=True)
+            l0 = self.backend.count_launches()
+            with torch.inference_mode():
+                bk.graph, bk.out = self.backend.capture(lambda bk=bk: self._mixed_run(bk))
+            self.launch_per_replay[(B, W)] = (self.backend.count_launches() - l0) // 3
+            self._mb[(B, W)] = bk
+        self.backend.sync()
+        self.validate_mixed()
+
+    def validate_mixed(self, tol: float = 5e-2) -> bool:
+        """Boot check of every captured mixed shape: B decode lanes (one token each at position 0)
+        and a W-token prefill on another lane, replayed and run eagerly from the same reset states,
+        must give the same logits within ``tol`` of their scale; ranks agree on the minimum."""
+        m = self.model
+        ok, worst = True, 0.0
+        with torch.inference_mode():
+            for (B, W), bk in sorted(self._mb.items()):
+                lanes, plane = list(range(B)), B
+                pblocks = list(range(1 + B, 1 + B + -(-W // m.block_size)))
+                ids = [(17 * i + 5) % min(m.cfg.vocab, 1000) for i in range(W)]
+                toks = [(7 * ln + 11) % 1000 for ln in lanes]
+
+                def reset():
+                    for ln in lanes:
+                        m.begin(ln)
+                        m.attach_blocks(ln, [1 + ln])
+                    m.begin(plane)
+                    m.attach_blocks(plane, pblocks)
+
+                reset()
+                self._mixed_fill(bk, lanes, toks, [0] * B, (plane, ids, 0))
+                bk.graph.replay()
+                got = bk.out.float().clone()
+                reset()
+                dec, pre = m.decode_mixed(lanes, toks, [0] * B, [(plane, ids, 0)])
+                exp = torch.cat([dec, pre[0]]).float()
+                for ln in lanes + [plane]:
+                    m.begin(ln)
+                    m.attach_blocks(ln, [])
+                err = (got - exp).abs().max().item()
+                scale = exp.abs().max().item() + 1e-6
+                worst = max(worst, err / scale)
+                if not (err <= tol * scale) or not bool(torch.isfinite(got).all()):
+                    ok = False
+        flag = torch.tensor([1 if ok else 0], dtype=torch.int32, device=m.device)
+        if getattr(m.comm, "world", 1) > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        agreed = bool(int(flag.item()))
+        if flags.get("QB_GRAPH_LOG") or not agreed:
+            print(f"[graph-capture] mixed validation: this rank {'ok' if ok else 'MISMATCH'} (worst relative "
+                  f"{worst:.2e}), all ranks {'ok' if agreed else 'disagree: mixed steps run eagerly'}", flush=True)
+        if not agreed:
+            for bk in self._mb.values():
+                bk.graph = bk.out = None
+            self._mb.clear()
+        self.mixed_validated = agreed
+        return agreed
+
+    def decode_mixed(self, lanes, tokens, positions, prefill_calls):
+        """``Model.decode_mixed``; one prefill segment of a captured width with at most a captured
+        number of decode rows is replayed from the smallest such shape (rows copied out)."""
+        m = self.model
+        calls = list(prefill_calls)
+        n = len(lanes)
+        if len(calls) == 1 and self._mb and not m.fault and m.mtp is None:
+            plane, pids, pstart = calls[0]
+            W = len(pids)
+            B = min((b for b, w in self._mb if w == W and b >= n), default=None)
+            if B is not None and pstart + W <= m.max_seq:
+                bk = self._mb[(B, W)]
+                with torch.inference_mode():
+                    self._mixed_fill(bk, lanes, tokens, positions, (plane, pids, pstart))
+                    bk.graph.replay()
+                    lg = bk.out.clone()
+                self.mixed_replays += 1
+                self.backend.add_launches(self.launch_per_replay.get((B, W), 0))
+                return lg[:n], [lg[B:B + 1]]
+        return m.decode_mixed(lanes, tokens, positions, calls)
+
     # ------------------------------------------------------------------ speculative rounds
     def _spec_fill(self, bk: _SpecBucket, lanes, tokens, positions) -> None:
         m = self.model
@@ -701,6 +873,9 @@ class GraphRunner:
         for pb in self._pb.values():
             pb.graph = pb.out = None
         self._pb.clear()
+        for mb in self._mb.values():
+            mb.graph = mb.out = None
+        self._mb.clear()
 
     # ------------------------------------------------------------------ runner
     def decode(self, lanes, tokens, positions):

@@ -80,6 +80,9 @@ _def("QB_MTP_DEVICE_ACCEPT", bool, True, "speculative rounds: accepted lengths c
      "round (draft, verify, accept, commit) replayed as one graph, read back once", lockstep=True)
 _def("QB_PREFILL_GRAPHS", str, "", "widths (comma-separated token counts) of captured single-segment prefill steps, "
      "replayed for one segment of exactly that length (empty: prefill runs eagerly)", lockstep=True)
+_def("QB_MIXED_GRAPHS", str, "", "captured mixed steps as decode-rows:prefill-width pairs (\"32:256,32:512\"): a mixed "
+     "step with at most that many decode lanes and one prefill segment of exactly that width replays (empty: eager)",
+     lockstep=True)
 _def("QB_GREEDY_HEAD", bool, True, "greedy decode ids from each rank's (max, index) over its vocabulary slice, "
      "gathered as 8-byte pairs (off: the full logits rows are all-gathered, then the argmax)", lockstep=True)
 _def("QB_MOE_FUSE_SHARED", bool, True, "MoE: the shared expert's gated rows are added in the routed combine kernel "

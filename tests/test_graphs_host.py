@@ -137,3 +137,32 @@ def test_host_prefill_graph_validation_failure_drops_them():
     m.attach_blocks(0, list(range(1, 9)))
     out = g.prefill_batch([(0, list(range(32)), 0)])[0]  # eager
     assert torch.isfinite(out).all() and out.abs().max() < 1e3 and g.prefill_replays == 0
+
+
+def test_host_mixed_graphs_match_eager():
+    """Captured mixed steps (decode rows padded with the pad lane + one prefill segment of a
+    captured width) give the eager mixed step's logits, and leave every lane's state alike: the
+    decode steps that follow agree with lanes that took the eager path."""
+    m = _model(max_batch=10)
+    g = GraphRunner(m, buckets=(1, 2), backend=HostGraphs())
+    g.prepare_mixed([(2, 32), (4, 32)])
+    assert g.mixed_validated and set(g._mb) == {(2, 32), (4, 32)}
+    prompts = [list(range(3, 20)), list(range(40, 61))]
+    _lanes(m, prompts, 0)  # lanes 0, 1: through the runner
+    _lanes(m, prompts, 3)  # lanes 3, 4: eager, same histories
+    new = list(range(200, 232))
+    for lane in (2, 5):  # the prefill segment's lanes
+        m.begin(lane)
+        m.attach_blocks(lane, list(range(1 + 8 * lane, 9 + 8 * lane)))
+    toks, pos = [7, 9], [len(p) for p in prompts]
+    dg, pg = g.decode_mixed([0, 1], toks, pos, [(2, new, 0)])
+    de, pe = m.decode_mixed([3, 4], toks, pos, [(5, new, 0)])
+    assert g.mixed_replays == 1  # 2 decode rows: the (2, 32) shape
+    assert torch.allclose(dg, de, atol=1e-4, rtol=1e-4) and torch.allclose(pg[0], pe[0], atol=1e-4, rtol=1e-4)
+    toks3 = dg.argmax(-1).tolist() + [int(pg[0].argmax())]
+    pos3 = [p + 1 for p in pos] + [32]
+    a = m.decode([0, 1, 2], toks3, pos3)
+    b = m.decode([3, 4, 5], toks3, pos3)
+    assert torch.allclose(a, b, atol=1e-4, rtol=1e-4)
+    dg1, _ = g.decode_mixed([0], [5], [pos3[0] + 1], [(2, list(range(33)), 33)])  # width 33: eager
+    assert g.mixed_replays == 1 and dg1.shape[0] == 1
