@@ -77,7 +77,12 @@ def parse(argv=None):
                     help="widths (comma-separated token counts) of captured single-segment prefill steps, e.g. "
                          "the prefill chunk size: a prompt chunk of exactly that length replays its graph "
                          "(sets QB_PREFILL_GRAPHS on every rank)")
+    ap.add_argument("--mixed-graphs", default=None,
+                    help="decode-rows:prefill-width pairs of captured mixed steps (with --mixed), e.g. 32:256 "
+                         "(sets QB_MIXED_GRAPHS on every rank)")
     args = ap.parse_args(argv)
+    if args.mixed_graphs is not None:
+        flags.put("QB_MIXED_GRAPHS", args.mixed_graphs)
     if args.prefill_graphs is not None:
         flags.put("QB_PREFILL_GRAPHS", args.prefill_graphs)  # read when the model and its graphs are built
     return args

@@ -181,3 +181,6 @@ def test_prefill_graphs_option_sets_the_flag(monkeypatch):
     assert flags.get("QB_PREFILL_GRAPHS") == ""
     server.parse(["--model-path", "tiny", "--prefill-graphs", "512,2048"])
     assert flags.get("QB_PREFILL_GRAPHS") == "512,2048"
+    monkeypatch.setenv("QB_MIXED_GRAPHS", "")
+    server.parse(["--model-path", "tiny", "--mixed", "--mixed-graphs", "32:256"])
+    assert flags.get("QB_MIXED_GRAPHS") == "32:256"
