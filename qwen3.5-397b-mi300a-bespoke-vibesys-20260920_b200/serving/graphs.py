@@ -282,7 +282,8 @@ class GraphRunner:
         self._spec: dict[int, _SpecBucket] = {}
         self.enabled = flags.get("QB_GRAPHS")
         self.replays = 0
-        self.launch_per_replay: dict[int, int] = {}
+        # kernels per replay: decode bucket B, prefill width -W, mixed shape (B, W)
+        self.launch_per_replay: dict[int | tuple[int, int], int] = {}
         self._pb: dict[int, _PrefillBucket] = {}  # captured prefill widths
         self._mb: dict[tuple[int, int], _MixedBucket] = {}  # captured (decode rows, prefill width)
         self.mixed_replays = 0
