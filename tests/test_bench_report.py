@@ -69,3 +69,35 @@ def test_loop_seconds_fits_the_budget():
     assert 90.0 <= bench.loop_seconds(a) <= 100.0
     a = _args(budget_seconds=1e6, max_seconds=780.0)
     assert bench.loop_seconds(a) == 780.0
+
+
+def test_line_carries_the_driver_contract():
+    """The JSON line has every key the benchmark contract names, with the right types: the
+    metric, value and unit, the GPU count, steps and warm-up as given, ms per step x steps = the
+    timed window, the direction and scaling kind, dtype and data, the config's model / batch /
+    sequence / parallelism, clocks, the end-to-end block with its per-step copy bytes, and the
+    launch count."""
+    import json
+
+    steps = [4.0] * 300
+    recs = [Rec(turn=1, submit_step=i, first_step=i, t_submit=0.0, t_first=0.004, generated=3) for i in range(250)]
+    line = bench.report(_args(steps=20, warmup=5), impl="ours", world=2, window_ms=sum(steps), host_s=1.3,
+                        records=recs, step_ms=steps, kinds_summary={}, clocks={"sm_mhz": 1900.0, "sm_max_mhz": 1965.0,
+                        "reasons": []}, h2d=20 * 1000, d2h=20 * 80, launches=12345, sched_steps=300, boot_s=1.0,
+                        warm_s=1.0, cfg_desc="full", expert_storage="all layers distinct", t_end=2.0)
+    parsed = json.loads(json.dumps(line))  # one plain JSON object
+    for k, t in (("metric", str), ("unit", str), ("n_gpus", int), ("steps", int), ("warmup", int),
+                 ("ms_per_step", float), ("higher_is_better", bool), ("scaling", str), ("dtype", str),
+                 ("data", str), ("config", dict), ("clocks", dict), ("e2e", dict), ("gpu_launches", int)):
+        assert isinstance(parsed[k], t), k
+    assert parsed["metric"] == bench.METRIC and parsed["n_gpus"] == 2
+    assert parsed["steps"] == 20 and parsed["warmup"] == 5
+    assert abs(parsed["ms_per_step"] * parsed["steps"] - sum(steps)) < 1e-6
+    assert parsed["higher_is_better"] is False and parsed["scaling"] == "strong" and parsed["dtype"] == "bf16"
+    assert isinstance(parsed["value"], float) and parsed["ttft_samples"] == 250
+    for k in ("model", "global_batch", "seq_len", "parallelism"):
+        assert k in parsed["config"], k
+    assert parsed["config"]["parallelism"] == "tp2+ep2"
+    e2e = parsed["e2e"]
+    assert e2e["h2d_bytes_per_step"] == 1000 and e2e["d2h_bytes_per_step"] == 80 and "value" in e2e
+    assert parsed["gpu_launches"] == 12345 and "vs_baseline" in parsed
