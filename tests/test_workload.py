@@ -46,3 +46,21 @@ def test_percentile():
     assert percentile([1.0, 2.0, 3.0, 4.0], 50) == 2.5
     assert percentile([5.0], 95) == 5.0
     assert abs(percentile(list(map(float, range(101))), 95) - 95.0) < 1e-9
+
+
+def test_defaults_are_the_named_workload():
+    """The chat workload's defaults, and bench.py's, are the configuration the headline is quoted
+    on: 256 sessions at concurrency 32, 6 turns, a 2000-8000-id first prompt, 200-1000 new ids per
+    later turn, 200-500 generated tokens per turn, seed 0."""
+    import os
+    import sys
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    import bench
+
+    s = ChatSpec()
+    assert (s.sessions, s.concurrency, s.turns, s.seed) == (256, 32, 6, 0)
+    assert (s.first_len, s.user_len, s.gen_len) == ((2000, 8000), (200, 1000), (200, 500))
+    a = bench.parse([])
+    assert (a.sessions, a.concurrency, a.turns, a.seed, a.gpus) == (256, 32, 6, 0, 1)
+    assert (tuple(a.first_len), tuple(a.user_len), tuple(a.gen_len)) == ((2000, 8000), (200, 1000), (200, 500))
