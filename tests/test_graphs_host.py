@@ -166,3 +166,29 @@ def test_host_mixed_graphs_match_eager():
     assert torch.allclose(a, b, atol=1e-4, rtol=1e-4)
     dg1, _ = g.decode_mixed([0], [5], [pos3[0] + 1], [(2, list(range(33)), 33)])  # width 33: eager
     assert g.mixed_replays == 1 and dg1.shape[0] == 1
+
+
+def test_two_gloo_ranks_graph_runner_with_greedy_head(tiny_dir, tmp_path):
+    """Two CPU ranks (TP=2 over gloo) prepare and validate decode buckets and a prefill width
+    through the host capture backend (the validation vote runs over the group); the replayed
+    steps give the eager steps' logits, greedy ids gathered as (max, index) pairs and the kept
+    full-vocabulary row of a finishing lane."""
+    import json
+    import os
+    import socket
+    import subprocess
+    import sys
+
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    here = os.path.dirname(os.path.abspath(__file__))
+    out = str(tmp_path / "res.json")
+    procs = [subprocess.Popen([sys.executable, os.path.join(here, "graphs_gloo_rank.py"), str(r), "2", tiny_dir,
+                               out, str(port)]) for r in range(2)]
+    assert [p.wait(timeout=600) for p in procs] == [0, 0]
+    res = json.load(open(out))
+    assert res["validated"] and res["prefill_validated"]
+    assert res["prefill_close"] and res["vocab"] == 4096
+    assert res["ids_match"] and res["kept_close"]
+    assert res["replays"] == [1, 2]
